@@ -1,0 +1,409 @@
+#!/usr/bin/env python
+"""Benchmark: batched differentiable iLQR, fwd+bwd solves/s on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one forward solve (all iLQR iterations) plus the implicit-diff
+backward of a batch of 16384 quadrotor MPC problems with horizon 20 and
+5 iterations (the training-scale rollout workload), each GPU solving its own
+batch (weak scaling; for N > 1 the first actions are all-gathered over NCCL
+inside the step). Prints one JSON line on rank 0.
+
+  value  whole-job solves/s with inputs resident in HBM (device time, max over
+         ranks); inputs (257 MB of cost blocks per GPU) exceed the 126 MB L2.
+  e2e    the same through the reference-facing operator
+         (mpc_compat.MPC(...)(x_init, QuadCost(C, c), dx) + autograd backward)
+         with host buffers: every step copies its inputs from pinned host
+         memory and reads the actions and dL/dx0 back.
+  --impl reference: the reference's CPU algorithm (the CPU oracle, a numpy
+         restatement of DiffMPC) on all host cores, over a bounded sample.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "ca-ac-mpc_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "iLQR fwd+bwd solves/s @B=16384,T=20 at 1/2/4/8 B200; p50 latency @B=16,T=5"
+WORKLOAD = "rollout_b16384_t20"
+
+
+def _args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--latency-reps", type=int, default=200)
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# clocks sampler (nvidia-smi during the timed region)
+# ---------------------------------------------------------------------------
+class Clocks:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                      "--format=csv,noheader,nounits"], capture_output=True,
+                                     text=True, timeout=5).stdout.strip()
+                if out:
+                    self.samples.append([x.strip() for x in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4)
+                          if len(s) > 5 + i and s[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle (numpy restatement of DiffMPC) over host cores
+# ---------------------------------------------------------------------------
+def cpu_oracle_rate(workers: int, chunk: int = 1024, reps: int = 1):
+    from oracle.cpu_pool import OraclePool
+    pool = OraclePool(workers, ROOT, PKG)
+    try:
+        best = None
+        for _ in range(reps):
+            n, t = pool.run(WORKLOAD, workers, chunk)
+            best = t if best is None else min(best, t)
+        return n / best, n, best
+    finally:
+        pool.close()
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import ilqr_workload as wl
+    cores = len(os.sched_getaffinity(0))
+    from oracle.cpu_pool import OraclePool
+    pool = OraclePool(cores, ROOT, PKG)
+    chunk = 1024
+    try:
+        for _ in range(args.warmup):
+            pool.run(WORKLOAD, cores, chunk)
+        times = []
+        n = 0
+        for _ in range(args.steps):
+            n, t = pool.run(WORKLOAD, cores, chunk)
+            times.append(t)
+    finally:
+        pool.close()
+    cfg = wl.CONFIGS[WORKLOAD]
+    step = statistics.mean(times)
+    value = n / step
+    sample = (f"{n} of {cfg['B']} elements per step ({cores} workers x {chunk}), T={cfg['T']}, "
+              f"{cfg['max_iter']} iterations, fwd+bwd")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "solves/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": step * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, reference value ranges)",
+        "config": {"workload": WORKLOAD, "B": cfg["B"], "T": cfg["T"], "iters": cfg["max_iter"],
+                   "alphas": list(cfg["alphas"]), "control_box": True},
+        "cpu_baseline": {"value": value, "unit": "solves/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "solves/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def fp32_peak_tflops(torch, device):
+    """Measured FP32 FMA throughput of this GPU (8 independent FMA chains per
+    thread, 8 CTAs x 256 threads per SM), best of 5 launches."""
+    import ctypes
+    L = ctypes.CDLL(os.path.join(PKG, "libilqr_probe.so"))
+    L.ilqr_probe_fma.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+    L.ilqr_probe_fma_flops.restype = ctypes.c_double
+    L.ilqr_probe_fma_flops.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    blocks, threads, iters = sms * 8, 256, 4096
+    out = torch.empty(blocks * threads, device=device)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+    best = 0.0
+    for _ in range(6):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        L.ilqr_probe_fma(ctypes.c_void_p(out.data_ptr()), blocks, threads, iters, stream)
+        e1.record()
+        torch.cuda.synchronize()
+        best = max(best, L.ilqr_probe_fma_flops(blocks, threads, iters) / (e0.elapsed_time(e1) * 1e-3) / 1e12)
+    return best
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import ilqr_costmodel as cm
+    import ilqr_native as nat
+    import ilqr_shard
+    import ilqr_workload as wl
+    import mpc_compat
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    cfg = wl.CONFIGS[WORKLOAD]
+    B, T, iters, alphas = cfg["B"], cfg["T"], cfg["max_iter"], cfg["alphas"]
+    inp = wl.make_inputs(B, T, seed=rank, target=cfg["target"], r=cfg["r"])
+    gXn, gUn = wl.make_backward_seeds(B, T, seed=1 + rank)
+    d = {k: torch.from_numpy(v).to(dev) for k, v in inp.items()}
+    gX, gU = torch.from_numpy(gXn).to(dev), torch.from_numpy(gUn).to(dev)
+    lo, hi = torch.from_numpy(wl.U_MIN).to(dev), torch.from_numpy(wl.U_MAX).to(dev)
+
+    stream = torch.cuda.current_stream(dev)
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+
+    def step(timing=None):
+        if timing is not None:
+            timing[0].record(stream)
+        out = nat.solve(d["x0"], d["U_init"], d["C"], d["c"], None, None, None, None, lo, hi,
+                        dt=wl.DT, max_iter=iters, reg_eps=wl.REG_EPS, alphas=alphas)
+        if timing is not None:
+            timing[1].record(stream)
+        g = nat.backward(out["X"], out["U"], d["C"], gX, gU, tight=out["tight"], dt=wl.DT,
+                         reg_eps=wl.REG_EPS, need=("x0", "C", "c"))
+        if timing is not None:
+            timing[2].record(stream)
+        if world > 1:
+            ilqr_shard.gather_first_actions(out["U"], B * world)
+        return out, g
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # ---- device-resident throughput ---------------------------------------
+    for _ in range(max(3, args.warmup)):
+        step()
+    barrier()
+    timings = [(ev(), ev(), ev()) for _ in range(args.steps)]
+    t_start, t_end = ev(), ev()
+    with Clocks(local) as clk:
+        barrier()
+        t_start.record(stream)
+        for i in range(args.steps):
+            step(timings[i])
+        t_end.record(stream)
+        barrier()
+    elapsed = t_start.elapsed_time(t_end) * 1e-3
+    solve_ms = [a.elapsed_time(b) for a, b, _ in timings]
+    bwd_ms = [b.elapsed_time(c) for _, b, c in timings]
+    if world > 1:
+        t = torch.tensor([elapsed], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed = float(t.item())
+    per_step = elapsed / args.steps
+    value = world * B / per_step
+
+    # ---- algorithmic counts for the roofline (same inputs -> same iterations)
+    st = nat.solve(d["x0"], d["U_init"], d["C"], d["c"], None, None, None, None, lo, hi, dt=wl.DT,
+                   max_iter=iters, reg_eps=wl.REG_EPS, alphas=alphas, want_stats=True)
+    it_n = st["iters"].cpu().numpy()
+    acc_n = np.minimum(it_n, st["stall_iter"].cpu().numpy())
+    f_solve = cm.solve_flops(T, len(alphas), it_n, acc_n)
+    f_bwd = cm.backward_flops(T, B)
+    peak_fp32 = fp32_peak_tflops(torch, dev)
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+    t_solve = statistics.mean(solve_ms) * 1e-3
+    t_bwd = statistics.mean(bwd_ms) * 1e-3
+    traffic = None
+    try:
+        prof = json.load(open(os.path.join(ROOT, "profiles", "solve_kernel_traffic.json")))
+        traffic = prof.get(WORKLOAD, {}).get("dram_bytes_per_launch")
+    except Exception:
+        pass
+    roofline = {
+        "bound": "fp32", "kernel": "solve_kernel (fused forward iLQR)",
+        "achieved": f_solve / t_solve / 1e12, "peak": peak_fp32, "unit": "TFLOP/s",
+        "frac": f_solve / t_solve / 1e12 / peak_fp32, "traffic": traffic,
+        "peak_source": "measured FMA probe on this GPU (no FP32 figure in MEASURED_PEAKS.json)",
+        "algorithmic_flops_per_launch": f_solve, "mean_launch_ms": t_solve * 1e3,
+        "hbm": {"algorithmic_bytes_per_launch": cm.solve_bytes(T, B),
+                "achieved_gbs": cm.solve_bytes(T, B) / t_solve / 1e9, "peak_gbs": hbm_peak,
+                "frac": cm.solve_bytes(T, B) / t_solve / 1e9 / hbm_peak,
+                "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
+        "backward_kernel": {"mean_launch_ms": t_bwd * 1e3, "tflops": f_bwd / t_bwd / 1e12,
+                            "fp32_frac": f_bwd / t_bwd / 1e12 / peak_fp32,
+                            "gbs": cm.backward_bytes(T, B) / t_bwd / 1e9,
+                            "hbm_frac": cm.backward_bytes(T, B) / t_bwd / 1e9 / hbm_peak},
+    }
+
+    # ---- end to end through the reference-facing operator, host buffers -----
+    e2e = None
+    if not args.no_e2e:
+        pin = lambda a: torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
+        h_x0 = pin(inp["x0"])
+        h_C = pin(np.transpose(inp["C"], (1, 0, 2, 3)))   # mpc.pytorch layout [T, B, n, n]
+        h_c = pin(np.transpose(inp["c"], (1, 0, 2)))
+        h_gX = pin(np.transpose(gXn, (1, 0, 2)))
+        h_gU = pin(np.transpose(gUn, (1, 0, 2)))
+        h_act = torch.empty(B * world, 4).pin_memory()
+        h_gx0 = torch.empty(B, 10).pin_memory()
+        mpc = mpc_compat.MPC(10, 4, T, u_lower=lo.view(1, 1, 4).expand(T, 1, 4),
+                             u_upper=hi.view(1, 1, 4).expand(T, 1, 4), lqr_iter=iters,
+                             eps=wl.REG_EPS, alphas=alphas)
+        dyn = type("Dyn", (), {"dt": wl.DT})()
+
+        def e2e_step():
+            x0 = h_x0.to(dev, non_blocking=True).requires_grad_(True)
+            C = h_C.to(dev, non_blocking=True).requires_grad_(True)
+            c = h_c.to(dev, non_blocking=True).requires_grad_(True)
+            gx = h_gX.to(dev, non_blocking=True)
+            gu = h_gU.to(dev, non_blocking=True)
+            x, u, _ = mpc(x0, mpc_compat.QuadCost(C, c), dyn)
+            ((x * gx).sum() + (u * gu).sum()).backward()
+            act = u[0].detach()
+            if world > 1:
+                act = ilqr_shard.gather_first_actions(u.detach().permute(1, 0, 2).contiguous(), B * world)
+            h_act.copy_(act, non_blocking=True)
+            h_gx0.copy_(x0.grad, non_blocking=True)
+
+        for _ in range(max(3, args.warmup)):
+            e2e_step()
+        barrier()
+        e0, e1 = ev(), ev()
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        barrier()
+        el = e0.elapsed_time(e1) * 1e-3
+        if world > 1:
+            t = torch.tensor([el], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            el = float(t.item())
+        h2d = sum(t.numel() * 4 for t in (h_x0, h_C, h_c, h_gX, h_gU))
+        e2e = {"value": world * B / (el / args.steps), "unit": "solves/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": (h_act.numel() + h_gx0.numel()) * 4,
+               "ms_per_step": el / args.steps * 1e3,
+               "path": "mpc_compat.MPC(...)(x_init, QuadCost(C, c), dx) + autograd backward"}
+
+    # ---- p50 latency, B=16 T=5, 10 iterations, fwd+bwd ----------------------
+    lat = None
+    if rank == 0 and args.latency_reps > 0:
+        lc, li = wl.config_inputs("latency_b16_t5")
+        ld = {k: torch.from_numpy(v).to(dev) for k, v in li.items()}
+        lgx, lgu = (torch.from_numpy(a).to(dev) for a in wl.make_backward_seeds(16, lc["T"]))
+        samples = []
+        for r in range(args.latency_reps + 10):
+            a, b = ev(), ev()
+            a.record(stream)
+            o = nat.solve(ld["x0"], ld["U_init"], ld["C"], ld["c"], None, None, None, None, lo, hi,
+                          dt=wl.DT, max_iter=lc["max_iter"], alphas=lc["alphas"])
+            nat.backward(o["X"], o["U"], ld["C"], lgx, lgu, tight=o["tight"], dt=wl.DT,
+                         need=("x0", "C", "c"))
+            b.record(stream)
+            b.synchronize()
+            if r >= 10:
+                samples.append(a.elapsed_time(b) * 1e3)
+        lat = {"p50_us": statistics.median(samples), "p90_us": sorted(samples)[int(0.9 * len(samples))],
+               "reps": len(samples), "config": "B=16, T=5, 10 iterations, fwd+bwd, device-resident"}
+
+    # ---- CPU baseline (rank 0, N=1) ------------------------------------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cores = len(os.sched_getaffinity(0))
+        rate, n, t = cpu_oracle_rate(cores)
+        cpu = {"value": rate, "unit": "solves/s", "cores": cores, "kind": "port",
+               "sample": f"{n} elements of {WORKLOAD} (T={T}, {iters} iterations, fwd+bwd), "
+                         f"{cores} spawned workers x 1024, oracle = numpy restatement of DiffMPC"}
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": value, "unit": "solves/s", "n_gpus": world,
+        "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": per_step * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; reference value ranges, dense C stored [B,T,14,14])",
+        "config": {"workload": WORKLOAD, "B_per_gpu": B, "T": T, "iters": iters,
+                   "alphas": list(alphas), "control_box": [wl.U_MIN.tolist(), wl.U_MAX.tolist()],
+                   "dt": wl.DT, "parallelism": f"batch sharded, {world} rank(s)",
+                   "l2": "inputs larger than L2 (C alone 257 MB per GPU), no flush",
+                   "per_step": "fused solve kernel + fused backward kernel"
+                               + (" + NCCL all-gather of first actions" if world > 1 else "")},
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+        "gpu_launches": 2 * args.steps, "clocks": clk.summary(),
+        "latency_b16_t5": lat,
+        "kernel_ms": {"solve_mean": statistics.mean(solve_ms), "backward_mean": statistics.mean(bwd_ms)},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = _args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

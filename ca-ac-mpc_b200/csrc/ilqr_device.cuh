@@ -1,0 +1,614 @@
+// ilqr_device.cuh -- device building blocks of the B200 iLQR solver.
+//
+// Compiled with -fmad=false: a*b+c is never contracted implicitly, so
+// elementwise model arithmetic rounds exactly like the reference's torch
+// elementwise ops, and the linear algebra uses explicit fmaf() with a fixed
+// summation order (deterministic: a recomputed rollout is bit-identical to
+// the candidate it repeats).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ilqr {
+
+constexpr int NX = 10;
+constexpr int NU = 4;
+constexpr int NT = 14;              // NX + NU
+constexpr int CBLK = NT * NT;       // floats of one C[b,t] block
+constexpr int WARP = 32;            // batch elements per CTA (one warp)
+constexpr int CSLAB = CBLK * WARP;  // floats of one staged C_t slab
+constexpr uint32_t SLAB_BYTES = CSLAB * 4u;
+constexpr float MASS = 0.752f;      // drone.py:166
+constexpr float GZ = -9.8066f;      // drone.py:187
+constexpr unsigned FULL = 0xffffffffu;
+constexpr uint32_t WAIT_LIMIT = 1u << 24;   // bounded mbarrier polls
+
+// Status bits (mirror ilqr_b200.h).
+constexpr uint32_t ELEM_CHOL_FALLBACK = 1u;
+constexpr uint32_t ELEM_NONFINITE = 2u;
+constexpr uint32_t ELEM_PIPE_TIMEOUT = 4u;
+
+// --------------------------------------------------------------------------
+// Quadrotor CTBR model (acmpc_public-master/diff_mpc_drones/drone.py)
+// --------------------------------------------------------------------------
+
+// One Euler/exp-map step, DroneDx.forward_CTBR (drone.py:409-465). The
+// expressions follow drone.py's operation order term by term (quat_mult at
+// :28-33, exp_map at :18-26, rotate_quat at :145-156); the zero terms of
+// quat_mult(q, [0,0,0,fc]) contribute exact zeros and are elided.
+__device__ __forceinline__ void drone_step(const float (&x)[NX], const float (&u)[NU],
+                                           float dt, float (&xn)[NX]) {
+  const float q0 = x[3], q1 = x[4], q2 = x[5], q3 = x[6];
+  const float wx = u[1], wy = u[2], wz = u[3], fc = u[0];
+  // p+ = p + dt v
+  xn[0] = x[0] + dt * x[7];
+  xn[1] = x[1] + dt * x[8];
+  xn[2] = x[2] + dt * x[9];
+  // exp_map(w, dt): torch.norm, F.normalize (eps 1e-12), cos/sin(|w| dt/2)
+  const float wn = sqrtf((wx * wx + wy * wy) + wz * wz);
+  const float den = fmaxf(wn, 1e-12f);
+  const float nx = wx / den, ny = wy / den, nz = wz / den;
+  const float half = wn * (dt * 0.5f);
+  float s, co;
+  sincosf(half, &s, &co);
+  const float e0 = co, e1 = nx * s, e2 = ny * s, e3 = nz * s;
+  // q+ = quat_mult(q, em): q1 := q, q2 := em
+  xn[3] = ((e0 * q0 - e1 * q1) - e2 * q2) - e3 * q3;
+  xn[4] = ((e0 * q1 + e1 * q0) - e2 * q3) + e3 * q2;
+  xn[5] = ((e0 * q2 + e2 * q0) + e1 * q3) - e3 * q1;
+  xn[6] = ((e0 * q3 - e1 * q2) + e2 * q1) + e3 * q0;
+  // rotate_quat(q, [0,0,fc]) = Im( (q (x) [0,0,0,fc]) (x) conj(q) )
+  const float f0 = -(fc * q3), f1 = fc * q2, f2 = -(fc * q1), f3 = fc * q0;
+  const float c1 = -q1, c2 = -q2, c3 = -q3;
+  const float r1 = ((q0 * f1 + c1 * f0) - c2 * f3) + c3 * f2;
+  const float r2 = ((q0 * f2 + c2 * f0) + c1 * f3) - c3 * f1;
+  const float r3 = ((q0 * f3 - c1 * f2) + c2 * f1) + c3 * f0;
+  // v+ = v + dt (rot/m + g)
+  xn[7] = x[7] + dt * (r1 / MASS + 0.0f);
+  xn[8] = x[8] + dt * (r2 / MASS + 0.0f);
+  xn[9] = x[9] + dt * (r3 / MASS + GZ);
+}
+
+// Nonzero entries of the discrete Jacobians A = I + dt J_x, B = dt J_u
+// (DroneDx.grad_input / get_A_B_mat_CTBR, drone.py:489-540). With state
+// blocks p = 0..2, q = 3..6, v = 7..9 and controls (fc, wx, wy, wz):
+//   A[p_i][v_i] = dt
+//   A[q][q]  = [[1,-h0,-h1,-h2],[h0,1,h2,-h1],[h1,-h2,1,h0],[h2,h1,-h0,1]]
+//   A[v][q]  = [[g2,g3,g0,g1],[-g1,-g0,g3,g2],[g0,-g1,-g2,g3]]
+//   B[q][w]  = rows [-e1,-e2,-e3],[e0,-e3,-e2],[e3,e0,-e1],[-e2,e1,e0]
+//   B[v][fc] = bv
+// with h_k = (w_k/2) dt, g_i = 2 (q_i fc / m) dt, e_i = (q_i/2) dt,
+// bv = (q^T M_k q / m) dt. All other entries are 0 (diagonal 1 for A).
+struct Jac {
+  float dt, h0, h1, h2, g0, g1, g2, g3, e0, e1, e2, e3, bv0, bv1, bv2;
+};
+
+__device__ __forceinline__ Jac drone_jac(const float (&x)[NX], const float (&u)[NU], float dt) {
+  Jac J;
+  J.dt = dt;
+  J.h0 = (0.5f * u[1]) * dt;
+  J.h1 = (0.5f * u[2]) * dt;
+  J.h2 = (0.5f * u[3]) * dt;
+  const float a0 = x[3], a1 = x[4], a2 = x[5], a3 = x[6], fc = u[0];
+  J.g0 = (2.0f * ((a0 * fc) / MASS)) * dt;
+  J.g1 = (2.0f * ((a1 * fc) / MASS)) * dt;
+  J.g2 = (2.0f * ((a2 * fc) / MASS)) * dt;
+  J.g3 = (2.0f * ((a3 * fc) / MASS)) * dt;
+  J.e0 = (0.5f * a0) * dt;
+  J.e1 = (0.5f * a1) * dt;
+  J.e2 = (0.5f * a2) * dt;
+  J.e3 = (0.5f * a3) * dt;
+  const float d1 = ((a2 * a0 + a3 * a1) + a0 * a2) + a1 * a3;
+  const float d2 = ((-a1 * a0 + -a0 * a1) + a3 * a2) + a2 * a3;
+  const float d3 = ((a0 * a0 + -a1 * a1) + -a2 * a2) + a3 * a3;
+  J.bv0 = (d1 / MASS) * dt;
+  J.bv1 = (d2 / MASS) * dt;
+  J.bv2 = (d3 / MASS) * dt;
+  return J;
+}
+
+// A[q_m][q_j]
+__device__ __forceinline__ float aqq(const Jac& J, int m, int j) {
+  switch (m * 4 + j) {
+    case 0: return 1.0f;   case 1: return -J.h0;  case 2: return -J.h1;  case 3: return -J.h2;
+    case 4: return J.h0;   case 5: return 1.0f;   case 6: return J.h2;   case 7: return -J.h1;
+    case 8: return J.h1;   case 9: return -J.h2;  case 10: return 1.0f;  case 11: return J.h0;
+    case 12: return J.h2;  case 13: return J.h1;  case 14: return -J.h0; default: return 1.0f;
+  }
+}
+// A[v_n][q_j]
+__device__ __forceinline__ float avq(const Jac& J, int n, int j) {
+  switch (n * 4 + j) {
+    case 0: return J.g2;   case 1: return J.g3;   case 2: return J.g0;   case 3: return J.g1;
+    case 4: return -J.g1;  case 5: return -J.g0;  case 6: return J.g3;   case 7: return J.g2;
+    case 8: return J.g0;   case 9: return -J.g1;  case 10: return -J.g2; default: return J.g3;
+  }
+}
+// B[q_m][w_k]
+__device__ __forceinline__ float bqw(const Jac& J, int m, int k) {
+  switch (m * 3 + k) {
+    case 0: return -J.e1;  case 1: return -J.e2;  case 2: return -J.e3;
+    case 3: return J.e0;   case 4: return -J.e3;  case 5: return -J.e2;
+    case 6: return J.e3;   case 7: return J.e0;   case 8: return -J.e1;
+    case 9: return -J.e2;  case 10: return J.e1;  default: return J.e0;
+  }
+}
+__device__ __forceinline__ float bvf(const Jac& J, int n) {
+  return n == 0 ? J.bv0 : (n == 1 ? J.bv1 : J.bv2);
+}
+
+// y = A x (sparse), the forward sweep / tangent step.
+__device__ __forceinline__ void jac_apply(const Jac& J, const float (&x)[NX], const float (&u)[NU],
+                                          float (&y)[NX]) {
+#pragma unroll
+  for (int i = 0; i < 3; ++i) y[i] = fmaf(J.dt, x[7 + i], x[i]);
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc = fmaf(aqq(J, m, j), x[3 + j], acc);
+#pragma unroll
+    for (int k = 0; k < 3; ++k) acc = fmaf(bqw(J, m, k), u[1 + k], acc);
+    y[3 + m] = acc;
+  }
+#pragma unroll
+  for (int n = 0; n < 3; ++n) {
+    float acc = x[7 + n];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc = fmaf(avq(J, n, j), x[3 + j], acc);
+    y[7 + n] = fmaf(bvf(J, n), u[0], acc);
+  }
+}
+
+// --------------------------------------------------------------------------
+// 4x4 Cholesky (lower triangle read, torch.linalg.cholesky semantics)
+// --------------------------------------------------------------------------
+struct Chol4 {
+  float l10, l20, l30, l21, l31, l32;
+  float r0, r1, r2, r3;  // reciprocals of the diagonal
+};
+
+__device__ __forceinline__ bool chol4(const float (&M)[NU][NU], Chol4& L) {
+  const float d0 = M[0][0];
+  const float l00 = sqrtf(d0);
+  L.r0 = 1.0f / l00;
+  L.l10 = M[1][0] * L.r0;
+  L.l20 = M[2][0] * L.r0;
+  L.l30 = M[3][0] * L.r0;
+  const float d1 = M[1][1] - L.l10 * L.l10;
+  const float l11 = sqrtf(d1);
+  L.r1 = 1.0f / l11;
+  L.l21 = (M[2][1] - L.l20 * L.l10) * L.r1;
+  L.l31 = (M[3][1] - L.l30 * L.l10) * L.r1;
+  const float d2 = (M[2][2] - L.l20 * L.l20) - L.l21 * L.l21;
+  const float l22 = sqrtf(d2);
+  L.r2 = 1.0f / l22;
+  L.l32 = ((M[3][2] - L.l30 * L.l20) - L.l31 * L.l21) * L.r2;
+  const float d3 = ((M[3][3] - L.l30 * L.l30) - L.l31 * L.l31) - L.l32 * L.l32;
+  const float l33 = sqrtf(d3);
+  L.r3 = 1.0f / l33;
+  return (d0 > 0.0f) && (d1 > 0.0f) && (d2 > 0.0f) && (d3 > 0.0f);
+}
+
+// x = (L L^T)^-1 b
+__device__ __forceinline__ void chol4_solve(const Chol4& L, const float (&b)[NU], float (&x)[NU]) {
+  const float y0 = b[0] * L.r0;
+  const float y1 = (b[1] - L.l10 * y0) * L.r1;
+  const float y2 = ((b[2] - L.l20 * y0) - L.l21 * y1) * L.r2;
+  const float y3 = (((b[3] - L.l30 * y0) - L.l31 * y1) - L.l32 * y2) * L.r3;
+  x[3] = y3 * L.r3;
+  x[2] = (y2 - L.l32 * x[3]) * L.r2;
+  x[1] = ((y1 - L.l21 * x[2]) - L.l31 * x[3]) * L.r1;
+  x[0] = (((y0 - L.l10 * x[1]) - L.l20 * x[2]) - L.l30 * x[3]) * L.r0;
+}
+
+// Fallback inverse for a Q_uu whose Cholesky failed, as _robust_solve's SVD
+// branch (DifferentialMPC/controller.py:758-779): M^-1 = V diag(1/S) U^T with
+// singular values floored at max(S)/1e12. One-sided Jacobi SVD (Hestenes) on
+// the columns of M, a fixed number of sweeps (bounded).
+static __device__ __noinline__ void svd_inverse4(const float (&M)[NU][NU], float (&Mi)[NU][NU]) {
+  float W[NU][NU], Vr[NU][NU];
+  for (int i = 0; i < NU; ++i)
+    for (int j = 0; j < NU; ++j) { W[i][j] = M[i][j]; Vr[i][j] = (i == j) ? 1.0f : 0.0f; }
+  for (int sweep = 0; sweep < 12; ++sweep) {
+    float off = 0.0f;
+    for (int p = 0; p < NU - 1; ++p)
+      for (int q = p + 1; q < NU; ++q) {
+        float a = 0.0f, b = 0.0f, g = 0.0f;
+        for (int i = 0; i < NU; ++i) {
+          a = fmaf(W[i][p], W[i][p], a);
+          b = fmaf(W[i][q], W[i][q], b);
+          g = fmaf(W[i][p], W[i][q], g);
+        }
+        if (g == 0.0f || fabsf(g) <= 1e-7f * sqrtf(a * b)) continue;
+        off = fmaxf(off, fabsf(g) / sqrtf(a * b));
+        const float zeta = (b - a) / (2.0f * g);
+        const float t = copysignf(1.0f, zeta) / (fabsf(zeta) + sqrtf(1.0f + zeta * zeta));
+        const float c = 1.0f / sqrtf(1.0f + t * t);
+        const float s = c * t;
+        for (int i = 0; i < NU; ++i) {
+          const float wp = W[i][p], wq = W[i][q];
+          W[i][p] = c * wp - s * wq;
+          W[i][q] = s * wp + c * wq;
+          const float vp = Vr[i][p], vq = Vr[i][q];
+          Vr[i][p] = c * vp - s * vq;
+          Vr[i][q] = s * vp + c * vq;
+        }
+      }
+    if (off <= 1e-7f) break;
+  }
+  float S[NU], smax = 0.0f;
+  for (int j = 0; j < NU; ++j) {
+    float n2 = 0.0f;
+    for (int i = 0; i < NU; ++i) n2 = fmaf(W[i][j], W[i][j], n2);
+    S[j] = sqrtf(n2);
+    smax = fmaxf(smax, S[j]);
+  }
+  const float floor_ = smax / 1e12f;
+  for (int i = 0; i < NU; ++i)
+    for (int j = 0; j < NU; ++j) Mi[i][j] = 0.0f;
+  for (int k = 0; k < NU; ++k) {
+    if (!(S[k] > 0.0f)) continue;
+    const float sr = S[k] > floor_ ? S[k] : floor_;
+    const float sc = 1.0f / (S[k] * sr);  // u_k = w_k / S_k, times 1/S_reg
+    for (int i = 0; i < NU; ++i)
+      for (int j = 0; j < NU; ++j) Mi[i][j] = fmaf(Vr[i][k] * sc, W[j][k], Mi[i][j]);
+  }
+}
+
+// --------------------------------------------------------------------------
+// One Riccati step with the sparse model Jacobians.
+//
+// Forward (MASKED=false), backward_lqr (DifferentialMPC/controller.py:697-723):
+//   Q_xx = l_xx + (A^T V) A        Q_xu = l_xu + (A^T V) B
+//   Q_uu = l_uu + (B^T V) B + reg I
+//   q_x = l_x + A^T v              q_u = l_u + B^T v
+//   [K | k] = -chol_solve(Q_uu + reg I, [Q_ux | q_u])   (reg added twice)
+//   V = Q_xx + (K^T Q_uu) K + K^T Q_ux + Q_xu K
+//   v = q_x + (K^T Q_uu) k + K^T q_u + Q_xu k
+// Backward (MASKED=true), _zero_constrained_lqr (controller.py:1035-1110):
+//   tight rows/cols of Q_uu zeroed, +1 on their diagonal, + (1e-8 reg) I;
+//   tight rows of Q_ux and entries of q_u zeroed for the solve only;
+//   V, v use the unmasked Q_uu, Q_ux, q_u, and v = q_x + K^T(Q_uu k + q_u) + Q_xu k.
+//
+// V is updated in place; the row (A^T .) and column (. A) transforms act on
+// one column / row at a time with four temporaries.
+// --------------------------------------------------------------------------
+template <bool MASKED>
+__device__ __forceinline__ bool riccati_step(float (&V)[NX][NX], float (&v)[NX], const Jac& J,
+                                             const float* __restrict__ Ct,
+                                             const float (&lx)[NX], const float (&lu)[NU],
+                                             float reg, uint32_t tight,
+                                             float (&K)[NU][NX], float (&k)[NU]) {
+  // ---- Q_uu = l_uu + (B^T V) B + reg I -----------------------------------
+  float Quu[NU][NU];
+  {
+    float BtV[NU][7];  // columns q (0..3) and v (4..6) of B^T V
+#pragma unroll
+    for (int c = 0; c < 7; ++c) {
+      const int col = c < 4 ? 3 + c : 7 + (c - 4);
+      float acc = bvf(J, 0) * V[7][col];
+      acc = fmaf(bvf(J, 1), V[8][col], acc);
+      BtV[0][c] = fmaf(bvf(J, 2), V[9][col], acc);
+#pragma unroll
+      for (int kk = 0; kk < 3; ++kk) {
+        float a2 = bqw(J, 0, kk) * V[3][col];
+#pragma unroll
+        for (int m = 1; m < 4; ++m) a2 = fmaf(bqw(J, m, kk), V[3 + m][col], a2);
+        BtV[1 + kk][c] = a2;
+      }
+    }
+#pragma unroll
+    for (int a = 0; a < NU; ++a) {
+      float acc = BtV[a][4] * bvf(J, 0);
+      acc = fmaf(BtV[a][5], bvf(J, 1), acc);
+      acc = fmaf(BtV[a][6], bvf(J, 2), acc);
+      Quu[a][0] = (Ct[(NX + a) * NT + NX] + acc) + (a == 0 ? reg : 0.0f);
+#pragma unroll
+      for (int kk = 0; kk < 3; ++kk) {
+        float a2 = BtV[a][0] * bqw(J, 0, kk);
+#pragma unroll
+        for (int m = 1; m < 4; ++m) a2 = fmaf(BtV[a][m], bqw(J, m, kk), a2);
+        Quu[a][1 + kk] = (Ct[(NX + a) * NT + NX + 1 + kk] + a2) + (a == 1 + kk ? reg : 0.0f);
+      }
+    }
+  }
+  // ---- q_x = l_x + A^T v ; q_u = l_u + B^T v ------------------------------
+  float qx[NX], qu[NU];
+#pragma unroll
+  for (int j = 0; j < 3; ++j) qx[j] = lx[j] + v[j];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float acc = aqq(J, 0, j) * v[3];
+#pragma unroll
+    for (int m = 1; m < 4; ++m) acc = fmaf(aqq(J, m, j), v[3 + m], acc);
+#pragma unroll
+    for (int n = 0; n < 3; ++n) acc = fmaf(avq(J, n, j), v[7 + n], acc);
+    qx[3 + j] = lx[3 + j] + acc;
+  }
+#pragma unroll
+  for (int j = 0; j < 3; ++j) qx[7 + j] = lx[7 + j] + fmaf(J.dt, v[j], v[7 + j]);
+  {
+    float acc = bvf(J, 0) * v[7];
+    acc = fmaf(bvf(J, 1), v[8], acc);
+    acc = fmaf(bvf(J, 2), v[9], acc);
+    qu[0] = lu[0] + acc;
+#pragma unroll
+    for (int kk = 0; kk < 3; ++kk) {
+      float a2 = bqw(J, 0, kk) * v[3];
+#pragma unroll
+      for (int m = 1; m < 4; ++m) a2 = fmaf(bqw(J, m, kk), v[3 + m], a2);
+      qu[1 + kk] = lu[1 + kk] + a2;
+    }
+  }
+  // ---- P = A^T V in place (column by column) ------------------------------
+#pragma unroll
+  for (int c = 0; c < NX; ++c) {
+    float t4[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float acc = aqq(J, 0, j) * V[3][c];
+#pragma unroll
+      for (int m = 1; m < 4; ++m) acc = fmaf(aqq(J, m, j), V[3 + m][c], acc);
+#pragma unroll
+      for (int n = 0; n < 3; ++n) acc = fmaf(avq(J, n, j), V[7 + n][c], acc);
+      t4[j] = acc;
+    }
+#pragma unroll
+    for (int j = 0; j < 3; ++j) V[7 + j][c] = fmaf(J.dt, V[j][c], V[7 + j][c]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) V[3 + j][c] = t4[j];
+  }
+  // ---- Q_xu = l_xu + P B ; Q_xx = l_xx + P A (row by row, in place) --------
+  float Qxu[NX][NU];
+#pragma unroll
+  for (int r = 0; r < NX; ++r) {
+    const float* Cr = Ct + r * NT;
+    {
+      float acc = V[r][7] * bvf(J, 0);
+      acc = fmaf(V[r][8], bvf(J, 1), acc);
+      acc = fmaf(V[r][9], bvf(J, 2), acc);
+      Qxu[r][0] = Cr[NX] + acc;
+#pragma unroll
+      for (int kk = 0; kk < 3; ++kk) {
+        float a2 = V[r][3] * bqw(J, 0, kk);
+#pragma unroll
+        for (int m = 1; m < 4; ++m) a2 = fmaf(V[r][3 + m], bqw(J, m, kk), a2);
+        Qxu[r][1 + kk] = Cr[NX + 1 + kk] + a2;
+      }
+    }
+    float t4[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float acc = V[r][3] * aqq(J, 0, j);
+#pragma unroll
+      for (int m = 1; m < 4; ++m) acc = fmaf(V[r][3 + m], aqq(J, m, j), acc);
+#pragma unroll
+      for (int n = 0; n < 3; ++n) acc = fmaf(V[r][7 + n], avq(J, n, j), acc);
+      t4[j] = acc;
+    }
+#pragma unroll
+    for (int j = 0; j < 3; ++j) V[r][7 + j] = fmaf(J.dt, V[r][j], V[r][7 + j]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) V[r][3 + j] = t4[j];
+#pragma unroll
+    for (int c = 0; c < NX; ++c) V[r][c] = Cr[c] + V[r][c];
+  }
+  // ---- gains ---------------------------------------------------------------
+  bool ok;
+  Chol4 L;
+  float Mi[NU][NU];
+  {
+    float Qs[NU][NU];
+#pragma unroll
+    for (int a = 0; a < NU; ++a)
+#pragma unroll
+      for (int b = 0; b < NU; ++b) {
+        if (MASKED) {
+          const bool ta = (tight >> a) & 1u, tb = (tight >> b) & 1u;
+          float val = (ta || tb) ? 0.0f : Quu[a][b];
+          if (a == b && ta) val = val + 1.0f;
+          Qs[a][b] = val + (a == b ? 1e-8f * reg : 0.0f);
+        } else {
+          Qs[a][b] = Quu[a][b] + (a == b ? reg : 0.0f);
+        }
+      }
+    ok = chol4(Qs, L);
+    if (!ok) svd_inverse4(Qs, Mi);
+  }
+  auto solve = [&](const float (&rhs)[NU], float (&out)[NU]) {
+    if (ok) {
+      chol4_solve(L, rhs, out);
+    } else {
+#pragma unroll
+      for (int a = 0; a < NU; ++a) {
+        float acc = Mi[a][0] * rhs[0];
+#pragma unroll
+        for (int b = 1; b < NU; ++b) acc = fmaf(Mi[a][b], rhs[b], acc);
+        out[a] = acc;
+      }
+    }
+  };
+#pragma unroll
+  for (int j = 0; j < NX; ++j) {
+    float rhs[NU], sol[NU];
+#pragma unroll
+    for (int a = 0; a < NU; ++a) rhs[a] = (MASKED && ((tight >> a) & 1u)) ? 0.0f : Qxu[j][a];
+    solve(rhs, sol);
+#pragma unroll
+    for (int a = 0; a < NU; ++a) K[a][j] = -sol[a];
+  }
+  {
+    float rhs[NU], sol[NU];
+#pragma unroll
+    for (int a = 0; a < NU; ++a) rhs[a] = (MASKED && ((tight >> a) & 1u)) ? 0.0f : qu[a];
+    solve(rhs, sol);
+#pragma unroll
+    for (int a = 0; a < NU; ++a) k[a] = -sol[a];
+  }
+  // ---- value update --------------------------------------------------------
+  float w[NU];  // backward: Q_uu k + q_u
+  if (MASKED) {
+#pragma unroll
+    for (int a = 0; a < NU; ++a) {
+      float acc = Quu[a][0] * k[0];
+#pragma unroll
+      for (int b = 1; b < NU; ++b) acc = fmaf(Quu[a][b], k[b], acc);
+      w[a] = acc + qu[a];
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < NX; ++r) {
+    float Z[NU];  // row r of K^T Q_uu
+#pragma unroll
+    for (int a = 0; a < NU; ++a) {
+      float acc = K[0][r] * Quu[0][a];
+#pragma unroll
+      for (int b = 1; b < NU; ++b) acc = fmaf(K[b][r], Quu[b][a], acc);
+      Z[a] = acc;
+    }
+    // v
+    float vk;
+    if (MASKED) {
+      float t2 = K[0][r] * w[0];
+#pragma unroll
+      for (int a = 1; a < NU; ++a) t2 = fmaf(K[a][r], w[a], t2);
+      float t3 = Qxu[r][0] * k[0];
+#pragma unroll
+      for (int a = 1; a < NU; ++a) t3 = fmaf(Qxu[r][a], k[a], t3);
+      vk = (qx[r] + t2) + t3;
+    } else {
+      float t1 = Z[0] * k[0];
+#pragma unroll
+      for (int a = 1; a < NU; ++a) t1 = fmaf(Z[a], k[a], t1);
+      float t2 = K[0][r] * qu[0];
+#pragma unroll
+      for (int a = 1; a < NU; ++a) t2 = fmaf(K[a][r], qu[a], t2);
+      float t3 = Qxu[r][0] * k[0];
+#pragma unroll
+      for (int a = 1; a < NU; ++a) t3 = fmaf(Qxu[r][a], k[a], t3);
+      vk = ((qx[r] + t1) + t2) + t3;
+    }
+    v[r] = vk;
+#pragma unroll
+    for (int c = 0; c < NX; ++c) {
+      float t1 = Z[0] * K[0][c];
+#pragma unroll
+      for (int a = 1; a < NU; ++a) t1 = fmaf(Z[a], K[a][c], t1);
+      float t2 = K[0][r] * Qxu[c][0];
+#pragma unroll
+      for (int a = 1; a < NU; ++a) t2 = fmaf(K[a][r], Qxu[c][a], t2);
+      float t3 = Qxu[r][0] * K[0][c];
+#pragma unroll
+      for (int a = 1; a < NU; ++a) t3 = fmaf(Qxu[r][a], K[a][c], t3);
+      V[r][c] = ((V[r][c] + t1) + t2) + t3;
+    }
+  }
+  return ok;
+}
+
+// --------------------------------------------------------------------------
+// TMA staging of C[b0:b0+32, t] (bulk tensor copies into shared memory)
+// --------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+// Bounded wait: returns false if the phase did not complete within WAIT_LIMIT polls.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* tm, uint64_t* bar, int c0, int c1,
+                                            int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* tm, const void* src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tm)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Double-buffered stream of C_t slabs for one warp of 32 batch elements.
+struct CPipe {
+  float* buf;         // [2][CSLAB]
+  uint64_t* bar;      // [2]
+  uint32_t parity;    // bit s: phase parity to wait for on bar[s]
+  const CUtensorMap* tm;
+  int b0;
+
+  __device__ __forceinline__ void issue(int slot, int t) {
+    mbar_expect_tx(&bar[slot], SLAB_BYTES);
+    tma_load_3d(buf + slot * CSLAB, tm, &bar[slot], 0, t, b0);
+  }
+  // Runs body(t, Crow) for t over [0, T) (reverse order if rev), with Crow
+  // pointing at this lane's 196-float C[b, t] block in shared memory.
+  // Returns false (after draining in-flight copies, bounded) on a timeout.
+  template <class F>
+  __device__ __forceinline__ bool run(int T, bool rev, F&& body) {
+    const int lane = threadIdx.x;
+    if (lane == 0) {
+      issue(0, rev ? T - 1 : 0);
+      if (T > 1) issue(1, rev ? T - 2 : 1);
+    }
+    __syncwarp();
+    for (int s = 0; s < T; ++s) {
+      const int slot = s & 1;
+      const bool ok = mbar_wait(&bar[slot], (parity >> slot) & 1u);
+      if (!__all_sync(FULL, ok)) {
+        // Drain the copies still in flight (bounded) before giving up.
+        for (int r = s; r < T && r < s + 2; ++r) mbar_wait(&bar[r & 1], (parity >> (r & 1)) & 1u);
+        return false;
+      }
+      parity ^= (1u << slot);
+      body(rev ? T - 1 - s : s, buf + slot * CSLAB + lane * CBLK);
+      __syncwarp();
+      if (lane == 0 && s + 2 < T) {
+        fence_proxy_async();
+        issue(slot, rev ? T - 3 - s : s + 2);
+      }
+      __syncwarp();
+    }
+    return true;
+  }
+};
+
+}  // namespace ilqr

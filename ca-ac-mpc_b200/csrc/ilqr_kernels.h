@@ -1,0 +1,90 @@
+// ilqr_kernels.h -- host-side launch interface shared by the .cu files.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define ILQR_MAX_ALPHAS_DEV 8
+
+namespace ilqr {
+
+struct SolveParams {
+  const float* x0;
+  const float* U_init;
+  const float* c;
+  const float* C_f;
+  const float* c_f;
+  const float* x_ref;
+  const float* u_ref;
+  const float* u_min;
+  const float* u_max;
+  const int8_t* forced;
+  float* X;
+  float* U;
+  uint8_t* tight;
+  int8_t* trace;
+  int32_t* iters;
+  uint32_t* status;
+  float* best_cost;
+  int32_t* stall_iter;
+  float* stall_gap;
+  float* ws;
+  int64_t B;
+  int64_t S;  // workspace element stride (B rounded up to 32)
+  int T;
+  int max_iter;
+  float dt;
+  float reg;
+  float alphas[ILQR_MAX_ALPHAS_DEV];
+  int n_alpha;
+  int has_bounds;
+};
+
+struct BackwardParams {
+  const float* X;
+  const float* U;
+  const float* C_f;
+  const float* x_ref;
+  const float* u_ref;
+  const uint8_t* tight;
+  const float* gX;
+  const float* gU;
+  float* g_x0;
+  float* g_c;
+  float* g_Cf;
+  float* g_cf;
+  float* g_xref;
+  float* g_uref;
+  float* ws;
+  int64_t B;
+  int64_t S;
+  int T;
+  float dt;
+  float reg;
+  int write_gC;
+};
+
+// Workspace floats per element slot (interleaved layout).
+inline int64_t solve_ws_fields(int T) { return (int64_t)(T + 1) * 10 + (int64_t)T * (4 + 40 + 4); }
+inline int64_t backward_ws_fields(int T) { return (int64_t)T * (40 + 4); }
+inline int64_t ws_stride(int64_t B) { return (B + 31) / 32 * 32; }
+
+size_t solve_smem_bytes();
+size_t backward_smem_bytes();
+cudaError_t launch_solve(const CUtensorMap& tmC, const SolveParams& p, cudaStream_t stream);
+cudaError_t launch_backward(const CUtensorMap& tmC, const CUtensorMap& tmG, const BackwardParams& p,
+                            cudaStream_t stream);
+cudaError_t launch_dynamics(const float* x, const float* u, int64_t n, float dt, float* xn, cudaStream_t s);
+cudaError_t launch_linearize(const float* X, const float* U, int64_t B, int T, float dt, float* A, float* Bm,
+                             cudaStream_t s);
+cudaError_t launch_adjoint_lqr(const float* A, const float* Bm, const float* l_xx, const float* l_uu,
+                               const float* l_xu, const float* l_x, const float* l_u, const float* l_xxN,
+                               const float* l_xN, const uint8_t* tight, int64_t B, int T, float reg, float* K,
+                               float* k, float* v0, cudaStream_t s);
+cudaError_t launch_assembly(const float* K, const float* k, const float* v0, const float* A, const float* Bm,
+                            const float* X, const float* U, const float* x_ref, const float* u_ref, int64_t B,
+                            int T, float* gC, float* gc, float* gx0, float* gxr, float* gur, float* gCf,
+                            float* gcf, cudaStream_t s);
+
+}  // namespace ilqr

@@ -1,0 +1,64 @@
+"""Algorithmic FLOP and byte counts of the fused solve / backward kernels.
+
+FLOPs count what the algorithm has to compute with the model's Jacobian
+structure exploited (A = I + dt J_x has 27 off-identity nonzeros, B 15), an
+FMA as 2, add/mul/sub/div/sqrt/sin/cos as 1, compares and negations as 0.
+Per batch element and time step (see ilqr_device.cuh / ilqr_solve.cu /
+ilqr_backward.cu for the expressions counted):
+
+  STEP   87   drone_step: p (6), |w| (6), normalise (3), half-angle (2),
+              sin/cos (2), em (3), quat_mult (28), thrust quaternion (4),
+              rotation (21), velocity (12)
+  CAND  102   candidate control: x - X (10), K dx (4 x 19), a k + a K dx, + U (16)
+  COST  435   tau^T C tau over a dense 14x14 block (14 x 27 + 28), c^T tau (27), sums
+  QUAD  392   l_tau = C tau + c (14 x 28)
+  JAC    57   nonzeros of A, B
+  RIC  5290   one Riccati step: B^T V (182), Q_uu (136), q_x (68), q_u (30),
+              A^T V (580), Q_xu (300), Q_xx (680), Cholesky (38), 11 solves
+              (352), K^T Q_uu (280), v (240), V (2400)
+  RICM 5250   masked adjoint step (backward)
+  SWEEP 229   dU = K dX + k (80), A dX + B dU (92), Jacobian (57)
+  GRADC 784   grad_C block (196 x 4)
+
+  solve(element)    = T (STEP + COST) + I T (RIC + QUAD + JAC)
+                      + I T n_alpha (CAND + STEP + COST) + A T (CAND + STEP)
+  backward(element) = T (RICM + JAC + SWEEP + GRADC)
+
+with I the iterations the element ran and A the accepted ones.
+
+Compulsory bytes (fp32, read once / written once, zero references and
+terminal cost as on the FastMPC surface):
+  solve    = 40 (x0) + T (16 U_init + 784 C + 56 c) + 40 (T+1) X + T (16 U + 4 tight)
+  backward = 40 (T+1) X + T (16 U + 784 C + 4 tight) + 40 (T+1) dL/dX + 16 T dL/dU
+             + 40 grad_x0 + T (784 grad_C + 56 grad_c)
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+STEP, CAND, COST, QUAD, JAC = 87, 102, 435, 392, 57
+RIC, RICM, SWEEP, GRADC = 5290, 5250, 229, 784
+
+
+def solve_flops(T: int, n_alpha: int, iters, accepts) -> float:
+    """Total solve FLOPs for elements that ran `iters` iterations and accepted
+    `accepts` of them (arrays over the batch)."""
+    I = np.asarray(iters, dtype=np.float64)
+    A = np.asarray(accepts, dtype=np.float64)
+    per = (T * (STEP + COST) + I * T * (RIC + QUAD + JAC)
+           + I * T * n_alpha * (CAND + STEP + COST) + A * T * (CAND + STEP))
+    return float(per.sum())
+
+
+def backward_flops(T: int, B: int) -> float:
+    return float(B) * T * (RICM + JAC + SWEEP + GRADC)
+
+
+def solve_bytes(T: int, B: int) -> float:
+    return float(B) * (40 + T * (16 + 784 + 56) + 40 * (T + 1) + T * (16 + 4))
+
+
+def backward_bytes(T: int, B: int) -> float:
+    return float(B) * (40 * (T + 1) + T * (16 + 784 + 4) + 40 * (T + 1) + 16 * T + 40
+                       + T * (784 + 56))

@@ -1,0 +1,315 @@
+"""ctypes binding of libilqr_b200.so (the C ABI in include/ilqr_b200.h).
+
+Tensor-level wrappers: they check device/dtype/shape/contiguity, allocate the
+outputs and the scratch workspace through torch's caching allocator, enqueue
+the CUDA work on torch's current stream and map a non-zero status to a
+RuntimeError, as the reference extension's TORCH_CHECKs do
+(differentialMPCPerformance/cpp/drone_ilqr_ext.cpp:1080-1088). There is no CPU
+fallback: loading fails loudly if the library is missing, and every entry
+point requires CUDA tensors.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from typing import Optional, Sequence
+
+import torch
+
+NX, NU, N = 10, 4, 14
+NOT_RUN = -128
+DEFAULT_ALPHAS = (1.0, 0.8, 0.5, 0.2, 0.1)  # DifferentialMPC/controller.py:211
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libilqr_b200.so")
+
+_lib = None
+_lib_lock = threading.Lock()
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I32 = ctypes.c_int32
+_F = ctypes.c_float
+
+
+def lib():
+    """Load the solver library (once). Raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lib_lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with `python ca-ac-mpc_b200/csrc/build.py` "
+                "(or __graft_entry__.build()); there is no CPU fallback")
+        L = ctypes.CDLL(LIB_PATH)
+        sig = {
+            "ilqr_b200_abi_version": ([], _I32),
+            "ilqr_b200_status_string": ([_I32], ctypes.c_char_p),
+            "ilqr_b200_check_device": ([_I32], _I32),
+            "ilqr_b200_solve_workspace_size": ([_I64, _I32, ctypes.POINTER(ctypes.c_size_t)], _I32),
+            "ilqr_b200_backward_workspace_size": ([_I64, _I32, ctypes.POINTER(ctypes.c_size_t)], _I32),
+            "ilqr_b200_solve_f32": ([_P] * 10 + [_I64, _I32, _F, _I32, _F, _F, _P, _I32, _P]
+                                    + [_P] * 9 + [_P, ctypes.c_size_t, _P], _I32),
+            "ilqr_b200_backward_f32": ([_P] * 9 + [_I64, _I32, _F, _F] + [_P] * 7
+                                       + [_P, ctypes.c_size_t, _P], _I32),
+            "ilqr_b200_dynamics_f32": ([_P, _P, _I64, _F, _P, _P], _I32),
+            "ilqr_b200_linearize_f32": ([_P, _P, _I64, _I32, _F, _P, _P, _P], _I32),
+            "ilqr_b200_adjoint_lqr_f32": ([_P] * 10 + [_I64, _I32, _F, _P, _P, _P, _P], _I32),
+            "ilqr_b200_implicit_diff_assembly_f32": ([_P] * 9 + [_I64, _I32] + [_P] * 7 + [_P], _I32),
+        }
+        for name, (argt, rest) in sig.items():
+            fn = getattr(L, name)
+            fn.argtypes = argt
+            fn.restype = rest
+        if L.ilqr_b200_abi_version() != 1:
+            raise RuntimeError("libilqr_b200.so ABI version mismatch")
+        _lib = L
+    return _lib
+
+
+EXPORTED_SYMBOLS = (
+    "ilqr_b200_abi_version", "ilqr_b200_status_string", "ilqr_b200_check_device",
+    "ilqr_b200_solve_workspace_size", "ilqr_b200_backward_workspace_size",
+    "ilqr_b200_solve_f32", "ilqr_b200_backward_f32", "ilqr_b200_dynamics_f32",
+    "ilqr_b200_linearize_f32", "ilqr_b200_adjoint_lqr_f32",
+    "ilqr_b200_implicit_diff_assembly_f32",
+)
+
+
+def _check(status: int, what: str):
+    if status != 0:
+        msg = lib().ilqr_b200_status_string(status).decode()
+        raise RuntimeError(f"{what} failed: {msg} (status {status})")
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _req(t: torch.Tensor, name: str, shape, device, dtype=torch.float32):
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a tensor")
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor (no CPU path)")
+    if t.device != device:
+        raise RuntimeError(f"{name} is on {t.device}, expected {device}")
+    if t.dtype != dtype:
+        raise RuntimeError(f"{name} must be {dtype}, got {t.dtype}")
+    if tuple(t.shape) != tuple(shape):
+        raise RuntimeError(f"{name} must have shape {tuple(shape)}, got {tuple(t.shape)}")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+    return t
+
+
+def _opt(t, name, shape, device, dtype=torch.float32):
+    return None if t is None else _req(t, name, shape, device, dtype)
+
+
+_checked_devices = set()
+
+
+def _cuda_device(t, name):
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor: the solver has no CPU path")
+    return t.device
+
+
+def _device_ok(device: torch.device):
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _checked_devices:
+        _check(lib().ilqr_b200_check_device(idx), "device check")
+        _checked_devices.add(idx)
+
+
+def workspace_bytes(kind: str, B: int, T: int) -> int:
+    n = ctypes.c_size_t(0)
+    fn = lib().ilqr_b200_solve_workspace_size if kind == "solve" else lib().ilqr_b200_backward_workspace_size
+    _check(fn(B, T, ctypes.byref(n)), "workspace query")
+    return int(n.value)
+
+
+def solve(x0, U_init, C, c, C_final=None, c_final=None, x_ref=None, u_ref=None,
+          u_min=None, u_max=None, dt=0.05, max_iter=10, reg_eps=1e-6, converge_tol=1e-6,
+          alphas: Sequence[float] = DEFAULT_ALPHAS, forced_trace=None, want_trace=False,
+          want_stats=False):
+    """Batched iLQR solve (DifferentiableMPCController.solve_step semantics).
+
+    Returns dict(X [B,T+1,10], U [B,T,4], tight [B,T,4] uint8) plus, when
+    requested, trace [B,max_iter] int8 and per-element iters / status /
+    best_cost / stall_iter / stall_gap.
+    """
+    L = lib()
+    dev = _cuda_device(x0, "x0")
+    _device_ok(dev)
+    B = x0.shape[0]
+    T = U_init.shape[1]
+    _req(x0, "x0", (B, NX), dev)
+    _req(U_init, "U_init", (B, T, NU), dev)
+    _req(C, "C", (B, T, N, N), dev)
+    _req(c, "c", (B, T, N), dev)
+    _opt(C_final, "C_final", (B, N, N), dev)
+    _opt(c_final, "c_final", (B, N), dev)
+    _opt(x_ref, "x_ref", (B, T + 1, NX), dev)
+    _opt(u_ref, "u_ref", (B, T, NU), dev)
+    if (u_min is None) != (u_max is None):
+        raise RuntimeError("u_min and u_max must both be given or both be None")
+    _opt(u_min, "u_min", (NU,), dev)
+    _opt(u_max, "u_max", (NU,), dev)
+    _opt(forced_trace, "forced_trace", (B, max_iter), dev, torch.int8)
+    al = [float(a) for a in alphas]
+    if not 1 <= len(al) <= 8:
+        raise RuntimeError("between 1 and 8 line-search step sizes are supported")
+    if C_final is None and c_final is not None:
+        C_final = torch.zeros(B, N, N, device=dev)
+    X = torch.empty(B, T + 1, NX, device=dev)
+    U = torch.empty(B, T, NU, device=dev)
+    tight = torch.empty(B, T, NU, device=dev, dtype=torch.uint8)
+    out = dict(X=X, U=U, tight=tight)
+    trace = iters = status = best = s_it = s_gap = None
+    if want_trace:
+        trace = out["trace"] = torch.empty(B, max_iter, device=dev, dtype=torch.int8)
+    if want_stats:
+        iters = out["iters"] = torch.empty(B, device=dev, dtype=torch.int32)
+        status = out["status"] = torch.empty(B, device=dev, dtype=torch.int32)
+        best = out["best_cost"] = torch.empty(B, device=dev)
+        s_it = out["stall_iter"] = torch.empty(B, device=dev, dtype=torch.int32)
+        s_gap = out["stall_gap"] = torch.empty(B, device=dev)
+    nbytes = workspace_bytes("solve", B, T)
+    ws = torch.empty(max(nbytes, 1), device=dev, dtype=torch.uint8)
+    a_arr = (ctypes.c_float * len(al))(*al)
+    st = L.ilqr_b200_solve_f32(
+        _ptr(x0), _ptr(U_init), _ptr(C), _ptr(c), _ptr(C_final), _ptr(c_final), _ptr(x_ref),
+        _ptr(u_ref), _ptr(u_min), _ptr(u_max), B, T, float(dt), int(max_iter), float(reg_eps),
+        float(converge_tol), ctypes.cast(a_arr, ctypes.c_void_p), len(al), _ptr(forced_trace), _ptr(X), _ptr(U), _ptr(tight),
+        _ptr(trace), _ptr(iters), _ptr(status), _ptr(best), _ptr(s_it), _ptr(s_gap),
+        _ptr(ws), nbytes, _stream(dev))
+    _check(st, "ilqr_b200_solve_f32")
+    return out
+
+
+def backward(X, U, C, grad_X, grad_U, C_final=None, x_ref=None, u_ref=None, tight=None,
+             dt=0.05, reg_eps=1e-6, need=("x0", "C", "c")):
+    """Fused implicit-diff backward at a solved (X, U) (ILQRSolve.backward
+    semantics). `need` selects outputs among x0, C, c, C_final, c_final,
+    x_ref, u_ref; returns a dict with those keys."""
+    L = lib()
+    dev = _cuda_device(X, "X")
+    _device_ok(dev)
+    B, T1, _ = X.shape
+    T = T1 - 1
+    _req(X, "X", (B, T + 1, NX), dev)
+    _req(U, "U", (B, T, NU), dev)
+    _req(C, "C", (B, T, N, N), dev)
+    _req(grad_X, "grad_X", (B, T + 1, NX), dev)
+    _req(grad_U, "grad_U", (B, T, NU), dev)
+    _opt(C_final, "C_final", (B, N, N), dev)
+    _opt(x_ref, "x_ref", (B, T + 1, NX), dev)
+    _opt(u_ref, "u_ref", (B, T, NU), dev)
+    _opt(tight, "tight_mask", (B, T, NU), dev, torch.uint8)
+    shapes = dict(x0=(B, NX), C=(B, T, N, N), c=(B, T, N), C_final=(B, N, N), c_final=(B, N),
+                  x_ref=(B, T + 1, NX), u_ref=(B, T, NU))
+    out = {k: torch.empty(shapes[k], device=dev) for k in need}
+    nbytes = workspace_bytes("backward", B, T)
+    ws = torch.empty(max(nbytes, 1), device=dev, dtype=torch.uint8)
+    g = lambda k: _ptr(out.get(k))
+    st = L.ilqr_b200_backward_f32(
+        _ptr(X), _ptr(U), _ptr(C), _ptr(C_final), _ptr(x_ref), _ptr(u_ref), _ptr(tight),
+        _ptr(grad_X), _ptr(grad_U), B, T, float(dt), float(reg_eps),
+        g("x0"), g("C"), g("c"), g("C_final"), g("c_final"), g("x_ref"), g("u_ref"),
+        _ptr(ws), nbytes, _stream(dev))
+    _check(st, "ilqr_b200_backward_f32")
+    return out
+
+
+def dynamics(x, u, dt):
+    dev = _cuda_device(x, "x")
+    _device_ok(dev)
+    n = x.shape[0]
+    _req(x, "x", (n, NX), dev)
+    _req(u, "u", (n, NU), dev)
+    xn = torch.empty_like(x)
+    _check(lib().ilqr_b200_dynamics_f32(_ptr(x), _ptr(u), n, float(dt), _ptr(xn), _stream(dev)),
+           "ilqr_b200_dynamics_f32")
+    return xn
+
+
+def linearize(X, U, dt):
+    dev = _cuda_device(X, "X")
+    _device_ok(dev)
+    B, T = U.shape[:2]
+    _req(X, "X", (B, T + 1, NX), dev)
+    _req(U, "U", (B, T, NU), dev)
+    A = torch.empty(B, T, NX, NX, device=dev)
+    Bm = torch.empty(B, T, NX, NU, device=dev)
+    _check(lib().ilqr_b200_linearize_f32(_ptr(X), _ptr(U), B, T, float(dt), _ptr(A), _ptr(Bm),
+                                         _stream(dev)), "ilqr_b200_linearize_f32")
+    return A, Bm
+
+
+def adjoint_lqr(A, Bm, l_xx, l_uu, l_xu, l_x, l_u, l_xxN, l_xN, tight, reg_eps):
+    dev = _cuda_device(A, "A_lin")
+    _device_ok(dev)
+    B, T = A.shape[:2]
+    for t, nm, sh in ((A, "A_lin", (B, T, NX, NX)), (Bm, "Bm_lin", (B, T, NX, NU)),
+                      (l_xx, "l_xx", (B, T, NX, NX)), (l_uu, "l_uu", (B, T, NU, NU)),
+                      (l_xu, "l_xu", (B, T, NX, NU)), (l_x, "l_x", (B, T, NX)), (l_u, "l_u", (B, T, NU)),
+                      (l_xxN, "l_xxN", (B, NX, NX)), (l_xN, "l_xN", (B, NX))):
+        _req(t, nm, sh, dev)
+    _opt(tight, "tight_mask", (B, T, NU), dev, torch.uint8)
+    K = torch.empty(B, T, NU, NX, device=dev)
+    k = torch.empty(B, T, NU, device=dev)
+    v0 = torch.empty(B, NX, device=dev)
+    _check(lib().ilqr_b200_adjoint_lqr_f32(
+        _ptr(A), _ptr(Bm), _ptr(l_xx), _ptr(l_uu), _ptr(l_xu), _ptr(l_x), _ptr(l_u), _ptr(l_xxN),
+        _ptr(l_xN), _ptr(tight), B, T, float(reg_eps), _ptr(K), _ptr(k), _ptr(v0), _stream(dev)),
+        "ilqr_b200_adjoint_lqr_f32")
+    return K, k, v0
+
+
+def implicit_diff_assembly(K, k, v0, A, Bm, X, U, x_ref=None, u_ref=None, need_xref=False,
+                           need_uref=False, need_C_final=False, need_c_final=False):
+    dev = _cuda_device(K, "K")
+    _device_ok(dev)
+    B, T = K.shape[:2]
+    for t, nm, sh in ((K, "K", (B, T, NU, NX)), (k, "k", (B, T, NU)), (v0, "v0", (B, NX)),
+                      (A, "A_lin", (B, T, NX, NX)), (Bm, "Bm_lin", (B, T, NX, NU)),
+                      (X, "X", (B, T + 1, NX)), (U, "U", (B, T, NU))):
+        _req(t, nm, sh, dev)
+    _opt(x_ref, "x_ref", (B, T + 1, NX), dev)
+    _opt(u_ref, "u_ref", (B, T, NU), dev)
+    gC = torch.empty(B, T, N, N, device=dev)
+    gc = torch.empty(B, T, N, device=dev)
+    gx0 = torch.empty(B, NX, device=dev)
+    gxr = torch.empty(B, T + 1, NX, device=dev) if need_xref else None
+    gur = torch.empty(B, T, NU, device=dev) if need_uref else None
+    gCf = torch.empty(B, N, N, device=dev) if need_C_final else None
+    gcf = torch.empty(B, N, device=dev) if need_c_final else None
+    _check(lib().ilqr_b200_implicit_diff_assembly_f32(
+        _ptr(K), _ptr(k), _ptr(v0), _ptr(A), _ptr(Bm), _ptr(X), _ptr(U), _ptr(x_ref), _ptr(u_ref),
+        B, T, _ptr(gC), _ptr(gc), _ptr(gx0), _ptr(gxr), _ptr(gur), _ptr(gCf), _ptr(gcf),
+        _stream(dev)), "ilqr_b200_implicit_diff_assembly_f32")
+    return gC, gc, gx0, gxr, gur, gCf, gcf
+
+
+def converged_flag(stall_iter, stall_gap, status, max_iter, converge_tol):
+    """The reference's global `converged` (controller.py:396-423) from the
+    per-element stall iteration and gap: the loop breaks at s = max(stall_iter)
+    if the largest gap is below converge_tol, else at s + 2 if that is still
+    inside max_iter; a loop that runs out reports convergence iff X, U are
+    finite. One device reduction and one host read."""
+    if stall_iter.numel() == 0:
+        return True
+    s = int(stall_iter.max().item())
+    if s < max_iter:
+        gap = float(stall_gap.max().item())
+        if (gap == gap and gap < converge_tol) or s + 2 <= max_iter - 1:
+            return True
+    return not bool(((status & 2) != 0).any().item())

@@ -68,11 +68,15 @@ def _block_inputs(seed: int, block: int, T: int, target: str, r: float):
     return x0, diag, ref
 
 
-def make_inputs(B: int, T: int, seed: int = 0, target: str = "cube", r: float = 5.0):
+def make_inputs(B: int, T: int, seed: int = 0, target: str = "cube", r: float = 5.0,
+                offset: int = 0):
     """Solve inputs for a batch of B elements and horizon T (float32 numpy).
 
-    Returns dict(x0 [B,10], C [B,T,14,14], c [B,T,14], U_init [B,T,4]).
+    `offset` (a multiple of 1024) selects elements [offset, offset + B) of the
+    seeded stream. Returns dict(x0 [B,10], C [B,T,14,14], c [B,T,14], U_init [B,T,4]).
     """
+    assert offset % BLOCK == 0
+    b_off = offset // BLOCK
     x0 = np.empty((B, NX), dtype=np.float32)
     C = np.zeros((B, T, N, N), dtype=np.float32)
     c = np.empty((B, T, N), dtype=np.float32)
@@ -80,7 +84,7 @@ def make_inputs(B: int, T: int, seed: int = 0, target: str = "cube", r: float = 
     for blk in range((B + BLOCK - 1) // BLOCK):
         lo, hi = blk * BLOCK, min(B, (blk + 1) * BLOCK)
         n = hi - lo
-        bx0, bdiag, bref = _block_inputs(seed, blk, T, target, r)
+        bx0, bdiag, bref = _block_inputs(seed, blk + b_off, T, target, r)
         x0[lo:hi] = bx0[:n]
         d32 = bdiag[:n].astype(np.float32)
         C[lo:hi, :, idx, idx] = d32
@@ -95,13 +99,14 @@ def make_inputs(B: int, T: int, seed: int = 0, target: str = "cube", r: float = 
     return dict(x0=x0, C=C, c=c, U_init=U_init)
 
 
-def make_backward_seeds(B: int, T: int, seed: int = 1):
+def make_backward_seeds(B: int, T: int, seed: int = 1, offset: int = 0):
     """Upstream gradients dL/dX [B,T+1,10], dL/dU [B,T,4] ~ N(0,1)."""
+    assert offset % BLOCK == 0
     gX = np.empty((B, T + 1, NX), dtype=np.float32)
     gU = np.empty((B, T, NU), dtype=np.float32)
     for blk in range((B + BLOCK - 1) // BLOCK):
         lo, hi = blk * BLOCK, min(B, (blk + 1) * BLOCK)
-        rng = np.random.default_rng([seed, blk])
+        rng = np.random.default_rng([seed, blk + offset // BLOCK])
         gX[lo:hi] = rng.normal(size=(BLOCK, T + 1, NX))[: hi - lo]
         gU[lo:hi] = rng.normal(size=(BLOCK, T, NU))[: hi - lo]
     return gX, gU

@@ -1,0 +1,254 @@
+"""mpc.pytorch-style MPC operator backed by the B200 iLQR solver.
+
+Drop-in for the reference's differentialMPCPerformance/mpc_compat.py: same
+names (QuadCost, GradMethods, FastMPC, MPC, DroneMPCFunction), same call
+`MPC(n_state, n_ctrl, T, ...)(x_init, QuadCost(C, c), dx)` returning
+(x [T+1,B,nx], u [T,B,nu], objs [T,B]), same layout normalisation and
+defaults (mpc_compat.py:80-125, 453-616). Differentiable w.r.t. x_init, C and
+c (and C_final, c_final, x_ref, u_ref through DroneMPCFunction) iff
+torch.is_grad_enabled() and backprop; otherwise runs under inference_mode.
+
+Behind it: one fused CUDA kernel for the whole forward solve and one for the
+implicit-differentiation backward (ilqr_native.solve / .backward), with the
+reference DiffMPC's numerics (DifferentialMPC/controller.py): step-size grid
+(1, .8, .5, .2, .1) unless overridden (alphas= or ACMPC_DIFFMPC_ALPHAS),
+regularisation added twice in the gain solve, strict-improvement acceptance,
+isclose tight mask, masked adjoint Riccati with unmasked value update.
+"""
+
+from __future__ import annotations
+
+import os
+from enum import Enum
+from typing import NamedTuple, Optional, Union
+
+import torch
+from torch import Tensor, nn
+
+try:
+    from . import ilqr_native as _nat
+    from .drone_ilqr import load_drone_ilqr_ext
+except ImportError:
+    import ilqr_native as _nat
+    from drone_ilqr import load_drone_ilqr_ext
+
+HOVER_THRUST = 0.752 * 9.8066  # mpc_compat.py:117
+
+
+class QuadCost(NamedTuple):
+    """Quadratic cost: 0.5 * z^T C z + c^T z where z = [x; u]"""
+    C: Tensor  # [T, B, n, n] or [T, n, n] or [n, n]
+    c: Optional[Tensor] = None  # [T, B, n] or [T, n] or [n]
+
+
+class GradMethods(Enum):
+    AUTO_DIFF = 1
+    FINITE_DIFF = 2
+    ANALYTIC = 3
+    ANALYTIC_CHECK = 4
+
+
+def _outer(x: Tensor, y: Tensor) -> Tensor:
+    """Batched outer product: x[..., i] * y[..., j] -> [..., i, j]."""
+    return x.unsqueeze(-1) * y.unsqueeze(-2)
+
+
+# Cached zero tensors keyed by (device, dtype, shape); never written into, and
+# never returned as an output (mpc_compat.py:66-77).
+_ZERO_CACHE: dict = {}
+
+
+def _zeros(shape, device, dtype) -> Tensor:
+    key = (device, dtype, tuple(shape))
+    t = _ZERO_CACHE.get(key)
+    if t is None:
+        t = torch.zeros(shape, device=device, dtype=dtype)
+        _ZERO_CACHE[key] = t
+    return t
+
+
+def _normalize_cost(C: Tensor, c: Optional[Tensor], B: int, T: int, n: int,
+                    device, dtype) -> tuple:
+    """Bring (C, c) to [B, T, n, n] / [B, T, n] float32 contiguous (mpc_compat.py:80-96)."""
+    if C.ndim == 2:
+        C = C.unsqueeze(0).unsqueeze(0).expand(T, B, n, n)
+    elif C.ndim == 3:
+        C = C.unsqueeze(1).expand(T, B, n, n)
+    if c is None:
+        c = _zeros((T, B, n), device, dtype)
+    elif c.ndim == 1:
+        c = c.unsqueeze(0).unsqueeze(0).expand(T, B, n)
+    elif c.ndim == 2:
+        c = c.unsqueeze(1).expand(T, B, n)
+    return C.permute(1, 0, 2, 3).contiguous().float(), c.permute(1, 0, 2).contiguous().float()
+
+
+def _normalize_bounds(u_lower, u_upper, nu, device, dtype):
+    """Flatten box bounds to [nu] float32 (mpc_compat.py:99-110); (None, None)
+    when either is missing."""
+    if u_lower is None or u_upper is None:
+        return None, None
+
+    def _flatten(b: Tensor) -> Tensor:
+        if b.ndim == 3:
+            return b[0, 0, :].contiguous()
+        if b.ndim == 1:
+            return b.contiguous()
+        return b.flatten()[:nu].contiguous()
+    return (_flatten(u_lower).to(device=device, dtype=torch.float32).contiguous(),
+            _flatten(u_upper).to(device=device, dtype=torch.float32).contiguous())
+
+
+def _normalize_init(u_init, B, T, nu, device, dtype) -> Tensor:
+    """U_init as [B, T, nu] float32; hover thrust when absent (mpc_compat.py:113-125)."""
+    if u_init is None:
+        out = torch.zeros(B, T, nu, device=device, dtype=torch.float32)
+        out[:, :, 0] = HOVER_THRUST
+        return out
+    if u_init.ndim == 3:
+        out = u_init.permute(1, 0, 2)
+    elif u_init.shape == (nu, B):
+        out = u_init.t().unsqueeze(1).expand(B, T, nu)
+    else:
+        out = u_init.unsqueeze(0).expand(B, T, nu)
+    return out.to(device=device).contiguous().float()
+
+
+def _f32(t):
+    return None if t is None else t.to(torch.float32).contiguous()
+
+
+class DroneMPCFunction(torch.autograd.Function):
+    """Differentiable batched iLQR solve.
+
+    forward(x0 [B,10], C [B,T,n,n], c [B,T,n], C_final [B,n,n] or None,
+    c_final [B,n] or None, x_ref [B,T+1,nx] or None, u_ref [B,T,nu] or None,
+    solver_cfg) -> (X [B,T+1,nx], U [B,T,nu]), as the reference's
+    DroneMPCFunction (mpc_compat.py:128-185). backward runs the fused
+    implicit-diff kernel (ILQRSolve.backward semantics, controller.py:68-133):
+    gradients w.r.t. x0, C, c, C_final, c_final, x_ref, u_ref.
+    """
+
+    @staticmethod
+    def forward(ctx, x0, C_bt, c_bt, C_final, c_final, x_ref, u_ref, solver_cfg):
+        out = _nat.solve(
+            _f32(x0), _f32(solver_cfg["U_init"]), _f32(C_bt), _f32(c_bt), _f32(C_final),
+            _f32(c_final), _f32(x_ref), _f32(u_ref), solver_cfg.get("u_min"), solver_cfg.get("u_max"),
+            dt=solver_cfg["dt"], max_iter=solver_cfg["lqr_iter"], reg_eps=solver_cfg["eps"],
+            converge_tol=solver_cfg.get("converge_tol", 1e-6),
+            alphas=solver_cfg.get("alphas", _nat.DEFAULT_ALPHAS))
+        X, U = out["X"], out["U"]
+        ctx.save_for_backward(X, U, _f32(C_bt), _f32(C_final) if C_final is not None else None,
+                              _f32(x_ref) if x_ref is not None else None, out["tight"])
+        ctx.dt = float(solver_cfg["dt"])
+        ctx.reg_eps = float(solver_cfg.get("reg_eps", solver_cfg["eps"]))
+        return X, U
+
+    @staticmethod
+    def backward(ctx, grad_X, grad_U):
+        X, U, C_bt, C_final, x_ref, tight = ctx.saved_tensors
+        need = ctx.needs_input_grad
+        names = ("x0", "C", "c", "C_final", "c_final", "x_ref", "u_ref")
+        want = tuple(nm for nm, nd in zip(names, need[:7]) if nd)
+        if not want:
+            return (None,) * 8
+        gX = torch.zeros_like(X) if grad_X is None else grad_X.to(torch.float32).contiguous()
+        gU = torch.zeros_like(U) if grad_U is None else grad_U.to(torch.float32).contiguous()
+        g = _nat.backward(X, U, C_bt, gX, gU, C_final=C_final, x_ref=x_ref, tight=tight,
+                          dt=ctx.dt, reg_eps=ctx.reg_eps, need=want)
+        return tuple(g.get(nm) for nm in names) + (None,)
+
+
+class FastMPC(nn.Module):
+    """Drop-in replacement for mpc.pytorch's MPC class (mpc_compat.py:453-612).
+
+    Only u_lower/u_upper/u_init/lqr_iter/eps/backprop influence the solve, as
+    in the reference; the extra keyword `alphas` selects the line-search step
+    sizes (default DiffMPC's (1, .8, .5, .2, .1), or ACMPC_DIFFMPC_ALPHAS).
+    """
+
+    def __init__(self, n_state: int, n_ctrl: int, T: int, u_lower: Optional[Tensor] = None,
+                 u_upper: Optional[Tensor] = None, u_init: Optional[Tensor] = None,
+                 lqr_iter: int = 20, verbose: int = -1, exit_unconverged: bool = False,
+                 detach_unconverged: bool = True, linesearch_decay: float = 0.2,
+                 max_linesearch_iter: int = 10, grad_method: GradMethods = GradMethods.ANALYTIC,
+                 eps: float = 1e-6, n_batch: Optional[int] = None, backprop: bool = True,
+                 slew_rate_penalty: Optional[float] = None, prev_ctrl: Optional[Tensor] = None,
+                 alphas=None, **kwargs):
+        super().__init__()
+        if n_state != _nat.NX or n_ctrl != _nat.NU:
+            raise ValueError(f"the solver's model has n_state={_nat.NX}, n_ctrl={_nat.NU}")
+        self.n_state = n_state
+        self.n_ctrl = n_ctrl
+        self.T = T
+        self.u_lower = u_lower
+        self.u_upper = u_upper
+        self.u_init = u_init
+        self.lqr_iter = lqr_iter
+        self.verbose = verbose
+        self.eps = eps
+        self.n_batch = n_batch
+        self.backprop = backprop
+        self.alphas = tuple(alphas) if alphas is not None else None
+        self._ext = None
+        self._dt = 0.02
+        self._bounds_key = None
+        self._bounds = (None, None)
+
+    def _get_ext(self):
+        if self._ext is None:
+            self._ext = load_drone_ilqr_ext()
+        return self._ext
+
+    def _alphas(self):
+        if self.alphas is not None:
+            return self.alphas
+        env = os.environ.get("ACMPC_DIFFMPC_ALPHAS")
+        if env:
+            return tuple(float(x.strip()) for x in env.split(",") if x.strip())
+        return _nat.DEFAULT_ALPHAS
+
+    def _get_bounds(self, device, dtype):
+        lo, hi = self.u_lower, self.u_upper
+        key = (id(lo), getattr(lo, "_version", None), id(hi), getattr(hi, "_version", None), device)
+        if key != self._bounds_key:
+            self._bounds = _normalize_bounds(lo, hi, self.n_ctrl, device, dtype)
+            self._bounds_key = key
+        return self._bounds
+
+    def forward(self, x_init: Tensor, cost: Union[QuadCost, nn.Module], dx: nn.Module):
+        assert isinstance(cost, QuadCost), "Only QuadCost supported"
+        B = x_init.size(0)
+        T = self.T
+        nx, nu = self.n_state, self.n_ctrl
+        n = nx + nu
+        device = x_init.device
+        dtype = x_init.dtype
+        dt = getattr(dx, "dt", 0.02)
+        self._get_ext()
+        C_bt, c_bt = _normalize_cost(cost.C, cost.c, B, T, n, device, dtype)
+        u_min, u_max = self._get_bounds(device, dtype)
+        U_init = _normalize_init(self.u_init, B, T, nu, device, dtype)
+        x0 = x_init.float().contiguous()
+        cfg = {"U_init": U_init, "u_min": u_min, "u_max": u_max, "dt": float(dt),
+               "lqr_iter": self.lqr_iter, "eps": self.eps, "converge_tol": 1e-6,
+               "reg_eps": self.eps, "nx": nx, "nu": nu, "alphas": self._alphas()}
+        if torch.is_grad_enabled() and self.backprop:
+            X, U = DroneMPCFunction.apply(x0, C_bt, c_bt, None, None, None, None, cfg)
+        else:
+            with torch.inference_mode():
+                out = _nat.solve(x0, U_init, C_bt, c_bt, None, None, None, None, u_min, u_max,
+                                 dt=float(dt), max_iter=self.lqr_iter, reg_eps=self.eps,
+                                 converge_tol=1e-6, alphas=self._alphas())
+            X, U = out["X"], out["U"]
+        x_out = X.permute(1, 0, 2).contiguous()
+        u_out = U.permute(1, 0, 2).contiguous()
+        if dtype != torch.float32:
+            x_out = x_out.to(dtype)
+            u_out = u_out.to(dtype)
+        objs = torch.zeros(T, B, device=device, dtype=dtype)
+        return x_out, u_out, objs
+
+
+# Alias for drop-in replacement
+MPC = FastMPC

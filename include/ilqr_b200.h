@@ -1,0 +1,168 @@
+/*
+ * ilqr_b200.h -- C ABI of the B200 batched differentiable iLQR solver for the
+ * 10-state collective-thrust/body-rate quadrotor model.
+ *
+ * Every entry point takes plain device pointers to float32 arrays laid out
+ * exactly as the reference's torch extension lays out its tensors (row-major,
+ * batch first), sizes, and a cudaStream_t. Work is enqueued on that stream;
+ * nothing is synchronised. Outputs are caller-owned. Scratch memory is a
+ * caller-provided device workspace whose size the *_workspace_size query
+ * reports. Functions return an ilqr_status_t and never throw.
+ *
+ * Numerics follow the reference's DiffMPC PyTorch implementation
+ * (DifferentialMPC/controller.py) on the DroneDx CTBR model
+ * (acmpc_public-master/diff_mpc_drones/drone.py:409-540).
+ *
+ * Each declaration names the reference interface it replaces.
+ */
+#ifndef ILQR_B200_H
+#define ILQR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ILQR_B200_ABI_VERSION 1
+#define ILQR_NX 10
+#define ILQR_NU 4
+#define ILQR_N 14
+#define ILQR_MAX_ALPHAS 8
+#define ILQR_TRACE_NOT_RUN (-128)
+
+typedef enum {
+  ILQR_OK = 0,
+  ILQR_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad size, bad alphas */
+  ILQR_ERR_MISALIGNED = 2,       /* C / grad_C not 16-byte aligned */
+  ILQR_ERR_WORKSPACE = 3,        /* workspace missing or too small */
+  ILQR_ERR_CUDA = 4,             /* launch or driver-entry-point failure */
+  ILQR_ERR_UNSUPPORTED_DEVICE = 5
+} ilqr_status_t;
+
+/* Per-element status bits written to elem_status[b] by ilqr_b200_solve_f32. */
+#define ILQR_ELEM_CHOL_FALLBACK 1u /* a Q_uu Cholesky failed; SVD inverse used */
+#define ILQR_ELEM_NONFINITE 2u     /* X or U of the returned solution not finite */
+#define ILQR_ELEM_PIPE_TIMEOUT 4u  /* an on-chip copy wait gave up (results invalid) */
+
+int ilqr_b200_abi_version(void);
+const char* ilqr_b200_status_string(int status);
+
+/* Returns ILQR_OK if `device` is a compute-capability 10.0 GPU. */
+int ilqr_b200_check_device(int device);
+
+/* Device workspace needed by ilqr_b200_solve_f32 for a batch B and horizon T. */
+int ilqr_b200_solve_workspace_size(int64_t B, int32_t T, size_t* bytes);
+
+/*
+ * Full iLQR solve for a batch of B independent elements.
+ * Replaces drone_ilqr_solve (differentialMPCPerformance/cpp/drone_ilqr_ext.cpp:664-1064)
+ * with the semantics of DifferentiableMPCController.solve_step
+ * (DifferentialMPC/controller.py:303-435).
+ *
+ * Inputs (device, float32, row-major):
+ *   x0 [B,10], U_init [B,T,4], C [B,T,14,14] (16-byte aligned), c [B,T,14],
+ *   C_final [B,14,14] or NULL (zeros), c_final [B,14] or NULL (zeros),
+ *   x_ref [B,T+1,10] or NULL (zeros), u_ref [B,T,4] or NULL (zeros),
+ *   u_min [4], u_max [4] or both NULL (no control bounds),
+ *   forced_trace [B,max_iter] int8 or NULL: replay recorded line-search
+ *   decisions instead of deciding (j >= 0 accept candidate j; other negative
+ *   values reject and continue; ILQR_TRACE_NOT_RUN stop).
+ * alphas: HOST array of n_alpha (1..8) line-search step sizes.
+ * Outputs (device): X [B,T+1,10], U [B,T,4], tight_mask [B,T,4] uint8
+ *   (U within isclose(atol 1e-7, rtol 1e-5) of a bound).
+ * Optional outputs (device, NULL to skip): trace [B,max_iter] int8,
+ *   iters [B] int32 (iterations run), elem_status [B] uint32,
+ *   best_cost [B] float, stall_iter [B] int32 (first rejected iteration or
+ *   max_iter), stall_gap [B] float (|cost - best| at that rejection).
+ */
+int ilqr_b200_solve_f32(
+    const float* x0, const float* U_init, const float* C, const float* c,
+    const float* C_final, const float* c_final, const float* x_ref, const float* u_ref,
+    const float* u_min, const float* u_max,
+    int64_t B, int32_t T, float dt, int32_t max_iter, float reg_eps, float converge_tol,
+    const float* alphas, int32_t n_alpha, const int8_t* forced_trace,
+    float* X, float* U, uint8_t* tight_mask,
+    int8_t* trace, int32_t* iters, uint32_t* elem_status, float* best_cost,
+    int32_t* stall_iter, float* stall_gap,
+    void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* Device workspace needed by ilqr_b200_backward_f32. */
+int ilqr_b200_backward_workspace_size(int64_t B, int32_t T, size_t* bytes);
+
+/*
+ * Fused implicit-differentiation backward at a solved (X, U): masked adjoint
+ * Riccati, dX/dU sweep and gradient assembly in one kernel, with A_t, B_t
+ * recomputed from (X_t, U_t) instead of read from memory.
+ * Replaces DroneMPCFunction.backward (differentialMPCPerformance/mpc_compat.py:187-450)
+ * plus drone_backward_pass_batched and drone_implicit_diff_assembly
+ * (cpp/drone_ilqr_ext.cpp:1066-1177, 1221-1278), with the semantics of
+ * ILQRSolve.backward / _zero_constrained_lqr (DifferentialMPC/controller.py:68-133,1006-1131).
+ *
+ * Inputs: X [B,T+1,10], U [B,T,4], C [B,T,14,14] (16-byte aligned),
+ *   C_final [B,14,14] or NULL, x_ref [B,T+1,10] or NULL, u_ref [B,T,4] or NULL,
+ *   tight_mask [B,T,4] uint8 or NULL (none tight), grad_X [B,T+1,10], grad_U [B,T,4].
+ * Outputs (each NULL to skip): grad_x0 [B,10], grad_C [B,T,14,14] (16-byte
+ *   aligned), grad_c [B,T,14], grad_C_final [B,14,14], grad_c_final [B,14],
+ *   grad_x_ref [B,T+1,10] (row T is 0), grad_u_ref [B,T,4].
+ */
+int ilqr_b200_backward_f32(
+    const float* X, const float* U, const float* C, const float* C_final,
+    const float* x_ref, const float* u_ref, const uint8_t* tight_mask,
+    const float* grad_X, const float* grad_U,
+    int64_t B, int32_t T, float dt, float reg_eps,
+    float* grad_x0, float* grad_C, float* grad_c, float* grad_C_final,
+    float* grad_c_final, float* grad_x_ref, float* grad_u_ref,
+    void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/*
+ * One step of the quadrotor model, x_next = f(x, u), for n states.
+ * Replaces DroneDx.forward_CTBR (acmpc_public-master/diff_mpc_drones/drone.py:409-465)
+ * and the reference's device step (cpp/forward_pass_kernel.cu:66-115).
+ */
+int ilqr_b200_dynamics_f32(const float* x, const float* u, int64_t n, float dt,
+                           float* x_next, cudaStream_t stream);
+
+/*
+ * Discrete Jacobians A = I + dt J_x [B,T,10,10] and B = dt J_u [B,T,10,4] at
+ * (X_t, U_t), t < T. Replaces drone_step_jacobian_kernel
+ * (cpp/drone_kernels.cu:64-189) / DroneDx.grad_input (drone.py:524-540); used
+ * to return A_lin, B_lin from the drone_ilqr_solve surface.
+ */
+int ilqr_b200_linearize_f32(const float* X, const float* U, int64_t B, int32_t T, float dt,
+                            float* A, float* Bm, cudaStream_t stream);
+
+/*
+ * Masked adjoint Riccati for caller-supplied A [B,T,10,10], Bm [B,T,10,4],
+ * l_xx [B,T,10,10], l_uu [B,T,4,4], l_xu [B,T,10,4], l_x [B,T,10],
+ * l_u [B,T,4], l_xxN [B,10,10], l_xN [B,10], tight_mask [B,T,4] uint8 or NULL.
+ * Outputs K [B,T,4,10], k [B,T,4], v0 [B,10].
+ * Replaces drone_backward_pass_batched (cpp/drone_ilqr_ext.cpp:1066-1177),
+ * with _zero_constrained_lqr semantics (controller.py:1035-1110).
+ */
+int ilqr_b200_adjoint_lqr_f32(
+    const float* A, const float* Bm, const float* l_xx, const float* l_uu,
+    const float* l_xu, const float* l_x, const float* l_u, const float* l_xxN,
+    const float* l_xN, const uint8_t* tight_mask, int64_t B, int32_t T, float reg_eps,
+    float* K, float* k, float* v0, cudaStream_t stream);
+
+/*
+ * dX/dU sweep and gradient assembly from (K, k, v0) and A, Bm, X, U.
+ * Replaces drone_implicit_diff_assembly (cpp/drone_ilqr_ext.cpp:1221-1278)
+ * with ILQRSolve.backward semantics (controller.py:84-125). x_ref / u_ref may
+ * be NULL (zeros). Outputs as for ilqr_b200_backward_f32 (each NULL to skip).
+ */
+int ilqr_b200_implicit_diff_assembly_f32(
+    const float* K, const float* k, const float* v0, const float* A, const float* Bm,
+    const float* X, const float* U, const float* x_ref, const float* u_ref,
+    int64_t B, int32_t T,
+    float* grad_C, float* grad_c, float* grad_x0, float* grad_x_ref,
+    float* grad_u_ref, float* grad_C_final, float* grad_c_final, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ILQR_B200_H */

@@ -425,6 +425,8 @@ def solve(x0, U_init, C, c, C_f=None, c_f=None, x_ref=None, u_ref=None,
     stall_gap = np.zeros(nb, dtype=np.float64)
     chol_fail = np.zeros(nb, dtype=bool)
     for i in range(max_iter):
+        if forced is not None:
+            active &= np.asarray(forced)[:, i] != NOT_RUN
         if not active.any():
             break
         ids = np.nonzero(active)[0]
@@ -453,9 +455,6 @@ def solve(x0, U_init, C, c, C_f=None, c_f=None, x_ref=None, u_ref=None,
             j = np.where(improved, f, j)
             new = costs[np.arange(len(ids)), j]
             stop = np.zeros(len(ids), dtype=bool)
-            nxt = np.asarray(forced)[ids, i + 1] if i + 1 < max_iter else None
-            if nxt is not None:
-                stop = nxt == NOT_RUN
         iters[ids] += 1
         trace[ids, i] = np.where(improved, j, -(j + 1)).astype(np.int8)
         acc = ids[improved]
@@ -532,6 +531,12 @@ def zero_constrained_lqr(A, Bm, H_xx, H_uu, H_xu, grad_x, grad_u, tight,
         L, ok = chol4(Q_uu_reg)
         Kt = -chol_solve(L, Q_ux_m)
         kt = -chol_solve(L, q_u_m[..., None])[..., 0]
+        if not ok.all():
+            # controller.py:1089-1092: a failed Cholesky falls back to an LU
+            # solve (taken per element here; the reference takes it batch-wide).
+            bad = ~ok
+            Kt[bad] = -np.linalg.solve(Q_uu_reg[bad], Q_ux_m[bad])
+            kt[bad] = -np.linalg.solve(Q_uu_reg[bad], q_u_m[bad][..., None])[..., 0]
         K[:, t] = Kt
         k[:, t] = kt
         KtT = _mT(Kt)

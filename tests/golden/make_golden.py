@@ -145,7 +145,9 @@ def run_reference(drone, DM, inp, T, max_iter, alphas, dt, bounds, gX, gU,
             assert torch.equal(X[b].detach(), rec_X[i][b, j]), "X is not the accepted candidate"
             assert torch.equal(U[b].detach(), rec_U[i][b, j]), "U is not the accepted candidate"
     g = lambda v: v.grad.detach().numpy().copy()
-    return dict(refreeze_drift=np.array(drift), reimproved=np.array(reimproved), X=X.detach().numpy().copy(), U=U.detach().numpy().copy(), trace=trace,
+    costs_all = torch.stack(rec_costs).numpy() if rec_costs else np.zeros((0, B, len(alphas)), np.float32)
+    return dict(costs=costs_all, obj0=rec_obj[0].numpy().copy(),
+                refreeze_drift=np.array(drift), reimproved=np.array(reimproved), X=X.detach().numpy().copy(), U=U.detach().numpy().copy(), trace=trace,
                 best_cost=best.numpy().copy(), converged=np.array(converged),
                 tight=tight, n_iter_run=np.array(len(rec_costs)),
                 grad_x0=g(x0), grad_C=g(C), grad_c=g(c), grad_C_final=g(C_f),
@@ -162,6 +164,7 @@ CASES = {
     "asym_b8_t4": (None, 8, 4, 5, (1.0, 0.8, 0.5, 0.2, 0.1), True, "asym"),
     "nobox_b8_t5": (None, 8, 5, 6, (1.0, 0.8, 0.5, 0.2, 0.1), False, None),
     "b1_t1": (None, 1, 1, 3, (1.0, 0.8, 0.5, 0.2, 0.1), True, None),
+    "indef_b8_t4": (None, 8, 4, 3, (1.0, 0.8, 0.5, 0.2, 0.1), True, "indef"),
 }
 
 
@@ -173,6 +176,11 @@ def make_case(drone, DM, name):
     else:
         inp = wl.make_inputs(B, T, seed=3)
     extra = None
+    if kind == "indef":
+        # A negative control weight on some elements makes Q_uu indefinite, so
+        # the reference's Cholesky fails and its SVD inverse is used.
+        for b in range(0, B, 2):
+            inp["C"][b, :, 11, 11] = -0.05
     if kind in ("dense", "asym"):
         extra = wl.make_dense_costs(B, T, seed=11, asymmetric=(kind == "asym"))
         inp["C"], inp["c"] = extra.pop("C"), extra.pop("c")

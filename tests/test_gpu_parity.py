@@ -1,0 +1,234 @@
+"""GPU parity of the CUDA solver (through the C ABI) against the reference's
+golden vectors and the CPU oracle. Bars: 1e-4 on X, U and 1e-3 on gradients
+(per-element norm-wise relative error, tests/parity.py)."""
+
+import numpy as np
+import pytest
+import torch
+
+import drone_ilqr
+import ilqr_native as nat
+import ilqr_workload as wl
+import mpc_compat
+import oracle as O
+from parity import (GRAD_KEYS, STRICT_CASES, TOL_GRAD, TOL_XU, case_kwargs, certify_ties, load,
+                    max_rel, same_decisions)
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+KEYMAP = {"grad_x0": "x0", "grad_C": "C", "grad_c": "c", "grad_C_final": "C_final",
+          "grad_c_final": "c_final", "grad_xref": "x_ref", "grad_uref": "u_ref"}
+
+
+def g(a, dtype=torch.float32):
+    return None if a is None else torch.as_tensor(np.ascontiguousarray(a)).to(DEV, dtype)
+
+
+def gpu_solve(d, forced=None, **over):
+    kw = case_kwargs(d)
+    kw.update(over)
+    out = nat.solve(g(d["x0"]), g(d["U_init"]), g(d["C"]), g(d["c"]), g(kw["C_f"]), g(kw["c_f"]),
+                    g(kw["x_ref"]), g(kw["u_ref"]), g(kw["u_min"]), g(kw["u_max"]), dt=kw["dt"],
+                    max_iter=kw["max_iter"], reg_eps=kw["reg"], alphas=kw["alphas"],
+                    forced_trace=g(forced, torch.int8), want_trace=True, want_stats=True)
+    torch.cuda.synchronize()
+    return {k: v.cpu().numpy() for k, v in out.items()}, kw
+
+
+def gpu_backward(d, X, U, tight, kw, gX=None, gU=None):
+    need = tuple(KEYMAP.values())
+    out = nat.backward(g(X), g(U), g(d["C"]), g(d["gX"] if gX is None else gX),
+                       g(d["gU"] if gU is None else gU), C_final=g(kw["C_f"]), x_ref=g(kw["x_ref"]),
+                       u_ref=g(kw["u_ref"]), tight=g(tight, torch.uint8), dt=kw["dt"],
+                       reg_eps=kw["reg"], need=need)
+    torch.cuda.synchronize()
+    return {gk: out[nk].cpu().numpy() for gk, nk in KEYMAP.items()}
+
+
+def test_dynamics_and_linearize_match_reference():
+    d = load("dynamics_n64")
+    xn = nat.dynamics(g(d["x"]), g(d["u"]), float(d["dt"])).cpu().numpy()
+    assert max_rel(xn, d["x_next"]) <= 4e-7
+    X = np.concatenate([d["x"][:, None], np.zeros_like(d["x"])[:, None]], 1)
+    A, Bm = nat.linearize(g(X), g(d["u"][:, None]), float(d["dt"]))
+    assert max_rel(A.cpu().numpy()[:, 0], d["A"]) <= 1e-6
+    assert max_rel(Bm.cpu().numpy()[:, 0], d["B"]) <= 1e-6
+
+
+@pytest.mark.parametrize("name", STRICT_CASES)
+def test_replay_matches_reference(name):
+    """Replaying the reference's decisions: X, U within 1e-4, tight mask
+    identical, gradients at the solution within 1e-3."""
+    d = load(name)
+    r, kw = gpu_solve(d, forced=d["ref_trace"])
+    assert max_rel(r["X"], d["ref_X"]) <= TOL_XU
+    assert max_rel(r["U"], d["ref_U"]) <= TOL_XU
+    assert np.array_equal(r["tight"].astype(bool), d["ref_tight"])
+    gr = gpu_backward(d, r["X"], r["U"], r["tight"], kw)
+    for k in GRAD_KEYS:
+        assert max_rel(gr[k], d["ref_" + k]) <= TOL_GRAD, k
+
+
+@pytest.mark.parametrize("name", STRICT_CASES)
+def test_backward_at_reference_solution(name):
+    d = load(name)
+    kw = case_kwargs(d)
+    gr = gpu_backward(d, d["ref_X"], d["ref_U"], d["ref_tight"].astype(np.uint8), kw)
+    for k in GRAD_KEYS:
+        assert max_rel(gr[k], d["ref_" + k]) <= TOL_GRAD, k
+
+
+@pytest.mark.parametrize("name", STRICT_CASES)
+def test_free_run(name):
+    """Free-running GPU solve: (a) the oracle replaying the GPU's own decisions
+    reproduces its X, U within 1e-4; (b) every decision where the GPU parts
+    from the reference is an fp32 tie in the reference's candidate costs;
+    (c) elements that never part match the reference within 1e-4."""
+    d = load(name)
+    r, kw = gpu_solve(d)
+    o = O.solve(d["x0"], d["U_init"], d["C"], d["c"], forced=r["trace"], **kw)
+    assert max_rel(r["X"], o["X"]) <= TOL_XU
+    assert max_rel(r["U"], o["U"]) <= TOL_XU
+    n_div, fails = certify_ties(r["trace"], d)
+    assert not fails, fails
+    same = same_decisions(r["trace"], d["ref_trace"])
+    assert max_rel(r["X"][same], d["ref_X"][same]) <= TOL_XU
+    assert max_rel(r["U"][same], d["ref_U"][same]) <= TOL_XU
+    conv = nat.converged_flag(torch.tensor(r["stall_iter"]), torch.tensor(r["stall_gap"]),
+                              torch.tensor(r["status"]), kw["max_iter"], 1e-6)
+    ref_conv = O.global_converged_flag(o["stall_iter"], o["stall_gap"], kw["max_iter"], 1e-6, True)
+    assert conv == ref_conv
+
+
+def test_chol_fallback_path():
+    d = load("indef_b8_t4")
+    r, _ = gpu_solve(d, forced=d["ref_trace"])
+    assert (r["status"][::2] & 1).all() and not (r["status"][1::2] & 1).any()
+
+
+def test_long_horizon_never_improving_elements_exact():
+    d = load("cfg5_b16_t50")
+    r, _ = gpu_solve(d, forced=d["ref_trace"])
+    never = d["ref_trace"].max(axis=1) < 0
+    assert max_rel(r["X"][never], d["ref_X"][never]) <= 1e-6
+    assert np.array_equal(r["U"][never], d["ref_U"][never])
+
+
+def _dx():
+    return type("Dx", (), {"dt": wl.DT})()
+
+
+def test_fastmpc_autograd_end_to_end():
+    """FastMPC(...)(x_init, QuadCost(C, c), dx) with autograd: outputs equal
+    the direct solve, gradients match the oracle backward at the GPU's
+    solution, and the layouts are mpc.pytorch's [T, B, ...]."""
+    d = load("cfg1_b16_t5")
+    B, T = d["x0"].shape[0], d["U_init"].shape[1]
+    x0 = g(d["x0"]).requires_grad_(True)
+    C = g(d["C"]).permute(1, 0, 2, 3).contiguous().requires_grad_(True)
+    c = g(d["c"]).permute(1, 0, 2).contiguous().requires_grad_(True)
+    lo = g(np.broadcast_to(wl.U_MIN, (T, 1, 4)).copy())
+    hi = g(np.broadcast_to(wl.U_MAX, (T, 1, 4)).copy())
+    m = mpc_compat.MPC(10, 4, T, u_lower=lo, u_upper=hi, lqr_iter=int(d["max_iter"]), eps=1e-6)
+    x, u, objs = m(x0, mpc_compat.QuadCost(C, c), _dx())
+    assert x.shape == (T + 1, B, 10) and u.shape == (T, B, 4) and objs.shape == (T, B)
+    gX = g(d["gX"]).permute(1, 0, 2)
+    gU = g(d["gU"]).permute(1, 0, 2)
+    ((x * gX).sum() + (u * gU).sum()).backward()
+    r, kw = gpu_solve(d)
+    assert np.array_equal(x.detach().permute(1, 0, 2).cpu().numpy(), r["X"])
+    assert np.array_equal(u.detach().permute(1, 0, 2).cpu().numpy(), r["U"])
+    o = O.backward(r["X"], r["U"], d["C"], None, None, None, r["tight"], d["gX"], d["gU"],
+                   kw["dt"], kw["reg"])
+    assert max_rel(x0.grad.cpu().numpy(), o["grad_x0"]) <= TOL_GRAD
+    assert max_rel(C.grad.permute(1, 0, 2, 3).cpu().numpy(), o["grad_C"]) <= TOL_GRAD
+    assert max_rel(c.grad.permute(1, 0, 2).cpu().numpy(), o["grad_c"]) <= TOL_GRAD
+    with torch.no_grad():
+        x2, u2, _ = m(x0, mpc_compat.QuadCost(C, c), _dx())
+    assert torch.equal(x2, x.detach()) and torch.equal(u2, u.detach())
+
+
+def test_extension_surface():
+    """load_drone_ilqr_ext(): drone_ilqr_solve's 10-tuple, and the explicit-A/B
+    backward pair agreeing with the fused backward."""
+    d = load("cfg2_b32_t10")
+    B, T = d["x0"].shape[0], d["U_init"].shape[1]
+    ext = drone_ilqr.load_drone_ilqr_ext()
+    z = lambda *s: torch.zeros(*s, device=DEV)
+    res = ext.drone_ilqr_solve(g(d["x0"]), g(d["U_init"]), g(d["C"]), g(d["c"]), z(B, 14, 14),
+                               z(B, 14), z(B, T + 1, 10), z(B, T, 4), g(wl.U_MIN), g(wl.U_MAX),
+                               wl.DT, int(d["max_iter"]), 1e-6, 1e-6)
+    X, U, l_xx, l_uu, l_xu, l_xxN, A, Bm, tight, conv = res
+    assert X.shape == (B, T + 1, 10) and U.shape == (B, T, 4)
+    assert l_xx.shape == (B, T, 10, 10) and l_uu.shape == (B, T, 4, 4) and l_xu.shape == (B, T, 10, 4)
+    assert l_xxN.shape == (B, 10, 10) and A.shape == (B, T, 10, 10) and Bm.shape == (B, T, 10, 4)
+    assert tight.dtype == torch.bool and isinstance(conv, bool)
+    r, kw = gpu_solve(d)
+    assert np.array_equal(X.cpu().numpy(), r["X"])
+    gX, gU = g(d["gX"]), g(d["gU"])
+    K, k, v0 = ext.drone_backward_pass_batched(A, Bm, l_xx, l_uu, l_xu, -gX[:, :T], -gU, l_xxN,
+                                               -gX[:, -1], tight, 1e-6)
+    gC, gc, gx0, gxr, gur, gCf, gcf = ext.drone_implicit_diff_assembly(
+        K, k, v0, A, Bm, X, U, z(B, T + 1, 10), z(B, T, 4), True, True, True, True)
+    fused = gpu_backward(d, r["X"], r["U"], r["tight"], kw)
+    assert max_rel(gC.cpu().numpy(), fused["grad_C"]) <= TOL_GRAD
+    assert max_rel(gc.cpu().numpy(), fused["grad_c"]) <= TOL_GRAD
+    assert max_rel((-v0).cpu().numpy(), fused["grad_x0"]) <= TOL_GRAD
+    assert max_rel(gxr.cpu().numpy(), fused["grad_xref"]) <= TOL_GRAD
+    assert max_rel(gCf.cpu().numpy(), fused["grad_C_final"]) <= TOL_GRAD
+
+
+def test_batch_not_multiple_of_warp_and_prefix_independence():
+    """Elements are independent: the first 16 elements of a B=45 solve are
+    bit-identical to a B=16 solve; padding lanes never write."""
+    cfg, inp = wl.config_inputs("rollout_b16384_t20", B=45)
+    d45 = dict(inp, bounds=np.array(True), dt=np.array(wl.DT), max_iter=np.array(5),
+               reg=np.array(1e-6), alphas=np.array(cfg["alphas"], np.float32))
+    d16 = {k: (v[:16] if isinstance(v, np.ndarray) and v.ndim > 1 else v) for k, v in d45.items()}
+    r45, _ = gpu_solve(d45)
+    r16, _ = gpu_solve(d16)
+    for k in ("X", "U", "tight", "trace"):
+        assert np.array_equal(r45[k][:16], r16[k]), k
+
+
+def test_invalid_inputs_raise():
+    d = load("b1_t1")
+    with pytest.raises(RuntimeError, match="shape"):
+        nat.solve(g(d["x0"]), g(d["U_init"]), g(d["C"])[:, :, :13], g(d["c"]))
+    with pytest.raises(RuntimeError, match="float32"):
+        nat.solve(g(d["x0"]).double(), g(d["U_init"]), g(d["C"]), g(d["c"]))
+    C = torch.empty(1 * 1 * 14 * 14 + 1, device=DEV)[1:].view(1, 1, 14, 14)
+    C.copy_(g(d["C"]))
+    with pytest.raises(RuntimeError, match="aligned"):
+        nat.solve(g(d["x0"]), g(d["U_init"]), C, g(d["c"]))
+    with pytest.raises(RuntimeError, match="step sizes"):
+        nat.solve(g(d["x0"]), g(d["U_init"]), g(d["C"]), g(d["c"]), alphas=())
+
+
+def test_empty_batch():
+    z = lambda *s: torch.zeros(*s, device=DEV)
+    out = nat.solve(z(0, 10), z(0, 3, 4), z(0, 3, 14, 14), z(0, 3, 14))
+    assert out["X"].shape == (0, 4, 10)
+
+
+@pytest.mark.parametrize("B,T,iters", [(16384, 20, 5)])
+def test_training_scale_properties(B, T, iters):
+    """Full training-scale batch: deterministic, finite, its first 16 elements
+    equal the 16-element solve (which the replay tests pin to the reference),
+    and the backward is exactly linear in the upstream gradient (x2 scaling)."""
+    cfg, inp = wl.config_inputs("rollout_b16384_t20", B=B)
+    t = {k: g(v) for k, v in inp.items()}
+    args = (t["x0"], t["U_init"], t["C"], t["c"], None, None, None, None, g(wl.U_MIN), g(wl.U_MAX))
+    kw = dict(dt=wl.DT, max_iter=iters, alphas=cfg["alphas"], want_trace=True)
+    a = nat.solve(*args, **kw)
+    b = nat.solve(*args, **kw)
+    assert torch.equal(a["X"], b["X"]) and torch.equal(a["U"], b["U"])
+    assert torch.isfinite(a["X"]).all() and torch.isfinite(a["U"]).all()
+    small = load("cfg3_b16_t20")
+    r16, _ = gpu_solve(small)
+    assert np.array_equal(a["X"][:16].cpu().numpy(), r16["X"])
+    gX, gU = wl.make_backward_seeds(B, T)
+    g1 = nat.backward(a["X"], a["U"], t["C"], g(gX), g(gU), tight=a["tight"], dt=wl.DT)
+    g2 = nat.backward(a["X"], a["U"], t["C"], g(2 * gX), g(2 * gU), tight=a["tight"], dt=wl.DT)
+    for k in g1:
+        assert torch.equal(2 * g1[k], g2[k]), k
