@@ -63,6 +63,7 @@ const char* ilqr_b200_status_string(int status) {
     case ILQR_ERR_WORKSPACE: return "workspace missing or too small";
     case ILQR_ERR_CUDA: return "CUDA launch or driver entry point failure";
     case ILQR_ERR_UNSUPPORTED_DEVICE: return "device is not compute capability 10.0 (B200)";
+    case ILQR_ERR_NOALLOC_LIMIT: return "problem too large for the fixed scratch of the no-allocation entry point";
     default: return "unknown status";
   }
 }

@@ -75,7 +75,7 @@ EXPORTED_SYMBOLS = (
     "ilqr_b200_solve_workspace_size", "ilqr_b200_backward_workspace_size",
     "ilqr_b200_solve_f32", "ilqr_b200_backward_f32", "ilqr_b200_dynamics_f32",
     "ilqr_b200_linearize_f32", "ilqr_b200_adjoint_lqr_f32",
-    "ilqr_b200_implicit_diff_assembly_f32",
+    "ilqr_b200_implicit_diff_assembly_f32", "ilqr_b200_solve_f32_noalloc",
 )
 
 

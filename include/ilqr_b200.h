@@ -39,7 +39,8 @@ typedef enum {
   ILQR_ERR_MISALIGNED = 2,       /* C / grad_C not 16-byte aligned */
   ILQR_ERR_WORKSPACE = 3,        /* workspace missing or too small */
   ILQR_ERR_CUDA = 4,             /* launch or driver-entry-point failure */
-  ILQR_ERR_UNSUPPORTED_DEVICE = 5
+  ILQR_ERR_UNSUPPORTED_DEVICE = 5,
+  ILQR_ERR_NOALLOC_LIMIT = 6     /* problem needs more than the fixed no-allocation scratch */
 } ilqr_status_t;
 
 /* Per-element status bits written to elem_status[b] by ilqr_b200_solve_f32. */
@@ -88,6 +89,32 @@ int ilqr_b200_solve_f32(
     int8_t* trace, int32_t* iters, uint32_t* elem_status, float* best_cost,
     int32_t* stall_iter, float* stall_gap,
     void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/*
+ * ilqr_b200_solve_f32 for callers that cannot allocate device memory. This
+ * entry point has no counterpart in the reference: it exists for hosts that
+ * must not allocate GPU memory while running (a control loop whose memory
+ * budget is fixed at start-up, a plugin whose host owns the device
+ * allocator). Same arguments and results as ilqr_b200_solve_f32 minus the
+ * workspace: the scratch is a fixed ILQR_NOALLOC_SCRATCH_BYTES array inside
+ * this library that every GPU loading the library holds until exit. Problems
+ * whose ilqr_b200_solve_workspace_size exceeds it are rejected with
+ * ILQR_ERR_NOALLOC_LIMIT (at T = 20 that is B > 3584). The entry point
+ * allocates nothing. Its first call on a device looks up the array's device
+ * address, so make that first call before any stream capture. All calls
+ * share the array: calls that overlap on the GPU (other streams, other host
+ * threads) race on it and must be serialised by the caller.
+ */
+#define ILQR_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
+int ilqr_b200_solve_f32_noalloc(
+    const float* x0, const float* U_init, const float* C, const float* c,
+    const float* C_final, const float* c_final, const float* x_ref, const float* u_ref,
+    const float* u_min, const float* u_max,
+    int64_t B, int32_t T, float dt, int32_t max_iter, float reg_eps, float converge_tol,
+    const float* alphas, int32_t n_alpha, const int8_t* forced_trace,
+    float* X, float* U, uint8_t* tight_mask,
+    int8_t* trace, int32_t* iters, uint32_t* elem_status, float* best_cost,
+    int32_t* stall_iter, float* stall_gap, cudaStream_t stream);
 
 /* Device workspace needed by ilqr_b200_backward_f32. */
 int ilqr_b200_backward_workspace_size(int64_t B, int32_t T, size_t* bytes);
