@@ -49,6 +49,8 @@ def _args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--latency-reps", type=int, default=200)
+    ap.add_argument("--batch", type=int, default=None,
+                    help="elements per GPU (default: the workload's 16384); for profiling runs")
     return ap.parse_args()
 
 
@@ -203,6 +205,8 @@ def run_ours(args):
 
     cfg = wl.CONFIGS[WORKLOAD]
     B, T, iters, alphas = cfg["B"], cfg["T"], cfg["max_iter"], cfg["alphas"]
+    if args.batch is not None:
+        B = args.batch
     inp = wl.make_inputs(B, T, seed=rank, target=cfg["target"], r=cfg["r"])
     gXn, gUn = wl.make_backward_seeds(B, T, seed=1 + rank)
     d = {k: torch.from_numpy(v).to(dev) for k, v in inp.items()}
