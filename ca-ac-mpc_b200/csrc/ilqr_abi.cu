@@ -8,8 +8,8 @@
 #include <mutex>
 
 #include "ilqr_b200.h"
-#include "ilqr_device.cuh"
 #include "ilqr_kernels.h"
+#include "ilqr_team.cuh"
 
 namespace {
 
@@ -30,13 +30,14 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// View of a [B, T, 14, 14] float tensor as {196, T, B}, box {196, 1, 32}.
+// View of a [B, T, 14, 14] float tensor as {196, T, B}, box {196, 1, 6}:
+// one box is the C_t blocks of the six elements a warp solves.
 int encode_cost_map(CUtensorMap* tm, const float* base, int64_t B, int32_t T) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return ILQR_ERR_CUDA;
   const cuuint64_t dims[3] = {(cuuint64_t)ilqr::CBLK, (cuuint64_t)T, (cuuint64_t)B};
   const cuuint64_t strides[2] = {(cuuint64_t)ilqr::CBLK * 4u, (cuuint64_t)T * ilqr::CBLK * 4u};
-  const cuuint32_t box[3] = {(cuuint32_t)ilqr::CBLK, 1u, (cuuint32_t)ilqr::WARP};
+  const cuuint32_t box[3] = {(cuuint32_t)ilqr::CBLK, 1u, (cuuint32_t)ilqr::EPW};
   const cuuint32_t estr[3] = {1u, 1u, 1u};
   std::memset(tm, 0, sizeof(*tm));
   const CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,

@@ -1,47 +1,61 @@
 // ilqr_backward.cu -- fused implicit-differentiation backward pass.
 //
-// One CTA = one warp = 32 batch elements, one thread per element. Two passes
-// over the horizon:
-//   1. reverse: masked adjoint Riccati (controller.py:1035-1110) with A_t, B_t
-//      recomputed from (X_t, U_t) and l_xx, l_xu, l_uu read from the TMA-staged
-//      C_t slab; gains (K_t, k_t) go to an element-interleaved workspace.
-//   2. forward: dU = K dX + k, dX+ = A dX + B dU (controller.py:1121-1129) and
-//      the gradients of ILQRSolve.backward (controller.py:84-125). grad_C[b, t]
-//      (784 B per element and step) is written into a [32 x 196] shared-memory
-//      slab and stored with one TMA bulk tensor store per step.
-#include "ilqr_device.cuh"
+// One CTA = one warp = 6 batch elements, a 5-lane team per element (as the
+// solve kernel). Two passes over the horizon:
+//   1. reverse: masked adjoint Riccati (controller.py:1035-1110) split by rows
+//      of V across the team (ilqr_team.cuh), A_t, B_t recomputed from
+//      (X_t, U_t), l_xx / l_xu / l_uu read from the TMA-staged C_t slab; the
+//      gains go to an element-interleaved workspace.
+//   2. forward: dU = K dX + k, dX+ = A dX + B dU (controller.py:1121-1129),
+//      computed by every lane of the team, and the gradients of
+//      ILQRSolve.backward (controller.py:84-125) with the rows of grad_C[b, t]
+//      split across the team, written into the shared-memory slab and stored
+//      with one TMA bulk tensor store per step for the warp's six elements.
 #include "ilqr_kernels.h"
+#include "ilqr_team.cuh"
 
 namespace ilqr {
 
 namespace {
 
-__global__ void __launch_bounds__(WARP) backward_kernel(const __grid_constant__ CUtensorMap tmC,
-                                                        const __grid_constant__ CUtensorMap tmG,
-                                                        const BackwardParams p) {
+__device__ __forceinline__ float pick14(const float (&v)[NT], int i) {
+  float r = v[0];
+#pragma unroll
+  for (int j = 1; j < NT; ++j) r = (i == j) ? v[j] : r;
+  return r;
+}
+
+__global__ void __launch_bounds__(32, 19) backward_kernel(const __grid_constant__ CUtensorMap tmC,
+                                                          const __grid_constant__ CUtensorMap tmG,
+                                                          const BackwardParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
-  float* cbuf = reinterpret_cast<float*>(smem);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 2 * SLAB_BYTES);
+  float* slab = reinterpret_cast<float*>(smem);
+  float* xch = slab + SLAB_E * CBLK;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(xch + SLAB_E * XS);
   const int lane = threadIdx.x;
-  const int64_t b0 = (int64_t)blockIdx.x * WARP;
-  const int64_t b = b0 + lane;
-  const bool valid = b < p.B;
+  const int e = lane / TEAM;
+  const int m = lane - e * TEAM;
+  const int64_t b0 = (int64_t)blockIdx.x * EPW;
+  const int64_t b = b0 + e;
+  const bool valid = (e < EPW) && (b < p.B);
+  const int64_t bw = valid ? b : b0;
   const int T = p.T;
-  const int64_t S = p.S;
   const float dt = p.dt;
-  float* Kw = p.ws + b;
-  float* kw = p.ws + (int64_t)T * NU * NX * S + b;
-  auto Kat = [&](int t, int a, int j) -> float& { return Kw[(int64_t)(t * NU * NX + a * NX + j) * S]; };
-  auto kat = [&](int t, int a) -> float& { return kw[(int64_t)(t * NU + a) * S]; };
+  float* Kw = p.ws;
+  float* kw = p.ws + (int64_t)T * NU * NX * p.S;
+  auto Kat = [&](int t, int a, int j) -> float& { return Kw[(int64_t)(t * NU * NX + a * NX + j) * p.S + bw]; };
+  auto kat = [&](int t, int a) -> float& { return kw[(int64_t)(t * NU + a) * p.S + bw]; };
   auto ld = [&](const float* q, int64_t i) { return valid ? __ldg(q + i) : 0.0f; };
 
   if (lane == 0) {
-    mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
+    mbar_init(bar, 1);
     fence_mbar_init();
   }
   __syncwarp();
-  CPipe pipe{cbuf, bar, 0u, &tmC, (int)b0};
+  TeamPipe pipe{slab, bar, 0u, &tmC, (int)b0, true};
+  float* xc = xch + e * XS;
+  float* Ce = slab + e * CBLK;
+  const int ra = row_a(m), rb = row_b(m);
 
   const float* Xb = p.X + b * (int64_t)(T + 1) * NX;
   const float* Ub = p.U + b * (int64_t)T * NU;
@@ -50,50 +64,54 @@ __global__ void __launch_bounds__(WARP) backward_kernel(const __grid_constant__ 
   const float* Cf = (p.C_f != nullptr && valid) ? p.C_f + b * CBLK : nullptr;
 
   // ---- 1. masked adjoint Riccati, V_T = C_f[:nx,:nx], v_T = -dL/dX_T --------
-  float V[NX][NX], v[NX];
+  float Va[NX], Vb[NX];
+  float va_ = -ld(gXb, T * NX + ra), vb_ = -ld(gXb, T * NX + rb);
 #pragma unroll
-  for (int i = 0; i < NX; ++i) {
-    v[i] = -ld(gXb, T * NX + i);
-#pragma unroll
-    for (int j = 0; j < NX; ++j) V[i][j] = Cf ? __ldg(Cf + i * NT + j) : 0.0f;
+  for (int j = 0; j < NX; ++j) {
+    Va[j] = Cf ? __ldg(Cf + ra * NT + j) : 0.0f;
+    Vb[j] = Cf ? __ldg(Cf + rb * NT + j) : 0.0f;
   }
-  bool ok = pipe.run(T, true, [&](int t, const float* Crow) {
-    float xb[NX], ub[NU], lx[NX], lu[NU];
+  bool ok = pipe.run(T, true, [&](int t, auto&& next) {
+    float xb[NX], ub[NU];
 #pragma unroll
-    for (int i = 0; i < NX; ++i) {
-      xb[i] = ld(Xb, t * NX + i);
-      lx[i] = -ld(gXb, t * NX + i);
-    }
+    for (int i = 0; i < NX; ++i) xb[i] = ld(Xb, t * NX + i);
 #pragma unroll
-    for (int a = 0; a < NU; ++a) {
-      ub[a] = ld(Ub, t * NU + a);
-      lu[a] = -ld(gUb, t * NU + a);
-    }
+    for (int a = 0; a < NU; ++a) ub[a] = ld(Ub, t * NU + a);
+    const float lxa = -ld(gXb, t * NX + ra), lxb = -ld(gXb, t * NX + rb);
+    if (m < NU) xc[X_LU + m] = -ld(gUb, t * NU + m);
     uint32_t tight = 0;
     if (p.tight != nullptr && valid) {
 #pragma unroll
       for (int a = 0; a < NU; ++a) tight |= (p.tight[(b * T + t) * NU + a] != 0 ? 1u : 0u) << a;
     }
+    __syncwarp();
     const Jac J = drone_jac(xb, ub, dt);
-    float K[NU][NX], k[NU];
-    riccati_step<true>(V, v, J, Crow, lx, lu, p.reg, tight, K, k);
+    float Ka[NU], Kb[NU], k[NU];
+    team_riccati<true>(Va, Vb, va_, vb_, J, DenseC{Ce}, lxa, lxb, p.reg, tight, m, xc, next, Ka, Kb, k);
+    if (valid) {
 #pragma unroll
-    for (int a = 0; a < NU; ++a) {
+      for (int a = 0; a < NU; ++a) {
+        Kat(t, a, ra) = Ka[a];
+        Kat(t, a, rb) = Kb[a];
+      }
+      if (m == 0) {
 #pragma unroll
-      for (int j = 0; j < NX; ++j) Kat(t, a, j) = K[a][j];
-      kat(t, a) = k[a];
+        for (int a = 0; a < NU; ++a) kat(t, a) = k[a];
+      }
     }
   });
-  if (!ok) return;  // bounded wait gave up; outputs are left untouched
+  if (!ok) return;  // a bounded wait gave up; outputs are left untouched
   if (valid && p.g_x0 != nullptr) {
-#pragma unroll
-    for (int i = 0; i < NX; ++i) p.g_x0[b * NX + i] = -v[i];
+    p.g_x0[b * NX + ra] = -va_;
+    p.g_x0[b * NX + rb] = -vb_;
   }
+  __syncwarp();
 
   // ---- 2. tangent sweep and gradient assembly -------------------------------
   float dx[NX];
 #pragma unroll
   for (int i = 0; i < NX; ++i) dx[i] = 0.0f;
+  const int nrows = (m < NT - 2 * TEAM) ? 3 : 2;  // rows m, m+5, m+10 of grad_C
   for (int t = 0; t < T; ++t) {
     float z[NT], du[NU];
 #pragma unroll
@@ -113,41 +131,36 @@ __global__ void __launch_bounds__(WARP) backward_kernel(const __grid_constant__ 
 #pragma unroll
     for (int a = 0; a < NU; ++a) dtau[NX + a] = du[a];
     if (p.write_gC) {
-      const int slot = t & 1;
-      if (t >= 2) {
-        if (lane == 0) bulk_wait_read<1>();
+      if (t > 0) {
+        if (lane == 0) bulk_wait_read<0>();  // previous step's store has read the slab
         __syncwarp();
       }
-      float4* row = reinterpret_cast<float4*>(cbuf + slot * CSLAB + lane * CBLK);
+      // grad_C = -1/2 (dtau (x) z + z (x) dtau), z = [X_t; U_t] (controller.py:87-96)
+      for (int s = 0; s < nrows; ++s) {
+        const int i = m + TEAM * s;
+        const float di = pick14(dtau, i), zi = pick14(z, i);
+        float2* row = reinterpret_cast<float2*>(Ce + i * NT);
 #pragma unroll
-      for (int q = 0; q < CBLK / 4; ++q) {
-        float g[4];
-#pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          const int e = 4 * q + m, i = e / NT, j = e % NT;
-          g[m] = -0.5f * (dtau[i] * z[j] + z[i] * dtau[j]);
+        for (int j = 0; j < NT; j += 2) {
+          const float g0 = -0.5f * (di * z[j] + zi * dtau[j]);
+          const float g1 = -0.5f * (di * z[j + 1] + zi * dtau[j + 1]);
+          row[j / 2] = make_float2(g0, g1);
         }
-        row[q] = make_float4(g[0], g[1], g[2], g[3]);
       }
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) {
-        tma_store_3d(&tmG, cbuf + slot * CSLAB, 0, t, (int)b0);
+        tma_store_3d(&tmG, slab, 0, t, (int)b0);
         bulk_commit();
       }
     }
     if (valid) {
-      if (p.g_c != nullptr) {
-#pragma unroll
-        for (int i = 0; i < NT; ++i) p.g_c[(b * T + t) * NT + i] = -dtau[i];
-      }
-      if (p.g_xref != nullptr) {
-#pragma unroll
-        for (int i = 0; i < NX; ++i) p.g_xref[(b * (T + 1) + t) * NX + i] = dx[i];
-      }
-      if (p.g_uref != nullptr) {
-#pragma unroll
-        for (int a = 0; a < NU; ++a) p.g_uref[(b * T + t) * NU + a] = du[a];
+      for (int s = 0; s < nrows; ++s) {
+        const int i = m + TEAM * s;
+        const float di = pick14(dtau, i);
+        if (p.g_c != nullptr) p.g_c[(b * T + t) * NT + i] = -di;
+        if (i < NX && p.g_xref != nullptr) p.g_xref[(b * (T + 1) + t) * NX + i] = di;
+        if (i >= NX && p.g_uref != nullptr) p.g_uref[(b * T + t) * NU + (i - NX)] = di;
       }
     }
     float xs[NX], us[NU];
@@ -164,21 +177,33 @@ __global__ void __launch_bounds__(WARP) backward_kernel(const __grid_constant__ 
   if (p.write_gC && lane == 0) bulk_wait<0>();
   __syncwarp();
   if (!valid) return;
-  if (p.g_xref != nullptr) {
+  if (p.g_xref != nullptr && m == 0) {
 #pragma unroll
     for (int i = 0; i < NX; ++i) p.g_xref[(b * (T + 1) + T) * NX + i] = 0.0f;
   }
   if (p.g_Cf != nullptr || p.g_cf != nullptr) {
-    float e[NX];
+    float ev[NX];
 #pragma unroll
     for (int i = 0; i < NX; ++i)
-      e[i] = ld(Xb, T * NX + i) - (p.x_ref != nullptr ? __ldg(p.x_ref + (b * (T + 1) + T) * NX + i) : 0.0f);
+      ev[i] = ld(Xb, T * NX + i) - (p.x_ref != nullptr ? __ldg(p.x_ref + (b * (T + 1) + T) * NX + i) : 0.0f);
     if (p.g_Cf != nullptr) {
-      for (int i = 0; i < NT; ++i)
-        for (int j = 0; j < NT; ++j)
-          p.g_Cf[b * CBLK + i * NT + j] = (i < NX && j < NX) ? -0.5f * (dx[i] * e[j] + e[i] * dx[j]) : 0.0f;
+      for (int f = m; f < CBLK; f += TEAM) {
+        const int i = f / NT, j = f - i * NT;
+        float g = 0.0f;
+        if (i < NX && j < NX) {
+          float di = 0.0f, dj = 0.0f, ei = 0.0f, ej = 0.0f;
+#pragma unroll
+          for (int q = 0; q < NX; ++q) {
+            if (q == i) { di = dx[q]; ei = ev[q]; }
+            if (q == j) { dj = dx[q]; ej = ev[q]; }
+          }
+          g = -0.5f * (di * ej + ei * dj);
+        }
+        p.g_Cf[b * CBLK + f] = g;
+      }
     }
-    if (p.g_cf != nullptr) {
+    if (p.g_cf != nullptr && m == 0) {
+#pragma unroll
       for (int i = 0; i < NT; ++i) p.g_cf[b * NT + i] = i < NX ? -dx[i] : 0.0f;
     }
   }
@@ -186,14 +211,12 @@ __global__ void __launch_bounds__(WARP) backward_kernel(const __grid_constant__ 
 
 }  // namespace
 
-size_t backward_smem_bytes() { return 2 * SLAB_BYTES + 2 * sizeof(uint64_t); }
+size_t backward_smem_bytes() { return (size_t)SLAB_E * CBLK * 4 + (size_t)SLAB_E * XS * 4 + sizeof(uint64_t); }
 
 cudaError_t launch_backward(const CUtensorMap& tmC, const CUtensorMap& tmG, const BackwardParams& p,
                             cudaStream_t stream) {
   const size_t smem = backward_smem_bytes();
-  const unsigned grid = (unsigned)((p.B + WARP - 1) / WARP);
-  cudaError_t e = cudaFuncSetAttribute(backward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
+  const unsigned grid = (unsigned)((p.B + EPW - 1) / EPW);
   backward_kernel<<<grid, WARP, smem, stream>>>(tmC, tmG, p);
   return cudaGetLastError();
 }

@@ -17,9 +17,7 @@ constexpr int NX = 10;
 constexpr int NU = 4;
 constexpr int NT = 14;              // NX + NU
 constexpr int CBLK = NT * NT;       // floats of one C[b,t] block
-constexpr int WARP = 32;            // batch elements per CTA (one warp)
-constexpr int CSLAB = CBLK * WARP;  // floats of one staged C_t slab
-constexpr uint32_t SLAB_BYTES = CSLAB * 4u;
+constexpr int WARP = 32;            // threads per CTA (one warp)
 constexpr float MASS = 0.752f;      // drone.py:166
 constexpr float GZ = -9.8066f;      // drone.py:187
 constexpr unsigned FULL = 0xffffffffu;
@@ -259,258 +257,7 @@ static __device__ __noinline__ void svd_inverse4(const float (&M)[NU][NU], float
 }
 
 // --------------------------------------------------------------------------
-// One Riccati step with the sparse model Jacobians.
-//
-// Forward (MASKED=false), backward_lqr (DifferentialMPC/controller.py:697-723):
-//   Q_xx = l_xx + (A^T V) A        Q_xu = l_xu + (A^T V) B
-//   Q_uu = l_uu + (B^T V) B + reg I
-//   q_x = l_x + A^T v              q_u = l_u + B^T v
-//   [K | k] = -chol_solve(Q_uu + reg I, [Q_ux | q_u])   (reg added twice)
-//   V = Q_xx + (K^T Q_uu) K + K^T Q_ux + Q_xu K
-//   v = q_x + (K^T Q_uu) k + K^T q_u + Q_xu k
-// Backward (MASKED=true), _zero_constrained_lqr (controller.py:1035-1110):
-//   tight rows/cols of Q_uu zeroed, +1 on their diagonal, + (1e-8 reg) I;
-//   tight rows of Q_ux and entries of q_u zeroed for the solve only;
-//   V, v use the unmasked Q_uu, Q_ux, q_u, and v = q_x + K^T(Q_uu k + q_u) + Q_xu k.
-//
-// V is updated in place; the row (A^T .) and column (. A) transforms act on
-// one column / row at a time with four temporaries.
-// --------------------------------------------------------------------------
-template <bool MASKED>
-__device__ __forceinline__ bool riccati_step(float (&V)[NX][NX], float (&v)[NX], const Jac& J,
-                                             const float* __restrict__ Ct,
-                                             const float (&lx)[NX], const float (&lu)[NU],
-                                             float reg, uint32_t tight,
-                                             float (&K)[NU][NX], float (&k)[NU]) {
-  // ---- Q_uu = l_uu + (B^T V) B + reg I -----------------------------------
-  float Quu[NU][NU];
-  {
-    float BtV[NU][7];  // columns q (0..3) and v (4..6) of B^T V
-#pragma unroll
-    for (int c = 0; c < 7; ++c) {
-      const int col = c < 4 ? 3 + c : 7 + (c - 4);
-      float acc = bvf(J, 0) * V[7][col];
-      acc = fmaf(bvf(J, 1), V[8][col], acc);
-      BtV[0][c] = fmaf(bvf(J, 2), V[9][col], acc);
-#pragma unroll
-      for (int kk = 0; kk < 3; ++kk) {
-        float a2 = bqw(J, 0, kk) * V[3][col];
-#pragma unroll
-        for (int m = 1; m < 4; ++m) a2 = fmaf(bqw(J, m, kk), V[3 + m][col], a2);
-        BtV[1 + kk][c] = a2;
-      }
-    }
-#pragma unroll
-    for (int a = 0; a < NU; ++a) {
-      float acc = BtV[a][4] * bvf(J, 0);
-      acc = fmaf(BtV[a][5], bvf(J, 1), acc);
-      acc = fmaf(BtV[a][6], bvf(J, 2), acc);
-      Quu[a][0] = (Ct[(NX + a) * NT + NX] + acc) + (a == 0 ? reg : 0.0f);
-#pragma unroll
-      for (int kk = 0; kk < 3; ++kk) {
-        float a2 = BtV[a][0] * bqw(J, 0, kk);
-#pragma unroll
-        for (int m = 1; m < 4; ++m) a2 = fmaf(BtV[a][m], bqw(J, m, kk), a2);
-        Quu[a][1 + kk] = (Ct[(NX + a) * NT + NX + 1 + kk] + a2) + (a == 1 + kk ? reg : 0.0f);
-      }
-    }
-  }
-  // ---- q_x = l_x + A^T v ; q_u = l_u + B^T v ------------------------------
-  float qx[NX], qu[NU];
-#pragma unroll
-  for (int j = 0; j < 3; ++j) qx[j] = lx[j] + v[j];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    float acc = aqq(J, 0, j) * v[3];
-#pragma unroll
-    for (int m = 1; m < 4; ++m) acc = fmaf(aqq(J, m, j), v[3 + m], acc);
-#pragma unroll
-    for (int n = 0; n < 3; ++n) acc = fmaf(avq(J, n, j), v[7 + n], acc);
-    qx[3 + j] = lx[3 + j] + acc;
-  }
-#pragma unroll
-  for (int j = 0; j < 3; ++j) qx[7 + j] = lx[7 + j] + fmaf(J.dt, v[j], v[7 + j]);
-  {
-    float acc = bvf(J, 0) * v[7];
-    acc = fmaf(bvf(J, 1), v[8], acc);
-    acc = fmaf(bvf(J, 2), v[9], acc);
-    qu[0] = lu[0] + acc;
-#pragma unroll
-    for (int kk = 0; kk < 3; ++kk) {
-      float a2 = bqw(J, 0, kk) * v[3];
-#pragma unroll
-      for (int m = 1; m < 4; ++m) a2 = fmaf(bqw(J, m, kk), v[3 + m], a2);
-      qu[1 + kk] = lu[1 + kk] + a2;
-    }
-  }
-  // ---- P = A^T V in place (column by column) ------------------------------
-#pragma unroll
-  for (int c = 0; c < NX; ++c) {
-    float t4[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float acc = aqq(J, 0, j) * V[3][c];
-#pragma unroll
-      for (int m = 1; m < 4; ++m) acc = fmaf(aqq(J, m, j), V[3 + m][c], acc);
-#pragma unroll
-      for (int n = 0; n < 3; ++n) acc = fmaf(avq(J, n, j), V[7 + n][c], acc);
-      t4[j] = acc;
-    }
-#pragma unroll
-    for (int j = 0; j < 3; ++j) V[7 + j][c] = fmaf(J.dt, V[j][c], V[7 + j][c]);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) V[3 + j][c] = t4[j];
-  }
-  // ---- Q_xu = l_xu + P B ; Q_xx = l_xx + P A (row by row, in place) --------
-  float Qxu[NX][NU];
-#pragma unroll
-  for (int r = 0; r < NX; ++r) {
-    const float* Cr = Ct + r * NT;
-    {
-      float acc = V[r][7] * bvf(J, 0);
-      acc = fmaf(V[r][8], bvf(J, 1), acc);
-      acc = fmaf(V[r][9], bvf(J, 2), acc);
-      Qxu[r][0] = Cr[NX] + acc;
-#pragma unroll
-      for (int kk = 0; kk < 3; ++kk) {
-        float a2 = V[r][3] * bqw(J, 0, kk);
-#pragma unroll
-        for (int m = 1; m < 4; ++m) a2 = fmaf(V[r][3 + m], bqw(J, m, kk), a2);
-        Qxu[r][1 + kk] = Cr[NX + 1 + kk] + a2;
-      }
-    }
-    float t4[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float acc = V[r][3] * aqq(J, 0, j);
-#pragma unroll
-      for (int m = 1; m < 4; ++m) acc = fmaf(V[r][3 + m], aqq(J, m, j), acc);
-#pragma unroll
-      for (int n = 0; n < 3; ++n) acc = fmaf(V[r][7 + n], avq(J, n, j), acc);
-      t4[j] = acc;
-    }
-#pragma unroll
-    for (int j = 0; j < 3; ++j) V[r][7 + j] = fmaf(J.dt, V[r][j], V[r][7 + j]);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) V[r][3 + j] = t4[j];
-#pragma unroll
-    for (int c = 0; c < NX; ++c) V[r][c] = Cr[c] + V[r][c];
-  }
-  // ---- gains ---------------------------------------------------------------
-  bool ok;
-  Chol4 L;
-  float Mi[NU][NU];
-  {
-    float Qs[NU][NU];
-#pragma unroll
-    for (int a = 0; a < NU; ++a)
-#pragma unroll
-      for (int b = 0; b < NU; ++b) {
-        if (MASKED) {
-          const bool ta = (tight >> a) & 1u, tb = (tight >> b) & 1u;
-          float val = (ta || tb) ? 0.0f : Quu[a][b];
-          if (a == b && ta) val = val + 1.0f;
-          Qs[a][b] = val + (a == b ? 1e-8f * reg : 0.0f);
-        } else {
-          Qs[a][b] = Quu[a][b] + (a == b ? reg : 0.0f);
-        }
-      }
-    ok = chol4(Qs, L);
-    if (!ok) svd_inverse4(Qs, Mi);
-  }
-  auto solve = [&](const float (&rhs)[NU], float (&out)[NU]) {
-    if (ok) {
-      chol4_solve(L, rhs, out);
-    } else {
-#pragma unroll
-      for (int a = 0; a < NU; ++a) {
-        float acc = Mi[a][0] * rhs[0];
-#pragma unroll
-        for (int b = 1; b < NU; ++b) acc = fmaf(Mi[a][b], rhs[b], acc);
-        out[a] = acc;
-      }
-    }
-  };
-#pragma unroll
-  for (int j = 0; j < NX; ++j) {
-    float rhs[NU], sol[NU];
-#pragma unroll
-    for (int a = 0; a < NU; ++a) rhs[a] = (MASKED && ((tight >> a) & 1u)) ? 0.0f : Qxu[j][a];
-    solve(rhs, sol);
-#pragma unroll
-    for (int a = 0; a < NU; ++a) K[a][j] = -sol[a];
-  }
-  {
-    float rhs[NU], sol[NU];
-#pragma unroll
-    for (int a = 0; a < NU; ++a) rhs[a] = (MASKED && ((tight >> a) & 1u)) ? 0.0f : qu[a];
-    solve(rhs, sol);
-#pragma unroll
-    for (int a = 0; a < NU; ++a) k[a] = -sol[a];
-  }
-  // ---- value update --------------------------------------------------------
-  float w[NU];  // backward: Q_uu k + q_u
-  if (MASKED) {
-#pragma unroll
-    for (int a = 0; a < NU; ++a) {
-      float acc = Quu[a][0] * k[0];
-#pragma unroll
-      for (int b = 1; b < NU; ++b) acc = fmaf(Quu[a][b], k[b], acc);
-      w[a] = acc + qu[a];
-    }
-  }
-#pragma unroll
-  for (int r = 0; r < NX; ++r) {
-    float Z[NU];  // row r of K^T Q_uu
-#pragma unroll
-    for (int a = 0; a < NU; ++a) {
-      float acc = K[0][r] * Quu[0][a];
-#pragma unroll
-      for (int b = 1; b < NU; ++b) acc = fmaf(K[b][r], Quu[b][a], acc);
-      Z[a] = acc;
-    }
-    // v
-    float vk;
-    if (MASKED) {
-      float t2 = K[0][r] * w[0];
-#pragma unroll
-      for (int a = 1; a < NU; ++a) t2 = fmaf(K[a][r], w[a], t2);
-      float t3 = Qxu[r][0] * k[0];
-#pragma unroll
-      for (int a = 1; a < NU; ++a) t3 = fmaf(Qxu[r][a], k[a], t3);
-      vk = (qx[r] + t2) + t3;
-    } else {
-      float t1 = Z[0] * k[0];
-#pragma unroll
-      for (int a = 1; a < NU; ++a) t1 = fmaf(Z[a], k[a], t1);
-      float t2 = K[0][r] * qu[0];
-#pragma unroll
-      for (int a = 1; a < NU; ++a) t2 = fmaf(K[a][r], qu[a], t2);
-      float t3 = Qxu[r][0] * k[0];
-#pragma unroll
-      for (int a = 1; a < NU; ++a) t3 = fmaf(Qxu[r][a], k[a], t3);
-      vk = ((qx[r] + t1) + t2) + t3;
-    }
-    v[r] = vk;
-#pragma unroll
-    for (int c = 0; c < NX; ++c) {
-      float t1 = Z[0] * K[0][c];
-#pragma unroll
-      for (int a = 1; a < NU; ++a) t1 = fmaf(Z[a], K[a][c], t1);
-      float t2 = K[0][r] * Qxu[c][0];
-#pragma unroll
-      for (int a = 1; a < NU; ++a) t2 = fmaf(K[a][r], Qxu[c][a], t2);
-      float t3 = Qxu[r][0] * K[0][c];
-#pragma unroll
-      for (int a = 1; a < NU; ++a) t3 = fmaf(Qxu[r][a], K[a][c], t3);
-      V[r][c] = ((V[r][c] + t1) + t2) + t3;
-    }
-  }
-  return ok;
-}
-
-// --------------------------------------------------------------------------
-// TMA staging of C[b0:b0+32, t] (bulk tensor copies into shared memory)
+// TMA bulk tensor copies and mbarriers
 // --------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -566,49 +313,5 @@ template <int N>
 __device__ __forceinline__ void bulk_wait() {
   asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
-
-// Double-buffered stream of C_t slabs for one warp of 32 batch elements.
-struct CPipe {
-  float* buf;         // [2][CSLAB]
-  uint64_t* bar;      // [2]
-  uint32_t parity;    // bit s: phase parity to wait for on bar[s]
-  const CUtensorMap* tm;
-  int b0;
-
-  __device__ __forceinline__ void issue(int slot, int t) {
-    mbar_expect_tx(&bar[slot], SLAB_BYTES);
-    tma_load_3d(buf + slot * CSLAB, tm, &bar[slot], 0, t, b0);
-  }
-  // Runs body(t, Crow) for t over [0, T) (reverse order if rev), with Crow
-  // pointing at this lane's 196-float C[b, t] block in shared memory.
-  // Returns false (after draining in-flight copies, bounded) on a timeout.
-  template <class F>
-  __device__ __forceinline__ bool run(int T, bool rev, F&& body) {
-    const int lane = threadIdx.x;
-    if (lane == 0) {
-      issue(0, rev ? T - 1 : 0);
-      if (T > 1) issue(1, rev ? T - 2 : 1);
-    }
-    __syncwarp();
-    for (int s = 0; s < T; ++s) {
-      const int slot = s & 1;
-      const bool ok = mbar_wait(&bar[slot], (parity >> slot) & 1u);
-      if (!__all_sync(FULL, ok)) {
-        // Drain the copies still in flight (bounded) before giving up.
-        for (int r = s; r < T && r < s + 2; ++r) mbar_wait(&bar[r & 1], (parity >> (r & 1)) & 1u);
-        return false;
-      }
-      parity ^= (1u << slot);
-      body(rev ? T - 1 - s : s, buf + slot * CSLAB + lane * CBLK);
-      __syncwarp();
-      if (lane == 0 && s + 2 < T) {
-        fence_proxy_async();
-        issue(slot, rev ? T - 3 - s : s + 2);
-      }
-      __syncwarp();
-    }
-    return true;
-  }
-};
 
 }  // namespace ilqr

@@ -1,0 +1,429 @@
+// ilqr_team.cuh -- one batch element per 5-lane team (6 elements per warp).
+//
+// Riccati step: lane m of a team owns two state rows of V, RA(m) and RB(m):
+//   RA = {3,4,5,6,0}  (the four quaternion rows, and p0)
+//   RB = {1,2,7,8,9}  (p1, p2 and the three velocity rows)
+// so that every lane runs the same instruction stream: for its RA row it
+// applies an 8-term combination over rows {3..9, own} of (V A) (the column of A
+// at a quaternion row has nonzeros exactly there; for p0 only the own-row
+// coefficient is 1), and for its RB row a 2-term combination (own row plus dt
+// times p_j for a velocity row, 0 for a position row). Terms with an exact
+// zero coefficient add exact zeros, so the result equals the structured sum.
+// Rows of V A, V B, v, K and Q_xu are exchanged through a per-element
+// shared-memory area; everything else stays in registers.
+//
+// Line search: lane m evaluates step size alpha_m (5 at a time).
+#pragma once
+
+#include "ilqr_device.cuh"
+
+namespace ilqr {
+
+constexpr int TEAM = 5;
+constexpr int EPW = 6;        // batch elements per warp
+constexpr int XS = 164;       // exchange floats per element (164 = 4 mod 32: bank spread)
+// exchange layout (floats); VA/VB/v are dead once K/Q_xu are written (a
+// warp sync separates the phases)
+constexpr int X_VA = 0;       // [10][10] rows of V A
+constexpr int X_VB = 100;     // [10][4]  rows of V B
+constexpr int X_V = 140;      // [10]     v
+constexpr int X_K = 0;        // [10][4]  K transposed: column c of K at X_K + 4c (reuses X_VA)
+constexpr int X_QXU = 40;     // [10][4]  Q_xu rows (reuses X_VA)
+constexpr int X_LU = 160;     // [4]      l_u
+constexpr int SLAB_E = EPW + 1;  // slab rows incl. a pad row for the two spare lanes
+constexpr uint32_t TSLAB_BYTES = EPW * CBLK * 4u;  // bytes one TMA box delivers
+
+__device__ __forceinline__ int row_a(int m) { return m < 4 ? 3 + m : 0; }
+
+// Access to one element's C_t block: dense (the TMA-staged slab) or diagonal
+// (the 14 diagonal values; every off-diagonal entry is an exact zero). Only
+// the rows the calling lane uses are held: its two state rows and the four
+// control rows.
+struct DenseC {
+  const float* Ct;
+  __device__ __forceinline__ float operator()(int i, int j) const { return Ct[i * NT + j]; }
+};
+struct DiagC {
+  int ra, rb;
+  float dra, drb, du0, du1, du2, du3;
+  __device__ __forceinline__ float operator()(int i, int j) const {
+    if (i != j) return 0.0f;
+    return i == ra ? dra : i == rb ? drb : i == NX ? du0 : i == NX + 1 ? du1 : i == NX + 2 ? du2 : du3;
+  }
+};
+__device__ __forceinline__ int row_b(int m) { return m == 0 ? 1 : (m == 1 ? 2 : 5 + m); }
+
+// Coefficients A[k][RA] for k = 3..9 and the own-row coefficient, for lane m.
+__device__ __forceinline__ void coef_a(const Jac& J, int m, float (&c)[8]) {
+  const float z = 0.0f;
+  // columns j of A[q][q] and A[v][q] (see the table in ilqr_device.cuh)
+  if (m == 0) {
+    c[0] = 1.0f; c[1] = J.h0; c[2] = J.h1; c[3] = J.h2; c[4] = J.g2; c[5] = -J.g1; c[6] = J.g0;
+  } else if (m == 1) {
+    c[0] = -J.h0; c[1] = 1.0f; c[2] = -J.h2; c[3] = J.h1; c[4] = J.g3; c[5] = -J.g0; c[6] = -J.g1;
+  } else if (m == 2) {
+    c[0] = -J.h1; c[1] = J.h2; c[2] = 1.0f; c[3] = -J.h0; c[4] = J.g0; c[5] = J.g3; c[6] = -J.g2;
+  } else if (m == 3) {
+    c[0] = -J.h2; c[1] = -J.h1; c[2] = J.h0; c[3] = 1.0f; c[4] = J.g1; c[5] = J.g2; c[6] = J.g3;
+  } else {
+    c[0] = z; c[1] = z; c[2] = z; c[3] = z; c[4] = z; c[5] = z; c[6] = z;
+  }
+  c[7] = (m == 4) ? 1.0f : z;
+}
+
+// Row [own | V] (A) -> (V A)[r][:] and (V B)[r][:] for one row r of V.
+__device__ __forceinline__ void row_VA_VB(const Jac& J, const float (&Vr)[NX], float (&va)[NX], float (&vb)[NU]) {
+#pragma unroll
+  for (int j = 0; j < 3; ++j) va[j] = Vr[j];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float acc = Vr[3] * aqq(J, 0, j);
+#pragma unroll
+    for (int mm = 1; mm < 4; ++mm) acc = fmaf(Vr[3 + mm], aqq(J, mm, j), acc);
+#pragma unroll
+    for (int n = 0; n < 3; ++n) acc = fmaf(Vr[7 + n], avq(J, n, j), acc);
+    va[3 + j] = acc;
+  }
+#pragma unroll
+  for (int j = 0; j < 3; ++j) va[7 + j] = fmaf(Vr[j], J.dt, Vr[7 + j]);
+  {
+    float acc = Vr[7] * J.bv0;
+    acc = fmaf(Vr[8], J.bv1, acc);
+    vb[0] = fmaf(Vr[9], J.bv2, acc);
+  }
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    float acc = Vr[3] * bqw(J, 0, k);
+#pragma unroll
+    for (int mm = 1; mm < 4; ++mm) acc = fmaf(Vr[3 + mm], bqw(J, mm, k), acc);
+    vb[1 + k] = acc;
+  }
+}
+
+// One Riccati step for a team.
+// Forward (MASKED=false), backward_lqr (DifferentialMPC/controller.py:697-723):
+//   Q_xx = l_xx + A^T V A          Q_xu = l_xu + A^T V B
+//   Q_uu = l_uu + B^T V B + reg I
+//   q_x = l_x + A^T v              q_u = l_u + B^T v
+//   [K | k] = -chol_solve(Q_uu + reg I, [Q_ux | q_u])   (reg added twice)
+//   V = Q_xx + (K^T Q_uu) K + K^T Q_ux + Q_xu K
+//   v = q_x + (K^T Q_uu) k + K^T q_u + Q_xu k
+// Backward (MASKED=true), _zero_constrained_lqr (controller.py:1035-1110):
+//   tight rows/cols of Q_uu zeroed, +1 on their diagonal, + (1e-8 reg) I;
+//   tight rows of Q_ux and entries of q_u zeroed for the solve only;
+//   V, v use the unmasked Q_uu, Q_ux, q_u, and v = q_x + K^T(Q_uu k + q_u) + Q_xu k.
+// Va, Vb: this lane's rows RA, RB of V (in V_{t+1}, out V_t); va_, vb_: the
+// matching entries of v. lxa, lxb: gradient terms of those rows; the four
+// control gradient terms are read from xc[X_LU..] (written by lanes 0..3
+// before the call). xc: this element's exchange area. Ct: this
+// element's C_t block in shared memory. after_c() is called once every lane
+// is done reading Ct (it may reuse the slab). Outputs: Ka, Kb = K[:, RA],
+// K[:, RB]; k. Returns false if the Cholesky failed (SVD inverse used).
+template <bool MASKED, class CAcc, class AfterC>
+__device__ __forceinline__ bool team_riccati(float (&Va)[NX], float (&Vb)[NX], float& va_, float& vb_,
+                                             const Jac& J, const CAcc& Ct, float lxa, float lxb,
+                                             float reg, uint32_t tight, int m,
+                                             float* __restrict__ xc, AfterC&& after_c, float (&Ka)[NU],
+                                             float (&Kb)[NU], float (&k)[NU]) {
+  const int ra = row_a(m), rb = row_b(m);
+  // ---- rows of V A and V B -> exchange ------------------------------------
+  {
+    float VAr[NX], VBr[NU];
+    row_VA_VB(J, Va, VAr, VBr);
+#pragma unroll
+    for (int c = 0; c < NX; c += 2)
+      *reinterpret_cast<float2*>(xc + X_VA + ra * NX + c) = make_float2(VAr[c], VAr[c + 1]);
+    *reinterpret_cast<float4*>(xc + X_VB + ra * NU) = make_float4(VBr[0], VBr[1], VBr[2], VBr[3]);
+    row_VA_VB(J, Vb, VAr, VBr);
+#pragma unroll
+    for (int c = 0; c < NX; c += 2)
+      *reinterpret_cast<float2*>(xc + X_VA + rb * NX + c) = make_float2(VAr[c], VAr[c + 1]);
+    *reinterpret_cast<float4*>(xc + X_VB + rb * NU) = make_float4(VBr[0], VBr[1], VBr[2], VBr[3]);
+  }
+  xc[X_V + ra] = va_;
+  xc[X_V + rb] = vb_;
+  __syncwarp();
+
+  // ---- Q_xx, Q_xu, q_x rows (A^T (V A) etc.), Q_uu and q_u ----------------
+  float ca[8];
+  coef_a(J, m, ca);
+  const float cb = (m >= 2) ? J.dt : 0.0f;
+  const int pb = (m >= 2) ? m - 2 : 0;
+  float Qa[NX], Qb[NX], Qxa[NU], Qxb[NU], qxa, qxb;
+  {
+    // RA: sum over rows 3..9 of (V A) and V B, then the own row.
+#pragma unroll
+    for (int c = 0; c < NX; c += 2) {
+      float2 acc = make_float2(0.0f, 0.0f);
+#pragma unroll
+      for (int s = 0; s < 7; ++s) {
+        const float2 r = *reinterpret_cast<const float2*>(xc + X_VA + (3 + s) * NX + c);
+        acc.x = fmaf(ca[s], r.x, acc.x);
+        acc.y = fmaf(ca[s], r.y, acc.y);
+      }
+      const float2 own = *reinterpret_cast<const float2*>(xc + X_VA + ra * NX + c);
+      acc.x = fmaf(ca[7], own.x, acc.x);
+      acc.y = fmaf(ca[7], own.y, acc.y);
+      Qa[c] = Ct(ra, c) + acc.x;
+      Qa[c + 1] = Ct(ra, c + 1) + acc.y;
+    }
+    float4 acc4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    float accv = 0.0f;
+#pragma unroll
+    for (int s = 0; s < 7; ++s) {
+      const float4 r = *reinterpret_cast<const float4*>(xc + X_VB + (3 + s) * NU);
+      acc4.x = fmaf(ca[s], r.x, acc4.x);
+      acc4.y = fmaf(ca[s], r.y, acc4.y);
+      acc4.z = fmaf(ca[s], r.z, acc4.z);
+      acc4.w = fmaf(ca[s], r.w, acc4.w);
+      accv = fmaf(ca[s], xc[X_V + 3 + s], accv);
+    }
+    {
+      const float4 own = *reinterpret_cast<const float4*>(xc + X_VB + ra * NU);
+      Qxa[0] = Ct(ra, NX + 0) + fmaf(ca[7], own.x, acc4.x);
+      Qxa[1] = Ct(ra, NX + 1) + fmaf(ca[7], own.y, acc4.y);
+      Qxa[2] = Ct(ra, NX + 2) + fmaf(ca[7], own.z, acc4.z);
+      Qxa[3] = Ct(ra, NX + 3) + fmaf(ca[7], own.w, acc4.w);
+    }
+    qxa = lxa + fmaf(ca[7], va_, accv);
+    // RB: own row plus cb times row pb.
+#pragma unroll
+    for (int c = 0; c < NX; ++c)
+      Qb[c] = Ct(rb, c) + fmaf(cb, xc[X_VA + pb * NX + c], xc[X_VA + rb * NX + c]);
+#pragma unroll
+    for (int a = 0; a < NU; ++a)
+      Qxb[a] = Ct(rb, NX + a) + fmaf(cb, xc[X_VB + pb * NU + a], xc[X_VB + rb * NU + a]);
+    qxb = lxb + fmaf(cb, xc[X_V + pb], vb_);
+  }
+  float Quu[NU][NU], qu[NU];
+  {
+    // Q_uu = l_uu + B^T (V B) + reg I: B^T rows are bv over the velocity rows
+    // (first control) and 0.5 dt Xi(q) over the quaternion rows (body rates);
+    // accumulated row by row of V B in index order.
+    float acc[NU][NU];
+#pragma unroll
+    for (int s = 0; s < 7; ++s) {
+      const float4 r4 = *reinterpret_cast<const float4*>(xc + X_VB + (3 + s) * NU);
+      const float r[NU] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+      for (int b = 0; b < NU; ++b) {
+        if (s >= 4) {
+          const float cf = bvf(J, s - 4);
+          acc[0][b] = (s == 4) ? cf * r[b] : fmaf(cf, r[b], acc[0][b]);
+        } else {
+#pragma unroll
+          for (int kk = 0; kk < 3; ++kk) {
+            const float cf = bqw(J, s, kk);
+            acc[1 + kk][b] = (s == 0) ? cf * r[b] : fmaf(cf, r[b], acc[1 + kk][b]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int a = 0; a < NU; ++a)
+#pragma unroll
+      for (int b = 0; b < NU; ++b)
+        Quu[a][b] = (Ct(NX + a, NX + b) + acc[a][b]) + (a == b ? reg : 0.0f);
+    float vq[7];
+#pragma unroll
+    for (int s = 0; s < 7; ++s) vq[s] = xc[X_V + 3 + s];
+    float lu[NU];
+#pragma unroll
+    for (int a = 0; a < NU; ++a) lu[a] = xc[X_LU + a];
+    {
+      float acc = J.bv0 * vq[4];
+      acc = fmaf(J.bv1, vq[5], acc);
+      qu[0] = lu[0] + fmaf(J.bv2, vq[6], acc);
+#pragma unroll
+      for (int kk = 0; kk < 3; ++kk) {
+        float a2 = bqw(J, 0, kk) * vq[0];
+#pragma unroll
+        for (int mm = 1; mm < 4; ++mm) a2 = fmaf(bqw(J, mm, kk), vq[mm], a2);
+        qu[1 + kk] = lu[1 + kk] + a2;
+      }
+    }
+  }
+  after_c();  // syncs the warp: C_t and the V A / V B / v rows are no longer read
+
+  // ---- gains -----------------------------------------------------------------
+  bool ok;
+  Chol4 L;
+  float Mi[NU][NU];
+  {
+    float Qs[NU][NU];
+#pragma unroll
+    for (int a = 0; a < NU; ++a)
+#pragma unroll
+      for (int b = 0; b < NU; ++b) {
+        if (MASKED) {
+          const bool ta = (tight >> a) & 1u, tb = (tight >> b) & 1u;
+          float val = (ta || tb) ? 0.0f : Quu[a][b];
+          if (a == b && ta) val = val + 1.0f;
+          Qs[a][b] = val + (a == b ? 1e-8f * reg : 0.0f);
+        } else {
+          Qs[a][b] = Quu[a][b] + (a == b ? reg : 0.0f);
+        }
+      }
+    ok = chol4(Qs, L);
+    if (!ok) svd_inverse4(Qs, Mi);
+  }
+  auto solve = [&](const float (&rhs)[NU], float (&out)[NU]) {
+    if (ok) {
+      chol4_solve(L, rhs, out);
+    } else {
+#pragma unroll
+      for (int a = 0; a < NU; ++a) {
+        float acc = Mi[a][0] * rhs[0];
+#pragma unroll
+        for (int b = 1; b < NU; ++b) acc = fmaf(Mi[a][b], rhs[b], acc);
+        out[a] = acc;
+      }
+    }
+  };
+  auto msk = [&](int a, float v) { return (MASKED && ((tight >> a) & 1u)) ? 0.0f : v; };
+  {
+    float rhs[NU], sol[NU];
+#pragma unroll
+    for (int a = 0; a < NU; ++a) rhs[a] = msk(a, Qxa[a]);
+    solve(rhs, sol);
+#pragma unroll
+    for (int a = 0; a < NU; ++a) Ka[a] = -sol[a];
+#pragma unroll
+    for (int a = 0; a < NU; ++a) rhs[a] = msk(a, Qxb[a]);
+    solve(rhs, sol);
+#pragma unroll
+    for (int a = 0; a < NU; ++a) Kb[a] = -sol[a];
+#pragma unroll
+    for (int a = 0; a < NU; ++a) rhs[a] = msk(a, qu[a]);
+    solve(rhs, sol);
+#pragma unroll
+    for (int a = 0; a < NU; ++a) k[a] = -sol[a];
+  }
+  // K columns and Q_xu rows -> exchange (over the dead V A area)
+  *reinterpret_cast<float4*>(xc + X_K + ra * NU) = make_float4(Ka[0], Ka[1], Ka[2], Ka[3]);
+  *reinterpret_cast<float4*>(xc + X_K + rb * NU) = make_float4(Kb[0], Kb[1], Kb[2], Kb[3]);
+  *reinterpret_cast<float4*>(xc + X_QXU + ra * NU) = make_float4(Qxa[0], Qxa[1], Qxa[2], Qxa[3]);
+  *reinterpret_cast<float4*>(xc + X_QXU + rb * NU) = make_float4(Qxb[0], Qxb[1], Qxb[2], Qxb[3]);
+  __syncwarp();
+
+  // ---- value update for my rows: V = Q_xx + (K^T Q_uu) K + K^T Q_ux + Q_xu K ---
+  float w[NU];
+  if (MASKED) {
+#pragma unroll
+    for (int a = 0; a < NU; ++a) {
+      float acc = Quu[a][0] * k[0];
+#pragma unroll
+      for (int b = 1; b < NU; ++b) acc = fmaf(Quu[a][b], k[b], acc);
+      w[a] = acc + qu[a];
+    }
+  }
+  auto update_row = [&](float (&Vr)[NX], const float (&Qr)[NX], const float (&Kr)[NU], const float (&Qxr)[NU],
+                        float qxr) -> float {
+    float Z[NU];
+#pragma unroll
+    for (int a = 0; a < NU; ++a) {
+      float acc = Kr[0] * Quu[0][a];
+#pragma unroll
+      for (int b = 1; b < NU; ++b) acc = fmaf(Kr[b], Quu[b][a], acc);
+      Z[a] = acc;
+    }
+    float vk;
+    if (MASKED) {
+      float t2 = Kr[0] * w[0];
+#pragma unroll
+      for (int a = 1; a < NU; ++a) t2 = fmaf(Kr[a], w[a], t2);
+      float t3 = Qxr[0] * k[0];
+#pragma unroll
+      for (int a = 1; a < NU; ++a) t3 = fmaf(Qxr[a], k[a], t3);
+      vk = (qxr + t2) + t3;
+    } else {
+      float t1 = Z[0] * k[0];
+#pragma unroll
+      for (int a = 1; a < NU; ++a) t1 = fmaf(Z[a], k[a], t1);
+      float t2 = Kr[0] * qu[0];
+#pragma unroll
+      for (int a = 1; a < NU; ++a) t2 = fmaf(Kr[a], qu[a], t2);
+      float t3 = Qxr[0] * k[0];
+#pragma unroll
+      for (int a = 1; a < NU; ++a) t3 = fmaf(Qxr[a], k[a], t3);
+      vk = ((qxr + t1) + t2) + t3;
+    }
+#pragma unroll
+    for (int c = 0; c < NX; ++c) {
+      const float4 qc = *reinterpret_cast<const float4*>(xc + X_QXU + c * NU);
+      const float4 k4 = *reinterpret_cast<const float4*>(xc + X_K + c * NU);
+      const float Kc[NU] = {k4.x, k4.y, k4.z, k4.w};
+      float t1 = Z[0] * Kc[0];
+#pragma unroll
+      for (int a = 1; a < NU; ++a) t1 = fmaf(Z[a], Kc[a], t1);
+      float t2 = Kr[0] * qc.x;
+      t2 = fmaf(Kr[1], qc.y, t2);
+      t2 = fmaf(Kr[2], qc.z, t2);
+      t2 = fmaf(Kr[3], qc.w, t2);
+      float t3 = Qxr[0] * Kc[0];
+#pragma unroll
+      for (int a = 1; a < NU; ++a) t3 = fmaf(Qxr[a], Kc[a], t3);
+      Vr[c] = ((Qr[c] + t1) + t2) + t3;
+    }
+    return vk;
+  };
+  va_ = update_row(Va, Qa, Ka, Qxa, qxa);
+  vb_ = update_row(Vb, Qb, Kb, Qxb, qxb);
+  __syncwarp();  // the exchange area is rewritten by the next step
+  return ok;
+}
+
+// Reduce over the 5 lanes of a team (all lanes get the result); lanes 30, 31
+// form a partial team of their own.
+__device__ __forceinline__ float team_sum(float x, int base) {
+  float s = __shfl_sync(FULL, x, base);
+#pragma unroll
+  for (int j = 1; j < TEAM; ++j) s += __shfl_sync(FULL, x, (base + j) & 31);
+  return s;
+}
+
+// Single-buffered stream of [6 x 196] C_t slabs for one warp.
+struct TeamPipe {
+  float* slab;      // [SLAB_E][CBLK]
+  uint64_t* bar;
+  uint32_t parity;
+  const CUtensorMap* tm;
+  int b0;
+  bool ok;
+
+  __device__ __forceinline__ void issue(int t) {
+    if (threadIdx.x == 0) {
+      fence_proxy_async();
+      mbar_expect_tx(bar, TSLAB_BYTES);
+      tma_load_3d(slab, tm, bar, 0, t, b0);
+    }
+  }
+  // Runs body(t, next) over t (reverse if rev). body must call next() exactly
+  // once, after its last read of the slab; next() syncs the warp and starts
+  // the copy of the following step. Returns false on a (bounded) wait timeout.
+  template <class F>
+  __device__ __forceinline__ bool run(int T, bool rev, F&& body) {
+    issue(rev ? T - 1 : 0);
+    for (int s = 0; s < T; ++s) {
+      const bool got = mbar_wait(bar, parity);
+      if (!__all_sync(FULL, got)) {
+        mbar_wait(bar, parity);  // give the copy in flight one more bounded wait
+        ok = false;
+        return false;
+      }
+      parity ^= 1u;
+      const int t = rev ? T - 1 - s : s;
+      bool called = false;
+      auto next = [&]() {
+        __syncwarp();
+        if (s + 1 < T) issue(rev ? t - 1 : t + 1);
+        called = true;
+      };
+      body(t, next);
+      if (!called) next();
+    }
+    return true;
+  }
+};
+
+}  // namespace ilqr
