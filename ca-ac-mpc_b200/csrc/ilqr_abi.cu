@@ -4,6 +4,7 @@
 // error is reported as a status code and nothing is launched on an invalid
 // call. TMA descriptors for C (and grad_C) are encoded per call through the
 // runtime's driver entry point, so the library does not link libcuda.
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -117,6 +118,8 @@ int ilqr_b200_solve_f32(const float* x0, const float* U_init, const float* C, co
   for (int i = 0; i < n_alpha; ++i) p.alphas[i] = alphas[i];
   p.n_alpha = n_alpha;
   p.has_bounds = (u_min != nullptr) ? 1 : 0;
+  const char* dc = std::getenv("ILQR_B200_DIAG_CACHE");
+  p.diag_cache = (dc != nullptr && dc[0] == '0') ? 0 : 1;
   CUtensorMap tmC;
   int st = encode_cost_map(&tmC, C, B, T);
   if (st != ILQR_OK) return st;

@@ -51,6 +51,10 @@ __global__ void __launch_bounds__(32, 19) backward_kernel(const __grid_constant_
     mbar_init(bar, 1);
     fence_mbar_init();
   }
+  // The pad rows (lanes 30, 31) are never filled by a copy: zero them so that
+  // no lane reads uninitialized shared memory.
+  for (int f = lane; f < CBLK; f += WARP) slab[(SLAB_E - 1) * CBLK + f] = 0.0f;
+  for (int f = lane; f < XS; f += WARP) xch[(SLAB_E - 1) * XS + f] = 0.0f;
   __syncwarp();
   TeamPipe pipe{slab, bar, 0u, &tmC, (int)b0, true};
   float* xc = xch + e * XS;
@@ -87,7 +91,7 @@ __global__ void __launch_bounds__(32, 19) backward_kernel(const __grid_constant_
     __syncwarp();
     const Jac J = drone_jac(xb, ub, dt);
     float Ka[NU], Kb[NU], k[NU];
-    team_riccati<true>(Va, Vb, va_, vb_, J, DenseC{Ce}, lxa, lxb, p.reg, tight, m, xc, next, Ka, Kb, k);
+    team_riccati<true>(Va, Vb, va_, vb_, J, DenseC{Ce}, lxa, lxb, p.reg, tight, m, valid, xc, next, Ka, Kb, k);
     if (valid) {
 #pragma unroll
       for (int a = 0; a < NU; ++a) {

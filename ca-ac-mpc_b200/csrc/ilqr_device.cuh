@@ -27,6 +27,7 @@ constexpr uint32_t WAIT_LIMIT = 1u << 24;   // bounded mbarrier polls
 constexpr uint32_t ELEM_CHOL_FALLBACK = 1u;
 constexpr uint32_t ELEM_NONFINITE = 2u;
 constexpr uint32_t ELEM_PIPE_TIMEOUT = 4u;
+constexpr uint32_t ELEM_DIAG_COST = 8u;
 
 // --------------------------------------------------------------------------
 // Quadrotor CTBR model (acmpc_public-master/diff_mpc_drones/drone.py)

@@ -39,6 +39,7 @@ struct SolveParams {
   float alphas[ILQR_MAX_ALPHAS_DEV];
   int n_alpha;
   int has_bounds;
+  int diag_cache;  // 1: detect diagonal C_t blocks and stop re-reading them after the first pass
 };
 
 struct BackwardParams {
@@ -65,8 +66,18 @@ struct BackwardParams {
   int write_gC;
 };
 
-// Workspace floats per element slot (interleaved layout).
-inline int64_t solve_ws_fields(int T) { return (int64_t)(T + 1) * 10 + (int64_t)T * (4 + 40 + 4); }
+// Solve workspace, in floats, element-interleaved with stride S (the record
+// of element b sits at (... * S + b) * width):
+//   trajectory slots [SOLVE_SLOTS][T+1][S][16]: x[10], u[4], 2 pad (u unused at t = T)
+//   gains K          [T][10][S][4]: column j of K_t (the 4 gains of state j)
+//   feedforward k    [T][S][4]
+//   cost diagonals   [T][S][16]: the 14 diagonal entries of C_t, 2 pad
+// One slot holds the nominal trajectory, the others the line-search candidates.
+constexpr int SOLVE_SLOTS = 6;
+constexpr int TRJ_REC = 16;
+inline int64_t solve_ws_fields(int T) {
+  return (int64_t)SOLVE_SLOTS * (T + 1) * TRJ_REC + (int64_t)T * (10 * 4 + 4 + TRJ_REC);
+}
 inline int64_t backward_ws_fields(int T) { return (int64_t)T * (40 + 4); }
 inline int64_t ws_stride(int64_t B) { return (B + 31) / 32 * 32; }
 

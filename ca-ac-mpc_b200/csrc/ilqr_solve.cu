@@ -3,10 +3,29 @@
 // Mapping: one CTA = one warp = 6 batch elements, a team of 5 lanes per
 // element (lanes 30, 31 are spare). The team splits each Riccati step by rows
 // of V (ilqr_team.cuh) and evaluates the line-search step sizes one per lane.
-// Per-element trajectories (nominal X, U) and gains (K, k) live in a
-// caller-provided workspace, element-interleaved (field f of element b at
-// ws[f * S + b]); the dense cost blocks C[b, t] of the warp's six elements are
-// staged into shared memory by one TMA bulk tensor copy per step.
+// Per-element state lives in a caller-provided workspace, element-interleaved
+// in 16-byte-aligned records (layout in ilqr_kernels.h): SOLVE_SLOTS
+// trajectory slots of (x_t, u_t) records, the gains K_t as one float4 per
+// state column, k_t, and the diagonals of C_t. The dense cost blocks C[b, t]
+// of the warp's six elements are staged into shared memory by one TMA bulk
+// tensor copy per step.
+//
+// Candidate slots: one slot holds the nominal trajectory; the line-search lane
+// of step size j (j < SOLVE_SLOTS - 1) stores its candidate rollout into
+// another slot as it goes, so accepting candidate j only re-points the
+// nominal slot (the stored records are exactly the rollout the reference
+// takes as its new X, U). Step sizes beyond those slots (n_alpha > 5) fall
+// back to one lane re-running the accepted candidate.
+//
+// Diagonal cost blocks: the first Riccati pass also checks whether every
+// C[b, t] block of the warp's elements is diagonal and copies the diagonals
+// into the workspace. If so, later passes stop reading C: the Riccati pass
+// rebuilds the blocks in shared memory from the 14 diagonals (off-diagonal
+// entries stay exact zeros, so every sum is the one the dense path forms) and
+// the line search evaluates tau^T C tau from the diagonals alone. Each product
+// with an off-diagonal zero that the dense path adds is an exact zero unless
+// tau holds an infinity or NaN, where the dense quadratic form is NaN; the
+// diagonal form reproduces that, so results are identical.
 //
 // Algorithm: DifferentiableMPCController.solve_step (controller.py:303-435)
 // with per-element freezing: an element stops at its first non-improving
@@ -19,12 +38,6 @@
 namespace ilqr {
 
 namespace {
-
-struct Ws {
-  float* base;
-  int64_t S;
-  __device__ __forceinline__ float* x(int64_t b, int t, int i) const { return base + (int64_t)(t * NX + i) * S + b; }
-};
 
 __device__ __forceinline__ float ldg_or0(const float* p, bool ok) { return ok ? __ldg(p) : 0.0f; }
 
@@ -49,25 +62,86 @@ __device__ __forceinline__ float terminal_cost(const float* __restrict__ Cf, con
   return 0.5f * q + l;
 }
 
+// The workspace records of one element (layout in ilqr_kernels.h).
+struct SolveWs {
+  float* trj;
+  float* gk;
+  float* gkk;
+  float* dg;
+  int64_t S;
+  int T1;
+  int64_t b;
+  __device__ __forceinline__ float4* rec(int s, int t) const {
+    return reinterpret_cast<float4*>(trj + (((int64_t)s * T1 + t) * S + b) * TRJ_REC);
+  }
+  __device__ __forceinline__ float4* kcol(int t, int j) const {
+    return reinterpret_cast<float4*>(gk + ((int64_t)(t * NX + j) * S + b) * 4);
+  }
+  __device__ __forceinline__ float4* kff(int t) const {
+    return reinterpret_cast<float4*>(gkk + ((int64_t)t * S + b) * 4);
+  }
+  __device__ __forceinline__ float* diag(int t) const { return dg + ((int64_t)t * S + b) * TRJ_REC; }
+};
+
+__device__ __forceinline__ void load_rec(const float4* r, float (&x)[NX], float (&u)[NU]) {
+  const float4 a = r[0], c = r[1], d = r[2], e = r[3];
+  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+  x[4] = c.x; x[5] = c.y; x[6] = c.z; x[7] = c.w;
+  x[8] = d.x; x[9] = d.y; u[0] = d.z; u[1] = d.w;
+  u[2] = e.x; u[3] = e.y;
+}
+
+__device__ __forceinline__ void load_rec_x(const float4* r, float (&x)[NX]) {
+  const float4 a = r[0], c = r[1], d = r[2];
+  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+  x[4] = c.x; x[5] = c.y; x[6] = c.z; x[7] = c.w;
+  x[8] = d.x; x[9] = d.y;
+}
+
+__device__ __forceinline__ void store_rec(float4* r, const float (&x)[NX], const float (&u)[NU]) {
+  r[0] = make_float4(x[0], x[1], x[2], x[3]);
+  r[1] = make_float4(x[4], x[5], x[6], x[7]);
+  r[2] = make_float4(x[8], x[9], u[0], u[1]);
+  r[3] = make_float4(u[2], u[3], 0.0f, 0.0f);
+}
+
+__device__ __forceinline__ void store_rec_x(float4* r, const float (&x)[NX]) {
+  r[0] = make_float4(x[0], x[1], x[2], x[3]);
+  r[1] = make_float4(x[4], x[5], x[6], x[7]);
+  r[2] = make_float4(x[8], x[9], 0.0f, 0.0f);
+}
+
 // Candidate control of the grid line search (controller.py:480-490):
 // u = U_t + a k_t + a (K_t (x - X_t)), then max(., u_min), min(., u_max).
-// K_t rows are read from the workspace one at a time.
-template <class KRow>
+// kcol(j) returns column j of K_t (the four gains of state j); each row of
+// K_t (x - X_t) is accumulated over j in index order.
+template <class KCol>
 __device__ __forceinline__ void candidate_u(const float (&x)[NX], const float (&xb)[NX], const float (&ub)[NU],
-                                            KRow&& krow, const float (&kt)[NU], float al,
+                                            KCol&& kcol, const float (&kt)[NU], float al,
                                             const float* __restrict__ lo, const float* __restrict__ hi,
                                             float (&u)[NU]) {
   float dx[NX];
 #pragma unroll
   for (int i = 0; i < NX; ++i) dx[i] = x[i] - xb[i];
+  float kd[NU];
+  {
+    const float4 c = kcol(0);
+    kd[0] = c.x * dx[0];
+    kd[1] = c.y * dx[0];
+    kd[2] = c.z * dx[0];
+    kd[3] = c.w * dx[0];
+  }
+#pragma unroll
+  for (int j = 1; j < NX; ++j) {
+    const float4 c = kcol(j);
+    kd[0] = fmaf(c.x, dx[j], kd[0]);
+    kd[1] = fmaf(c.y, dx[j], kd[1]);
+    kd[2] = fmaf(c.z, dx[j], kd[2]);
+    kd[3] = fmaf(c.w, dx[j], kd[3]);
+  }
 #pragma unroll
   for (int a = 0; a < NU; ++a) {
-    float Kr[NX];
-    krow(a, Kr);
-    float kd = Kr[0] * dx[0];
-#pragma unroll
-    for (int i = 1; i < NX; ++i) kd = fmaf(Kr[i], dx[i], kd);
-    float v = ub[a] + (al * kt[a] + al * kd);
+    float v = ub[a] + (al * kt[a] + al * kd[a]);
     if (lo != nullptr) {
       v = (v != v) ? v : fmaxf(v, __ldg(lo + a));
       v = (v != v) ? v : fminf(v, __ldg(hi + a));
@@ -83,10 +157,13 @@ __device__ __forceinline__ float pick(const float (&v)[NT], int i) {
   return r;
 }
 
+__device__ __forceinline__ float4 f4(const float (&v)[NU]) { return make_float4(v[0], v[1], v[2], v[3]); }
+
 template <int NAC, bool HAS_REF>
 __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ CUtensorMap tmC,
                                                        const SolveParams p) {
   static_assert(NAC == TEAM, "one step size per team lane");
+  static_assert(NAC <= SOLVE_SLOTS - 1, "a slot per candidate of the first chunk");
   extern __shared__ __align__(128) unsigned char smem[];
   float* slab = reinterpret_cast<float*>(smem);
   float* xch = slab + SLAB_E * CBLK;
@@ -98,25 +175,30 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
   const int64_t b0 = (int64_t)blockIdx.x * EPW;
   const int64_t b = b0 + e;
   const bool valid = (e < EPW) && (b < p.B);
-  const int64_t bw = valid ? b : b0;  // workspace slot read by this lane (never written when !valid)
+  const int64_t bw = valid ? b : b0;  // workspace record read by this lane (never written when !valid)
   const int T = p.T;
   const float dt = p.dt;
-  const Ws ws{p.ws, p.S};
-  float* Kw = p.ws + (int64_t)((T + 1) * NX + T * NU) * p.S;
-  float* kw = Kw + (int64_t)T * NU * NX * p.S;
-  auto Xn = [&](int t, int i) -> float& { return *ws.x(bw, t, i); };
-  auto Un = [&](int t, int a) -> float& { return p.ws[(int64_t)((T + 1) * NX + t * NU + a) * p.S + bw]; };
-  auto Kat = [&](int t, int a, int j) -> float& { return Kw[(int64_t)(t * NU * NX + a * NX + j) * p.S + bw]; };
-  auto kat = [&](int t, int a) -> float& { return kw[(int64_t)(t * NU + a) * p.S + bw]; };
+  SolveWs W;
+  W.trj = p.ws;
+  W.gk = W.trj + (int64_t)SOLVE_SLOTS * (T + 1) * p.S * TRJ_REC;
+  W.gkk = W.gk + (int64_t)T * NX * p.S * 4;
+  W.dg = W.gkk + (int64_t)T * p.S * 4;
+  W.S = p.S;
+  W.T1 = T + 1;
+  W.b = bw;
 
   if (lane == 0) {
     mbar_init(bar, 1);
     fence_mbar_init();
   }
+  // The pad rows (lanes 30, 31) are never filled by a copy: zero them so that
+  // no lane reads uninitialized shared memory.
+  for (int f = lane; f < CBLK; f += WARP) slab[(SLAB_E - 1) * CBLK + f] = 0.0f;
+  for (int f = lane; f < XS; f += WARP) xch[(SLAB_E - 1) * XS + f] = 0.0f;
   __syncwarp();
   TeamPipe pipe{slab, bar, 0u, &tmC, (int)b0, true};
   float* xc = xch + e * XS;
-  const float* Ce = slab + e * CBLK;
+  float* Ce = slab + e * CBLK;
   const int ra = row_a(m), rb = row_b(m);
 
   const bool bounds = p.has_bounds != 0;
@@ -138,7 +220,7 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
   if (p.trace != nullptr && writer)
     for (int i = 0; i < p.max_iter; ++i) p.trace[b * p.max_iter + i] = (int8_t)-128;
 
-  // ---- initial open-loop rollout with U_init (controller.py:305, 578-603) --
+  // ---- initial open-loop rollout with U_init into slot 0 (controller.py:305, 578-603)
   {
     float x[NX];
     load_x0(x);
@@ -146,30 +228,25 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
       float u[NU];
 #pragma unroll
       for (int a = 0; a < NU; ++a) u[a] = ldg_or0(p.U_init + (b * T + t) * NU + a, valid);
-      if (writer) {
-#pragma unroll
-        for (int i = 0; i < NX; ++i) Xn(t, i) = x[i];
-#pragma unroll
-        for (int a = 0; a < NU; ++a) Un(t, a) = u[a];
-      }
+      if (writer) store_rec(W.rec(0, t), x, u);
       float xn[NX];
       drone_step(x, u, dt, xn);
 #pragma unroll
       for (int i = 0; i < NX; ++i) x[i] = xn[i];
     }
-    if (writer) {
-#pragma unroll
-      for (int i = 0; i < NX; ++i) Xn(T, i) = x[i];
-    }
+    if (writer) store_rec_x(W.rec(0, T), x);
   }
   __syncwarp();
 
+  int nom = 0;  // slot of the nominal trajectory (the same in every lane of a team)
   uint32_t status = 0;
   bool active = valid;
   int iters = 0;
   int stall_iter = p.max_iter;
   float stall_gap = 0.0f;
   float best = 0.0f;
+  bool diag = false;  // warp-uniform: all C[b, t] of the warp's elements are diagonal (known after pass 1)
+  bool offd = false;  // this lane saw a nonzero off-diagonal entry during pass 1
 
   // The first pass always runs: it also yields the initial objective (with
   // max_iter == 0 only that).
@@ -183,9 +260,10 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
     // ---- backward Riccati pass (controller.py:315-318, 697-723) ------------
     float Va[NX], Vb[NX], va_, vb_;
     {
-      float tn[NX];
+      float xT[NX], tn[NX];
+      load_rec_x(W.rec(nom, T), xT);
 #pragma unroll
-      for (int i = 0; i < NX; ++i) tn[i] = Xn(T, i) - xref(T, i);
+      for (int i = 0; i < NX; ++i) tn[i] = xT[i] - xref(T, i);
       float acca = 0.0f, accb = 0.0f;
 #pragma unroll
       for (int j = 0; j < NX; ++j) {
@@ -200,18 +278,13 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
     bool fallback = false;
     float cost_q = 0.0f, cost_l = 0.0f;  // initial objective, first pass only
     const bool first = (it == 0);
-    bool ok = pipe.run(T, true, [&](int t, auto&& next) {
-      float xb[NX], ub[NU], tau[NT], ct[NT];
+    auto ric_body = [&](int t, auto&& next) {
+      float xb[NX], ub[NU], tau[NT];
+      load_rec(W.rec(nom, t), xb, ub);
 #pragma unroll
-      for (int i = 0; i < NX; ++i) {
-        xb[i] = Xn(t, i);
-        tau[i] = xb[i] - xref(t, i);
-      }
+      for (int i = 0; i < NX; ++i) tau[i] = xb[i] - xref(t, i);
 #pragma unroll
-      for (int a = 0; a < NU; ++a) {
-        ub[a] = Un(t, a);
-        tau[NX + a] = ub[a] - uref(t, a);
-      }
+      for (int a = 0; a < NU; ++a) tau[NX + a] = ub[a] - uref(t, a);
       // quadraticize my rows (cost.py:149-165): l_tau = C tau + c
       auto rowdot = [&](int r) {
         const float* Cr = Ce + r * NT;
@@ -230,34 +303,57 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
         const float ta = pick(tau, ra), tb = pick(tau, rb), tu = pick(tau, ru);
         cost_q += fmaf(ta, sa, tb * sb) + (m < NU ? tu * su : 0.0f);
         cost_l += fmaf(ca_, ta, cb_ * tb) + (m < NU ? cu * tu : 0.0f);
+        if (p.diag_cache && valid) {
+          // the team scans the block for off-diagonal nonzeros (the diagonal
+          // sits at flat index 15 i) and keeps a copy of the diagonal
+          const float4* c4 = reinterpret_cast<const float4*>(Ce);
+          for (int q = m; q < CBLK / 4; q += TEAM) {
+            const float4 v = c4[q];
+            const int f = 4 * q;
+            offd |= (v.x != 0.0f && f % (NT + 1) != 0) || (v.y != 0.0f && (f + 1) % (NT + 1) != 0) ||
+                    (v.z != 0.0f && (f + 2) % (NT + 1) != 0) || (v.w != 0.0f && (f + 3) % (NT + 1) != 0);
+          }
+          float* dgt = W.diag(t);
+          for (int i = m; i < NT; i += TEAM) dgt[i] = Ce[i * (NT + 1)];
+        }
       }
       __syncwarp();
       const Jac J = drone_jac(xb, ub, dt);
       float Ka[NU], Kb[NU], k[NU];
-      if (!team_riccati<false>(Va, Vb, va_, vb_, J, DenseC{Ce}, lxa, lxb, p.reg, 0u, m, xc, next, Ka, Kb, k))
+      if (!team_riccati<false>(Va, Vb, va_, vb_, J, DenseC{Ce}, lxa, lxb, p.reg, 0u, m, valid, xc, next, Ka, Kb,
+                               k))
         fallback = true;
       if (valid) {
-#pragma unroll
-        for (int a = 0; a < NU; ++a) {
-          Kat(t, a, ra) = Ka[a];
-          Kat(t, a, rb) = Kb[a];
-        }
-        if (m == 0) {
-#pragma unroll
-          for (int a = 0; a < NU; ++a) kat(t, a) = k[a];
-        }
+        *W.kcol(t, ra) = f4(Ka);
+        *W.kcol(t, rb) = f4(Kb);
+        if (m == 0) *W.kff(t) = f4(k);
       }
-    });
+    };
+    bool ok = pipe.run(
+        T, true, !diag,
+        [&](int t) {
+          const float* dgt = W.diag(t);
+          for (int i = m; i < NT; i += TEAM) Ce[i * (NT + 1)] = dgt[i];
+        },
+        ric_body);
     if (!ok) {
       status |= ELEM_PIPE_TIMEOUT;
       active = false;
       break;
     }
+    if (first && p.diag_cache) {
+      diag = !__any_sync(FULL, offd);
+      if (diag) {  // off-diagonal entries of the rebuilt blocks stay zero from here on
+        for (int f = lane; f < SLAB_E * CBLK; f += WARP) slab[f] = 0.0f;
+        __syncwarp();
+      }
+    }
     if (team_sum(fallback ? 1.0f : 0.0f, base) > 0.0f && active) status |= ELEM_CHOL_FALLBACK;
     if (first) {
-      float tn[NX];
+      float xT[NX], tn[NX];
+      load_rec_x(W.rec(nom, T), xT);
 #pragma unroll
-      for (int i = 0; i < NX; ++i) tn[i] = Xn(T, i) - xref(T, i);
+      for (int i = 0; i < NX; ++i) tn[i] = xT[i] - xref(T, i);
       best = (0.5f * team_sum(cost_q, base) + team_sum(cost_l, base)) + terminal_cost(Cf, cf, tn);
     }
     __syncwarp();
@@ -269,72 +365,95 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
     bool have = false, nan_seen = false;
     float cand[ILQR_MAX_ALPHAS_DEV];
     for (int a0 = 0; a0 < p.n_alpha; a0 += NAC) {
-      const float al = (a0 + m < p.n_alpha) ? p.alphas[a0 + m] : 0.0f;
+      const int j = a0 + m;
+      const float al = (j < p.n_alpha) ? p.alphas[j] : 0.0f;
+      const bool keep = valid && j < p.n_alpha && j < SOLVE_SLOTS - 1;  // candidate stored in a slot
+      const int cs = j < nom ? j : j + 1;
       float x[NX], sq = 0.0f, sl = 0.0f;
       load_x0(x);
-      ok = pipe.run(T, false, [&](int t, auto&& next) {
+      auto ls_body = [&](int t, auto&& next) {
         float xb[NX], ub[NU], kt[NU], u[NU];
-#pragma unroll
-        for (int i = 0; i < NX; ++i) xb[i] = Xn(t, i);
-#pragma unroll
-        for (int a = 0; a < NU; ++a) {
-          ub[a] = Un(t, a);
-          kt[a] = kat(t, a);
+        load_rec(W.rec(nom, t), xb, ub);
+        {
+          const float4 k4 = *W.kff(t);
+          kt[0] = k4.x; kt[1] = k4.y; kt[2] = k4.z; kt[3] = k4.w;
         }
-        candidate_u(x, xb, ub,
-                    [&](int a, float (&Kr)[NX]) {
-#pragma unroll
-                      for (int j = 0; j < NX; ++j) Kr[j] = Kat(t, a, j);
-                    },
-                    kt, al, lo, hi, u);
+        candidate_u(x, xb, ub, [&](int jj) { return *W.kcol(t, jj); }, kt, al, lo, hi, u);
+        if (keep) store_rec(W.rec(cs, t), x, u);
         float tau[NT];
 #pragma unroll
         for (int i = 0; i < NX; ++i) tau[i] = x[i] - xref(t, i);
 #pragma unroll
         for (int a = 0; a < NU; ++a) tau[NX + a] = u[a] - uref(t, a);
         float q = 0.0f;
+        if (diag) {
+          const float4* d4 = reinterpret_cast<const float4*>(W.diag(t));
+          const float4 g0 = d4[0], g1 = d4[1], g2 = d4[2], g3 = d4[3];
+          const float dgv[NT] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z,
+                                 g1.w, g2.x, g2.y, g2.z, g2.w, g3.x, g3.y};
+          bool nonfinite = false;
 #pragma unroll
-        for (int i = 0; i < NT; ++i) {
-          const float2* r2 = reinterpret_cast<const float2*>(Ce + i * NT);
-          float r = 0.0f;
-#pragma unroll
-          for (int j = 0; j < NT / 2; ++j) {
-            const float2 c2 = r2[j];
-            r = (j == 0) ? c2.x * tau[0] : fmaf(c2.x, tau[2 * j], r);
-            r = fmaf(c2.y, tau[2 * j + 1], r);
+          for (int i = 0; i < NT; ++i) {
+            q = fmaf(tau[i], dgv[i] * tau[i], q);
+            nonfinite |= !isfinite(tau[i]);
           }
-          q = fmaf(tau[i], r, q);
+          if (nonfinite) q = __int_as_float(0x7fffffff);  // dense form: 0 * inf or 0 * NaN
+        } else {
+#pragma unroll
+          for (int i = 0; i < NT; ++i) {
+            const float2* r2 = reinterpret_cast<const float2*>(Ce + i * NT);
+            float r = 0.0f;
+#pragma unroll
+            for (int jj = 0; jj < NT / 2; ++jj) {
+              const float2 c2 = r2[jj];
+              r = (jj == 0) ? c2.x * tau[0] : fmaf(c2.x, tau[2 * jj], r);
+              r = fmaf(c2.y, tau[2 * jj + 1], r);
+            }
+            q = fmaf(tau[i], r, q);
+          }
         }
         next();
-        float l = ldg_or0(cb + t * NT, valid) * tau[0];
+        float l;
+        {
+          const float2* c2 = reinterpret_cast<const float2*>(cb + t * NT);
+          float2 cc = valid ? __ldg(c2) : make_float2(0.0f, 0.0f);
+          l = cc.x * tau[0];
+          l = fmaf(cc.y, tau[1], l);
 #pragma unroll
-        for (int j = 1; j < NT; ++j) l = fmaf(ldg_or0(cb + t * NT + j, valid), tau[j], l);
+          for (int jj = 1; jj < NT / 2; ++jj) {
+            cc = valid ? __ldg(c2 + jj) : make_float2(0.0f, 0.0f);
+            l = fmaf(cc.x, tau[2 * jj], l);
+            l = fmaf(cc.y, tau[2 * jj + 1], l);
+          }
+        }
         sq += q;
         sl += l;
         float xn[NX];
         drone_step(x, u, dt, xn);
 #pragma unroll
         for (int i = 0; i < NX; ++i) x[i] = xn[i];
-      });
+      };
+      ok = pipe.run(T, false, !diag, [](int) {}, ls_body);
       if (!ok) break;
+      if (keep) store_rec_x(W.rec(cs, T), x);
       float tn[NX];
 #pragma unroll
       for (int i = 0; i < NX; ++i) tn[i] = x[i] - xref(T, i);
       const float mine = (0.5f * sq + sl) + terminal_cost(Cf, cf, tn);
       // gather the team's costs; torch.argmin semantics (first NaN, else first minimum)
 #pragma unroll
-      for (int j = 0; j < NAC; ++j) {
-        const float cj = __shfl_sync(FULL, mine, (base + j) & 31);
-        if (a0 + j >= p.n_alpha) continue;
-        cand[a0 + j] = cj;
+      for (int jj = 0; jj < NAC; ++jj) {
+        const float cj = __shfl_sync(FULL, mine, (base + jj) & 31);
+        if (a0 + jj >= p.n_alpha) continue;
+        cand[a0 + jj] = cj;
         if (!nan_seen) {
           if (cj != cj) {
             nan_seen = true;
-            jbest = a0 + j;
+            jbest = a0 + jj;
             cmin = cj;
           } else if (!have || cj < cmin) {
             have = true;
-            jbest = a0 + j;
+            jbest = a0 + jj;
             cmin = cj;
           }
         }
@@ -368,39 +487,31 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
       if (accept) best = cand[jsel];
       if (!accept && p.forced == nullptr) active = false;
     }
-    // ---- lane 0 re-runs the accepted candidate, writing the new nominal -----
-    if (__any_sync(FULL, accept)) {
-      if (accept && m == 0) {
+    // ---- new nominal: the accepted candidate's slot, or a re-run into a free
+    // slot for a step size that had none --------------------------------------
+    const bool rerun = accept && jsel >= SOLVE_SLOTS - 1;
+    if (accept && !rerun) nom = jsel < nom ? jsel : jsel + 1;
+    if (__any_sync(FULL, rerun)) {
+      const int dst = nom == 0 ? 1 : 0;
+      if (rerun && m == 0) {
         const float al = p.alphas[jsel];
         float x[NX];
         load_x0(x);
         for (int t = 0; t < T; ++t) {
           float xb[NX], ub[NU], kt[NU], u[NU];
-#pragma unroll
-          for (int i = 0; i < NX; ++i) xb[i] = Xn(t, i);
-#pragma unroll
-          for (int a = 0; a < NU; ++a) {
-            ub[a] = Un(t, a);
-            kt[a] = kat(t, a);
-          }
-          candidate_u(x, xb, ub,
-                      [&](int a, float (&Kr)[NX]) {
-#pragma unroll
-                        for (int j = 0; j < NX; ++j) Kr[j] = Kat(t, a, j);
-                      },
-                      kt, al, lo, hi, u);
-#pragma unroll
-          for (int i = 0; i < NX; ++i) Xn(t, i) = x[i];
-#pragma unroll
-          for (int a = 0; a < NU; ++a) Un(t, a) = u[a];
+          load_rec(W.rec(nom, t), xb, ub);
+          const float4 k4 = *W.kff(t);
+          kt[0] = k4.x; kt[1] = k4.y; kt[2] = k4.z; kt[3] = k4.w;
+          candidate_u(x, xb, ub, [&](int jj) { return *W.kcol(t, jj); }, kt, al, lo, hi, u);
+          store_rec(W.rec(dst, t), x, u);
           float xn[NX];
           drone_step(x, u, dt, xn);
 #pragma unroll
           for (int i = 0; i < NX; ++i) x[i] = xn[i];
         }
-#pragma unroll
-        for (int i = 0; i < NX; ++i) Xn(T, i) = x[i];
+        store_rec_x(W.rec(dst, T), x);
       }
+      if (rerun) nom = dst;
       __syncwarp();
     }
   }
@@ -408,14 +519,17 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
   // ---- outputs (lanes of a team split the writes) -----------------------------
   bool finite = true;
   if (valid) {
+    const float* nrec = reinterpret_cast<const float*>(W.rec(nom, 0));
+    const int64_t rstride = W.S * TRJ_REC;  // floats between the records of t and t + 1
     for (int f = m; f < (T + 1) * NX; f += TEAM) {
-      const float xv = *ws.x(bw, 0, f);
+      const int t = f / NX, i = f - t * NX;
+      const float xv = nrec[t * rstride + i];
       finite &= isfinite(xv);
       p.X[b * (T + 1) * NX + f] = xv;
     }
     for (int f = m; f < T * NU; f += TEAM) {
       const int t = f / NU, a = f - t * NU;
-      const float uv = Un(t, a);
+      const float uv = nrec[t * rstride + NX + a];
       finite &= isfinite(uv);
       p.U[b * T * NU + f] = uv;
       if (p.tight != nullptr) {
@@ -434,6 +548,7 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
   }
   const bool all_finite = team_sum(finite ? 0.0f : 1.0f, base) == 0.0f;
   if (!all_finite) status |= ELEM_NONFINITE;
+  if (diag) status |= ELEM_DIAG_COST;
   if (writer) {
     if (p.iters) p.iters[b] = iters;
     if (p.status) p.status[b] = status;

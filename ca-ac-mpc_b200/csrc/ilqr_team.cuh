@@ -35,23 +35,13 @@ constexpr uint32_t TSLAB_BYTES = EPW * CBLK * 4u;  // bytes one TMA box delivers
 
 __device__ __forceinline__ int row_a(int m) { return m < 4 ? 3 + m : 0; }
 
-// Access to one element's C_t block: dense (the TMA-staged slab) or diagonal
-// (the 14 diagonal values; every off-diagonal entry is an exact zero). Only
-// the rows the calling lane uses are held: its two state rows and the four
-// control rows.
+__device__ __forceinline__ int row_b(int m) { return m == 0 ? 1 : (m == 1 ? 2 : 5 + m); }
+
+// Access to one element's C_t block in shared memory.
 struct DenseC {
   const float* Ct;
   __device__ __forceinline__ float operator()(int i, int j) const { return Ct[i * NT + j]; }
 };
-struct DiagC {
-  int ra, rb;
-  float dra, drb, du0, du1, du2, du3;
-  __device__ __forceinline__ float operator()(int i, int j) const {
-    if (i != j) return 0.0f;
-    return i == ra ? dra : i == rb ? drb : i == NX ? du0 : i == NX + 1 ? du1 : i == NX + 2 ? du2 : du3;
-  }
-};
-__device__ __forceinline__ int row_b(int m) { return m == 0 ? 1 : (m == 1 ? 2 : 5 + m); }
 
 // Coefficients A[k][RA] for k = 3..9 and the own-row coefficient, for lane m.
 __device__ __forceinline__ void coef_a(const Jac& J, int m, float (&c)[8]) {
@@ -115,14 +105,15 @@ __device__ __forceinline__ void row_VA_VB(const Jac& J, const float (&Vr)[NX], f
 // Va, Vb: this lane's rows RA, RB of V (in V_{t+1}, out V_t); va_, vb_: the
 // matching entries of v. lxa, lxb: gradient terms of those rows; the four
 // control gradient terms are read from xc[X_LU..] (written by lanes 0..3
-// before the call). xc: this element's exchange area. Ct: this
-// element's C_t block in shared memory. after_c() is called once every lane
+// before the call). live: the lane's team owns a batch element. xc: this
+// element's exchange area. Ct: this element's C_t block in shared memory
+// (DenseC). after_c() is called once every lane
 // is done reading Ct (it may reuse the slab). Outputs: Ka, Kb = K[:, RA],
 // K[:, RB]; k. Returns false if the Cholesky failed (SVD inverse used).
 template <bool MASKED, class CAcc, class AfterC>
 __device__ __forceinline__ bool team_riccati(float (&Va)[NX], float (&Vb)[NX], float& va_, float& vb_,
                                              const Jac& J, const CAcc& Ct, float lxa, float lxb,
-                                             float reg, uint32_t tight, int m,
+                                             float reg, uint32_t tight, int m, bool live,
                                              float* __restrict__ xc, AfterC&& after_c, float (&Ka)[NU],
                                              float (&Kb)[NU], float (&k)[NU]) {
   const int ra = row_a(m), rb = row_b(m);
@@ -264,7 +255,9 @@ __device__ __forceinline__ bool team_riccati(float (&Va)[NX], float (&Vb)[NX], f
           Qs[a][b] = Quu[a][b] + (a == b ? reg : 0.0f);
         }
       }
-    ok = chol4(Qs, L);
+    // A lane without an element (live == false) never takes the SVD path: its
+    // numbers are discarded, and the warp would wait for its sweeps.
+    ok = chol4(Qs, L) || !live;
     if (!ok) svd_inverse4(Qs, Mi);
   }
   auto solve = [&](const float (&rhs)[NU], float (&out)[NU]) {
@@ -400,29 +393,40 @@ struct TeamPipe {
   }
   // Runs body(t, next) over t (reverse if rev). body must call next() exactly
   // once, after its last read of the slab; next() syncs the warp and starts
-  // the copy of the following step. Returns false on a (bounded) wait timeout.
-  template <class F>
-  __device__ __forceinline__ bool run(int T, bool rev, F&& body) {
-    issue(rev ? T - 1 : 0);
+  // the copy of the following step. With dense == false no copy is made:
+  // fill(t) runs before body(t) instead (it may write the slab) and the warp
+  // syncs after it. Returns false on a (bounded) wait timeout.
+  template <class Fill, class F>
+  __device__ __forceinline__ bool run(int T, bool rev, bool dense, Fill&& fill, F&& body) {
+    if (dense) issue(rev ? T - 1 : 0);
     for (int s = 0; s < T; ++s) {
-      const bool got = mbar_wait(bar, parity);
-      if (!__all_sync(FULL, got)) {
-        mbar_wait(bar, parity);  // give the copy in flight one more bounded wait
-        ok = false;
-        return false;
-      }
-      parity ^= 1u;
       const int t = rev ? T - 1 - s : s;
+      if (dense) {
+        const bool got = mbar_wait(bar, parity);
+        if (!__all_sync(FULL, got)) {
+          mbar_wait(bar, parity);  // give the copy in flight one more bounded wait
+          ok = false;
+          return false;
+        }
+        parity ^= 1u;
+      } else {
+        fill(t);
+        __syncwarp();
+      }
       bool called = false;
       auto next = [&]() {
         __syncwarp();
-        if (s + 1 < T) issue(rev ? t - 1 : t + 1);
+        if (dense && s + 1 < T) issue(rev ? t - 1 : t + 1);
         called = true;
       };
       body(t, next);
       if (!called) next();
     }
     return true;
+  }
+  template <class F>
+  __device__ __forceinline__ bool run(int T, bool rev, F&& body) {
+    return run(T, rev, true, [](int) {}, body);
   }
 };
 

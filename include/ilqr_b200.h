@@ -47,6 +47,7 @@ typedef enum {
 #define ILQR_ELEM_CHOL_FALLBACK 1u /* a Q_uu Cholesky failed; SVD inverse used */
 #define ILQR_ELEM_NONFINITE 2u     /* X or U of the returned solution not finite */
 #define ILQR_ELEM_PIPE_TIMEOUT 4u  /* an on-chip copy wait gave up (results invalid) */
+#define ILQR_ELEM_DIAG_COST 8u     /* C blocks were diagonal: passes after the first read their diagonals only */
 
 int ilqr_b200_abi_version(void);
 const char* ilqr_b200_status_string(int status);
@@ -78,6 +79,10 @@ int ilqr_b200_solve_workspace_size(int64_t B, int32_t T, size_t* bytes);
  *   iters [B] int32 (iterations run), elem_status [B] uint32,
  *   best_cost [B] float, stall_iter [B] int32 (first rejected iteration or
  *   max_iter), stall_gap [B] float (|cost - best| at that rejection).
+ * When every C_t block of a group of six consecutive elements is diagonal
+ * (checked during the first pass), later passes read a compact copy of the
+ * diagonals from the workspace instead of C; results are identical to the
+ * dense path. The environment variable ILQR_B200_DIAG_CACHE=0 turns this off.
  */
 int ilqr_b200_solve_f32(
     const float* x0, const float* U_init, const float* C, const float* c,
@@ -99,7 +104,7 @@ int ilqr_b200_solve_f32(
  * workspace: the scratch is a fixed ILQR_NOALLOC_SCRATCH_BYTES array inside
  * this library that every GPU loading the library holds until exit. Problems
  * whose ilqr_b200_solve_workspace_size exceeds it are rejected with
- * ILQR_ERR_NOALLOC_LIMIT (at T = 20 that is B > 3584). The entry point
+ * ILQR_ERR_NOALLOC_LIMIT (at T = 20 that is B > 1280). The entry point
  * allocates nothing. Its first call on a device looks up the array's device
  * address, so make that first call before any stream capture. All calls
  * share the array: calls that overlap on the GPU (other streams, other host

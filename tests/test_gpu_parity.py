@@ -232,3 +232,53 @@ def test_training_scale_properties(B, T, iters):
     g2 = nat.backward(a["X"], a["U"], t["C"], g(2 * gX), g(2 * gU), tight=a["tight"], dt=wl.DT)
     for k in g1:
         assert torch.equal(2 * g1[k], g2[k]), k
+
+
+def test_diag_cost_cache_identical_to_dense_path(monkeypatch):
+    """Diagonal C blocks are detected in the first pass and later passes read
+    only their diagonals. Every result must equal the dense path's
+    (ILQR_B200_DIAG_CACHE=0): here with one warp of six elements holding a
+    single off-diagonal entry (that warp stays dense) and one element that
+    starts at an infinite position (the quadratic form's 0 * inf = NaN rule)."""
+    cfg, inp = wl.config_inputs("rollout_b16384_t20", B=96)
+    inp["C"][7, 3, 2, 5] = inp["C"][7, 3, 5, 2] = np.float32(1e-3)
+    inp["x0"][20, 0] = np.inf
+    t = {k: g(v) for k, v in inp.items()}
+    args = (t["x0"], t["U_init"], t["C"], t["c"], None, None, None, None, g(wl.U_MIN), g(wl.U_MAX))
+    kw = dict(dt=wl.DT, max_iter=cfg["max_iter"], alphas=cfg["alphas"], want_trace=True, want_stats=True)
+    on = {k: v.cpu().numpy() for k, v in nat.solve(*args, **kw).items()}
+    monkeypatch.setenv("ILQR_B200_DIAG_CACHE", "0")
+    off = {k: v.cpu().numpy() for k, v in nat.solve(*args, **kw).items()}
+    diag_bit = 8
+    assert not (off["status"] & diag_bit).any()
+    warp_dense = np.zeros(96, bool)
+    warp_dense[6:12] = True
+    assert ((on["status"] & diag_bit) != 0).tolist() == (~warp_dense).tolist()
+    assert not np.isfinite(off["X"][20]).all()
+    for k in on:
+        a, b = on[k], off[k]
+        if k == "status":
+            a = a & ~diag_bit
+        assert np.array_equal(a, b, equal_nan=a.dtype.kind == "f"), k
+
+
+@pytest.mark.parametrize("forced", [False, True])
+def test_more_step_sizes_than_candidate_slots(forced):
+    """Seven step sizes: the first five candidates are kept in workspace slots,
+    the last two are re-run when accepted. Free-running and replaying a trace
+    that accepts step sizes 6 and 7, the GPU matches the oracle given the same
+    decisions."""
+    d = dict(load("cfg3_b16_t20"))
+    d["alphas"] = np.array([1.0, 0.8, 0.6, 0.5, 0.3, 0.2, 0.1], np.float32)
+    trace = None
+    if forced:
+        trace = np.tile(np.array([[5, 6, 0, -1, 6, 2, 5, -1, -1, 4]], np.int8), (16, 1))
+        trace = trace[:, : int(d["max_iter"])]
+        trace[1::3] = np.roll(trace[1::3], 2, axis=1)
+    r, kw = gpu_solve(d, forced=trace)
+    o = O.solve(d["x0"], d["U_init"], d["C"], d["c"], forced=r["trace"] if trace is None else trace, **kw)
+    assert max_rel(r["X"], o["X"]) <= TOL_XU
+    assert max_rel(r["U"], o["U"]) <= TOL_XU
+    if forced:
+        acc = trace >= 0
+        assert (r["trace"][acc] == trace[acc]).all()
