@@ -170,24 +170,22 @@ struct Chol4 {
 };
 
 __device__ __forceinline__ bool chol4(const float (&M)[NU][NU], Chol4& L) {
+  // Only the reciprocals of the diagonal of L enter the solves: each is one
+  // correctly rounded 1/sqrt(d).
   const float d0 = M[0][0];
-  const float l00 = sqrtf(d0);
-  L.r0 = 1.0f / l00;
+  L.r0 = __frsqrt_rn(d0);
   L.l10 = M[1][0] * L.r0;
   L.l20 = M[2][0] * L.r0;
   L.l30 = M[3][0] * L.r0;
   const float d1 = M[1][1] - L.l10 * L.l10;
-  const float l11 = sqrtf(d1);
-  L.r1 = 1.0f / l11;
+  L.r1 = __frsqrt_rn(d1);
   L.l21 = (M[2][1] - L.l20 * L.l10) * L.r1;
   L.l31 = (M[3][1] - L.l30 * L.l10) * L.r1;
   const float d2 = (M[2][2] - L.l20 * L.l20) - L.l21 * L.l21;
-  const float l22 = sqrtf(d2);
-  L.r2 = 1.0f / l22;
+  L.r2 = __frsqrt_rn(d2);
   L.l32 = ((M[3][2] - L.l30 * L.l20) - L.l31 * L.l21) * L.r2;
   const float d3 = ((M[3][3] - L.l30 * L.l30) - L.l31 * L.l31) - L.l32 * L.l32;
-  const float l33 = sqrtf(d3);
-  L.r3 = 1.0f / l33;
+  L.r3 = __frsqrt_rn(d3);
   return (d0 > 0.0f) && (d1 > 0.0f) && (d2 > 0.0f) && (d3 > 0.0f);
 }
 

@@ -314,7 +314,9 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
                     (v.z != 0.0f && (f + 2) % (NT + 1) != 0) || (v.w != 0.0f && (f + 3) % (NT + 1) != 0);
           }
           float* dgt = W.diag(t);
-          for (int i = m; i < NT; i += TEAM) dgt[i] = Ce[i * (NT + 1)];
+#pragma unroll
+          for (int s3 = 0; s3 < 3; ++s3)
+            if (m + TEAM * s3 < NT) dgt[m + TEAM * s3] = Ce[(m + TEAM * s3) * (NT + 1)];
         }
       }
       __syncwarp();
@@ -333,7 +335,9 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
         T, true, !diag,
         [&](int t) {
           const float* dgt = W.diag(t);
-          for (int i = m; i < NT; i += TEAM) Ce[i * (NT + 1)] = dgt[i];
+#pragma unroll
+          for (int s3 = 0; s3 < 3; ++s3)
+            if (m + TEAM * s3 < NT) Ce[(m + TEAM * s3) * (NT + 1)] = dgt[m + TEAM * s3];
         },
         ric_body);
     if (!ok) {

@@ -96,8 +96,8 @@ __device__ __forceinline__ void row_VA_VB(const Jac& J, const float (&Vr)[NX], f
 //   Q_uu = l_uu + B^T V B + reg I
 //   q_x = l_x + A^T v              q_u = l_u + B^T v
 //   [K | k] = -chol_solve(Q_uu + reg I, [Q_ux | q_u])   (reg added twice)
-//   V = Q_xx + (K^T Q_uu) K + K^T Q_ux + Q_xu K
-//   v = q_x + (K^T Q_uu) k + K^T q_u + Q_xu k
+//   V = Q_xx + (K^T Q_uu + Q_xu) K + K^T Q_ux
+//   v = q_x + (K^T Q_uu + Q_xu) k + K^T q_u
 // Backward (MASKED=true), _zero_constrained_lqr (controller.py:1035-1110):
 //   tight rows/cols of Q_uu zeroed, +1 on their diagonal, + (1e-8 reg) I;
 //   tight rows of Q_ux and entries of q_u zeroed for the solve only;
@@ -310,15 +310,17 @@ __device__ __forceinline__ bool team_riccati(float (&Va)[NX], float (&Vb)[NX], f
       w[a] = acc + qu[a];
     }
   }
+  // (K^T Q_uu) K + Q_xu K is formed as (K^T Q_uu + Q_xu) K: one 4-term
+  // product per entry instead of two.
   auto update_row = [&](float (&Vr)[NX], const float (&Qr)[NX], const float (&Kr)[NU], const float (&Qxr)[NU],
                         float qxr) -> float {
-    float Z[NU];
+    float Wr[NU];
 #pragma unroll
     for (int a = 0; a < NU; ++a) {
       float acc = Kr[0] * Quu[0][a];
 #pragma unroll
       for (int b = 1; b < NU; ++b) acc = fmaf(Kr[b], Quu[b][a], acc);
-      Z[a] = acc;
+      Wr[a] = acc + Qxr[a];
     }
     float vk;
     if (MASKED) {
@@ -330,33 +332,27 @@ __device__ __forceinline__ bool team_riccati(float (&Va)[NX], float (&Vb)[NX], f
       for (int a = 1; a < NU; ++a) t3 = fmaf(Qxr[a], k[a], t3);
       vk = (qxr + t2) + t3;
     } else {
-      float t1 = Z[0] * k[0];
+      float t1 = Wr[0] * k[0];
 #pragma unroll
-      for (int a = 1; a < NU; ++a) t1 = fmaf(Z[a], k[a], t1);
+      for (int a = 1; a < NU; ++a) t1 = fmaf(Wr[a], k[a], t1);
       float t2 = Kr[0] * qu[0];
 #pragma unroll
       for (int a = 1; a < NU; ++a) t2 = fmaf(Kr[a], qu[a], t2);
-      float t3 = Qxr[0] * k[0];
-#pragma unroll
-      for (int a = 1; a < NU; ++a) t3 = fmaf(Qxr[a], k[a], t3);
-      vk = ((qxr + t1) + t2) + t3;
+      vk = (qxr + t1) + t2;
     }
 #pragma unroll
     for (int c = 0; c < NX; ++c) {
       const float4 qc = *reinterpret_cast<const float4*>(xc + X_QXU + c * NU);
       const float4 k4 = *reinterpret_cast<const float4*>(xc + X_K + c * NU);
-      const float Kc[NU] = {k4.x, k4.y, k4.z, k4.w};
-      float t1 = Z[0] * Kc[0];
-#pragma unroll
-      for (int a = 1; a < NU; ++a) t1 = fmaf(Z[a], Kc[a], t1);
+      float t1 = Wr[0] * k4.x;
+      t1 = fmaf(Wr[1], k4.y, t1);
+      t1 = fmaf(Wr[2], k4.z, t1);
+      t1 = fmaf(Wr[3], k4.w, t1);
       float t2 = Kr[0] * qc.x;
       t2 = fmaf(Kr[1], qc.y, t2);
       t2 = fmaf(Kr[2], qc.z, t2);
       t2 = fmaf(Kr[3], qc.w, t2);
-      float t3 = Qxr[0] * Kc[0];
-#pragma unroll
-      for (int a = 1; a < NU; ++a) t3 = fmaf(Qxr[a], Kc[a], t3);
-      Vr[c] = ((Qr[c] + t1) + t2) + t3;
+      Vr[c] = (Qr[c] + t1) + t2;
     }
     return vk;
   };
