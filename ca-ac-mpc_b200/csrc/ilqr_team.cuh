@@ -21,15 +21,16 @@ namespace ilqr {
 
 constexpr int TEAM = 5;
 constexpr int EPW = 6;        // batch elements per warp
-constexpr int XS = 164;       // exchange floats per element (164 = 4 mod 32: bank spread)
-// exchange layout (floats); VA/VB/v are dead once K/Q_xu are written (a
-// warp sync separates the phases)
+constexpr int XS = 180;       // exchange floats per element (180 = 20 mod 32: bank spread)
+// exchange layout (floats). V B, v and l_u are dead once the gains are solved
+// (a warp sync separates the phases); K and Q_xu rows take their place while
+// the V A rows stay for the value update.
 constexpr int X_VA = 0;       // [10][10] rows of V A
 constexpr int X_VB = 100;     // [10][4]  rows of V B
 constexpr int X_V = 140;      // [10]     v
-constexpr int X_K = 0;        // [10][4]  K transposed: column c of K at X_K + 4c (reuses X_VA)
-constexpr int X_QXU = 40;     // [10][4]  Q_xu rows (reuses X_VA)
-constexpr int X_LU = 160;     // [4]      l_u
+constexpr int X_LU = 152;     // [4]      l_u
+constexpr int X_K = 100;      // [10][4]  K transposed: column c of K at X_K + 4c (over V B)
+constexpr int X_QXU = 140;    // [10][4]  Q_xu rows (over v, l_u)
 constexpr int SLAB_E = EPW + 1;  // slab rows incl. a pad row for the two spare lanes
 constexpr uint32_t TSLAB_BYTES = EPW * CBLK * 4u;  // bytes one TMA box delivers
 
@@ -107,8 +108,8 @@ __device__ __forceinline__ void row_VA_VB(const Jac& J, const float (&Vr)[NX], f
 // control gradient terms are read from xc[X_LU..] (written by lanes 0..3
 // before the call). live: the lane's team owns a batch element. xc: this
 // element's exchange area. Ct: this element's C_t block in shared memory
-// (DenseC). after_c() is called once every lane
-// is done reading Ct (it may reuse the slab). Outputs: Ka, Kb = K[:, RA],
+// (DenseC). after_c() is called at the end, once every lane is done reading
+// Ct and the exchange area (it may reuse the slab); it must sync the warp. Outputs: Ka, Kb = K[:, RA],
 // K[:, RB]; k. Returns false if the Cholesky failed (SVD inverse used).
 template <bool MASKED, class CAcc, class AfterC>
 __device__ __forceinline__ bool team_riccati(float (&Va)[NX], float (&Vb)[NX], float& va_, float& vb_,
@@ -135,29 +136,14 @@ __device__ __forceinline__ bool team_riccati(float (&Va)[NX], float (&Vb)[NX], f
   xc[X_V + rb] = vb_;
   __syncwarp();
 
-  // ---- Q_xx, Q_xu, q_x rows (A^T (V A) etc.), Q_uu and q_u ----------------
+  // ---- Q_xu rows and q_x entries of my rows, Q_uu and q_u -----------------
   float ca[8];
   coef_a(J, m, ca);
   const float cb = (m >= 2) ? J.dt : 0.0f;
   const int pb = (m >= 2) ? m - 2 : 0;
-  float Qa[NX], Qb[NX], Qxa[NU], Qxb[NU], qxa, qxb;
+  float Qxa[NU], Qxb[NU], qxa, qxb;
   {
-    // RA: sum over rows 3..9 of (V A) and V B, then the own row.
-#pragma unroll
-    for (int c = 0; c < NX; c += 2) {
-      float2 acc = make_float2(0.0f, 0.0f);
-#pragma unroll
-      for (int s = 0; s < 7; ++s) {
-        const float2 r = *reinterpret_cast<const float2*>(xc + X_VA + (3 + s) * NX + c);
-        acc.x = fmaf(ca[s], r.x, acc.x);
-        acc.y = fmaf(ca[s], r.y, acc.y);
-      }
-      const float2 own = *reinterpret_cast<const float2*>(xc + X_VA + ra * NX + c);
-      acc.x = fmaf(ca[7], own.x, acc.x);
-      acc.y = fmaf(ca[7], own.y, acc.y);
-      Qa[c] = Ct(ra, c) + acc.x;
-      Qa[c + 1] = Ct(ra, c + 1) + acc.y;
-    }
+    // RA: sum over rows 3..9 of V B (and v), then the own row.
     float4 acc4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     float accv = 0.0f;
 #pragma unroll
@@ -178,9 +164,6 @@ __device__ __forceinline__ bool team_riccati(float (&Va)[NX], float (&Vb)[NX], f
     }
     qxa = lxa + fmaf(ca[7], va_, accv);
     // RB: own row plus cb times row pb.
-#pragma unroll
-    for (int c = 0; c < NX; ++c)
-      Qb[c] = Ct(rb, c) + fmaf(cb, xc[X_VA + pb * NX + c], xc[X_VA + rb * NX + c]);
 #pragma unroll
     for (int a = 0; a < NU; ++a)
       Qxb[a] = Ct(rb, NX + a) + fmaf(cb, xc[X_VB + pb * NU + a], xc[X_VB + rb * NU + a]);
@@ -234,7 +217,7 @@ __device__ __forceinline__ bool team_riccati(float (&Va)[NX], float (&Vb)[NX], f
       }
     }
   }
-  after_c();  // syncs the warp: C_t and the V A / V B / v rows are no longer read
+  __syncwarp();  // V B, v and l_u are no longer read: K and Q_xu rows go there
 
   // ---- gains -----------------------------------------------------------------
   bool ok;
@@ -292,14 +275,15 @@ __device__ __forceinline__ bool team_riccati(float (&Va)[NX], float (&Vb)[NX], f
 #pragma unroll
     for (int a = 0; a < NU; ++a) k[a] = -sol[a];
   }
-  // K columns and Q_xu rows -> exchange (over the dead V A area)
+  // K columns and Q_xu rows -> exchange (over V B, v, l_u)
   *reinterpret_cast<float4*>(xc + X_K + ra * NU) = make_float4(Ka[0], Ka[1], Ka[2], Ka[3]);
   *reinterpret_cast<float4*>(xc + X_K + rb * NU) = make_float4(Kb[0], Kb[1], Kb[2], Kb[3]);
   *reinterpret_cast<float4*>(xc + X_QXU + ra * NU) = make_float4(Qxa[0], Qxa[1], Qxa[2], Qxa[3]);
   *reinterpret_cast<float4*>(xc + X_QXU + rb * NU) = make_float4(Qxb[0], Qxb[1], Qxb[2], Qxb[3]);
-  __syncwarp();
 
-  // ---- value update for my rows: V = Q_xx + (K^T Q_uu) K + K^T Q_ux + Q_xu K ---
+  // ---- value update for my rows -------------------------------------------------
+  // (K^T Q_uu) K + Q_xu K is formed as (K^T Q_uu + Q_xu) K: one 4-term
+  // product per entry instead of two. W = K^T Q_uu + Q_xu for my rows.
   float w[NU];
   if (MASKED) {
 #pragma unroll
@@ -310,11 +294,7 @@ __device__ __forceinline__ bool team_riccati(float (&Va)[NX], float (&Vb)[NX], f
       w[a] = acc + qu[a];
     }
   }
-  // (K^T Q_uu) K + Q_xu K is formed as (K^T Q_uu + Q_xu) K: one 4-term
-  // product per entry instead of two.
-  auto update_row = [&](float (&Vr)[NX], const float (&Qr)[NX], const float (&Kr)[NU], const float (&Qxr)[NU],
-                        float qxr) -> float {
-    float Wr[NU];
+  auto wrow = [&](const float (&Kr)[NU], const float (&Qxr)[NU], float (&Wr)[NU]) {
 #pragma unroll
     for (int a = 0; a < NU; ++a) {
       float acc = Kr[0] * Quu[0][a];
@@ -322,7 +302,8 @@ __device__ __forceinline__ bool team_riccati(float (&Va)[NX], float (&Vb)[NX], f
       for (int b = 1; b < NU; ++b) acc = fmaf(Kr[b], Quu[b][a], acc);
       Wr[a] = acc + Qxr[a];
     }
-    float vk;
+  };
+  auto vrow = [&](const float (&Kr)[NU], const float (&Qxr)[NU], const float (&Wr)[NU], float qxr) {
     if (MASKED) {
       float t2 = Kr[0] * w[0];
 #pragma unroll
@@ -330,7 +311,7 @@ __device__ __forceinline__ bool team_riccati(float (&Va)[NX], float (&Vb)[NX], f
       float t3 = Qxr[0] * k[0];
 #pragma unroll
       for (int a = 1; a < NU; ++a) t3 = fmaf(Qxr[a], k[a], t3);
-      vk = (qxr + t2) + t3;
+      return (qxr + t2) + t3;
     } else {
       float t1 = Wr[0] * k[0];
 #pragma unroll
@@ -338,27 +319,59 @@ __device__ __forceinline__ bool team_riccati(float (&Va)[NX], float (&Vb)[NX], f
       float t2 = Kr[0] * qu[0];
 #pragma unroll
       for (int a = 1; a < NU; ++a) t2 = fmaf(Kr[a], qu[a], t2);
-      vk = (qxr + t1) + t2;
+      return (qxr + t1) + t2;
+    }
+  };
+  float Wa[NU], Wb[NU];
+  wrow(Ka, Qxa, Wa);
+  wrow(Kb, Qxb, Wb);
+  va_ = vrow(Ka, Qxa, Wa, qxa);
+  vb_ = vrow(Kb, Qxb, Wb, qxb);
+  __syncwarp();  // K and Q_xu rows of the whole team are in the exchange
+  // Q_xx entries of my rows are formed column by column here (A^T (V A) from
+  // the V A rows still in the exchange, plus l_xx), then
+  // V[r][c] = (Q_xx[r][c] + W_r K_c) + K_r Q_xu[c].
+#pragma unroll
+  for (int c = 0; c < NX; c += 2) {
+    float2 qa = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int s = 0; s < 7; ++s) {
+      const float2 r = *reinterpret_cast<const float2*>(xc + X_VA + (3 + s) * NX + c);
+      qa.x = fmaf(ca[s], r.x, qa.x);
+      qa.y = fmaf(ca[s], r.y, qa.y);
+    }
+    {
+      const float2 own = *reinterpret_cast<const float2*>(xc + X_VA + ra * NX + c);
+      qa.x = Ct(ra, c) + fmaf(ca[7], own.x, qa.x);
+      qa.y = Ct(ra, c + 1) + fmaf(ca[7], own.y, qa.y);
+    }
+    float2 qb;
+    {
+      const float2 pr = *reinterpret_cast<const float2*>(xc + X_VA + pb * NX + c);
+      const float2 own = *reinterpret_cast<const float2*>(xc + X_VA + rb * NX + c);
+      qb.x = Ct(rb, c) + fmaf(cb, pr.x, own.x);
+      qb.y = Ct(rb, c + 1) + fmaf(cb, pr.y, own.y);
     }
 #pragma unroll
-    for (int c = 0; c < NX; ++c) {
-      const float4 qc = *reinterpret_cast<const float4*>(xc + X_QXU + c * NU);
-      const float4 k4 = *reinterpret_cast<const float4*>(xc + X_K + c * NU);
-      float t1 = Wr[0] * k4.x;
-      t1 = fmaf(Wr[1], k4.y, t1);
-      t1 = fmaf(Wr[2], k4.z, t1);
-      t1 = fmaf(Wr[3], k4.w, t1);
-      float t2 = Kr[0] * qc.x;
-      t2 = fmaf(Kr[1], qc.y, t2);
-      t2 = fmaf(Kr[2], qc.z, t2);
-      t2 = fmaf(Kr[3], qc.w, t2);
-      Vr[c] = (Qr[c] + t1) + t2;
+    for (int h = 0; h < 2; ++h) {
+      const float4 k4 = *reinterpret_cast<const float4*>(xc + X_K + (c + h) * NU);
+      const float4 q4 = *reinterpret_cast<const float4*>(xc + X_QXU + (c + h) * NU);
+      auto entry = [&](float q, const float (&Wr)[NU], const float (&Kr)[NU]) {
+        float t1 = Wr[0] * k4.x;
+        t1 = fmaf(Wr[1], k4.y, t1);
+        t1 = fmaf(Wr[2], k4.z, t1);
+        t1 = fmaf(Wr[3], k4.w, t1);
+        float t2 = Kr[0] * q4.x;
+        t2 = fmaf(Kr[1], q4.y, t2);
+        t2 = fmaf(Kr[2], q4.z, t2);
+        t2 = fmaf(Kr[3], q4.w, t2);
+        return (q + t1) + t2;
+      };
+      Va[c + h] = entry(h ? qa.y : qa.x, Wa, Ka);
+      Vb[c + h] = entry(h ? qb.y : qb.x, Wb, Kb);
     }
-    return vk;
-  };
-  va_ = update_row(Va, Qa, Ka, Qxa, qxa);
-  vb_ = update_row(Vb, Qb, Kb, Qxb, qxb);
-  __syncwarp();  // the exchange area is rewritten by the next step
+  }
+  after_c();  // syncs the warp: C_t and the exchange area are no longer read
   return ok;
 }
 
