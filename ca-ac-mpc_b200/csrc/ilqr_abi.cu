@@ -105,6 +105,12 @@ int ilqr_b200_solve_f32(const float* x0, const float* U_init, const float* C, co
   if (!x0 || !U_init || !C || !c || !X || !U) return ILQR_ERR_INVALID_ARGUMENT;
   if (!aligned16(C)) return ILQR_ERR_MISALIGNED;
   if ((C_final == nullptr) && (c_final != nullptr)) return ILQR_ERR_INVALID_ARGUMENT;
+  // workspace records are indexed with 32-bit unsigned integers on the device
+  {
+    const int64_t recs = ilqr::SOLVE_SLOTS * ((int64_t)T + 1) > (int64_t)T * 10 ? ilqr::SOLVE_SLOTS * ((int64_t)T + 1)
+                                                                                 : (int64_t)T * 10;
+    if (recs * ilqr::ws_stride(B) >= ((int64_t)1 << 32)) return ILQR_ERR_INVALID_ARGUMENT;
+  }
   size_t need = 0;
   ilqr_b200_solve_workspace_size(B, T, &need);
   if (workspace == nullptr || workspace_bytes < need) return ILQR_ERR_WORKSPACE;

@@ -130,7 +130,7 @@ __global__ void adjoint_lqr_kernel(const float* __restrict__ A, const float* __r
     Chol4 L;
     float Mi[NU][NU];
     const bool ok = chol4(Qs, L);
-    if (!ok) svd_inverse4(Qs, Mi);
+    if (!ok) svd_inverse4(&Qs[0][0], &Mi[0][0]);
     float K[NU][NX], k[NU];
     for (int j = 0; j <= NX; ++j) {
       float rhs[NU], sol[NU];

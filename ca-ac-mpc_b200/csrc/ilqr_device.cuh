@@ -205,10 +205,11 @@ __device__ __forceinline__ void chol4_solve(const Chol4& L, const float (&b)[NU]
 // branch (DifferentialMPC/controller.py:758-779): M^-1 = V diag(1/S) U^T with
 // singular values floored at max(S)/1e12. One-sided Jacobi SVD (Hestenes) on
 // the columns of M, a fixed number of sweeps (bounded).
-static __device__ __noinline__ void svd_inverse4(const float (&M)[NU][NU], float (&Mi)[NU][NU]) {
+// M and Mi are row-major 4 x 4 arrays (in shared memory for the callers here).
+static __device__ __noinline__ void svd_inverse4(const float* M, float* Mi) {
   float W[NU][NU], Vr[NU][NU];
   for (int i = 0; i < NU; ++i)
-    for (int j = 0; j < NU; ++j) { W[i][j] = M[i][j]; Vr[i][j] = (i == j) ? 1.0f : 0.0f; }
+    for (int j = 0; j < NU; ++j) { W[i][j] = M[i * NU + j]; Vr[i][j] = (i == j) ? 1.0f : 0.0f; }
   for (int sweep = 0; sweep < 12; ++sweep) {
     float off = 0.0f;
     for (int p = 0; p < NU - 1; ++p)
@@ -244,15 +245,18 @@ static __device__ __noinline__ void svd_inverse4(const float (&M)[NU][NU], float
     smax = fmaxf(smax, S[j]);
   }
   const float floor_ = smax / 1e12f;
+  float R[NU][NU];
   for (int i = 0; i < NU; ++i)
-    for (int j = 0; j < NU; ++j) Mi[i][j] = 0.0f;
+    for (int j = 0; j < NU; ++j) R[i][j] = 0.0f;
   for (int k = 0; k < NU; ++k) {
     if (!(S[k] > 0.0f)) continue;
     const float sr = S[k] > floor_ ? S[k] : floor_;
     const float sc = 1.0f / (S[k] * sr);  // u_k = w_k / S_k, times 1/S_reg
     for (int i = 0; i < NU; ++i)
-      for (int j = 0; j < NU; ++j) Mi[i][j] = fmaf(Vr[i][k] * sc, W[j][k], Mi[i][j]);
+      for (int j = 0; j < NU; ++j) R[i][j] = fmaf(Vr[i][k] * sc, W[j][k], R[i][j]);
   }
+  for (int i = 0; i < NU; ++i)
+    for (int j = 0; j < NU; ++j) Mi[i * NU + j] = R[i][j];
 }
 
 // --------------------------------------------------------------------------

@@ -62,25 +62,33 @@ __device__ __forceinline__ float terminal_cost(const float* __restrict__ Cf, con
   return 0.5f * q + l;
 }
 
-// The workspace records of one element (layout in ilqr_kernels.h).
+// The workspace records of one element (layout in ilqr_kernels.h). Addresses
+// are rebuilt from the kernel parameters on every use (they live in the
+// constant bank), so only the element index occupies a register; record
+// indices fit in 32 bits (checked by the host).
 struct SolveWs {
-  float* trj;
-  float* gk;
-  float* gkk;
-  float* dg;
-  int64_t S;
-  int T1;
-  int64_t b;
+  const SolveParams& p;
+  uint32_t b;
+  __device__ __forceinline__ uint32_t S() const { return (uint32_t)p.S; }
   __device__ __forceinline__ float4* rec(int s, int t) const {
-    return reinterpret_cast<float4*>(trj + (((int64_t)s * T1 + t) * S + b) * TRJ_REC);
+    const uint32_t r = ((uint32_t)s * (uint32_t)(p.T + 1) + (uint32_t)t) * S() + b;
+    return reinterpret_cast<float4*>(p.ws + (size_t)r * TRJ_REC);
+  }
+  __device__ __forceinline__ float* gk() const {
+    return p.ws + (size_t)SOLVE_SLOTS * (uint32_t)(p.T + 1) * S() * TRJ_REC;
   }
   __device__ __forceinline__ float4* kcol(int t, int j) const {
-    return reinterpret_cast<float4*>(gk + ((int64_t)(t * NX + j) * S + b) * 4);
+    const uint32_t r = (uint32_t)(t * NX + j) * S() + b;
+    return reinterpret_cast<float4*>(gk() + (size_t)r * 4);
   }
   __device__ __forceinline__ float4* kff(int t) const {
-    return reinterpret_cast<float4*>(gkk + ((int64_t)t * S + b) * 4);
+    const uint32_t r = (uint32_t)t * S() + b;
+    return reinterpret_cast<float4*>(gk() + (size_t)p.T * NX * S() * 4 + (size_t)r * 4);
   }
-  __device__ __forceinline__ float* diag(int t) const { return dg + ((int64_t)t * S + b) * TRJ_REC; }
+  __device__ __forceinline__ float* diag(int t) const {
+    const uint32_t r = (uint32_t)t * S() + b;
+    return gk() + (size_t)p.T * (NX + 1) * S() * 4 + (size_t)r * TRJ_REC;
+  }
 };
 
 __device__ __forceinline__ void load_rec(const float4* r, float (&x)[NX], float (&u)[NU]) {
@@ -178,14 +186,7 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
   const int64_t bw = valid ? b : b0;  // workspace record read by this lane (never written when !valid)
   const int T = p.T;
   const float dt = p.dt;
-  SolveWs W;
-  W.trj = p.ws;
-  W.gk = W.trj + (int64_t)SOLVE_SLOTS * (T + 1) * p.S * TRJ_REC;
-  W.gkk = W.gk + (int64_t)T * NX * p.S * 4;
-  W.dg = W.gkk + (int64_t)T * p.S * 4;
-  W.S = p.S;
-  W.T1 = T + 1;
-  W.b = bw;
+  const SolveWs W{p, (uint32_t)bw};
 
   if (lane == 0) {
     mbar_init(bar, 1);
@@ -524,7 +525,7 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
   bool finite = true;
   if (valid) {
     const float* nrec = reinterpret_cast<const float*>(W.rec(nom, 0));
-    const int64_t rstride = W.S * TRJ_REC;  // floats between the records of t and t + 1
+    const int64_t rstride = p.S * TRJ_REC;  // floats between the records of t and t + 1
     for (int f = m; f < (T + 1) * NX; f += TEAM) {
       const int t = f / NX, i = f - t * NX;
       const float xv = nrec[t * rstride + i];

@@ -220,9 +220,12 @@ __device__ __forceinline__ bool team_riccati(float (&Va)[NX], float (&Vb)[NX], f
   __syncwarp();  // V B, v and l_u are no longer read: K and Q_xu rows go there
 
   // ---- gains -----------------------------------------------------------------
+  // The rare SVD fallback works in shared memory (over V B, dead here, before
+  // K is written): Q at sv[0..16), its inverse at sv[16..32). Every lane of a
+  // team forms the same Q and inverse, so their identical writes are benign.
   bool ok;
   Chol4 L;
-  float Mi[NU][NU];
+  float* sv = xc + X_K;
   {
     float Qs[NU][NU];
 #pragma unroll
@@ -241,17 +244,26 @@ __device__ __forceinline__ bool team_riccati(float (&Va)[NX], float (&Vb)[NX], f
     // A lane without an element (live == false) never takes the SVD path: its
     // numbers are discarded, and the warp would wait for its sweeps.
     ok = chol4(Qs, L) || !live;
-    if (!ok) svd_inverse4(Qs, Mi);
+    if (!ok) {
+#pragma unroll
+      for (int a = 0; a < NU; ++a)
+#pragma unroll
+        for (int b = 0; b < NU; ++b) sv[a * NU + b] = Qs[a][b];
+      svd_inverse4(sv, sv + NU * NU);
+    }
   }
+  const bool any_fallback = __any_sync(FULL, !ok);
+  if (any_fallback) __syncwarp();  // every fallback inverse of the warp is written
   auto solve = [&](const float (&rhs)[NU], float (&out)[NU]) {
     if (ok) {
       chol4_solve(L, rhs, out);
     } else {
+      const float* Mi = sv + NU * NU;
 #pragma unroll
       for (int a = 0; a < NU; ++a) {
-        float acc = Mi[a][0] * rhs[0];
+        float acc = Mi[a * NU] * rhs[0];
 #pragma unroll
-        for (int b = 1; b < NU; ++b) acc = fmaf(Mi[a][b], rhs[b], acc);
+        for (int b = 1; b < NU; ++b) acc = fmaf(Mi[a * NU + b], rhs[b], acc);
         out[a] = acc;
       }
     }
@@ -275,6 +287,7 @@ __device__ __forceinline__ bool team_riccati(float (&Va)[NX], float (&Vb)[NX], f
 #pragma unroll
     for (int a = 0; a < NU; ++a) k[a] = -sol[a];
   }
+  if (any_fallback) __syncwarp();  // the fallback inverses are read; K goes over them
   // K columns and Q_xu rows -> exchange (over V B, v, l_u)
   *reinterpret_cast<float4*>(xc + X_K + ra * NU) = make_float4(Ka[0], Ka[1], Ka[2], Ka[3]);
   *reinterpret_cast<float4*>(xc + X_K + rb * NU) = make_float4(Kb[0], Kb[1], Kb[2], Kb[3]);
