@@ -5,7 +5,8 @@
 //   1. reverse: masked adjoint Riccati (controller.py:1035-1110) split by rows
 //      of V across the team (ilqr_team.cuh), A_t, B_t recomputed from
 //      (X_t, U_t), l_xx / l_xu / l_uu read from the TMA-staged C_t slab; the
-//      gains go to an element-interleaved workspace.
+//      gains go to an element-interleaved workspace (one float4 per column of
+//      K_t and one for k_t).
 //   2. forward: dU = K dX + k, dX+ = A dX + B dU (controller.py:1121-1129),
 //      computed by every lane of the team, and the gradients of
 //      ILQRSolve.backward (controller.py:84-125) with the rows of grad_C[b, t]
@@ -41,10 +42,14 @@ __global__ void __launch_bounds__(32, 19) backward_kernel(const __grid_constant_
   const int64_t bw = valid ? b : b0;
   const int T = p.T;
   const float dt = p.dt;
-  float* Kw = p.ws;
-  float* kw = p.ws + (int64_t)T * NU * NX * p.S;
-  auto Kat = [&](int t, int a, int j) -> float& { return Kw[(int64_t)(t * NU * NX + a * NX + j) * p.S + bw]; };
-  auto kat = [&](int t, int a) -> float& { return kw[(int64_t)(t * NU + a) * p.S + bw]; };
+  // workspace: K_t columns [T][10][S][4] (the 4 gains of state j), k_t [T][S][4]
+  auto kcol = [&](int t, int j) {
+    return reinterpret_cast<float4*>(p.ws + ((size_t)(t * NX + j) * (size_t)p.S + (size_t)bw) * 4);
+  };
+  auto kff = [&](int t) {
+    return reinterpret_cast<float4*>(p.ws + ((size_t)T * NX * (size_t)p.S + (size_t)t * p.S + (size_t)bw) * 4);
+  };
+  auto f4 = [](const float (&v)[NU]) { return make_float4(v[0], v[1], v[2], v[3]); };
   auto ld = [&](const float* q, int64_t i) { return valid ? __ldg(q + i) : 0.0f; };
 
   if (lane == 0) {
@@ -93,15 +98,9 @@ __global__ void __launch_bounds__(32, 19) backward_kernel(const __grid_constant_
     float Ka[NU], Kb[NU], k[NU];
     team_riccati<true>(Va, Vb, va_, vb_, J, DenseC{Ce}, lxa, lxb, p.reg, tight, m, valid, xc, next, Ka, Kb, k);
     if (valid) {
-#pragma unroll
-      for (int a = 0; a < NU; ++a) {
-        Kat(t, a, ra) = Ka[a];
-        Kat(t, a, rb) = Kb[a];
-      }
-      if (m == 0) {
-#pragma unroll
-        for (int a = 0; a < NU; ++a) kat(t, a) = k[a];
-      }
+      *kcol(t, ra) = f4(Ka);
+      *kcol(t, rb) = f4(Kb);
+      if (m == 0) *kff(t) = f4(k);
     }
   });
   if (!ok) return;  // a bounded wait gave up; outputs are left untouched
@@ -122,12 +121,23 @@ __global__ void __launch_bounds__(32, 19) backward_kernel(const __grid_constant_
     for (int i = 0; i < NX; ++i) z[i] = ld(Xb, t * NX + i);
 #pragma unroll
     for (int a = 0; a < NU; ++a) z[NX + a] = ld(Ub, t * NU + a);
+    {
+      // dU = K dX + k, each row accumulated over j in index order
+      float4 c = *kcol(t, 0);
+      float acc[NU] = {c.x * dx[0], c.y * dx[0], c.z * dx[0], c.w * dx[0]};
 #pragma unroll
-    for (int a = 0; a < NU; ++a) {
-      float acc = Kat(t, a, 0) * dx[0];
-#pragma unroll
-      for (int j = 1; j < NX; ++j) acc = fmaf(Kat(t, a, j), dx[j], acc);
-      du[a] = acc + kat(t, a);
+      for (int j = 1; j < NX; ++j) {
+        c = *kcol(t, j);
+        acc[0] = fmaf(c.x, dx[j], acc[0]);
+        acc[1] = fmaf(c.y, dx[j], acc[1]);
+        acc[2] = fmaf(c.z, dx[j], acc[2]);
+        acc[3] = fmaf(c.w, dx[j], acc[3]);
+      }
+      const float4 kk = *kff(t);
+      du[0] = acc[0] + kk.x;
+      du[1] = acc[1] + kk.y;
+      du[2] = acc[2] + kk.z;
+      du[3] = acc[3] + kk.w;
     }
     float dtau[NT];
 #pragma unroll

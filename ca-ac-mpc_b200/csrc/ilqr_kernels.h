@@ -78,6 +78,7 @@ constexpr int TRJ_REC = 16;
 inline int64_t solve_ws_fields(int T) {
   return (int64_t)SOLVE_SLOTS * (T + 1) * TRJ_REC + (int64_t)T * (10 * 4 + 4 + TRJ_REC);
 }
+// Backward workspace: K_t columns [T][10][S][4] and k_t [T][S][4].
 inline int64_t backward_ws_fields(int T) { return (int64_t)T * (40 + 4); }
 inline int64_t ws_stride(int64_t B) { return (B + 31) / 32 * 32; }
 
