@@ -275,16 +275,17 @@ def run_ours(args):
     hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
     t_solve = statistics.mean(solve_ms) * 1e-3
     t_bwd = statistics.mean(bwd_ms) * 1e-3
-    traffic = None
+    traffic, traffic_src = None, None
     try:
         prof = json.load(open(os.path.join(ROOT, "profiles", "solve_kernel_traffic.json")))
         traffic = prof.get(WORKLOAD, {}).get("dram_bytes_per_launch")
+        traffic_src = prof.get(WORKLOAD, {}).get("source")
     except Exception:
         pass
     roofline = {
         "bound": "fp32", "kernel": "solve_kernel (fused forward iLQR)",
         "achieved": f_solve / t_solve / 1e12, "peak": peak_fp32, "unit": "TFLOP/s",
-        "frac": f_solve / t_solve / 1e12 / peak_fp32, "traffic": traffic,
+        "frac": f_solve / t_solve / 1e12 / peak_fp32, "traffic": traffic, "traffic_source": traffic_src,
         "peak_source": "measured FMA probe on this GPU (no FP32 figure in MEASURED_PEAKS.json)",
         "algorithmic_flops_per_launch": f_solve, "mean_launch_ms": t_solve * 1e3,
         "hbm": {"algorithmic_bytes_per_launch": cm.solve_bytes(T, B),

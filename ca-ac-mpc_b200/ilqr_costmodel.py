@@ -21,10 +21,14 @@ ilqr_backward.cu for the expressions counted):
   GRADC 784   grad_C block (196 x 4)
 
   solve(element)    = T (STEP + COST) + I T (RIC + QUAD + JAC)
-                      + I T n_alpha (CAND + STEP + COST) + A T (CAND + STEP)
+                      + I T n_alpha (CAND + STEP + COST)
   backward(element) = T (RICM + JAC + SWEEP + GRADC)
 
-with I the iterations the element ran and A the accepted ones.
+with I the iterations the element ran. An accepted candidate becomes the new
+nominal trajectory as it was rolled out in the line search
+(controller.py:360-415), so acceptance adds no work. These structured counts
+are below the dense counts of the same algorithm (a dense Riccati step is
+about 9.8 kFLOP); the achieved rates reported against them are conservative.
 
 Compulsory bytes (fp32, read once / written once, zero references and
 terminal cost as on the FastMPC surface):
@@ -41,13 +45,12 @@ STEP, CAND, COST, QUAD, JAC = 87, 102, 435, 392, 57
 RIC, RICM, SWEEP, GRADC = 5290, 5250, 229, 784
 
 
-def solve_flops(T: int, n_alpha: int, iters, accepts) -> float:
-    """Total solve FLOPs for elements that ran `iters` iterations and accepted
-    `accepts` of them (arrays over the batch)."""
+def solve_flops(T: int, n_alpha: int, iters, accepts=None) -> float:
+    """Total solve FLOPs for elements that ran `iters` iterations (an array
+    over the batch). `accepts` is accepted for callers that track it; it does
+    not change the count."""
     I = np.asarray(iters, dtype=np.float64)
-    A = np.asarray(accepts, dtype=np.float64)
-    per = (T * (STEP + COST) + I * T * (RIC + QUAD + JAC)
-           + I * T * n_alpha * (CAND + STEP + COST) + A * T * (CAND + STEP))
+    per = T * (STEP + COST) + I * T * (RIC + QUAD + JAC) + I * T * n_alpha * (CAND + STEP + COST)
     return float(per.sum())
 
 
