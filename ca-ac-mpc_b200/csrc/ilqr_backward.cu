@@ -31,14 +31,18 @@ __global__ void __launch_bounds__(32, 19) backward_kernel(const __grid_constant_
                                                           const BackwardParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   float* slab = reinterpret_cast<float*>(smem);
-  float* xch = slab + SLAB_E * CBLK;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(xch + SLAB_E * XS);
+  float* xch = slab + EPW * CBLK;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(xch + EPW * XS);
   const int lane = threadIdx.x;
-  const int e = lane / TEAM;
-  const int m = lane - e * TEAM;
+  // Lanes 30, 31 mirror lanes 25, 26 (element 5, members 0 and 1): same loads
+  // and arithmetic, bit-identical shared-memory writes, no global writes.
+  const bool dup = lane >= EPW * TEAM;
+  const int e = dup ? EPW - 1 : lane / TEAM;
+  const int m = lane - (dup ? EPW * TEAM : e * TEAM);
   const int64_t b0 = (int64_t)blockIdx.x * EPW;
   const int64_t b = b0 + e;
-  const bool valid = (e < EPW) && (b < p.B);
+  const bool valid = b < p.B;
+  const bool own = valid && !dup;
   const int64_t bw = valid ? b : b0;
   const int T = p.T;
   const float dt = p.dt;
@@ -56,10 +60,6 @@ __global__ void __launch_bounds__(32, 19) backward_kernel(const __grid_constant_
     mbar_init(bar, 1);
     fence_mbar_init();
   }
-  // The pad rows (lanes 30, 31) are never filled by a copy: zero them so that
-  // no lane reads uninitialized shared memory.
-  for (int f = lane; f < CBLK; f += WARP) slab[(SLAB_E - 1) * CBLK + f] = 0.0f;
-  for (int f = lane; f < XS; f += WARP) xch[(SLAB_E - 1) * XS + f] = 0.0f;
   __syncwarp();
   TeamPipe pipe{slab, bar, 0u, &tmC, (int)b0, true};
   float* xc = xch + e * XS;
@@ -97,14 +97,14 @@ __global__ void __launch_bounds__(32, 19) backward_kernel(const __grid_constant_
     const Jac J = drone_jac(xb, ub, dt);
     float Ka[NU], Kb[NU], k[NU];
     team_riccati<true>(Va, Vb, va_, vb_, J, DenseC{Ce}, lxa, lxb, p.reg, tight, m, valid, xc, next, Ka, Kb, k);
-    if (valid) {
+    if (own) {
       *kcol(t, ra) = f4(Ka);
       *kcol(t, rb) = f4(Kb);
       if (m == 0) *kff(t) = f4(k);
     }
   });
   if (!ok) return;  // a bounded wait gave up; outputs are left untouched
-  if (valid && p.g_x0 != nullptr) {
+  if (own && p.g_x0 != nullptr) {
     p.g_x0[b * NX + ra] = -va_;
     p.g_x0[b * NX + rb] = -vb_;
   }
@@ -168,7 +168,7 @@ __global__ void __launch_bounds__(32, 19) backward_kernel(const __grid_constant_
         bulk_commit();
       }
     }
-    if (valid) {
+    if (own) {
       for (int s = 0; s < nrows; ++s) {
         const int i = m + TEAM * s;
         const float di = pick14(dtau, i);
@@ -190,7 +190,7 @@ __global__ void __launch_bounds__(32, 19) backward_kernel(const __grid_constant_
   }
   if (p.write_gC && lane == 0) bulk_wait<0>();
   __syncwarp();
-  if (!valid) return;
+  if (!own) return;
   if (p.g_xref != nullptr && m == 0) {
 #pragma unroll
     for (int i = 0; i < NX; ++i) p.g_xref[(b * (T + 1) + T) * NX + i] = 0.0f;
@@ -225,7 +225,7 @@ __global__ void __launch_bounds__(32, 19) backward_kernel(const __grid_constant_
 
 }  // namespace
 
-size_t backward_smem_bytes() { return (size_t)SLAB_E * CBLK * 4 + (size_t)SLAB_E * XS * 4 + sizeof(uint64_t); }
+size_t backward_smem_bytes() { return (size_t)EPW * CBLK * 4 + (size_t)EPW * XS * 4 + sizeof(uint64_t); }
 
 cudaError_t launch_backward(const CUtensorMap& tmC, const CUtensorMap& tmG, const BackwardParams& p,
                             cudaStream_t stream) {

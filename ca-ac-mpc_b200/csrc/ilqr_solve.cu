@@ -1,7 +1,7 @@
 // ilqr_solve.cu -- fused batched iLQR forward solve (all iterations, one launch).
 //
 // Mapping: one CTA = one warp = 6 batch elements, a team of 5 lanes per
-// element (lanes 30, 31 are spare). The team splits each Riccati step by rows
+// element (lanes 30, 31 mirror two lanes of the sixth element). The team splits each Riccati step by rows
 // of V (ilqr_team.cuh) and evaluates the line-search step sizes one per lane.
 // Per-element state lives in a caller-provided workspace, element-interleaved
 // in 16-byte-aligned records (layout in ilqr_kernels.h): SOLVE_SLOTS
@@ -174,16 +174,21 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
   static_assert(NAC <= SOLVE_SLOTS - 1, "a slot per candidate of the first chunk");
   extern __shared__ __align__(128) unsigned char smem[];
   float* slab = reinterpret_cast<float*>(smem);
-  float* xch = slab + SLAB_E * CBLK;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(xch + SLAB_E * XS);
+  float* xch = slab + EPW * CBLK;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(xch + EPW * XS);
   const int lane = threadIdx.x;
-  const int e = lane / TEAM;
-  const int m = lane - e * TEAM;
+  // Lanes 30, 31 mirror lanes 25, 26 (element 5, members 0 and 1): they load
+  // and compute exactly what those lanes do, so their shared-memory writes are
+  // bit-identical to the ones they duplicate, and they write no global memory.
+  const bool dup = lane >= EPW * TEAM;
+  const int e = dup ? EPW - 1 : lane / TEAM;
+  const int m = lane - (dup ? EPW * TEAM : e * TEAM);
   const int base = e * TEAM;
   const int64_t b0 = (int64_t)blockIdx.x * EPW;
   const int64_t b = b0 + e;
-  const bool valid = (e < EPW) && (b < p.B);
-  const int64_t bw = valid ? b : b0;  // workspace record read by this lane (never written when !valid)
+  const bool valid = b < p.B;        // the lane's element exists (loads, compute)
+  const bool own = valid && !dup;     // ... and this lane writes its results
+  const int64_t bw = valid ? b : b0;  // workspace record read by this lane (never written when !own)
   const int T = p.T;
   const float dt = p.dt;
   const SolveWs W{p, (uint32_t)bw};
@@ -192,10 +197,6 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
     mbar_init(bar, 1);
     fence_mbar_init();
   }
-  // The pad rows (lanes 30, 31) are never filled by a copy: zero them so that
-  // no lane reads uninitialized shared memory.
-  for (int f = lane; f < CBLK; f += WARP) slab[(SLAB_E - 1) * CBLK + f] = 0.0f;
-  for (int f = lane; f < XS; f += WARP) xch[(SLAB_E - 1) * XS + f] = 0.0f;
   __syncwarp();
   TeamPipe pipe{slab, bar, 0u, &tmC, (int)b0, true};
   float* xc = xch + e * XS;
@@ -217,7 +218,7 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
 #pragma unroll
     for (int i = 0; i < NX; ++i) x[i] = ldg_or0(p.x0 + b * NX + i, valid);
   };
-  const bool writer = valid && m == 0;
+  const bool writer = own && m == 0;
   if (p.trace != nullptr && writer)
     for (int i = 0; i < p.max_iter; ++i) p.trace[b * p.max_iter + i] = (int8_t)-128;
 
@@ -281,7 +282,18 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
     const bool first = (it == 0);
     auto ric_body = [&](int t, auto&& next) {
       float xb[NX], ub[NU], tau[NT];
+      // every global load of the step is issued here, before the first use
       load_rec(W.rec(nom, t), xb, ub);
+      const int ru = NX + (m < NU ? m : 0);
+      const float ca_ = ldg_or0(cb + t * NT + ra, valid), cb_ = ldg_or0(cb + t * NT + rb, valid);
+      const float cu = ldg_or0(cb + t * NT + ru, valid);
+      if (diag) {  // rebuild the diagonal of the slab from the workspace copy
+        const float* dgt = W.diag(t);
+#pragma unroll
+        for (int s3 = 0; s3 < 3; ++s3)
+          if (m + TEAM * s3 < NT) Ce[(m + TEAM * s3) * (NT + 1)] = dgt[m + TEAM * s3];
+        __syncwarp();
+      }
 #pragma unroll
       for (int i = 0; i < NX; ++i) tau[i] = xb[i] - xref(t, i);
 #pragma unroll
@@ -294,17 +306,15 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
         for (int j = 1; j < NT; ++j) s = fmaf(Cr[j], tau[j], s);
         return s;
       };
-      const float ca_ = ldg_or0(cb + t * NT + ra, valid), cb_ = ldg_or0(cb + t * NT + rb, valid);
       const float sa = rowdot(ra), sb = rowdot(rb);
       const float lxa = sa + ca_, lxb = sb + cb_;
-      const int ru = NX + (m < NU ? m : 0);
-      const float su = rowdot(ru), cu = ldg_or0(cb + t * NT + ru, valid);
+      const float su = rowdot(ru);
       if (m < NU) xc[X_LU + m] = su + cu;
       if (first) {
         const float ta = pick(tau, ra), tb = pick(tau, rb), tu = pick(tau, ru);
         cost_q += fmaf(ta, sa, tb * sb) + (m < NU ? tu * su : 0.0f);
         cost_l += fmaf(ca_, ta, cb_ * tb) + (m < NU ? cu * tu : 0.0f);
-        if (p.diag_cache && valid) {
+        if (p.diag_cache && valid) {  // (mirror lanes check too; only owners write)
           // the team scans the block for off-diagonal nonzeros (the diagonal
           // sits at flat index 15 i) and keeps a copy of the diagonal
           const float4* c4 = reinterpret_cast<const float4*>(Ce);
@@ -317,7 +327,7 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
           float* dgt = W.diag(t);
 #pragma unroll
           for (int s3 = 0; s3 < 3; ++s3)
-            if (m + TEAM * s3 < NT) dgt[m + TEAM * s3] = Ce[(m + TEAM * s3) * (NT + 1)];
+            if (own && m + TEAM * s3 < NT) dgt[m + TEAM * s3] = Ce[(m + TEAM * s3) * (NT + 1)];
         }
       }
       __syncwarp();
@@ -326,21 +336,13 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
       if (!team_riccati<false>(Va, Vb, va_, vb_, J, DenseC{Ce}, lxa, lxb, p.reg, 0u, m, valid, xc, next, Ka, Kb,
                                k))
         fallback = true;
-      if (valid) {
+      if (own) {
         *W.kcol(t, ra) = f4(Ka);
         *W.kcol(t, rb) = f4(Kb);
         if (m == 0) *W.kff(t) = f4(k);
       }
     };
-    bool ok = pipe.run(
-        T, true, !diag,
-        [&](int t) {
-          const float* dgt = W.diag(t);
-#pragma unroll
-          for (int s3 = 0; s3 < 3; ++s3)
-            if (m + TEAM * s3 < NT) Ce[(m + TEAM * s3) * (NT + 1)] = dgt[m + TEAM * s3];
-        },
-        ric_body);
+    bool ok = pipe.run(T, true, !diag, [](int) {}, ric_body);
     if (!ok) {
       status |= ELEM_PIPE_TIMEOUT;
       active = false;
@@ -349,7 +351,7 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
     if (first && p.diag_cache) {
       diag = !__any_sync(FULL, offd);
       if (diag) {  // off-diagonal entries of the rebuilt blocks stay zero from here on
-        for (int f = lane; f < SLAB_E * CBLK; f += WARP) slab[f] = 0.0f;
+        for (int f = lane; f < EPW * CBLK; f += WARP) slab[f] = 0.0f;
         __syncwarp();
       }
     }
@@ -372,7 +374,7 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
     for (int a0 = 0; a0 < p.n_alpha; a0 += NAC) {
       const int j = a0 + m;
       const float al = (j < p.n_alpha) ? p.alphas[j] : 0.0f;
-      const bool keep = valid && j < p.n_alpha && j < SOLVE_SLOTS - 1;  // candidate stored in a slot
+      const bool keep = own && j < p.n_alpha && j < SOLVE_SLOTS - 1;  // candidate stored in a slot
       const int cs = j < nom ? j : j + 1;
       float x[NX], sq = 0.0f, sl = 0.0f;
       load_x0(x);
@@ -390,6 +392,19 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
         for (int i = 0; i < NX; ++i) tau[i] = x[i] - xref(t, i);
 #pragma unroll
         for (int a = 0; a < NU; ++a) tau[NX + a] = u[a] - uref(t, a);
+        float l;  // c^T tau (c is not in the slab: its loads go ahead of the slab sync)
+        {
+          const float2* c2 = reinterpret_cast<const float2*>(cb + t * NT);
+          float2 cc = valid ? __ldg(c2) : make_float2(0.0f, 0.0f);
+          l = cc.x * tau[0];
+          l = fmaf(cc.y, tau[1], l);
+#pragma unroll
+          for (int jj = 1; jj < NT / 2; ++jj) {
+            cc = valid ? __ldg(c2 + jj) : make_float2(0.0f, 0.0f);
+            l = fmaf(cc.x, tau[2 * jj], l);
+            l = fmaf(cc.y, tau[2 * jj + 1], l);
+          }
+        }
         float q = 0.0f;
         if (diag) {
           const float4* d4 = reinterpret_cast<const float4*>(W.diag(t));
@@ -418,19 +433,6 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
           }
         }
         next();
-        float l;
-        {
-          const float2* c2 = reinterpret_cast<const float2*>(cb + t * NT);
-          float2 cc = valid ? __ldg(c2) : make_float2(0.0f, 0.0f);
-          l = cc.x * tau[0];
-          l = fmaf(cc.y, tau[1], l);
-#pragma unroll
-          for (int jj = 1; jj < NT / 2; ++jj) {
-            cc = valid ? __ldg(c2 + jj) : make_float2(0.0f, 0.0f);
-            l = fmaf(cc.x, tau[2 * jj], l);
-            l = fmaf(cc.y, tau[2 * jj + 1], l);
-          }
-        }
         sq += q;
         sl += l;
         float xn[NX];
@@ -484,7 +486,7 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
       } else {
         accept = cmin < best;
       }
-      if (p.trace != nullptr && m == 0) p.trace[b * p.max_iter + it] = (int8_t)(accept ? jsel : -(jbest + 1));
+      if (p.trace != nullptr && m == 0 && own) p.trace[b * p.max_iter + it] = (int8_t)(accept ? jsel : -(jbest + 1));
       if (!accept && stall_iter == p.max_iter) {
         stall_iter = it;
         stall_gap = fabsf(cmin - best);
@@ -498,7 +500,7 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
     if (accept && !rerun) nom = jsel < nom ? jsel : jsel + 1;
     if (__any_sync(FULL, rerun)) {
       const int dst = nom == 0 ? 1 : 0;
-      if (rerun && m == 0) {
+      if (rerun && m == 0 && own) {
         const float al = p.alphas[jsel];
         float x[NX];
         load_x0(x);
@@ -523,7 +525,7 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
 
   // ---- outputs (lanes of a team split the writes) -----------------------------
   bool finite = true;
-  if (valid) {
+  if (own) {
     const float* nrec = reinterpret_cast<const float*>(W.rec(nom, 0));
     const int64_t rstride = p.S * TRJ_REC;  // floats between the records of t and t + 1
     for (int f = m; f < (T + 1) * NX; f += TEAM) {
@@ -565,7 +567,7 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
 
 }  // namespace
 
-size_t solve_smem_bytes() { return (size_t)SLAB_E * CBLK * 4 + (size_t)SLAB_E * XS * 4 + sizeof(uint64_t); }
+size_t solve_smem_bytes() { return (size_t)EPW * CBLK * 4 + (size_t)EPW * XS * 4 + sizeof(uint64_t); }
 
 cudaError_t launch_solve(const CUtensorMap& tmC, const SolveParams& p, cudaStream_t stream) {
   const size_t smem = solve_smem_bytes();

@@ -31,7 +31,6 @@ constexpr int X_V = 140;      // [10]     v
 constexpr int X_LU = 152;     // [4]      l_u
 constexpr int X_K = 100;      // [10][4]  K transposed: column c of K at X_K + 4c (over V B)
 constexpr int X_QXU = 140;    // [10][4]  Q_xu rows (over v, l_u)
-constexpr int SLAB_E = EPW + 1;  // slab rows incl. a pad row for the two spare lanes
 constexpr uint32_t TSLAB_BYTES = EPW * CBLK * 4u;  // bytes one TMA box delivers
 
 __device__ __forceinline__ int row_a(int m) { return m < 4 ? 3 + m : 0; }
@@ -389,7 +388,7 @@ __device__ __forceinline__ bool team_riccati(float (&Va)[NX], float (&Vb)[NX], f
 }
 
 // Reduce over the 5 lanes of a team (all lanes get the result); lanes 30, 31
-// form a partial team of their own.
+// (mirrors of lanes 25, 26) pass base 25 and get the sixth element's sum.
 __device__ __forceinline__ float team_sum(float x, int base) {
   float s = __shfl_sync(FULL, x, base);
 #pragma unroll
@@ -399,7 +398,7 @@ __device__ __forceinline__ float team_sum(float x, int base) {
 
 // Single-buffered stream of [6 x 196] C_t slabs for one warp.
 struct TeamPipe {
-  float* slab;      // [SLAB_E][CBLK]
+  float* slab;      // [EPW][CBLK]
   uint64_t* bar;
   uint32_t parity;
   const CUtensorMap* tm;
