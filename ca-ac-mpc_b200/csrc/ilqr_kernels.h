@@ -71,12 +71,13 @@ struct BackwardParams {
 //   trajectory slots [SOLVE_SLOTS][T+1][S][16]: x[10], u[4], 2 pad (u unused at t = T)
 //   gains K          [T][10][S][4]: column j of K_t (the 4 gains of state j)
 //   feedforward k    [T][S][4]
-//   cost diagonals   [T][S][16]: the 14 diagonal entries of C_t, 2 pad
+//   cost records     [T][S][32]: the 14 diagonal entries of C_t, 2 pad, c_t (14), 2 pad
 // One slot holds the nominal trajectory, the others the line-search candidates.
 constexpr int SOLVE_SLOTS = 6;
 constexpr int TRJ_REC = 16;
+constexpr int COST_REC = 32;
 inline int64_t solve_ws_fields(int T) {
-  return (int64_t)SOLVE_SLOTS * (T + 1) * TRJ_REC + (int64_t)T * (10 * 4 + 4 + TRJ_REC);
+  return (int64_t)SOLVE_SLOTS * (T + 1) * TRJ_REC + (int64_t)T * (10 * 4 + 4 + COST_REC);
 }
 // Backward workspace: K_t columns [T][10][S][4] and k_t [T][S][4].
 inline int64_t backward_ws_fields(int T) { return (int64_t)T * (40 + 4); }

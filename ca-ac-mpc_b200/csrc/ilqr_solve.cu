@@ -85,10 +85,12 @@ struct SolveWs {
     const uint32_t r = (uint32_t)t * S() + b;
     return reinterpret_cast<float4*>(gk() + (size_t)p.T * NX * S() * 4 + (size_t)r * 4);
   }
+  // cost record of step t: diag(C_t) at [0, 14), c_t at [16, 30)
   __device__ __forceinline__ float* diag(int t) const {
     const uint32_t r = (uint32_t)t * S() + b;
-    return gk() + (size_t)p.T * (NX + 1) * S() * 4 + (size_t)r * TRJ_REC;
+    return gk() + (size_t)p.T * (NX + 1) * S() * 4 + (size_t)r * COST_REC;
   }
+  __device__ __forceinline__ float* cvec(int t) const { return diag(t) + 16; }
 };
 
 __device__ __forceinline__ void load_rec(const float4* r, float (&x)[NX], float (&u)[NU]) {
@@ -285,8 +287,19 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
       // every global load of the step is issued here, before the first use
       load_rec(W.rec(nom, t), xb, ub);
       const int ru = NX + (m < NU ? m : 0);
-      const float ca_ = ldg_or0(cb + t * NT + ra, valid), cb_ = ldg_or0(cb + t * NT + rb, valid);
-      const float cu = ldg_or0(cb + t * NT + ru, valid);
+      // c_t from the input on the first pass (which copies it into the cost
+      // record), from the record afterwards
+      float ca_, cb_, cu;
+      if (first) {
+        ca_ = ldg_or0(cb + t * NT + ra, valid);
+        cb_ = ldg_or0(cb + t * NT + rb, valid);
+        cu = ldg_or0(cb + t * NT + ru, valid);
+      } else {
+        const float* cr = W.cvec(t);
+        ca_ = cr[ra];
+        cb_ = cr[rb];
+        cu = cr[ru];
+      }
       if (diag) {  // rebuild the diagonal of the slab from the workspace copy
         const float* dgt = W.diag(t);
 #pragma unroll
@@ -311,6 +324,12 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
       const float su = rowdot(ru);
       if (m < NU) xc[X_LU + m] = su + cu;
       if (first) {
+        if (own) {
+          float* cr = W.cvec(t);
+          cr[ra] = ca_;
+          cr[rb] = cb_;
+          if (m < NU) cr[ru] = cu;
+        }
         const float ta = pick(tau, ra), tb = pick(tau, rb), tu = pick(tau, ru);
         cost_q += fmaf(ta, sa, tb * sb) + (m < NU ? tu * su : 0.0f);
         cost_l += fmaf(ca_, ta, cb_ * tb) + (m < NU ? cu * tu : 0.0f);
@@ -392,18 +411,15 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
         for (int i = 0; i < NX; ++i) tau[i] = x[i] - xref(t, i);
 #pragma unroll
         for (int a = 0; a < NU; ++a) tau[NX + a] = u[a] - uref(t, a);
-        float l;  // c^T tau (c is not in the slab: its loads go ahead of the slab sync)
+        float l;  // c^T tau, c_t from the cost record
         {
-          const float2* c2 = reinterpret_cast<const float2*>(cb + t * NT);
-          float2 cc = valid ? __ldg(c2) : make_float2(0.0f, 0.0f);
-          l = cc.x * tau[0];
-          l = fmaf(cc.y, tau[1], l);
+          const float4* c4 = reinterpret_cast<const float4*>(W.cvec(t));
+          const float4 h0 = c4[0], h1 = c4[1], h2 = c4[2], h3 = c4[3];
+          const float cv[NT] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z,
+                                h1.w, h2.x, h2.y, h2.z, h2.w, h3.x, h3.y};
+          l = cv[0] * tau[0];
 #pragma unroll
-          for (int jj = 1; jj < NT / 2; ++jj) {
-            cc = valid ? __ldg(c2 + jj) : make_float2(0.0f, 0.0f);
-            l = fmaf(cc.x, tau[2 * jj], l);
-            l = fmaf(cc.y, tau[2 * jj + 1], l);
-          }
+          for (int jj = 1; jj < NT; ++jj) l = fmaf(cv[jj], tau[jj], l);
         }
         float q = 0.0f;
         if (diag) {

@@ -104,7 +104,7 @@ int ilqr_b200_solve_f32(
  * workspace: the scratch is a fixed ILQR_NOALLOC_SCRATCH_BYTES array inside
  * this library that every GPU loading the library holds until exit. Problems
  * whose ilqr_b200_solve_workspace_size exceeds it are rejected with
- * ILQR_ERR_NOALLOC_LIMIT (at T = 20 that is B > 1280). The entry point
+ * ILQR_ERR_NOALLOC_LIMIT (at T = 20 that is B > 1184). The entry point
  * allocates nothing. Its first call on a device looks up the array's device
  * address, so make that first call before any stream capture. All calls
  * share the array: calls that overlap on the GPU (other streams, other host

@@ -44,7 +44,7 @@ def test_workspace_sizes():
     L = nat.lib()
     n = ctypes.c_size_t()
     assert L.ilqr_b200_solve_workspace_size(16384, 20, ctypes.byref(n)) == 0
-    assert n.value == (6 * 21 * 16 + 20 * (40 + 4 + 16)) * 16384 * 4
+    assert n.value == (6 * 21 * 16 + 20 * (40 + 4 + 32)) * 16384 * 4
     assert L.ilqr_b200_backward_workspace_size(33, 5, ctypes.byref(n)) == 0
     assert n.value == 5 * 44 * 64 * 4
     assert L.ilqr_b200_solve_workspace_size(-1, 20, ctypes.byref(n)) == 1

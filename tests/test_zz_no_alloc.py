@@ -81,14 +81,14 @@ def test_noalloc_matches_workspace_entry_point_on_consecutive_calls():
 def test_noalloc_rejects_problems_beyond_the_fixed_scratch():
     f = _fn()
     need = ctypes.c_size_t()
-    nat.lib().ilqr_b200_solve_workspace_size(1280, 20, ctypes.byref(need))
+    nat.lib().ilqr_b200_solve_workspace_size(1184, 20, ctypes.byref(need))
     assert need.value <= SCRATCH_BYTES
-    nat.lib().ilqr_b200_solve_workspace_size(1281, 20, ctypes.byref(need))
+    nat.lib().ilqr_b200_solve_workspace_size(1185, 20, ctypes.byref(need))
     assert need.value > SCRATCH_BYTES
     cfg, t = _inputs("rollout_b16384_t20", 1)
     fake = ctypes.c_void_p(t["C"].data_ptr())
     al = (ctypes.c_float * 5)(*cfg["alphas"])
-    st = f(*([fake] * 4 + [None] * 6), 1281, 20, wl.DT, 5, wl.REG_EPS, wl.CONVERGE_TOL,
+    st = f(*([fake] * 4 + [None] * 6), 1185, 20, wl.DT, 5, wl.REG_EPS, wl.CONVERGE_TOL,
            ctypes.cast(al, ctypes.c_void_p), 5, None, fake, fake, None, None, None, None, None, None,
            None, None)
     assert st == STATUS_NOALLOC_LIMIT
