@@ -90,20 +90,27 @@ int ilqr_b200_backward_workspace_size(int64_t B, int32_t T, size_t* bytes) {
   return ILQR_OK;
 }
 
-int ilqr_b200_solve_f32(const float* x0, const float* U_init, const float* C, const float* c,
-                        const float* C_final, const float* c_final, const float* x_ref, const float* u_ref,
-                        const float* u_min, const float* u_max, int64_t B, int32_t T, float dt, int32_t max_iter,
-                        float reg_eps, float converge_tol, const float* alphas, int32_t n_alpha,
-                        const int8_t* forced_trace, float* X, float* U, uint8_t* tight_mask, int8_t* trace,
-                        int32_t* iters, uint32_t* elem_status, float* best_cost, int32_t* stall_iter,
-                        float* stall_gap, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
-  (void)converge_tol;  // global stopping only affects the reported flag; see stall_iter / stall_gap
+}  // extern "C"
+
+namespace {
+
+// Shared by the dense-cost and the sigmoid-cost solve: sig.p == nullptr means
+// dense C, c (and optional terminal cost and references).
+int solve_impl(const float* x0, const float* U_init, const float* C, const float* c, const float* C_final,
+               const float* c_final, const float* x_ref, const float* u_ref, const ilqr::SigmoidCost& sig,
+               const float* u_min, const float* u_max, int64_t B, int32_t T, float dt, int32_t max_iter,
+               float reg_eps, const float* alphas, int32_t n_alpha, const int8_t* forced_trace, float* X, float* U,
+               uint8_t* tight_mask, int8_t* trace, int32_t* iters, uint32_t* elem_status, float* best_cost,
+               int32_t* stall_iter, float* stall_gap, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   if (B < 0 || T < 1 || max_iter < 0 || n_alpha < 1 || n_alpha > ILQR_MAX_ALPHAS || alphas == nullptr)
     return ILQR_ERR_INVALID_ARGUMENT;
   if ((u_min == nullptr) != (u_max == nullptr)) return ILQR_ERR_INVALID_ARGUMENT;
   if (B == 0) return ILQR_OK;
-  if (!x0 || !U_init || !C || !c || !X || !U) return ILQR_ERR_INVALID_ARGUMENT;
-  if (!aligned16(C)) return ILQR_ERR_MISALIGNED;
+  if (!x0 || !U_init || !X || !U) return ILQR_ERR_INVALID_ARGUMENT;
+  if (sig.p == nullptr) {
+    if (!C || !c) return ILQR_ERR_INVALID_ARGUMENT;
+    if (!aligned16(C)) return ILQR_ERR_MISALIGNED;
+  }
   if ((C_final == nullptr) && (c_final != nullptr)) return ILQR_ERR_INVALID_ARGUMENT;
   // workspace records are indexed with 32-bit unsigned integers on the device
   {
@@ -126,22 +133,28 @@ int ilqr_b200_solve_f32(const float* x0, const float* U_init, const float* C, co
   p.has_bounds = (u_min != nullptr) ? 1 : 0;
   const char* dc = std::getenv("ILQR_B200_DIAG_CACHE");
   p.diag_cache = (dc != nullptr && dc[0] == '0') ? 0 : 1;
+  p.sig = sig;
   CUtensorMap tmC;
-  int st = encode_cost_map(&tmC, C, B, T);
-  if (st != ILQR_OK) return st;
+  std::memset(&tmC, 0, sizeof(tmC));  // never read in sigmoid mode (no pass copies C)
+  if (sig.p == nullptr) {
+    const int st = encode_cost_map(&tmC, C, B, T);
+    if (st != ILQR_OK) return st;
+  }
   return cuda_status(ilqr::launch_solve(tmC, p, stream));
 }
 
-int ilqr_b200_backward_f32(const float* X, const float* U, const float* C, const float* C_final,
-                           const float* x_ref, const float* u_ref, const uint8_t* tight_mask, const float* grad_X,
-                           const float* grad_U, int64_t B, int32_t T, float dt, float reg_eps, float* grad_x0,
-                           float* grad_C, float* grad_c, float* grad_C_final, float* grad_c_final,
-                           float* grad_x_ref, float* grad_u_ref, void* workspace, size_t workspace_bytes,
-                           cudaStream_t stream) {
+int backward_impl(const float* X, const float* U, const float* C, const float* C_final, const float* x_ref,
+                  const float* u_ref, const ilqr::SigmoidCost& sig, const uint8_t* tight_mask, const float* grad_X,
+                  const float* grad_U, int64_t B, int32_t T, float dt, float reg_eps, float* grad_x0, float* grad_C,
+                  float* grad_c, float* grad_C_final, float* grad_c_final, float* grad_x_ref, float* grad_u_ref,
+                  float* grad_sig, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   if (B < 0 || T < 1) return ILQR_ERR_INVALID_ARGUMENT;
   if (B == 0) return ILQR_OK;
-  if (!X || !U || !C || !grad_X || !grad_U) return ILQR_ERR_INVALID_ARGUMENT;
-  if (!aligned16(C) || (grad_C != nullptr && !aligned16(grad_C))) return ILQR_ERR_MISALIGNED;
+  if (!X || !U || !grad_X || !grad_U) return ILQR_ERR_INVALID_ARGUMENT;
+  if (sig.p == nullptr) {
+    if (!C) return ILQR_ERR_INVALID_ARGUMENT;
+    if (!aligned16(C) || (grad_C != nullptr && !aligned16(grad_C))) return ILQR_ERR_MISALIGNED;
+  }
   size_t need = 0;
   ilqr_b200_backward_workspace_size(B, T, &need);
   if (workspace == nullptr || workspace_bytes < need) return ILQR_ERR_WORKSPACE;
@@ -151,13 +164,77 @@ int ilqr_b200_backward_f32(const float* X, const float* U, const float* C, const
   p.g_cf = grad_c_final; p.g_xref = grad_x_ref; p.g_uref = grad_u_ref;
   p.ws = static_cast<float*>(workspace);
   p.B = B; p.S = ilqr::ws_stride(B); p.T = T; p.dt = dt; p.reg = reg_eps;
-  p.write_gC = grad_C != nullptr ? 1 : 0;
+  p.write_gC = (sig.p == nullptr && grad_C != nullptr) ? 1 : 0;
+  p.sig = sig;
+  p.g_sig = grad_sig;
   CUtensorMap tmC, tmG;
-  int st = encode_cost_map(&tmC, C, B, T);
-  if (st != ILQR_OK) return st;
-  st = encode_cost_map(&tmG, grad_C != nullptr ? grad_C : C, B, T);
-  if (st != ILQR_OK) return st;
+  std::memset(&tmC, 0, sizeof(tmC));  // never read in sigmoid mode
+  std::memset(&tmG, 0, sizeof(tmG));
+  if (sig.p == nullptr) {
+    int st = encode_cost_map(&tmC, C, B, T);
+    if (st != ILQR_OK) return st;
+    st = encode_cost_map(&tmG, grad_C != nullptr ? grad_C : C, B, T);
+    if (st != ILQR_OK) return st;
+  }
   return cuda_status(ilqr::launch_backward(tmC, tmG, p, stream));
+}
+
+}  // namespace
+
+extern "C" {
+
+int ilqr_b200_solve_f32(const float* x0, const float* U_init, const float* C, const float* c,
+                        const float* C_final, const float* c_final, const float* x_ref, const float* u_ref,
+                        const float* u_min, const float* u_max, int64_t B, int32_t T, float dt, int32_t max_iter,
+                        float reg_eps, float converge_tol, const float* alphas, int32_t n_alpha,
+                        const int8_t* forced_trace, float* X, float* U, uint8_t* tight_mask, int8_t* trace,
+                        int32_t* iters, uint32_t* elem_status, float* best_cost, int32_t* stall_iter,
+                        float* stall_gap, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  (void)converge_tol;  // global stopping only affects the reported flag; see stall_iter / stall_gap
+  const ilqr::SigmoidCost none{nullptr, 0.0f, 0.0f, 0.0f, 0.0f};
+  return solve_impl(x0, U_init, C, c, C_final, c_final, x_ref, u_ref, none, u_min, u_max, B, T, dt, max_iter,
+                    reg_eps, alphas, n_alpha, forced_trace, X, U, tight_mask, trace, iters, elem_status, best_cost,
+                    stall_iter, stall_gap, workspace, workspace_bytes, stream);
+}
+
+int ilqr_b200_solve_sigmoid_f32(const float* x0, const float* U_init, const float* sigmoid_cost, float cost_eps,
+                                float range_q, float range_p, float range_pt, const float* u_min,
+                                const float* u_max, int64_t B, int32_t T, float dt, int32_t max_iter,
+                                float reg_eps, float converge_tol, const float* alphas, int32_t n_alpha,
+                                const int8_t* forced_trace, float* X, float* U, uint8_t* tight_mask,
+                                int8_t* trace, int32_t* iters, uint32_t* elem_status, float* best_cost,
+                                int32_t* stall_iter, float* stall_gap, void* workspace, size_t workspace_bytes,
+                                cudaStream_t stream) {
+  (void)converge_tol;
+  if (B > 0 && sigmoid_cost == nullptr) return ILQR_ERR_INVALID_ARGUMENT;
+  const ilqr::SigmoidCost sig{sigmoid_cost, cost_eps, range_q, range_p, range_pt};
+  return solve_impl(x0, U_init, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, sig, u_min, u_max, B, T, dt,
+                    max_iter, reg_eps, alphas, n_alpha, forced_trace, X, U, tight_mask, trace, iters, elem_status,
+                    best_cost, stall_iter, stall_gap, workspace, workspace_bytes, stream);
+}
+
+int ilqr_b200_backward_f32(const float* X, const float* U, const float* C, const float* C_final,
+                           const float* x_ref, const float* u_ref, const uint8_t* tight_mask, const float* grad_X,
+                           const float* grad_U, int64_t B, int32_t T, float dt, float reg_eps, float* grad_x0,
+                           float* grad_C, float* grad_c, float* grad_C_final, float* grad_c_final,
+                           float* grad_x_ref, float* grad_u_ref, void* workspace, size_t workspace_bytes,
+                           cudaStream_t stream) {
+  const ilqr::SigmoidCost none{nullptr, 0.0f, 0.0f, 0.0f, 0.0f};
+  return backward_impl(X, U, C, C_final, x_ref, u_ref, none, tight_mask, grad_X, grad_U, B, T, dt, reg_eps, grad_x0,
+                       grad_C, grad_c, grad_C_final, grad_c_final, grad_x_ref, grad_u_ref, nullptr, workspace,
+                       workspace_bytes, stream);
+}
+
+int ilqr_b200_backward_sigmoid_f32(const float* X, const float* U, const float* sigmoid_cost, float cost_eps,
+                                   float range_q, float range_p, float range_pt, const uint8_t* tight_mask,
+                                   const float* grad_X, const float* grad_U, int64_t B, int32_t T, float dt,
+                                   float reg_eps, float* grad_x0, float* grad_sigmoid_cost, void* workspace,
+                                   size_t workspace_bytes, cudaStream_t stream) {
+  if (B > 0 && sigmoid_cost == nullptr) return ILQR_ERR_INVALID_ARGUMENT;
+  const ilqr::SigmoidCost sig{sigmoid_cost, cost_eps, range_q, range_p, range_pt};
+  return backward_impl(X, U, nullptr, nullptr, nullptr, nullptr, sig, tight_mask, grad_X, grad_U, B, T, dt,
+                       reg_eps, grad_x0, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, grad_sigmoid_cost,
+                       workspace, workspace_bytes, stream);
 }
 
 int ilqr_b200_dynamics_f32(const float* x, const float* u, int64_t n, float dt, float* x_next,

@@ -80,7 +80,22 @@ __global__ void __launch_bounds__(32, 19) backward_kernel(const __grid_constant_
     Va[j] = Cf ? __ldg(Cf + ra * NT + j) : 0.0f;
     Vb[j] = Cf ? __ldg(Cf + rb * NT + j) : 0.0f;
   }
-  bool ok = pipe.run(T, true, [&](int t, auto&& next) {
+  // Costs from policy parameters: the slab holds zeros off the diagonal and
+  // each step's diagonal is built from the parameters instead of copied.
+  const bool sigm = p.sig.p != nullptr;
+  const float* sgrow = sigm ? p.sig.p + bw * (int64_t)(2 * NT) * T : nullptr;
+  if (sigm) {
+    for (int f = lane; f < EPW * CBLK; f += WARP) slab[f] = 0.0f;
+    __syncwarp();
+  }
+  auto sig_fill = [&](int t) {
+#pragma unroll
+    for (int s3 = 0; s3 < 3; ++s3) {
+      const int i = m + TEAM * s3;
+      if (i < NT) Ce[i * (NT + 1)] = sig_diag(p.sig, sgrow, T, t, i);
+    }
+  };
+  bool ok = pipe.run(T, true, !sigm, sig_fill, [&](int t, auto&& next) {
     float xb[NX], ub[NU];
 #pragma unroll
     for (int i = 0; i < NX; ++i) xb[i] = ld(Xb, t * NX + i);
@@ -166,6 +181,21 @@ __global__ void __launch_bounds__(32, 19) backward_kernel(const __grid_constant_
       if (lane == 0) {
         tma_store_3d(&tmG, slab, 0, t, (int)b0);
         bulk_commit();
+      }
+    }
+    if (own && sigm && p.g_sig != nullptr) {
+      // gradient of the parameters through _build_cost_tensors: dL/dx_q =
+      // grad_C[t,i,i] range_q, dL/dx_p = grad_c[t,i] range_p, and for the
+      // thrust entry c = -(x_p range_pt + eps): dL/dx_p = -grad_c range_pt
+      float* gq = p.g_sig + b * (int64_t)(2 * NT) * T;
+      for (int s = 0; s < nrows; ++s) {
+        const int i = m + TEAM * s;
+        const float di = pick14(dtau, i), zi = pick14(z, i);
+        const float gii = -0.5f * (di * zi + zi * di);
+        const int off = sig_off(T, t, i);
+        gq[off] = gii * p.sig.range_q;
+        const float gc = -di;
+        gq[14 * T + off] = i == NX ? (-gc) * p.sig.range_pt : gc * p.sig.range_p;
       }
     }
     if (own) {

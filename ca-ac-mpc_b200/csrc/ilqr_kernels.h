@@ -9,6 +9,14 @@
 
 namespace ilqr {
 
+// Diagonal quadratic costs given as the policy's sigmoid outputs [B, 28 T]
+// (x_q = p[:, :14T], x_p = p[:, 14T:]): diag(C_t)_i = x_q * range_q + eps,
+// c_t,i = (x_p - 0.5) range_p, and for the thrust entry -(x_p range_pt + eps).
+struct SigmoidCost {
+  const float* p;
+  float eps, range_q, range_p, range_pt;
+};
+
 struct SolveParams {
   const float* x0;
   const float* U_init;
@@ -40,6 +48,7 @@ struct SolveParams {
   int n_alpha;
   int has_bounds;
   int diag_cache;  // 1: detect diagonal C_t blocks and stop re-reading them after the first pass
+  SigmoidCost sig;  // sig.p != nullptr: costs built from policy parameters (C, c unused)
 };
 
 struct BackwardParams {
@@ -64,6 +73,8 @@ struct BackwardParams {
   float dt;
   float reg;
   int write_gC;
+  SigmoidCost sig;  // sig.p != nullptr: costs from policy parameters; grad goes to g_sig
+  float* g_sig;     // [B, 28 T] gradient of the parameters (sigmoid mode)
 };
 
 // Solve workspace, in floats, element-interleaved with stride S (the record

@@ -208,7 +208,7 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
   const bool bounds = p.has_bounds != 0;
   const float* lo = bounds ? p.u_min : nullptr;
   const float* hi = bounds ? p.u_max : nullptr;
-  const float* cb = p.c + b * (int64_t)T * NT;
+  const float* cb = p.c != nullptr ? p.c + b * (int64_t)T * NT : nullptr;
   const float* xrb = (HAS_REF && p.x_ref != nullptr) ? p.x_ref + b * (int64_t)(T + 1) * NX : nullptr;
   const float* urb = (HAS_REF && p.u_ref != nullptr) ? p.u_ref + b * (int64_t)T * NU : nullptr;
   auto xref = [&](int t, int i) { return (HAS_REF && xrb != nullptr) ? ldg_or0(xrb + t * NX + i, valid) : 0.0f; };
@@ -249,8 +249,16 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
   int stall_iter = p.max_iter;
   float stall_gap = 0.0f;
   float best = 0.0f;
-  bool diag = false;  // warp-uniform: all C[b, t] of the warp's elements are diagonal (known after pass 1)
+  // Costs from policy parameters are diagonal by construction: the slab holds
+  // zeros off the diagonal from the start, and no pass reads C.
+  const bool sigm = p.sig.p != nullptr;
+  const float* sgrow = sigm ? p.sig.p + bw * (int64_t)(2 * NT) * T : nullptr;
+  bool diag = sigm;   // warp-uniform: all C[b, t] of the warp's elements are diagonal (known after pass 1)
   bool offd = false;  // this lane saw a nonzero off-diagonal entry during pass 1
+  if (sigm) {
+    for (int f = lane; f < EPW * CBLK; f += WARP) slab[f] = 0.0f;
+    __syncwarp();
+  }
 
   // The first pass always runs: it also yields the initial objective (with
   // max_iter == 0 only that).
@@ -290,7 +298,11 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
       // c_t from the input on the first pass (which copies it into the cost
       // record), from the record afterwards
       float ca_, cb_, cu;
-      if (first) {
+      if (first && sigm) {
+        ca_ = sig_c(p.sig, sgrow, T, t, ra);
+        cb_ = sig_c(p.sig, sgrow, T, t, rb);
+        cu = sig_c(p.sig, sgrow, T, t, ru);
+      } else if (first) {
         ca_ = ldg_or0(cb + t * NT + ra, valid);
         cb_ = ldg_or0(cb + t * NT + rb, valid);
         cu = ldg_or0(cb + t * NT + ru, valid);
@@ -300,7 +312,19 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
         cb_ = cr[rb];
         cu = cr[ru];
       }
-      if (diag) {  // rebuild the diagonal of the slab from the workspace copy
+      if (diag && first && sigm) {  // build the diagonal from the parameters, keep a copy
+        float* dgt = W.diag(t);
+#pragma unroll
+        for (int s3 = 0; s3 < 3; ++s3) {
+          const int i = m + TEAM * s3;
+          if (i < NT) {
+            const float dv = sig_diag(p.sig, sgrow, T, t, i);
+            Ce[i * (NT + 1)] = dv;
+            if (own) dgt[i] = dv;
+          }
+        }
+        __syncwarp();
+      } else if (diag) {  // rebuild the diagonal of the slab from the workspace copy
         const float* dgt = W.diag(t);
 #pragma unroll
         for (int s3 = 0; s3 < 3; ++s3)
@@ -333,7 +357,7 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
         const float ta = pick(tau, ra), tb = pick(tau, rb), tu = pick(tau, ru);
         cost_q += fmaf(ta, sa, tb * sb) + (m < NU ? tu * su : 0.0f);
         cost_l += fmaf(ca_, ta, cb_ * tb) + (m < NU ? cu * tu : 0.0f);
-        if (p.diag_cache && valid) {  // (mirror lanes check too; only owners write)
+        if (p.diag_cache && valid && !sigm) {  // (mirror lanes check too; only owners write)
           // the team scans the block for off-diagonal nonzeros (the diagonal
           // sits at flat index 15 i) and keeps a copy of the diagonal
           const float4* c4 = reinterpret_cast<const float4*>(Ce);
@@ -367,7 +391,7 @@ __global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ C
       active = false;
       break;
     }
-    if (first && p.diag_cache) {
+    if (first && p.diag_cache && !sigm) {
       diag = !__any_sync(FULL, offd);
       if (diag) {  // off-diagonal entries of the rebuilt blocks stay zero from here on
         for (int f = lane; f < EPW * CBLK; f += WARP) slab[f] = 0.0f;

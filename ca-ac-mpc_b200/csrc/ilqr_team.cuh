@@ -16,6 +16,7 @@
 #pragma once
 
 #include "ilqr_device.cuh"
+#include "ilqr_kernels.h"
 
 namespace ilqr {
 
@@ -36,6 +37,28 @@ constexpr uint32_t TSLAB_BYTES = EPW * CBLK * 4u;  // bytes one TMA box delivers
 __device__ __forceinline__ int row_a(int m) { return m < 4 ? 3 + m : 0; }
 
 __device__ __forceinline__ int row_b(int m) { return m == 0 ? 1 : (m == 1 ? 2 : 5 + m); }
+
+// Offset of entry i (tau order: p 0..2, q 3..6, v 7..9, thrust 10, w 11..13)
+// of step t within the x_q half of a sigmoid cost row (the x_p half adds 14 T).
+// _build_cost_tensors (training_modules/mlp_mpc_policy_diffmpc.py:194-247)
+// slices x_q into blocks of T steps: p (3), q (4), v (3), w (3), thrust (1).
+__device__ __forceinline__ int sig_off(int T, int t, int i) {
+  if (i < 3) return 3 * t + i;
+  if (i < 7) return 3 * T + 4 * t + (i - 3);
+  if (i < 10) return 7 * T + 3 * t + (i - 7);
+  if (i == 10) return 13 * T + t;
+  return 10 * T + 3 * t + (i - 11);
+}
+
+// diag(C_t)_i and c_t,i from a sigmoid cost row q (fp32, the reference's
+// operation order: one multiply, then one add or subtract).
+__device__ __forceinline__ float sig_diag(const SigmoidCost& s, const float* q, int T, int t, int i) {
+  return __ldg(q + sig_off(T, t, i)) * s.range_q + s.eps;
+}
+__device__ __forceinline__ float sig_c(const SigmoidCost& s, const float* q, int T, int t, int i) {
+  const float x = __ldg(q + 14 * T + sig_off(T, t, i));
+  return i == NX ? -(x * s.range_pt + s.eps) : (x - 0.5f) * s.range_p;
+}
 
 // Access to one element's C_t block in shared memory.
 struct DenseC {

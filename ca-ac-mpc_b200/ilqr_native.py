@@ -55,6 +55,10 @@ def lib():
                                     + [_P] * 9 + [_P, ctypes.c_size_t, _P], _I32),
             "ilqr_b200_backward_f32": ([_P] * 9 + [_I64, _I32, _F, _F] + [_P] * 7
                                        + [_P, ctypes.c_size_t, _P], _I32),
+            "ilqr_b200_solve_sigmoid_f32": ([_P] * 3 + [_F] * 4 + [_P] * 2 + [_I64, _I32, _F, _I32, _F, _F, _P, _I32, _P]
+                                            + [_P] * 9 + [_P, ctypes.c_size_t, _P], _I32),
+            "ilqr_b200_backward_sigmoid_f32": ([_P] * 3 + [_F] * 4 + [_P] * 3 + [_I64, _I32, _F, _F] + [_P] * 2
+                                               + [_P, ctypes.c_size_t, _P], _I32),
             "ilqr_b200_dynamics_f32": ([_P, _P, _I64, _F, _P, _P], _I32),
             "ilqr_b200_linearize_f32": ([_P, _P, _I64, _I32, _F, _P, _P, _P], _I32),
             "ilqr_b200_adjoint_lqr_f32": ([_P] * 10 + [_I64, _I32, _F, _P, _P, _P, _P], _I32),
@@ -76,6 +80,7 @@ EXPORTED_SYMBOLS = (
     "ilqr_b200_solve_f32", "ilqr_b200_backward_f32", "ilqr_b200_dynamics_f32",
     "ilqr_b200_linearize_f32", "ilqr_b200_adjoint_lqr_f32",
     "ilqr_b200_implicit_diff_assembly_f32", "ilqr_b200_solve_f32_noalloc",
+    "ilqr_b200_solve_sigmoid_f32", "ilqr_b200_backward_sigmoid_f32",
 )
 
 
@@ -226,6 +231,99 @@ def backward(X, U, C, grad_X, grad_U, C_final=None, x_ref=None, u_ref=None, tigh
         g("x0"), g("C"), g("c"), g("C_final"), g("c_final"), g("x_ref"), g("u_ref"),
         _ptr(ws), nbytes, _stream(dev))
     _check(st, "ilqr_b200_backward_f32")
+    return out
+
+
+class SigmoidCostSpec:
+    """Constants of the policy's cost construction from its sigmoid output
+    (_build_cost_tensors, training_modules/mlp_mpc_policy_diffmpc.py:194-247):
+    x_q = s * range_q + eps, c = (x_p - 0.5) * range_p, thrust c =
+    -(x_p * range_pt + eps) with range_pt = range_q * mass * 9.806."""
+
+    def __init__(self, eps: float = 0.1, range_q: float = 100000.0, range_p: float = 100000.0,
+                 mass: float = 0.752, range_pt: Optional[float] = None):
+        self.eps = float(eps)
+        self.range_q = float(range_q)
+        self.range_p = float(range_p)
+        self.range_pt = float(range_q * mass * 9.806 if range_pt is None else range_pt)
+
+    def args(self):
+        return (self.eps, self.range_q, self.range_p, self.range_pt)
+
+
+def solve_sigmoid(x0, U_init, sigmoid_cost, spec: Optional[SigmoidCostSpec] = None, u_min=None, u_max=None,
+                  dt=0.05, max_iter=10, reg_eps=1e-6, converge_tol=1e-6,
+                  alphas: Sequence[float] = DEFAULT_ALPHAS, forced_trace=None, want_trace=False,
+                  want_stats=False):
+    """solve() with the costs built in the kernel from the policy's sigmoid
+    output [B, 28 T] (zero terminal cost and references, as in the policy).
+    Returns the same dict as solve()."""
+    L = lib()
+    spec = spec or SigmoidCostSpec()
+    dev = _cuda_device(x0, "x0")
+    _device_ok(dev)
+    B = x0.shape[0]
+    T = U_init.shape[1]
+    _req(x0, "x0", (B, NX), dev)
+    _req(U_init, "U_init", (B, T, NU), dev)
+    _req(sigmoid_cost, "sigmoid_cost", (B, 2 * N * T), dev)
+    if (u_min is None) != (u_max is None):
+        raise RuntimeError("u_min and u_max must both be given or both be None")
+    _opt(u_min, "u_min", (NU,), dev)
+    _opt(u_max, "u_max", (NU,), dev)
+    _opt(forced_trace, "forced_trace", (B, max_iter), dev, torch.int8)
+    al = [float(a) for a in alphas]
+    if not 1 <= len(al) <= 8:
+        raise RuntimeError("between 1 and 8 line-search step sizes are supported")
+    out = dict(X=torch.empty(B, T + 1, NX, device=dev), U=torch.empty(B, T, NU, device=dev),
+               tight=torch.empty(B, T, NU, device=dev, dtype=torch.uint8))
+    trace = iters = status = best = s_it = s_gap = None
+    if want_trace:
+        trace = out["trace"] = torch.empty(B, max_iter, device=dev, dtype=torch.int8)
+    if want_stats:
+        iters = out["iters"] = torch.empty(B, device=dev, dtype=torch.int32)
+        status = out["status"] = torch.empty(B, device=dev, dtype=torch.int32)
+        best = out["best_cost"] = torch.empty(B, device=dev)
+        s_it = out["stall_iter"] = torch.empty(B, device=dev, dtype=torch.int32)
+        s_gap = out["stall_gap"] = torch.empty(B, device=dev)
+    nbytes = workspace_bytes("solve", B, T)
+    ws = torch.empty(max(nbytes, 1), device=dev, dtype=torch.uint8)
+    a_arr = (ctypes.c_float * len(al))(*al)
+    st = L.ilqr_b200_solve_sigmoid_f32(
+        _ptr(x0), _ptr(U_init), _ptr(sigmoid_cost), *spec.args(), _ptr(u_min), _ptr(u_max),
+        B, T, float(dt), int(max_iter), float(reg_eps), float(converge_tol),
+        ctypes.cast(a_arr, ctypes.c_void_p), len(al), _ptr(forced_trace), _ptr(out["X"]), _ptr(out["U"]),
+        _ptr(out["tight"]), _ptr(trace), _ptr(iters), _ptr(status), _ptr(best), _ptr(s_it), _ptr(s_gap),
+        _ptr(ws), nbytes, _stream(dev))
+    _check(st, "ilqr_b200_solve_sigmoid_f32")
+    return out
+
+
+def backward_sigmoid(X, U, sigmoid_cost, grad_X, grad_U, spec: Optional[SigmoidCostSpec] = None,
+                     tight=None, dt=0.05, reg_eps=1e-6, need=("x0", "sigmoid_cost")):
+    """backward() for solve_sigmoid(): returns a dict with the gradients of
+    x0 [B, 10] and of the sigmoid cost row [B, 28 T] (as selected by need)."""
+    L = lib()
+    spec = spec or SigmoidCostSpec()
+    dev = _cuda_device(X, "X")
+    _device_ok(dev)
+    B, T1, _ = X.shape
+    T = T1 - 1
+    _req(X, "X", (B, T + 1, NX), dev)
+    _req(U, "U", (B, T, NU), dev)
+    _req(sigmoid_cost, "sigmoid_cost", (B, 2 * N * T), dev)
+    _req(grad_X, "grad_X", (B, T + 1, NX), dev)
+    _req(grad_U, "grad_U", (B, T, NU), dev)
+    _opt(tight, "tight_mask", (B, T, NU), dev, torch.uint8)
+    shapes = dict(x0=(B, NX), sigmoid_cost=(B, 2 * N * T))
+    out = {k: torch.empty(shapes[k], device=dev) for k in need}
+    nbytes = workspace_bytes("backward", B, T)
+    ws = torch.empty(max(nbytes, 1), device=dev, dtype=torch.uint8)
+    st = L.ilqr_b200_backward_sigmoid_f32(
+        _ptr(X), _ptr(U), _ptr(sigmoid_cost), *spec.args(), _ptr(tight), _ptr(grad_X), _ptr(grad_U),
+        B, T, float(dt), float(reg_eps), _ptr(out.get("x0")), _ptr(out.get("sigmoid_cost")),
+        _ptr(ws), nbytes, _stream(dev))
+    _check(st, "ilqr_b200_backward_sigmoid_f32")
     return out
 
 

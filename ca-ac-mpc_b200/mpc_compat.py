@@ -159,6 +159,60 @@ class DroneMPCFunction(torch.autograd.Function):
         return tuple(g.get(nm) for nm in names) + (None,)
 
 
+class SigmoidQuadCost(NamedTuple):
+    """Diagonal quadratic costs given as the policy's sigmoid output
+    [B, 28 T] instead of dense C, c. The policy builds C, c from this tensor
+    in a Python loop over t (_build_cost_tensors,
+    training_modules/mlp_mpc_policy_diffmpc.py:194-247); passing it here
+    builds them inside the kernels, and autograd returns the gradient of
+    sigmoid_cost. Results equal a QuadCost of the C, c the policy would build.
+    range_pt defaults to range_q * mass * 9.806, as in the policy."""
+    sigmoid_cost: Tensor
+    eps: float = 0.1
+    range_q: float = 100000.0
+    range_p: float = 100000.0
+    mass: float = 0.752
+    range_pt: Optional[float] = None
+
+    def spec(self):
+        return _nat.SigmoidCostSpec(self.eps, self.range_q, self.range_p, self.mass, self.range_pt)
+
+
+class SigmoidMPCFunction(torch.autograd.Function):
+    """DroneMPCFunction for SigmoidQuadCost: forward(x0 [B,10],
+    sigmoid_cost [B,28T], solver_cfg) -> (X, U); backward returns the
+    gradients of x0 and sigmoid_cost."""
+
+    @staticmethod
+    def forward(ctx, x0, sigmoid_cost, solver_cfg):
+        spec = solver_cfg["sigmoid_spec"]
+        sc = _f32(sigmoid_cost)
+        out = _nat.solve_sigmoid(
+            _f32(x0), _f32(solver_cfg["U_init"]), sc, spec, solver_cfg.get("u_min"), solver_cfg.get("u_max"),
+            dt=solver_cfg["dt"], max_iter=solver_cfg["lqr_iter"], reg_eps=solver_cfg["eps"],
+            converge_tol=solver_cfg.get("converge_tol", 1e-6),
+            alphas=solver_cfg.get("alphas", _nat.DEFAULT_ALPHAS))
+        X, U = out["X"], out["U"]
+        ctx.save_for_backward(X, U, sc, out["tight"])
+        ctx.spec = spec
+        ctx.dt = float(solver_cfg["dt"])
+        ctx.reg_eps = float(solver_cfg.get("reg_eps", solver_cfg["eps"]))
+        return X, U
+
+    @staticmethod
+    def backward(ctx, grad_X, grad_U):
+        X, U, sc, tight = ctx.saved_tensors
+        need = ctx.needs_input_grad
+        want = tuple(nm for nm, nd in zip(("x0", "sigmoid_cost"), need[:2]) if nd)
+        if not want:
+            return None, None, None
+        gX = torch.zeros_like(X) if grad_X is None else grad_X.to(torch.float32).contiguous()
+        gU = torch.zeros_like(U) if grad_U is None else grad_U.to(torch.float32).contiguous()
+        g = _nat.backward_sigmoid(X, U, sc, gX, gU, ctx.spec, tight=tight, dt=ctx.dt,
+                                  reg_eps=ctx.reg_eps, need=want)
+        return g.get("x0"), g.get("sigmoid_cost"), None
+
+
 class FastMPC(nn.Module):
     """Drop-in replacement for mpc.pytorch's MPC class (mpc_compat.py:453-612).
 
@@ -216,8 +270,8 @@ class FastMPC(nn.Module):
             self._bounds_key = key
         return self._bounds
 
-    def forward(self, x_init: Tensor, cost: Union[QuadCost, nn.Module], dx: nn.Module):
-        assert isinstance(cost, QuadCost), "Only QuadCost supported"
+    def forward(self, x_init: Tensor, cost: Union[QuadCost, SigmoidQuadCost, nn.Module], dx: nn.Module):
+        assert isinstance(cost, (QuadCost, SigmoidQuadCost)), "Only QuadCost (or SigmoidQuadCost) supported"
         B = x_init.size(0)
         T = self.T
         nx, nu = self.n_state, self.n_ctrl
@@ -226,14 +280,26 @@ class FastMPC(nn.Module):
         dtype = x_init.dtype
         dt = getattr(dx, "dt", 0.02)
         self._get_ext()
-        C_bt, c_bt = _normalize_cost(cost.C, cost.c, B, T, n, device, dtype)
+        sigm = isinstance(cost, SigmoidQuadCost)
+        if not sigm:
+            C_bt, c_bt = _normalize_cost(cost.C, cost.c, B, T, n, device, dtype)
         u_min, u_max = self._get_bounds(device, dtype)
         U_init = _normalize_init(self.u_init, B, T, nu, device, dtype)
         x0 = x_init.float().contiguous()
         cfg = {"U_init": U_init, "u_min": u_min, "u_max": u_max, "dt": float(dt),
                "lqr_iter": self.lqr_iter, "eps": self.eps, "converge_tol": 1e-6,
                "reg_eps": self.eps, "nx": nx, "nu": nu, "alphas": self._alphas()}
-        if torch.is_grad_enabled() and self.backprop:
+        if sigm:
+            cfg["sigmoid_spec"] = cost.spec()
+            if torch.is_grad_enabled() and self.backprop:
+                X, U = SigmoidMPCFunction.apply(x0, cost.sigmoid_cost, cfg)
+            else:
+                with torch.inference_mode():
+                    out = _nat.solve_sigmoid(x0, U_init, _f32(cost.sigmoid_cost), cfg["sigmoid_spec"], u_min,
+                                             u_max, dt=float(dt), max_iter=self.lqr_iter, reg_eps=self.eps,
+                                             converge_tol=1e-6, alphas=self._alphas())
+                X, U = out["X"], out["U"]
+        elif torch.is_grad_enabled() and self.backprop:
             X, U = DroneMPCFunction.apply(x0, C_bt, c_bt, None, None, None, None, cfg)
         else:
             with torch.inference_mode():

@@ -150,6 +150,50 @@ int ilqr_b200_backward_f32(
     void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /*
+ * Costs from policy parameters. The policy builds its dense costs from a
+ * sigmoid output s [B, 28 T] in a Python loop over t
+ * (_build_cost_tensors, acmpc_public-master/training_modules/mlp_mpc_policy_diffmpc.py:194-247)
+ * and then calls the solver; these two entry points replace that construction
+ * plus ilqr_b200_solve_f32 / ilqr_b200_backward_f32 with the costs built
+ * inside the kernels (28 instead of 210 floats per element and step read,
+ * and a [B, 28 T] gradient written instead of grad_C).
+ *
+ * x_q = s[:, :14T] * range_q + cost_eps, x_p = s[:, 14T:]. x_q holds blocks of
+ * T steps p (3), q (4), v (3), w (3), thrust (1); diag(C_t) is, in tau order
+ * (p, q, v, thrust, w), the step-t slice of those blocks; c_t is
+ * (x_p - 0.5) * range_p on the same slices except the thrust entry,
+ * -(x_p * range_pt + cost_eps). The policy's values: cost_eps 0.1,
+ * range_q = range_p = 1e5, range_pt = range_q * mass * 9.806. C_final, c_final,
+ * x_ref, u_ref are zero (as in the policy). Everything else as
+ * ilqr_b200_solve_f32 (same workspace size); results equal that entry point's
+ * on the dense C, c the policy would build.
+ */
+int ilqr_b200_solve_sigmoid_f32(
+    const float* x0, const float* U_init, const float* sigmoid_cost,
+    float cost_eps, float range_q, float range_p, float range_pt,
+    const float* u_min, const float* u_max,
+    int64_t B, int32_t T, float dt, int32_t max_iter, float reg_eps, float converge_tol,
+    const float* alphas, int32_t n_alpha, const int8_t* forced_trace,
+    float* X, float* U, uint8_t* tight_mask,
+    int8_t* trace, int32_t* iters, uint32_t* elem_status, float* best_cost,
+    int32_t* stall_iter, float* stall_gap,
+    void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/*
+ * Backward of ilqr_b200_solve_sigmoid_f32: as ilqr_b200_backward_f32, with
+ * the gradient of the sigmoid cost row, grad_sigmoid_cost [B, 28 T] (NULL to
+ * skip), in place of grad_C / grad_c: the chain rule of the construction
+ * above applied to the diagonal of grad_C and to grad_c.
+ */
+int ilqr_b200_backward_sigmoid_f32(
+    const float* X, const float* U, const float* sigmoid_cost,
+    float cost_eps, float range_q, float range_p, float range_pt,
+    const uint8_t* tight_mask, const float* grad_X, const float* grad_U,
+    int64_t B, int32_t T, float dt, float reg_eps,
+    float* grad_x0, float* grad_sigmoid_cost,
+    void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/*
  * One step of the quadrotor model, x_next = f(x, u), for n states.
  * Replaces DroneDx.forward_CTBR (acmpc_public-master/diff_mpc_drones/drone.py:409-465)
  * and the reference's device step (cpp/forward_pass_kernel.cu:66-115).

@@ -601,10 +601,74 @@ def backward(X, U, C, C_f, x_ref, u_ref, tight, grad_X, grad_U, dt, reg,
                 dX=dX, dU=dU, K=K, k=k)
 
 
+def _sigmoid_slices(T):
+    """(offset into x_q, length-T index) of each tau entry's block.
+    _build_cost_tensors (training_modules/mlp_mpc_policy_diffmpc.py:204-216)
+    slices x_q / x_p into blocks of T steps: p (3), q (4), v (3), w (3),
+    thrust (1); the diagonal and c list them in tau order p, q, v, thrust, w
+    (:226-243)."""
+    t = np.arange(T)
+    idx = np.empty((T, N), dtype=np.int64)
+    for i in range(3):
+        idx[:, i] = 3 * t + i
+    for i in range(4):
+        idx[:, 3 + i] = 3 * T + 4 * t + i
+    for i in range(3):
+        idx[:, 7 + i] = 7 * T + 3 * t + i
+    idx[:, 10] = 13 * T + t
+    for i in range(3):
+        idx[:, 11 + i] = 10 * T + 3 * t + i
+    return idx
+
+
+def sigmoid_costs(sc, T, eps=0.1, range_q=100000.0, range_p=100000.0, range_pt=None, mass=MASS):
+    """C [B,T,14,14] (diagonal) and c [B,T,14] from the policy's sigmoid output
+    sc [B, 28 T], in float32 with the reference's operation order
+    (_build_cost_tensors, mlp_mpc_policy_diffmpc.py:194-247):
+    x_q = sc[:, :14T] * range_q + eps; x_p = sc[:, 14T:];
+    c = (x_p - 0.5) * range_p, thrust entry c = -(x_p * range_pt + eps)
+    with range_pt = range_q * mass * 9.806 (a Python float, rounded to fp32)."""
+    f32 = np.float32
+    sc = np.asarray(sc, dtype=f32)
+    nb = sc.shape[0]
+    rpt = f32(range_q * mass * 9.806 if range_pt is None else range_pt)
+    x_q = sc[:, :14 * T] * f32(range_q) + f32(eps)
+    x_p = sc[:, 14 * T:]
+    idx = _sigmoid_slices(T)
+    diag = x_q[:, idx]                                   # [B, T, 14]
+    xp = x_p[:, idx]
+    c = (xp - f32(0.5)) * f32(range_p)
+    c[..., 10] = -(xp[..., 10] * rpt + f32(eps))
+    C = np.zeros((nb, T, N, N), dtype=f32)
+    ii = np.arange(N)
+    C[:, :, ii, ii] = diag
+    return C, c.astype(f32)
+
+
+def sigmoid_cost_grad(grad_C, grad_c, T, range_q=100000.0, range_p=100000.0, range_pt=None, mass=MASS):
+    """Gradient of the sigmoid output through sigmoid_costs (the chain rule
+    torch's autograd applies to _build_cost_tensors): the diagonal of grad_C
+    times range_q, grad_c times range_p, and for the thrust entry
+    (-grad_c) * range_pt."""
+    f32 = np.float32
+    rpt = f32(range_q * mass * 9.806 if range_pt is None else range_pt)
+    grad_C = np.asarray(grad_C, dtype=f32)
+    grad_c = np.asarray(grad_c, dtype=f32)
+    nb = grad_C.shape[0]
+    idx = _sigmoid_slices(T)
+    ii = np.arange(N)
+    g = np.zeros((nb, 28 * T), dtype=f32)
+    g[:, idx] = grad_C[:, :, ii, ii] * f32(range_q)
+    gp = grad_c * f32(range_p)
+    gp[..., 10] = (-grad_c[..., 10]) * rpt
+    g[:, 14 * T + idx] = gp
+    return g
+
+
 __all__ = [
     "NX", "NU", "N", "MASS", "GRAV_Z", "NOT_RUN", "DEFAULT_ALPHAS",
     "drone_step", "drone_jacobian", "rollout", "linearize", "objective",
     "quadraticize", "chol4", "chol_solve", "riccati", "line_search",
     "argmin_nan_first", "tight_mask", "solve", "global_converged_flag",
-    "zero_constrained_lqr", "backward",
+    "zero_constrained_lqr", "backward", "sigmoid_costs", "sigmoid_cost_grad",
 ]

@@ -56,6 +56,20 @@ def import_reference(ref_root):
     return drone, DifferentialMPC
 
 
+def import_policy_cost_builder(ref_root):
+    """The policy's own cost construction, _build_cost_tensors
+    (training_modules/mlp_mpc_policy_diffmpc.py:194-247). The module imports
+    gym.spaces only for its class definitions: a stub stands in for it."""
+    gym = types.ModuleType("gym")
+    gym.spaces = types.ModuleType("gym.spaces")
+    gym.spaces.Space = gym.spaces.Box = type("Space", (), {})
+    sys.modules.setdefault("gym", gym)
+    sys.modules.setdefault("gym.spaces", gym.spaces)
+    sys.path.insert(0, os.path.join(ref_root, "acmpc_public-master", "training_modules"))
+    import mlp_mpc_policy_diffmpc as pol
+    return pol.CustomNetworkDiffMPC._build_cost_tensors
+
+
 def run_reference(drone, DM, inp, T, max_iter, alphas, dt, bounds, gX, gU,
                   extra=None, reg=1e-6):
     import torch
@@ -76,8 +90,8 @@ def run_reference(drone, DM, inp, T, max_iter, alphas, dt, bounds, gX, gU,
         grad_method=DM.GradMethod.ANALYTIC, max_iter=max_iter, exit_unconverged=False,
         detach_unconverged=False, device="cpu", verbose=0, use_vmap_line_search=False,
         alphas=tuple(alphas))
-    t = lambda a: torch.tensor(a).clone().requires_grad_(True)
-    x0, C, c = t(inp["x0"]), t(inp["C"]), t(inp["c"])
+    t = lambda a: a if isinstance(a, torch.Tensor) else torch.tensor(a).clone().requires_grad_(True)
+    x0, C, c = t(inp["x0"]), t(inp["C"]), t(inp["c"])  # C, c may come from a construction graph
     ex = extra or {}
     C_f = t(ex.get("C_final", np.zeros((B, n, n), np.float32)))
     c_f = t(ex.get("c_final", np.zeros((B, n), np.float32)))
@@ -144,7 +158,7 @@ def run_reference(drone, DM, inp, T, max_iter, alphas, dt, bounds, gX, gU,
             i, j = last_acc[b]
             assert torch.equal(X[b].detach(), rec_X[i][b, j]), "X is not the accepted candidate"
             assert torch.equal(U[b].detach(), rec_U[i][b, j]), "U is not the accepted candidate"
-    g = lambda v: v.grad.detach().numpy().copy()
+    g = lambda v: v.grad.detach().numpy().copy() if v.grad is not None else np.zeros(tuple(v.shape), np.float32)
     costs_all = torch.stack(rec_costs).numpy() if rec_costs else np.zeros((0, B, len(alphas)), np.float32)
     return dict(costs=costs_all, obj0=rec_obj[0].numpy().copy(),
                 refreeze_drift=np.array(drift), reimproved=np.array(reimproved), X=X.detach().numpy().copy(), U=U.detach().numpy().copy(), trace=trace,
@@ -200,6 +214,36 @@ def make_case(drone, DM, name):
           f"converged={bool(out['converged'])} tight={tf:.3f} refreeze_drift={float(out['refreeze_drift']):.1e} reimproved={int(out['reimproved'])} -> {os.path.getsize(path)/1e3:.0f} kB")
 
 
+def make_sigmoid_case(drone, DM, build, name="sigmoid_b16_t10", B=16, T=10, max_iter=5):
+    """Costs from the policy's sigmoid output: the reference's construction
+    feeds DiffMPC, and the gradient flows back to the sigmoid output."""
+    import torch
+    rng = np.random.default_rng(21)
+    sc = (1.0 / (1.0 + np.exp(-rng.normal(0.0, 1.5, (B, 28 * T))))).astype(np.float32)
+    inp = wl.make_inputs(B, T, seed=4)
+    dx = types.SimpleNamespace(n_state=10, n_ctrl=4, mass=0.752)
+    fake = types.SimpleNamespace(T=T, dx=dx, mpc_device=torch.device("cpu"))
+    sct = torch.tensor(sc).requires_grad_(True)
+    C, c, Cf, cf = build(fake, sct)
+    inp_t = dict(x0=inp["x0"], U_init=inp["U_init"], C=C, c=c)
+    gX, gU = wl.make_backward_seeds(B, T, seed=1)
+    alphas = (1.0, 0.8, 0.5, 0.2, 0.1)
+    out = run_reference(drone, DM, inp_t, T, max_iter, alphas, wl.DT, True, gX, gU)
+    arrays = dict(x0=inp["x0"], U_init=inp["U_init"], sigmoid_cost=sc,
+                  C=C.detach().numpy().copy(), c=c.detach().numpy().copy())
+    arrays.update(gX=gX, gU=gU, dt=np.array(wl.DT), max_iter=np.array(max_iter),
+                  alphas=np.array(alphas, dtype=np.float32), bounds=np.array(True),
+                  reg=np.array(1e-6), converge_tol=np.array(1e-6),
+                  cost_eps=np.array(0.1), range_q=np.array(100000.0), range_p=np.array(100000.0),
+                  range_pt=np.array(100000.0 * 0.752 * 9.806))
+    arrays.update({"ref_" + k: v for k, v in out.items() if k not in ("grad_C", "grad_c")})
+    arrays["ref_grad_sigmoid_cost"] = sct.grad.detach().numpy().copy()
+    path = os.path.join(HERE, name + ".npz")
+    np.savez_compressed(path, **arrays)
+    print(f"{name}: B={B} T={T} iters={max_iter} run={int(out['n_iter_run'])} "
+          f"tight={out['tight'].mean():.3f} -> {os.path.getsize(path)/1e3:.0f} kB")
+
+
 def make_dynamics(drone):
     import torch
     rng = np.random.default_rng(5)
@@ -229,11 +273,14 @@ def main():
     ap.add_argument("--only", nargs="*")
     args = ap.parse_args()
     drone, DM = import_reference(args.ref)
-    make_dynamics(drone)
+    if not args.only:
+        make_dynamics(drone)
     for name in CASES:
         if args.only and name not in args.only:
             continue
         make_case(drone, DM, name)
+    if not args.only or "sigmoid_b16_t10" in args.only:
+        make_sigmoid_case(drone, DM, import_policy_cost_builder(args.ref))
 
 
 if __name__ == "__main__":

@@ -282,3 +282,83 @@ def test_more_step_sizes_than_candidate_slots(forced):
     if forced:
         acc = trace >= 0
         assert (r["trace"][acc] == trace[acc]).all()
+
+
+def _sig_spec(d):
+    return nat.SigmoidCostSpec(float(d["cost_eps"]), float(d["range_q"]), float(d["range_p"]),
+                               range_pt=float(d["range_pt"]))
+
+
+def test_sigmoid_cost_replay_matches_reference():
+    """Costs built in the kernel from the policy's sigmoid output: replaying the
+    reference's decisions, X, U match within 1e-4 and the gradient of the
+    sigmoid output within 1e-3 (reference: _build_cost_tensors + DiffMPC +
+    autograd)."""
+    d = load("sigmoid_b16_t10")
+    kw = case_kwargs(d)
+    spec = _sig_spec(d)
+    r = nat.solve_sigmoid(g(d["x0"]), g(d["U_init"]), g(d["sigmoid_cost"]), spec, g(kw["u_min"]),
+                          g(kw["u_max"]), dt=kw["dt"], max_iter=kw["max_iter"], reg_eps=kw["reg"],
+                          alphas=kw["alphas"], forced_trace=g(d["ref_trace"], torch.int8))
+    assert max_rel(r["X"].cpu().numpy(), d["ref_X"]) <= TOL_XU
+    assert max_rel(r["U"].cpu().numpy(), d["ref_U"]) <= TOL_XU
+    assert np.array_equal(r["tight"].cpu().numpy().astype(bool), d["ref_tight"])
+    gr = nat.backward_sigmoid(g(d["ref_X"]), g(d["ref_U"]), g(d["sigmoid_cost"]), g(d["gX"]), g(d["gU"]),
+                              spec, tight=g(d["ref_tight"], torch.uint8), dt=kw["dt"], reg_eps=kw["reg"])
+    assert max_rel(gr["sigmoid_cost"].cpu().numpy(), d["ref_grad_sigmoid_cost"]) <= TOL_GRAD
+    assert max_rel(gr["x0"].cpu().numpy(), d["ref_grad_x0"]) <= TOL_GRAD
+
+
+def test_sigmoid_cost_path_equals_dense_path():
+    """On the dense C, c the policy would build from the same sigmoid output,
+    the dense entry points give bit-identical solves, and their gradients
+    chained through the construction equal the sigmoid backward's, at
+    B=600, T=20 (free-running decisions included)."""
+    B, T = 600, 20
+    rng = np.random.default_rng(8)
+    sc = (1.0 / (1.0 + np.exp(-rng.normal(0.0, 1.5, (B, 28 * T))))).astype(np.float32)
+    inp = wl.make_inputs(B, T, seed=2)
+    spec = nat.SigmoidCostSpec()
+    C, c = O.sigmoid_costs(sc, T, *spec.args())
+    common = dict(dt=wl.DT, max_iter=5, alphas=(1.0, 0.8, 0.5, 0.2, 0.1), want_trace=True, want_stats=True)
+    x0, Ui, lo, hi = g(inp["x0"]), g(inp["U_init"]), g(wl.U_MIN), g(wl.U_MAX)
+    dn = nat.solve(x0, Ui, g(C), g(c), None, None, None, None, lo, hi, **common)
+    sg = nat.solve_sigmoid(x0, Ui, g(sc), spec, lo, hi, **common)
+    for k in dn:
+        a, b = dn[k].cpu().numpy(), sg[k].cpu().numpy()
+        assert np.array_equal(a, b, equal_nan=a.dtype.kind == "f"), k
+    gX, gU = (g(a) for a in wl.make_backward_seeds(B, T))
+    gd = nat.backward(dn["X"], dn["U"], g(C), gX, gU, tight=dn["tight"], dt=wl.DT, need=("x0", "C", "c"))
+    gs = nat.backward_sigmoid(sg["X"], sg["U"], g(sc), gX, gU, spec, tight=sg["tight"], dt=wl.DT)
+    chained = O.sigmoid_cost_grad(gd["C"].cpu().numpy(), gd["c"].cpu().numpy(), T, spec.range_q,
+                                  spec.range_p, spec.range_pt)
+    assert np.array_equal(chained, gs["sigmoid_cost"].cpu().numpy())
+    assert torch.equal(gd["x0"], gs["x0"])
+
+
+def test_fastmpc_sigmoid_cost_autograd():
+    """FastMPC with a SigmoidQuadCost: the same X, U as a QuadCost of the
+    policy's dense costs, and autograd delivers the kernel's gradient of the
+    sigmoid output."""
+    d = load("sigmoid_b16_t10")
+    T = d["U_init"].shape[1]
+    lo, hi = g(wl.U_MIN), g(wl.U_MAX)
+    mpc = mpc_compat.FastMPC(10, 4, T, u_lower=lo.view(1, 1, 4).expand(T, 1, 4),
+                             u_upper=hi.view(1, 1, 4).expand(T, 1, 4), lqr_iter=int(d["max_iter"]),
+                             eps=1e-6)
+    x0 = g(d["x0"])
+    sc = g(d["sigmoid_cost"]).requires_grad_(True)
+    x, u, _ = mpc(x0, mpc_compat.SigmoidQuadCost(sc), _dx())
+    C = g(d["C"]).permute(1, 0, 2, 3)
+    c = g(d["c"]).permute(1, 0, 2)
+    with torch.no_grad():
+        xd, ud, _ = mpc(x0, mpc_compat.QuadCost(C, c), _dx())
+    assert torch.equal(x, xd) and torch.equal(u, ud)
+    gx, gu = g(d["gX"]).permute(1, 0, 2), g(d["gU"]).permute(1, 0, 2)
+    ((x * gx).sum() + (u * gu).sum()).backward()
+    spec = nat.SigmoidCostSpec()
+    out = nat.solve_sigmoid(x0, g(d["U_init"]), g(d["sigmoid_cost"]), spec, lo, hi, dt=wl.DT,
+                            max_iter=int(d["max_iter"]), reg_eps=1e-6)
+    ref = nat.backward_sigmoid(out["X"], out["U"], g(d["sigmoid_cost"]), g(d["gX"]), g(d["gU"]), spec,
+                               tight=out["tight"], dt=wl.DT, reg_eps=1e-6)
+    assert torch.equal(sc.grad, ref["sigmoid_cost"])

@@ -107,3 +107,30 @@ def test_chol_fallback_is_exercised():
     d = load("indef_b8_t4")
     r, _ = _solve(d, forced=d["ref_trace"])
     assert r["chol_fail"][::2].all() and not r["chol_fail"][1::2].any()
+
+
+def test_sigmoid_cost_construction_matches_reference():
+    """The policy's cost construction from its sigmoid output, restated, is
+    bit-identical to the reference's _build_cost_tensors."""
+    d = load("sigmoid_b16_t10")
+    T = d["U_init"].shape[1]
+    C, c = O.sigmoid_costs(d["sigmoid_cost"], T, float(d["cost_eps"]), float(d["range_q"]),
+                           float(d["range_p"]), float(d["range_pt"]))
+    assert np.array_equal(C, d["C"])
+    assert np.array_equal(c, d["c"])
+
+
+def test_sigmoid_cost_gradient_matches_reference():
+    """Replaying the reference's decisions on the reference-built costs, the
+    oracle's backward plus the chain rule reproduce the reference's gradient
+    of the sigmoid output."""
+    d = load("sigmoid_b16_t10")
+    T = d["U_init"].shape[1]
+    r, kw = _solve(d, forced=d["ref_trace"])
+    assert max_rel(r["X"], d["ref_X"]) <= TOL_XU
+    assert max_rel(r["U"], d["ref_U"]) <= TOL_XU
+    g = _backward(d, d["ref_X"], d["ref_U"], d["ref_tight"], kw)
+    gs = O.sigmoid_cost_grad(g["grad_C"], g["grad_c"], T, float(d["range_q"]), float(d["range_p"]),
+                             float(d["range_pt"]))
+    assert max_rel(gs, d["ref_grad_sigmoid_cost"]) <= TOL_GRAD
+    assert max_rel(g["grad_x0"], d["ref_grad_x0"]) <= TOL_GRAD
