@@ -48,6 +48,8 @@ def _args():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-sigmoid", action="store_true",
+                    help="skip the section for costs given as the policy's sigmoid output")
     ap.add_argument("--latency-reps", type=int, default=200)
     ap.add_argument("--batch", type=int, default=None,
                     help="elements per GPU (default: the workload's 16384); for profiling runs")
@@ -369,6 +371,88 @@ def run_ours(args):
         lat = {"p50_us": statistics.median(samples), "p90_us": sorted(samples)[int(0.9 * len(samples))],
                "reps": len(samples), "config": "B=16, T=5, 10 iterations, fwd+bwd, device-resident"}
 
+    # ---- costs from the policy's sigmoid output [B, 28 T] (SigmoidQuadCost) ----
+    # Same batch, horizon, iterations and model; the costs are the diagonal
+    # ones the policy builds from its sigmoid output, built inside the kernels.
+    sig = None
+    if not args.no_sigmoid:
+        rng = np.random.default_rng(100 + rank)
+        scn = (1.0 / (1.0 + np.exp(-rng.normal(0.0, 1.5, (B, 28 * T))))).astype(np.float32)
+        sc = torch.from_numpy(scn).to(dev)
+        spec = nat.SigmoidCostSpec()
+
+        def sig_step(timing=None):
+            if timing is not None:
+                timing[0].record(stream)
+            o = nat.solve_sigmoid(d["x0"], d["U_init"], sc, spec, lo, hi, dt=wl.DT, max_iter=iters,
+                                  reg_eps=wl.REG_EPS, alphas=alphas)
+            if timing is not None:
+                timing[1].record(stream)
+            nat.backward_sigmoid(o["X"], o["U"], sc, gX, gU, spec, tight=o["tight"], dt=wl.DT,
+                                 reg_eps=wl.REG_EPS)
+            if timing is not None:
+                timing[2].record(stream)
+
+        for _ in range(max(3, args.warmup)):
+            sig_step()
+        barrier()
+        stim = [(ev(), ev(), ev()) for _ in range(args.steps)]
+        s0, s1 = ev(), ev()
+        s0.record(stream)
+        for i in range(args.steps):
+            sig_step(stim[i])
+        s1.record(stream)
+        barrier()
+        sel = s0.elapsed_time(s1) * 1e-3
+        if world > 1:
+            t = torch.tensor([sel], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            sel = float(t.item())
+        # end to end through FastMPC / SigmoidQuadCost with host buffers
+        pin = lambda a: torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
+        h_x0, h_sc = pin(inp["x0"]), pin(scn)
+        h_gX, h_gU = pin(np.transpose(gXn, (1, 0, 2))), pin(np.transpose(gUn, (1, 0, 2)))
+        h_act, h_gx0 = torch.empty(B, 4).pin_memory(), torch.empty(B, 10).pin_memory()
+        smpc = mpc_compat.MPC(10, 4, T, u_lower=lo.view(1, 1, 4).expand(T, 1, 4),
+                              u_upper=hi.view(1, 1, 4).expand(T, 1, 4), lqr_iter=iters,
+                              eps=wl.REG_EPS, alphas=alphas)
+        sdyn = type("Dyn", (), {"dt": wl.DT})()
+
+        def sig_e2e():
+            x0 = h_x0.to(dev, non_blocking=True).requires_grad_(True)
+            scd = h_sc.to(dev, non_blocking=True).requires_grad_(True)
+            gx = h_gX.to(dev, non_blocking=True)
+            gu = h_gU.to(dev, non_blocking=True)
+            x, u, _ = smpc(x0, mpc_compat.SigmoidQuadCost(scd), sdyn)
+            ((x * gx).sum() + (u * gu).sum()).backward()
+            h_act.copy_(u[0].detach(), non_blocking=True)
+            h_gx0.copy_(x0.grad, non_blocking=True)
+
+        for _ in range(max(3, args.warmup)):
+            sig_e2e()
+        barrier()
+        e0, e1 = ev(), ev()
+        e0.record(stream)
+        for _ in range(args.steps):
+            sig_e2e()
+        e1.record(stream)
+        barrier()
+        sel_e2e = e0.elapsed_time(e1) * 1e-3
+        if world > 1:
+            t = torch.tensor([sel_e2e], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            sel_e2e = float(t.item())
+        h2d = sum(t.numel() * 4 for t in (h_x0, h_sc, h_gX, h_gU))
+        sig = {"workload": f"policy_sigmoid_b{B}_t{T}", "value": world * B / (sel / args.steps),
+               "unit": "solves/s", "ms_per_step": sel / args.steps * 1e3,
+               "kernel_ms": {"solve_mean": statistics.mean(a.elapsed_time(b) for a, b, _ in stim),
+                             "backward_mean": statistics.mean(b.elapsed_time(c) for _, b, c in stim)},
+               "input": "sigmoid output [B, 28 T] (28 floats per element and step instead of 210)",
+               "e2e": {"value": world * B / (sel_e2e / args.steps), "unit": "solves/s",
+                       "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": (h_act.numel() + h_gx0.numel()) * 4,
+                       "ms_per_step": sel_e2e / args.steps * 1e3,
+                       "path": "mpc_compat.MPC(...)(x_init, SigmoidQuadCost(s), dx) + autograd backward"}}
+
     # ---- CPU baseline (rank 0, N=1) ------------------------------------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -397,6 +481,7 @@ def run_ours(args):
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
         "gpu_launches": 2 * args.steps, "clocks": clk.summary(),
         "latency_b16_t5": lat,
+        "policy_sigmoid_cost": sig,
         "kernel_ms": {"solve_mean": statistics.mean(solve_ms), "backward_mean": statistics.mean(bwd_ms)},
     }
     print(json.dumps(line), flush=True)
