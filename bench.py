@@ -453,6 +453,73 @@ def run_ours(args):
                        "ms_per_step": sel_e2e / args.steps * 1e3,
                        "path": "mpc_compat.MPC(...)(x_init, SigmoidQuadCost(s), dx) + autograd backward"}}
 
+    # ---- the policy actor's MPC step: one call vs the reference's chunk loop ---
+    # PolicyMPC.actor against a restatement of forward_actor's loop
+    # (mlp_mpc_policy_diffmpc.py:326-402): 1024-element chunks, dense costs
+    # built with a Python loop over t, one host read per chunk. Both run on
+    # this solver, without gradients (evaluation), rank 0 only.
+    actor = None
+    if rank == 0 and not args.no_sigmoid:
+        import policy_mpc
+        pm = policy_mpc.PolicyMPC(T, wl.DT, lqr_iter=iters, eps=wl.REG_EPS, alphas=alphas, device=dev)
+        sc_all = sc
+        st_all = d["x0"]
+
+        def build_dense(s_chunk):
+            n_c = s_chunk.shape[0]
+            x_q = s_chunk[:, :14 * T] * 100000.0 + 0.1
+            x_p = s_chunk[:, 14 * T:]
+            Cc = torch.zeros(n_c, T, 14, 14, device=dev)
+            cc = torch.zeros(n_c, T, 14, device=dev)
+            for t_ in range(T):
+                dv = torch.cat([x_q[:, 3 * t_:3 * t_ + 3], x_q[:, 3 * T + 4 * t_:3 * T + 4 * t_ + 4],
+                                x_q[:, 7 * T + 3 * t_:7 * T + 3 * t_ + 3], x_q[:, 13 * T + t_:13 * T + t_ + 1],
+                                x_q[:, 10 * T + 3 * t_:10 * T + 3 * t_ + 3]], dim=1)
+                Cc[:, t_] = torch.diag_embed(dv)
+                cc[:, t_] = torch.cat([(x_p[:, 3 * t_:3 * t_ + 3] - 0.5) * 1e5,
+                                       (x_p[:, 3 * T + 4 * t_:3 * T + 4 * t_ + 4] - 0.5) * 1e5,
+                                       (x_p[:, 7 * T + 3 * t_:7 * T + 3 * t_ + 3] - 0.5) * 1e5,
+                                       -(x_p[:, 13 * T + t_:13 * T + t_ + 1] * (1e5 * 0.752 * 9.806) + 0.1),
+                                       (x_p[:, 10 * T + 3 * t_:10 * T + 3 * t_ + 3] - 0.5) * 1e5], dim=1)
+            return Cc, cc
+
+        loop_mpc = mpc_compat.MPC(10, 4, T, u_lower=lo.view(1, 1, 4).expand(T, 1, 4),
+                                  u_upper=hi.view(1, 1, 4).expand(T, 1, 4), lqr_iter=iters,
+                                  eps=wl.REG_EPS, alphas=alphas)
+        ldyn = type("Dyn", (), {"dt": wl.DT})()
+        u_prev = torch.zeros(B, 4, device=dev)
+        u_prev[:, 0] = 0.752 * 9.8066
+
+        def chunk_loop():
+            nom_u = torch.zeros(B, T, 4, device=dev)
+            bad = 0
+            for s0_ in range(0, B, 1024):
+                e_ = min(B, s0_ + 1024)
+                Cc, cc = build_dense(sc_all[s0_:e_])
+                loop_mpc.u_init = u_prev[s0_:e_].unsqueeze(1).expand(-1, T, -1).permute(1, 0, 2).contiguous()
+                _, U_tbn, _ = loop_mpc(st_all[s0_:e_], mpc_compat.QuadCost(Cc.permute(1, 0, 2, 3).contiguous(),
+                                                                           cc.permute(1, 0, 2).contiguous()), ldyn)
+                nom_u[s0_:e_] = U_tbn.permute(1, 0, 2)
+                bad += int((~torch.isfinite(U_tbn)).any().cpu().item())
+            return nom_u
+
+        def timed(fn, reps):
+            out = []
+            for _ in range(reps + 2):
+                a, b_ = ev(), ev()
+                a.record(stream)
+                with torch.no_grad():
+                    fn()
+                b_.record(stream)
+                b_.synchronize()
+                out.append(a.elapsed_time(b_))
+            return statistics.median(out[2:])
+
+        one = timed(lambda: pm.actor(sc_all, st_all), max(3, args.steps // 2))
+        loop = timed(chunk_loop, max(3, args.steps // 2))
+        actor = {"B": B, "T": T, "iters": iters, "one_call_ms": one, "reference_chunk_loop_ms": loop,
+                 "note": "no gradients; the chunk loop is the reference's forward_actor loop on this solver"}
+
     # ---- CPU baseline (rank 0, N=1) ------------------------------------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -482,6 +549,7 @@ def run_ours(args):
         "gpu_launches": 2 * args.steps, "clocks": clk.summary(),
         "latency_b16_t5": lat,
         "policy_sigmoid_cost": sig,
+        "policy_actor_step": actor,
         "kernel_ms": {"solve_mean": statistics.mean(solve_ms), "backward_mean": statistics.mean(bwd_ms)},
     }
     print(json.dumps(line), flush=True)
