@@ -169,23 +169,33 @@ struct Chol4 {
   float r0, r1, r2, r3;  // reciprocals of the diagonal
 };
 
+// 1/sqrt(d): the hardware approximation refined by one Newton-Raphson step
+// for the inverse square root, y <- y (3 - d y^2) / 2 (about 1 ulp). Only the
+// reciprocals of the diagonal of L enter the solves. Subnormal, zero, negative,
+// infinite or NaN d (a failed or degenerate factorisation) take the correctly
+// rounded library routine instead.
+__device__ __forceinline__ float inv_sqrt(float d) {
+  if (!(d >= 1.17549435e-38f && d <= 3.4e38f)) return __frsqrt_rn(d);
+  const float y = rsqrtf(d);
+  const float h = 0.5f * d * y;
+  return fmaf(-h, y * y, 1.5f * y);
+}
+
 __device__ __forceinline__ bool chol4(const float (&M)[NU][NU], Chol4& L) {
-  // Only the reciprocals of the diagonal of L enter the solves: each is one
-  // correctly rounded 1/sqrt(d).
   const float d0 = M[0][0];
-  L.r0 = __frsqrt_rn(d0);
+  L.r0 = inv_sqrt(d0);
   L.l10 = M[1][0] * L.r0;
   L.l20 = M[2][0] * L.r0;
   L.l30 = M[3][0] * L.r0;
   const float d1 = M[1][1] - L.l10 * L.l10;
-  L.r1 = __frsqrt_rn(d1);
+  L.r1 = inv_sqrt(d1);
   L.l21 = (M[2][1] - L.l20 * L.l10) * L.r1;
   L.l31 = (M[3][1] - L.l30 * L.l10) * L.r1;
   const float d2 = (M[2][2] - L.l20 * L.l20) - L.l21 * L.l21;
-  L.r2 = __frsqrt_rn(d2);
+  L.r2 = inv_sqrt(d2);
   L.l32 = ((M[3][2] - L.l30 * L.l20) - L.l31 * L.l21) * L.r2;
   const float d3 = ((M[3][3] - L.l30 * L.l30) - L.l31 * L.l31) - L.l32 * L.l32;
-  L.r3 = __frsqrt_rn(d3);
+  L.r3 = inv_sqrt(d3);
   return (d0 > 0.0f) && (d1 > 0.0f) && (d2 > 0.0f) && (d3 > 0.0f);
 }
 
