@@ -368,8 +368,24 @@ def run_ours(args):
             b.synchronize()
             if r >= 10:
                 samples.append(a.elapsed_time(b) * 1e3)
+        # the same step replayed from a CUDA graph (ilqr_native.CapturedSolve):
+        # inputs copied into its static buffers, then one graph launch
+        cap = nat.CapturedSolve(16, lc["T"], dev, lo, hi, dt=wl.DT, max_iter=lc["max_iter"],
+                                alphas=lc["alphas"])
+        gsamples = []
+        for r in range(args.latency_reps + 10):
+            a, b = ev(), ev()
+            a.record(stream)
+            cap(ld["x0"], ld["U_init"], ld["C"], ld["c"], lgx, lgu)
+            b.record(stream)
+            b.synchronize()
+            if r >= 10:
+                gsamples.append(a.elapsed_time(b) * 1e3)
         lat = {"p50_us": statistics.median(samples), "p90_us": sorted(samples)[int(0.9 * len(samples))],
-               "reps": len(samples), "config": "B=16, T=5, 10 iterations, fwd+bwd, device-resident"}
+               "reps": len(samples), "config": "B=16, T=5, 10 iterations, fwd+bwd, device-resident",
+               "p50_graph_us": statistics.median(gsamples),
+               "p90_graph_us": sorted(gsamples)[int(0.9 * len(gsamples))],
+               "graph": "ilqr_native.CapturedSolve: input copies + one CUDA graph replay of solve + backward"}
 
     # ---- costs from the policy's sigmoid output [B, 28 T] (SigmoidQuadCost) ----
     # Same batch, horizon, iterations and model; the costs are the diagonal

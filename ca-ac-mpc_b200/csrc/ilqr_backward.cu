@@ -26,7 +26,8 @@ __device__ __forceinline__ float pick14(const float (&v)[NT], int i) {
   return r;
 }
 
-__global__ void __launch_bounds__(32, 19) backward_kernel(const __grid_constant__ CUtensorMap tmC,
+template <int MINB>
+__global__ void __launch_bounds__(32, MINB) backward_kernel(const __grid_constant__ CUtensorMap tmC,
                                                           const __grid_constant__ CUtensorMap tmG,
                                                           const BackwardParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -261,7 +262,10 @@ cudaError_t launch_backward(const CUtensorMap& tmC, const CUtensorMap& tmG, cons
                             cudaStream_t stream) {
   const size_t smem = backward_smem_bytes();
   const unsigned grid = (unsigned)((p.B + EPW - 1) / EPW);
-  backward_kernel<<<grid, WARP, smem, stream>>>(tmC, tmG, p);
+  const int tier = pick_tier(grid);
+  if (tier == TIER_HI) backward_kernel<TIER_HI><<<grid, WARP, smem, stream>>>(tmC, tmG, p);
+  else if (tier == TIER_MID) backward_kernel<TIER_MID><<<grid, WARP, smem, stream>>>(tmC, tmG, p);
+  else backward_kernel<TIER_LO><<<grid, WARP, smem, stream>>>(tmC, tmG, p);
   return cudaGetLastError();
 }
 

@@ -169,8 +169,8 @@ __device__ __forceinline__ float pick(const float (&v)[NT], int i) {
 
 __device__ __forceinline__ float4 f4(const float (&v)[NU]) { return make_float4(v[0], v[1], v[2], v[3]); }
 
-template <int NAC, bool HAS_REF>
-__global__ void __launch_bounds__(32, 19) solve_kernel(const __grid_constant__ CUtensorMap tmC,
+template <int NAC, bool HAS_REF, int MINB>
+__global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__ CUtensorMap tmC,
                                                        const SolveParams p) {
   static_assert(NAC == TEAM, "one step size per team lane");
   static_assert(NAC <= SOLVE_SLOTS - 1, "a slot per candidate of the first chunk");
@@ -613,10 +613,15 @@ cudaError_t launch_solve(const CUtensorMap& tmC, const SolveParams& p, cudaStrea
   const size_t smem = solve_smem_bytes();
   const unsigned grid = (unsigned)((p.B + EPW - 1) / EPW);
   const bool ref = p.x_ref != nullptr || p.u_ref != nullptr;
+  const int tier = pick_tier(grid);
   if (ref) {
-    solve_kernel<TEAM, true><<<grid, WARP, smem, stream>>>(tmC, p);
+    if (tier == TIER_HI) solve_kernel<TEAM, true, TIER_HI><<<grid, WARP, smem, stream>>>(tmC, p);
+    else if (tier == TIER_MID) solve_kernel<TEAM, true, TIER_MID><<<grid, WARP, smem, stream>>>(tmC, p);
+    else solve_kernel<TEAM, true, TIER_LO><<<grid, WARP, smem, stream>>>(tmC, p);
   } else {
-    solve_kernel<TEAM, false><<<grid, WARP, smem, stream>>>(tmC, p);
+    if (tier == TIER_HI) solve_kernel<TEAM, false, TIER_HI><<<grid, WARP, smem, stream>>>(tmC, p);
+    else if (tier == TIER_MID) solve_kernel<TEAM, false, TIER_MID><<<grid, WARP, smem, stream>>>(tmC, p);
+    else solve_kernel<TEAM, false, TIER_LO><<<grid, WARP, smem, stream>>>(tmC, p);
   }
   return cudaGetLastError();
 }

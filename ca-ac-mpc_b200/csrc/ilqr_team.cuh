@@ -34,6 +34,19 @@ constexpr int X_K = 100;      // [10][4]  K transposed: column c of K at X_K + 4
 constexpr int X_QXU = 140;    // [10][4]  Q_xu rows (over v, l_u)
 constexpr uint32_t TSLAB_BYTES = EPW * CBLK * 4u;  // bytes one TMA box delivers
 
+// Register tiers. Each kernel is compiled for three minimum residencies
+// (CTAs of one warp per SM); the launch picks the fattest tier whose
+// residency still fits the whole grid in one wave on 148 SMs. 19 CTAs per SM
+// caps registers at 96 (one scheduler holds five warps of its 16 K
+// registers), 12 at 168, 8 at 255; fewer registers spill.
+constexpr int SMS = 148;
+constexpr int TIER_LO = 19, TIER_MID = 12, TIER_HI = 8;
+inline int pick_tier(int64_t grid) {
+  if (grid <= (int64_t)SMS * TIER_HI) return TIER_HI;
+  if (grid <= (int64_t)SMS * TIER_MID) return TIER_MID;
+  return TIER_LO;
+}
+
 __device__ __forceinline__ int row_a(int m) { return m < 4 ? 3 + m : 0; }
 
 __device__ __forceinline__ int row_b(int m) { return m == 0 ? 1 : (m == 1 ? 2 : 5 + m); }

@@ -21,6 +21,7 @@ import torch
 NX, NU, N = 10, 4, 14
 NOT_RUN = -128
 DEFAULT_ALPHAS = (1.0, 0.8, 0.5, 0.2, 0.1)  # DifferentialMPC/controller.py:211
+HOVER_THRUST = 0.752 * 9.8066  # hover U_init (mlp_mpc_policy_diffmpc.py:249-252)
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libilqr_b200.so")
 
 _lib = None
@@ -325,6 +326,75 @@ def backward_sigmoid(X, U, sigmoid_cost, grad_X, grad_U, spec: Optional[SigmoidC
         _ptr(ws), nbytes, _stream(dev))
     _check(st, "ilqr_b200_backward_sigmoid_f32")
     return out
+
+
+class CapturedSolve:
+    """A fixed-shape solve (and optionally its backward) captured once into a
+    CUDA graph and replayed: the launch sequence a control loop repeats every
+    tick (solve, then backward) costs one graph launch instead of the host work
+    of two entry-point calls. Inputs are copied into static device buffers on
+    the current stream; the returned tensors are static buffers that the next
+    call overwrites. Dense costs (C, c) by default, or the policy's sigmoid
+    output when spec is a SigmoidCostSpec."""
+
+    def __init__(self, B: int, T: int, device=None, u_min=None, u_max=None, dt=0.05, max_iter=10,
+                 reg_eps=1e-6, alphas: Sequence[float] = DEFAULT_ALPHAS, with_backward: bool = True,
+                 need=("x0", "C", "c"), spec: Optional[SigmoidCostSpec] = None):
+        dev = torch.device("cuda") if device is None else torch.device(device)
+        if dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+        _device_ok(dev)
+        self.B, self.T, self.spec = B, T, spec
+        z = lambda *sh: torch.zeros(*sh, device=dev)
+        self.x0, self.U_init = z(B, NX), z(B, T, NU)
+        self.U_init[:, :, 0] = HOVER_THRUST
+        if spec is None:
+            self.C, self.c = z(B, T, N, N), z(B, T, N)
+            eye = torch.eye(N, device=dev)
+            self.C.copy_(eye.expand(B, T, N, N))
+        else:
+            self.sc = torch.full((B, 2 * N * T), 0.5, device=dev)
+        self.gX, self.gU = z(B, T + 1, NX), z(B, T, NU)
+        self.lo = None if u_min is None else u_min.to(dev, torch.float32).contiguous()
+        self.hi = None if u_max is None else u_max.to(dev, torch.float32).contiguous()
+        kw = dict(dt=dt, max_iter=max_iter, reg_eps=reg_eps, alphas=alphas)
+        bwd = dict(dt=dt, reg_eps=reg_eps)
+
+        def run():
+            if spec is None:
+                out = solve(self.x0, self.U_init, self.C, self.c, None, None, None, None, self.lo, self.hi, **kw)
+                g = backward(out["X"], out["U"], self.C, self.gX, self.gU, tight=out["tight"], need=need,
+                             **bwd) if with_backward else {}
+            else:
+                out = solve_sigmoid(self.x0, self.U_init, self.sc, spec, self.lo, self.hi, **kw)
+                g = backward_sigmoid(out["X"], out["U"], self.sc, self.gX, self.gU, spec, tight=out["tight"],
+                                     **bwd) if with_backward else {}
+            return out, g
+
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            run()  # warm-up outside the capture (library load, first-call work)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out, self.grads = run()
+
+    def __call__(self, x0, U_init=None, C=None, c=None, grad_X=None, grad_U=None, sigmoid_cost=None):
+        self.x0.copy_(x0)
+        if U_init is not None:
+            self.U_init.copy_(U_init)
+        if self.spec is None:
+            self.C.copy_(C)
+            self.c.copy_(c)
+        else:
+            self.sc.copy_(sigmoid_cost)
+        if grad_X is not None:
+            self.gX.copy_(grad_X)
+        if grad_U is not None:
+            self.gU.copy_(grad_U)
+        self.graph.replay()
+        return self.out, self.grads
 
 
 def dynamics(x, u, dt):

@@ -362,3 +362,33 @@ def test_fastmpc_sigmoid_cost_autograd():
     ref = nat.backward_sigmoid(out["X"], out["U"], g(d["sigmoid_cost"]), g(d["gX"]), g(d["gU"]), spec,
                                tight=out["tight"], dt=wl.DT, reg_eps=1e-6)
     assert torch.equal(sc.grad, ref["sigmoid_cost"])
+
+
+@pytest.mark.parametrize("sigmoid", [False, True])
+def test_captured_solve_equals_eager_calls(sigmoid):
+    """A solve + backward captured in a CUDA graph and replayed with new inputs
+    gives the eager entry points' results bit for bit."""
+    B, T, iters = 40, 8, 4
+    lo, hi = g(wl.U_MIN), g(wl.U_MAX)
+    spec = nat.SigmoidCostSpec() if sigmoid else None
+    cap = nat.CapturedSolve(B, T, DEV, lo, hi, dt=wl.DT, max_iter=iters, spec=spec)
+    rng = np.random.default_rng(9)
+    for seed in (1, 2):
+        inp = wl.make_inputs(B, T, seed=seed)
+        gX, gU = (g(a) for a in wl.make_backward_seeds(B, T, seed=seed))
+        x0, Ui = g(inp["x0"]), g(inp["U_init"])
+        if sigmoid:
+            sc = g((1 / (1 + np.exp(-rng.normal(0, 1.5, (B, 28 * T))))).astype(np.float32))
+            out, gr = cap(x0, Ui, grad_X=gX, grad_U=gU, sigmoid_cost=sc)
+            ref = nat.solve_sigmoid(x0, Ui, sc, spec, lo, hi, dt=wl.DT, max_iter=iters)
+            rg = nat.backward_sigmoid(ref["X"], ref["U"], sc, gX, gU, spec, tight=ref["tight"], dt=wl.DT)
+        else:
+            C, c = g(inp["C"]), g(inp["c"])
+            out, gr = cap(x0, Ui, C, c, gX, gU)
+            ref = nat.solve(x0, Ui, C, c, None, None, None, None, lo, hi, dt=wl.DT, max_iter=iters)
+            rg = nat.backward(ref["X"], ref["U"], C, gX, gU, tight=ref["tight"], dt=wl.DT)
+        torch.cuda.synchronize()
+        for k in ("X", "U", "tight"):
+            assert torch.equal(out[k], ref[k]), (seed, k)
+        for k in rg:
+            assert torch.equal(gr[k], rg[k]), (seed, k)
