@@ -1,10 +1,11 @@
 // ilqr_device.cuh -- device building blocks of the B200 iLQR solver.
 //
-// Compiled with -fmad=false: a*b+c is never contracted implicitly, so
-// elementwise model arithmetic rounds exactly like the reference's torch
-// elementwise ops, and the linear algebra uses explicit fmaf() with a fixed
-// summation order (deterministic: a recomputed rollout is bit-identical to
-// the candidate it repeats).
+// Compiled with -fmad=false: a*b+c is never contracted implicitly, so the
+// model arithmetic follows the reference's torch elementwise ops term by term
+// (divisions by the mass and the normalisation of the body rates are
+// multiplications by reciprocals, within 1 ulp of a division), and the linear
+// algebra uses explicit fmaf() with a fixed summation order (deterministic: a
+// recomputed rollout is bit-identical to the candidate it repeats).
 #pragma once
 
 #include <cuda.h>
@@ -45,10 +46,11 @@ __device__ __forceinline__ void drone_step(const float (&x)[NX], const float (&u
   xn[0] = x[0] + dt * x[7];
   xn[1] = x[1] + dt * x[8];
   xn[2] = x[2] + dt * x[9];
-  // exp_map(w, dt): torch.norm, F.normalize (eps 1e-12), cos/sin(|w| dt/2)
+  // exp_map(w, dt): torch.norm, F.normalize (eps 1e-12), cos/sin(|w| dt/2);
+  // the three quotients use one correctly rounded reciprocal
   const float wn = sqrtf((wx * wx + wy * wy) + wz * wz);
-  const float den = fmaxf(wn, 1e-12f);
-  const float nx = wx / den, ny = wy / den, nz = wz / den;
+  const float rden = __frcp_rn(fmaxf(wn, 1e-12f));
+  const float nx = wx * rden, ny = wy * rden, nz = wz * rden;
   const float half = wn * (dt * 0.5f);
   float s, co;
   sincosf(half, &s, &co);
@@ -64,10 +66,11 @@ __device__ __forceinline__ void drone_step(const float (&x)[NX], const float (&u
   const float r1 = ((q0 * f1 + c1 * f0) - c2 * f3) + c3 * f2;
   const float r2 = ((q0 * f2 + c2 * f0) + c1 * f3) - c3 * f1;
   const float r3 = ((q0 * f3 - c1 * f2) + c2 * f1) + c3 * f0;
-  // v+ = v + dt (rot/m + g)
-  xn[7] = x[7] + dt * (r1 / MASS + 0.0f);
-  xn[8] = x[8] + dt * (r2 / MASS + 0.0f);
-  xn[9] = x[9] + dt * (r3 / MASS + GZ);
+  // v+ = v + dt (rot/m + g), rot/m as rot * (1/m)
+  constexpr float INV_MASS = 1.0f / MASS;
+  xn[7] = x[7] + dt * (r1 * INV_MASS + 0.0f);
+  xn[8] = x[8] + dt * (r2 * INV_MASS + 0.0f);
+  xn[9] = x[9] + dt * (r3 * INV_MASS + GZ);
 }
 
 // Nonzero entries of the discrete Jacobians A = I + dt J_x, B = dt J_u
@@ -90,11 +93,14 @@ __device__ __forceinline__ Jac drone_jac(const float (&x)[NX], const float (&u)[
   J.h0 = (0.5f * u[1]) * dt;
   J.h1 = (0.5f * u[2]) * dt;
   J.h2 = (0.5f * u[3]) * dt;
+  // The linearisation multiplies by 1/m (within 1 ulp of the reference's
+  // division; the dynamics step itself keeps the division).
+  constexpr float INV_MASS = 1.0f / MASS;
   const float a0 = x[3], a1 = x[4], a2 = x[5], a3 = x[6], fc = u[0];
-  J.g0 = (2.0f * ((a0 * fc) / MASS)) * dt;
-  J.g1 = (2.0f * ((a1 * fc) / MASS)) * dt;
-  J.g2 = (2.0f * ((a2 * fc) / MASS)) * dt;
-  J.g3 = (2.0f * ((a3 * fc) / MASS)) * dt;
+  J.g0 = (2.0f * ((a0 * fc) * INV_MASS)) * dt;
+  J.g1 = (2.0f * ((a1 * fc) * INV_MASS)) * dt;
+  J.g2 = (2.0f * ((a2 * fc) * INV_MASS)) * dt;
+  J.g3 = (2.0f * ((a3 * fc) * INV_MASS)) * dt;
   J.e0 = (0.5f * a0) * dt;
   J.e1 = (0.5f * a1) * dt;
   J.e2 = (0.5f * a2) * dt;
@@ -102,9 +108,9 @@ __device__ __forceinline__ Jac drone_jac(const float (&x)[NX], const float (&u)[
   const float d1 = ((a2 * a0 + a3 * a1) + a0 * a2) + a1 * a3;
   const float d2 = ((-a1 * a0 + -a0 * a1) + a3 * a2) + a2 * a3;
   const float d3 = ((a0 * a0 + -a1 * a1) + -a2 * a2) + a3 * a3;
-  J.bv0 = (d1 / MASS) * dt;
-  J.bv1 = (d2 / MASS) * dt;
-  J.bv2 = (d3 / MASS) * dt;
+  J.bv0 = (d1 * INV_MASS) * dt;
+  J.bv1 = (d2 * INV_MASS) * dt;
+  J.bv2 = (d3 * INV_MASS) * dt;
   return J;
 }
 

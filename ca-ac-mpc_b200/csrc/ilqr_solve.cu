@@ -121,6 +121,15 @@ __device__ __forceinline__ void store_rec_x(float4* r, const float (&x)[NX]) {
   r[2] = make_float4(x[8], x[9], 0.0f, 0.0f);
 }
 
+// torch.clamp semantics: a NaN stays NaN (max.NaN / min.NaN return NaN when
+// either operand is NaN; the bounds are finite).
+__device__ __forceinline__ float clamp_nan(float v, float lo, float hi) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(v), "f"(lo));
+  asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(r), "f"(hi));
+  return r;
+}
+
 // Candidate control of the grid line search (controller.py:480-490):
 // u = U_t + a k_t + a (K_t (x - X_t)), then max(., u_min), min(., u_max).
 // kcol(j) returns column j of K_t (the four gains of state j); each row of
@@ -152,10 +161,7 @@ __device__ __forceinline__ void candidate_u(const float (&x)[NX], const float (&
 #pragma unroll
   for (int a = 0; a < NU; ++a) {
     float v = ub[a] + (al * kt[a] + al * kd[a]);
-    if (lo != nullptr) {
-      v = (v != v) ? v : fmaxf(v, __ldg(lo + a));
-      v = (v != v) ? v : fminf(v, __ldg(hi + a));
-    }
+    if (lo != nullptr) v = clamp_nan(v, __ldg(lo + a), __ldg(hi + a));
     u[a] = v;
   }
 }
@@ -451,13 +457,17 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
           const float4 g0 = d4[0], g1 = d4[1], g2 = d4[2], g3 = d4[3];
           const float dgv[NT] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z,
                                  g1.w, g2.x, g2.y, g2.z, g2.w, g3.x, g3.y};
-          bool nonfinite = false;
 #pragma unroll
-          for (int i = 0; i < NT; ++i) {
-            q = fmaf(tau[i], dgv[i] * tau[i], q);
-            nonfinite |= !isfinite(tau[i]);
+          for (int i = 0; i < NT; ++i) q = fmaf(tau[i], dgv[i] * tau[i], q);
+          // The dense form is NaN when any tau_j is infinite or NaN (an
+          // off-diagonal 0 times it); the diagonal sum is then not finite
+          // either, so only a non-finite q needs the check.
+          if (!isfinite(q)) {
+            bool nonfinite = false;
+#pragma unroll
+            for (int i = 0; i < NT; ++i) nonfinite |= !isfinite(tau[i]);
+            if (nonfinite) q = __int_as_float(0x7fffffff);
           }
-          if (nonfinite) q = __int_as_float(0x7fffffff);  // dense form: 0 * inf or 0 * NaN
         } else {
 #pragma unroll
           for (int i = 0; i < NT; ++i) {
