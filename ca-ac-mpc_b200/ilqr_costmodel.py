@@ -54,6 +54,25 @@ def solve_flops(T: int, n_alpha: int, iters, accepts=None) -> float:
     return float(per.sum())
 
 
+# Dense algorithmic counts of the same algorithm (the reference computes these
+# products with dense matmuls): per element, a Riccati step with
+# quadraticisation 10.3 kFLOP, a line-search candidate step 0.66 kFLOP, the
+# initial rollout and linearisation 1.0 kFLOP per step, the backward
+# 10.8 kFLOP per step (masked Riccati, sweep, grad_C).
+RIC_DENSE, LS_DENSE, INIT_DENSE, BWD_DENSE = 10300, 660, 1000, 10800
+
+
+def solve_flops_dense(T: int, n_alpha: int, iters) -> float:
+    """F = T [I (10.3k + 0.66k n_alpha) + 1.0k] summed over the batch, I the
+    iterations each element ran."""
+    I = np.asarray(iters, dtype=np.float64)
+    return float((T * (I * (RIC_DENSE + LS_DENSE * n_alpha) + INIT_DENSE)).sum())
+
+
+def backward_flops_dense(T: int, B: int) -> float:
+    return float(B) * T * BWD_DENSE
+
+
 def backward_flops(T: int, B: int) -> float:
     return float(B) * T * (RICM + JAC + SWEEP + GRADC)
 
