@@ -392,3 +392,29 @@ def test_captured_solve_equals_eager_calls(sigmoid):
             assert torch.equal(out[k], ref[k]), (seed, k)
         for k in rg:
             assert torch.equal(gr[k], rg[k]), (seed, k)
+
+
+@pytest.mark.parametrize("name", ["inference_b262144_t10", "stress_b65536_t50"])
+def test_full_size_configs(name):
+    """The largest configurations run at full size (many waves of CTAs, 2-3 GB
+    of costs): finite results, the first 16 elements equal to a 16-element
+    solve of the same inputs, and for the stress case a backward that is
+    linear in the upstream gradient."""
+    cfg, inp = wl.config_inputs(name)
+    B, T = cfg["B"], cfg["T"]
+    lo, hi = g(wl.U_MIN), g(wl.U_MAX)
+    t = {k: g(v) for k, v in inp.items()}
+    kw = dict(dt=wl.DT, max_iter=cfg["max_iter"], alphas=cfg["alphas"])
+    a = nat.solve(t["x0"], t["U_init"], t["C"], t["c"], None, None, None, None, lo, hi, **kw)
+    assert torch.isfinite(a["X"]).all() and torch.isfinite(a["U"]).all()
+    s = nat.solve(*(t[k][:16].contiguous() for k in ("x0", "U_init", "C", "c")), None, None, None, None,
+                  lo, hi, **kw)
+    assert torch.equal(a["X"][:16], s["X"]) and torch.equal(a["U"][:16], s["U"])
+    if cfg["backward"]:
+        gX, gU = wl.make_backward_seeds(B, T)
+        g1 = nat.backward(a["X"], a["U"], t["C"], g(gX), g(gU), tight=a["tight"], dt=wl.DT, need=("x0", "c"))
+        g2 = nat.backward(a["X"], a["U"], t["C"], g(2 * gX), g(2 * gU), tight=a["tight"], dt=wl.DT,
+                          need=("x0", "c"))
+        for k in g1:
+            assert torch.isfinite(g1[k]).all()
+            assert torch.equal(2 * g1[k], g2[k]), k
