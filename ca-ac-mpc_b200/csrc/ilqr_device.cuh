@@ -276,6 +276,21 @@ static __device__ __noinline__ void svd_inverse4(const float* M, float* Mi) {
 }
 
 // --------------------------------------------------------------------------
+// cp.async: 16-byte global -> shared copies that complete in the background
+// --------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+               "l"(gmem_src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// --------------------------------------------------------------------------
 // TMA bulk tensor copies and mbarriers
 // --------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

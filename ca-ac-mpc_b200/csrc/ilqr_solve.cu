@@ -41,6 +41,14 @@ namespace {
 
 __device__ __forceinline__ float ldg_or0(const float* p, bool ok) { return ok ? __ldg(p) : 0.0f; }
 
+// Line-search staging (the 12-CTA register tier, which has the shared
+// memory): per element and step one 368-byte record, copied with
+// cp.async one step ahead into one of two buffers: nominal (x, u) at [0, 16),
+// k at [16, 20), the ten K columns at [20, 60), the cost record at [60, 92).
+constexpr int STG_F = 92;
+constexpr int STG_CHUNKS = STG_F / 4;   // 23 copies of 16 bytes
+constexpr int STG_OFF = 16;             // bytes between the mbarrier and the first buffer
+
 // Terminal cost 1/2 tauN^T C_f tauN + c_f^T tauN with tauN = [x_T - xref_T; 0].
 __device__ __forceinline__ float terminal_cost(const float* __restrict__ Cf, const float* __restrict__ cf,
                                                const float (&tn)[NX]) {
@@ -179,6 +187,9 @@ template <int NAC, bool HAS_REF, int MINB>
 __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__ CUtensorMap tmC,
                                                        const SolveParams p) {
   static_assert(NAC == TEAM, "one step size per team lane");
+  // staging pays at the 12-CTA tier (B=8192: -9 %); at 8 CTAs per SM the
+  // loads are short already and the copies cost more than they hide
+  constexpr bool STAGE = MINB == TIER_MID;
   static_assert(NAC <= SOLVE_SLOTS - 1, "a slot per candidate of the first chunk");
   extern __shared__ __align__(128) unsigned char smem[];
   float* slab = reinterpret_cast<float*>(smem);
@@ -221,6 +232,8 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
   auto uref = [&](int t, int a) { return (HAS_REF && urb != nullptr) ? ldg_or0(urb + t * NU + a, valid) : 0.0f; };
   const float* Cf = (p.C_f != nullptr && valid) ? p.C_f + b * CBLK : nullptr;
   const float* cf = (p.c_f != nullptr && valid) ? p.c_f + b * NT : nullptr;
+  // staging buffers of this element (STAGE only): buffer s at stg + s * EPW * STG_F
+  float* stg = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(bar) + STG_OFF) + e * STG_F;
 
   auto load_x0 = [&](float (&x)[NX]) {
 #pragma unroll
@@ -249,6 +262,23 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
   __syncwarp();
 
   int nom = 0;  // slot of the nominal trajectory (the same in every lane of a team)
+  auto stage_ls = [&](int t, int buf) {  // issue the copies of step t's record (the owner lanes of a team)
+    if (!dup) {
+      float* d = stg + buf * EPW * STG_F;
+#pragma unroll
+      for (int i = 0; i < 5; ++i) {
+        const int q = m + TEAM * i;
+        if (q < STG_CHUNKS) {
+          const void* src = q < 4    ? (const void*)(W.rec(nom, t) + q)
+                            : q == 4 ? (const void*)W.kff(t)
+                            : q < 15 ? (const void*)W.kcol(t, q - 5)
+                                     : (const void*)(W.diag(t) + 4 * (q - 15));
+          cp_async16(d + 4 * q, src);
+        }
+      }
+    }
+    cp_async_commit();
+  };
   uint32_t status = 0;
   bool active = valid;
   int iters = 0;
@@ -429,12 +459,28 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
       load_x0(x);
       auto ls_body = [&](int t, auto&& next) {
         float xb[NX], ub[NU], kt[NU], u[NU];
-        load_rec(W.rec(nom, t), xb, ub);
+        // step t's record: staged one step ahead (STAGE) or read directly
+        const float* sb = stg + (t & 1) * EPW * STG_F;
+        if constexpr (STAGE) {
+          if (t + 1 < T) {
+            stage_ls(t + 1, (t + 1) & 1);
+            cp_async_wait<1>();
+          } else {
+            cp_async_wait<0>();
+          }
+          __syncwarp();
+        }
+        const float4* rec_t = STAGE ? reinterpret_cast<const float4*>(sb) : W.rec(nom, t);
+        const float4* kff_t = STAGE ? reinterpret_cast<const float4*>(sb + 16) : W.kff(t);
+        const float4* kcol_t = STAGE ? reinterpret_cast<const float4*>(sb + 20) : W.kcol(t, 0);
+        const float* cost_t = STAGE ? sb + 60 : W.diag(t);
+        const int64_t kstride = STAGE ? 1 : (int64_t)p.S;  // float4s between K columns
+        load_rec(rec_t, xb, ub);
         {
-          const float4 k4 = *W.kff(t);
+          const float4 k4 = *kff_t;
           kt[0] = k4.x; kt[1] = k4.y; kt[2] = k4.z; kt[3] = k4.w;
         }
-        candidate_u(x, xb, ub, [&](int jj) { return *W.kcol(t, jj); }, kt, al, lo, hi, u);
+        candidate_u(x, xb, ub, [&](int jj) { return kcol_t[jj * kstride]; }, kt, al, lo, hi, u);
         if (keep) store_rec(W.rec(cs, t), x, u);
         float tau[NT];
 #pragma unroll
@@ -443,7 +489,7 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
         for (int a = 0; a < NU; ++a) tau[NX + a] = u[a] - uref(t, a);
         float l;  // c^T tau, c_t from the cost record
         {
-          const float4* c4 = reinterpret_cast<const float4*>(W.cvec(t));
+          const float4* c4 = reinterpret_cast<const float4*>(cost_t + 16);
           const float4 h0 = c4[0], h1 = c4[1], h2 = c4[2], h3 = c4[3];
           const float cv[NT] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z,
                                 h1.w, h2.x, h2.y, h2.z, h2.w, h3.x, h3.y};
@@ -453,7 +499,7 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
         }
         float q = 0.0f;
         if (diag) {
-          const float4* d4 = reinterpret_cast<const float4*>(W.diag(t));
+          const float4* d4 = reinterpret_cast<const float4*>(cost_t);
           const float4 g0 = d4[0], g1 = d4[1], g2 = d4[2], g3 = d4[3];
           const float dgv[NT] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z,
                                  g1.w, g2.x, g2.y, g2.z, g2.w, g3.x, g3.y};
@@ -490,6 +536,7 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
 #pragma unroll
         for (int i = 0; i < NX; ++i) x[i] = xn[i];
       };
+      if constexpr (STAGE) stage_ls(0, 0);
       ok = pipe.run(T, false, !diag, [](int) {}, ls_body);
       if (!ok) break;
       if (keep) store_rec_x(W.rec(cs, T), x);
@@ -617,13 +664,15 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
 
 }  // namespace
 
-size_t solve_smem_bytes() { return (size_t)EPW * CBLK * 4 + (size_t)EPW * XS * 4 + sizeof(uint64_t); }
+size_t solve_smem_bytes(bool stage) {
+  return (size_t)EPW * CBLK * 4 + (size_t)EPW * XS * 4 + (stage ? STG_OFF + 2 * EPW * STG_F * 4 : sizeof(uint64_t));
+}
 
 cudaError_t launch_solve(const CUtensorMap& tmC, const SolveParams& p, cudaStream_t stream) {
-  const size_t smem = solve_smem_bytes();
   const unsigned grid = (unsigned)((p.B + EPW - 1) / EPW);
   const bool ref = p.x_ref != nullptr || p.u_ref != nullptr;
   const int tier = pick_tier(grid);
+  const size_t smem = solve_smem_bytes(tier == TIER_MID);
   if (ref) {
     if (tier == TIER_HI) solve_kernel<TEAM, true, TIER_HI><<<grid, WARP, smem, stream>>>(tmC, p);
     else if (tier == TIER_MID) solve_kernel<TEAM, true, TIER_MID><<<grid, WARP, smem, stream>>>(tmC, p);
