@@ -94,7 +94,7 @@ inline int64_t solve_ws_fields(int T) {
 inline int64_t backward_ws_fields(int T) { return (int64_t)T * (40 + 4); }
 inline int64_t ws_stride(int64_t B) { return (B + 31) / 32 * 32; }
 
-size_t solve_smem_bytes(bool stage);
+size_t solve_smem_bytes(int tier);
 size_t backward_smem_bytes();
 cudaError_t launch_solve(const CUtensorMap& tmC, const SolveParams& p, cudaStream_t stream);
 cudaError_t launch_backward(const CUtensorMap& tmC, const CUtensorMap& tmG, const BackwardParams& p,

@@ -187,9 +187,15 @@ template <int NAC, bool HAS_REF, int MINB>
 __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__ CUtensorMap tmC,
                                                        const SolveParams p) {
   static_assert(NAC == TEAM, "one step size per team lane");
-  // staging pays at the 12-CTA tier (B=8192: -9 %); at 8 CTAs per SM the
-  // loads are short already and the copies cost more than they hide
-  constexpr bool STAGE = MINB == TIER_MID;
+  // Staging pays at the 12-CTA tier (B=8192: -9 %), which stages the whole
+  // record; the 19-CTA tier has shared memory for the K columns only. At 8
+  // CTAs per SM the loads are short already and the copies cost more than
+  // they hide.
+  constexpr bool STAGE = MINB != TIER_HI;
+  constexpr bool FULL_REC = MINB == TIER_MID;
+  constexpr int SF = FULL_REC ? STG_F : 40;       // floats per element and buffer
+  constexpr int Q0 = FULL_REC ? 0 : 5;            // first chunk of the record staged
+  constexpr int NQ = FULL_REC ? STG_CHUNKS : 10;  // chunks staged
   static_assert(NAC <= SOLVE_SLOTS - 1, "a slot per candidate of the first chunk");
   extern __shared__ __align__(128) unsigned char smem[];
   float* slab = reinterpret_cast<float*>(smem);
@@ -233,7 +239,7 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
   const float* Cf = (p.C_f != nullptr && valid) ? p.C_f + b * CBLK : nullptr;
   const float* cf = (p.c_f != nullptr && valid) ? p.c_f + b * NT : nullptr;
   // staging buffers of this element (STAGE only): buffer s at stg + s * EPW * STG_F
-  float* stg = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(bar) + STG_OFF) + e * STG_F;
+  float* stg = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(bar) + STG_OFF) + e * SF;
 
   auto load_x0 = [&](float (&x)[NX]) {
 #pragma unroll
@@ -264,16 +270,16 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
   int nom = 0;  // slot of the nominal trajectory (the same in every lane of a team)
   auto stage_ls = [&](int t, int buf) {  // issue the copies of step t's record (the owner lanes of a team)
     if (!dup) {
-      float* d = stg + buf * EPW * STG_F;
+      float* d = stg + buf * EPW * SF;
 #pragma unroll
-      for (int i = 0; i < 5; ++i) {
-        const int q = m + TEAM * i;
-        if (q < STG_CHUNKS) {
+      for (int i = 0; i < (NQ + TEAM - 1) / TEAM; ++i) {
+        const int q = Q0 + m + TEAM * i;
+        if (q < Q0 + NQ) {
           const void* src = q < 4    ? (const void*)(W.rec(nom, t) + q)
                             : q == 4 ? (const void*)W.kff(t)
                             : q < 15 ? (const void*)W.kcol(t, q - 5)
                                      : (const void*)(W.diag(t) + 4 * (q - 15));
-          cp_async16(d + 4 * q, src);
+          cp_async16(d + 4 * (q - Q0), src);
         }
       }
     }
@@ -460,7 +466,7 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
       auto ls_body = [&](int t, auto&& next) {
         float xb[NX], ub[NU], kt[NU], u[NU];
         // step t's record: staged one step ahead (STAGE) or read directly
-        const float* sb = stg + (t & 1) * EPW * STG_F;
+        const float* sb = stg + (t & 1) * EPW * SF;  // staged chunks Q0.. of step t's record
         if constexpr (STAGE) {
           if (t + 1 < T) {
             stage_ls(t + 1, (t + 1) & 1);
@@ -470,10 +476,10 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
           }
           __syncwarp();
         }
-        const float4* rec_t = STAGE ? reinterpret_cast<const float4*>(sb) : W.rec(nom, t);
-        const float4* kff_t = STAGE ? reinterpret_cast<const float4*>(sb + 16) : W.kff(t);
-        const float4* kcol_t = STAGE ? reinterpret_cast<const float4*>(sb + 20) : W.kcol(t, 0);
-        const float* cost_t = STAGE ? sb + 60 : W.diag(t);
+        const float4* rec_t = FULL_REC ? reinterpret_cast<const float4*>(sb) : W.rec(nom, t);
+        const float4* kff_t = FULL_REC ? reinterpret_cast<const float4*>(sb + 16) : W.kff(t);
+        const float4* kcol_t = STAGE ? reinterpret_cast<const float4*>(sb + 20 - 4 * Q0) : W.kcol(t, 0);
+        const float* cost_t = FULL_REC ? sb + 60 : W.diag(t);
         const int64_t kstride = STAGE ? 1 : (int64_t)p.S;  // float4s between K columns
         load_rec(rec_t, xb, ub);
         {
@@ -664,15 +670,18 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
 
 }  // namespace
 
-size_t solve_smem_bytes(bool stage) {
-  return (size_t)EPW * CBLK * 4 + (size_t)EPW * XS * 4 + (stage ? STG_OFF + 2 * EPW * STG_F * 4 : sizeof(uint64_t));
+size_t solve_smem_bytes(int tier) {
+  const size_t base = (size_t)EPW * CBLK * 4 + (size_t)EPW * XS * 4;
+  if (tier == TIER_MID) return base + STG_OFF + 2 * EPW * STG_F * 4;
+  if (tier == TIER_LO) return base + STG_OFF + 2 * EPW * 40 * 4;
+  return base + sizeof(uint64_t);
 }
 
 cudaError_t launch_solve(const CUtensorMap& tmC, const SolveParams& p, cudaStream_t stream) {
   const unsigned grid = (unsigned)((p.B + EPW - 1) / EPW);
   const bool ref = p.x_ref != nullptr || p.u_ref != nullptr;
   const int tier = pick_tier(grid);
-  const size_t smem = solve_smem_bytes(tier == TIER_MID);
+  const size_t smem = solve_smem_bytes(tier);
   if (ref) {
     if (tier == TIER_HI) solve_kernel<TEAM, true, TIER_HI><<<grid, WARP, smem, stream>>>(tmC, p);
     else if (tier == TIER_MID) solve_kernel<TEAM, true, TIER_MID><<<grid, WARP, smem, stream>>>(tmC, p);
