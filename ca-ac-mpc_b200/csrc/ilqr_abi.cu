@@ -237,6 +237,14 @@ int ilqr_b200_backward_sigmoid_f32(const float* X, const float* U, const float* 
                        workspace, workspace_bytes, stream);
 }
 
+int ilqr_b200_pnqp4_batch_f32(const float* H, const float* q, const float* lower, const float* upper,
+                              const float* x_init, int64_t n, float* x_out, float* free_mask,
+                              cudaStream_t stream) {
+  if (n < 0) return ILQR_ERR_INVALID_ARGUMENT;
+  if (n > 0 && (!H || !q || !lower || !upper || !x_out || !free_mask)) return ILQR_ERR_INVALID_ARGUMENT;
+  return cuda_status(ilqr::launch_pnqp4_batch(H, q, lower, upper, x_init, n, x_out, free_mask, stream));
+}
+
 int ilqr_b200_dynamics_f32(const float* x, const float* u, int64_t n, float dt, float* x_next,
                            cudaStream_t stream) {
   if (n < 0) return ILQR_ERR_INVALID_ARGUMENT;

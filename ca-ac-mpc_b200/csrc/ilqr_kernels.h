@@ -106,6 +106,8 @@ cudaError_t launch_adjoint_lqr(const float* A, const float* Bm, const float* l_x
                                const float* l_xu, const float* l_x, const float* l_u, const float* l_xxN,
                                const float* l_xN, const uint8_t* tight, int64_t B, int T, float reg, float* K,
                                float* k, float* v0, cudaStream_t s);
+cudaError_t launch_pnqp4_batch(const float* H, const float* q, const float* lower, const float* upper,
+                               const float* x_init, int64_t n, float* x_out, float* free_mask, cudaStream_t stream);
 cudaError_t launch_assembly(const float* K, const float* k, const float* v0, const float* A, const float* Bm,
                             const float* X, const float* U, const float* x_ref, const float* u_ref, int64_t B,
                             int T, float* gC, float* gc, float* gx0, float* gxr, float* gur, float* gCf,

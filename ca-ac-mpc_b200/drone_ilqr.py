@@ -116,6 +116,14 @@ class DroneIlqrExt:
                                            bool(compute_uref), bool(compute_C_final),
                                            bool(compute_c_final))
 
+    # ---- drone_pnqp4_batch (cpp/drone_ilqr_ext.cpp:1285-1316) ----------------
+    def drone_pnqp4_batch(self, H, q, lower, upper, x_init=None):
+        """n independent 4-d box QPs: returns (x* [n,4], free_mask [n,4]).
+        An empty or absent x_init starts from the unconstrained solution."""
+        f = lambda t: t.to(torch.float32).contiguous()
+        xi = None if x_init is None or x_init.numel() == 0 else f(x_init)
+        return _nat.pnqp4_batch(f(H), f(q), f(lower), f(upper), xi)
+
     # ---- CUDA-graph helpers (cpp/drone_ilqr_ext.cpp:1181-1212) ---------------
     def clear_cuda_graph_cache(self):
         self._graph_status = (False, 0, 0)

@@ -61,6 +61,7 @@ def lib():
             "ilqr_b200_backward_sigmoid_f32": ([_P] * 3 + [_F] * 4 + [_P] * 3 + [_I64, _I32, _F, _F] + [_P] * 2
                                                + [_P, ctypes.c_size_t, _P], _I32),
             "ilqr_b200_dynamics_f32": ([_P, _P, _I64, _F, _P, _P], _I32),
+            "ilqr_b200_pnqp4_batch_f32": ([_P] * 5 + [_I64, _P, _P, _P], _I32),
             "ilqr_b200_linearize_f32": ([_P, _P, _I64, _I32, _F, _P, _P, _P], _I32),
             "ilqr_b200_adjoint_lqr_f32": ([_P] * 10 + [_I64, _I32, _F, _P, _P, _P, _P], _I32),
             "ilqr_b200_implicit_diff_assembly_f32": ([_P] * 9 + [_I64, _I32] + [_P] * 7 + [_P], _I32),
@@ -81,7 +82,7 @@ EXPORTED_SYMBOLS = (
     "ilqr_b200_solve_f32", "ilqr_b200_backward_f32", "ilqr_b200_dynamics_f32",
     "ilqr_b200_linearize_f32", "ilqr_b200_adjoint_lqr_f32",
     "ilqr_b200_implicit_diff_assembly_f32", "ilqr_b200_solve_f32_noalloc",
-    "ilqr_b200_solve_sigmoid_f32", "ilqr_b200_backward_sigmoid_f32",
+    "ilqr_b200_solve_sigmoid_f32", "ilqr_b200_backward_sigmoid_f32", "ilqr_b200_pnqp4_batch_f32",
 )
 
 
@@ -395,6 +396,25 @@ class CapturedSolve:
             self.gU.copy_(grad_U)
         self.graph.replay()
         return self.out, self.grads
+
+
+def pnqp4_batch(H, q, lower, upper, x_init=None):
+    """n independent 4-d box QPs by projected Newton (drone_pnqp4_batch):
+    returns (x* [n,4], free_mask [n,4])."""
+    dev = _cuda_device(H, "H")
+    _device_ok(dev)
+    n = H.shape[0]
+    _req(H, "H", (n, 4, 4), dev)
+    for t, nm in ((q, "q"), (lower, "lower"), (upper, "upper")):
+        _req(t, nm, (n, 4), dev)
+    if x_init is not None and x_init.numel() == 0:
+        x_init = None
+    _opt(x_init, "x_init", (n, 4), dev)
+    x = torch.empty(n, 4, device=dev)
+    fm = torch.empty(n, 4, device=dev)
+    _check(lib().ilqr_b200_pnqp4_batch_f32(_ptr(H), _ptr(q), _ptr(lower), _ptr(upper), _ptr(x_init), n,
+                                           _ptr(x), _ptr(fm), _stream(dev)), "ilqr_b200_pnqp4_batch_f32")
+    return x, fm
 
 
 def dynamics(x, u, dt):

@@ -125,6 +125,23 @@ int ilqr_b200_solve_f32_noalloc(
 int ilqr_b200_backward_workspace_size(int64_t B, int32_t T, size_t* bytes);
 
 /*
+ * n independent 4-dimensional box-constrained QPs,
+ *   min 1/2 x^T H x + q^T x  s.t.  lower <= x <= upper,
+ * by projected Newton, one thread per problem: mpc.pytorch's pnqp
+ * (acmpc_public-master/mpc.pytorch/mpc/pnqp.py:5-84) with the reference
+ * extension's per-problem settings (at most 10 Newton steps and 10 Armijo
+ * trials, gamma 0.1, decay 0.1, ridge 1e-11, step tolerance 1e-4, bounds
+ * active within 1e-8). Replaces drone_pnqp4_batch
+ * (differentialMPCPerformance/cpp/drone_ilqr_ext.cpp:1285-1316).
+ * Inputs (device, float32): H [n,4,4], q, lower, upper [n,4], x_init [n,4] or
+ * NULL (a zero row starts from the unconstrained solution).
+ * Outputs: x_out [n,4], free_mask [n,4] (1 free, 0 held at a bound).
+ */
+int ilqr_b200_pnqp4_batch_f32(
+    const float* H, const float* q, const float* lower, const float* upper,
+    const float* x_init, int64_t n, float* x_out, float* free_mask, cudaStream_t stream);
+
+/*
  * Fused implicit-differentiation backward at a solved (X, U): masked adjoint
  * Riccati, dX/dU sweep and gradient assembly in one kernel, with A_t, B_t
  * recomputed from (X_t, U_t) instead of read from memory.

@@ -665,10 +665,88 @@ def sigmoid_cost_grad(grad_C, grad_c, T, range_q=100000.0, range_p=100000.0, ran
     return g
 
 
+def _solve4_pivot(A, b):
+    """Gaussian elimination with partial pivoting on one 4x4 system (float32),
+    pivots of magnitude below 1e-10 replaced by +-1e-10, as the reference's
+    PNQP step (differentialMPCPerformance/cpp/pnqp_kernel.cuh:15-54)."""
+    f32 = np.float32
+    A = A.astype(f32).copy()
+    b = b.astype(f32).copy()
+    for k in range(4):
+        r = k + int(np.argmax(np.abs(A[k:, k])))
+        if np.abs(A[r, k]) > np.abs(A[k, k]) and r != k:
+            A[[k, r]] = A[[r, k]]
+            b[[k, r]] = b[[r, k]]
+        piv = A[k, k]
+        if abs(piv) < f32(1e-10):
+            piv = f32(-1e-10) if piv < 0 else f32(1e-10)
+        for i in range(k + 1, 4):
+            f = f32(A[i, k] / piv)
+            for j in range(k + 1, 4):
+                A[i, j] = f32(A[i, j] - f32(f * A[k, j]))
+            b[i] = f32(b[i] - f32(f * b[k]))
+            A[i, k] = 0
+    x = np.zeros(4, f32)
+    for i in range(3, -1, -1):
+        s_ = b[i]
+        for j in range(i + 1, 4):
+            s_ = f32(s_ - f32(A[i, j] * x[j]))
+        x[i] = f32(s_ / A[i, i])
+    return x
+
+
+def pnqp4(H, q, lower, upper, x_init=None):
+    """Projected-Newton box QP min 1/2 x^T H x + q^T x, lower <= x <= upper, for
+    [N,4] problems (the reference's PNQP-4, pnqp_kernel.cuh:91-208, with
+    mpc.pytorch.pnqp's constants: ridge 1e-11, Armijo gamma 0.1, decay 0.1,
+    step tolerance 1e-4; per problem: at most 10 Newton steps, 10 Armijo
+    trials, a bound counts as active within 1e-8). A zero x_init starts from the
+    unconstrained solution. Returns (x*, free_mask) in float32."""
+    f32 = np.float32
+    H = np.asarray(H, f32)
+    q = np.asarray(q, f32)
+    lo = np.asarray(lower, f32)
+    hi = np.asarray(upper, f32)
+    n = H.shape[0]
+    X = np.zeros((n, 4), f32)
+    F = np.zeros((n, 4), f32)
+    eps = f32(1e-8)
+    obj = lambda h, qq, x: f32(f32(0.5) * f32(x @ (h @ x))) + f32(qq @ x)
+    for b in range(n):
+        x = np.zeros(4, f32) if x_init is None else np.asarray(x_init[b], f32).copy()
+        if not np.any(x != 0):
+            x = _solve4_pivot(H[b], -q[b])
+        x = np.minimum(np.maximum(x, lo[b]), hi[b])
+        for _ in range(10):
+            g = (H[b] @ x + q[b]).astype(f32)
+            clamped = ((x <= lo[b] + eps) & (g > 0)) | ((x >= hi[b] - eps) & (g < 0))
+            fr = (~clamped).astype(f32)
+            Hm = (H[b] * fr[:, None] * fr[None, :]).astype(f32) + np.eye(4, dtype=f32) * f32(1e-11)
+            dx = _solve4_pivot(Hm, -g * fr)
+            if float(dx @ dx) < 1e-8:
+                break
+            ox = obj(H[b], q[b], x)
+            alpha = f32(1.0)
+            for _ls in range(10):
+                mx = np.minimum(np.maximum(x + alpha * dx, lo[b]), hi[b]).astype(f32)
+                om = obj(H[b], q[b], mx)
+                den = f32(g @ (x - mx))
+                arm = (ox - om) / (den if abs(den) > 1e-12 else f32(1e-12))
+                if arm > 0.1:
+                    break
+                alpha = f32(alpha * f32(0.1))
+            x = mx
+        g = (H[b] @ x + q[b]).astype(f32)
+        clamped = ((x <= lo[b] + eps) & (g > 0)) | ((x >= hi[b] - eps) & (g < 0))
+        X[b] = x
+        F[b] = (~clamped).astype(f32)
+    return X, F
+
+
 __all__ = [
     "NX", "NU", "N", "MASS", "GRAV_Z", "NOT_RUN", "DEFAULT_ALPHAS",
     "drone_step", "drone_jacobian", "rollout", "linearize", "objective",
     "quadraticize", "chol4", "chol_solve", "riccati", "line_search",
     "argmin_nan_first", "tight_mask", "solve", "global_converged_flag",
-    "zero_constrained_lqr", "backward", "sigmoid_costs", "sigmoid_cost_grad",
+    "zero_constrained_lqr", "backward", "sigmoid_costs", "sigmoid_cost_grad", "pnqp4",
 ]

@@ -2,6 +2,8 @@
 golden vectors and the CPU oracle. Bars: 1e-4 on X, U and 1e-3 on gradients
 (per-element norm-wise relative error, tests/parity.py)."""
 
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -11,7 +13,7 @@ import ilqr_native as nat
 import ilqr_workload as wl
 import mpc_compat
 import oracle as O
-from parity import (GRAD_KEYS, STRICT_CASES, TOL_GRAD, TOL_XU, case_kwargs, certify_ties, load,
+from parity import (GOLDEN_DIR, GRAD_KEYS, STRICT_CASES, TOL_GRAD, TOL_XU, case_kwargs, certify_ties, load,
                     max_rel, same_decisions)
 
 pytestmark = pytest.mark.gpu
@@ -418,3 +420,23 @@ def test_full_size_configs(name):
         for k in g1:
             assert torch.isfinite(g1[k]).all()
             assert torch.equal(2 * g1[k], g2[k]), k
+
+
+def test_pnqp4_batch_matches_oracle_and_optimum():
+    """drone_pnqp4_batch on the GPU: the same iterates as the oracle's
+    restatement (to fp32 rounding) and the exact box-QP optimum on all but a
+    few hard problems; a warm start at the optimum stays there."""
+    d = np.load(os.path.join(GOLDEN_DIR, "pnqp4_n256.npz"))
+    ext = drone_ilqr.load_drone_ilqr_ext()
+    H, q, lo, hi = (g(d[k]) for k in ("H", "q", "lower", "upper"))
+    x, free = ext.drone_pnqp4_batch(H, q, lo, hi, None)
+    x, free = x.cpu().numpy(), free.cpu().numpy()
+    ox, ofree = O.pnqp4(d["H"], d["q"], d["lower"], d["upper"])
+    scale = np.maximum(1.0, np.abs(ox).max(axis=1, keepdims=True))
+    close = (np.abs(x - ox) / scale).max(axis=1) <= 1e-4
+    assert close.sum() >= 250 and (free[close] == ofree[close]).all()
+    at_opt = (np.abs(x - d["opt_x"]) / np.maximum(1.0, np.abs(d["opt_x"]).max(1, keepdims=True))).max(1) <= 1e-4
+    assert at_opt.sum() >= 250
+    assert (x >= d["lower"]).all() and (x <= d["upper"]).all()
+    xw, fw = ext.drone_pnqp4_batch(H, q, lo, hi, g(d["opt_x"].astype(np.float32)))
+    assert (np.abs(xw.cpu().numpy() - d["opt_x"]).max(1) <= 1e-4 * np.maximum(1.0, np.abs(d["opt_x"]).max(1))).sum() >= 250

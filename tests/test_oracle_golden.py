@@ -1,11 +1,13 @@
 """Pin the CPU oracle to the reference DiffMPC (golden vectors made by running
 the reference itself, tests/golden/make_golden.py). CPU only."""
 
+import os
+
 import numpy as np
 import pytest
 
 import oracle as O
-from parity import (GRAD_KEYS, STRICT_CASES, TOL_GRAD, TOL_XU, case_kwargs, certify_ties, load,
+from parity import (GOLDEN_DIR, GRAD_KEYS, STRICT_CASES, TOL_GRAD, TOL_XU, case_kwargs, certify_ties, load,
                     max_rel, same_decisions)
 
 
@@ -134,3 +136,20 @@ def test_sigmoid_cost_gradient_matches_reference():
                              float(d["range_pt"]))
     assert max_rel(gs, d["ref_grad_sigmoid_cost"]) <= TOL_GRAD
     assert max_rel(g["grad_x0"], d["ref_grad_x0"]) <= TOL_GRAD
+
+
+def test_pnqp4_reaches_the_optimum():
+    """The box-QP restatement (projected Newton, at most 10 steps, as the
+    reference's PNQP-4) reaches the exact optimum (enumerated active sets, H
+    positive definite) on all but a few problems, and agrees with the
+    reference specification, mpc.pytorch's pnqp, wherever that one reached it."""
+    d = np.load(os.path.join(GOLDEN_DIR, "pnqp4_n256.npz"))
+    x, free = O.pnqp4(d["H"], d["q"], d["lower"], d["upper"])
+    scale = np.maximum(1.0, np.abs(d["opt_x"]).max(axis=1, keepdims=True))
+    at_opt = (np.abs(x - d["opt_x"]) / scale).max(axis=1) <= 1e-4
+    assert at_opt.sum() >= 250, int(at_opt.sum())
+    assert (x >= d["lower"]).all() and (x <= d["upper"]).all()
+    ref_at_opt = np.abs(d["ref_x"] - d["opt_x"]).max(axis=1) <= 1e-6
+    both = at_opt & ref_at_opt
+    assert both.sum() >= 240
+    assert np.array_equal(free[both], d["ref_free"][both])
