@@ -1,0 +1,917 @@
+// ilqr_dense.cu -- fused iLQR solve and implicit-diff backward for the
+// 13-state rotor-thrust quadrotor (ilqr_rotor13.cuh).
+//
+// The same algorithm as ilqr_solve.cu / ilqr_backward.cu (DiffMPC semantics:
+// DifferentialMPC/controller.py:303-533 solve loop, Riccati and grid line
+// search, :997-1003 tight mask, :68-133 and :1006-1131 implicit-diff backward),
+// for a model whose Jacobians are dense enough that a row-per-lane layout
+// pays: one batch element per group of 16 lanes, two elements per warp.
+//
+// Riccati step (lanes 0..12 own the state rows i, lanes 0..3 also the control
+// rows, all 16 lanes the 4 x 4 Q_uu entries), matrices in shared memory:
+//   J   lane i writes row i of A_t, B_t (from the nominal x_t, u_t)
+//   P1  (V B)_i., (A^T V)_i. = sum_k A_ki V_k., q_x,i ; q_u (lanes 0..3)
+//   P2  Q_xx,i. = C_xx,i. + (A^T V)_i. A ; Q_xu,i. = C_xu,i. + A_.i^T (V B)
+//       Q_uu,ab = C_uu,ab + B_.a^T (V B)_.b + reg [a = b]   (one entry per lane)
+//   P3  K_.i = -(Q_uu + reg I)^-1 Q_xu,i.^T by a Cholesky every lane repeats
+//       (SVD inverse when it fails); k by lane 13; M = Q_uu K + Q_ux
+//   P4  V_i. = Q_xx,i. + K_.i^T M + Q_xu,i. K ; v_i likewise
+// with a warp barrier after each. The line search runs one step size per lane
+// (lane j rolls out candidate j over the horizon), so the n_alpha candidates
+// of an element run side by side; each candidate trajectory is kept in its
+// own workspace slot and the accepted one becomes the nominal.
+#include <cstdint>
+
+#include "ilqr_b200.h"
+#include "ilqr_device.cuh"
+#include "ilqr_kernels.h"
+#include "ilqr_rotor13.cuh"
+
+namespace ilqr {
+namespace r13 {
+
+namespace {
+
+constexpr int GL = 16;             // lanes per element
+constexpr int EPW = 2;             // elements per warp
+constexpr int WPC = 4;             // warps per CTA
+constexpr int EPC = EPW * WPC;     // elements per CTA
+constexpr int THREADS = WPC * 32;  // threads per CTA
+constexpr int REC = 20;            // floats per trajectory record: x[13], u[4], 3 pad
+
+// Shared memory of one element (floats). The block size is an odd multiple
+// of 16 floats, so the two elements of a warp use opposite halves of the
+// banks for the same offsets.
+constexpr int S_V = 0;       // V [13][13]
+constexpr int S_A = 172;     // A_t [13][13]
+constexpr int S_B = 344;     // B_t [13][4]
+constexpr int S_VB = 396;    // V B [13][4]
+constexpr int S_K = 448;     // K_t [4][13]
+constexpr int S_M = 500;     // Q_uu K + Q_ux [4][13]
+constexpr int S_VV = 552;    // v [13]
+constexpr int S_Z = 568;     // nominal x_t, u_t [20]
+constexpr int S_QUU = 588;   // Q_uu [4][4] (regularised once)
+constexpr int S_QU = 604;    // q_u [4]
+constexpr int S_KF = 608;    // k_t [4]
+constexpr int S_MK = 612;    // Q_uu k + q_u [4]
+constexpr int S_SVD = 616;   // SVD fallback: matrix [16], inverse [16]
+constexpr int S_ELEM = 656;  // floats per element (41 x 16)
+
+__device__ __forceinline__ float clampn(float v, float lo, float hi) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(v), "f"(lo));
+  asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(r), "f"(hi));
+  return r;
+}
+
+__device__ __forceinline__ float group_sum(float v, unsigned mask) {
+#pragma unroll
+  for (int o = GL / 2; o > 0; o >>= 1) v += __shfl_xor_sync(mask, v, o);
+  return v;
+}
+
+// Workspace of one element (floats, element-major):
+//   slots  [n_slot][T+1][REC]   trajectory records
+//   K cols [T][13] float4        column j of K_t (the four gains of state j)
+//   k      [T] float4
+struct Ws {
+  float* base;
+  int T;
+  int n_slot;
+  __device__ float4* rec(int slot, int t) const {
+    return reinterpret_cast<float4*>(base + ((int64_t)slot * (T + 1) + t) * REC);
+  }
+  __device__ float4* kcol(int t, int j) const {
+    return reinterpret_cast<float4*>(base + (int64_t)n_slot * (T + 1) * REC) + (int64_t)t * (NX + 1) + j;
+  }
+  __device__ float4* kff(int t) const { return kcol(t, NX); }
+};
+
+__device__ __forceinline__ void load_rec(const float4* r, float* x, float* u) {
+  const float4 a = r[0], b = r[1], c = r[2], d = r[3], e = r[4];
+  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+  x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+  x[8] = c.x; x[9] = c.y; x[10] = c.z; x[11] = c.w;
+  x[12] = d.x; u[0] = d.y; u[1] = d.z; u[2] = d.w;
+  u[3] = e.x;
+}
+
+__device__ __forceinline__ void store_rec(float4* r, const float* x, const float* u) {
+  r[0] = make_float4(x[0], x[1], x[2], x[3]);
+  r[1] = make_float4(x[4], x[5], x[6], x[7]);
+  r[2] = make_float4(x[8], x[9], x[10], x[11]);
+  r[3] = make_float4(x[12], u[0], u[1], u[2]);
+  r[4] = make_float4(u[3], 0.0f, 0.0f, 0.0f);
+}
+
+// 1/2 tau^T C tau and c^T tau of one step, accumulated over rows in index
+// order (the costs the line search compares and the initial objective).
+__device__ __forceinline__ void step_cost(const float* __restrict__ Ct, const float* __restrict__ ct,
+                                          const float* tau, float& q, float& l) {
+  l = __ldg(ct) * tau[0];
+#pragma unroll
+  for (int j = 1; j < NT; ++j) l = fmaf(__ldg(ct + j), tau[j], l);
+  q = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NT; ++i) {
+    const float* row = Ct + i * NT;
+    float r = __ldg(row) * tau[0];
+#pragma unroll
+    for (int j = 1; j < NT; ++j) r = fmaf(__ldg(row + j), tau[j], r);
+    q = fmaf(tau[i], r, q);
+  }
+}
+
+// Terminal cost 1/2 tN^T C_f tN + c_f^T tN, tN = [x_T - x_ref_T; 0].
+__device__ __forceinline__ float terminal_cost(const float* __restrict__ Cf, const float* __restrict__ cf,
+                                               const float* tn) {
+  if (Cf == nullptr) return 0.0f;
+  float q = 0.0f, l = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NX; ++i) {
+    const float* row = Cf + i * NT;
+    float r = __ldg(row) * tn[0];
+#pragma unroll
+    for (int j = 1; j < NX; ++j) r = fmaf(__ldg(row + j), tn[j], r);
+    q = fmaf(tn[i], r, q);
+    if (cf != nullptr) l = fmaf(__ldg(cf + i), tn[i], l);
+  }
+  return 0.5f * q + l;
+}
+
+// Inputs of one Riccati step that differ between the solve and the backward.
+struct StepIn {
+  float lx;       // l_x,i (state-row lanes)
+  float lu;       // l_u,a for a = lane (lanes 0..3)
+  float cxx[NX];  // C_xx,i.
+  float cxu[NU];  // C_xu,i.
+  float cuu;      // C_uu,ab for (a, b) = (lane / 4, lane % 4)
+};
+
+// One step of the Riccati recursion for the element of this lane's group.
+// MASKED selects the implicit-diff form (_zero_constrained_lqr,
+// controller.py:1070-1110): tight rows/columns of Q_uu replaced by the
+// identity plus a (1e-8 reg) I ridge for the gain solve, tight rows of Q_ux
+// and entries of q_u zeroed; otherwise the forward form (backward_lqr,
+// controller.py:697-723) solves with Q_uu + reg I (reg a second time).
+// V and v are updated with the unmasked Q_uu (once regularised), Q_ux, q_u.
+// Returns true if the Cholesky failed and the SVD inverse was used.
+template <bool MASKED>
+__device__ __forceinline__ bool riccati_step(float* sm, int g, bool rowx, bool live, unsigned wmask, const StepIn& in,
+                                             float reg, const bool* tight, float (&Vr)[NX], float& vi, float (&Kc)[NU],
+                                             float (&kf)[NU]) {
+  // ---- P1 ---------------------------------------------------------------
+  float acol[NX];
+#pragma unroll
+  for (int k = 0; k < NX; ++k) acol[k] = rowx ? sm[S_A + k * NX + g] : 0.0f;
+  float w[NX];
+  float qx = 0.0f;
+  if (rowx) {
+    float vb[NU];
+#pragma unroll
+    for (int a = 0; a < NU; ++a) {
+      float s = Vr[0] * sm[S_B + a];
+#pragma unroll
+      for (int k = 1; k < NX; ++k) s = fmaf(Vr[k], sm[S_B + k * NU + a], s);
+      vb[a] = s;
+    }
+#pragma unroll
+    for (int a = 0; a < NU; ++a) sm[S_VB + g * NU + a] = vb[a];
+#pragma unroll
+    for (int j = 0; j < NX; ++j) {
+      float s = acol[0] * sm[S_V + j];
+#pragma unroll
+      for (int k = 1; k < NX; ++k) s = fmaf(acol[k], sm[S_V + k * NX + j], s);
+      w[j] = s;
+    }
+    float s = acol[0] * sm[S_VV];
+#pragma unroll
+    for (int k = 1; k < NX; ++k) s = fmaf(acol[k], sm[S_VV + k], s);
+    qx = in.lx + s;
+  }
+  if (g < NU) {
+    float s = sm[S_B + g] * sm[S_VV];
+#pragma unroll
+    for (int k = 1; k < NX; ++k) s = fmaf(sm[S_B + k * NU + g], sm[S_VV + k], s);
+    sm[S_QU + g] = in.lu + s;
+  }
+  __syncwarp(wmask);
+  // ---- P2 ---------------------------------------------------------------
+  float qxx[NX], qxu[NU];
+  if (rowx) {
+#pragma unroll
+    for (int j = 0; j < NX; ++j) {
+      float s = w[0] * sm[S_A + j];
+#pragma unroll
+      for (int k = 1; k < NX; ++k) s = fmaf(w[k], sm[S_A + k * NX + j], s);
+      qxx[j] = in.cxx[j] + s;
+    }
+#pragma unroll
+    for (int a = 0; a < NU; ++a) {
+      float s = acol[0] * sm[S_VB + a];
+#pragma unroll
+      for (int k = 1; k < NX; ++k) s = fmaf(acol[k], sm[S_VB + k * NU + a], s);
+      qxu[a] = in.cxu[a] + s;
+    }
+  }
+  {
+    const int a = g >> 2, b = g & 3;
+    float s = sm[S_B + a] * sm[S_VB + b];
+#pragma unroll
+    for (int k = 1; k < NX; ++k) s = fmaf(sm[S_B + k * NU + a], sm[S_VB + k * NU + b], s);
+    float q = in.cuu + s;
+    if (a == b) q = q + reg;
+    sm[S_QUU + g] = q;
+  }
+  __syncwarp(wmask);
+  // ---- P3: gains ----------------------------------------------------------
+  float Q[NU][NU], qu[NU];
+#pragma unroll
+  for (int a = 0; a < NU; ++a) {
+#pragma unroll
+    for (int b = 0; b < NU; ++b) Q[a][b] = sm[S_QUU + a * NU + b];
+    qu[a] = sm[S_QU + a];
+  }
+  bool msk[NU] = {false, false, false, false};
+  if (MASKED) {
+#pragma unroll
+    for (int a = 0; a < NU; ++a) msk[a] = tight[a];
+  }
+  float G[NU][NU];  // the matrix the gains are solved with
+#pragma unroll
+  for (int a = 0; a < NU; ++a)
+#pragma unroll
+    for (int b = 0; b < NU; ++b) {
+      if (MASKED) {
+        float v = (msk[a] || msk[b]) ? 0.0f : Q[a][b];
+        if (a == b && msk[a]) v = v + 1.0f;
+        if (a == b) v = v + 1e-8f * reg;
+        G[a][b] = v;
+      } else {
+        G[a][b] = (a == b) ? Q[a][b] + reg : Q[a][b];
+      }
+    }
+  float rhs[NU];
+  if (g < NX) {
+#pragma unroll
+    for (int a = 0; a < NU; ++a) rhs[a] = (MASKED && msk[a]) ? 0.0f : qxu[a];
+  } else {
+#pragma unroll
+    for (int a = 0; a < NU; ++a) rhs[a] = (MASKED && msk[a]) ? 0.0f : qu[a];
+  }
+  Chol4 L;
+  const bool ok = chol4(G, L);
+  float sol[NU];
+  chol4_solve(L, rhs, sol);
+  const bool fb = !ok && live;
+  if (__any_sync(wmask, fb)) {
+    float* M = sm + S_SVD;
+    if (fb && g == 0) {
+#pragma unroll
+      for (int a = 0; a < NU; ++a)
+#pragma unroll
+        for (int b = 0; b < NU; ++b) M[a * NU + b] = G[a][b];
+      svd_inverse4(M, M + 16);
+    }
+    __syncwarp(wmask);
+    if (fb) {
+#pragma unroll
+      for (int a = 0; a < NU; ++a) {
+        float s = M[16 + a * NU] * rhs[0];
+#pragma unroll
+        for (int b = 1; b < NU; ++b) s = fmaf(M[16 + a * NU + b], rhs[b], s);
+        sol[a] = s;
+      }
+    }
+    __syncwarp(wmask);
+  }
+#pragma unroll
+  for (int a = 0; a < NU; ++a) sol[a] = -sol[a];
+  if (rowx) {
+#pragma unroll
+    for (int a = 0; a < NU; ++a) {
+      Kc[a] = sol[a];
+      sm[S_K + a * NX + g] = sol[a];
+    }
+#pragma unroll
+    for (int a = 0; a < NU; ++a) {
+      float s = Q[a][0] * sol[0];
+#pragma unroll
+      for (int b = 1; b < NU; ++b) s = fmaf(Q[a][b], sol[b], s);
+      sm[S_M + a * NX + g] = s + qxu[a];
+    }
+  } else if (g == NX) {
+#pragma unroll
+    for (int a = 0; a < NU; ++a) {
+      kf[a] = sol[a];
+      sm[S_KF + a] = sol[a];
+    }
+#pragma unroll
+    for (int a = 0; a < NU; ++a) {
+      float s = Q[a][0] * sol[0];
+#pragma unroll
+      for (int b = 1; b < NU; ++b) s = fmaf(Q[a][b], sol[b], s);
+      sm[S_MK + a] = s + qu[a];
+    }
+  }
+  __syncwarp(wmask);
+  // ---- P4: V, v -----------------------------------------------------------
+  if (rowx) {
+#pragma unroll
+    for (int j = 0; j < NX; ++j) {
+      float s = qxx[j];
+#pragma unroll
+      for (int a = 0; a < NU; ++a) s = fmaf(Kc[a], sm[S_M + a * NX + j], s);
+#pragma unroll
+      for (int a = 0; a < NU; ++a) s = fmaf(qxu[a], sm[S_K + a * NX + j], s);
+      Vr[j] = s;
+    }
+    float s = qx;
+#pragma unroll
+    for (int a = 0; a < NU; ++a) s = fmaf(Kc[a], sm[S_MK + a], s);
+#pragma unroll
+    for (int a = 0; a < NU; ++a) s = fmaf(qxu[a], sm[S_KF + a], s);
+    vi = s;
+#pragma unroll
+    for (int j = 0; j < NX; ++j) sm[S_V + g * NX + j] = Vr[j];
+    sm[S_VV + g] = vi;
+  }
+  return fb;
+}
+
+// Lane g writes row g of A_t, B_t (state-row lanes) from the nominal x, u in
+// sm[S_Z].
+__device__ __forceinline__ void jacobian_rows(float* sm, int g, float dt) {
+  if (g < NX) {
+    float a[NX], b[NU];
+    jac_row(g, sm + S_Z, sm + S_Z + NX, dt, a, b);
+#pragma unroll
+    for (int j = 0; j < NX; ++j) sm[S_A + g * NX + j] = a[j];
+#pragma unroll
+    for (int j = 0; j < NU; ++j) sm[S_B + g * NU + j] = b[j];
+  }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Solve (controller.py:303-435)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(THREADS) dense_solve_kernel(DenseSolveParams p) {
+  extern __shared__ float smem[];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int e = lane >> 4;   // element slot of the warp
+  const int g = lane & 15;   // lane in the group
+  const int64_t b = ((int64_t)blockIdx.x * WPC + warp) * EPW + e;
+  const bool valid = b < p.B;
+  const int64_t bw = valid ? b : 0;  // a valid element for address formation
+  float* sm = smem + (warp * EPW + e) * S_ELEM;
+  const unsigned FULLW = 0xffffffffu;
+  const int gbase = lane & 16;
+  const int T = p.T;
+  const float dt = p.dt;
+  const bool rowx = g < NX;
+  const float* lo = p.has_bounds ? p.u_min : nullptr;
+  const float* hi = p.has_bounds ? p.u_max : nullptr;
+  Ws W{p.ws + bw * p.ws_fields, T, p.n_alpha + 1};
+  const float* Cb = p.C + bw * (int64_t)T * NT * NT;
+  const float* cb = p.c + bw * (int64_t)T * NT;
+  const float* Cf = p.C_f ? p.C_f + bw * NT * NT : nullptr;
+  const float* cf = p.c_f ? p.c_f + bw * NT : nullptr;
+  const float* xr = p.x_ref ? p.x_ref + bw * (int64_t)(T + 1) * NX : nullptr;
+  const float* ur = p.u_ref ? p.u_ref + bw * (int64_t)T * NU : nullptr;
+  auto xref = [&](int t, int i) { return xr ? __ldg(xr + t * NX + i) : 0.0f; };
+  auto uref = [&](int t, int a) { return ur ? __ldg(ur + t * NU + a) : 0.0f; };
+
+  if (p.trace != nullptr && valid && g == 0)
+    for (int i = 0; i < p.max_iter; ++i) p.trace[b * p.max_iter + i] = (int8_t)-128;
+
+  // ---- initial rollout and objective (controller.py:307-313), lane 0 -------
+  float best = 0.0f;
+  if (g == 0 && valid) {
+    float x[NX];
+#pragma unroll
+    for (int i = 0; i < NX; ++i) x[i] = __ldg(p.x0 + b * NX + i);
+    float sq = 0.0f, sl = 0.0f;
+    for (int t = 0; t < T; ++t) {
+      float u[NU];
+#pragma unroll
+      for (int a = 0; a < NU; ++a) u[a] = __ldg(p.U_init + (b * T + t) * NU + a);
+      store_rec(W.rec(0, t), x, u);
+      float tau[NT];
+#pragma unroll
+      for (int i = 0; i < NX; ++i) tau[i] = x[i] - xref(t, i);
+#pragma unroll
+      for (int a = 0; a < NU; ++a) tau[NX + a] = u[a] - uref(t, a);
+      float q, l;
+      step_cost(Cb + (int64_t)t * NT * NT, cb + (int64_t)t * NT, tau, q, l);
+      sq += q;
+      sl += l;
+      float xn[NX];
+      step(x, u, dt, xn);
+#pragma unroll
+      for (int i = 0; i < NX; ++i) x[i] = xn[i];
+    }
+    const float zu[NU] = {0.0f, 0.0f, 0.0f, 0.0f};
+    store_rec(W.rec(0, T), x, zu);
+    float tn[NX];
+#pragma unroll
+    for (int i = 0; i < NX; ++i) tn[i] = x[i] - xref(T, i);
+    best = (0.5f * sq + sl) + terminal_cost(Cf, cf, tn);
+  }
+  best = __shfl_sync(FULLW, best, gbase);
+  __syncwarp();
+
+  uint32_t status = 0;
+  bool active = valid;
+  int iters = 0;
+  int stall_iter = p.max_iter;
+  float stall_gap = 0.0f;
+  int nom = 0;
+
+  for (int it = 0; it < p.max_iter; ++it) {
+    if (p.forced != nullptr && active && p.forced[b * p.max_iter + it] == (int8_t)-128) active = false;
+    if (!__any_sync(FULLW, active)) break;
+
+    // ---- backward Riccati pass (controller.py:315-318, 697-723) ------------
+    float Vr[NX], vi = 0.0f, Kc[NU], kf[NU];
+    {
+      if (g < 5) reinterpret_cast<float4*>(sm + S_Z)[g] = W.rec(nom, T)[g];
+      __syncwarp();
+      if (rowx) {
+        float tn[NX];
+#pragma unroll
+        for (int j = 0; j < NX; ++j) tn[j] = sm[S_Z + j] - xref(T, j);
+        float s = 0.0f;
+#pragma unroll
+        for (int j = 0; j < NX; ++j) {
+          Vr[j] = Cf ? __ldg(Cf + g * NT + j) : 0.0f;
+          s = fmaf(Vr[j], tn[j], s);
+        }
+        vi = s + (cf ? __ldg(cf + g) : 0.0f);
+#pragma unroll
+        for (int j = 0; j < NX; ++j) sm[S_V + g * NX + j] = Vr[j];
+        sm[S_VV + g] = vi;
+      }
+    }
+    bool fallback = false;
+    for (int t = T - 1; t >= 0; --t) {
+      __syncwarp();
+      if (g < 5) reinterpret_cast<float4*>(sm + S_Z)[g] = W.rec(nom, t)[g];
+      __syncwarp();
+      jacobian_rows(sm, g, dt);
+      // l_tau = C tau + c for this lane's rows (cost.py:130-171)
+      float tau[NT];
+#pragma unroll
+      for (int i = 0; i < NX; ++i) tau[i] = sm[S_Z + i] - xref(t, i);
+#pragma unroll
+      for (int a = 0; a < NU; ++a) tau[NX + a] = sm[S_Z + NX + a] - uref(t, a);
+      const float* Ct = Cb + (int64_t)t * NT * NT;
+      const float* ct = cb + (int64_t)t * NT;
+      StepIn in;
+      in.lx = 0.0f;
+      in.lu = 0.0f;
+      if (rowx) {
+        const float* row = Ct + g * NT;
+        float crow[NT];
+#pragma unroll
+        for (int j = 0; j < NT; ++j) crow[j] = __ldg(row + j);
+        float s = crow[0] * tau[0];
+#pragma unroll
+        for (int j = 1; j < NT; ++j) s = fmaf(crow[j], tau[j], s);
+        in.lx = s + __ldg(ct + g);
+#pragma unroll
+        for (int j = 0; j < NX; ++j) in.cxx[j] = crow[j];
+#pragma unroll
+        for (int a = 0; a < NU; ++a) in.cxu[a] = crow[NX + a];
+      }
+      if (g < NU) {
+        const float* row = Ct + (NX + g) * NT;
+        float s = __ldg(row) * tau[0];
+#pragma unroll
+        for (int j = 1; j < NT; ++j) s = fmaf(__ldg(row + j), tau[j], s);
+        in.lu = s + __ldg(ct + NX + g);
+      }
+      in.cuu = __ldg(Ct + (NX + (g >> 2)) * NT + NX + (g & 3));
+      __syncwarp();
+      const bool fb = riccati_step<false>(sm, g, rowx, valid, FULLW, in, p.reg, nullptr, Vr, vi, Kc, kf);
+      fallback |= fb;
+      if (valid) {
+        if (rowx) *W.kcol(t, g) = make_float4(Kc[0], Kc[1], Kc[2], Kc[3]);
+        if (g == NX) *W.kff(t) = make_float4(kf[0], kf[1], kf[2], kf[3]);
+      }
+    }
+    if (fallback && active) status |= ELEM_CHOL_FALLBACK;
+    __syncwarp();
+
+    // ---- grid line search (controller.py:360-388, 437-533): lane j = step j --
+    float mine = 0.0f;
+    if (valid && g < p.n_alpha) {
+      const float al = p.alphas[g];
+      const int cs = g < nom ? g : g + 1;
+      float x[NX];
+#pragma unroll
+      for (int i = 0; i < NX; ++i) x[i] = __ldg(p.x0 + b * NX + i);
+      float sq = 0.0f, sl = 0.0f;
+      for (int t = 0; t < T; ++t) {
+        float xb[NX], ub[NU];
+        load_rec(W.rec(nom, t), xb, ub);
+        const float4 k4 = *W.kff(t);
+        float dx[NX];
+#pragma unroll
+        for (int j = 0; j < NX; ++j) dx[j] = x[j] - xb[j];
+        float kd[NU];
+        {
+          const float4 c = *W.kcol(t, 0);
+          kd[0] = c.x * dx[0];
+          kd[1] = c.y * dx[0];
+          kd[2] = c.z * dx[0];
+          kd[3] = c.w * dx[0];
+        }
+#pragma unroll
+        for (int j = 1; j < NX; ++j) {
+          const float4 c = *W.kcol(t, j);
+          kd[0] = fmaf(c.x, dx[j], kd[0]);
+          kd[1] = fmaf(c.y, dx[j], kd[1]);
+          kd[2] = fmaf(c.z, dx[j], kd[2]);
+          kd[3] = fmaf(c.w, dx[j], kd[3]);
+        }
+        const float kt[NU] = {k4.x, k4.y, k4.z, k4.w};
+        float u[NU];
+#pragma unroll
+        for (int a = 0; a < NU; ++a) {
+          float v = ub[a] + (al * kt[a] + al * kd[a]);
+          if (lo != nullptr) v = clampn(v, __ldg(lo + a), __ldg(hi + a));
+          u[a] = v;
+        }
+        store_rec(W.rec(cs, t), x, u);
+        float tau[NT];
+#pragma unroll
+        for (int i = 0; i < NX; ++i) tau[i] = x[i] - xref(t, i);
+#pragma unroll
+        for (int a = 0; a < NU; ++a) tau[NX + a] = u[a] - uref(t, a);
+        float q, l;
+        step_cost(Cb + (int64_t)t * NT * NT, cb + (int64_t)t * NT, tau, q, l);
+        sq += q;
+        sl += l;
+        float xn[NX];
+        step(x, u, dt, xn);
+#pragma unroll
+        for (int i = 0; i < NX; ++i) x[i] = xn[i];
+      }
+      const float zu[NU] = {0.0f, 0.0f, 0.0f, 0.0f};
+      store_rec(W.rec(cs, T), x, zu);
+      float tn[NX];
+#pragma unroll
+      for (int i = 0; i < NX; ++i) tn[i] = x[i] - xref(T, i);
+      mine = (0.5f * sq + sl) + terminal_cost(Cf, cf, tn);
+    }
+    // torch.argmin semantics over the step sizes: first NaN, else first minimum
+    int jbest = 0;
+    float cmin = 0.0f;
+    bool have = false, nan_seen = false;
+    float cand[ILQR_MAX_ALPHAS_DEV];
+#pragma unroll
+    for (int jj = 0; jj < ILQR_MAX_ALPHAS_DEV; ++jj) {
+      const float cj = __shfl_sync(FULLW, mine, gbase + jj);
+      cand[jj] = cj;
+      if (jj >= p.n_alpha) continue;
+      if (!nan_seen) {
+        if (cj != cj) {
+          nan_seen = true;
+          jbest = jj;
+          cmin = cj;
+        } else if (!have || cj < cmin) {
+          have = true;
+          jbest = jj;
+          cmin = cj;
+        }
+      }
+    }
+
+    // ---- decision (controller.py:396-415) ---------------------------------
+    if (active) {
+      bool accept;
+      int jsel = jbest;
+      ++iters;
+      if (p.forced != nullptr) {
+        const int8_t d = p.forced[b * p.max_iter + it];
+        accept = d >= 0 && d < p.n_alpha;
+        if (accept) jsel = d;
+      } else {
+        accept = cmin < best;
+      }
+      if (p.trace != nullptr && g == 0) p.trace[b * p.max_iter + it] = (int8_t)(accept ? jsel : -(jbest + 1));
+      if (!accept && stall_iter == p.max_iter) {
+        stall_iter = it;
+        stall_gap = fabsf(cmin - best);
+      }
+      if (accept) {
+        float cs = cand[0];
+#pragma unroll
+        for (int jj = 1; jj < ILQR_MAX_ALPHAS_DEV; ++jj) cs = (jj == jsel) ? cand[jj] : cs;
+        best = cs;
+        nom = jsel < nom ? jsel : jsel + 1;
+      }
+      if (!accept && p.forced == nullptr) active = false;
+    }
+    __syncwarp();
+  }
+
+  // ---- outputs ------------------------------------------------------------------
+  bool finite = true;
+  if (valid) {
+    const float* nrec = reinterpret_cast<const float*>(W.rec(nom, 0));
+    for (int f = g; f < (T + 1) * NX; f += GL) {
+      const int t = f / NX, i = f - t * NX;
+      const float xv = nrec[t * REC + i];
+      finite &= isfinite(xv);
+      p.X[b * (T + 1) * NX + f] = xv;
+    }
+    for (int f = g; f < T * NU; f += GL) {
+      const int t = f / NU, a = f - t * NU;
+      const float uv = nrec[t * REC + NX + a];
+      finite &= isfinite(uv);
+      p.U[b * T * NU + f] = uv;
+      if (p.tight != nullptr) {
+        // torch.isclose(U, bound, rtol=1e-5, atol=1e-7) against u_min, u_max
+        bool tt = false;
+        if (lo != nullptr) {
+          const float l_ = __ldg(lo + a), h_ = __ldg(hi + a);
+          const float e0 = fabsf(uv - l_), e1 = fabsf(uv - h_);
+          tt = (uv == l_) || (isfinite(e0) && e0 <= 1e-7f + fabsf(1e-5f * l_)) || (uv == h_) ||
+               (isfinite(e1) && e1 <= 1e-7f + fabsf(1e-5f * h_));
+        }
+        p.tight[b * T * NU + f] = tt ? 1 : 0;
+      }
+    }
+  }
+  const bool all_finite = group_sum(finite ? 0.0f : 1.0f, FULLW) == 0.0f;
+  if (!all_finite) status |= ELEM_NONFINITE;
+  if (valid && g == 0) {
+    if (p.iters) p.iters[b] = iters;
+    if (p.status) p.status[b] = status;
+    if (p.best_cost) p.best_cost[b] = best;
+    if (p.stall_iter) p.stall_iter[b] = stall_iter;
+    if (p.stall_gap) p.stall_gap[b] = stall_gap;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Implicit-diff backward (controller.py:68-133, 1006-1131)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(THREADS) dense_backward_kernel(DenseBackwardParams p) {
+  extern __shared__ float smem[];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int e = lane >> 4;
+  const int g = lane & 15;
+  const int64_t b = ((int64_t)blockIdx.x * WPC + warp) * EPW + e;
+  const bool valid = b < p.B;
+  const int64_t bw = valid ? b : 0;
+  float* sm = smem + (warp * EPW + e) * S_ELEM;
+  const unsigned FULLW = 0xffffffffu;
+  const int T = p.T;
+  const float dt = p.dt;
+  const bool rowx = g < NX;
+  const float* Xb = p.X + bw * (int64_t)(T + 1) * NX;
+  const float* Ub = p.U + bw * (int64_t)T * NU;
+  const float* Cb = p.C + bw * (int64_t)T * NT * NT;
+  const float* Cf = p.C_f ? p.C_f + bw * NT * NT : nullptr;
+  const float* xr = p.x_ref ? p.x_ref + bw * (int64_t)(T + 1) * NX : nullptr;
+  const float* gX = p.gX + bw * (int64_t)(T + 1) * NX;
+  const float* gU = p.gU + bw * (int64_t)T * NU;
+  const uint8_t* tb = p.tight ? p.tight + bw * (int64_t)T * NU : nullptr;
+  float4* kws = reinterpret_cast<float4*>(p.ws + bw * (int64_t)T * (NX + 1) * 4);
+
+  auto load_z = [&](int t) {
+    // nominal x_t (and u_t for t < T) into sm[S_Z]
+    if (g < NX) sm[S_Z + g] = __ldg(Xb + t * NX + g);
+    if (g < NU) sm[S_Z + NX + g] = t < T ? __ldg(Ub + t * NU + g) : 0.0f;
+  };
+
+  // ---- masked adjoint Riccati: V_T = C_f,xx, v_T = -dL/dX_T -------------
+  float Vr[NX], vi = 0.0f, Kc[NU], kf[NU];
+  if (rowx) {
+#pragma unroll
+    for (int j = 0; j < NX; ++j) {
+      Vr[j] = Cf ? __ldg(Cf + g * NT + j) : 0.0f;
+      sm[S_V + g * NX + j] = Vr[j];
+    }
+    vi = -__ldg(gX + T * NX + g);
+    sm[S_VV + g] = vi;
+  }
+  for (int t = T - 1; t >= 0; --t) {
+    __syncwarp();
+    load_z(t);
+    __syncwarp();
+    jacobian_rows(sm, g, dt);
+    const float* Ct = Cb + (int64_t)t * NT * NT;
+    StepIn in;
+    in.lx = rowx ? -__ldg(gX + t * NX + g) : 0.0f;
+    in.lu = g < NU ? -__ldg(gU + t * NU + g) : 0.0f;
+    if (rowx) {
+#pragma unroll
+      for (int j = 0; j < NX; ++j) in.cxx[j] = __ldg(Ct + g * NT + j);
+#pragma unroll
+      for (int a = 0; a < NU; ++a) in.cxu[a] = __ldg(Ct + g * NT + NX + a);
+    }
+    in.cuu = __ldg(Ct + (NX + (g >> 2)) * NT + NX + (g & 3));
+    bool tight[NU];
+#pragma unroll
+    for (int a = 0; a < NU; ++a) tight[a] = tb ? (tb[t * NU + a] != 0) : false;
+    __syncwarp();
+    riccati_step<true>(sm, g, rowx, valid, FULLW, in, p.reg, tight, Vr, vi, Kc, kf);
+    if (valid) {
+      if (rowx) kws[t * (NX + 1) + g] = make_float4(Kc[0], Kc[1], Kc[2], Kc[3]);
+      if (g == NX) kws[t * (NX + 1) + NX] = make_float4(kf[0], kf[1], kf[2], kf[3]);
+    }
+  }
+  if (valid && rowx && p.g_x0) p.g_x0[b * NX + g] = -vi;
+  __syncwarp();
+
+  // ---- tangent sweep dU = K dX + k, dX+ = A dX + B dU, and the gradients ------
+  float* dxs = sm + S_VV;  // dX_t [13]
+  if (rowx) dxs[g] = 0.0f;
+  for (int t = 0; t < T; ++t) {
+    __syncwarp();
+    load_z(t);
+    __syncwarp();
+    jacobian_rows(sm, g, dt);
+    float dx[NX];
+#pragma unroll
+    for (int j = 0; j < NX; ++j) dx[j] = dxs[j];
+    float du[NU];
+    {
+      const float4* kc = kws + t * (NX + 1);
+      const float4 c0 = valid ? kc[0] : make_float4(0.f, 0.f, 0.f, 0.f);
+      float kd[NU] = {c0.x * dx[0], c0.y * dx[0], c0.z * dx[0], c0.w * dx[0]};
+#pragma unroll
+      for (int j = 1; j < NX; ++j) {
+        const float4 c = valid ? kc[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+        kd[0] = fmaf(c.x, dx[j], kd[0]);
+        kd[1] = fmaf(c.y, dx[j], kd[1]);
+        kd[2] = fmaf(c.z, dx[j], kd[2]);
+        kd[3] = fmaf(c.w, dx[j], kd[3]);
+      }
+      const float4 k4 = valid ? kc[NX] : make_float4(0.f, 0.f, 0.f, 0.f);
+      du[0] = kd[0] + k4.x;
+      du[1] = kd[1] + k4.y;
+      du[2] = kd[2] + k4.z;
+      du[3] = kd[3] + k4.w;
+    }
+    __syncwarp();
+    // dX_{t+1} row g
+    float dxn = 0.0f;
+    if (rowx) {
+      float s = sm[S_A + g * NX] * dx[0];
+#pragma unroll
+      for (int k = 1; k < NX; ++k) s = fmaf(sm[S_A + g * NX + k], dx[k], s);
+      float sb = sm[S_B + g * NU] * du[0];
+#pragma unroll
+      for (int a = 1; a < NU; ++a) sb = fmaf(sm[S_B + g * NU + a], du[a], sb);
+      dxn = s + sb;
+    }
+    if (valid) {
+      // dtau = [dX_t; dU_t], z = [X_t; U_t]:
+      // grad_C_t = -1/2 (dtau z^T + z dtau^T), grad_c_t = -dtau
+      float z[NT], dz[NT];
+#pragma unroll
+      for (int i = 0; i < NX; ++i) {
+        z[i] = sm[S_Z + i];
+        dz[i] = dx[i];
+      }
+#pragma unroll
+      for (int a = 0; a < NU; ++a) {
+        z[NX + a] = sm[S_Z + NX + a];
+        dz[NX + a] = du[a];
+      }
+      const int64_t off = (b * T + t) * NT;
+      if (p.g_C) {
+        float* gC = p.g_C + off * NT;
+        if (rowx) {
+#pragma unroll
+          for (int j = 0; j < NT; ++j) gC[g * NT + j] = -0.5f * (dz[g] * z[j] + z[g] * dz[j]);
+        }
+        if (g < NU) {
+          const int i = NX + g;
+#pragma unroll
+          for (int j = 0; j < NT; ++j) gC[i * NT + j] = -0.5f * (dz[i] * z[j] + z[i] * dz[j]);
+        }
+      }
+      if (p.g_c) {
+        if (rowx) p.g_c[off + g] = -dz[g];
+        if (g < NU) p.g_c[off + NX + g] = -dz[NX + g];
+      }
+      if (p.g_xref && rowx) p.g_xref[(b * (T + 1) + t) * NX + g] = dx[g];
+      if (p.g_uref && g < NU) p.g_uref[(b * T + t) * NU + g] = du[g];
+    }
+    if (rowx) dxs[g] = dxn;
+  }
+  __syncwarp();
+  if (valid) {
+    // terminal: grad_C_final xx = -1/2 (dX_T e^T + e dX_T^T), e = X_T - x_ref_T
+    float dxT[NX], eT[NX];
+#pragma unroll
+    for (int j = 0; j < NX; ++j) {
+      dxT[j] = dxs[j];
+      eT[j] = __ldg(Xb + T * NX + j) - (xr ? __ldg(xr + T * NX + j) : 0.0f);
+    }
+    if (p.g_xref && rowx) p.g_xref[(b * (T + 1) + T) * NX + g] = 0.0f;
+    if (p.g_Cf) {
+      float* gCf = p.g_Cf + b * NT * NT;
+      if (rowx) {
+#pragma unroll
+        for (int j = 0; j < NT; ++j)
+          gCf[g * NT + j] = j < NX ? -0.5f * (dxT[g] * eT[j] + eT[g] * dxT[j]) : 0.0f;
+      }
+      if (g < NU) {
+#pragma unroll
+        for (int j = 0; j < NT; ++j) gCf[(NX + g) * NT + j] = 0.0f;
+      }
+    }
+    if (p.g_cf) {
+      if (rowx) p.g_cf[b * NT + g] = -dxT[g];
+      if (g < NU) p.g_cf[b * NT + NX + g] = 0.0f;
+    }
+  }
+}
+
+// One model step / Jacobian per thread (component checks and callers that
+// want the model alone).
+__global__ void rotor13_dynamics_kernel(const float* __restrict__ x, const float* __restrict__ u, int64_t n,
+                                        float dt, float* __restrict__ xn) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float xv[NX], uv[NU], out[NX];
+#pragma unroll
+  for (int j = 0; j < NX; ++j) xv[j] = __ldg(x + i * NX + j);
+#pragma unroll
+  for (int j = 0; j < NU; ++j) uv[j] = __ldg(u + i * NU + j);
+  step(xv, uv, dt, out);
+#pragma unroll
+  for (int j = 0; j < NX; ++j) xn[i * NX + j] = out[j];
+}
+
+// Thread per (element, step, row): row r of A [B,T,13,13] and B [B,T,13,4].
+__global__ void rotor13_linearize_kernel(const float* __restrict__ X, const float* __restrict__ U, int64_t B,
+                                         int T, float dt, float* __restrict__ A, float* __restrict__ Bm) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= B * T * NX) return;
+  const int r = (int)(idx % NX);
+  const int64_t bt = idx / NX;
+  const int64_t b = bt / T;
+  const int t = (int)(bt - b * T);
+  float xv[NX], uv[NU], a[NX], bb[NU];
+#pragma unroll
+  for (int j = 0; j < NX; ++j) xv[j] = __ldg(X + (b * (T + 1) + t) * NX + j);
+#pragma unroll
+  for (int j = 0; j < NU; ++j) uv[j] = __ldg(U + bt * NU + j);
+  jac_row(r, xv, uv, dt, a, bb);
+#pragma unroll
+  for (int j = 0; j < NX; ++j) A[(bt * NX + r) * NX + j] = a[j];
+#pragma unroll
+  for (int j = 0; j < NU; ++j) Bm[(bt * NX + r) * NU + j] = bb[j];
+}
+
+}  // namespace r13
+
+int64_t dense_solve_ws_fields(int T, int n_alpha) {
+  return (int64_t)(n_alpha + 1) * (T + 1) * r13::REC + (int64_t)T * (r13::NX + 1) * 4;
+}
+
+int64_t dense_backward_ws_fields(int T) { return (int64_t)T * (r13::NX + 1) * 4; }
+
+static size_t dense_smem_bytes() { return (size_t)r13::EPC * r13::S_ELEM * sizeof(float); }
+
+cudaError_t launch_dense_solve(const DenseSolveParams& p, cudaStream_t stream) {
+  if (p.B == 0) return cudaSuccess;
+  const int64_t grid = (p.B + r13::EPC - 1) / r13::EPC;
+  r13::dense_solve_kernel<<<(unsigned)grid, r13::THREADS, dense_smem_bytes(), stream>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dense_backward(const DenseBackwardParams& p, cudaStream_t stream) {
+  if (p.B == 0) return cudaSuccess;
+  const int64_t grid = (p.B + r13::EPC - 1) / r13::EPC;
+  r13::dense_backward_kernel<<<(unsigned)grid, r13::THREADS, dense_smem_bytes(), stream>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rotor13_dynamics(const float* x, const float* u, int64_t n, float dt, float* xn,
+                                    cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  r13::rotor13_dynamics_kernel<<<(unsigned)((n + 127) / 128), 128, 0, s>>>(x, u, n, dt, xn);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rotor13_linearize(const float* X, const float* U, int64_t B, int T, float dt, float* A,
+                                     float* Bm, cudaStream_t s) {
+  const int64_t n = B * T * r13::NX;
+  if (n == 0) return cudaSuccess;
+  r13::rotor13_linearize_kernel<<<(unsigned)((n + 127) / 128), 128, 0, s>>>(X, U, B, T, dt, A, Bm);
+  return cudaGetLastError();
+}
+
+}  // namespace ilqr

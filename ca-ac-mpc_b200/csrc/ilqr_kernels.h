@@ -94,6 +94,78 @@ inline int64_t solve_ws_fields(int T) {
 inline int64_t backward_ws_fields(int T) { return (int64_t)T * (40 + 4); }
 inline int64_t ws_stride(int64_t B) { return (B + 31) / 32 * 32; }
 
+// The 13-state rotor-thrust model (ilqr_rotor13.cuh), solved by the dense
+// row-per-lane kernels of ilqr_dense.cu. Dense inputs as the 10-state entry
+// points, with 13 states and tau = [x; u] of length 17.
+struct DenseSolveParams {
+  const float* x0;
+  const float* U_init;
+  const float* C;
+  const float* c;
+  const float* C_f;
+  const float* c_f;
+  const float* x_ref;
+  const float* u_ref;
+  const float* u_min;
+  const float* u_max;
+  const int8_t* forced;
+  float* X;
+  float* U;
+  uint8_t* tight;
+  int8_t* trace;
+  int32_t* iters;
+  uint32_t* status;
+  float* best_cost;
+  int32_t* stall_iter;
+  float* stall_gap;
+  float* ws;
+  int64_t ws_fields;  // floats of workspace per element
+  int64_t B;
+  int T;
+  int max_iter;
+  float dt;
+  float reg;
+  float alphas[ILQR_MAX_ALPHAS_DEV];
+  int n_alpha;
+  int has_bounds;
+};
+
+struct DenseBackwardParams {
+  const float* X;
+  const float* U;
+  const float* C;
+  const float* C_f;
+  const float* x_ref;
+  const float* u_ref;
+  const uint8_t* tight;
+  const float* gX;
+  const float* gU;
+  float* g_x0;
+  float* g_C;
+  float* g_c;
+  float* g_Cf;
+  float* g_cf;
+  float* g_xref;
+  float* g_uref;
+  float* ws;
+  int64_t B;
+  int T;
+  float dt;
+  float reg;
+};
+
+// Per-element workspace of the dense solve: (n_alpha + 1) trajectory slots of
+// T + 1 records of 20 floats, then K_t columns and k_t as [T][14] float4.
+int64_t dense_solve_ws_fields(int T, int n_alpha);
+// Per-element workspace of the dense backward: K_t, k_t as [T][14] float4.
+int64_t dense_backward_ws_fields(int T);
+cudaError_t launch_dense_solve(const DenseSolveParams& p, cudaStream_t stream);
+cudaError_t launch_dense_backward(const DenseBackwardParams& p, cudaStream_t stream);
+cudaError_t launch_rotor13_dynamics(const float* x, const float* u, int64_t n, float dt, float* xn,
+                                    cudaStream_t s);
+cudaError_t launch_rotor13_linearize(const float* X, const float* U, int64_t B, int T, float dt, float* A,
+                                     float* Bm, cudaStream_t s);
+
 size_t solve_smem_bytes(int tier);
 size_t backward_smem_bytes();
 cudaError_t launch_solve(const CUtensorMap& tmC, const SolveParams& p, cudaStream_t stream);

@@ -65,6 +65,14 @@ def lib():
             "ilqr_b200_linearize_f32": ([_P, _P, _I64, _I32, _F, _P, _P, _P], _I32),
             "ilqr_b200_adjoint_lqr_f32": ([_P] * 10 + [_I64, _I32, _F, _P, _P, _P, _P], _I32),
             "ilqr_b200_implicit_diff_assembly_f32": ([_P] * 9 + [_I64, _I32] + [_P] * 7 + [_P], _I32),
+            "ilqr_b200_rotor13_solve_workspace_size": ([_I64, _I32, _I32, ctypes.POINTER(ctypes.c_size_t)], _I32),
+            "ilqr_b200_rotor13_backward_workspace_size": ([_I64, _I32, ctypes.POINTER(ctypes.c_size_t)], _I32),
+            "ilqr_b200_rotor13_solve_f32": ([_P] * 10 + [_I64, _I32, _F, _I32, _F, _F, _P, _I32, _P]
+                                            + [_P] * 9 + [_P, ctypes.c_size_t, _P], _I32),
+            "ilqr_b200_rotor13_backward_f32": ([_P] * 9 + [_I64, _I32, _F, _F] + [_P] * 7
+                                               + [_P, ctypes.c_size_t, _P], _I32),
+            "ilqr_b200_rotor13_dynamics_f32": ([_P, _P, _I64, _F, _P, _P], _I32),
+            "ilqr_b200_rotor13_linearize_f32": ([_P, _P, _I64, _I32, _F, _P, _P, _P], _I32),
         }
         for name, (argt, rest) in sig.items():
             fn = getattr(L, name)
@@ -83,6 +91,9 @@ EXPORTED_SYMBOLS = (
     "ilqr_b200_linearize_f32", "ilqr_b200_adjoint_lqr_f32",
     "ilqr_b200_implicit_diff_assembly_f32", "ilqr_b200_solve_f32_noalloc",
     "ilqr_b200_solve_sigmoid_f32", "ilqr_b200_backward_sigmoid_f32", "ilqr_b200_pnqp4_batch_f32",
+    "ilqr_b200_rotor13_solve_workspace_size", "ilqr_b200_rotor13_backward_workspace_size",
+    "ilqr_b200_rotor13_solve_f32", "ilqr_b200_rotor13_backward_f32", "ilqr_b200_rotor13_dynamics_f32",
+    "ilqr_b200_rotor13_linearize_f32",
 )
 
 
@@ -501,3 +512,132 @@ def converged_flag(stall_iter, stall_gap, status, max_iter, converge_tol):
         if (gap == gap and gap < converge_tol) or s + 2 <= max_iter - 1:
             return True
     return not bool(((status & 2) != 0).any().item())
+
+
+# ---------------------------------------------------------------------------
+# 13-state rotor-thrust quadrotor (state p, q, v, w; four rotor thrusts as
+# fractions of F_MAX13 in [0, 1]): the same solver on DiffMPC's model-generic
+# path (DifferentialMPC/controller.py:147-160, 607-615).
+# ---------------------------------------------------------------------------
+
+NX13 = 13
+N13 = NX13 + NU
+MASS13 = 0.75
+F_MAX13 = 8.5
+HOVER_U13 = MASS13 * 9.8066 / (4.0 * F_MAX13)  # per-rotor hover thrust fraction
+
+
+def rotor13_solve(x0, U_init, C, c, C_final=None, c_final=None, x_ref=None, u_ref=None,
+                  u_min=None, u_max=None, dt=0.05, max_iter=10, reg_eps=1e-6, converge_tol=1e-6,
+                  alphas: Sequence[float] = DEFAULT_ALPHAS, forced_trace=None, want_trace=False,
+                  want_stats=False):
+    """solve() for the rotor model: X [B,T+1,13], U [B,T,4], C [B,T,17,17]."""
+    L = lib()
+    dev = _cuda_device(x0, "x0")
+    _device_ok(dev)
+    B = x0.shape[0]
+    T = U_init.shape[1]
+    _req(x0, "x0", (B, NX13), dev)
+    _req(U_init, "U_init", (B, T, NU), dev)
+    _req(C, "C", (B, T, N13, N13), dev)
+    _req(c, "c", (B, T, N13), dev)
+    _opt(C_final, "C_final", (B, N13, N13), dev)
+    _opt(c_final, "c_final", (B, N13), dev)
+    _opt(x_ref, "x_ref", (B, T + 1, NX13), dev)
+    _opt(u_ref, "u_ref", (B, T, NU), dev)
+    if (u_min is None) != (u_max is None):
+        raise RuntimeError("u_min and u_max must both be given or both be None")
+    _opt(u_min, "u_min", (NU,), dev)
+    _opt(u_max, "u_max", (NU,), dev)
+    _opt(forced_trace, "forced_trace", (B, max_iter), dev, torch.int8)
+    al = [float(a) for a in alphas]
+    if not 1 <= len(al) <= 8:
+        raise RuntimeError("between 1 and 8 line-search step sizes are supported")
+    if C_final is None and c_final is not None:
+        C_final = torch.zeros(B, N13, N13, device=dev)
+    X = torch.empty(B, T + 1, NX13, device=dev)
+    U = torch.empty(B, T, NU, device=dev)
+    tight = torch.empty(B, T, NU, device=dev, dtype=torch.uint8)
+    out = dict(X=X, U=U, tight=tight)
+    trace = iters = status = best = s_it = s_gap = None
+    if want_trace:
+        trace = out["trace"] = torch.empty(B, max_iter, device=dev, dtype=torch.int8)
+    if want_stats:
+        iters = out["iters"] = torch.empty(B, device=dev, dtype=torch.int32)
+        status = out["status"] = torch.empty(B, device=dev, dtype=torch.int32)
+        best = out["best_cost"] = torch.empty(B, device=dev)
+        s_it = out["stall_iter"] = torch.empty(B, device=dev, dtype=torch.int32)
+        s_gap = out["stall_gap"] = torch.empty(B, device=dev)
+    n = ctypes.c_size_t(0)
+    _check(L.ilqr_b200_rotor13_solve_workspace_size(B, T, len(al), ctypes.byref(n)), "workspace query")
+    nbytes = int(n.value)
+    ws = torch.empty(max(nbytes, 16), device=dev, dtype=torch.uint8)
+    a_arr = (ctypes.c_float * len(al))(*al)
+    st = L.ilqr_b200_rotor13_solve_f32(
+        _ptr(x0), _ptr(U_init), _ptr(C), _ptr(c), _ptr(C_final), _ptr(c_final), _ptr(x_ref),
+        _ptr(u_ref), _ptr(u_min), _ptr(u_max), B, T, float(dt), int(max_iter), float(reg_eps),
+        float(converge_tol), ctypes.cast(a_arr, ctypes.c_void_p), len(al), _ptr(forced_trace), _ptr(X), _ptr(U),
+        _ptr(tight), _ptr(trace), _ptr(iters), _ptr(status), _ptr(best), _ptr(s_it), _ptr(s_gap),
+        _ptr(ws), nbytes, _stream(dev))
+    _check(st, "ilqr_b200_rotor13_solve_f32")
+    return out
+
+
+def rotor13_backward(X, U, C, grad_X, grad_U, C_final=None, x_ref=None, u_ref=None, tight=None,
+                     dt=0.05, reg_eps=1e-6, need=("x0", "C", "c")):
+    """backward() for the rotor model; `need` as there."""
+    L = lib()
+    dev = _cuda_device(X, "X")
+    _device_ok(dev)
+    B, T1, _ = X.shape
+    T = T1 - 1
+    _req(X, "X", (B, T + 1, NX13), dev)
+    _req(U, "U", (B, T, NU), dev)
+    _req(C, "C", (B, T, N13, N13), dev)
+    _req(grad_X, "grad_X", (B, T + 1, NX13), dev)
+    _req(grad_U, "grad_U", (B, T, NU), dev)
+    _opt(C_final, "C_final", (B, N13, N13), dev)
+    _opt(x_ref, "x_ref", (B, T + 1, NX13), dev)
+    _opt(u_ref, "u_ref", (B, T, NU), dev)
+    _opt(tight, "tight_mask", (B, T, NU), dev, torch.uint8)
+    shapes = dict(x0=(B, NX13), C=(B, T, N13, N13), c=(B, T, N13), C_final=(B, N13, N13),
+                  c_final=(B, N13), x_ref=(B, T + 1, NX13), u_ref=(B, T, NU))
+    out = {k: torch.empty(shapes[k], device=dev) for k in need}
+    n = ctypes.c_size_t(0)
+    _check(L.ilqr_b200_rotor13_backward_workspace_size(B, T, ctypes.byref(n)), "workspace query")
+    nbytes = int(n.value)
+    ws = torch.empty(max(nbytes, 16), device=dev, dtype=torch.uint8)
+    g = lambda k: _ptr(out.get(k))
+    st = L.ilqr_b200_rotor13_backward_f32(
+        _ptr(X), _ptr(U), _ptr(C), _ptr(C_final), _ptr(x_ref), _ptr(u_ref), _ptr(tight),
+        _ptr(grad_X), _ptr(grad_U), B, T, float(dt), float(reg_eps),
+        g("x0"), g("C"), g("c"), g("C_final"), g("c_final"), g("x_ref"), g("u_ref"),
+        _ptr(ws), nbytes, _stream(dev))
+    _check(st, "ilqr_b200_rotor13_backward_f32")
+    return out
+
+
+def rotor13_dynamics(x, u, dt):
+    """One rotor-model step for x [n,13], u [n,4]."""
+    dev = _cuda_device(x, "x")
+    n = x.shape[0]
+    _req(x, "x", (n, NX13), dev)
+    _req(u, "u", (n, NU), dev)
+    xn = torch.empty(n, NX13, device=dev)
+    _check(lib().ilqr_b200_rotor13_dynamics_f32(_ptr(x), _ptr(u), n, float(dt), _ptr(xn), _stream(dev)),
+           "ilqr_b200_rotor13_dynamics_f32")
+    return xn
+
+
+def rotor13_linearize(X, U, dt):
+    """Rotor-model Jacobians A [B,T,13,13], B [B,T,13,4] at (X_t, U_t)."""
+    dev = _cuda_device(X, "X")
+    B, T1, _ = X.shape
+    T = T1 - 1
+    _req(X, "X", (B, T + 1, NX13), dev)
+    _req(U, "U", (B, T, NU), dev)
+    A = torch.empty(B, T, NX13, NX13, device=dev)
+    Bm = torch.empty(B, T, NX13, NU, device=dev)
+    _check(lib().ilqr_b200_rotor13_linearize_f32(_ptr(X), _ptr(U), B, T, float(dt), _ptr(A), _ptr(Bm),
+                                                _stream(dev)), "ilqr_b200_rotor13_linearize_f32")
+    return A, Bm

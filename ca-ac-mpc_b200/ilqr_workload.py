@@ -99,15 +99,15 @@ def make_inputs(B: int, T: int, seed: int = 0, target: str = "cube", r: float = 
     return dict(x0=x0, C=C, c=c, U_init=U_init)
 
 
-def make_backward_seeds(B: int, T: int, seed: int = 1, offset: int = 0):
-    """Upstream gradients dL/dX [B,T+1,10], dL/dU [B,T,4] ~ N(0,1)."""
+def make_backward_seeds(B: int, T: int, seed: int = 1, offset: int = 0, nx: int = NX):
+    """Upstream gradients dL/dX [B,T+1,nx], dL/dU [B,T,4] ~ N(0,1)."""
     assert offset % BLOCK == 0
-    gX = np.empty((B, T + 1, NX), dtype=np.float32)
+    gX = np.empty((B, T + 1, nx), dtype=np.float32)
     gU = np.empty((B, T, NU), dtype=np.float32)
     for blk in range((B + BLOCK - 1) // BLOCK):
         lo, hi = blk * BLOCK, min(B, (blk + 1) * BLOCK)
         rng = np.random.default_rng([seed, blk + offset // BLOCK])
-        gX[lo:hi] = rng.normal(size=(BLOCK, T + 1, NX))[: hi - lo]
+        gX[lo:hi] = rng.normal(size=(BLOCK, T + 1, nx))[: hi - lo]
         gU[lo:hi] = rng.normal(size=(BLOCK, T, NU))[: hi - lo]
     return gX, gU
 
@@ -139,3 +139,65 @@ def config_inputs(name: str, B: int | None = None, seed: int = 0):
     nb = cfg["B"] if B is None else B
     inp = make_inputs(nb, cfg["T"], seed=seed, target=cfg["target"], r=cfg["r"])
     return cfg, inp
+
+
+# --------------------------------------------------------------------------
+# 13-state rotor-thrust quadrotor (rotor13): state p, q, v, w; four rotor
+# thrusts as fractions of 8.5 N in the box [0, 1]; mass 0.75 kg.
+# --------------------------------------------------------------------------
+
+NX13 = 13
+N13 = NX13 + NU
+MASS13 = 0.75
+F_MAX13 = 8.5
+HOVER_U13 = MASS13 * G / (4.0 * F_MAX13)
+U_MIN13 = np.zeros(NU, dtype=np.float32)
+U_MAX13 = np.ones(NU, dtype=np.float32)
+
+
+def make_rotor13_inputs(B: int, T: int, seed: int = 0, target: str = "cube", r: float = 5.0,
+                        offset: int = 0):
+    """Rotor13 solve inputs with the same draws as make_inputs:
+    x0 = hover at (0,0,1) + N(0, 0.1^2) position and N(0, 0.2^2) velocity
+    noise, identity attitude, zero body rates; C[b,t] diagonal, all 17
+    entries log-uniform in [1e-2, 1e2]; c[b,t] = -C[b,t] tau_ref[b] with
+    tau_ref = (r, 1,0,0,0, 0,0,0, 0,0,0, hover x4) and r in a 10 m cube (or
+    on a sphere); U_init = hover thrust on every rotor.
+    Returns dict(x0 [B,13], C [B,T,17,17], c [B,T,17], U_init [B,T,4])."""
+    assert offset % BLOCK == 0
+    b_off = offset // BLOCK
+    x0 = np.zeros((B, NX13), dtype=np.float32)
+    C = np.zeros((B, T, N13, N13), dtype=np.float32)
+    c = np.empty((B, T, N13), dtype=np.float32)
+    idx = np.arange(N13)
+    for blk in range((B + BLOCK - 1) // BLOCK):
+        lo, hi = blk * BLOCK, min(B, (blk + 1) * BLOCK)
+        n = hi - lo
+        rng = np.random.default_rng([seed, 13, blk + b_off])
+        p0 = np.array([0.0, 0.0, 1.0]) + rng.normal(0.0, 0.1, (BLOCK, 3))
+        v0 = rng.normal(0.0, 0.2, (BLOCK, 3))
+        diag = np.exp(rng.uniform(np.log(1e-2), np.log(1e2), (BLOCK, T, N13)))
+        if target == "cube":
+            ref = rng.uniform(-r, r, (BLOCK, 3))
+        else:
+            d = rng.normal(size=(BLOCK, 3))
+            ref = r * d / np.linalg.norm(d, axis=1, keepdims=True)
+        x0[lo:hi, 0:3] = p0[:n]
+        x0[lo:hi, 3] = 1.0
+        x0[lo:hi, 7:10] = v0[:n]
+        d32 = diag[:n].astype(np.float32)
+        C[lo:hi, :, idx, idx] = d32
+        tau = np.zeros((n, N13), dtype=np.float32)
+        tau[:, 0:3] = ref[:n]
+        tau[:, 3] = 1.0
+        tau[:, NX13:] = np.float32(HOVER_U13)
+        c[lo:hi] = -(d32 * tau[:, None, :])
+    U_init = np.full((B, T, NU), np.float32(HOVER_U13), dtype=np.float32)
+    return dict(x0=x0, C=C, c=c, U_init=U_init)
+
+
+def rotor13_config_inputs(name: str, B: int | None = None, seed: int = 0):
+    """Rotor13 inputs for one of CONFIGS (optionally its first B elements)."""
+    cfg = CONFIGS[name]
+    nb = cfg["B"] if B is None else B
+    return cfg, make_rotor13_inputs(nb, cfg["T"], seed=seed, target=cfg["target"], r=cfg["r"])

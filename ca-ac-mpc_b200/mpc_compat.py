@@ -99,11 +99,15 @@ def _normalize_bounds(u_lower, u_upper, nu, device, dtype):
             _flatten(u_upper).to(device=device, dtype=torch.float32).contiguous())
 
 
-def _normalize_init(u_init, B, T, nu, device, dtype) -> Tensor:
-    """U_init as [B, T, nu] float32; hover thrust when absent (mpc_compat.py:113-125)."""
+def _normalize_init(u_init, B, T, nu, device, dtype, nx: int = 10) -> Tensor:
+    """U_init as [B, T, nu] float32; hover thrust when absent (mpc_compat.py:113-125;
+    for the 13-state rotor model, the hover fraction on every rotor)."""
     if u_init is None:
         out = torch.zeros(B, T, nu, device=device, dtype=torch.float32)
-        out[:, :, 0] = HOVER_THRUST
+        if nx == _nat.NX13:
+            out[:] = _nat.HOVER_U13
+        else:
+            out[:, :, 0] = HOVER_THRUST
         return out
     if u_init.ndim == 3:
         out = u_init.permute(1, 0, 2)
@@ -127,11 +131,14 @@ class DroneMPCFunction(torch.autograd.Function):
     DroneMPCFunction (mpc_compat.py:128-185). backward runs the fused
     implicit-diff kernel (ILQRSolve.backward semantics, controller.py:68-133):
     gradients w.r.t. x0, C, c, C_final, c_final, x_ref, u_ref.
+    solver_cfg["nx"] == 13 selects the 13-state rotor-thrust model.
     """
 
     @staticmethod
     def forward(ctx, x0, C_bt, c_bt, C_final, c_final, x_ref, u_ref, solver_cfg):
-        out = _nat.solve(
+        r13 = solver_cfg.get("nx", _nat.NX) == _nat.NX13
+        ctx.r13 = r13
+        out = (_nat.rotor13_solve if r13 else _nat.solve)(
             _f32(x0), _f32(solver_cfg["U_init"]), _f32(C_bt), _f32(c_bt), _f32(C_final),
             _f32(c_final), _f32(x_ref), _f32(u_ref), solver_cfg.get("u_min"), solver_cfg.get("u_max"),
             dt=solver_cfg["dt"], max_iter=solver_cfg["lqr_iter"], reg_eps=solver_cfg["eps"],
@@ -154,8 +161,9 @@ class DroneMPCFunction(torch.autograd.Function):
             return (None,) * 8
         gX = torch.zeros_like(X) if grad_X is None else grad_X.to(torch.float32).contiguous()
         gU = torch.zeros_like(U) if grad_U is None else grad_U.to(torch.float32).contiguous()
-        g = _nat.backward(X, U, C_bt, gX, gU, C_final=C_final, x_ref=x_ref, tight=tight,
-                          dt=ctx.dt, reg_eps=ctx.reg_eps, need=want)
+        bwd = _nat.rotor13_backward if ctx.r13 else _nat.backward
+        g = bwd(X, U, C_bt, gX, gU, C_final=C_final, x_ref=x_ref, tight=tight,
+                dt=ctx.dt, reg_eps=ctx.reg_eps, need=want)
         return tuple(g.get(nm) for nm in names) + (None,)
 
 
@@ -219,6 +227,8 @@ class FastMPC(nn.Module):
     Only u_lower/u_upper/u_init/lqr_iter/eps/backprop influence the solve, as
     in the reference; the extra keyword `alphas` selects the line-search step
     sizes (default DiffMPC's (1, .8, .5, .2, .1), or ACMPC_DIFFMPC_ALPHAS).
+    n_state selects the model: 10 is the reference's CTBR quadrotor, 13 the
+    rotor-thrust rigid body (four rotor thrusts in [0, 1]; dense QuadCost only).
     """
 
     def __init__(self, n_state: int, n_ctrl: int, T: int, u_lower: Optional[Tensor] = None,
@@ -230,8 +240,8 @@ class FastMPC(nn.Module):
                  slew_rate_penalty: Optional[float] = None, prev_ctrl: Optional[Tensor] = None,
                  alphas=None, **kwargs):
         super().__init__()
-        if n_state != _nat.NX or n_ctrl != _nat.NU:
-            raise ValueError(f"the solver's model has n_state={_nat.NX}, n_ctrl={_nat.NU}")
+        if n_state not in (_nat.NX, _nat.NX13) or n_ctrl != _nat.NU:
+            raise ValueError(f"the solver's models have n_state {_nat.NX} or {_nat.NX13} and n_ctrl={_nat.NU}")
         self.n_state = n_state
         self.n_ctrl = n_ctrl
         self.T = T
@@ -281,10 +291,13 @@ class FastMPC(nn.Module):
         dt = getattr(dx, "dt", 0.02)
         self._get_ext()
         sigm = isinstance(cost, SigmoidQuadCost)
+        r13 = nx == _nat.NX13
+        if sigm and r13:
+            raise ValueError("SigmoidQuadCost builds the 10-state policy's costs; use QuadCost with n_state=13")
         if not sigm:
             C_bt, c_bt = _normalize_cost(cost.C, cost.c, B, T, n, device, dtype)
         u_min, u_max = self._get_bounds(device, dtype)
-        U_init = _normalize_init(self.u_init, B, T, nu, device, dtype)
+        U_init = _normalize_init(self.u_init, B, T, nu, device, dtype, nx)
         x0 = x_init.float().contiguous()
         cfg = {"U_init": U_init, "u_min": u_min, "u_max": u_max, "dt": float(dt),
                "lqr_iter": self.lqr_iter, "eps": self.eps, "converge_tol": 1e-6,
@@ -303,9 +316,10 @@ class FastMPC(nn.Module):
             X, U = DroneMPCFunction.apply(x0, C_bt, c_bt, None, None, None, None, cfg)
         else:
             with torch.inference_mode():
-                out = _nat.solve(x0, U_init, C_bt, c_bt, None, None, None, None, u_min, u_max,
-                                 dt=float(dt), max_iter=self.lqr_iter, reg_eps=self.eps,
-                                 converge_tol=1e-6, alphas=self._alphas())
+                out = (_nat.rotor13_solve if r13 else _nat.solve)(
+                    x0, U_init, C_bt, c_bt, None, None, None, None, u_min, u_max,
+                    dt=float(dt), max_iter=self.lqr_iter, reg_eps=self.eps,
+                    converge_tol=1e-6, alphas=self._alphas())
             X, U = out["X"], out["U"]
         x_out = X.permute(1, 0, 2).contiguous()
         u_out = U.permute(1, 0, 2).contiguous()

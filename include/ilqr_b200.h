@@ -254,6 +254,67 @@ int ilqr_b200_implicit_diff_assembly_f32(
     float* grad_C, float* grad_c, float* grad_x0, float* grad_x_ref,
     float* grad_u_ref, float* grad_C_final, float* grad_c_final, cudaStream_t stream);
 
+/*
+ * ---------------------------------------------------------------------------
+ * 13-state rotor-thrust quadrotor. The reference's extension hard-codes the
+ * 10-state CTBR model (cpp/drone_ilqr_ext.cpp:687-688); its DiffMPC solver
+ * takes any model as f_dyn and linearises it by autodiff
+ * (DifferentialMPC/controller.py:147-160, 607-615). These entry points are
+ * that solver (same semantics as the 10-state entry points above) on the
+ * rigid body x = [p (3), q (4, wxyz), v (3), w (3)] with four rotor thrusts
+ * u in [0, 1] x 8.5 N, mass 0.75 kg, arm 0.15 m (X layout), inertia
+ * diag(2.5e-3, 2.5e-3, 4.5e-3), explicit Euler step. tau = [x; u] has 17
+ * entries: C [B,T,17,17], c [B,T,17], C_final [B,17,17], c_final [B,17],
+ * x_ref [B,T+1,13], u_ref [B,T,4], X [B,T+1,13], U [B,T,4].
+ * ---------------------------------------------------------------------------
+ */
+
+/* Device workspace of ilqr_b200_rotor13_solve_f32 (depends on n_alpha). */
+int ilqr_b200_rotor13_solve_workspace_size(int64_t B, int32_t T, int32_t n_alpha, size_t* bytes);
+
+/*
+ * Batched solve on the rotor model: arguments, results and the per-element
+ * decision outputs as ilqr_b200_solve_f32 (DiffMPC solve_step,
+ * controller.py:303-435), with 13-state shapes. The workspace must be
+ * 16-byte aligned. C needs no alignment.
+ */
+int ilqr_b200_rotor13_solve_f32(
+    const float* x0, const float* U_init, const float* C, const float* c,
+    const float* C_final, const float* c_final, const float* x_ref, const float* u_ref,
+    const float* u_min, const float* u_max,
+    int64_t B, int32_t T, float dt, int32_t max_iter, float reg_eps, float converge_tol,
+    const float* alphas, int32_t n_alpha, const int8_t* forced_trace,
+    float* X, float* U, uint8_t* tight_mask,
+    int8_t* trace, int32_t* iters, uint32_t* elem_status, float* best_cost,
+    int32_t* stall_iter, float* stall_gap,
+    void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* Device workspace of ilqr_b200_rotor13_backward_f32. */
+int ilqr_b200_rotor13_backward_workspace_size(int64_t B, int32_t T, size_t* bytes);
+
+/*
+ * Implicit-diff backward on the rotor model at a solved (X, U): as
+ * ilqr_b200_backward_f32 (ILQRSolve.backward / _zero_constrained_lqr,
+ * controller.py:68-133, 1006-1131) with 13-state shapes; every output may be
+ * NULL. u_ref is accepted for symmetry and not read.
+ */
+int ilqr_b200_rotor13_backward_f32(
+    const float* X, const float* U, const float* C, const float* C_final,
+    const float* x_ref, const float* u_ref, const uint8_t* tight_mask,
+    const float* grad_X, const float* grad_U,
+    int64_t B, int32_t T, float dt, float reg_eps,
+    float* grad_x0, float* grad_C, float* grad_c, float* grad_C_final,
+    float* grad_c_final, float* grad_x_ref, float* grad_u_ref,
+    void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* One rotor-model step x_next = x + dt f(x, u) for n states [n,13], [n,4]. */
+int ilqr_b200_rotor13_dynamics_f32(const float* x, const float* u, int64_t n, float dt,
+                                   float* x_next, cudaStream_t stream);
+
+/* Rotor-model Jacobians A [B,T,13,13], B [B,T,13,4] at (X_t, U_t), t < T. */
+int ilqr_b200_rotor13_linearize_f32(const float* X, const float* U, int64_t B, int32_t T, float dt,
+                                    float* A, float* Bm, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -14,3 +14,4 @@ tests/test_oracle_golden.py.
 """
 
 from .diffmpc_oracle import *  # noqa: F401,F403
+from .rotor13_model import *  # noqa: F401,F403

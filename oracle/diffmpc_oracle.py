@@ -157,23 +157,42 @@ def drone_jacobian(x, u, dt, mass=MASS):
     return A, Bm
 
 
-def rollout(x0, U, dt):
+class Model:
+    """A discrete dynamics model as the solver sees it (DiffMPC's f_dyn and
+    f_dyn_jac, controller.py:147-160): step(x [B,nx], u [B,nu], dt) -> x_next
+    and jacobian(x, u, dt) -> (A [B,nx,nx], B [B,nx,nu])."""
+
+    def __init__(self, name, nx, nu, step, jacobian):
+        self.name, self.nx, self.nu = name, nx, nu
+        self.step, self.jacobian = step, jacobian
+
+    def __repr__(self):
+        return f"Model({self.name}, nx={self.nx}, nu={self.nu})"
+
+
+DRONE10 = Model("drone_ctbr10", NX, NU, drone_step, drone_jacobian)
+
+
+def rollout(x0, U, dt, model=None):
     """controller.py:578-603 (open-loop rollout)."""
+    model = model or DRONE10
     nb, T, _ = U.shape
-    X = np.empty((nb, T + 1, NX), dtype=x0.dtype)
+    X = np.empty((nb, T + 1, model.nx), dtype=x0.dtype)
     X[:, 0] = x0
     xt = x0
     for t in range(T):
-        xt = drone_step(xt, U[:, t], dt)
+        xt = model.step(xt, U[:, t], dt)
         X[:, t + 1] = xt
     return X
 
 
-def linearize(X, U, dt):
-    """controller.py:616-622 (ANALYTIC branch)."""
+def linearize(X, U, dt, model=None):
+    """controller.py:607-622: the model's Jacobian at every (X_t, U_t)."""
+    model = model or DRONE10
+    nx, nu = model.nx, model.nu
     nb, T = U.shape[:2]
-    A, Bm = drone_jacobian(X[:, :-1].reshape(-1, NX), U.reshape(-1, NU), dt)
-    return A.reshape(nb, T, NX, NX), Bm.reshape(nb, T, NX, NU)
+    A, Bm = model.jacobian(X[:, :-1].reshape(-1, nx), U.reshape(-1, nu), dt)
+    return A.reshape(nb, T, nx, nx), Bm.reshape(nb, T, nx, nu)
 
 
 # --------------------------------------------------------------------------
@@ -189,7 +208,7 @@ def objective(X, U, x_ref, u_ref, C, c, C_f, c_f):
     run_q = np.einsum("bti,btij,btj->b", tau, C, tau).astype(dtype)
     run_l = np.einsum("bti,bti->b", c, tau).astype(dtype)
     tauN = np.concatenate([X[:, -1] - x_ref[:, -1],
-                           np.zeros((X.shape[0], NU), dtype=dtype)], axis=-1)
+                           np.zeros((X.shape[0], U.shape[-1]), dtype=dtype)], axis=-1)
     fin_q = np.einsum("bi,bij,bj->b", tauN, C_f, tauN).astype(dtype)
     fin_l = np.einsum("bi,bi->b", c_f, tauN).astype(dtype)
     return (half * run_q + run_l) + (half * fin_q + fin_l)
@@ -201,11 +220,12 @@ def quadraticize(X, U, x_ref, u_ref, C, c, C_f, c_f):
     T = U.shape[1]
     tau = np.concatenate([X[:, :T] - x_ref[:, :T], U - u_ref], axis=-1)
     l_tau = np.einsum("btij,btj->bti", C, tau).astype(dtype) + c
+    nx = X.shape[-1]
     tauN = np.concatenate([X[:, -1] - x_ref[:, -1],
-                           np.zeros((X.shape[0], NU), dtype=dtype)], axis=-1)
+                           np.zeros((X.shape[0], U.shape[-1]), dtype=dtype)], axis=-1)
     lN = np.einsum("bij,bj->bi", C_f, tauN).astype(dtype) + c_f
-    return (l_tau[..., :NX], l_tau[..., NX:], C[..., :NX, :NX],
-            C[..., :NX, NX:], C[..., NX:, NX:], lN[..., :NX], C_f[..., :NX, :NX])
+    return (l_tau[..., :nx], l_tau[..., nx:], C[..., :nx, :nx],
+            C[..., :nx, nx:], C[..., nx:, nx:], lN[..., :nx], C_f[..., :nx, :nx])
 
 
 # --------------------------------------------------------------------------
@@ -289,16 +309,17 @@ def riccati(A, Bm, l_x, l_u, l_xx, l_xu, l_uu, l_xN, l_xxN, reg, batch_fallback=
 
     Q_uu carries reg*I once; the gain solve adds reg*I a second time
     (controller.py:706, :711); V, v use the once-regularised Q_uu.
-    Returns K [B,T,4,10], k [B,T,4], and a per-element flag set where a
+    Returns K [B,T,nu,nx], k [B,T,nu], and a per-element flag set where a
     Cholesky failed and the SVD fallback was used.
     """
     dtype = A.dtype
-    nb, T = A.shape[:2]
-    I_nu = np.eye(NU, dtype=dtype)[None] * dtype.type(reg)
+    nb, T, nx = A.shape[:3]
+    nu = Bm.shape[-1]
+    I_nu = np.eye(nu, dtype=dtype)[None] * dtype.type(reg)
     V = l_xxN.copy()
     v = l_xN.copy()
-    K = np.empty((nb, T, NU, NX), dtype=dtype)
-    k = np.empty((nb, T, NU), dtype=dtype)
+    K = np.empty((nb, T, nu, nx), dtype=dtype)
+    k = np.empty((nb, T, nu), dtype=dtype)
     chol_fail = np.zeros(nb, dtype=bool)
     for t in reversed(range(T)):
         At, Bt = A[:, t], Bm[:, t]
@@ -309,7 +330,7 @@ def riccati(A, Bm, l_x, l_u, l_xx, l_xu, l_uu, l_xN, l_xxN, reg, batch_fallback=
         Q_uu = l_uu[:, t] + (_mT(Bt) @ V) @ Bt + I_nu
         q_x = l_x[:, t] + (AtT @ v[..., None])[..., 0]
         q_u = l_u[:, t] + (_mT(Bt) @ v[..., None])[..., 0]
-        Q_uu_reg = Q_uu + dtype.type(reg) * np.eye(NU, dtype=dtype)[None]
+        Q_uu_reg = Q_uu + dtype.type(reg) * np.eye(nu, dtype=dtype)[None]
         Kt, kt, fb = robust_gain_solve(Q_uu_reg, Q_ux, q_u, batch_fallback)
         chol_fail |= fb
         K[:, t] = Kt
@@ -326,13 +347,15 @@ def riccati(A, Bm, l_x, l_u, l_xx, l_xu, l_uu, l_xN, l_xxN, reg, batch_fallback=
 # --------------------------------------------------------------------------
 
 def line_search(x0, Xn, Un, K, k, x_ref, u_ref, C, c, C_f, c_f, u_min, u_max,
-                alphas, dt):
+                alphas, dt, model=None):
     """evaluate_alphas_batch_optimized (controller.py:437-533).
 
     u_t = U_t + a*k_t + a*(K_t (x_t - X_t)), clamped by max(., u_min) then
     min(., u_max) (controller.py:486-490). Returns candidates
-    Xc [B,nA,T+1,10], Uc [B,nA,T,4], costs [B,nA].
+    Xc [B,nA,T+1,nx], Uc [B,nA,T,nu], costs [B,nA].
     """
+    model = model or DRONE10
+    NX, NU = model.nx, model.nu
     dtype = x0.dtype
     nb = x0.shape[0]
     T = Un.shape[1]
@@ -353,7 +376,7 @@ def line_search(x0, Xn, Un, K, k, x_ref, u_ref, C, c, C_f, c_f, u_min, u_max,
         if u_max is not None:
             u = np.where(np.isnan(u), u, np.minimum(u, u_max))
         Uc[:, :, t] = u
-        x = drone_step(x.reshape(-1, NX), u.reshape(-1, NU), dt).reshape(nb, na, NX)
+        x = model.step(x.reshape(-1, NX), u.reshape(-1, NU), dt).reshape(nb, na, NX)
         Xc[:, :, t + 1] = x
     rep = lambda arr: np.repeat(arr, na, axis=0)
     costs = objective(Xc.reshape(nb * na, T + 1, NX), Uc.reshape(nb * na, T, NU),
@@ -391,7 +414,7 @@ def tight_mask(U, u_min, u_max, atol=1e-7, rtol=1e-5):
 def solve(x0, U_init, C, c, C_f=None, c_f=None, x_ref=None, u_ref=None,
           u_min=None, u_max=None, dt=0.05, max_iter=10, reg=1e-6,
           converge_tol=1e-6, alphas=DEFAULT_ALPHAS, forced=None,
-          dtype=np.float32, reference_batch=False):
+          dtype=np.float32, reference_batch=False, model=None):
     """DifferentiableMPCController.solve_step (controller.py:303-435).
 
     Inputs are [B,...] arrays (C_f, c_f, x_ref, u_ref default to zeros, as on
@@ -400,8 +423,12 @@ def solve(x0, U_init, C, c, C_f=None, c_f=None, x_ref=None, u_ref=None,
     every iteration, and a Cholesky failure anywhere at a time step switches
     the whole batch to the SVD solve (controller.py:745-760 under vmap). Returns a dict with X, U, trace, best_cost, iters
     (iterations each element ran), converged (the reference's global flag),
-    tight (tight mask at the final U) and chol_fail.
+    tight (tight mask at the final U) and chol_fail. ``model`` is the
+    dynamics (default: the reference's 10-state CTBR quadrotor).
     """
+    model = model or DRONE10
+    NX, NU = model.nx, model.nu
+    N = NX + NU
     dtype = np.dtype(dtype)
     x0 = _f(x0, dtype)
     nb = x0.shape[0]
@@ -416,7 +443,7 @@ def solve(x0, U_init, C, c, C_f=None, c_f=None, x_ref=None, u_ref=None,
     u_min = None if u_min is None else _f(u_min, dtype)
     u_max = None if u_max is None else _f(u_max, dtype)
 
-    X = rollout(x0, U, dt)
+    X = rollout(x0, U, dt, model)
     best = objective(X, U, x_ref, u_ref, C, c, C_f, c_f)
     active = np.ones(nb, dtype=bool)
     trace = np.full((nb, max_iter), NOT_RUN, dtype=np.int8)
@@ -437,13 +464,13 @@ def solve(x0, U_init, C, c, C_f=None, c_f=None, x_ref=None, u_ref=None,
         sub = lambda arr: arr[ids]
         l_x, l_u, l_xx, l_xu, l_uu, l_xN, l_xxN = quadraticize(
             sub(X), sub(U), sub(x_ref), sub(u_ref), sub(C), sub(c), sub(C_f), sub(c_f))
-        A, Bm = linearize(sub(X), sub(U), dt)
+        A, Bm = linearize(sub(X), sub(U), dt, model)
         K, k, cf = riccati(A, Bm, l_x, l_u, l_xx, l_xu, l_uu, l_xN, l_xxN, reg,
                            batch_fallback=reference_batch)
         chol_fail[ids] |= cf
         Xc, Uc, costs = line_search(sub(x0), sub(X), sub(U), K, k, sub(x_ref), sub(u_ref),
                                     sub(C), sub(c), sub(C_f), sub(c_f), u_min, u_max,
-                                    alphas, dt)
+                                    alphas, dt, model)
         j = argmin_nan_first(costs)
         new = costs[np.arange(len(ids)), j]
         if forced is None:
@@ -502,10 +529,11 @@ def zero_constrained_lqr(A, Bm, H_xx, H_uu, H_xu, grad_x, grad_u, tight,
     diagonal plus a (1e-8*reg)*I ridge; Q_ux tight rows and q_u tight entries
     zeroed; V and v are then updated with the UNMASKED Q_uu, Q_ux, q_u.
     Sweep: dU = K dX + k, dX_{t+1} = A dX + B dU, dX_0 = 0.
-    Returns dX [B,T+1,10], dU [B,T,4], v0 [B,10], K, k.
+    Returns dX [B,T+1,nx], dU [B,T,nu], v0 [B,nx], K, k.
     """
     dtype = A.dtype
-    nb, T = A.shape[:2]
+    nb, T, NX = A.shape[:3]
+    NU = Bm.shape[-1]
     V = H_xx_final.copy()
     v = grad_x_final.copy()
     eye = np.eye(NU, dtype=dtype)[None]
@@ -554,7 +582,7 @@ def zero_constrained_lqr(A, Bm, H_xx, H_uu, H_xu, grad_x, grad_u, tight,
 
 
 def backward(X, U, C, C_f, x_ref, u_ref, tight, grad_X, grad_U, dt, reg,
-             dtype=np.float32):
+             dtype=np.float32, model=None):
     """ILQRSolve.backward (controller.py:68-133) at a solved (X, U).
 
     grad_C = -1/2 (dtau (x) z + z (x) dtau) with z = [X_t; U_t] (not tau);
@@ -562,6 +590,9 @@ def backward(X, U, C, C_f, x_ref, u_ref, tight, grad_X, grad_U, dt, reg,
     grad_uref = dU; grad_C_final xx block = -1/2 (dX_T (x) e + e (x) dX_T),
     e = X_T - x_ref_T; grad_c_final[:nx] = -dX_T.
     """
+    model = model or DRONE10
+    NX, NU = model.nx, model.nu
+    N = NX + NU
     dtype = np.dtype(dtype)
     X = _f(X, dtype)
     U = _f(U, dtype)
@@ -572,7 +603,7 @@ def backward(X, U, C, C_f, x_ref, u_ref, tight, grad_X, grad_U, dt, reg,
     u_ref = np.zeros((nb, T, NU), dtype) if u_ref is None else _f(u_ref, dtype)
     gX = _f(grad_X, dtype)
     gU = _f(grad_U, dtype)
-    A, Bm = linearize(X, U, dt)
+    A, Bm = linearize(X, U, dt, model)
     H_xx, H_xu, H_uu = C[..., :NX, :NX], C[..., :NX, NX:], C[..., NX:, NX:]
     dX, dU, v0, K, k = zero_constrained_lqr(
         A, Bm, H_xx, H_uu, H_xu, -gX[:, :-1], -gU, tight, -gX[:, -1],
@@ -744,7 +775,7 @@ def pnqp4(H, q, lower, upper, x_init=None):
 
 
 __all__ = [
-    "NX", "NU", "N", "MASS", "GRAV_Z", "NOT_RUN", "DEFAULT_ALPHAS",
+    "NX", "NU", "N", "MASS", "GRAV_Z", "NOT_RUN", "DEFAULT_ALPHAS", "Model", "DRONE10",
     "drone_step", "drone_jacobian", "rollout", "linearize", "objective",
     "quadraticize", "chol4", "chol_solve", "riccati", "line_search",
     "argmin_nan_first", "tight_mask", "solve", "global_converged_flag",

@@ -71,31 +71,44 @@ def import_policy_cost_builder(ref_root):
 
 
 def run_reference(drone, DM, inp, T, max_iter, alphas, dt, bounds, gX, gU,
-                  extra=None, reg=1e-6):
+                  extra=None, reg=1e-6, model=None, dtype=None):
+    """Run the reference DiffMPC fwd+bwd and record its decisions. `model`
+    None is the reference's DroneDx with its analytic Jacobian; otherwise a
+    dict(nx, f_dyn, u_min, u_max) run through GradMethod.AUTO_DIFF
+    (controller.py:607-615), the controller's model-generic path. `dtype`
+    (a torch dtype) runs the reference in that precision instead of float32."""
     import torch
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     B = inp["x0"].shape[0]
-    n = 14
-    dx = drone.DroneDx(device="cpu")
-    dx.dt = dt
-    f_dyn = lambda x, u, _dt: dx(x, u)
-    f_jac = lambda x, u, _dt: dx.grad_input(x, u)
-    cost = DM.GeneralQuadCost(nx=10, nu=4, C=torch.zeros(1, T, n, n), c=torch.zeros(1, T, n),
+    if model is None:
+        nx = 10
+        dx = drone.DroneDx(device="cpu")
+        dx.dt = dt
+        f_dyn = lambda x, u, _dt: dx(x, u)
+        f_jac = lambda x, u, _dt: dx.grad_input(x, u)
+        gm = DM.GradMethod.ANALYTIC
+        lo, hi = wl.U_MIN, wl.U_MAX
+    else:
+        nx, f_dyn, f_jac = model["nx"], model["f_dyn"], None
+        gm = DM.GradMethod.AUTO_DIFF
+        lo, hi = model["u_min"], model["u_max"]
+    n = nx + 4
+    cost = DM.GeneralQuadCost(nx=nx, nu=4, C=torch.zeros(1, T, n, n), c=torch.zeros(1, T, n),
                               C_final=torch.zeros(1, n, n), c_final=torch.zeros(1, n), device="cpu")
-    u_min = torch.tensor(wl.U_MIN) if bounds else None
-    u_max = torch.tensor(wl.U_MAX) if bounds else None
+    u_min = torch.tensor(lo, dtype=dtype) if bounds else None
+    u_max = torch.tensor(hi, dtype=dtype) if bounds else None
     ctrl = DM.DifferentiableMPCController(
         f_dyn=f_dyn, f_dyn_jac=f_jac, total_time=T * dt, step_size=dt, horizon=T,
         cost_module=cost, u_min=u_min, u_max=u_max, reg_eps=reg,
-        grad_method=DM.GradMethod.ANALYTIC, max_iter=max_iter, exit_unconverged=False,
+        grad_method=gm, max_iter=max_iter, exit_unconverged=False,
         detach_unconverged=False, device="cpu", verbose=0, use_vmap_line_search=False,
         alphas=tuple(alphas))
-    t = lambda a: a if isinstance(a, torch.Tensor) else torch.tensor(a).clone().requires_grad_(True)
+    t = lambda a: a if isinstance(a, torch.Tensor) else torch.tensor(a, dtype=dtype).clone().requires_grad_(True)
     x0, C, c = t(inp["x0"]), t(inp["C"]), t(inp["c"])  # C, c may come from a construction graph
     ex = extra or {}
     C_f = t(ex.get("C_final", np.zeros((B, n, n), np.float32)))
     c_f = t(ex.get("c_final", np.zeros((B, n), np.float32)))
-    x_ref = t(ex.get("x_ref", np.zeros((B, T + 1, 10), np.float32)))
+    x_ref = t(ex.get("x_ref", np.zeros((B, T + 1, nx), np.float32)))
     u_ref = t(ex.get("u_ref", np.zeros((B, T, 4), np.float32)))
     cost.C, cost.c, cost.C_final, cost.c_final = C, c, C_f, c_f
     cost.set_reference(x_ref, u_ref)
@@ -118,10 +131,10 @@ def run_reference(drone, DM, inp, T, max_iter, alphas, dt, bounds, gX, gU,
 
     ctrl.evaluate_alphas_batch_optimized = eval_hook
     cost.objective = obj_hook
-    X, U = ctrl(x0, U_init=torch.tensor(inp["U_init"]))
+    X, U = ctrl(x0, U_init=torch.tensor(inp["U_init"], dtype=dtype))
     converged = bool(ctrl.converged)
     tight = ctrl.tight_mask_last.detach().numpy().copy()
-    L = (X * torch.tensor(gX)).sum() + (U * torch.tensor(gU)).sum()
+    L = (X * torch.tensor(gX, dtype=dtype)).sum() + (U * torch.tensor(gU, dtype=dtype)).sum()
     L.backward()
 
     # Reconstruct the decision trace exactly as solve_step decides. A rejected

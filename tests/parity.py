@@ -32,6 +32,11 @@ U_MAX = np.array([34.0, 10.0, 10.0, 4.0], np.float32)
 # checked separately.
 STRICT_CASES = ("cfg1_b16_t5", "cfg2_b32_t10", "cfg3_b16_t20", "dense_b8_t6", "asym_b8_t4",
                 "nobox_b8_t5", "b1_t1", "indef_b8_t4")
+# Rotor13 (13-state rotor-thrust model) cases: made by running the reference
+# DiffMPC with GradMethod.AUTO_DIFF on a model written for it
+# (tests/golden/make_rotor13_golden.py); the solver is pinned, the model is not.
+R13_CASES = ("r13_cfg1_b16_t5", "r13_cfg2_b32_t10", "r13_cfg3_b16_t20", "r13_dense_b8_t6",
+             "r13_nobox_b8_t5")
 GRAD_KEYS = ("grad_x0", "grad_C", "grad_c", "grad_C_final", "grad_c_final", "grad_xref", "grad_uref")
 
 
@@ -62,10 +67,18 @@ def max_rel(a, b):
 def case_kwargs(d):
     """Solver arguments of a golden case (numpy)."""
     bounds = bool(d["bounds"])
+    lo, hi = d.get("u_min", U_MIN), d.get("u_max", U_MAX)
     return dict(C_f=d.get("C_final"), c_f=d.get("c_final"), x_ref=d.get("x_ref"),
-                u_ref=d.get("u_ref"), u_min=U_MIN if bounds else None,
-                u_max=U_MAX if bounds else None, dt=float(d["dt"]), max_iter=int(d["max_iter"]),
+                u_ref=d.get("u_ref"), u_min=lo if bounds else None,
+                u_max=hi if bounds else None, dt=float(d["dt"]), max_iter=int(d["max_iter"]),
                 reg=float(d["reg"]), alphas=tuple(float(a) for a in d["alphas"]))
+
+
+def case_model(d):
+    """The oracle model a golden case was made with (10-state CTBR unless
+    the case says rotor13)."""
+    import oracle as O
+    return O.ROTOR13 if str(d.get("model", "")) == "rotor13" else O.DRONE10
 
 
 def reference_best_before(d):
@@ -131,3 +144,28 @@ def same_decisions(trace, ref_trace):
                 out[b] = False
                 break
     return out
+
+
+# Rounding-dominated problems (the 13-state rotor model): two fp32
+# realisations of the same decisions -- the reference's and the oracle's --
+# scatter around the fp64 solution by up to O(1) on ill-conditioned elements
+# (measured: their per-element errors against fp64 differ by up to ~12x).
+# An fp32 implementation passes if, per element, its error against the fp64
+# solution is within SPREAD_FACTOR times the larger of the two reference
+# realisations' errors, and it meets the plain bar wherever both realisations
+# are within WELL_CONDITIONED of fp64.
+SPREAD_FACTOR = 30.0
+WELL_CONDITIONED = 1e-5
+
+
+def rounding_spread(ref32, oracle32, exact64):
+    """Per-element fp32 rounding scale: max(rel(ref32, fp64), rel(oracle32, fp64))."""
+    return np.maximum(rel_per_elem(ref32, exact64), rel_per_elem(oracle32, exact64))
+
+
+def within_rounding(a, ref32, exact64, spread, tol):
+    """Failures (element, error vs fp64, spread) of the rounding-aware bar."""
+    e64 = rel_per_elem(a, exact64)
+    e32 = rel_per_elem(a, ref32)
+    bad = (e64 > np.maximum(tol, SPREAD_FACTOR * spread)) | ((spread <= WELL_CONDITIONED) & (e32 > tol))
+    return [(int(b), float(e64[b]), float(e32[b]), float(spread[b])) for b in np.nonzero(bad)[0]]

@@ -51,6 +51,59 @@ def test_workspace_sizes():
     assert L.ilqr_b200_solve_workspace_size(4, 0, ctypes.byref(n)) == 1
 
 
+def test_rotor13_workspace_sizes():
+    """Rotor13 solve: (n_alpha + 1) slots of (T + 1) records of 20 floats plus
+    K_t columns and k_t ([T][14] float4) per element; backward: the gains."""
+    L = nat.lib()
+    n = ctypes.c_size_t()
+    assert L.ilqr_b200_rotor13_solve_workspace_size(16384, 20, 5, ctypes.byref(n)) == 0
+    assert n.value == (6 * 21 * 20 + 20 * 14 * 4) * 16384 * 4
+    assert L.ilqr_b200_rotor13_solve_workspace_size(3, 4, 8, ctypes.byref(n)) == 0
+    assert n.value == (9 * 5 * 20 + 4 * 56) * 3 * 4
+    assert L.ilqr_b200_rotor13_backward_workspace_size(33, 5, ctypes.byref(n)) == 0
+    assert n.value == 5 * 56 * 33 * 4
+    assert L.ilqr_b200_rotor13_solve_workspace_size(4, 5, 9, ctypes.byref(n)) == 1
+    assert L.ilqr_b200_rotor13_solve_workspace_size(4, 0, 5, ctypes.byref(n)) == 1
+
+
+def test_rotor13_argument_validation_without_gpu():
+    L = nat.lib()
+    f = L.ilqr_b200_rotor13_solve_f32
+    assert f(*_solve_args(n_alpha=0)) == 1
+    assert f(*_solve_args(n_alpha=9)) == 1
+    assert f(*_solve_args(x0=None)) == 1
+    assert f(*_solve_args(u_min=ctypes.c_void_p(0x10000))) == 1
+    assert f(*_solve_args(ws_bytes=16)) == 3
+    assert f(*_solve_args(ws=ctypes.c_void_p(0x10004))) == 2      # workspace misaligned
+    assert f(*_solve_args(B=0)) == 0
+    fake = ctypes.c_void_p(0x10000)
+    args = [fake, fake, fake, None, None, None, None, fake, fake, 4, 5, 0.05, 1e-6,
+            fake, fake, fake, None, None, None, None, fake, 1 << 30, None]
+    g = L.ilqr_b200_rotor13_backward_f32
+    bad = list(args); bad[0] = None
+    assert g(*bad) == 1
+    bad = list(args); bad[-2] = 0
+    assert g(*bad) == 3
+
+
+def test_rotor13_surface_without_gpu():
+    """FastMPC(13, 4, T) selects the rotor model, defaults U_init to the
+    hover fraction, refuses SigmoidQuadCost and CPU tensors."""
+    B, T = 2, 3
+    m = mpc_compat.FastMPC(13, 4, T, lqr_iter=2)
+    init = mpc_compat._normalize_init(None, B, T, 4, torch.device("cpu"), torch.float32, 13)
+    assert torch.allclose(init, torch.full((B, T, 4), nat.HOVER_U13))
+    x = torch.zeros(B, 13)
+    x[:, 3] = 1
+    with pytest.raises(ValueError):
+        m(x, mpc_compat.SigmoidQuadCost(torch.zeros(B, 28 * T)), type("Dx", (), {"dt": 0.05})())
+    C = torch.eye(17).expand(T, B, 17, 17)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        m(x, mpc_compat.QuadCost(C, None), type("Dx", (), {"dt": 0.05})())
+    with pytest.raises(ValueError):
+        mpc_compat.FastMPC(12, 4, T)
+
+
 def _solve_args(**over):
     fake = ctypes.c_void_p(0x10000)
     a = dict(x0=fake, U_init=fake, C=fake, c=fake, C_final=None, c_final=None, x_ref=None,
