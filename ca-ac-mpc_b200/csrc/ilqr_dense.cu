@@ -106,19 +106,23 @@ __device__ __forceinline__ void store_rec(float4* r, const float* x, const float
 
 // 1/2 tau^T C tau and c^T tau of one step, accumulated over rows in index
 // order (the costs the line search compares and the initial objective).
+// ts is this lane's 17-float shared-memory scratch: the row loop is not
+// unrolled (it would keep 289 loads in flight), so tau_i is read from there.
 __device__ __forceinline__ void step_cost(const float* __restrict__ Ct, const float* __restrict__ ct,
-                                          const float* tau, float& q, float& l) {
+                                          const float* tau, float* ts, float& q, float& l) {
   l = __ldg(ct) * tau[0];
 #pragma unroll
   for (int j = 1; j < NT; ++j) l = fmaf(__ldg(ct + j), tau[j], l);
-  q = 0.0f;
 #pragma unroll
+  for (int j = 0; j < NT; ++j) ts[j] = tau[j];
+  q = 0.0f;
+#pragma unroll 1
   for (int i = 0; i < NT; ++i) {
     const float* row = Ct + i * NT;
     float r = __ldg(row) * tau[0];
 #pragma unroll
     for (int j = 1; j < NT; ++j) r = fmaf(__ldg(row + j), tau[j], r);
-    q = fmaf(tau[i], r, q);
+    q = fmaf(ts[i], r, q);
   }
 }
 
@@ -137,6 +141,67 @@ __device__ __forceinline__ float terminal_cost(const float* __restrict__ Cf, con
     if (cf != nullptr) l = fmaf(__ldg(cf + i), tn[i], l);
   }
   return 0.5f * q + l;
+}
+
+// x = M^-1 b for one 4 x 4 system by Gaussian elimination with partial
+// pivoting (M and b are copies). Returns the smallest and largest pivot
+// magnitudes: a ratio below 1e-12 (or a non-finite pivot) marks M as
+// singular to working precision.
+__device__ __forceinline__ void lu_solve4(const float (&Min)[NU][NU], const float (&bin)[NU], float (&x)[NU],
+                                          float& pmin, float& pmax) {
+  float M[NU][NU], b[NU];
+#pragma unroll
+  for (int i = 0; i < NU; ++i) {
+#pragma unroll
+    for (int j = 0; j < NU; ++j) M[i][j] = Min[i][j];
+    b[i] = bin[i];
+  }
+  pmin = 3.4e38f;
+  pmax = 0.0f;
+#pragma unroll
+  for (int k = 0; k < NU; ++k) {
+    int r = k;
+    float best = fabsf(M[k][k]);
+#pragma unroll
+    for (int i = k + 1; i < NU; ++i) {
+      const float v = fabsf(M[i][k]);
+      if (v > best) {
+        best = v;
+        r = i;
+      }
+    }
+#pragma unroll
+    for (int i = k + 1; i < NU; ++i) {
+      if (i == r) {
+#pragma unroll
+        for (int j = 0; j < NU; ++j) {
+          const float t = M[k][j];
+          M[k][j] = M[i][j];
+          M[i][j] = t;
+        }
+        const float t = b[k];
+        b[k] = b[i];
+        b[i] = t;
+      }
+    }
+    const float piv = M[k][k];
+    pmin = fminf(pmin, fabsf(piv));
+    pmax = fmaxf(pmax, fabsf(piv));
+#pragma unroll
+    for (int i = k + 1; i < NU; ++i) {
+      const float f = M[i][k] / piv;
+#pragma unroll
+      for (int j = k + 1; j < NU; ++j) M[i][j] = M[i][j] - f * M[k][j];
+      b[i] = b[i] - f * b[k];
+    }
+  }
+#pragma unroll
+  for (int i = NU - 1; i >= 0; --i) {
+    float s = b[i];
+#pragma unroll
+    for (int j = i + 1; j < NU; ++j) s = s - M[i][j] * x[j];
+    x[i] = s / M[i][i];
+  }
 }
 
 // Inputs of one Riccati step that differ between the solve and the backward.
@@ -262,11 +327,24 @@ __device__ __forceinline__ bool riccati_step(float* sm, int g, bool rowx, bool l
   Chol4 L;
   const bool ok = chol4(G, L);
   float sol[NU];
-  chol4_solve(L, rhs, sol);
   const bool fb = !ok && live;
-  if (__any_sync(wmask, fb)) {
+  // A failed Cholesky falls back to the inverse: the reference takes an SVD
+  // pseudo-inverse with singular values floored at max / 1e12 in the forward
+  // Riccati (controller.py:758-779) and an LU solve in the masked one
+  // (controller.py:1089-1092). Both equal the LU solve unless the matrix is
+  // singular to that ratio; only then is the SVD inverse formed.
+  bool sing = false;
+  if (ok) {
+    chol4_solve(L, rhs, sol);
+  } else {
+    float pmin, pmax;
+    lu_solve4(G, rhs, sol, pmin, pmax);
+    sing = !MASKED && !(pmin > 1e-12f * pmax);
+  }
+  const bool need_svd = sing && live;
+  if (__any_sync(wmask, need_svd)) {
     float* M = sm + S_SVD;
-    if (fb && g == 0) {
+    if (need_svd && g == 0) {
 #pragma unroll
       for (int a = 0; a < NU; ++a)
 #pragma unroll
@@ -274,7 +352,7 @@ __device__ __forceinline__ bool riccati_step(float* sm, int g, bool rowx, bool l
       svd_inverse4(M, M + 16);
     }
     __syncwarp(wmask);
-    if (fb) {
+    if (need_svd) {
 #pragma unroll
       for (int a = 0; a < NU; ++a) {
         float s = M[16 + a * NU] * rhs[0];
@@ -342,14 +420,16 @@ __device__ __forceinline__ bool riccati_step(float* sm, int g, bool rowx, bool l
 // Lane g writes row g of A_t, B_t (state-row lanes) from the nominal x, u in
 // sm[S_Z].
 __device__ __forceinline__ void jacobian_rows(float* sm, int g, float dt) {
-  if (g < NX) {
-    float a[NX], b[NU];
-    jac_row(g, sm + S_Z, sm + S_Z + NX, dt, a, b);
+  if (g < NX) jac_row(g, sm + S_Z, sm + S_Z + NX, dt, sm + S_A + g * NX, sm + S_B + g * NU);
+}
+
+// v[i] for a lane-dependent i, without a dynamically indexed local array.
+template <int N>
+__device__ __forceinline__ float pick(const float (&v)[N], int i) {
+  float r = v[0];
 #pragma unroll
-    for (int j = 0; j < NX; ++j) sm[S_A + g * NX + j] = a[j];
-#pragma unroll
-    for (int j = 0; j < NU; ++j) sm[S_B + g * NU + j] = b[j];
-  }
+  for (int j = 1; j < N; ++j) r = (i == j) ? v[j] : r;
+  return r;
 }
 
 }  // namespace
@@ -357,7 +437,7 @@ __device__ __forceinline__ void jacobian_rows(float* sm, int g, float dt) {
 // ---------------------------------------------------------------------------
 // Solve (controller.py:303-435)
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(THREADS) dense_solve_kernel(DenseSolveParams p) {
+__global__ void __launch_bounds__(THREADS, 3) dense_solve_kernel(DenseSolveParams p) {
   extern __shared__ float smem[];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -405,7 +485,7 @@ __global__ void __launch_bounds__(THREADS) dense_solve_kernel(DenseSolveParams p
 #pragma unroll
       for (int a = 0; a < NU; ++a) tau[NX + a] = u[a] - uref(t, a);
       float q, l;
-      step_cost(Cb + (int64_t)t * NT * NT, cb + (int64_t)t * NT, tau, q, l);
+      step_cost(Cb + (int64_t)t * NT * NT, cb + (int64_t)t * NT, tau, sm + S_V, q, l);
       sq += q;
       sl += l;
       float xn[NX];
@@ -508,7 +588,9 @@ __global__ void __launch_bounds__(THREADS) dense_solve_kernel(DenseSolveParams p
     // ---- grid line search (controller.py:360-388, 437-533): lane j = step j --
     float mine = 0.0f;
     if (valid && g < p.n_alpha) {
-      const float al = p.alphas[g];
+      float al = p.alphas[0];
+#pragma unroll
+      for (int jj = 1; jj < ILQR_MAX_ALPHAS_DEV; ++jj) al = (g == jj) ? p.alphas[jj] : al;
       const int cs = g < nom ? g : g + 1;
       float x[NX];
 #pragma unroll
@@ -552,7 +634,7 @@ __global__ void __launch_bounds__(THREADS) dense_solve_kernel(DenseSolveParams p
 #pragma unroll
         for (int a = 0; a < NU; ++a) tau[NX + a] = u[a] - uref(t, a);
         float q, l;
-        step_cost(Cb + (int64_t)t * NT * NT, cb + (int64_t)t * NT, tau, q, l);
+        step_cost(Cb + (int64_t)t * NT * NT, cb + (int64_t)t * NT, tau, sm + S_V + g * NT, q, l);
         sq += q;
         sl += l;
         float xn[NX];
@@ -732,8 +814,8 @@ __global__ void __launch_bounds__(THREADS) dense_backward_kernel(DenseBackwardPa
   __syncwarp();
 
   // ---- tangent sweep dU = K dX + k, dX+ = A dX + B dU, and the gradients ------
-  float* dxs = sm + S_VV;  // dX_t [13]
-  if (rowx) dxs[g] = 0.0f;
+  float* dts = sm + S_M;  // dtau_t = [dX_t; dU_t] (17)
+  if (rowx) dts[g] = 0.0f;
   for (int t = 0; t < T; ++t) {
     __syncwarp();
     load_z(t);
@@ -741,7 +823,7 @@ __global__ void __launch_bounds__(THREADS) dense_backward_kernel(DenseBackwardPa
     jacobian_rows(sm, g, dt);
     float dx[NX];
 #pragma unroll
-    for (int j = 0; j < NX; ++j) dx[j] = dxs[j];
+    for (int j = 0; j < NX; ++j) dx[j] = dts[j];
     float du[NU];
     {
       const float4* kc = kws + t * (NX + 1);
@@ -761,8 +843,8 @@ __global__ void __launch_bounds__(THREADS) dense_backward_kernel(DenseBackwardPa
       du[2] = kd[2] + k4.z;
       du[3] = kd[3] + k4.w;
     }
-    __syncwarp();
-    // dX_{t+1} row g
+    if (g < NU) dts[NX + g] = pick(du, g);
+    // dX_{t+1}, row g (A_t row g was written by this lane)
     float dxn = 0.0f;
     if (rowx) {
       float s = sm[S_A + g * NX] * dx[0];
@@ -773,58 +855,43 @@ __global__ void __launch_bounds__(THREADS) dense_backward_kernel(DenseBackwardPa
       for (int a = 1; a < NU; ++a) sb = fmaf(sm[S_B + g * NU + a], du[a], sb);
       dxn = s + sb;
     }
+    __syncwarp();
     if (valid) {
       // dtau = [dX_t; dU_t], z = [X_t; U_t]:
       // grad_C_t = -1/2 (dtau z^T + z dtau^T), grad_c_t = -dtau
-      float z[NT], dz[NT];
-#pragma unroll
-      for (int i = 0; i < NX; ++i) {
-        z[i] = sm[S_Z + i];
-        dz[i] = dx[i];
-      }
-#pragma unroll
-      for (int a = 0; a < NU; ++a) {
-        z[NX + a] = sm[S_Z + NX + a];
-        dz[NX + a] = du[a];
-      }
       const int64_t off = (b * T + t) * NT;
+      const float* z = sm + S_Z;
+      auto grad_row = [&](int i, float* gC) {
+        const float dzi = dts[i], zi = z[i];
+#pragma unroll
+        for (int j = 0; j < NT; ++j) gC[i * NT + j] = -0.5f * (dzi * z[j] + zi * dts[j]);
+      };
       if (p.g_C) {
         float* gC = p.g_C + off * NT;
-        if (rowx) {
-#pragma unroll
-          for (int j = 0; j < NT; ++j) gC[g * NT + j] = -0.5f * (dz[g] * z[j] + z[g] * dz[j]);
-        }
-        if (g < NU) {
-          const int i = NX + g;
-#pragma unroll
-          for (int j = 0; j < NT; ++j) gC[i * NT + j] = -0.5f * (dz[i] * z[j] + z[i] * dz[j]);
-        }
+        if (rowx) grad_row(g, gC);
+        if (g < NU) grad_row(NX + g, gC);
       }
       if (p.g_c) {
-        if (rowx) p.g_c[off + g] = -dz[g];
-        if (g < NU) p.g_c[off + NX + g] = -dz[NX + g];
+        if (rowx) p.g_c[off + g] = -dts[g];
+        if (g < NU) p.g_c[off + NX + g] = -dts[NX + g];
       }
-      if (p.g_xref && rowx) p.g_xref[(b * (T + 1) + t) * NX + g] = dx[g];
-      if (p.g_uref && g < NU) p.g_uref[(b * T + t) * NU + g] = du[g];
+      if (p.g_xref && rowx) p.g_xref[(b * (T + 1) + t) * NX + g] = dts[g];
+      if (p.g_uref && g < NU) p.g_uref[(b * T + t) * NU + g] = dts[NX + g];
     }
-    if (rowx) dxs[g] = dxn;
+    __syncwarp();
+    if (rowx) dts[g] = dxn;
   }
   __syncwarp();
   if (valid) {
     // terminal: grad_C_final xx = -1/2 (dX_T e^T + e dX_T^T), e = X_T - x_ref_T
-    float dxT[NX], eT[NX];
-#pragma unroll
-    for (int j = 0; j < NX; ++j) {
-      dxT[j] = dxs[j];
-      eT[j] = __ldg(Xb + T * NX + j) - (xr ? __ldg(xr + T * NX + j) : 0.0f);
-    }
+    auto eT = [&](int j) { return __ldg(Xb + T * NX + j) - (xr ? __ldg(xr + T * NX + j) : 0.0f); };
     if (p.g_xref && rowx) p.g_xref[(b * (T + 1) + T) * NX + g] = 0.0f;
     if (p.g_Cf) {
       float* gCf = p.g_Cf + b * NT * NT;
       if (rowx) {
+        const float dg = dts[g], eg = eT(g);
 #pragma unroll
-        for (int j = 0; j < NT; ++j)
-          gCf[g * NT + j] = j < NX ? -0.5f * (dxT[g] * eT[j] + eT[g] * dxT[j]) : 0.0f;
+        for (int j = 0; j < NT; ++j) gCf[g * NT + j] = j < NX ? -0.5f * (dg * eT(j) + eg * dts[j]) : 0.0f;
       }
       if (g < NU) {
 #pragma unroll
@@ -832,7 +899,7 @@ __global__ void __launch_bounds__(THREADS) dense_backward_kernel(DenseBackwardPa
       }
     }
     if (p.g_cf) {
-      if (rowx) p.g_cf[b * NT + g] = -dxT[g];
+      if (rowx) p.g_cf[b * NT + g] = -dts[g];
       if (g < NU) p.g_cf[b * NT + NX + g] = 0.0f;
     }
   }

@@ -283,6 +283,7 @@ def robust_gain_solve(Q_uu_reg, Q_ux, q_u, batch_fallback=False):
     reference's fallback is taken by the whole batch at that time step when
     any element fails; here it is taken per failing element (for the others
     the SVD and Cholesky solves agree to rounding times the condition number).
+    A non-finite Q_uu (where the reference's SVD raises) gives NaN gains.
     Returns (K, k, fallback_used[B])."""
     L, ok = chol4(Q_uu_reg)
     K = -chol_solve(L, Q_ux)
@@ -290,6 +291,11 @@ def robust_gain_solve(Q_uu_reg, Q_ux, q_u, batch_fallback=False):
     bad = ~ok
     if batch_fallback and bad.any():
         bad = np.ones_like(bad)
+    nonfinite = bad & ~np.isfinite(Q_uu_reg).all(axis=(-1, -2))
+    if nonfinite.any():
+        K[nonfinite] = np.nan
+        k[nonfinite] = np.nan
+        bad = bad & ~nonfinite
     if bad.any():
         Ub, S, Vh = np.linalg.svd(Q_uu_reg[bad])
         floor = S.max(axis=-1, keepdims=True) / Q_uu_reg.dtype.type(1e12)
@@ -297,7 +303,7 @@ def robust_gain_solve(Q_uu_reg, Q_ux, q_u, batch_fallback=False):
         Q_inv = _mT(Vh) @ (np.eye(S.shape[-1], dtype=S.dtype)[None] / S_reg[:, None, :]) @ _mT(Ub)
         K[bad] = -(Q_inv @ Q_ux[bad])
         k[bad] = -(Q_inv @ q_u[bad][..., None])[..., 0]
-    return K, k, bad
+    return K, k, bad | nonfinite
 
 
 # --------------------------------------------------------------------------
