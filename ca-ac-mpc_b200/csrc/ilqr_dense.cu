@@ -56,6 +56,18 @@ constexpr int S_KF = 608;    // k_t [4]
 constexpr int S_MK = 612;    // Q_uu k + q_u [4]
 constexpr int S_SVD = 616;   // SVD fallback: matrix [16], inverse [16]
 constexpr int S_ELEM = 656;  // floats per element (41 x 16)
+// Outside the Riccati pass the first 404 floats stage one step of a rollout:
+// C_t (289), c_t (17), x_ref_t (13), u_ref_t (4), U_init_t (4), then the
+// nominal record (20) and the K_t columns and k_t (56) as float4s.
+constexpr int L_C = 0;
+constexpr int L_CV = 289;
+constexpr int L_XR = 306;
+constexpr int L_UR = 319;
+constexpr int L_U0 = 323;
+constexpr int L_NSC = 327;   // staged scalars
+constexpr int L_F4 = 328;    // float4 area: record (5), K columns and k (14)
+constexpr int L_NF4 = 19;
+constexpr int L_PF = 21;     // scalar prefetch slots per lane (16 x 21 >= 327)
 
 __device__ __forceinline__ float clampn(float v, float lo, float hi) {
   float r;
@@ -104,25 +116,21 @@ __device__ __forceinline__ void store_rec(float4* r, const float* x, const float
   r[4] = make_float4(u[3], 0.0f, 0.0f, 0.0f);
 }
 
-// 1/2 tau^T C tau and c^T tau of one step, accumulated over rows in index
-// order (the costs the line search compares and the initial objective).
-// ts is this lane's 17-float shared-memory scratch: the row loop is not
-// unrolled (it would keep 289 loads in flight), so tau_i is read from there.
-__device__ __forceinline__ void step_cost(const float* __restrict__ Ct, const float* __restrict__ ct,
-                                          const float* tau, float* ts, float& q, float& l) {
-  l = __ldg(ct) * tau[0];
+// 1/2 tau^T C tau and c^T tau of one step from the staged C_t, c_t,
+// accumulated over rows in index order (the costs the line search compares
+// and the initial objective).
+__device__ __forceinline__ void step_cost_smem(const float* st, const float* tau, float& q, float& l) {
+  l = st[L_CV] * tau[0];
 #pragma unroll
-  for (int j = 1; j < NT; ++j) l = fmaf(__ldg(ct + j), tau[j], l);
-#pragma unroll
-  for (int j = 0; j < NT; ++j) ts[j] = tau[j];
+  for (int j = 1; j < NT; ++j) l = fmaf(st[L_CV + j], tau[j], l);
   q = 0.0f;
-#pragma unroll 1
-  for (int i = 0; i < NT; ++i) {
-    const float* row = Ct + i * NT;
-    float r = __ldg(row) * tau[0];
 #pragma unroll
-    for (int j = 1; j < NT; ++j) r = fmaf(__ldg(row + j), tau[j], r);
-    q = fmaf(ts[i], r, q);
+  for (int i = 0; i < NT; ++i) {
+    const float* row = st + L_C + i * NT;
+    float r = row[0] * tau[0];
+#pragma unroll
+    for (int j = 1; j < NT; ++j) r = fmaf(row[j], tau[j], r);
+    q = fmaf(tau[i], r, q);
   }
 }
 
@@ -437,7 +445,10 @@ __device__ __forceinline__ float pick(const float (&v)[N], int i) {
 // ---------------------------------------------------------------------------
 // Solve (controller.py:303-435)
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(THREADS, 3) dense_solve_kernel(DenseSolveParams p) {
+#ifndef ILQR_R13_MINB
+#define ILQR_R13_MINB 2  // resident CTAs per SM the register budget targets
+#endif
+__global__ void __launch_bounds__(THREADS, ILQR_R13_MINB) dense_solve_kernel(DenseSolveParams p) {
   extern __shared__ float smem[];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -467,41 +478,131 @@ __global__ void __launch_bounds__(THREADS, 3) dense_solve_kernel(DenseSolveParam
   if (p.trace != nullptr && valid && g == 0)
     for (int i = 0; i < p.max_iter; ++i) p.trace[b * p.max_iter + i] = (int8_t)-128;
 
-  // ---- initial rollout and objective (controller.py:307-313), lane 0 -------
-  float best = 0.0f;
-  if (g == 0 && valid) {
+  // ---- rollouts: the initial one (controller.py:307-313, lane 0 of the
+  // group, controls U_init) and the line search's (controller.py:360-388,
+  // 437-533, lane j = step size j). All 16 lanes stage step t + 1 (costs,
+  // references, nominal record, gains) into shared memory while the
+  // candidate lanes roll out step t from the staged copy.
+  const int nsc = L_NSC;
+  auto scalar_src = [&](int t, int f, bool init) -> float {
+    if (f < L_CV) return __ldg(Cb + (int64_t)t * NT * NT + f);
+    if (f < L_XR) return __ldg(cb + (int64_t)t * NT + (f - L_CV));
+    if (f < L_UR) return xr ? __ldg(xr + t * NX + (f - L_XR)) : 0.0f;
+    if (f < L_U0) return ur ? __ldg(ur + t * NU + (f - L_UR)) : 0.0f;
+    return init ? __ldg(p.U_init + (b * T + t) * NU + (f - L_U0)) : 0.0f;
+  };
+  auto rollout = [&](bool init, int nomslot, int cs, float al, bool cand) -> float {
+    float pf[L_PF];
+    float4 pf4[2];
+    auto prefetch = [&](int t) {
+      if (!valid) return;
+#pragma unroll
+      for (int k = 0; k < L_PF; ++k) {
+        const int f = g + GL * k;
+        if (f < nsc) pf[k] = scalar_src(t, f, init);
+      }
+      if (!init) {
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const int q = g + GL * k;
+          if (q < L_NF4) pf4[k] = q < 5 ? W.rec(nomslot, t)[q] : *W.kcol(t, q - 5);
+        }
+      }
+    };
+    auto commit = [&]() {
+#pragma unroll
+      for (int k = 0; k < L_PF; ++k) {
+        const int f = g + GL * k;
+        if (f < nsc) sm[f] = pf[k];
+      }
+      if (!init) {
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const int q = g + GL * k;
+          if (q < L_NF4) reinterpret_cast<float4*>(sm + L_F4)[q] = pf4[k];
+        }
+      }
+    };
     float x[NX];
+    if (cand) {
 #pragma unroll
-    for (int i = 0; i < NX; ++i) x[i] = __ldg(p.x0 + b * NX + i);
-    float sq = 0.0f, sl = 0.0f;
-    for (int t = 0; t < T; ++t) {
-      float u[NU];
-#pragma unroll
-      for (int a = 0; a < NU; ++a) u[a] = __ldg(p.U_init + (b * T + t) * NU + a);
-      store_rec(W.rec(0, t), x, u);
-      float tau[NT];
-#pragma unroll
-      for (int i = 0; i < NX; ++i) tau[i] = x[i] - xref(t, i);
-#pragma unroll
-      for (int a = 0; a < NU; ++a) tau[NX + a] = u[a] - uref(t, a);
-      float q, l;
-      step_cost(Cb + (int64_t)t * NT * NT, cb + (int64_t)t * NT, tau, sm + S_V, q, l);
-      sq += q;
-      sl += l;
-      float xn[NX];
-      step(x, u, dt, xn);
-#pragma unroll
-      for (int i = 0; i < NX; ++i) x[i] = xn[i];
+      for (int i = 0; i < NX; ++i) x[i] = __ldg(p.x0 + b * NX + i);
     }
-    const float zu[NU] = {0.0f, 0.0f, 0.0f, 0.0f};
-    store_rec(W.rec(0, T), x, zu);
-    float tn[NX];
+    float sq = 0.0f, sl = 0.0f;
+    prefetch(0);
+    for (int t = 0; t < T; ++t) {
+      __syncwarp();
+      commit();
+      __syncwarp();
+      if (t + 1 < T) prefetch(t + 1);
+      if (cand) {
+        float u[NU];
+        if (init) {
 #pragma unroll
-    for (int i = 0; i < NX; ++i) tn[i] = x[i] - xref(T, i);
-    best = (0.5f * sq + sl) + terminal_cost(Cf, cf, tn);
-  }
+          for (int a = 0; a < NU; ++a) u[a] = sm[L_U0 + a];
+        } else {
+          float xb[NX], ub[NU];
+          load_rec(reinterpret_cast<const float4*>(sm + L_F4), xb, ub);
+          const float4* kc = reinterpret_cast<const float4*>(sm + L_F4) + 5;
+          float dx[NX];
+#pragma unroll
+          for (int j = 0; j < NX; ++j) dx[j] = x[j] - xb[j];
+          float kd[NU];
+          {
+            const float4 c = kc[0];
+            kd[0] = c.x * dx[0];
+            kd[1] = c.y * dx[0];
+            kd[2] = c.z * dx[0];
+            kd[3] = c.w * dx[0];
+          }
+#pragma unroll
+          for (int j = 1; j < NX; ++j) {
+            const float4 c = kc[j];
+            kd[0] = fmaf(c.x, dx[j], kd[0]);
+            kd[1] = fmaf(c.y, dx[j], kd[1]);
+            kd[2] = fmaf(c.z, dx[j], kd[2]);
+            kd[3] = fmaf(c.w, dx[j], kd[3]);
+          }
+          const float4 k4 = kc[NX];
+          const float kt[NU] = {k4.x, k4.y, k4.z, k4.w};
+#pragma unroll
+          for (int a = 0; a < NU; ++a) {
+            float v = ub[a] + (al * kt[a] + al * kd[a]);
+            if (lo != nullptr) v = clampn(v, __ldg(lo + a), __ldg(hi + a));
+            u[a] = v;
+          }
+        }
+        store_rec(W.rec(cs, t), x, u);
+        float tau[NT];
+#pragma unroll
+        for (int i = 0; i < NX; ++i) tau[i] = x[i] - sm[L_XR + i];
+#pragma unroll
+        for (int a = 0; a < NU; ++a) tau[NX + a] = u[a] - sm[L_UR + a];
+        float q, l;
+        step_cost_smem(sm, tau, q, l);
+        sq += q;
+        sl += l;
+        float xn[NX];
+        step(x, u, dt, xn);
+#pragma unroll
+        for (int i = 0; i < NX; ++i) x[i] = xn[i];
+      }
+    }
+    float cost = 0.0f;
+    if (cand) {
+      const float zu[NU] = {0.0f, 0.0f, 0.0f, 0.0f};
+      store_rec(W.rec(cs, T), x, zu);
+      float tn[NX];
+#pragma unroll
+      for (int i = 0; i < NX; ++i) tn[i] = x[i] - xref(T, i);
+      cost = (0.5f * sq + sl) + terminal_cost(Cf, cf, tn);
+    }
+    __syncwarp();
+    return cost;
+  };
+
+  float best = rollout(true, 0, 0, 0.0f, valid && g == 0);
   best = __shfl_sync(FULLW, best, gbase);
-  __syncwarp();
 
   uint32_t status = 0;
   bool active = valid;
@@ -586,69 +687,10 @@ __global__ void __launch_bounds__(THREADS, 3) dense_solve_kernel(DenseSolveParam
     __syncwarp();
 
     // ---- grid line search (controller.py:360-388, 437-533): lane j = step j --
-    float mine = 0.0f;
-    if (valid && g < p.n_alpha) {
-      float al = p.alphas[0];
+    float al = p.alphas[0];
 #pragma unroll
-      for (int jj = 1; jj < ILQR_MAX_ALPHAS_DEV; ++jj) al = (g == jj) ? p.alphas[jj] : al;
-      const int cs = g < nom ? g : g + 1;
-      float x[NX];
-#pragma unroll
-      for (int i = 0; i < NX; ++i) x[i] = __ldg(p.x0 + b * NX + i);
-      float sq = 0.0f, sl = 0.0f;
-      for (int t = 0; t < T; ++t) {
-        float xb[NX], ub[NU];
-        load_rec(W.rec(nom, t), xb, ub);
-        const float4 k4 = *W.kff(t);
-        float dx[NX];
-#pragma unroll
-        for (int j = 0; j < NX; ++j) dx[j] = x[j] - xb[j];
-        float kd[NU];
-        {
-          const float4 c = *W.kcol(t, 0);
-          kd[0] = c.x * dx[0];
-          kd[1] = c.y * dx[0];
-          kd[2] = c.z * dx[0];
-          kd[3] = c.w * dx[0];
-        }
-#pragma unroll
-        for (int j = 1; j < NX; ++j) {
-          const float4 c = *W.kcol(t, j);
-          kd[0] = fmaf(c.x, dx[j], kd[0]);
-          kd[1] = fmaf(c.y, dx[j], kd[1]);
-          kd[2] = fmaf(c.z, dx[j], kd[2]);
-          kd[3] = fmaf(c.w, dx[j], kd[3]);
-        }
-        const float kt[NU] = {k4.x, k4.y, k4.z, k4.w};
-        float u[NU];
-#pragma unroll
-        for (int a = 0; a < NU; ++a) {
-          float v = ub[a] + (al * kt[a] + al * kd[a]);
-          if (lo != nullptr) v = clampn(v, __ldg(lo + a), __ldg(hi + a));
-          u[a] = v;
-        }
-        store_rec(W.rec(cs, t), x, u);
-        float tau[NT];
-#pragma unroll
-        for (int i = 0; i < NX; ++i) tau[i] = x[i] - xref(t, i);
-#pragma unroll
-        for (int a = 0; a < NU; ++a) tau[NX + a] = u[a] - uref(t, a);
-        float q, l;
-        step_cost(Cb + (int64_t)t * NT * NT, cb + (int64_t)t * NT, tau, sm + S_V + g * NT, q, l);
-        sq += q;
-        sl += l;
-        float xn[NX];
-        step(x, u, dt, xn);
-#pragma unroll
-        for (int i = 0; i < NX; ++i) x[i] = xn[i];
-      }
-      const float zu[NU] = {0.0f, 0.0f, 0.0f, 0.0f};
-      store_rec(W.rec(cs, T), x, zu);
-      float tn[NX];
-#pragma unroll
-      for (int i = 0; i < NX; ++i) tn[i] = x[i] - xref(T, i);
-      mine = (0.5f * sq + sl) + terminal_cost(Cf, cf, tn);
-    }
+    for (int jj = 1; jj < ILQR_MAX_ALPHAS_DEV; ++jj) al = (g == jj) ? p.alphas[jj] : al;
+    const float mine = rollout(false, nom, g < nom ? g : g + 1, al, valid && g < p.n_alpha);
     // torch.argmin semantics over the step sizes: first NaN, else first minimum
     int jbest = 0;
     float cmin = 0.0f;
