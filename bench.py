@@ -50,6 +50,8 @@ def _args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-sigmoid", action="store_true",
                     help="skip the section for costs given as the policy's sigmoid output")
+    ap.add_argument("--no-rotor13", action="store_true",
+                    help="skip the section for the 13-state rotor-thrust model")
     ap.add_argument("--latency-reps", type=int, default=200)
     ap.add_argument("--batch", type=int, default=None,
                     help="elements per GPU (default: the workload's 16384); for profiling runs")
@@ -546,6 +548,127 @@ def run_ours(args):
         actor = {"B": B, "T": T, "iters": iters, "one_call_ms": one, "reference_chunk_loop_ms": loop,
                  "note": "no gradients; the chunk loop is the reference's forward_actor loop on this solver"}
 
+    # ---- 13-state rotor-thrust model (ilqr_dense.cu) ---------------------------
+    # The benchmark configurations' rigid body (four rotor thrusts in [0, 1]),
+    # same batch, horizon, iterations and step sizes, dense C [B,T,17,17].
+    r13 = None
+    if not args.no_rotor13:
+        ri = wl.make_rotor13_inputs(B, T, seed=rank, target=cfg["target"], r=cfg["r"])
+        rd = {k: torch.from_numpy(v).to(dev) for k, v in ri.items()}
+        rgXn, rgUn = wl.make_backward_seeds(B, T, seed=1 + rank, nx=wl.NX13)
+        rgX, rgU = torch.from_numpy(rgXn).to(dev), torch.from_numpy(rgUn).to(dev)
+        rlo, rhi = torch.from_numpy(wl.U_MIN13).to(dev), torch.from_numpy(wl.U_MAX13).to(dev)
+        r_iters = []
+
+        def r13_step(timing=None):
+            if timing is not None:
+                timing[0].record(stream)
+            o = nat.rotor13_solve(rd["x0"], rd["U_init"], rd["C"], rd["c"], u_min=rlo, u_max=rhi, dt=wl.DT,
+                                  max_iter=iters, reg_eps=wl.REG_EPS, alphas=alphas, want_stats=timing is not None)
+            if timing is not None:
+                timing[1].record(stream)
+                r_iters.append(o["iters"])
+            nat.rotor13_backward(o["X"], o["U"], rd["C"], rgX, rgU, tight=o["tight"], dt=wl.DT,
+                                 reg_eps=wl.REG_EPS)
+            if timing is not None:
+                timing[2].record(stream)
+
+        for _ in range(max(3, args.warmup)):
+            r13_step()
+        barrier()
+        rtim = [(ev(), ev(), ev()) for _ in range(args.steps)]
+        r0, r1 = ev(), ev()
+        r0.record(stream)
+        for i in range(args.steps):
+            r13_step(rtim[i])
+        r1.record(stream)
+        barrier()
+        rel_s = r0.elapsed_time(r1) * 1e-3
+        if world > 1:
+            t = torch.tensor([rel_s], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            rel_s = float(t.item())
+        r_solve = statistics.mean(a.elapsed_time(b_) for a, b_, _ in rtim)
+        r_bwd = statistics.mean(b_.elapsed_time(c_) for _, b_, c_ in rtim)
+        it_np = torch.stack(r_iters).float().mean(0).cpu().numpy()
+        fl_s = cm.r13_solve_flops_dense(T, len(alphas), it_np)
+        fl_b = cm.r13_backward_flops_dense(T, B)
+        # end to end through FastMPC(13, 4, T) with host buffers
+        pin = lambda a: torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
+        h_x0 = pin(ri["x0"])
+        h_C = pin(np.transpose(ri["C"], (1, 0, 2, 3)))
+        h_c = pin(np.transpose(ri["c"], (1, 0, 2)))
+        h_gX, h_gU = pin(np.transpose(rgXn, (1, 0, 2))), pin(np.transpose(rgUn, (1, 0, 2)))
+        h_act, h_gx0 = torch.empty(B, 4).pin_memory(), torch.empty(B, wl.NX13).pin_memory()
+        rmpc = mpc_compat.MPC(wl.NX13, 4, T, u_lower=rlo.view(1, 1, 4).expand(T, 1, 4),
+                              u_upper=rhi.view(1, 1, 4).expand(T, 1, 4), lqr_iter=iters,
+                              eps=wl.REG_EPS, alphas=alphas)
+        rdyn = type("Dyn", (), {"dt": wl.DT})()
+
+        def r13_e2e():
+            x0 = h_x0.to(dev, non_blocking=True).requires_grad_(True)
+            Cd = h_C.to(dev, non_blocking=True).requires_grad_(True)
+            cd = h_c.to(dev, non_blocking=True).requires_grad_(True)
+            gx = h_gX.to(dev, non_blocking=True)
+            gu = h_gU.to(dev, non_blocking=True)
+            x, u, _ = rmpc(x0, mpc_compat.QuadCost(Cd, cd), rdyn)
+            ((x * gx).sum() + (u * gu).sum()).backward()
+            h_act.copy_(u[0].detach(), non_blocking=True)
+            h_gx0.copy_(x0.grad, non_blocking=True)
+
+        for _ in range(max(3, args.warmup)):
+            r13_e2e()
+        barrier()
+        e0, e1 = ev(), ev()
+        e0.record(stream)
+        for _ in range(args.steps):
+            r13_e2e()
+        e1.record(stream)
+        barrier()
+        rel_e2e = e0.elapsed_time(e1) * 1e-3
+        if world > 1:
+            t = torch.tensor([rel_e2e], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            rel_e2e = float(t.item())
+        h2d = sum(t.numel() * 4 for t in (h_x0, h_C, h_c, h_gX, h_gU))
+        # latency: B = 16, T = 5, 10 iterations, solve + backward, device-resident
+        lc13 = wl.CONFIGS["latency_b16_t5"]
+        li = wl.make_rotor13_inputs(16, lc13["T"], seed=rank, target=lc13["target"], r=lc13["r"])
+        ld13 = {k: torch.from_numpy(v).to(dev) for k, v in li.items()}
+        lgx13, lgu13 = [torch.from_numpy(a).to(dev) for a in wl.make_backward_seeds(16, lc13["T"], nx=wl.NX13)]
+        lsamp = []
+        for rep in range(args.latency_reps + 10):
+            a, b_ = ev(), ev()
+            a.record(stream)
+            o = nat.rotor13_solve(ld13["x0"], ld13["U_init"], ld13["C"], ld13["c"], u_min=rlo, u_max=rhi,
+                                  dt=wl.DT, max_iter=lc13["max_iter"], reg_eps=wl.REG_EPS, alphas=lc13["alphas"])
+            nat.rotor13_backward(o["X"], o["U"], ld13["C"], lgx13, lgu13, tight=o["tight"], dt=wl.DT,
+                                 reg_eps=wl.REG_EPS)
+            b_.record(stream)
+            b_.synchronize()
+            if rep >= 10:
+                lsamp.append(a.elapsed_time(b_) * 1e3)
+        r13 = {"workload": f"rotor13_b{B}_t{T}", "value": world * B / (rel_s / args.steps), "unit": "solves/s",
+               "ms_per_step": rel_s / args.steps * 1e3,
+               "model": "13-state rotor-thrust rigid body (p, q, v, w; 4 rotor thrusts in [0,1] x 8.5 N), "
+                        "dense C [B,T,17,17]",
+               "kernel_ms": {"solve_mean": r_solve, "backward_mean": r_bwd},
+               "mean_iters": float(it_np.mean()),
+               "roofline": {"bound": "fp32", "unit": "TFLOP/s", "peak": peak_fp32,
+                            "solve_achieved": fl_s / (r_solve * 1e-3) / 1e12,
+                            "backward_achieved": fl_b / (r_bwd * 1e-3) / 1e12,
+                            "solve_frac": fl_s / (r_solve * 1e-3) / 1e12 / peak_fp32,
+                            "backward_frac": fl_b / (r_bwd * 1e-3) / 1e12 / peak_fp32,
+                            "count": "dense per-unit counts (ilqr_costmodel: Riccati 16.9k, candidate 0.88k, "
+                                     "initial 0.75k, backward 18.0k FLOP per element and step)"},
+               "e2e": {"value": world * B / (rel_e2e / args.steps), "unit": "solves/s",
+                       "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": (h_act.numel() + h_gx0.numel()) * 4,
+                       "ms_per_step": rel_e2e / args.steps * 1e3,
+                       "path": "mpc_compat.MPC(13, 4, T)(x_init, QuadCost(C, c), dx) + autograd backward"},
+               "latency_b16_t5": {"p50_us": statistics.median(lsamp),
+                                  "p90_us": sorted(lsamp)[int(0.9 * len(lsamp))], "reps": len(lsamp),
+                                  "config": "B=16, T=5, 10 iterations, fwd+bwd, device-resident, eager"}}
+
     # ---- CPU baseline (rank 0, N=1) ------------------------------------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -576,6 +699,7 @@ def run_ours(args):
         "latency_b16_t5": lat,
         "policy_sigmoid_cost": sig,
         "policy_actor_step": actor,
+        "rotor13": r13,
         "kernel_ms": {"solve_mean": statistics.mean(solve_ms), "backward_mean": statistics.mean(bwd_ms)},
     }
     print(json.dumps(line), flush=True)

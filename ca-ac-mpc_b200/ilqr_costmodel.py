@@ -84,3 +84,27 @@ def solve_bytes(T: int, B: int) -> float:
 def backward_bytes(T: int, B: int) -> float:
     return float(B) * (40 * (T + 1) + T * (16 + 784 + 4) + 40 * (T + 1) + 16 * T + 40
                        + T * (784 + 56))
+
+
+# Dense algorithmic counts for the 13-state rotor model (ilqr_dense.cu), per
+# element and time step, an FMA as 2:
+#   Riccati step 16.9 kFLOP: l_tau = C tau + c (17 x 17), Jacobian (~100),
+#     A^T V and (A^T V) A (2 x 13^3), V B and A^T (V B) (2 x 13^2 x 4),
+#     B^T V B (4 x 4 x 13), q_x, q_u, Cholesky and 14 solves (~480),
+#     M = Q_uu K + Q_ux (4 x 4 x 13), V and v updates (13 x 13 x 8, 13 x 8)
+#   line-search candidate step 0.88 kFLOP: K dx (4 x 13), controls and clamp,
+#     1/2 tau^T C tau + c^T tau (17 x 17 + 2 x 17), model step (~80)
+#   initial rollout step 0.75 kFLOP (the candidate step without K dx)
+#   backward step 18.0 kFLOP: the masked Riccati step without the
+#     quadraticisation, the dX/dU sweep (K dX, A dX, B dU) and grad_C (17 x 17 x 4)
+R13_RIC_DENSE, R13_LS_DENSE, R13_INIT_DENSE, R13_BWD_DENSE = 16900, 880, 750, 18000
+
+
+def r13_solve_flops_dense(T: int, n_alpha: int, iters) -> float:
+    """F = T [I (16.9k + 0.88k n_alpha) + 0.75k] summed over the batch."""
+    I = np.asarray(iters, dtype=np.float64)
+    return float((T * (I * (R13_RIC_DENSE + R13_LS_DENSE * n_alpha) + R13_INIT_DENSE)).sum())
+
+
+def r13_backward_flops_dense(T: int, B: int) -> float:
+    return float(B) * T * R13_BWD_DENSE
