@@ -52,6 +52,9 @@ def _args():
                     help="skip the section for costs given as the policy's sigmoid output")
     ap.add_argument("--no-rotor13", action="store_true",
                     help="skip the section for the 13-state rotor-thrust model")
+    ap.add_argument("--all-configs", action="store_true",
+                    help="instead of the benchmark line: one JSON line per workload configuration "
+                         "(both models, 1 GPU, device-resident)")
     ap.add_argument("--latency-reps", type=int, default=200)
     ap.add_argument("--batch", type=int, default=None,
                     help="elements per GPU (default: the workload's 16384); for profiling runs")
@@ -594,6 +597,7 @@ def run_ours(args):
         fl_s = cm.r13_solve_flops_dense(T, len(alphas), it_np)
         fl_b = cm.r13_backward_flops_dense(T, B)
         # end to end through FastMPC(13, 4, T) with host buffers
+        r13_e2e_res = None
         pin = lambda a: torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
         h_x0 = pin(ri["x0"])
         h_C = pin(np.transpose(ri["C"], (1, 0, 2, 3)))
@@ -616,21 +620,26 @@ def run_ours(args):
             h_act.copy_(u[0].detach(), non_blocking=True)
             h_gx0.copy_(x0.grad, non_blocking=True)
 
-        for _ in range(max(3, args.warmup)):
-            r13_e2e()
-        barrier()
-        e0, e1 = ev(), ev()
-        e0.record(stream)
-        for _ in range(args.steps):
-            r13_e2e()
-        e1.record(stream)
-        barrier()
-        rel_e2e = e0.elapsed_time(e1) * 1e-3
-        if world > 1:
-            t = torch.tensor([rel_e2e], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            rel_e2e = float(t.item())
-        h2d = sum(t.numel() * 4 for t in (h_x0, h_C, h_c, h_gX, h_gU))
+        if not args.no_e2e:
+            for _ in range(max(3, args.warmup)):
+                r13_e2e()
+            barrier()
+            e0, e1 = ev(), ev()
+            e0.record(stream)
+            for _ in range(args.steps):
+                r13_e2e()
+            e1.record(stream)
+            barrier()
+            rel_e2e = e0.elapsed_time(e1) * 1e-3
+            if world > 1:
+                t = torch.tensor([rel_e2e], device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                rel_e2e = float(t.item())
+            h2d = sum(t.numel() * 4 for t in (h_x0, h_C, h_c, h_gX, h_gU))
+            r13_e2e_res = {"value": world * B / (rel_e2e / args.steps), "unit": "solves/s",
+                           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": (h_act.numel() + h_gx0.numel()) * 4,
+                           "ms_per_step": rel_e2e / args.steps * 1e3,
+                           "path": "mpc_compat.MPC(13, 4, T)(x_init, QuadCost(C, c), dx) + autograd backward"}
         # latency: B = 16, T = 5, 10 iterations, solve + backward, device-resident
         lc13 = wl.CONFIGS["latency_b16_t5"]
         li = wl.make_rotor13_inputs(16, lc13["T"], seed=rank, target=lc13["target"], r=lc13["r"])
@@ -661,10 +670,7 @@ def run_ours(args):
                             "backward_frac": fl_b / (r_bwd * 1e-3) / 1e12 / peak_fp32,
                             "count": "dense per-unit counts (ilqr_costmodel: Riccati 16.9k, candidate 0.88k, "
                                      "initial 0.75k, backward 18.0k FLOP per element and step)"},
-               "e2e": {"value": world * B / (rel_e2e / args.steps), "unit": "solves/s",
-                       "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": (h_act.numel() + h_gx0.numel()) * 4,
-                       "ms_per_step": rel_e2e / args.steps * 1e3,
-                       "path": "mpc_compat.MPC(13, 4, T)(x_init, QuadCost(C, c), dx) + autograd backward"},
+               "e2e": r13_e2e_res,
                "latency_b16_t5": {"p50_us": statistics.median(lsamp),
                                   "p90_us": sorted(lsamp)[int(0.9 * len(lsamp))], "reps": len(lsamp),
                                   "config": "B=16, T=5, 10 iterations, fwd+bwd, device-resident, eager"}}
@@ -705,10 +711,84 @@ def run_ours(args):
     print(json.dumps(line), flush=True)
 
 
+def run_all_configs(args):
+    """Every workload configuration on one GPU, for both models: fwd (+bwd
+    where the configuration has it) solves/s with device-resident inputs,
+    the mean iterations the elements ran, and the solve / backward kernel
+    times. Batch sizes above 65536 run as consecutive 65536-element slices
+    (the solve is per element; the slices reuse one workspace size)."""
+    import numpy as np
+    import torch
+
+    import ilqr_native as nat
+    import ilqr_workload as wl
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+    for model in ("drone10", "rotor13"):
+        r13 = model == "rotor13"
+        for name, cfg in wl.CONFIGS.items():
+            if r13 and name == "stress_b65536_t50":
+                continue  # the reference's own fp32 solve fails there on this model
+            B, T, iters, alphas = cfg["B"], cfg["T"], cfg["max_iter"], cfg["alphas"]
+            sl = min(B, 65536)
+            if r13:
+                inp = wl.make_rotor13_inputs(sl, T, seed=0, target=cfg["target"], r=cfg["r"])
+                lo, hi = wl.U_MIN13, wl.U_MAX13
+                gXn, gUn = wl.make_backward_seeds(sl, T, nx=wl.NX13)
+            else:
+                inp = wl.make_inputs(sl, T, seed=0, target=cfg["target"], r=cfg["r"])
+                lo, hi = wl.U_MIN, wl.U_MAX
+                gXn, gUn = wl.make_backward_seeds(sl, T)
+            d = {k: torch.from_numpy(v).to(dev) for k, v in inp.items()}
+            gX, gU = torch.from_numpy(gXn).to(dev), torch.from_numpy(gUn).to(dev)
+            tl, th = torch.from_numpy(lo).to(dev), torch.from_numpy(hi).to(dev)
+            solve = nat.rotor13_solve if r13 else nat.solve
+            bwd = nat.rotor13_backward if r13 else nat.backward
+            its = []
+
+            def one(timing):
+                timing[0].record(stream)
+                o = solve(d["x0"], d["U_init"], d["C"], d["c"], u_min=tl, u_max=th, dt=wl.DT, max_iter=iters,
+                          reg_eps=wl.REG_EPS, alphas=alphas, want_stats=True)
+                timing[1].record(stream)
+                its.append(o["iters"])
+                if cfg["backward"]:
+                    bwd(o["X"], o["U"], d["C"], gX, gU, tight=o["tight"], dt=wl.DT, reg_eps=wl.REG_EPS)
+                timing[2].record(stream)
+
+            n_sl = B // sl
+            for _ in range(max(3, args.warmup)):
+                one((ev(), ev(), ev()))
+            torch.cuda.synchronize()
+            reps = max(3, args.steps // 2) if B <= 1024 else max(3, min(args.steps, 10))
+            tims = [[(ev(), ev(), ev()) for _ in range(n_sl)] for _ in range(reps)]
+            for r in range(reps):
+                for k in range(n_sl):
+                    one(tims[r][k])
+            torch.cuda.synchronize()
+            step_ms = [sum(a.elapsed_time(c) for a, _, c in tims[r]) for r in range(reps)]
+            solve_ms = statistics.mean(sum(a.elapsed_time(b_) for a, b_, _ in tims[r]) for r in range(reps))
+            bwd_ms = statistics.mean(sum(b_.elapsed_time(c) for _, b_, c in tims[r]) for r in range(reps))
+            med = statistics.median(step_ms)
+            line = {"model": model, "workload": name, "B": B, "T": T, "iters": iters, "alphas": list(alphas),
+                    "backward": cfg["backward"], "slices": n_sl,
+                    "ms_per_call_p50": med, "solves_per_s": B / (med * 1e-3),
+                    "solve_ms": solve_ms, "backward_ms": bwd_ms,
+                    "mean_iters_run": float(torch.stack(its[-n_sl:]).float().mean().item()),
+                    "reps": reps, "data": "synthetic (seeded)", "device_resident": True}
+            print(json.dumps(line), flush=True)
+            del d, gX, gU
+            torch.cuda.empty_cache()
+
+
 def main():
     args = _args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.all_configs:
+        run_all_configs(args)
     else:
         run_ours(args)
 
