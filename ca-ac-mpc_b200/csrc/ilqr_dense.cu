@@ -55,7 +55,8 @@ constexpr int S_QU = 604;    // q_u [4]
 constexpr int S_KF = 608;    // k_t [4]
 constexpr int S_MK = 612;    // Q_uu k + q_u [4]
 constexpr int S_SVD = 616;   // SVD fallback: matrix [16], inverse [16]
-constexpr int S_ELEM = 656;  // floats per element (41 x 16)
+constexpr int S_TAU = 656;   // per-lane tau scratch of the rollouts [16][17]
+constexpr int S_ELEM = 944;  // floats per element (59 x 16)
 // Outside the Riccati pass the first 404 floats stage one step of a rollout:
 // C_t (289), c_t (17), x_ref_t (13), u_ref_t (4), U_init_t (4), then the
 // nominal record (20) and the K_t columns and k_t (56) as float4s.
@@ -116,23 +117,22 @@ __device__ __forceinline__ void store_rec(float4* r, const float* x, const float
   r[4] = make_float4(u[3], 0.0f, 0.0f, 0.0f);
 }
 
-// 1/2 tau^T C tau and c^T tau of one step from the staged C_t, c_t,
-// accumulated over rows in index order (the costs the line search compares
-// and the initial objective).
-__device__ __forceinline__ void step_cost_smem(const float* st, const float* tau, float& q, float& l) {
-  l = st[L_CV] * tau[0];
-#pragma unroll
-  for (int j = 1; j < NT; ++j) l = fmaf(st[L_CV + j], tau[j], l);
-  q = 0.0f;
-#pragma unroll
-  for (int i = 0; i < NT; ++i) {
+// The rows r, r + n, r + 2n, ... of tau^T C tau (C_t staged), with tau_i read
+// from this lane's scratch ts (the row index is not a compile-time constant).
+__device__ __forceinline__ float step_quad_rows(const float* st, const float* tau, const float* ts, int r, int n) {
+  float q = 0.0f;
+  for (int i = r; i < NT; i += n) {
     const float* row = st + L_C + i * NT;
-    float r = row[0] * tau[0];
+    float v = row[0] * tau[0];
 #pragma unroll
-    for (int j = 1; j < NT; ++j) r = fmaf(row[j], tau[j], r);
-    q = fmaf(tau[i], r, q);
+    for (int j = 1; j < NT; ++j) v = fmaf(row[j], tau[j], v);
+    q = fmaf(ts[i], v, q);
   }
+  return q;
 }
+
+// Lanes per line-search candidate when n candidates share an element's 16 lanes.
+__device__ __forceinline__ int lanes_per_candidate(int n) { return n <= 4 ? 4 : (n <= 5 ? 3 : 2); }
 
 // Terminal cost 1/2 tN^T C_f tN + c_f^T tN, tN = [x_T - x_ref_T; 0].
 __device__ __forceinline__ float terminal_cost(const float* __restrict__ Cf, const float* __restrict__ cf,
@@ -491,7 +491,19 @@ __global__ void __launch_bounds__(THREADS, ILQR_R13_MINB) dense_solve_kernel(Den
     if (f < L_U0) return ur ? __ldg(ur + t * NU + (f - L_UR)) : 0.0f;
     return init ? __ldg(p.U_init + (b * T + t) * NU + (f - L_U0)) : 0.0f;
   };
-  auto rollout = [&](bool init, int nomslot, int cs, float al, bool cand) -> float {
+  // n_cand candidates, lanes_per_candidate(n_cand) lanes each: every lane of
+  // candidate j rolls it out (identical arithmetic) and costs its share of
+  // the rows of the quadratic form; the shares are summed at the end.
+  auto rollout = [&](bool init, int nomslot, int n_cand) -> float {
+    const int lpc = lanes_per_candidate(n_cand);
+    const int j = g / lpc, rsub = g - j * lpc;
+    const bool cand = valid && j < n_cand;
+    const bool lead = cand && rsub == 0;  // stores the records, adds the linear and terminal terms
+    const int cs = init ? 0 : (j < nomslot ? j : j + 1);
+    float al = p.alphas[0];
+#pragma unroll
+    for (int jj = 1; jj < ILQR_MAX_ALPHAS_DEV; ++jj) al = (j == jj) ? p.alphas[jj] : al;
+    float* ts = sm + S_TAU + g * NT;
     float pf[L_PF];
     float4 pf4[2];
     auto prefetch = [&](int t) {
@@ -572,36 +584,48 @@ __global__ void __launch_bounds__(THREADS, ILQR_R13_MINB) dense_solve_kernel(Den
             u[a] = v;
           }
         }
-        store_rec(W.rec(cs, t), x, u);
+        if (lead) store_rec(W.rec(cs, t), x, u);
         float tau[NT];
 #pragma unroll
         for (int i = 0; i < NX; ++i) tau[i] = x[i] - sm[L_XR + i];
 #pragma unroll
         for (int a = 0; a < NU; ++a) tau[NX + a] = u[a] - sm[L_UR + a];
-        float q, l;
-        step_cost_smem(sm, tau, q, l);
-        sq += q;
-        sl += l;
+#pragma unroll
+        for (int i = 0; i < NT; ++i) ts[i] = tau[i];
+        sq += step_quad_rows(sm, tau, ts, rsub, lpc);
+        if (lead) {
+          float l = sm[L_CV] * tau[0];
+#pragma unroll
+          for (int jj = 1; jj < NT; ++jj) l = fmaf(sm[L_CV + jj], tau[jj], l);
+          sl += l;
+        }
         float xn[NX];
         step(x, u, dt, xn);
 #pragma unroll
         for (int i = 0; i < NX; ++i) x[i] = xn[i];
       }
     }
+    // the candidate's row shares, in sub-lane order
+    const int base = (lane & 16) + j * lpc;
+    float sqa = __shfl_sync(FULLW, sq, base & 31);
+    for (int k = 1; k < 4; ++k) {
+      const float v = __shfl_sync(FULLW, sq, (base + k) & 31);
+      if (k < lpc) sqa += v;
+    }
     float cost = 0.0f;
-    if (cand) {
+    if (lead) {
       const float zu[NU] = {0.0f, 0.0f, 0.0f, 0.0f};
       store_rec(W.rec(cs, T), x, zu);
       float tn[NX];
 #pragma unroll
       for (int i = 0; i < NX; ++i) tn[i] = x[i] - xref(T, i);
-      cost = (0.5f * sq + sl) + terminal_cost(Cf, cf, tn);
+      cost = (0.5f * sqa + sl) + terminal_cost(Cf, cf, tn);
     }
     __syncwarp();
     return cost;
   };
 
-  float best = rollout(true, 0, 0, 0.0f, valid && g == 0);
+  float best = rollout(true, 0, 1);
   best = __shfl_sync(FULLW, best, gbase);
 
   uint32_t status = 0;
@@ -687,10 +711,8 @@ __global__ void __launch_bounds__(THREADS, ILQR_R13_MINB) dense_solve_kernel(Den
     __syncwarp();
 
     // ---- grid line search (controller.py:360-388, 437-533): lane j = step j --
-    float al = p.alphas[0];
-#pragma unroll
-    for (int jj = 1; jj < ILQR_MAX_ALPHAS_DEV; ++jj) al = (g == jj) ? p.alphas[jj] : al;
-    const float mine = rollout(false, nom, g < nom ? g : g + 1, al, valid && g < p.n_alpha);
+    const float mine = rollout(false, nom, p.n_alpha);
+    const int lpc_ls = lanes_per_candidate(p.n_alpha);
     // torch.argmin semantics over the step sizes: first NaN, else first minimum
     int jbest = 0;
     float cmin = 0.0f;
@@ -698,7 +720,7 @@ __global__ void __launch_bounds__(THREADS, ILQR_R13_MINB) dense_solve_kernel(Den
     float cand[ILQR_MAX_ALPHAS_DEV];
 #pragma unroll
     for (int jj = 0; jj < ILQR_MAX_ALPHAS_DEV; ++jj) {
-      const float cj = __shfl_sync(FULLW, mine, gbase + jj);
+      const float cj = __shfl_sync(FULLW, mine, (gbase + jj * lpc_ls) & 31);
       cand[jj] = cj;
       if (jj >= p.n_alpha) continue;
       if (!nan_seen) {
