@@ -207,6 +207,33 @@ def test_invalid_inputs_raise():
         nat.solve(g(d["x0"]), g(d["U_init"]), g(d["C"]), g(d["c"]), alphas=())
 
 
+def test_nonfinite_elements_are_isolated():
+    """A NaN in one element's x0 and an infinite cost weight in another's C:
+    both reject their first step as the reference does (objective NaN / inf,
+    never improved), keep U_init and their initial rollout, and are flagged
+    non-finite where X is; every other element of the batch (warp-mates
+    included) is bit-identical to the run without them."""
+    d = load("cfg1_b16_t5")
+    bad = dict(d)
+    bad["x0"] = d["x0"].copy()
+    bad["x0"][3, 0] = np.nan
+    bad["C"] = d["C"].copy()
+    bad["C"][7, 2, 1, 1] = np.inf
+    r, kw = gpu_solve(bad)
+    r0, _ = gpu_solve(d)
+    with np.errstate(invalid="ignore", over="ignore"):
+        o = O.solve(bad["x0"], d["U_init"], bad["C"], d["c"], **kw)
+    others = [b for b in range(16) if b not in (3, 7)]
+    for k in ("X", "U", "tight", "trace"):
+        assert np.array_equal(r[k][others], r0[k][others]), k
+    for b in (3, 7):
+        assert r["trace"][b, 0] < 0 and (r["trace"][b, 1:] == -128).all()
+        assert np.array_equal(r["U"][b], d["U_init"][b])
+        assert np.array_equal(r["X"][b], o["X"][b], equal_nan=True)
+    assert r["status"][3] & 2 and np.isnan(r["best_cost"][3])
+    assert not (r["status"][7] & 2) and np.isinf(r["best_cost"][7])
+
+
 def test_empty_batch():
     z = lambda *s: torch.zeros(*s, device=DEV)
     out = nat.solve(z(0, 10), z(0, 3, 4), z(0, 3, 14, 14), z(0, 3, 14))

@@ -242,3 +242,25 @@ def test_rotor13_rollout_config_prefix():
         assert not fails, (key, fails[:5])
     well = rel_per_elem(reals[0]["X"], o64["X"]) <= WELL_CONDITIONED
     assert well.mean() > 0.5
+
+
+def test_rotor13_nonfinite_elements_are_isolated():
+    """As the 10-state test: a NaN x0 and an infinite cost weight stay
+    confined to their elements (rejected first step, U_init kept), and the
+    rest of the batch is bit-identical to the run without them."""
+    d = load("r13_cfg1_b16_t5")
+    bad = dict(d)
+    bad["x0"] = d["x0"].copy()
+    bad["x0"][3, 0] = np.nan
+    bad["C"] = d["C"].copy()
+    bad["C"][7, 2, 1, 1] = np.inf
+    r = _gpu_solve(bad)
+    r0 = _gpu_solve(d)
+    others = [b for b in range(16) if b not in (3, 7)]
+    for k in ("X", "U", "tight", "trace"):
+        assert np.array_equal(r[k][others], r0[k][others]), k
+    for b in (3, 7):
+        assert r["trace"][b, 0] < 0 and (r["trace"][b, 1:] == -128).all()
+        assert np.array_equal(r["U"][b], d["U_init"][b])
+    assert r["status"][3] & 2 and np.isnan(r["best_cost"][3])
+    assert np.isinf(r["best_cost"][7])
