@@ -56,7 +56,18 @@ constexpr int S_KF = 608;    // k_t [4]
 constexpr int S_MK = 612;    // Q_uu k + q_u [4]
 constexpr int S_SVD = 616;   // SVD fallback: matrix [16], inverse [16]
 constexpr int S_TAU = 656;   // per-lane tau scratch of the rollouts [16][17]
-constexpr int S_ELEM = 944;  // floats per element (59 x 16)
+constexpr int S_ELEM = 944;  // floats per element in the solve (59 x 16)
+constexpr int S_STG = 944;   // backward: two buffers staging a step's inputs
+constexpr int S_ELEM_BWD = 1616;  // floats per element in the backward (101 x 16)
+// One staged backward step (floats, relative to a buffer): C_t (in the tangent
+// sweep the K_t columns and k_t as 14 float4), the tight mask (4 bytes), x_t and
+// u_t, dL/dX_t, dL/dU_t.
+constexpr int R_C = 0;
+constexpr int R_TM = 289;
+constexpr int R_REC = 292;
+constexpr int R_GX = 312;
+constexpr int R_GU = 325;
+constexpr int R_SIZE = 332;
 // Outside the Riccati pass the first 404 floats stage one step of a rollout:
 // C_t (289), c_t (17), x_ref_t (13), u_ref_t (4), U_init_t (4), then the
 // nominal record (20) and the K_t columns and k_t (56) as float4s.
@@ -69,6 +80,12 @@ constexpr int L_NSC = 327;   // staged scalars
 constexpr int L_F4 = 328;    // float4 area: record (5), K columns and k (14)
 constexpr int L_NF4 = 19;
 constexpr int L_PF = 21;     // scalar prefetch slots per lane (16 x 21 >= 327)
+
+// 4-byte global -> shared copy completing in the background (cp.async groups
+// as cp_async16's).
+__device__ __forceinline__ void cp_async4(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
 
 __device__ __forceinline__ float clampn(float v, float lo, float hi) {
   float r;
@@ -425,10 +442,10 @@ __device__ __forceinline__ bool riccati_step(float* sm, int g, bool rowx, bool l
   return fb;
 }
 
-// Lane g writes row g of A_t, B_t (state-row lanes) from the nominal x, u in
-// sm[S_Z].
-__device__ __forceinline__ void jacobian_rows(float* sm, int g, float dt) {
-  if (g < NX) jac_row(g, sm + S_Z, sm + S_Z + NX, dt, sm + S_A + g * NX, sm + S_B + g * NU);
+// Lane g writes row g of A_t, B_t (state-row lanes) at the state and control
+// z = [x_t (13); u_t (4)].
+__device__ __forceinline__ void jacobian_rows(float* sm, const float* z, int g, float dt) {
+  if (g < NX) jac_row(g, z, z + NX, dt, sm + S_A + g * NX, sm + S_B + g * NU);
 }
 
 // v[i] for a lane-dependent i, without a dynamically indexed local array.
@@ -665,7 +682,7 @@ __global__ void __launch_bounds__(THREADS, ILQR_R13_MINB) dense_solve_kernel(Den
       __syncwarp();
       if (g < 5) reinterpret_cast<float4*>(sm + S_Z)[g] = W.rec(nom, t)[g];
       __syncwarp();
-      jacobian_rows(sm, g, dt);
+      jacobian_rows(sm, sm + S_Z, g, dt);
       // l_tau = C tau + c for this lane's rows (cost.py:130-171)
       float tau[NT];
 #pragma unroll
@@ -816,7 +833,7 @@ __global__ void __launch_bounds__(THREADS) dense_backward_kernel(DenseBackwardPa
   const int64_t b = ((int64_t)blockIdx.x * WPC + warp) * EPW + e;
   const bool valid = b < p.B;
   const int64_t bw = valid ? b : 0;
-  float* sm = smem + (warp * EPW + e) * S_ELEM;
+  float* sm = smem + (warp * EPW + e) * S_ELEM_BWD;
   const unsigned FULLW = 0xffffffffu;
   const int T = p.T;
   const float dt = p.dt;
@@ -831,12 +848,6 @@ __global__ void __launch_bounds__(THREADS) dense_backward_kernel(DenseBackwardPa
   const uint8_t* tb = p.tight ? p.tight + bw * (int64_t)T * NU : nullptr;
   float4* kws = reinterpret_cast<float4*>(p.ws + bw * (int64_t)T * (NX + 1) * 4);
 
-  auto load_z = [&](int t) {
-    // nominal x_t (and u_t for t < T) into sm[S_Z]
-    if (g < NX) sm[S_Z + g] = __ldg(Xb + t * NX + g);
-    if (g < NU) sm[S_Z + NX + g] = t < T ? __ldg(Ub + t * NU + g) : 0.0f;
-  };
-
   // ---- masked adjoint Riccati: V_T = C_f,xx, v_T = -dL/dX_T -------------
   float Vr[NX], vi = 0.0f, Kc[NU], kf[NU];
   if (rowx) {
@@ -848,25 +859,53 @@ __global__ void __launch_bounds__(THREADS) dense_backward_kernel(DenseBackwardPa
     vi = -__ldg(gX + T * NX + g);
     sm[S_VV + g] = vi;
   }
-  for (int t = T - 1; t >= 0; --t) {
-    __syncwarp();
-    load_z(t);
-    __syncwarp();
-    jacobian_rows(sm, g, dt);
+  // Step t - 1's inputs (C, X, U, dL/dX, dL/dU, tight mask) are copied into
+  // the other staging buffer while step t computes.
+  auto stage_z = [&](int t, float* st) {
+    if (g < NX) cp_async4(st + R_REC + g, Xb + t * NX + g);
+    if (g < NU) cp_async4(st + R_REC + NX + g, Ub + t * NU + g);
+  };
+  auto bwd_stage = [&](int t, float* st) {
     const float* Ct = Cb + (int64_t)t * NT * NT;
+    for (int f = g; f < NT * NT; f += GL) cp_async4(st + R_C + f, Ct + f);
+    stage_z(t, st);
+    if (g < NX) cp_async4(st + R_GX + g, gX + t * NX + g);
+    if (g < NU) cp_async4(st + R_GU + g, gU + t * NU + g);
+    if (g == 0) {
+      if (tb) cp_async4(st + R_TM, tb + t * NU);
+      else reinterpret_cast<uint32_t*>(st)[R_TM] = 0u;
+    }
+  };
+  auto stb = [&](int t) { return sm + S_STG + ((T - 1 - t) & 1) * R_SIZE; };
+  bwd_stage(T - 1, stb(T - 1));
+  cp_async_commit();
+  for (int t = T - 1; t >= 0; --t) {
+    if (t > 0) {
+      bwd_stage(t - 1, stb(t - 1));
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncwarp();
+    const float* st = stb(t);
+    jacobian_rows(sm, st + R_REC, g, dt);
     StepIn in;
-    in.lx = rowx ? -__ldg(gX + t * NX + g) : 0.0f;
-    in.lu = g < NU ? -__ldg(gU + t * NU + g) : 0.0f;
+    in.lx = rowx ? -st[R_GX + g] : 0.0f;
+    in.lu = g < NU ? -st[R_GU + g] : 0.0f;
     if (rowx) {
 #pragma unroll
-      for (int j = 0; j < NX; ++j) in.cxx[j] = __ldg(Ct + g * NT + j);
+      for (int j = 0; j < NX; ++j) in.cxx[j] = st[R_C + g * NT + j];
 #pragma unroll
-      for (int a = 0; a < NU; ++a) in.cxu[a] = __ldg(Ct + g * NT + NX + a);
+      for (int a = 0; a < NU; ++a) in.cxu[a] = st[R_C + g * NT + NX + a];
     }
-    in.cuu = __ldg(Ct + (NX + (g >> 2)) * NT + NX + (g & 3));
+    in.cuu = st[R_C + (NX + (g >> 2)) * NT + NX + (g & 3)];
     bool tight[NU];
+    {
+      const uint32_t tw = reinterpret_cast<const uint32_t*>(st)[R_TM];
 #pragma unroll
-    for (int a = 0; a < NU; ++a) tight[a] = tb ? (tb[t * NU + a] != 0) : false;
+      for (int a = 0; a < NU; ++a) tight[a] = ((tw >> (8 * a)) & 0xffu) != 0u;
+    }
     __syncwarp();
     riccati_step<true>(sm, g, rowx, valid, FULLW, in, p.reg, tight, Vr, vi, Kc, kf);
     if (valid) {
@@ -880,28 +919,49 @@ __global__ void __launch_bounds__(THREADS) dense_backward_kernel(DenseBackwardPa
   // ---- tangent sweep dU = K dX + k, dX+ = A dX + B dU, and the gradients ------
   float* dts = sm + S_M;  // dtau_t = [dX_t; dU_t] (17)
   if (rowx) dts[g] = 0.0f;
+  // Step t + 1's X, U and K_t columns are copied into the other staging
+  // buffer while step t computes (the gains were written by this warp's
+  // lanes in the pass above; cp.async.cg reads them from L2).
+  auto sweep_stage = [&](int t, float* st) {
+    stage_z(t, st);
+    if (g < NX + 1) {
+      float4* d4 = reinterpret_cast<float4*>(st + R_C) + g;
+      if (valid) cp_async16(d4, kws + t * (NX + 1) + g);
+      else *d4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  auto sb = [&](int t) { return sm + S_STG + (t & 1) * R_SIZE; };
+  __syncwarp();
+  sweep_stage(0, sb(0));
+  cp_async_commit();
   for (int t = 0; t < T; ++t) {
+    if (t + 1 < T) {
+      sweep_stage(t + 1, sb(t + 1));
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
     __syncwarp();
-    load_z(t);
-    __syncwarp();
-    jacobian_rows(sm, g, dt);
+    const float* st = sb(t);
+    jacobian_rows(sm, st + R_REC, g, dt);
     float dx[NX];
 #pragma unroll
     for (int j = 0; j < NX; ++j) dx[j] = dts[j];
     float du[NU];
     {
-      const float4* kc = kws + t * (NX + 1);
-      const float4 c0 = valid ? kc[0] : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4* kc = reinterpret_cast<const float4*>(st + R_C);
+      const float4 c0 = kc[0];
       float kd[NU] = {c0.x * dx[0], c0.y * dx[0], c0.z * dx[0], c0.w * dx[0]};
 #pragma unroll
       for (int j = 1; j < NX; ++j) {
-        const float4 c = valid ? kc[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 c = kc[j];
         kd[0] = fmaf(c.x, dx[j], kd[0]);
         kd[1] = fmaf(c.y, dx[j], kd[1]);
         kd[2] = fmaf(c.z, dx[j], kd[2]);
         kd[3] = fmaf(c.w, dx[j], kd[3]);
       }
-      const float4 k4 = valid ? kc[NX] : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 k4 = kc[NX];
       du[0] = kd[0] + k4.x;
       du[1] = kd[1] + k4.y;
       du[2] = kd[2] + k4.z;
@@ -924,7 +984,7 @@ __global__ void __launch_bounds__(THREADS) dense_backward_kernel(DenseBackwardPa
       // dtau = [dX_t; dU_t], z = [X_t; U_t]:
       // grad_C_t = -1/2 (dtau z^T + z dtau^T), grad_c_t = -dtau
       const int64_t off = (b * T + t) * NT;
-      const float* z = sm + S_Z;
+      const float* z = st + R_REC;
       auto grad_row = [&](int i, float* gC) {
         const float dzi = dts[i], zi = z[i];
 #pragma unroll
@@ -1014,19 +1074,23 @@ int64_t dense_solve_ws_fields(int T, int n_alpha) {
 
 int64_t dense_backward_ws_fields(int T) { return (int64_t)T * (r13::NX + 1) * 4; }
 
-static size_t dense_smem_bytes() { return (size_t)r13::EPC * r13::S_ELEM * sizeof(float); }
+static size_t dense_smem_bytes(int elem_floats) { return (size_t)r13::EPC * elem_floats * sizeof(float); }
 
 cudaError_t launch_dense_solve(const DenseSolveParams& p, cudaStream_t stream) {
   if (p.B == 0) return cudaSuccess;
   const int64_t grid = (p.B + r13::EPC - 1) / r13::EPC;
-  r13::dense_solve_kernel<<<(unsigned)grid, r13::THREADS, dense_smem_bytes(), stream>>>(p);
+  r13::dense_solve_kernel<<<(unsigned)grid, r13::THREADS, dense_smem_bytes(r13::S_ELEM), stream>>>(p);
   return cudaGetLastError();
 }
 
 cudaError_t launch_dense_backward(const DenseBackwardParams& p, cudaStream_t stream) {
   if (p.B == 0) return cudaSuccess;
+  // more than the default 48 KB of dynamic shared memory per CTA
+  cudaError_t e = cudaFuncSetAttribute(r13::dense_backward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)dense_smem_bytes(r13::S_ELEM_BWD));
+  if (e != cudaSuccess) return e;
   const int64_t grid = (p.B + r13::EPC - 1) / r13::EPC;
-  r13::dense_backward_kernel<<<(unsigned)grid, r13::THREADS, dense_smem_bytes(), stream>>>(p);
+  r13::dense_backward_kernel<<<(unsigned)grid, r13::THREADS, dense_smem_bytes(r13::S_ELEM_BWD), stream>>>(p);
   return cudaGetLastError();
 }
 
