@@ -458,7 +458,21 @@ def run_ours(args):
             b.synchronize()
             if r >= 10:
                 gsamples.append(a.elapsed_time(b) * 1e3)
+        # the same step through ilqr_native.BoundSolve (arguments prepared once)
+        bound = nat.BoundSolve(16, lc["T"], dev, lo, hi, dt=wl.DT, max_iter=lc["max_iter"], alphas=lc["alphas"])
+        bsamples = []
+        for r in range(args.latency_reps + 10):
+            a, b = ev(), ev()
+            a.record(stream)
+            bound(ld["x0"], ld["U_init"], ld["C"], ld["c"], lgx, lgu)
+            b.record(stream)
+            b.synchronize()
+            if r >= 10:
+                bsamples.append(a.elapsed_time(b) * 1e3)
         lat = {"p50_us": statistics.median(samples), "p90_us": sorted(samples)[int(0.9 * len(samples))],
+               "p50_bound_us": statistics.median(bsamples),
+               "p90_bound_us": sorted(bsamples)[int(0.9 * len(bsamples))],
+               "bound": "ilqr_native.BoundSolve: solve + backward entry points with arguments prepared once",
                "reps": len(samples), "config": "B=16, T=5, 10 iterations, fwd+bwd, device-resident",
                "p50_graph_us": statistics.median(gsamples),
                "p90_graph_us": sorted(gsamples)[int(0.9 * len(gsamples))],

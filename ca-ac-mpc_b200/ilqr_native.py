@@ -409,6 +409,84 @@ class CapturedSolve:
         return self.out, self.grads
 
 
+class BoundSolve:
+    """A fixed-shape solve (and optionally its backward) with everything but
+    the inputs prepared once: outputs and workspaces allocated, arguments
+    validated and packed for the C ABI. A call checks that the inputs have the
+    bound shapes, device and dtype, swaps their pointers into the packed
+    arguments and makes one C call per kernel on the current stream; no
+    copies and no allocation. The returned tensors are the bound outputs,
+    overwritten by the next call. For latency-bound control loops that call
+    the solver with the same shapes every tick."""
+
+    def __init__(self, B: int, T: int, device=None, u_min=None, u_max=None, dt=0.05, max_iter=10,
+                 reg_eps=1e-6, alphas: Sequence[float] = DEFAULT_ALPHAS, with_backward: bool = True,
+                 need=("x0", "C", "c")):
+        L = lib()
+        dev = torch.device("cuda") if device is None else torch.device(device)
+        if dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+        _device_ok(dev)
+        self.dev, self.B, self.T = dev, B, T
+        self.lo = None if u_min is None else u_min.to(dev, torch.float32).contiguous()
+        self.hi = None if u_max is None else u_max.to(dev, torch.float32).contiguous()
+        if (self.lo is None) != (self.hi is None):
+            raise RuntimeError("u_min and u_max must both be given or both be None")
+        al = [float(a) for a in alphas]
+        if not 1 <= len(al) <= 8:
+            raise RuntimeError("between 1 and 8 line-search step sizes are supported")
+        self._al = (ctypes.c_float * len(al))(*al)
+        self.out = dict(X=torch.empty(B, T + 1, NX, device=dev), U=torch.empty(B, T, NU, device=dev),
+                        tight=torch.empty(B, T, NU, device=dev, dtype=torch.uint8))
+        nb = workspace_bytes("solve", B, T)
+        self._ws = torch.empty(max(nb, 1), device=dev, dtype=torch.uint8)
+        o = self.out
+        # argument list of ilqr_b200_solve_f32; inputs at 0..3 are set per call
+        self._sargs = [None, None, None, None, None, None, None, None, _ptr(self.lo), _ptr(self.hi), B, T,
+                       float(dt), int(max_iter), float(reg_eps), 1e-6, ctypes.cast(self._al, ctypes.c_void_p),
+                       len(al), None, _ptr(o["X"]), _ptr(o["U"]), _ptr(o["tight"]), None, None, None, None,
+                       None, None, _ptr(self._ws), nb, None]
+        self.grads = {}
+        self._bargs = None
+        if with_backward:
+            shapes = dict(x0=(B, NX), C=(B, T, N, N), c=(B, T, N), C_final=(B, N, N), c_final=(B, N),
+                          x_ref=(B, T + 1, NX), u_ref=(B, T, NU))
+            self.grads = {k: torch.empty(shapes[k], device=dev) for k in need}
+            nbb = workspace_bytes("backward", B, T)
+            self._wsb = torch.empty(max(nbb, 1), device=dev, dtype=torch.uint8)
+            gp = lambda k: _ptr(self.grads.get(k))
+            # argument list of ilqr_b200_backward_f32; C, grad_X, grad_U set per call
+            self._bargs = [_ptr(o["X"]), _ptr(o["U"]), None, None, None, None, _ptr(o["tight"]), None, None, B, T,
+                           float(dt), float(reg_eps), gp("x0"), gp("C"), gp("c"), gp("C_final"), gp("c_final"),
+                           gp("x_ref"), gp("u_ref"), _ptr(self._wsb), nbb, None]
+        self._solve = L.ilqr_b200_solve_f32
+        self._backward = L.ilqr_b200_backward_f32
+
+    def _check(self, t, name, shape):
+        if t.device != self.dev or t.dtype != torch.float32 or tuple(t.shape) != shape or not t.is_contiguous():
+            raise RuntimeError(f"{name} must be a contiguous float32 {shape} tensor on {self.dev}")
+        return ctypes.c_void_p(t.data_ptr())
+
+    def __call__(self, x0, U_init, C, c, grad_X=None, grad_U=None):
+        B, T = self.B, self.T
+        a = self._sargs
+        a[0] = self._check(x0, "x0", (B, NX))
+        a[1] = self._check(U_init, "U_init", (B, T, NU))
+        a[2] = cp = self._check(C, "C", (B, T, N, N))
+        a[3] = self._check(c, "c", (B, T, N))
+        stream = ctypes.c_void_p(torch.cuda.current_stream(self.dev).cuda_stream)
+        a[-1] = stream
+        _check(self._solve(*a), "ilqr_b200_solve_f32")
+        if self._bargs is not None and grad_X is not None:
+            b = self._bargs
+            b[2] = cp
+            b[7] = self._check(grad_X, "grad_X", (B, T + 1, NX))
+            b[8] = self._check(grad_U, "grad_U", (B, T, NU))
+            b[-1] = stream
+            _check(self._backward(*b), "ilqr_b200_backward_f32")
+        return self.out, self.grads
+
+
 def pnqp4_batch(H, q, lower, upper, x_init=None):
     """n independent 4-d box QPs by projected Newton (drone_pnqp4_batch):
     returns (x* [n,4], free_mask [n,4])."""

@@ -234,6 +234,28 @@ def test_nonfinite_elements_are_isolated():
     assert not (r["status"][7] & 2) and np.isinf(r["best_cost"][7])
 
 
+def test_bound_solve_equals_eager_calls():
+    """BoundSolve (prepared arguments, bound outputs) returns what the eager
+    entry points return, call after call with changing inputs."""
+    d = load("cfg1_b16_t5")
+    kw = case_kwargs(d)
+    bs = nat.BoundSolve(16, 5, DEV, g(kw["u_min"]), g(kw["u_max"]), dt=kw["dt"], max_iter=kw["max_iter"],
+                        reg_eps=kw["reg"], alphas=kw["alphas"])
+    for scale in (1.0, 0.5):
+        x0 = g(d["x0"] * np.float32(scale))
+        out, grads = bs(x0, g(d["U_init"]), g(d["C"]), g(d["c"]), g(d["gX"]), g(d["gU"]))
+        ref = nat.solve(x0, g(d["U_init"]), g(d["C"]), g(d["c"]), None, None, None, None, g(kw["u_min"]),
+                        g(kw["u_max"]), dt=kw["dt"], max_iter=kw["max_iter"], reg_eps=kw["reg"], alphas=kw["alphas"])
+        rg = nat.backward(ref["X"], ref["U"], g(d["C"]), g(d["gX"]), g(d["gU"]), tight=ref["tight"], dt=kw["dt"],
+                          reg_eps=kw["reg"])
+        for k in ("X", "U", "tight"):
+            assert torch.equal(out[k], ref[k]), k
+        for k in ("x0", "C", "c"):
+            assert torch.equal(grads[k], rg[k]), k
+    with pytest.raises(RuntimeError, match="float32"):
+        bs(g(d["x0"]).double(), g(d["U_init"]), g(d["C"]), g(d["c"]))
+
+
 def test_empty_batch():
     z = lambda *s: torch.zeros(*s, device=DEV)
     out = nat.solve(z(0, 10), z(0, 3, 4), z(0, 3, 14, 14), z(0, 3, 14))
