@@ -229,6 +229,19 @@ __device__ __forceinline__ void lu_solve4(const float (&Min)[NU][NU], const floa
   }
 }
 
+// Structural nonzeros of the rotor model's A_t by column (rows k with A_kj
+// possibly nonzero; ilqr_rotor13.cuh): p columns only their diagonal, quaternion
+// columns the quaternion and velocity rows, velocity columns the position row
+// and the diagonal, rate columns the quaternion and rate rows. B_t is zero in
+// rows 0..6. Products over these sets skip exact zeros only, so they round as
+// the dense products (for finite values).
+__host__ __device__ constexpr int a_col_nnz(int j) { return j < 3 ? 1 : (j < 7 ? 7 : (j < 10 ? 2 : 7)); }
+__host__ __device__ constexpr int a_col_row(int j, int m) {
+  return j < 3 ? j
+               : (j < 7 ? 3 + m : (j < 10 ? (m == 0 ? j - 7 : j) : (m < 4 ? 3 + m : 6 + m)));
+}
+constexpr int B_ROW0 = 7;  // first row of B_t that can be nonzero
+
 // Inputs of one Riccati step that differ between the solve and the backward.
 struct StepIn {
   float lx;       // l_x,i (state-row lanes)
@@ -260,9 +273,9 @@ __device__ __forceinline__ bool riccati_step(float* sm, int g, bool rowx, bool l
     float vb[NU];
 #pragma unroll
     for (int a = 0; a < NU; ++a) {
-      float s = Vr[0] * sm[S_B + a];
+      float s = Vr[B_ROW0] * sm[S_B + B_ROW0 * NU + a];
 #pragma unroll
-      for (int k = 1; k < NX; ++k) s = fmaf(Vr[k], sm[S_B + k * NU + a], s);
+      for (int k = B_ROW0 + 1; k < NX; ++k) s = fmaf(Vr[k], sm[S_B + k * NU + a], s);
       vb[a] = s;
     }
 #pragma unroll
@@ -280,9 +293,9 @@ __device__ __forceinline__ bool riccati_step(float* sm, int g, bool rowx, bool l
     qx = in.lx + s;
   }
   if (g < NU) {
-    float s = sm[S_B + g] * sm[S_VV];
+    float s = sm[S_B + B_ROW0 * NU + g] * sm[S_VV + B_ROW0];
 #pragma unroll
-    for (int k = 1; k < NX; ++k) s = fmaf(sm[S_B + k * NU + g], sm[S_VV + k], s);
+    for (int k = B_ROW0 + 1; k < NX; ++k) s = fmaf(sm[S_B + k * NU + g], sm[S_VV + k], s);
     sm[S_QU + g] = in.lu + s;
   }
   __syncwarp(wmask);
@@ -291,9 +304,15 @@ __device__ __forceinline__ bool riccati_step(float* sm, int g, bool rowx, bool l
   if (rowx) {
 #pragma unroll
     for (int j = 0; j < NX; ++j) {
-      float s = w[0] * sm[S_A + j];
+      const int k0 = a_col_row(j, 0);
+      float s = w[k0] * sm[S_A + k0 * NX + j];
 #pragma unroll
-      for (int k = 1; k < NX; ++k) s = fmaf(w[k], sm[S_A + k * NX + j], s);
+      for (int m = 1; m < 7; ++m) {
+        if (m < a_col_nnz(j)) {
+          const int k = a_col_row(j, m);
+          s = fmaf(w[k], sm[S_A + k * NX + j], s);
+        }
+      }
       qxx[j] = in.cxx[j] + s;
     }
 #pragma unroll
@@ -306,9 +325,9 @@ __device__ __forceinline__ bool riccati_step(float* sm, int g, bool rowx, bool l
   }
   {
     const int a = g >> 2, b = g & 3;
-    float s = sm[S_B + a] * sm[S_VB + b];
+    float s = sm[S_B + B_ROW0 * NU + a] * sm[S_VB + B_ROW0 * NU + b];
 #pragma unroll
-    for (int k = 1; k < NX; ++k) s = fmaf(sm[S_B + k * NU + a], sm[S_VB + k * NU + b], s);
+    for (int k = B_ROW0 + 1; k < NX; ++k) s = fmaf(sm[S_B + k * NU + a], sm[S_VB + k * NU + b], s);
     float q = in.cuu + s;
     if (a == b) q = q + reg;
     sm[S_QUU + g] = q;
