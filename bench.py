@@ -815,12 +815,85 @@ def run_ours(args):
     print(json.dumps(line), flush=True)
 
 
+def run_sharded_inference(args):
+    """The inference configuration as specified (B=262144, T=10, 10
+    iterations, forward only) sharded over the ranks of torch.distributed.run:
+    each rank solves its B / world elements, then the first actions of all
+    ranks are all-gathered (NCCL) into every rank's [B, 4] tensor. Time per
+    call is the max over ranks; rank 0 prints one JSON line per model."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import ilqr_native as nat
+    import ilqr_shard
+    import ilqr_workload as wl
+    world = int(os.environ["WORLD_SIZE"])
+    rank = int(os.environ["RANK"])
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    stream = torch.cuda.current_stream(dev)
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+    cfg = wl.CONFIGS["inference_b262144_t10"]
+    B, T = cfg["B"], cfg["T"]
+    lo_, hi_ = ilqr_shard.shard_bounds(B, rank, world)
+    nb = hi_ - lo_
+    for model in ("drone10", "rotor13"):
+        r13 = model == "rotor13"
+        mk = wl.make_rotor13_inputs if r13 else wl.make_inputs
+        inp = mk(nb, T, seed=rank, target=cfg["target"], r=cfg["r"])
+        d = {k: torch.from_numpy(v).to(dev) for k, v in inp.items()}
+        tl = torch.from_numpy(wl.U_MIN13 if r13 else wl.U_MIN).to(dev)
+        th = torch.from_numpy(wl.U_MAX13 if r13 else wl.U_MAX).to(dev)
+        solve = nat.rotor13_solve if r13 else nat.solve
+
+        def call():
+            o = solve(d["x0"], d["U_init"], d["C"], d["c"], u_min=tl, u_max=th, dt=wl.DT,
+                      max_iter=cfg["max_iter"], reg_eps=wl.REG_EPS, alphas=cfg["alphas"])
+            return ilqr_shard.gather_first_actions(o["U"], B)
+
+        for _ in range(max(3, args.warmup)):
+            call()
+        dist.barrier()
+        torch.cuda.synchronize()
+        reps = max(3, min(args.steps, 10))
+        e0, e1 = ev(), ev()
+        e0.record(stream)
+        for _ in range(reps):
+            acts = call()
+        e1.record(stream)
+        dist.barrier()
+        torch.cuda.synchronize()
+        el = torch.tensor([e0.elapsed_time(e1) / reps], device=dev)
+        dist.all_reduce(el, op=dist.ReduceOp.MAX)
+        ms = float(el.item())
+        if rank == 0:
+            print(json.dumps({"model": model, "workload": "inference_b262144_t10", "B": B, "T": T,
+                              "iters": cfg["max_iter"], "n_gpus": world, "elements_per_gpu": nb,
+                              "ms_per_call_max_over_ranks": ms, "solves_per_s": B / (ms * 1e-3),
+                              "actions_gathered": list(acts.shape), "reps": reps,
+                              "per_call": "forward solve of the rank's shard + NCCL all-gather of the first actions",
+                              "data": "synthetic (seeded)", "device_resident": True}), flush=True)
+        del d
+        torch.cuda.empty_cache()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def run_all_configs(args):
     """Every workload configuration on one GPU, for both models: fwd (+bwd
     where the configuration has it) solves/s with device-resident inputs,
     the mean iterations the elements ran, and the solve / backward kernel
     times. Batch sizes above 65536 run as consecutive 65536-element slices
-    (the solve is per element; the slices reuse one workspace size)."""
+    (the solve is per element; the slices reuse one workspace size). Under
+    torch.distributed.run (WORLD_SIZE > 1) only the sharded inference
+    configuration runs (run_sharded_inference)."""
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        run_sharded_inference(args)
+        return
     import numpy as np
     import torch
 

@@ -4,7 +4,7 @@ tests/golden/make_rotor13_golden.py) and against the oracle.
 
 On this model fp32 rounding is strongly amplified: the reference's own fp32
 solution differs from its fp64 solution by up to O(1) on some elements at
-T >= 10 (the line of the Riccati recursion loses definiteness). The bars are
+T >= 10 (the fp32 Riccati recursion loses definiteness). The bars are
 therefore the rounding-aware ones of parity.within_rounding: the plain bars
 (1e-4 on X and U, 1e-3 on gradients) wherever the reference is
 well-conditioned, and the reference's own fp32 scatter elsewhere.
