@@ -189,6 +189,51 @@ def fp32_peak_tflops(torch, device):
     return best
 
 
+def time_streaming(torch, dev, stream, host, compute, warm, steps, barrier):
+    """Seconds for `steps` calls of compute(device_buffers) with host inputs
+    streamed: the host tensors of call k + 1 are copied into the other half of
+    a device double buffer on a second stream while call k computes, as a
+    data loader prefetches the next batch. compute enqueues one call's work
+    and its result read-back on `stream`; every call's copies and read-back
+    are inside the timed region."""
+    cstream = torch.cuda.Stream(dev)
+    bufs = [[torch.empty_like(h, device=dev) for h in host] for _ in range(2)]
+    ready = [torch.cuda.Event() for _ in range(2)]
+    free = [torch.cuda.Event() for _ in range(2)]
+    for f_ in free:
+        f_.record(stream)
+
+    def prefetch(k):
+        i = k % 2
+        with torch.cuda.stream(cstream):
+            cstream.wait_event(free[i])
+            for dst, src in zip(bufs[i], host):
+                dst.copy_(src, non_blocking=True)
+            ready[i].record(cstream)
+
+    def run(n):
+        prefetch(0)
+        if n > 1:
+            prefetch(1)
+        for k in range(n):
+            i = k % 2
+            stream.wait_event(ready[i])
+            compute(bufs[i])
+            free[i].record(stream)
+            if k + 2 < n:
+                prefetch(k + 2)
+
+    run(warm)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    cstream.wait_event(e0)
+    run(steps)
+    e1.record(stream)
+    barrier()
+    return e0.elapsed_time(e1) * 1e-3
+
+
 def bind_to_gpu_numa_node(torch, dev_index):
     """Pin this process to the host CPUs NVML reports as local to its GPU, so
     the pinned host buffers of the end-to-end measurement are allocated and
@@ -385,30 +430,10 @@ def run_ours(args):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             el_seq = float(t.item())
 
-        # Streaming: the inputs of step k + 1 are copied into the other half of
-        # a device double buffer on a second stream while step k computes, as a
-        # data loader prefetches the next batch. Every step's copies and its
-        # result read-back are inside the timed region.
-        cstream = torch.cuda.Stream(dev)
         host = (h_x0, h_C, h_c, h_gX, h_gU)
-        bufs = [[torch.empty_like(h, device=dev) for h in host] for _ in range(2)]
-        ready = [torch.cuda.Event() for _ in range(2)]
-        free = [torch.cuda.Event() for _ in range(2)]
-        for f_ in free:
-            f_.record(stream)
 
-        def prefetch(k):
-            i = k % 2
-            with torch.cuda.stream(cstream):
-                cstream.wait_event(free[i])
-                for dst, src in zip(bufs[i], host):
-                    dst.copy_(src, non_blocking=True)
-                ready[i].record(cstream)
-
-        def stream_step(k, n):
-            i = k % 2
-            stream.wait_event(ready[i])
-            bx0, bC, bc, bgx, bgu = bufs[i]
+        def e2e_compute(bufs):
+            bx0, bC, bc, bgx, bgu = bufs
             x0 = bx0.detach().requires_grad_(True)
             C = bC.detach().requires_grad_(True)
             c = bc.detach().requires_grad_(True)
@@ -419,26 +444,8 @@ def run_ours(args):
                 act = ilqr_shard.gather_first_actions(u.detach().permute(1, 0, 2).contiguous(), B * world)
             h_act.copy_(act, non_blocking=True)
             h_gx0.copy_(x0.grad, non_blocking=True)
-            free[i].record(stream)
-            if k + 2 < n:
-                prefetch(k + 2)
 
-        def run_stream(n):
-            prefetch(0)
-            if n > 1:
-                prefetch(1)
-            for k in range(n):
-                stream_step(k, n)
-
-        run_stream(max(3, args.warmup))
-        barrier()
-        e0, e1 = ev(), ev()
-        e0.record(stream)
-        cstream.wait_event(e0)
-        run_stream(args.steps)
-        e1.record(stream)
-        barrier()
-        el = e0.elapsed_time(e1) * 1e-3
+        el = time_streaming(torch, dev, stream, host, e2e_compute, max(3, args.warmup), args.steps, barrier)
         if world > 1:
             t = torch.tensor([el], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -574,16 +581,34 @@ def run_ours(args):
             t = torch.tensor([sel_e2e], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             sel_e2e = float(t.item())
+        def sig_compute(bufs):
+            bx0, bsc, bgx, bgu = bufs
+            x0 = bx0.detach().requires_grad_(True)
+            scd = bsc.detach().requires_grad_(True)
+            x, u, _ = smpc(x0, mpc_compat.SigmoidQuadCost(scd), sdyn)
+            ((x * bgx).sum() + (u * bgu).sum()).backward()
+            h_act.copy_(u[0].detach(), non_blocking=True)
+            h_gx0.copy_(x0.grad, non_blocking=True)
+
+        sel_str = time_streaming(torch, dev, stream, (h_x0, h_sc, h_gX, h_gU), sig_compute, max(3, args.warmup),
+                                 args.steps, barrier)
+        if world > 1:
+            t = torch.tensor([sel_str], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            sel_str = float(t.item())
         h2d = sum(t.numel() * 4 for t in (h_x0, h_sc, h_gX, h_gU))
         sig = {"workload": f"policy_sigmoid_b{B}_t{T}", "value": world * B / (sel / args.steps),
                "unit": "solves/s", "ms_per_step": sel / args.steps * 1e3,
                "kernel_ms": {"solve_mean": statistics.mean(a.elapsed_time(b) for a, b, _ in stim),
                              "backward_mean": statistics.mean(b.elapsed_time(c) for _, b, c in stim)},
                "input": "sigmoid output [B, 28 T] (28 floats per element and step instead of 210)",
-               "e2e": {"value": world * B / (sel_e2e / args.steps), "unit": "solves/s",
+               "e2e": {"value": world * B / (sel_str / args.steps), "unit": "solves/s",
                        "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": (h_act.numel() + h_gx0.numel()) * 4,
-                       "ms_per_step": sel_e2e / args.steps * 1e3,
-                       "path": "mpc_compat.MPC(...)(x_init, SigmoidQuadCost(s), dx) + autograd backward"}}
+                       "ms_per_step": sel_str / args.steps * 1e3,
+                       "path": "mpc_compat.MPC(...)(x_init, SigmoidQuadCost(s), dx) + autograd backward",
+                       "streaming": "inputs of step k+1 copied on a second stream while step k computes (double buffer)",
+                       "sequential": {"value": world * B / (sel_e2e / args.steps),
+                                      "ms_per_step": sel_e2e / args.steps * 1e3}}}
 
     # ---- the policy actor's MPC step: one call vs the reference's chunk loop ---
     # PolicyMPC.actor against a restatement of forward_actor's loop
@@ -736,11 +761,30 @@ def run_ours(args):
                 t = torch.tensor([rel_e2e], device=dev)
                 dist.all_reduce(t, op=dist.ReduceOp.MAX)
                 rel_e2e = float(t.item())
+            def r13_compute(bufs):
+                bx0, bC, bc, bgx, bgu = bufs
+                x0 = bx0.detach().requires_grad_(True)
+                Cd = bC.detach().requires_grad_(True)
+                cd = bc.detach().requires_grad_(True)
+                x, u, _ = rmpc(x0, mpc_compat.QuadCost(Cd, cd), rdyn)
+                ((x * bgx).sum() + (u * bgu).sum()).backward()
+                h_act.copy_(u[0].detach(), non_blocking=True)
+                h_gx0.copy_(x0.grad, non_blocking=True)
+
+            rel_str = time_streaming(torch, dev, stream, (h_x0, h_C, h_c, h_gX, h_gU), r13_compute,
+                                     max(3, args.warmup), args.steps, barrier)
+            if world > 1:
+                t = torch.tensor([rel_str], device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                rel_str = float(t.item())
             h2d = sum(t.numel() * 4 for t in (h_x0, h_C, h_c, h_gX, h_gU))
-            r13_e2e_res = {"value": world * B / (rel_e2e / args.steps), "unit": "solves/s",
+            r13_e2e_res = {"value": world * B / (rel_str / args.steps), "unit": "solves/s",
                            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": (h_act.numel() + h_gx0.numel()) * 4,
-                           "ms_per_step": rel_e2e / args.steps * 1e3,
-                           "path": "mpc_compat.MPC(13, 4, T)(x_init, QuadCost(C, c), dx) + autograd backward"}
+                           "ms_per_step": rel_str / args.steps * 1e3,
+                           "path": "mpc_compat.MPC(13, 4, T)(x_init, QuadCost(C, c), dx) + autograd backward",
+                           "streaming": "inputs of step k+1 copied on a second stream while step k computes",
+                           "sequential": {"value": world * B / (rel_e2e / args.steps),
+                                          "ms_per_step": rel_e2e / args.steps * 1e3}}
         # latency: B = 16, T = 5, 10 iterations, solve + backward, device-resident
         lc13 = wl.CONFIGS["latency_b16_t5"]
         li = wl.make_rotor13_inputs(16, lc13["T"], seed=rank, target=lc13["target"], r=lc13["r"])
