@@ -38,6 +38,7 @@ constexpr int WPC = 4;             // warps per CTA
 constexpr int EPC = EPW * WPC;     // elements per CTA
 constexpr int THREADS = WPC * 32;  // threads per CTA
 constexpr int REC = 20;            // floats per trajectory record: x[13], u[4], 3 pad
+constexpr int SM_COUNT = 148;      // B200 SMs (the launch's one-wave test)
 
 // Shared memory of one element (floats). The block size is an odd multiple
 // of 16 floats, so the two elements of a warp use opposite halves of the
@@ -56,7 +57,8 @@ constexpr int S_KF = 608;    // k_t [4]
 constexpr int S_MK = 612;    // Q_uu k + q_u [4]
 constexpr int S_SVD = 616;   // SVD fallback: matrix [16], inverse [16]
 constexpr int S_TAU = 656;   // per-lane tau scratch of the rollouts [16][17]
-constexpr int S_ELEM = 944;  // floats per element in the solve (59 x 16)
+constexpr int S_LS2 = 928;   // second rollout staging buffer (the first is at 0)
+constexpr int S_ELEM = 1360; // floats per element in the solve (85 x 16)
 constexpr int S_STG = 944;   // backward: two buffers staging a step's inputs
 constexpr int S_ELEM_BWD = 1616;  // floats per element in the backward (101 x 16)
 // One staged backward step (floats, relative to a buffer): C_t (in the tangent
@@ -481,10 +483,11 @@ __device__ __forceinline__ float pick(const float (&v)[N], int i) {
 // ---------------------------------------------------------------------------
 // Solve (controller.py:303-435)
 // ---------------------------------------------------------------------------
-#ifndef ILQR_R13_MINB
-#define ILQR_R13_MINB 2  // resident CTAs per SM the register budget targets
-#endif
-__global__ void __launch_bounds__(THREADS, ILQR_R13_MINB) dense_solve_kernel(DenseSolveParams p) {
+// MINB: resident CTAs per SM the register budget targets. 2 (254 registers,
+// no spills) is faster while the grid fits one wave at 2 CTAs per SM; beyond
+// that 3 (168 registers, about 90 B of spills) is, by the extra warps per SM.
+template <int MINB>
+__global__ void __launch_bounds__(THREADS, MINB) dense_solve_kernel(DenseSolveParams p) {
   extern __shared__ float smem[];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -520,13 +523,6 @@ __global__ void __launch_bounds__(THREADS, ILQR_R13_MINB) dense_solve_kernel(Den
   // references, nominal record, gains) into shared memory while the
   // candidate lanes roll out step t from the staged copy.
   const int nsc = L_NSC;
-  auto scalar_src = [&](int t, int f, bool init) -> float {
-    if (f < L_CV) return __ldg(Cb + (int64_t)t * NT * NT + f);
-    if (f < L_XR) return __ldg(cb + (int64_t)t * NT + (f - L_CV));
-    if (f < L_UR) return xr ? __ldg(xr + t * NX + (f - L_XR)) : 0.0f;
-    if (f < L_U0) return ur ? __ldg(ur + t * NU + (f - L_UR)) : 0.0f;
-    return init ? __ldg(p.U_init + (b * T + t) * NU + (f - L_U0)) : 0.0f;
-  };
   // n_cand candidates, lanes_per_candidate(n_cand) lanes each: every lane of
   // candidate j rolls it out (identical arithmetic) and costs its share of
   // the rows of the quadratic form; the shares are summed at the end.
@@ -540,34 +536,34 @@ __global__ void __launch_bounds__(THREADS, ILQR_R13_MINB) dense_solve_kernel(Den
 #pragma unroll
     for (int jj = 1; jj < ILQR_MAX_ALPHAS_DEV; ++jj) al = (j == jj) ? p.alphas[jj] : al;
     float* ts = sm + S_TAU + g * NT;
-    float pf[L_PF];
-    float4 pf4[2];
-    auto prefetch = [&](int t) {
+    // step t's inputs go to buffer t & 1 by cp.async, issued one step ahead
+    auto buf = [&](int t) { return (t & 1) ? sm + S_LS2 : sm; };
+    auto stage = [&](int t) {
       if (!valid) return;
+      float* st = buf(t);
 #pragma unroll
       for (int k = 0; k < L_PF; ++k) {
         const int f = g + GL * k;
-        if (f < nsc) pf[k] = scalar_src(t, f, init);
-      }
-      if (!init) {
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const int q = g + GL * k;
-          if (q < L_NF4) pf4[k] = q < 5 ? W.rec(nomslot, t)[q] : *W.kcol(t, q - 5);
+        if (f < L_CV) {
+          cp_async4(st + f, Cb + (int64_t)t * NT * NT + f);
+        } else if (f < L_XR) {
+          cp_async4(st + f, cb + (int64_t)t * NT + (f - L_CV));
+        } else if (f < L_UR) {
+          if (xr) cp_async4(st + f, xr + t * NX + (f - L_XR));
+          else st[f] = 0.0f;
+        } else if (f < L_U0) {
+          if (ur) cp_async4(st + f, ur + t * NU + (f - L_UR));
+          else st[f] = 0.0f;
+        } else if (f < nsc && init) {
+          cp_async4(st + f, p.U_init + (b * T + t) * NU + (f - L_U0));
         }
       }
-    };
-    auto commit = [&]() {
-#pragma unroll
-      for (int k = 0; k < L_PF; ++k) {
-        const int f = g + GL * k;
-        if (f < nsc) sm[f] = pf[k];
-      }
       if (!init) {
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
           const int q = g + GL * k;
-          if (q < L_NF4) reinterpret_cast<float4*>(sm + L_F4)[q] = pf4[k];
+          if (q < L_NF4)
+            cp_async16(st + L_F4 + 4 * q, q < 5 ? (const void*)(W.rec(nomslot, t) + q) : (const void*)W.kcol(t, q - 5));
         }
       }
     };
@@ -577,21 +573,28 @@ __global__ void __launch_bounds__(THREADS, ILQR_R13_MINB) dense_solve_kernel(Den
       for (int i = 0; i < NX; ++i) x[i] = __ldg(p.x0 + b * NX + i);
     }
     float sq = 0.0f, sl = 0.0f;
-    prefetch(0);
+    stage(0);
+    cp_async_commit();
     for (int t = 0; t < T; ++t) {
+      __syncwarp();  // every lane is done with buffer (t + 1) & 1 (step t - 1)
+      if (t + 1 < T) {
+        stage(t + 1);
+        cp_async_commit();
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
+      }
       __syncwarp();
-      commit();
-      __syncwarp();
-      if (t + 1 < T) prefetch(t + 1);
+      const float* st = buf(t);
       if (cand) {
         float u[NU];
         if (init) {
 #pragma unroll
-          for (int a = 0; a < NU; ++a) u[a] = sm[L_U0 + a];
+          for (int a = 0; a < NU; ++a) u[a] = st[L_U0 + a];
         } else {
           float xb[NX], ub[NU];
-          load_rec(reinterpret_cast<const float4*>(sm + L_F4), xb, ub);
-          const float4* kc = reinterpret_cast<const float4*>(sm + L_F4) + 5;
+          load_rec(reinterpret_cast<const float4*>(st + L_F4), xb, ub);
+          const float4* kc = reinterpret_cast<const float4*>(st + L_F4) + 5;
           float dx[NX];
 #pragma unroll
           for (int j = 0; j < NX; ++j) dx[j] = x[j] - xb[j];
@@ -623,16 +626,16 @@ __global__ void __launch_bounds__(THREADS, ILQR_R13_MINB) dense_solve_kernel(Den
         if (lead) store_rec(W.rec(cs, t), x, u);
         float tau[NT];
 #pragma unroll
-        for (int i = 0; i < NX; ++i) tau[i] = x[i] - sm[L_XR + i];
+        for (int i = 0; i < NX; ++i) tau[i] = x[i] - st[L_XR + i];
 #pragma unroll
-        for (int a = 0; a < NU; ++a) tau[NX + a] = u[a] - sm[L_UR + a];
+        for (int a = 0; a < NU; ++a) tau[NX + a] = u[a] - st[L_UR + a];
 #pragma unroll
         for (int i = 0; i < NT; ++i) ts[i] = tau[i];
-        sq += step_quad_rows(sm, tau, ts, rsub, lpc);
+        sq += step_quad_rows(st, tau, ts, rsub, lpc);
         if (lead) {
-          float l = sm[L_CV] * tau[0];
+          float l = st[L_CV] * tau[0];
 #pragma unroll
-          for (int jj = 1; jj < NT; ++jj) l = fmaf(sm[L_CV + jj], tau[jj], l);
+          for (int jj = 1; jj < NT; ++jj) l = fmaf(st[L_CV + jj], tau[jj], l);
           sl += l;
         }
         float xn[NX];
@@ -1098,7 +1101,11 @@ static size_t dense_smem_bytes(int elem_floats) { return (size_t)r13::EPC * elem
 cudaError_t launch_dense_solve(const DenseSolveParams& p, cudaStream_t stream) {
   if (p.B == 0) return cudaSuccess;
   const int64_t grid = (p.B + r13::EPC - 1) / r13::EPC;
-  r13::dense_solve_kernel<<<(unsigned)grid, r13::THREADS, dense_smem_bytes(r13::S_ELEM), stream>>>(p);
+  const size_t smem = dense_smem_bytes(r13::S_ELEM);
+  if (grid > 2 * r13::SM_COUNT)
+    r13::dense_solve_kernel<3><<<(unsigned)grid, r13::THREADS, smem, stream>>>(p);
+  else
+    r13::dense_solve_kernel<2><<<(unsigned)grid, r13::THREADS, smem, stream>>>(p);
   return cudaGetLastError();
 }
 

@@ -264,3 +264,28 @@ def test_rotor13_nonfinite_elements_are_isolated():
         assert np.array_equal(r["U"][b], d["U_init"][b])
     assert r["status"][3] & 2 and np.isnan(r["best_cost"][3])
     assert np.isinf(r["best_cost"][7])
+
+
+def test_rotor13_register_tiers_are_bit_identical():
+    """The solve runs a 2-CTA-per-SM register budget for grids of one wave
+    and a 3-CTA one beyond (B > 2368); both give the same bits: the first
+    512 elements of a B=2400 solve equal a B=512 solve (the generator's
+    batches share prefixes), the backward likewise."""
+    cfg, inp = wl.rotor13_config_inputs("rollout_b16384_t20", B=2400)
+    t = lambda a: _t(a)
+    lo, hi = _t(wl.U_MIN13), _t(wl.U_MAX13)
+    gX, gU = wl.make_backward_seeds(2400, cfg["T"], nx=wl.NX13)
+    outs = []
+    for B in (2400, 512):
+        o = nat.rotor13_solve(t(inp["x0"][:B]), t(inp["U_init"][:B]), t(inp["C"][:B]), t(inp["c"][:B]),
+                              u_min=lo, u_max=hi, dt=wl.DT, max_iter=cfg["max_iter"], alphas=cfg["alphas"],
+                              want_trace=True)
+        g = nat.rotor13_backward(o["X"], o["U"], t(inp["C"][:B]), t(gX[:B]), t(gU[:B]), tight=o["tight"],
+                                 dt=wl.DT)
+        outs.append(({k: v[:512].cpu().numpy() for k, v in o.items()},
+                     {k: v[:512].cpu().numpy() for k, v in g.items()}))
+    (o1, g1), (o2, g2) = outs
+    for k in o2:
+        assert np.array_equal(o1[k], o2[k], equal_nan=True), k
+    for k in g2:
+        assert np.array_equal(g1[k], g2[k], equal_nan=True), k
