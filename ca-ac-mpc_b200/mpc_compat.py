@@ -14,6 +14,9 @@ reference DiffMPC's numerics (DifferentialMPC/controller.py): step-size grid
 (1, .8, .5, .2, .1) unless overridden (alphas= or ACMPC_DIFFMPC_ALPHAS),
 regularisation added twice in the gain solve, strict-improvement acceptance,
 isclose tight mask, masked adjoint Riccati with unmasked value update.
+n_state=10 is the reference's CTBR quadrotor; n_state=13 selects the 13-state
+rotor-thrust rigid body (ilqr_native.rotor13_solve / .rotor13_backward), the
+same solver on a model DiffMPC would linearise with GradMethod.AUTO_DIFF.
 """
 
 from __future__ import annotations
