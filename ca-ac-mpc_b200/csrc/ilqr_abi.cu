@@ -31,13 +31,15 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// View of a [B, T, 14, 14] float tensor as {196, T, B}, box {196, 1, 6}:
-// one box is the C_t blocks of the six elements a warp solves.
-int encode_cost_map(CUtensorMap* tm, const float* base, int64_t B, int32_t T) {
+// View of a [B, T, 14, 14] (or, time-major, [T, B, 14, 14]) float tensor as
+// {196, T, B}, box {196, 1, 6}: one box is the C_t blocks of the six elements
+// a warp solves. The two layouts differ only in the strides of T and B.
+int encode_cost_map(CUtensorMap* tm, const float* base, int64_t B, int32_t T, bool time_major) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return ILQR_ERR_CUDA;
   const cuuint64_t dims[3] = {(cuuint64_t)ilqr::CBLK, (cuuint64_t)T, (cuuint64_t)B};
-  const cuuint64_t strides[2] = {(cuuint64_t)ilqr::CBLK * 4u, (cuuint64_t)T * ilqr::CBLK * 4u};
+  const cuuint64_t blk = (cuuint64_t)ilqr::CBLK * 4u;
+  const cuuint64_t strides[2] = {time_major ? (cuuint64_t)B * blk : blk, time_major ? blk : (cuuint64_t)T * blk};
   const cuuint32_t box[3] = {(cuuint32_t)ilqr::CBLK, 1u, (cuuint32_t)ilqr::EPW};
   const cuuint32_t estr[3] = {1u, 1u, 1u};
   std::memset(tm, 0, sizeof(*tm));
@@ -101,7 +103,8 @@ int solve_impl(const float* x0, const float* U_init, const float* C, const float
                const float* u_min, const float* u_max, int64_t B, int32_t T, float dt, int32_t max_iter,
                float reg_eps, const float* alphas, int32_t n_alpha, const int8_t* forced_trace, float* X, float* U,
                uint8_t* tight_mask, int8_t* trace, int32_t* iters, uint32_t* elem_status, float* best_cost,
-               int32_t* stall_iter, float* stall_gap, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+               int32_t* stall_iter, float* stall_gap, void* workspace, size_t workspace_bytes, cudaStream_t stream,
+               bool time_major = false) {
   if (B < 0 || T < 1 || max_iter < 0 || n_alpha < 1 || n_alpha > ILQR_MAX_ALPHAS || alphas == nullptr)
     return ILQR_ERR_INVALID_ARGUMENT;
   if ((u_min == nullptr) != (u_max == nullptr)) return ILQR_ERR_INVALID_ARGUMENT;
@@ -134,10 +137,12 @@ int solve_impl(const float* x0, const float* U_init, const float* C, const float
   const char* dc = std::getenv("ILQR_B200_DIAG_CACHE");
   p.diag_cache = (dc != nullptr && dc[0] == '0') ? 0 : 1;
   p.sig = sig;
+  p.c_bstride = time_major ? ilqr::NT : (int64_t)T * ilqr::NT;
+  p.c_tstride = time_major ? B * ilqr::NT : ilqr::NT;
   CUtensorMap tmC;
   std::memset(&tmC, 0, sizeof(tmC));  // never read in sigmoid mode (no pass copies C)
   if (sig.p == nullptr) {
-    const int st = encode_cost_map(&tmC, C, B, T);
+    const int st = encode_cost_map(&tmC, C, B, T, time_major);
     if (st != ILQR_OK) return st;
   }
   return cuda_status(ilqr::launch_solve(tmC, p, stream));
@@ -147,7 +152,8 @@ int backward_impl(const float* X, const float* U, const float* C, const float* C
                   const float* u_ref, const ilqr::SigmoidCost& sig, const uint8_t* tight_mask, const float* grad_X,
                   const float* grad_U, int64_t B, int32_t T, float dt, float reg_eps, float* grad_x0, float* grad_C,
                   float* grad_c, float* grad_C_final, float* grad_c_final, float* grad_x_ref, float* grad_u_ref,
-                  float* grad_sig, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+                  float* grad_sig, void* workspace, size_t workspace_bytes, cudaStream_t stream,
+                  bool time_major = false) {
   if (B < 0 || T < 1) return ILQR_ERR_INVALID_ARGUMENT;
   if (B == 0) return ILQR_OK;
   if (!X || !U || !grad_X || !grad_U) return ILQR_ERR_INVALID_ARGUMENT;
@@ -167,13 +173,15 @@ int backward_impl(const float* X, const float* U, const float* C, const float* C
   p.write_gC = (sig.p == nullptr && grad_C != nullptr) ? 1 : 0;
   p.sig = sig;
   p.g_sig = grad_sig;
+  p.gc_bstride = time_major ? ilqr::NT : (int64_t)T * ilqr::NT;
+  p.gc_tstride = time_major ? B * ilqr::NT : ilqr::NT;
   CUtensorMap tmC, tmG;
   std::memset(&tmC, 0, sizeof(tmC));  // never read in sigmoid mode
   std::memset(&tmG, 0, sizeof(tmG));
   if (sig.p == nullptr) {
-    int st = encode_cost_map(&tmC, C, B, T);
+    int st = encode_cost_map(&tmC, C, B, T, time_major);
     if (st != ILQR_OK) return st;
-    st = encode_cost_map(&tmG, grad_C != nullptr ? grad_C : C, B, T);
+    st = encode_cost_map(&tmG, grad_C != nullptr ? grad_C : C, B, T, time_major);
     if (st != ILQR_OK) return st;
   }
   return cuda_status(ilqr::launch_backward(tmC, tmG, p, stream));
@@ -195,6 +203,21 @@ int ilqr_b200_solve_f32(const float* x0, const float* U_init, const float* C, co
   return solve_impl(x0, U_init, C, c, C_final, c_final, x_ref, u_ref, none, u_min, u_max, B, T, dt, max_iter,
                     reg_eps, alphas, n_alpha, forced_trace, X, U, tight_mask, trace, iters, elem_status, best_cost,
                     stall_iter, stall_gap, workspace, workspace_bytes, stream);
+}
+
+int ilqr_b200_solve_tm_f32(const float* x0, const float* U_init, const float* C, const float* c,
+                           const float* C_final, const float* c_final, const float* x_ref, const float* u_ref,
+                           const float* u_min, const float* u_max, int64_t B, int32_t T, float dt,
+                           int32_t max_iter, float reg_eps, float converge_tol, const float* alphas,
+                           int32_t n_alpha, const int8_t* forced_trace, float* X, float* U, uint8_t* tight_mask,
+                           int8_t* trace, int32_t* iters, uint32_t* elem_status, float* best_cost,
+                           int32_t* stall_iter, float* stall_gap, void* workspace, size_t workspace_bytes,
+                           cudaStream_t stream) {
+  (void)converge_tol;
+  const ilqr::SigmoidCost none{nullptr, 0.0f, 0.0f, 0.0f, 0.0f};
+  return solve_impl(x0, U_init, C, c, C_final, c_final, x_ref, u_ref, none, u_min, u_max, B, T, dt, max_iter,
+                    reg_eps, alphas, n_alpha, forced_trace, X, U, tight_mask, trace, iters, elem_status, best_cost,
+                    stall_iter, stall_gap, workspace, workspace_bytes, stream, true);
 }
 
 int ilqr_b200_solve_sigmoid_f32(const float* x0, const float* U_init, const float* sigmoid_cost, float cost_eps,
@@ -223,6 +246,18 @@ int ilqr_b200_backward_f32(const float* X, const float* U, const float* C, const
   return backward_impl(X, U, C, C_final, x_ref, u_ref, none, tight_mask, grad_X, grad_U, B, T, dt, reg_eps, grad_x0,
                        grad_C, grad_c, grad_C_final, grad_c_final, grad_x_ref, grad_u_ref, nullptr, workspace,
                        workspace_bytes, stream);
+}
+
+int ilqr_b200_backward_tm_f32(const float* X, const float* U, const float* C, const float* C_final,
+                              const float* x_ref, const float* u_ref, const uint8_t* tight_mask,
+                              const float* grad_X, const float* grad_U, int64_t B, int32_t T, float dt,
+                              float reg_eps, float* grad_x0, float* grad_C, float* grad_c, float* grad_C_final,
+                              float* grad_c_final, float* grad_x_ref, float* grad_u_ref, void* workspace,
+                              size_t workspace_bytes, cudaStream_t stream) {
+  const ilqr::SigmoidCost none{nullptr, 0.0f, 0.0f, 0.0f, 0.0f};
+  return backward_impl(X, U, C, C_final, x_ref, u_ref, none, tight_mask, grad_X, grad_U, B, T, dt, reg_eps, grad_x0,
+                       grad_C, grad_c, grad_C_final, grad_c_final, grad_x_ref, grad_u_ref, nullptr, workspace,
+                       workspace_bytes, stream, true);
 }
 
 int ilqr_b200_backward_sigmoid_f32(const float* X, const float* U, const float* sigmoid_cost, float cost_eps,

@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(32, MINB) backward_kernel(const __grid_constan
       for (int s = 0; s < nrows; ++s) {
         const int i = m + TEAM * s;
         const float di = pick14(dtau, i);
-        if (p.g_c != nullptr) p.g_c[(b * T + t) * NT + i] = -di;
+        if (p.g_c != nullptr) p.g_c[b * p.gc_bstride + t * p.gc_tstride + i] = -di;
         if (i < NX && p.g_xref != nullptr) p.g_xref[(b * (T + 1) + t) * NX + i] = di;
         if (i >= NX && p.g_uref != nullptr) p.g_uref[(b * T + t) * NU + (i - NX)] = di;
       }

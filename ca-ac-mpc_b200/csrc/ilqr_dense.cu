@@ -505,8 +505,10 @@ __global__ void __launch_bounds__(THREADS, MINB) dense_solve_kernel(DenseSolvePa
   const float* lo = p.has_bounds ? p.u_min : nullptr;
   const float* hi = p.has_bounds ? p.u_max : nullptr;
   Ws W{p.ws + bw * p.ws_fields, T, p.n_alpha + 1};
-  const float* Cb = p.C + bw * (int64_t)T * NT * NT;
-  const float* cb = p.c + bw * (int64_t)T * NT;
+  // step t's cost block and linear term (batch-major or time-major layout)
+  const int64_t cbs = p.cost_bstride, cts = p.cost_tstride;
+  auto Cstep = [&](int t) { return p.C + (bw * cbs + (int64_t)t * cts) * (NT * NT); };
+  auto cstep = [&](int t) { return p.c + (bw * cbs + (int64_t)t * cts) * NT; };
   const float* Cf = p.C_f ? p.C_f + bw * NT * NT : nullptr;
   const float* cf = p.c_f ? p.c_f + bw * NT : nullptr;
   const float* xr = p.x_ref ? p.x_ref + bw * (int64_t)(T + 1) * NX : nullptr;
@@ -545,9 +547,9 @@ __global__ void __launch_bounds__(THREADS, MINB) dense_solve_kernel(DenseSolvePa
       for (int k = 0; k < L_PF; ++k) {
         const int f = g + GL * k;
         if (f < L_CV) {
-          cp_async4(st + f, Cb + (int64_t)t * NT * NT + f);
+          cp_async4(st + f, Cstep(t) + f);
         } else if (f < L_XR) {
-          cp_async4(st + f, cb + (int64_t)t * NT + (f - L_CV));
+          cp_async4(st + f, cstep(t) + (f - L_CV));
         } else if (f < L_UR) {
           if (xr) cp_async4(st + f, xr + t * NX + (f - L_XR));
           else st[f] = 0.0f;
@@ -711,8 +713,8 @@ __global__ void __launch_bounds__(THREADS, MINB) dense_solve_kernel(DenseSolvePa
       for (int i = 0; i < NX; ++i) tau[i] = sm[S_Z + i] - xref(t, i);
 #pragma unroll
       for (int a = 0; a < NU; ++a) tau[NX + a] = sm[S_Z + NX + a] - uref(t, a);
-      const float* Ct = Cb + (int64_t)t * NT * NT;
-      const float* ct = cb + (int64_t)t * NT;
+      const float* Ct = Cstep(t);
+      const float* ct = cstep(t);
       StepIn in;
       in.lx = 0.0f;
       in.lu = 0.0f;
@@ -864,7 +866,8 @@ __global__ void __launch_bounds__(THREADS, 4) dense_backward_kernel(DenseBackwar
   const bool rowx = g < NX;
   const float* Xb = p.X + bw * (int64_t)(T + 1) * NX;
   const float* Ub = p.U + bw * (int64_t)T * NU;
-  const float* Cb = p.C + bw * (int64_t)T * NT * NT;
+  const int64_t cbs = p.cost_bstride, cts = p.cost_tstride;
+  auto Cstep = [&](int t) { return p.C + (bw * cbs + (int64_t)t * cts) * (NT * NT); };
   const float* Cf = p.C_f ? p.C_f + bw * NT * NT : nullptr;
   const float* xr = p.x_ref ? p.x_ref + bw * (int64_t)(T + 1) * NX : nullptr;
   const float* gX = p.gX + bw * (int64_t)(T + 1) * NX;
@@ -890,7 +893,7 @@ __global__ void __launch_bounds__(THREADS, 4) dense_backward_kernel(DenseBackwar
     if (g < NU) cp_async4(st + R_REC + NX + g, Ub + t * NU + g);
   };
   auto bwd_stage = [&](int t, float* st) {
-    const float* Ct = Cb + (int64_t)t * NT * NT;
+    const float* Ct = Cstep(t);
     for (int f = g; f < NT * NT; f += GL) cp_async4(st + R_C + f, Ct + f);
     stage_z(t, st);
     if (g < NX) cp_async4(st + R_GX + g, gX + t * NX + g);
@@ -1007,7 +1010,7 @@ __global__ void __launch_bounds__(THREADS, 4) dense_backward_kernel(DenseBackwar
     if (valid) {
       // dtau = [dX_t; dU_t], z = [X_t; U_t]:
       // grad_C_t = -1/2 (dtau z^T + z dtau^T), grad_c_t = -dtau
-      const int64_t off = (b * T + t) * NT;
+      const int64_t off = (b * cbs + (int64_t)t * cts) * NT;
       const float* z = st + R_REC;
       auto grad_row = [&](int i, float* gC) {
         const float dzi = dts[i], zi = z[i];

@@ -49,6 +49,10 @@ struct SolveParams {
   int has_bounds;
   int diag_cache;  // 1: detect diagonal C_t blocks and stop re-reading them after the first pass
   SigmoidCost sig;  // sig.p != nullptr: costs built from policy parameters (C, c unused)
+  // floats between the c records of consecutive elements / steps: T * 14 / 14
+  // for batch-major costs [B, T, 14], 14 / B * 14 for time-major [T, B, 14]
+  int64_t c_bstride;
+  int64_t c_tstride;
 };
 
 struct BackwardParams {
@@ -75,6 +79,8 @@ struct BackwardParams {
   int write_gC;
   SigmoidCost sig;  // sig.p != nullptr: costs from policy parameters; grad goes to g_sig
   float* g_sig;     // [B, 28 T] gradient of the parameters (sigmoid mode)
+  int64_t gc_bstride;  // layout of grad_c, as SolveParams::c_bstride / c_tstride
+  int64_t gc_tstride;
 };
 
 // Solve workspace, in floats, element-interleaved with stride S (the record
@@ -128,6 +134,10 @@ struct DenseSolveParams {
   float alphas[ILQR_MAX_ALPHAS_DEV];
   int n_alpha;
   int has_bounds;
+  // C blocks (and c records) between consecutive elements / steps: (T, 1)
+  // batch-major [B, T, ...], (1, B) time-major [T, B, ...]
+  int64_t cost_bstride;
+  int64_t cost_tstride;
 };
 
 struct DenseBackwardParams {
@@ -152,6 +162,8 @@ struct DenseBackwardParams {
   int T;
   float dt;
   float reg;
+  int64_t cost_bstride;  // C, c, grad_C, grad_c layout, as DenseSolveParams
+  int64_t cost_tstride;
 };
 
 // Per-element workspace of the dense solve: (n_alpha + 1) trajectory slots of

@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
   const bool bounds = p.has_bounds != 0;
   const float* lo = bounds ? p.u_min : nullptr;
   const float* hi = bounds ? p.u_max : nullptr;
-  const float* cb = p.c != nullptr ? p.c + b * (int64_t)T * NT : nullptr;
+  const float* cb = p.c != nullptr ? p.c + b * p.c_bstride : nullptr;
   const float* xrb = (HAS_REF && p.x_ref != nullptr) ? p.x_ref + b * (int64_t)(T + 1) * NX : nullptr;
   const float* urb = (HAS_REF && p.u_ref != nullptr) ? p.u_ref + b * (int64_t)T * NU : nullptr;
   auto xref = [&](int t, int i) { return (HAS_REF && xrb != nullptr) ? ldg_or0(xrb + t * NX + i, valid) : 0.0f; };
@@ -345,9 +345,9 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
         cb_ = sig_c(p.sig, sgrow, T, t, rb);
         cu = sig_c(p.sig, sgrow, T, t, ru);
       } else if (first) {
-        ca_ = ldg_or0(cb + t * NT + ra, valid);
-        cb_ = ldg_or0(cb + t * NT + rb, valid);
-        cu = ldg_or0(cb + t * NT + ru, valid);
+        ca_ = ldg_or0(cb + t * p.c_tstride + ra, valid);
+        cb_ = ldg_or0(cb + t * p.c_tstride + rb, valid);
+        cu = ldg_or0(cb + t * p.c_tstride + ru, valid);
       } else {
         const float* cr = W.cvec(t);
         ca_ = cr[ra];

@@ -72,6 +72,14 @@ def lib():
             "ilqr_b200_rotor13_backward_f32": ([_P] * 9 + [_I64, _I32, _F, _F] + [_P] * 7
                                                + [_P, ctypes.c_size_t, _P], _I32),
             "ilqr_b200_rotor13_dynamics_f32": ([_P, _P, _I64, _F, _P, _P], _I32),
+            "ilqr_b200_solve_tm_f32": ([_P] * 10 + [_I64, _I32, _F, _I32, _F, _F, _P, _I32, _P]
+                                       + [_P] * 9 + [_P, ctypes.c_size_t, _P], _I32),
+            "ilqr_b200_backward_tm_f32": ([_P] * 9 + [_I64, _I32, _F, _F] + [_P] * 7
+                                          + [_P, ctypes.c_size_t, _P], _I32),
+            "ilqr_b200_rotor13_solve_tm_f32": ([_P] * 10 + [_I64, _I32, _F, _I32, _F, _F, _P, _I32, _P]
+                                               + [_P] * 9 + [_P, ctypes.c_size_t, _P], _I32),
+            "ilqr_b200_rotor13_backward_tm_f32": ([_P] * 9 + [_I64, _I32, _F, _F] + [_P] * 7
+                                                  + [_P, ctypes.c_size_t, _P], _I32),
             "ilqr_b200_rotor13_linearize_f32": ([_P, _P, _I64, _I32, _F, _P, _P, _P], _I32),
         }
         for name, (argt, rest) in sig.items():
@@ -93,7 +101,8 @@ EXPORTED_SYMBOLS = (
     "ilqr_b200_solve_sigmoid_f32", "ilqr_b200_backward_sigmoid_f32", "ilqr_b200_pnqp4_batch_f32",
     "ilqr_b200_rotor13_solve_workspace_size", "ilqr_b200_rotor13_backward_workspace_size",
     "ilqr_b200_rotor13_solve_f32", "ilqr_b200_rotor13_backward_f32", "ilqr_b200_rotor13_dynamics_f32",
-    "ilqr_b200_rotor13_linearize_f32",
+    "ilqr_b200_rotor13_linearize_f32", "ilqr_b200_solve_tm_f32", "ilqr_b200_backward_tm_f32",
+    "ilqr_b200_rotor13_solve_tm_f32", "ilqr_b200_rotor13_backward_tm_f32",
 )
 
 
@@ -157,12 +166,13 @@ def workspace_bytes(kind: str, B: int, T: int) -> int:
 def solve(x0, U_init, C, c, C_final=None, c_final=None, x_ref=None, u_ref=None,
           u_min=None, u_max=None, dt=0.05, max_iter=10, reg_eps=1e-6, converge_tol=1e-6,
           alphas: Sequence[float] = DEFAULT_ALPHAS, forced_trace=None, want_trace=False,
-          want_stats=False):
+          want_stats=False, time_major=False):
     """Batched iLQR solve (DifferentiableMPCController.solve_step semantics).
 
     Returns dict(X [B,T+1,10], U [B,T,4], tight [B,T,4] uint8) plus, when
     requested, trace [B,max_iter] int8 and per-element iters / status /
-    best_cost / stall_iter / stall_gap.
+    best_cost / stall_iter / stall_gap. time_major: C [T,B,14,14] and
+    c [T,B,14] (mpc.pytorch's layout) instead of [B,T,...].
     """
     L = lib()
     dev = _cuda_device(x0, "x0")
@@ -171,8 +181,9 @@ def solve(x0, U_init, C, c, C_final=None, c_final=None, x_ref=None, u_ref=None,
     T = U_init.shape[1]
     _req(x0, "x0", (B, NX), dev)
     _req(U_init, "U_init", (B, T, NU), dev)
-    _req(C, "C", (B, T, N, N), dev)
-    _req(c, "c", (B, T, N), dev)
+    bt = (T, B) if time_major else (B, T)
+    _req(C, "C", (*bt, N, N), dev)
+    _req(c, "c", (*bt, N), dev)
     _opt(C_final, "C_final", (B, N, N), dev)
     _opt(c_final, "c_final", (B, N), dev)
     _opt(x_ref, "x_ref", (B, T + 1, NX), dev)
@@ -203,7 +214,8 @@ def solve(x0, U_init, C, c, C_final=None, c_final=None, x_ref=None, u_ref=None,
     nbytes = workspace_bytes("solve", B, T)
     ws = torch.empty(max(nbytes, 1), device=dev, dtype=torch.uint8)
     a_arr = (ctypes.c_float * len(al))(*al)
-    st = L.ilqr_b200_solve_f32(
+    fn = L.ilqr_b200_solve_tm_f32 if time_major else L.ilqr_b200_solve_f32
+    st = fn(
         _ptr(x0), _ptr(U_init), _ptr(C), _ptr(c), _ptr(C_final), _ptr(c_final), _ptr(x_ref),
         _ptr(u_ref), _ptr(u_min), _ptr(u_max), B, T, float(dt), int(max_iter), float(reg_eps),
         float(converge_tol), ctypes.cast(a_arr, ctypes.c_void_p), len(al), _ptr(forced_trace), _ptr(X), _ptr(U), _ptr(tight),
@@ -214,10 +226,11 @@ def solve(x0, U_init, C, c, C_final=None, c_final=None, x_ref=None, u_ref=None,
 
 
 def backward(X, U, C, grad_X, grad_U, C_final=None, x_ref=None, u_ref=None, tight=None,
-             dt=0.05, reg_eps=1e-6, need=("x0", "C", "c")):
+             dt=0.05, reg_eps=1e-6, need=("x0", "C", "c"), time_major=False):
     """Fused implicit-diff backward at a solved (X, U) (ILQRSolve.backward
     semantics). `need` selects outputs among x0, C, c, C_final, c_final,
-    x_ref, u_ref; returns a dict with those keys."""
+    x_ref, u_ref; returns a dict with those keys. time_major: C and the
+    gradients of C, c are [T,B,...]."""
     L = lib()
     dev = _cuda_device(X, "X")
     _device_ok(dev)
@@ -225,20 +238,22 @@ def backward(X, U, C, grad_X, grad_U, C_final=None, x_ref=None, u_ref=None, tigh
     T = T1 - 1
     _req(X, "X", (B, T + 1, NX), dev)
     _req(U, "U", (B, T, NU), dev)
-    _req(C, "C", (B, T, N, N), dev)
+    bt = (T, B) if time_major else (B, T)
+    _req(C, "C", (*bt, N, N), dev)
     _req(grad_X, "grad_X", (B, T + 1, NX), dev)
     _req(grad_U, "grad_U", (B, T, NU), dev)
     _opt(C_final, "C_final", (B, N, N), dev)
     _opt(x_ref, "x_ref", (B, T + 1, NX), dev)
     _opt(u_ref, "u_ref", (B, T, NU), dev)
     _opt(tight, "tight_mask", (B, T, NU), dev, torch.uint8)
-    shapes = dict(x0=(B, NX), C=(B, T, N, N), c=(B, T, N), C_final=(B, N, N), c_final=(B, N),
+    shapes = dict(x0=(B, NX), C=(*bt, N, N), c=(*bt, N), C_final=(B, N, N), c_final=(B, N),
                   x_ref=(B, T + 1, NX), u_ref=(B, T, NU))
     out = {k: torch.empty(shapes[k], device=dev) for k in need}
     nbytes = workspace_bytes("backward", B, T)
     ws = torch.empty(max(nbytes, 1), device=dev, dtype=torch.uint8)
     g = lambda k: _ptr(out.get(k))
-    st = L.ilqr_b200_backward_f32(
+    fn = L.ilqr_b200_backward_tm_f32 if time_major else L.ilqr_b200_backward_f32
+    st = fn(
         _ptr(X), _ptr(U), _ptr(C), _ptr(C_final), _ptr(x_ref), _ptr(u_ref), _ptr(tight),
         _ptr(grad_X), _ptr(grad_U), B, T, float(dt), float(reg_eps),
         g("x0"), g("C"), g("c"), g("C_final"), g("c_final"), g("x_ref"), g("u_ref"),
@@ -608,8 +623,9 @@ HOVER_U13 = MASS13 * 9.8066 / (4.0 * F_MAX13)  # per-rotor hover thrust fraction
 def rotor13_solve(x0, U_init, C, c, C_final=None, c_final=None, x_ref=None, u_ref=None,
                   u_min=None, u_max=None, dt=0.05, max_iter=10, reg_eps=1e-6, converge_tol=1e-6,
                   alphas: Sequence[float] = DEFAULT_ALPHAS, forced_trace=None, want_trace=False,
-                  want_stats=False):
-    """solve() for the rotor model: X [B,T+1,13], U [B,T,4], C [B,T,17,17]."""
+                  want_stats=False, time_major=False):
+    """solve() for the rotor model: X [B,T+1,13], U [B,T,4], C [B,T,17,17]
+    ([T,B,17,17] and c [T,B,17] when time_major)."""
     L = lib()
     dev = _cuda_device(x0, "x0")
     _device_ok(dev)
@@ -617,8 +633,9 @@ def rotor13_solve(x0, U_init, C, c, C_final=None, c_final=None, x_ref=None, u_re
     T = U_init.shape[1]
     _req(x0, "x0", (B, NX13), dev)
     _req(U_init, "U_init", (B, T, NU), dev)
-    _req(C, "C", (B, T, N13, N13), dev)
-    _req(c, "c", (B, T, N13), dev)
+    bt = (T, B) if time_major else (B, T)
+    _req(C, "C", (*bt, N13, N13), dev)
+    _req(c, "c", (*bt, N13), dev)
     _opt(C_final, "C_final", (B, N13, N13), dev)
     _opt(c_final, "c_final", (B, N13), dev)
     _opt(x_ref, "x_ref", (B, T + 1, NX13), dev)
@@ -651,7 +668,8 @@ def rotor13_solve(x0, U_init, C, c, C_final=None, c_final=None, x_ref=None, u_re
     nbytes = int(n.value)
     ws = torch.empty(max(nbytes, 16), device=dev, dtype=torch.uint8)
     a_arr = (ctypes.c_float * len(al))(*al)
-    st = L.ilqr_b200_rotor13_solve_f32(
+    fn = L.ilqr_b200_rotor13_solve_tm_f32 if time_major else L.ilqr_b200_rotor13_solve_f32
+    st = fn(
         _ptr(x0), _ptr(U_init), _ptr(C), _ptr(c), _ptr(C_final), _ptr(c_final), _ptr(x_ref),
         _ptr(u_ref), _ptr(u_min), _ptr(u_max), B, T, float(dt), int(max_iter), float(reg_eps),
         float(converge_tol), ctypes.cast(a_arr, ctypes.c_void_p), len(al), _ptr(forced_trace), _ptr(X), _ptr(U),
@@ -662,8 +680,8 @@ def rotor13_solve(x0, U_init, C, c, C_final=None, c_final=None, x_ref=None, u_re
 
 
 def rotor13_backward(X, U, C, grad_X, grad_U, C_final=None, x_ref=None, u_ref=None, tight=None,
-                     dt=0.05, reg_eps=1e-6, need=("x0", "C", "c")):
-    """backward() for the rotor model; `need` as there."""
+                     dt=0.05, reg_eps=1e-6, need=("x0", "C", "c"), time_major=False):
+    """backward() for the rotor model; `need` and `time_major` as there."""
     L = lib()
     dev = _cuda_device(X, "X")
     _device_ok(dev)
@@ -671,14 +689,15 @@ def rotor13_backward(X, U, C, grad_X, grad_U, C_final=None, x_ref=None, u_ref=No
     T = T1 - 1
     _req(X, "X", (B, T + 1, NX13), dev)
     _req(U, "U", (B, T, NU), dev)
-    _req(C, "C", (B, T, N13, N13), dev)
+    bt = (T, B) if time_major else (B, T)
+    _req(C, "C", (*bt, N13, N13), dev)
     _req(grad_X, "grad_X", (B, T + 1, NX13), dev)
     _req(grad_U, "grad_U", (B, T, NU), dev)
     _opt(C_final, "C_final", (B, N13, N13), dev)
     _opt(x_ref, "x_ref", (B, T + 1, NX13), dev)
     _opt(u_ref, "u_ref", (B, T, NU), dev)
     _opt(tight, "tight_mask", (B, T, NU), dev, torch.uint8)
-    shapes = dict(x0=(B, NX13), C=(B, T, N13, N13), c=(B, T, N13), C_final=(B, N13, N13),
+    shapes = dict(x0=(B, NX13), C=(*bt, N13, N13), c=(*bt, N13), C_final=(B, N13, N13),
                   c_final=(B, N13), x_ref=(B, T + 1, NX13), u_ref=(B, T, NU))
     out = {k: torch.empty(shapes[k], device=dev) for k in need}
     n = ctypes.c_size_t(0)
@@ -686,7 +705,8 @@ def rotor13_backward(X, U, C, grad_X, grad_U, C_final=None, x_ref=None, u_ref=No
     nbytes = int(n.value)
     ws = torch.empty(max(nbytes, 16), device=dev, dtype=torch.uint8)
     g = lambda k: _ptr(out.get(k))
-    st = L.ilqr_b200_rotor13_backward_f32(
+    fn = L.ilqr_b200_rotor13_backward_tm_f32 if time_major else L.ilqr_b200_rotor13_backward_f32
+    st = fn(
         _ptr(X), _ptr(U), _ptr(C), _ptr(C_final), _ptr(x_ref), _ptr(u_ref), _ptr(tight),
         _ptr(grad_X), _ptr(grad_U), B, T, float(dt), float(reg_eps),
         g("x0"), g("C"), g("c"), g("C_final"), g("c_final"), g("x_ref"), g("u_ref"),

@@ -86,6 +86,24 @@ def _normalize_cost(C: Tensor, c: Optional[Tensor], B: int, T: int, n: int,
     return C.permute(1, 0, 2, 3).contiguous().float(), c.permute(1, 0, 2).contiguous().float()
 
 
+def _normalize_cost_tm(C: Tensor, c: Optional[Tensor], B: int, T: int, n: int, device, dtype) -> tuple:
+    """(C, c) as time-major [T, B, n, n] / [T, B, n] float32 contiguous: the
+    QuadCost layout itself, passed to the kernels without the reference's
+    transpose to batch-major (a contiguous float32 [T, B, n, n] C is used as
+    is, and its gradient comes back in the same layout)."""
+    if C.ndim == 2:
+        C = C.unsqueeze(0).unsqueeze(0).expand(T, B, n, n)
+    elif C.ndim == 3:
+        C = C.unsqueeze(1).expand(T, B, n, n)
+    if c is None:
+        c = _zeros((T, B, n), device, dtype)
+    elif c.ndim == 1:
+        c = c.unsqueeze(0).unsqueeze(0).expand(T, B, n)
+    elif c.ndim == 2:
+        c = c.unsqueeze(1).expand(T, B, n)
+    return C.contiguous().float(), c.contiguous().float()
+
+
 def _normalize_bounds(u_lower, u_upper, nu, device, dtype):
     """Flatten box bounds to [nu] float32 (mpc_compat.py:99-110); (None, None)
     when either is missing."""
@@ -130,7 +148,8 @@ class DroneMPCFunction(torch.autograd.Function):
 
     forward(x0 [B,10], C [B,T,n,n], c [B,T,n], C_final [B,n,n] or None,
     c_final [B,n] or None, x_ref [B,T+1,nx] or None, u_ref [B,T,nu] or None,
-    solver_cfg) -> (X [B,T+1,nx], U [B,T,nu]), as the reference's
+    solver_cfg) -> (X [B,T+1,nx], U [B,T,nu]) (C, c time-major [T,B,...] when
+    solver_cfg["time_major"]), as the reference's
     DroneMPCFunction (mpc_compat.py:128-185). backward runs the fused
     implicit-diff kernel (ILQRSolve.backward semantics, controller.py:68-133):
     gradients w.r.t. x0, C, c, C_final, c_final, x_ref, u_ref.
@@ -141,12 +160,13 @@ class DroneMPCFunction(torch.autograd.Function):
     def forward(ctx, x0, C_bt, c_bt, C_final, c_final, x_ref, u_ref, solver_cfg):
         r13 = solver_cfg.get("nx", _nat.NX) == _nat.NX13
         ctx.r13 = r13
+        ctx.time_major = bool(solver_cfg.get("time_major", False))
         out = (_nat.rotor13_solve if r13 else _nat.solve)(
             _f32(x0), _f32(solver_cfg["U_init"]), _f32(C_bt), _f32(c_bt), _f32(C_final),
             _f32(c_final), _f32(x_ref), _f32(u_ref), solver_cfg.get("u_min"), solver_cfg.get("u_max"),
             dt=solver_cfg["dt"], max_iter=solver_cfg["lqr_iter"], reg_eps=solver_cfg["eps"],
             converge_tol=solver_cfg.get("converge_tol", 1e-6),
-            alphas=solver_cfg.get("alphas", _nat.DEFAULT_ALPHAS))
+            alphas=solver_cfg.get("alphas", _nat.DEFAULT_ALPHAS), time_major=ctx.time_major)
         X, U = out["X"], out["U"]
         ctx.save_for_backward(X, U, _f32(C_bt), _f32(C_final) if C_final is not None else None,
                               _f32(x_ref) if x_ref is not None else None, out["tight"])
@@ -166,7 +186,7 @@ class DroneMPCFunction(torch.autograd.Function):
         gU = torch.zeros_like(U) if grad_U is None else grad_U.to(torch.float32).contiguous()
         bwd = _nat.rotor13_backward if ctx.r13 else _nat.backward
         g = bwd(X, U, C_bt, gX, gU, C_final=C_final, x_ref=x_ref, tight=tight,
-                dt=ctx.dt, reg_eps=ctx.reg_eps, need=want)
+                dt=ctx.dt, reg_eps=ctx.reg_eps, need=want, time_major=ctx.time_major)
         return tuple(g.get(nm) for nm in names) + (None,)
 
 
@@ -298,13 +318,13 @@ class FastMPC(nn.Module):
         if sigm and r13:
             raise ValueError("SigmoidQuadCost builds the 10-state policy's costs; use QuadCost with n_state=13")
         if not sigm:
-            C_bt, c_bt = _normalize_cost(cost.C, cost.c, B, T, n, device, dtype)
+            C_tb, c_tb = _normalize_cost_tm(cost.C, cost.c, B, T, n, device, dtype)
         u_min, u_max = self._get_bounds(device, dtype)
         U_init = _normalize_init(self.u_init, B, T, nu, device, dtype, nx)
         x0 = x_init.float().contiguous()
         cfg = {"U_init": U_init, "u_min": u_min, "u_max": u_max, "dt": float(dt),
                "lqr_iter": self.lqr_iter, "eps": self.eps, "converge_tol": 1e-6,
-               "reg_eps": self.eps, "nx": nx, "nu": nu, "alphas": self._alphas()}
+               "reg_eps": self.eps, "nx": nx, "nu": nu, "alphas": self._alphas(), "time_major": True}
         if sigm:
             cfg["sigmoid_spec"] = cost.spec()
             if torch.is_grad_enabled() and self.backprop:
@@ -316,13 +336,13 @@ class FastMPC(nn.Module):
                                              converge_tol=1e-6, alphas=self._alphas())
                 X, U = out["X"], out["U"]
         elif torch.is_grad_enabled() and self.backprop:
-            X, U = DroneMPCFunction.apply(x0, C_bt, c_bt, None, None, None, None, cfg)
+            X, U = DroneMPCFunction.apply(x0, C_tb, c_tb, None, None, None, None, cfg)
         else:
             with torch.inference_mode():
                 out = (_nat.rotor13_solve if r13 else _nat.solve)(
-                    x0, U_init, C_bt, c_bt, None, None, None, None, u_min, u_max,
+                    x0, U_init, C_tb, c_tb, None, None, None, None, u_min, u_max,
                     dt=float(dt), max_iter=self.lqr_iter, reg_eps=self.eps,
-                    converge_tol=1e-6, alphas=self._alphas())
+                    converge_tol=1e-6, alphas=self._alphas(), time_major=True)
             X, U = out["X"], out["U"]
         x_out = X.permute(1, 0, 2).contiguous()
         u_out = U.permute(1, 0, 2).contiguous()

@@ -167,6 +167,33 @@ int ilqr_b200_backward_f32(
     void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /*
+ * ilqr_b200_solve_f32 / ilqr_b200_backward_f32 with time-major costs: C and
+ * grad_C [T,B,14,14], c and grad_c [T,B,14] -- the layout of mpc.pytorch's
+ * QuadCost, which the MPC operator receives (differentialMPCPerformance/
+ * mpc_compat.py:80-96 copies it to batch-major). Every other argument, and
+ * every result, as there; results equal those entry points' on the same costs.
+ */
+int ilqr_b200_solve_tm_f32(
+    const float* x0, const float* U_init, const float* C, const float* c,
+    const float* C_final, const float* c_final, const float* x_ref, const float* u_ref,
+    const float* u_min, const float* u_max,
+    int64_t B, int32_t T, float dt, int32_t max_iter, float reg_eps, float converge_tol,
+    const float* alphas, int32_t n_alpha, const int8_t* forced_trace,
+    float* X, float* U, uint8_t* tight_mask,
+    int8_t* trace, int32_t* iters, uint32_t* elem_status, float* best_cost,
+    int32_t* stall_iter, float* stall_gap,
+    void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+int ilqr_b200_backward_tm_f32(
+    const float* X, const float* U, const float* C, const float* C_final,
+    const float* x_ref, const float* u_ref, const uint8_t* tight_mask,
+    const float* grad_X, const float* grad_U,
+    int64_t B, int32_t T, float dt, float reg_eps,
+    float* grad_x0, float* grad_C, float* grad_c, float* grad_C_final,
+    float* grad_c_final, float* grad_x_ref, float* grad_u_ref,
+    void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/*
  * Costs from policy parameters. The policy builds its dense costs from a
  * sigmoid output s [B, 28 T] in a Python loop over t
  * (_build_cost_tensors, acmpc_public-master/training_modules/mlp_mpc_policy_diffmpc.py:194-247)
@@ -299,6 +326,28 @@ int ilqr_b200_rotor13_backward_workspace_size(int64_t B, int32_t T, size_t* byte
  * NULL. u_ref is accepted for symmetry and not read.
  */
 int ilqr_b200_rotor13_backward_f32(
+    const float* X, const float* U, const float* C, const float* C_final,
+    const float* x_ref, const float* u_ref, const uint8_t* tight_mask,
+    const float* grad_X, const float* grad_U,
+    int64_t B, int32_t T, float dt, float reg_eps,
+    float* grad_x0, float* grad_C, float* grad_c, float* grad_C_final,
+    float* grad_c_final, float* grad_x_ref, float* grad_u_ref,
+    void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* The rotor-model solve and backward with time-major costs (C, grad_C
+ * [T,B,17,17], c, grad_c [T,B,17]); otherwise as the two entry points above. */
+int ilqr_b200_rotor13_solve_tm_f32(
+    const float* x0, const float* U_init, const float* C, const float* c,
+    const float* C_final, const float* c_final, const float* x_ref, const float* u_ref,
+    const float* u_min, const float* u_max,
+    int64_t B, int32_t T, float dt, int32_t max_iter, float reg_eps, float converge_tol,
+    const float* alphas, int32_t n_alpha, const int8_t* forced_trace,
+    float* X, float* U, uint8_t* tight_mask,
+    int8_t* trace, int32_t* iters, uint32_t* elem_status, float* best_cost,
+    int32_t* stall_iter, float* stall_gap,
+    void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+int ilqr_b200_rotor13_backward_tm_f32(
     const float* X, const float* U, const float* C, const float* C_final,
     const float* x_ref, const float* u_ref, const uint8_t* tight_mask,
     const float* grad_X, const float* grad_U,

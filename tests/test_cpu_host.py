@@ -168,6 +168,14 @@ def test_normalize_cost_layouts():
     c1 = torch.randn(n)
     _, cb = mpc_compat._normalize_cost(C4, c1, B, T, n, torch.device("cpu"), torch.float32)
     assert torch.equal(cb[2, 3], c1)
+    # The time-major form the operator hands to the kernels is the same data
+    # without the transpose, for every accepted shape of C and c.
+    cpu = torch.device("cpu")
+    for C, c in ((C2, None), (C4, c3), (C4, c1), (torch.randn(T, n, n), torch.randn(T, n))):
+        Cb, cb = mpc_compat._normalize_cost(C, c, B, T, n, cpu, torch.float32)
+        Ct, ct = mpc_compat._normalize_cost_tm(C, c, B, T, n, cpu, torch.float32)
+        assert Ct.is_contiguous() and ct.is_contiguous()
+        assert torch.equal(Ct, Cb.transpose(0, 1)) and torch.equal(ct, cb.transpose(0, 1))
 
 
 def test_normalize_bounds_and_init():
