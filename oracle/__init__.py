@@ -7,6 +7,9 @@ CUDA solver: only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline
 leg may import it. The product path (the C-ABI library and the Python surface
 in ca-ac-mpc_b200/) never imports, links or executes anything here.
 
+fastmpc_oracle.py restates the reference FastMPC extension's CUDA build (its
+own numerics mode of the same solver).
+
 Pinning: the oracle is checked against golden vectors produced by running the
 reference DiffMPC itself (tests/golden/make_golden.py, which imports the
 reference from its source tree in the build container); see
@@ -15,3 +18,4 @@ tests/test_oracle_golden.py.
 
 from .diffmpc_oracle import *  # noqa: F401,F403
 from .rotor13_model import *  # noqa: F401,F403
+from .fastmpc_oracle import *  # noqa: F401,F403
