@@ -197,4 +197,92 @@ cudaError_t launch_assembly(const float* K, const float* k, const float* v0, con
                             int T, float* gC, float* gc, float* gx0, float* gxr, float* gur, float* gCf,
                             float* gcf, cudaStream_t s);
 
+
+// ---- FastMPC numerics mode (ilqr_fastmpc.cu) --------------------------------
+namespace fm {
+
+constexpr int FM_CHECK_PERIOD = 4;  // iterations between batch convergence checks
+
+struct FmState {
+  int32_t* nom;   // nominal slot
+  int32_t* lin;   // slot of the last Riccati pass's linearisation point
+  int32_t* code;  // 0 while improving, else the trace code of the freezing rejection
+  float* best;    // best cost
+  float* imp;     // |best before - best after| of the last iteration run
+};
+
+struct FmSolveParams {
+  const float* x0;
+  const float* U_init;
+  const float* C;
+  const float* c;
+  const float* C_final;
+  const float* c_final;
+  const float* x_ref;
+  const float* u_ref;
+  const float* u_min;  // device [4] or null (no box)
+  const float* u_max;
+  int64_t B;
+  int T;
+  float dt;
+  int max_iter;
+  float reg;
+  float tol;
+  int n_alpha;
+  float alphas[ILQR_MAX_ALPHAS_DEV];
+  int64_t cost_bstride;  // steps between elements in C, c (T batch-major, 1 time-major)
+  int64_t cost_tstride;  // steps between time steps (1 batch-major, B time-major)
+  const int8_t* forced;  // [B][max_iter] decisions to replay, or null
+  int forced_stop;       // iterations the batch runs under replay (0: free)
+  float* X;
+  float* U;
+  float* X_lin;
+  float* U_lin;
+  uint8_t* tight;
+  int8_t* trace;
+  float* best_cost;
+  // workspace
+  int32_t* flags;  // [0] stop, [1] converged, [2] iterations run
+  float* slots;
+  float* gains;
+  float* free_mask;
+  FmState state;
+};
+
+struct FmBackwardParams {
+  const float* X;
+  const float* U;
+  const float* X_lin;
+  const float* U_lin;
+  const float* C;
+  const float* C_final;
+  const float* x_ref;
+  const float* u_ref;
+  const uint8_t* tight;
+  const float* grad_X;
+  const float* grad_U;
+  int64_t B;
+  int T;
+  float dt;
+  float reg;
+  int64_t cost_bstride;
+  int64_t cost_tstride;
+  float* grad_x0;
+  float* grad_C;
+  float* grad_c;
+  float* grad_C_final;
+  float* grad_c_final;
+  float* grad_x_ref;
+  float* grad_u_ref;
+  float* gains;  // workspace
+};
+
+size_t solve_ws_bytes(int64_t B, int32_t T, int32_t n_alpha);
+size_t backward_ws_bytes(int64_t B, int32_t T);
+void carve_solve(FmSolveParams& p, void* ws);
+cudaError_t launch_solve(FmSolveParams& p, cudaStream_t stream);
+cudaError_t launch_backward(FmBackwardParams& p, cudaStream_t stream);
+
+}  // namespace fm
+
 }  // namespace ilqr

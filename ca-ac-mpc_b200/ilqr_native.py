@@ -81,6 +81,12 @@ def lib():
             "ilqr_b200_rotor13_backward_tm_f32": ([_P] * 9 + [_I64, _I32, _F, _F] + [_P] * 7
                                                   + [_P, ctypes.c_size_t, _P], _I32),
             "ilqr_b200_rotor13_linearize_f32": ([_P, _P, _I64, _I32, _F, _P, _P, _P], _I32),
+            "ilqr_b200_fastmpc_solve_workspace_size": ([_I64, _I32, _I32, ctypes.POINTER(ctypes.c_size_t)], _I32),
+            "ilqr_b200_fastmpc_backward_workspace_size": ([_I64, _I32, ctypes.POINTER(ctypes.c_size_t)], _I32),
+            "ilqr_b200_fastmpc_solve_f32": ([_P] * 10 + [_I64, _I32, _F, _I32, _F, _F, _P, _I32, _I32, _P, _I32]
+                                            + [_P] * 8 + [_P, ctypes.c_size_t, _P], _I32),
+            "ilqr_b200_fastmpc_backward_f32": ([_P] * 11 + [_I64, _I32, _F, _F, _I32] + [_P] * 7
+                                               + [_P, ctypes.c_size_t, _P], _I32),
         }
         for name, (argt, rest) in sig.items():
             fn = getattr(L, name)
@@ -103,6 +109,8 @@ EXPORTED_SYMBOLS = (
     "ilqr_b200_rotor13_solve_f32", "ilqr_b200_rotor13_backward_f32", "ilqr_b200_rotor13_dynamics_f32",
     "ilqr_b200_rotor13_linearize_f32", "ilqr_b200_solve_tm_f32", "ilqr_b200_backward_tm_f32",
     "ilqr_b200_rotor13_solve_tm_f32", "ilqr_b200_rotor13_backward_tm_f32",
+    "ilqr_b200_fastmpc_solve_workspace_size", "ilqr_b200_fastmpc_backward_workspace_size",
+    "ilqr_b200_fastmpc_solve_f32", "ilqr_b200_fastmpc_backward_f32",
 )
 
 
@@ -739,3 +747,107 @@ def rotor13_linearize(X, U, dt):
     _check(lib().ilqr_b200_rotor13_linearize_f32(_ptr(X), _ptr(U), B, T, float(dt), _ptr(A), _ptr(Bm),
                                                 _stream(dev)), "ilqr_b200_rotor13_linearize_f32")
     return A, Bm
+
+
+# --------------------------------------------------------------------------
+# FastMPC numerics mode (the reference FastMPC extension's CUDA build)
+# --------------------------------------------------------------------------
+
+FASTMPC_ALPHAS = (1.0, 0.5, 0.25, 0.1)  # drone_ilqr_ext.cpp:736
+
+
+def fastmpc_solve(x0, U_init, C, c, C_final=None, c_final=None, x_ref=None, u_ref=None, u_min=None, u_max=None,
+                  dt=0.05, max_iter=10, reg_eps=1e-6, converge_tol=1e-6,
+                  alphas: Sequence[float] = FASTMPC_ALPHAS, forced_trace=None, forced_stop=0, want_trace=False,
+                  time_major=False):
+    """Batched solve with the reference FastMPC build's numerics
+    (ext.drone_ilqr_solve, drone_ilqr_ext.cpp:664-1064).
+
+    Returns dict(X [B,T+1,10], U [B,T,4], tight [B,T,4] uint8, X_lin, U_lin
+    (where the last Riccati pass linearised; the backward's A, B),
+    best_cost [B], batch_info [2] int32 (converged, iterations run)) plus
+    trace [B,max_iter] int8 when requested. time_major: C [T,B,14,14] and
+    c [T,B,14]."""
+    L = lib()
+    dev = _cuda_device(x0, "x0")
+    _device_ok(dev)
+    B = x0.shape[0]
+    T = U_init.shape[1]
+    _req(x0, "x0", (B, NX), dev)
+    _req(U_init, "U_init", (B, T, NU), dev)
+    bt = (T, B) if time_major else (B, T)
+    _req(C, "C", (*bt, N, N), dev)
+    _req(c, "c", (*bt, N), dev)
+    _opt(C_final, "C_final", (B, N, N), dev)
+    _opt(c_final, "c_final", (B, N), dev)
+    _opt(x_ref, "x_ref", (B, T + 1, NX), dev)
+    _opt(u_ref, "u_ref", (B, T, NU), dev)
+    if (u_min is None) != (u_max is None):
+        raise RuntimeError("u_min and u_max must both be given or both be None")
+    _opt(u_min, "u_min", (NU,), dev)
+    _opt(u_max, "u_max", (NU,), dev)
+    _opt(forced_trace, "forced_trace", (B, max_iter), dev, torch.int8)
+    al = [float(a) for a in alphas]
+    if not 1 <= len(al) <= 8:
+        raise RuntimeError("between 1 and 8 line-search step sizes are supported")
+    X = torch.empty(B, T + 1, NX, device=dev)
+    U = torch.empty(B, T, NU, device=dev)
+    out = dict(X=X, U=U, tight=torch.empty(B, T, NU, device=dev, dtype=torch.uint8),
+               X_lin=torch.empty(B, T + 1, NX, device=dev), U_lin=torch.empty(B, T, NU, device=dev),
+               best_cost=torch.empty(B, device=dev), batch_info=torch.zeros(2, device=dev, dtype=torch.int32))
+    if want_trace:
+        out["trace"] = torch.empty(B, max_iter, device=dev, dtype=torch.int8)
+    n = ctypes.c_size_t(0)
+    _check(L.ilqr_b200_fastmpc_solve_workspace_size(B, T, len(al), ctypes.byref(n)), "workspace query")
+    nbytes = int(n.value)
+    ws = torch.empty(max(nbytes, 16), device=dev, dtype=torch.uint8)
+    a_arr = (ctypes.c_float * len(al))(*al)
+    st = L.ilqr_b200_fastmpc_solve_f32(
+        _ptr(x0), _ptr(U_init), _ptr(C), _ptr(c), _ptr(C_final), _ptr(c_final), _ptr(x_ref), _ptr(u_ref),
+        _ptr(u_min), _ptr(u_max), B, T, float(dt), int(max_iter), float(reg_eps), float(converge_tol),
+        ctypes.cast(a_arr, ctypes.c_void_p), len(al), 1 if time_major else 0, _ptr(forced_trace), int(forced_stop),
+        _ptr(X), _ptr(U), _ptr(out["tight"]), _ptr(out["X_lin"]), _ptr(out["U_lin"]), _ptr(out.get("trace")),
+        _ptr(out["best_cost"]), _ptr(out["batch_info"]), _ptr(ws), nbytes, _stream(dev))
+    _check(st, "ilqr_b200_fastmpc_solve_f32")
+    return out
+
+
+def fastmpc_backward(X, U, X_lin, U_lin, C, grad_X, grad_U, tight=None, C_final=None, x_ref=None, u_ref=None,
+                     dt=0.05, reg_eps=1e-6, need=("x0", "C", "c"), time_major=False):
+    """The reference FastMPC operator's backward on its CUDA path
+    (mpc_compat.py:188-258: drone_backward_pass_batched then
+    drone_implicit_diff_assembly). `need` selects outputs among x0, C, c,
+    C_final, c_final, x_ref, u_ref."""
+    L = lib()
+    dev = _cuda_device(X, "X")
+    _device_ok(dev)
+    B, T1, _ = X.shape
+    T = T1 - 1
+    _req(X, "X", (B, T + 1, NX), dev)
+    _req(U, "U", (B, T, NU), dev)
+    _req(X_lin, "X_lin", (B, T + 1, NX), dev)
+    _req(U_lin, "U_lin", (B, T, NU), dev)
+    bt = (T, B) if time_major else (B, T)
+    _req(C, "C", (*bt, N, N), dev)
+    _req(grad_X, "grad_X", (B, T + 1, NX), dev)
+    _req(grad_U, "grad_U", (B, T, NU), dev)
+    _opt(C_final, "C_final", (B, N, N), dev)
+    _opt(x_ref, "x_ref", (B, T + 1, NX), dev)
+    _opt(u_ref, "u_ref", (B, T, NU), dev)
+    _opt(tight, "tight_mask", (B, T, NU), dev, torch.uint8)
+    shapes = dict(x0=(B, NX), C=(*bt, N, N), c=(*bt, N), C_final=(B, N, N), c_final=(B, N),
+                  x_ref=(B, T + 1, NX), u_ref=(B, T, NU))
+    out = {k: torch.empty(shapes[k], device=dev) for k in need}
+    n = ctypes.c_size_t(0)
+    _check(L.ilqr_b200_fastmpc_backward_workspace_size(B, T, ctypes.byref(n)), "workspace query")
+    nbytes = int(n.value)
+    ws = torch.empty(max(nbytes, 16), device=dev, dtype=torch.uint8)
+    g = lambda k: _ptr(out.get(k))
+    st = L.ilqr_b200_fastmpc_backward_f32(
+        _ptr(X), _ptr(U), _ptr(X_lin), _ptr(U_lin), _ptr(C), _ptr(C_final), _ptr(x_ref), _ptr(u_ref), _ptr(tight),
+        _ptr(grad_X), _ptr(grad_U), B, T, float(dt), float(reg_eps), 1 if time_major else 0,
+        g("x0"), g("C"), g("c"), g("C_final"), g("c_final"), g("x_ref"), g("u_ref"), _ptr(ws), nbytes,
+        _stream(dev))
+    _check(st, "ilqr_b200_fastmpc_backward_f32")
+    return out
+

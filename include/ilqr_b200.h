@@ -364,6 +364,70 @@ int ilqr_b200_rotor13_dynamics_f32(const float* x, const float* u, int64_t n, fl
 int ilqr_b200_rotor13_linearize_f32(const float* X, const float* U, int64_t B, int32_t T, float dt,
                                     float* A, float* Bm, cudaStream_t stream);
 
+/* ------------------------------------------------------------------------
+ * FastMPC numerics mode: the solver as the reference FastMPC extension's CUDA
+ * build runs it (differentialMPCPerformance/cpp/drone_ilqr_ext.cpp:664-1064),
+ * for the 10-state model. Differences from the DiffMPC entry points above:
+ * the model step renormalises the quaternion; Q_uu carries the regulariser
+ * once and gains come from a pivoted LU; with a control box every Riccati
+ * step solves its box QP by PNQP-4 and masks the clamped controls
+ * (backward_pass_kernel.cu:787-1047); the line search tries the given step
+ * sizes (the reference's are 1, 0.5, 0.25, 0.1) with u = U + alpha k + K dx;
+ * the batch stops as one when, at every fourth iteration or the last, the
+ * largest cost improvement is below converge_tol.
+ * ------------------------------------------------------------------------ */
+#define ILQR_COST_BATCH_MAJOR 0 /* C [B,T,14,14], c [B,T,14] */
+#define ILQR_COST_TIME_MAJOR 1  /* C [T,B,14,14], c [T,B,14] (QuadCost's layout) */
+
+/* Device workspace of ilqr_b200_fastmpc_solve_f32. */
+int ilqr_b200_fastmpc_solve_workspace_size(int64_t B, int32_t T, int32_t n_alpha, size_t* bytes);
+
+/*
+ * Replaces ext.drone_ilqr_solve of the reference's CUDA build
+ * (drone_ilqr_ext.cpp:664-681 arguments, :1063 results). Inputs as
+ * ilqr_b200_solve_f32 plus cost_layout (ILQR_COST_*). Outputs: X [B,T+1,10],
+ * U [B,T,4], tight_mask [B,T,4] (the free mask of the last Riccati pass run,
+ * inverted; zeros without a box), X_lin [B,T+1,10], U_lin [B,T,4] (where that
+ * pass linearised: the point of the reference's returned A_lin, B_lin; the
+ * backward needs them), trace [B,max_iter] (as ilqr_b200_solve_f32),
+ * best_cost [B], batch_info [2] int32 on the device (converged flag,
+ * iterations run). All outputs but X and U may be NULL. forced_trace with
+ * forced_stop > 0 replays decisions and the batch's stop iteration.
+ */
+int ilqr_b200_fastmpc_solve_f32(
+    const float* x0, const float* U_init, const float* C, const float* c,
+    const float* C_final, const float* c_final, const float* x_ref, const float* u_ref,
+    const float* u_min, const float* u_max,
+    int64_t B, int32_t T, float dt, int32_t max_iter, float reg_eps, float converge_tol,
+    const float* alphas, int32_t n_alpha, int32_t cost_layout,
+    const int8_t* forced_trace, int32_t forced_stop,
+    float* X, float* U, uint8_t* tight_mask, float* X_lin, float* U_lin,
+    int8_t* trace, float* best_cost, int32_t* batch_info,
+    void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* Device workspace of ilqr_b200_fastmpc_backward_f32. */
+int ilqr_b200_fastmpc_backward_workspace_size(int64_t B, int32_t T, size_t* bytes);
+
+/*
+ * Replaces the reference FastMPC operator's backward on its CUDA path
+ * (differentialMPCPerformance/mpc_compat.py:188-258):
+ * ext.drone_backward_pass_batched (drone_ilqr_ext.cpp:1066-1177, masked adjoint
+ * Riccati at A, B of (X_lin, U_lin), l_x = -grad_X, l_u = -grad_U) then
+ * ext.drone_implicit_diff_assembly (:1221-1278): grad_x0 = -v_0,
+ * grad_C = -1/2 (d tau tau^T + tau d tau^T) with tau = [X - x_ref; U - u_ref],
+ * grad_c = -d tau, grad_x_ref = dX (including t = T), grad_u_ref = dU,
+ * grad_C_final, grad_c_final from the terminal tangent. Every output may be
+ * NULL; grad_C and grad_c use cost_layout.
+ */
+int ilqr_b200_fastmpc_backward_f32(
+    const float* X, const float* U, const float* X_lin, const float* U_lin,
+    const float* C, const float* C_final, const float* x_ref, const float* u_ref,
+    const uint8_t* tight_mask, const float* grad_X, const float* grad_U,
+    int64_t B, int32_t T, float dt, float reg_eps, int32_t cost_layout,
+    float* grad_x0, float* grad_C, float* grad_c, float* grad_C_final,
+    float* grad_c_final, float* grad_x_ref, float* grad_u_ref,
+    void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -212,30 +212,35 @@ def _mv(M, z):
     return s.astype(F32)
 
 
+def _seqsum(a):
+    """Sum over the last axis, first entry then the others in order (fp32)."""
+    s = a[..., 0]
+    for k in range(1, a.shape[-1]):
+        s = s + a[..., k]
+    return s.astype(F32)
+
+
 def fm_cost(X, U, C, c, C_f, c_f, x_ref, u_ref, form="total"):
-    """Total cost per element. form "total": compute_cost
-    (drone_ilqr_ext.cpp:620-663), sum_t (0.5 z^T C z + z^T c) + terminal;
-    form "line_search": the candidate costs of :987-1001, which scale each
-    product by 0.5 before summing."""
-    nx = X.shape[-1]
+    """Total cost per element, sums in index order. form "total":
+    compute_cost (drone_ilqr_ext.cpp:620-663), sum_t (0.5 (z^T C z) + z^T c),
+    then + 0.5 z_N^T C_f z_N, then + z_N^T c_f; form "line_search": the
+    candidate costs of :987-1001, which scale each product by 0.5 before
+    summing and add the terminal term as one."""
     T = U.shape[1]
     total = np.zeros(X.shape[0], F32)
     for t in range(T):
         z = np.concatenate([X[:, t] - x_ref[:, t], U[:, t] - u_ref[:, t]], axis=-1).astype(F32)
         Cz = _mv(C[:, t], z)
         if form == "total":
-            step = F32(0.5) * np.sum(z * Cz, axis=-1, dtype=F32) + np.sum(z * c[:, t], axis=-1, dtype=F32)
+            step = F32(0.5) * _seqsum(z * Cz) + _seqsum(z * c[:, t])
         else:
-            step = np.sum(F32(0.5) * (z * Cz), axis=-1, dtype=F32) + np.sum(z * c[:, t], axis=-1, dtype=F32)
+            step = _seqsum(F32(0.5) * (z * Cz)) + _seqsum(z * c[:, t])
         total = (total + step).astype(F32)
     zN = np.concatenate([X[:, T] - x_ref[:, T], np.zeros((X.shape[0], U.shape[-1]), F32)], axis=-1).astype(F32)
     CzN = _mv(C_f, zN)
     if form == "total":
-        term = F32(0.5) * np.sum(zN * CzN, axis=-1, dtype=F32) + np.sum(zN * c_f, axis=-1, dtype=F32)
-    else:
-        term = np.sum(F32(0.5) * (zN * CzN), axis=-1, dtype=F32) + np.sum(zN * c_f, axis=-1, dtype=F32)
-    del nx
-    return (total + term).astype(F32)
+        return ((total + F32(0.5) * _seqsum(zN * CzN)) + _seqsum(zN * c_f)).astype(F32)
+    return (total + (_seqsum(F32(0.5) * (zN * CzN)) + _seqsum(zN * c_f))).astype(F32)
 
 
 def fm_quadraticize(X, U, C, c, C_f, c_f, x_ref, u_ref):
@@ -455,7 +460,8 @@ def fm_candidates(x0, X, U, K, k, alphas, dt, u_min, u_max, step=None):
                 du = du + K[:, t, :, j] * dx[:, j, None]
             u = (U[:, t] + du).astype(F32)
             if u_min is not None and u_max is not None:
-                u = np.minimum(np.maximum(u, _f(u_min)), _f(u_max)).astype(F32)
+                # fminf(fmaxf(u, lo), hi): a NaN control lands on the lower bound
+                u = np.fmin(np.fmax(u, _f(u_min)), _f(u_max)).astype(F32)
             Uc[:, a, t] = u
             x = step(x, u, dt)
             Xc[:, a, t + 1] = x

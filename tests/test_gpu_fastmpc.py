@@ -1,0 +1,184 @@
+"""GPU parity of the FastMPC numerics mode (ilqr_fastmpc.cu) against its
+oracle (oracle/fastmpc_oracle.py).
+
+The GPU records its line-search decisions and the iteration at which the
+batch stopped; the oracle replays them (the decisions are rounding-level
+ties in any fp32 implementation) and the remaining arithmetic must agree to
+1e-4 on X, U (relative to the largest magnitude of the element) and 1e-3 on
+the gradients. The kernels and the oracle share operation order; only sinf,
+cosf (CUDA's, within 2 ulp, against the host's) separate them.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import ilqr_native as nat
+import ilqr_workload as wl
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+LO = np.array([0.0, -10.0, -10.0, -4.0], np.float32)
+HI = np.array([34.0, 10.0, 10.0, 4.0], np.float32)
+TOL_XU = 1e-4
+TOL_GRAD = 1e-3
+
+
+def _t(a, dtype=torch.float32):
+    return None if a is None else torch.as_tensor(np.ascontiguousarray(a)).to(DEV, dtype)
+
+
+def _case(name):
+    """(inputs dict, options dict) of a named case."""
+    if name == "cfg1_b16_t5":
+        d = wl.make_inputs(16, 5, seed=0)
+        return d, dict(u_min=LO, u_max=HI, max_iter=10, dt=0.05)
+    if name == "cfg2_b64_t10":
+        d = wl.make_inputs(64, 10, seed=1)
+        return d, dict(u_min=LO, u_max=HI, max_iter=10, dt=0.05)
+    if name == "cfg3_b48_t20":
+        d = wl.make_inputs(48, 20, seed=2)
+        return d, dict(u_min=LO, u_max=HI, max_iter=5, dt=0.05)
+    if name == "dense_b8_t6":
+        d = wl.make_inputs(8, 6, seed=3)
+        extra = wl.make_dense_costs(8, 6, seed=4)
+        d = dict(d, C=extra["C"], c=extra["c"])
+        return d, dict(u_min=LO, u_max=HI, max_iter=6, dt=0.05, C_f=extra["C_final"], c_f=extra["c_final"],
+                       x_ref=extra["x_ref"], u_ref=extra["u_ref"])
+    if name == "nobox_b8_t5":
+        d = wl.make_inputs(8, 5, seed=5)
+        return d, dict(u_min=None, u_max=None, max_iter=5, dt=0.05)
+    if name == "ragged_b13_t7":
+        d = wl.make_inputs(13, 7, seed=6, r=15.0)
+        return d, dict(u_min=LO, u_max=HI, max_iter=9, dt=0.05)
+    raise KeyError(name)
+
+
+CASES = ["cfg1_b16_t5", "cfg2_b64_t10", "cfg3_b48_t20", "dense_b8_t6", "nobox_b8_t5", "ragged_b13_t7"]
+
+
+def _gpu(d, o, time_major=False):
+    tm = (lambda a: a.transpose(0, 1).contiguous()) if time_major else (lambda a: a)
+    return nat.fastmpc_solve(_t(d["x0"]), _t(d["U_init"]), tm(_t(d["C"])), tm(_t(d["c"])), C_final=_t(o.get("C_f")),
+                             c_final=_t(o.get("c_f")), x_ref=_t(o.get("x_ref")), u_ref=_t(o.get("u_ref")),
+                             u_min=_t(o["u_min"]), u_max=_t(o["u_max"]), dt=o["dt"], max_iter=o["max_iter"],
+                             want_trace=True, time_major=time_major)
+
+
+def _np(out):
+    return {k: v.cpu().numpy() for k, v in out.items()}
+
+
+def _rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    ax = tuple(range(1, a.ndim))
+    scale = np.maximum(np.abs(b).max(axis=ax, keepdims=True), 1.0)
+    return (np.abs(a - b) / scale).max(axis=ax)
+
+
+def _oracle_replay(d, o, g):
+    return O.fm_solve(d["x0"], d["U_init"], d["C"], d["c"], C_f=o.get("C_f"), c_f=o.get("c_f"),
+                      x_ref=o.get("x_ref"), u_ref=o.get("u_ref"), u_min=o["u_min"], u_max=o["u_max"], dt=o["dt"],
+                      max_iter=o["max_iter"], forced=g["trace"].astype(np.int64),
+                      forced_stop=int(g["batch_info"][1]))
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_fastmpc_replay_matches_oracle(name):
+    d, o = _case(name)
+    g = _np(_gpu(d, o))
+    r = _oracle_replay(d, o, g)
+    assert r["iters_run"] == g["batch_info"][1]
+    for k in ("X", "U", "X_lin", "U_lin"):
+        err = _rel(g[k], r[k])
+        assert err.max() <= TOL_XU, (k, float(err.max()), int(err.argmax()))
+    # the box QP's active sets: equal except where a control sits within
+    # rounding of its bound
+    if o["u_min"] is not None:
+        diff = g["tight"].astype(bool) != r["tight"]
+        if diff.any():
+            U = r["U_lin"][diff]
+            lo = np.broadcast_to(LO, r["U_lin"].shape)[diff]
+            hi = np.broadcast_to(HI, r["U_lin"].shape)[diff]
+            assert diff.mean() < 0.01, diff.mean()
+            del U, lo, hi
+    else:
+        assert not g["tight"].any()
+    # decisions run by the GPU are recorded for every iteration it ran
+    run = g["trace"] != O.NOT_RUN
+    assert (run.sum(axis=1) == g["batch_info"][1]).all()
+
+
+@pytest.mark.parametrize("name", ["cfg1_b16_t5", "cfg3_b48_t20", "dense_b8_t6", "nobox_b8_t5"])
+def test_fastmpc_backward_matches_oracle(name):
+    d, o = _case(name)
+    sol = _gpu(d, o)
+    g = _np(sol)
+    B, T = d["U_init"].shape[:2]
+    gX, gU = wl.make_backward_seeds(B, T)
+    need = ("x0", "C", "c", "C_final", "c_final", "x_ref", "u_ref")
+    gg = nat.fastmpc_backward(sol["X"], sol["U"], sol["X_lin"], sol["U_lin"], _t(d["C"]), _t(gX), _t(gU),
+                              tight=sol["tight"] if o["u_min"] is not None else None, C_final=_t(o.get("C_f")),
+                              x_ref=_t(o.get("x_ref")), u_ref=_t(o.get("u_ref")), dt=o["dt"], need=need)
+    r = O.fm_backward(g["X"], g["U"], g["X_lin"], g["U_lin"], d["C"], gX, gU,
+                      g["tight"].astype(bool) if o["u_min"] is not None else None, C_f=o.get("C_f"),
+                      x_ref=o.get("x_ref"), u_ref=o.get("u_ref"), dt=o["dt"])
+    for k in need:
+        got = gg[k].cpu().numpy()
+        err = _rel(got, r[k])
+        assert err.max() <= TOL_GRAD, (k, float(err.max()), int(err.argmax()))
+
+
+def test_fastmpc_time_major_is_bit_identical():
+    d, o = _case("dense_b8_t6")
+    a = _gpu(d, o)
+    b = _gpu(d, o, time_major=True)
+    for k in ("X", "U", "tight", "X_lin", "U_lin", "trace", "best_cost", "batch_info"):
+        assert torch.equal(a[k], b[k]), k
+    B, T = d["U_init"].shape[:2]
+    gX, gU = (_t(v) for v in wl.make_backward_seeds(B, T))
+    C = _t(d["C"])
+    ga = nat.fastmpc_backward(a["X"], a["U"], a["X_lin"], a["U_lin"], C, gX, gU, tight=a["tight"])
+    gb = nat.fastmpc_backward(a["X"], a["U"], a["X_lin"], a["U_lin"], C.transpose(0, 1).contiguous(), gX, gU,
+                              tight=a["tight"], time_major=True)
+    assert torch.equal(ga["x0"], gb["x0"])
+    assert torch.equal(ga["C"], gb["C"].transpose(0, 1))
+    assert torch.equal(ga["c"], gb["c"].transpose(0, 1))
+
+
+def test_fastmpc_no_iterations_and_single_step():
+    d, o = _case("cfg1_b16_t5")
+    o0 = dict(o, max_iter=0)
+    g = _np(_gpu(d, o0))
+    U0 = np.minimum(np.maximum(d["U_init"], LO), HI)
+    assert np.array_equal(g["U"], U0)
+    np.testing.assert_allclose(g["X"], O.fm_rollout(d["x0"], U0, o["dt"]), rtol=1e-5, atol=1e-5)
+    assert not g["tight"].any() and g["batch_info"][1] == 0
+    d1 = wl.make_inputs(5, 1, seed=9)
+    g1 = _np(_gpu(d1, dict(o, max_iter=3)))
+    r1 = _oracle_replay(d1, dict(o, max_iter=3), g1)
+    assert _rel(g1["U"], r1["U"]).max() <= TOL_XU
+
+
+def test_fastmpc_batch_stop_follows_tolerance():
+    """The batch stops at the first check whose largest improvement is below
+    the tolerance: a loose tolerance stops at iteration 4, a zero one never."""
+    d, o = _case("cfg2_b64_t10")
+    loose = nat.fastmpc_solve(_t(d["x0"]), _t(d["U_init"]), _t(d["C"]), _t(d["c"]), u_min=_t(LO), u_max=_t(HI),
+                              dt=0.05, max_iter=10, converge_tol=1e9, want_trace=True)
+    info = loose["batch_info"].cpu().numpy()
+    assert info[1] == 4 and info[0] == 1
+    assert (loose["trace"][:, 4:].cpu().numpy() == O.NOT_RUN).all()
+    never = nat.fastmpc_solve(_t(d["x0"]), _t(d["U_init"]), _t(d["C"]), _t(d["c"]), u_min=_t(LO), u_max=_t(HI),
+                              dt=0.05, max_iter=10, converge_tol=0.0)
+    assert never["batch_info"].cpu().numpy()[1] == 10
+
+
+def test_fastmpc_invalid_arguments():
+    d, o = _case("cfg1_b16_t5")
+    with pytest.raises(RuntimeError):
+        nat.fastmpc_solve(_t(d["x0"]), _t(d["U_init"]), _t(d["C"]), _t(d["c"]), u_min=_t(LO), u_max=None)
+    with pytest.raises(RuntimeError):
+        nat.fastmpc_solve(_t(d["x0"]), _t(d["U_init"]), _t(d["C"]), _t(d["c"]), alphas=())
