@@ -50,6 +50,8 @@ def _args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-sigmoid", action="store_true",
                     help="skip the section for costs given as the policy's sigmoid output")
+    ap.add_argument("--no-fastmpc", action="store_true",
+                    help="skip the FastMPC-numerics section")
     ap.add_argument("--no-rotor13", action="store_true",
                     help="skip the section for the 13-state rotor-thrust model")
     ap.add_argument("--all-configs", action="store_true",
@@ -842,6 +844,82 @@ def run_ours(args):
                                   "p90_us": sorted(lsamp)[int(0.9 * len(lsamp))], "reps": len(lsamp),
                                   "config": "B=16, T=5, 10 iterations, fwd+bwd, device-resident, eager"}}
 
+    # ---- FastMPC numerics mode (ilqr_fastmpc.cu) --------------------------------
+    # The reference FastMPC extension's own numerics on the same inputs: PNQP
+    # box QP in every Riccati step, step sizes (1, .5, .25, .1), batch-wide
+    # convergence. Device-resident solve + backward, then the operator call
+    # MPC(..., numerics="fastmpc") with autograd on the same device tensors.
+    fmr = None
+    if not args.no_fastmpc:
+        fm_alphas = nat.FASTMPC_ALPHAS
+        fm_tim = [(ev(), ev(), ev()) for _ in range(args.steps)]
+        fm_info = []
+
+        def fm_step(timing=None):
+            if timing is not None:
+                timing[0].record(stream)
+            o = nat.fastmpc_solve(d["x0"], d["U_init"], d["C"], d["c"], u_min=lo, u_max=hi, dt=wl.DT,
+                                  max_iter=iters, reg_eps=wl.REG_EPS, alphas=fm_alphas)
+            if timing is not None:
+                timing[1].record(stream)
+                fm_info.append(o["batch_info"])
+            nat.fastmpc_backward(o["X"], o["U"], o["X_lin"], o["U_lin"], d["C"], gX, gU, tight=o["tight"], dt=wl.DT,
+                                 reg_eps=wl.REG_EPS)
+            if timing is not None:
+                timing[2].record(stream)
+            return o
+
+        for _ in range(max(3, args.warmup)):
+            fm_last = fm_step()
+        barrier()
+        f0, f1 = ev(), ev()
+        f0.record(stream)
+        for i in range(args.steps):
+            fm_step(fm_tim[i])
+        f1.record(stream)
+        barrier()
+        fel = f0.elapsed_time(f1) * 1e-3
+        if world > 1:
+            t = torch.tensor([fel], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            fel = float(t.item())
+        fmpc = mpc_compat.MPC(10, 4, T, u_lower=lo.view(1, 1, 4).expand(T, 1, 4),
+                              u_upper=hi.view(1, 1, 4).expand(T, 1, 4), lqr_iter=iters, eps=wl.REG_EPS,
+                              numerics="fastmpc")
+        fdyn = type("Dyn", (), {"dt": wl.DT})()
+        fC = d["C"].transpose(0, 1).contiguous()
+        fc_ = d["c"].transpose(0, 1).contiguous()
+        fgX, fgU = gX.transpose(0, 1).contiguous(), gU.transpose(0, 1).contiguous()
+
+        def fm_op():
+            x0 = d["x0"].detach().requires_grad_(True)
+            Cd = fC.detach().requires_grad_(True)
+            cd = fc_.detach().requires_grad_(True)
+            x, u, _ = fmpc(x0, mpc_compat.QuadCost(Cd, cd), fdyn)
+            ((x * fgX).sum() + (u * fgU).sum()).backward()
+
+        for _ in range(max(3, args.warmup)):
+            fm_op()
+        barrier()
+        f0.record(stream)
+        for _ in range(args.steps):
+            fm_op()
+        f1.record(stream)
+        barrier()
+        fop = f0.elapsed_time(f1) * 1e-3
+        del fC, fc_, fgX, fgU
+        info = torch.stack(fm_info).float().mean(0).cpu().numpy()
+        fmr = {"workload": WORKLOAD, "value": world * B / (fel / args.steps), "unit": "solves/s",
+               "ms_per_step": fel / args.steps * 1e3,
+               "numerics": "reference FastMPC CUDA build: PNQP-aware Riccati, alphas (1, .5, .25, .1), "
+                           "batch convergence every 4 iterations",
+               "kernel_ms": {"solve_mean": statistics.mean(a.elapsed_time(b_) for a, b_, _ in fm_tim),
+                             "backward_mean": statistics.mean(b_.elapsed_time(c_) for _, b_, c_ in fm_tim)},
+               "iterations_run": float(info[1]), "tight_fraction": float(fm_last["tight"].float().mean()),
+               "operator_device_resident": {"value": world * B / (fop / args.steps),
+                                            "ms_per_step": fop / args.steps * 1e3,
+                                            "path": "mpc_compat.MPC(..., numerics='fastmpc') + autograd"}}
+
     # ---- CPU baseline (rank 0, N=1) ------------------------------------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -876,6 +954,7 @@ def run_ours(args):
         "policy_sigmoid_cost": sig,
         "policy_actor_step": actor,
         "rotor13": r13,
+        "fastmpc_numerics": fmr,
         "kernel_ms": {"solve_mean": statistics.mean(solve_ms), "backward_mean": statistics.mean(bwd_ms)},
     }
     print(json.dumps(line), flush=True)

@@ -548,14 +548,58 @@ __device__ __forceinline__ void quad_lin(const float* __restrict__ Cm, const flo
   lin = sl;
 }
 
+// quad_lin split over L lanes: this lane (r of the L lanes starting at warp
+// lane `first`) forms rows r, r + L, ... of C z; the 14 row terms are then
+// gathered by shuffles and summed in index order, so every one of the L lanes
+// returns the sums quad_lin returns.
+template <int L>
+__device__ __forceinline__ void quad_split(const float* __restrict__ Cm, const float* __restrict__ cv,
+                                           const float (&z)[Nf], int r, unsigned gm, int first, int form,
+                                           float& quad, float& lin) {
+  constexpr int RPL = (Nf + L - 1) / L;
+  float tr[RPL];
+#pragma unroll
+  for (int k = 0; k < RPL; ++k) {
+    const int i = r + k * L;
+    float term = 0.0f;
+    if (i < Nf) {
+      const float* row = Cm + i * Nf;
+      auto ld = [&](int j) { return Cm != nullptr ? __ldg(row + j) : 0.0f; };
+      float cz = ld(0) * z[0];
+#pragma unroll
+      for (int j = 1; j < Nf; ++j) cz = cz + ld(j) * z[j];
+      float zi = z[0];
+#pragma unroll
+      for (int q = 1; q < Nf; ++q) zi = (q == i) ? z[q] : zi;
+      term = form == 0 ? zi * cz : 0.5f * (zi * cz);
+    }
+    tr[k] = term;
+  }
+  float sq = 0.0f, sl = 0.0f;
+#pragma unroll
+  for (int i = 0; i < Nf; ++i) {
+    const float v = __shfl_sync(gm, tr[i / L], first + i % L);
+    sq = i == 0 ? v : sq + v;
+    const float lt = z[i] * (cv != nullptr ? __ldg(cv + i) : 0.0f);
+    sl = i == 0 ? lt : sl + lt;
+  }
+  quad = form == 0 ? 0.5f * sq : sq;
+  lin = sl;
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------------------
 // Solve
 // ---------------------------------------------------------------------------
 
-template <bool BOUNDED>
-__global__ void __launch_bounds__(THREADS) fm_solve_kernel(FmSolveParams p, int it0, int it1) {
+#ifndef FM_SOLVE_MINB
+#define FM_SOLVE_MINB 2
+#endif
+
+// LPC lanes per line-search candidate (4 for up to four step sizes, else 2).
+template <bool BOUNDED, int LPC>
+__global__ void __launch_bounds__(THREADS, FM_SOLVE_MINB) fm_solve_kernel(FmSolveParams p, int it0, int it1) {
   if (*(volatile const int32_t*)(p.flags) != 0) return;  // the batch stopped at an earlier check
   __shared__ float smem[EPC * S_ELEM];
   __shared__ uint32_t jtab[36];
@@ -599,8 +643,9 @@ __global__ void __launch_bounds__(THREADS) fm_solve_kernel(FmSolveParams p, int 
     if (p.trace != nullptr)
       for (int i = l; i < p.max_iter; i += GL) p.trace[b * p.max_iter + i] = (int8_t)ILQR_TRACE_NOT_RUN;
     for (int i = l; i < T * NUf; i += GL) fmw[i] = 1.0f;
-    // initial rollout of clamp(U_init) and its cost (compute_cost form), lane 0
-    if (l == 0) {
+    // initial rollout of clamp(U_init) and its cost (compute_cost form): every
+    // lane steps the same trajectory, the cost rows are split over the group
+    {
       float x[10];
 #pragma unroll
       for (int i = 0; i < 10; ++i) x[i] = __ldg(x0 + i);
@@ -616,16 +661,16 @@ __global__ void __launch_bounds__(THREADS) fm_solve_kernel(FmSolveParams p, int 
         float z[Nf];
 #pragma unroll
         for (int i = 0; i < 10; ++i) {
-          rec[i] = x[i];
+          if (l == 0) rec[i] = x[i];
           z[i] = x[i] - (xr != nullptr ? xr[t * NXf + i] : 0.0f);
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          rec[10 + i] = u[i];
+          if (l == 0) rec[10 + i] = u[i];
           z[10 + i] = u[i] - (ur != nullptr ? ur[t * NUf + i] : 0.0f);
         }
         float qd, ln;
-        quad_lin(Cstep(t), cstep(t), z, 0, qd, ln);
+        quad_split<GL>(Cstep(t), cstep(t), z, l, G.gm, G.base, 0, qd, ln);
         total = total + (qd + ln);
         step_matrix(x, u, p.dt, x);
       }
@@ -633,16 +678,15 @@ __global__ void __launch_bounds__(THREADS) fm_solve_kernel(FmSolveParams p, int 
       float z[Nf];
 #pragma unroll
       for (int i = 0; i < 10; ++i) {
-        rec[i] = x[i];
+        if (l == 0) rec[i] = x[i];
         z[i] = x[i] - (xr != nullptr ? xr[T * NXf + i] : 0.0f);
       }
 #pragma unroll
       for (int i = 10; i < Nf; ++i) z[i] = 0.0f;
       float qd, ln;
-      quad_lin(Cf, cf, z, 0, qd, ln);
+      quad_split<GL>(Cf, cf, z, l, G.gm, G.base, 0, qd, ln);
       best = (total + qd) + ln;
     }
-    best = __shfl_sync(G.gm, best, G.base);
     nom = 0;
     lin = 0;
     code = 0;
@@ -687,12 +731,18 @@ __global__ void __launch_bounds__(THREADS) fm_solve_kernel(FmSolveParams p, int 
       riccati_step<BOUNDED ? 1 : 0>(G, Vr, cx, lxi, cu, luj, p.reg, p.u_min, p.u_max, nullptr,
                                     kw + (int64_t)t * KREC, BOUNDED ? fmw + t * NUf : nullptr);
     }
-    // ---- line search: candidate l on lane l ----
+    // ---- line search: candidate a on lanes a*LPC .. a*LPC + LPC - 1 ----
+    // (lanes past the last candidate repeat it without writing)
     float cost = 0.0f;
-    if (l < nA) {
-      const float al = pick_alpha(p.alphas, l);
-      const int slot = l < nom ? l : l + 1;
+    {
+      const int a_own = l / LPC;
+      const int r = l % LPC;
+      const bool writer = a_own < nA && r == 0;
+      const int a = a_own < nA ? a_own : nA - 1;
+      const float al = pick_alpha(p.alphas, a);
+      const int slot = a < nom ? a : a + 1;
       float* crec = slots + (int64_t)slot * rec_stride;
+      const int first = G.base + a_own * LPC;
       float x[10];
 #pragma unroll
       for (int i = 0; i < 10; ++i) x[i] = __ldg(x0 + i);
@@ -714,16 +764,16 @@ __global__ void __launch_bounds__(THREADS) fm_solve_kernel(FmSolveParams p, int 
         float* rec = crec + (int64_t)t * REC;
 #pragma unroll
         for (int i = 0; i < 10; ++i) {
-          rec[i] = x[i];
+          if (writer) rec[i] = x[i];
           z[i] = x[i] - (xr != nullptr ? xr[t * NXf + i] : 0.0f);
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          rec[10 + i] = u[i];
+          if (writer) rec[10 + i] = u[i];
           z[10 + i] = u[i] - (ur != nullptr ? ur[t * NUf + i] : 0.0f);
         }
         float qd, ln;
-        quad_lin(Cstep(t), cstep(t), z, 1, qd, ln);
+        quad_split<LPC>(Cstep(t), cstep(t), z, r, G.gm, first, 1, qd, ln);
         total = total + (qd + ln);
         step_cross(x, u, p.dt, x);
       }
@@ -731,19 +781,19 @@ __global__ void __launch_bounds__(THREADS) fm_solve_kernel(FmSolveParams p, int 
       float z[Nf];
 #pragma unroll
       for (int i = 0; i < 10; ++i) {
-        rec[i] = x[i];
+        if (writer) rec[i] = x[i];
         z[i] = x[i] - (xr != nullptr ? xr[T * NXf + i] : 0.0f);
       }
 #pragma unroll
       for (int i = 10; i < Nf; ++i) z[i] = 0.0f;
       float qd, ln;
-      quad_lin(Cf, cf, z, 1, qd, ln);
+      quad_split<LPC>(Cf, cf, z, r, G.gm, first, 1, qd, ln);
       cost = total + (qd + ln);
     }
     // ---- decision (lane 0 of the group) ----
     float cst[ILQR_MAX_ALPHAS_DEV];
 #pragma unroll
-    for (int a = 0; a < ILQR_MAX_ALPHAS_DEV; ++a) cst[a] = __shfl_sync(G.gm, cost, G.base + a);
+    for (int a = 0; a < ILQR_MAX_ALPHAS_DEV; ++a) cst[a] = __shfl_sync(G.gm, cost, G.base + (a * LPC) % GL);
     // argmin over the step sizes: the first NaN if any (no improvement), else
     // the first minimum; improvement is strict (drone_ilqr_ext.cpp:1003-1022)
     int j = 0;
@@ -1040,10 +1090,13 @@ cudaError_t launch_solve(FmSolveParams& p, cudaStream_t stream) {
   for (int s = 0; s < segs; ++s) {
     const int it0 = s * FM_CHECK_PERIOD;
     const int it1 = p.max_iter > 0 ? (it0 + FM_CHECK_PERIOD < p.max_iter ? it0 + FM_CHECK_PERIOD : p.max_iter) : 0;
+    const bool wide = p.n_alpha <= GL / 4;
     if (bounded) {
-      fm_solve_kernel<true><<<grid, THREADS, 0, stream>>>(p, it0, it1);
+      if (wide) fm_solve_kernel<true, 4><<<grid, THREADS, 0, stream>>>(p, it0, it1);
+      else fm_solve_kernel<true, 2><<<grid, THREADS, 0, stream>>>(p, it0, it1);
     } else {
-      fm_solve_kernel<false><<<grid, THREADS, 0, stream>>>(p, it0, it1);
+      if (wide) fm_solve_kernel<false, 4><<<grid, THREADS, 0, stream>>>(p, it0, it1);
+      else fm_solve_kernel<false, 2><<<grid, THREADS, 0, stream>>>(p, it0, it1);
     }
     if (p.max_iter > 0) fm_check_kernel<<<1, 1024, 0, stream>>>(p, it1);
   }

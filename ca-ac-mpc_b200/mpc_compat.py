@@ -17,6 +17,13 @@ isclose tight mask, masked adjoint Riccati with unmasked value update.
 n_state=10 is the reference's CTBR quadrotor; n_state=13 selects the 13-state
 rotor-thrust rigid body (ilqr_native.rotor13_solve / .rotor13_backward), the
 same solver on a model DiffMPC would linearise with GradMethod.AUTO_DIFF.
+
+numerics="fastmpc" (or ACMPC_FASTMPC_NUMERICS=fastmpc) selects instead the
+numerics of the reference FastMPC extension's CUDA build
+(differentialMPCPerformance/cpp): PNQP-aware Riccati pass, step sizes
+(1, .5, .25, .1) with u = U + alpha k + K dx, the quaternion renormalising
+step, batch-wide convergence checked every fourth iteration, and its masked
+adjoint backward (ilqr_native.fastmpc_solve / .fastmpc_backward).
 """
 
 from __future__ import annotations
@@ -244,6 +251,40 @@ class SigmoidMPCFunction(torch.autograd.Function):
         return g.get("x0"), g.get("sigmoid_cost"), None
 
 
+class FastMPCNumericsFunction(torch.autograd.Function):
+    """The reference FastMPC operator's autograd function with its own
+    numerics (differentialMPCPerformance/mpc_compat.py:128-450 on the CUDA
+    build): forward(x0 [B,10], C [T,B,14,14], c [T,B,14], solver_cfg) ->
+    (X [B,T+1,10], U [B,T,4]); backward returns the gradients of x0, C, c."""
+
+    @staticmethod
+    def forward(ctx, x0, C_tb, c_tb, solver_cfg):
+        C32 = _f32(C_tb)
+        out = _nat.fastmpc_solve(
+            _f32(x0), _f32(solver_cfg["U_init"]), C32, _f32(c_tb), None, None, None, None,
+            solver_cfg.get("u_min"), solver_cfg.get("u_max"), dt=solver_cfg["dt"], max_iter=solver_cfg["lqr_iter"],
+            reg_eps=solver_cfg["eps"], converge_tol=solver_cfg.get("converge_tol", 1e-6),
+            alphas=solver_cfg.get("alphas", _nat.FASTMPC_ALPHAS), time_major=True)
+        X, U = out["X"], out["U"]
+        bounded = solver_cfg.get("u_min") is not None
+        ctx.save_for_backward(X, U, out["X_lin"], out["U_lin"], C32, out["tight"] if bounded else None)
+        ctx.dt = float(solver_cfg["dt"])
+        ctx.reg_eps = float(solver_cfg.get("reg_eps", solver_cfg["eps"]))
+        return X, U
+
+    @staticmethod
+    def backward(ctx, grad_X, grad_U):
+        X, U, X_lin, U_lin, C32, tight = ctx.saved_tensors
+        want = tuple(nm for nm, nd in zip(("x0", "C", "c"), ctx.needs_input_grad[:3]) if nd)
+        if not want:
+            return None, None, None, None
+        gX = torch.zeros_like(X) if grad_X is None else grad_X.to(torch.float32).contiguous()
+        gU = torch.zeros_like(U) if grad_U is None else grad_U.to(torch.float32).contiguous()
+        g = _nat.fastmpc_backward(X, U, X_lin, U_lin, C32, gX, gU, tight=tight, dt=ctx.dt, reg_eps=ctx.reg_eps,
+                                  need=want, time_major=True)
+        return g.get("x0"), g.get("C"), g.get("c"), None
+
+
 class FastMPC(nn.Module):
     """Drop-in replacement for mpc.pytorch's MPC class (mpc_compat.py:453-612).
 
@@ -252,6 +293,9 @@ class FastMPC(nn.Module):
     sizes (default DiffMPC's (1, .8, .5, .2, .1), or ACMPC_DIFFMPC_ALPHAS).
     n_state selects the model: 10 is the reference's CTBR quadrotor, 13 the
     rotor-thrust rigid body (four rotor thrusts in [0, 1]; dense QuadCost only).
+    numerics: "diffmpc" (default) or "fastmpc" (the reference FastMPC build's
+    own numerics; 10-state model, dense QuadCost; ACMPC_FASTMPC_NUMERICS sets
+    the default).
     """
 
     def __init__(self, n_state: int, n_ctrl: int, T: int, u_lower: Optional[Tensor] = None,
@@ -261,8 +305,14 @@ class FastMPC(nn.Module):
                  max_linesearch_iter: int = 10, grad_method: GradMethods = GradMethods.ANALYTIC,
                  eps: float = 1e-6, n_batch: Optional[int] = None, backprop: bool = True,
                  slew_rate_penalty: Optional[float] = None, prev_ctrl: Optional[Tensor] = None,
-                 alphas=None, **kwargs):
+                 alphas=None, numerics: Optional[str] = None, **kwargs):
         super().__init__()
+        numerics = (numerics or os.environ.get("ACMPC_FASTMPC_NUMERICS", "diffmpc")).strip().lower()
+        if numerics not in ("diffmpc", "fastmpc"):
+            raise ValueError(f"numerics must be 'diffmpc' or 'fastmpc', not {numerics!r}")
+        if numerics == "fastmpc" and n_state != _nat.NX:
+            raise ValueError("the FastMPC numerics mode runs the 10-state model")
+        self.numerics = numerics
         if n_state not in (_nat.NX, _nat.NX13) or n_ctrl != _nat.NU:
             raise ValueError(f"the solver's models have n_state {_nat.NX} or {_nat.NX13} and n_ctrl={_nat.NU}")
         self.n_state = n_state
@@ -290,6 +340,8 @@ class FastMPC(nn.Module):
     def _alphas(self):
         if self.alphas is not None:
             return self.alphas
+        if self.numerics == "fastmpc":
+            return _nat.FASTMPC_ALPHAS
         env = os.environ.get("ACMPC_DIFFMPC_ALPHAS")
         if env:
             return tuple(float(x.strip()) for x in env.split(",") if x.strip())
@@ -317,6 +369,8 @@ class FastMPC(nn.Module):
         r13 = nx == _nat.NX13
         if sigm and r13:
             raise ValueError("SigmoidQuadCost builds the 10-state policy's costs; use QuadCost with n_state=13")
+        if sigm and self.numerics == "fastmpc":
+            raise ValueError("the FastMPC numerics mode takes QuadCost")
         if not sigm:
             C_tb, c_tb = _normalize_cost_tm(cost.C, cost.c, B, T, n, device, dtype)
         u_min, u_max = self._get_bounds(device, dtype)
@@ -334,6 +388,15 @@ class FastMPC(nn.Module):
                     out = _nat.solve_sigmoid(x0, U_init, _f32(cost.sigmoid_cost), cfg["sigmoid_spec"], u_min,
                                              u_max, dt=float(dt), max_iter=self.lqr_iter, reg_eps=self.eps,
                                              converge_tol=1e-6, alphas=self._alphas())
+                X, U = out["X"], out["U"]
+        elif self.numerics == "fastmpc":
+            if torch.is_grad_enabled() and self.backprop:
+                X, U = FastMPCNumericsFunction.apply(x0, C_tb, c_tb, cfg)
+            else:
+                with torch.inference_mode():
+                    out = _nat.fastmpc_solve(x0, U_init, C_tb, c_tb, None, None, None, None, u_min, u_max,
+                                             dt=float(dt), max_iter=self.lqr_iter, reg_eps=self.eps,
+                                             converge_tol=1e-6, alphas=self._alphas(), time_major=True)
                 X, U = out["X"], out["U"]
         elif torch.is_grad_enabled() and self.backprop:
             X, U = DroneMPCFunction.apply(x0, C_tb, c_tb, None, None, None, None, cfg)

@@ -104,6 +104,57 @@ def test_rotor13_surface_without_gpu():
         mpc_compat.FastMPC(12, 4, T)
 
 
+def test_fastmpc_numerics_surface_without_gpu(monkeypatch):
+    """numerics="fastmpc" (or ACMPC_FASTMPC_NUMERICS) selects the reference
+    FastMPC build's numerics: its step sizes by default, the 10-state model
+    only, QuadCost only, and no CPU path."""
+    B, T = 2, 3
+    m = mpc_compat.FastMPC(10, 4, T, lqr_iter=2, numerics="fastmpc")
+    assert m.numerics == "fastmpc" and m._alphas() == nat.FASTMPC_ALPHAS == (1.0, 0.5, 0.25, 0.1)
+    assert mpc_compat.FastMPC(10, 4, T).numerics == "diffmpc"
+    monkeypatch.setenv("ACMPC_FASTMPC_NUMERICS", "fastmpc")
+    assert mpc_compat.FastMPC(10, 4, T).numerics == "fastmpc"
+    with pytest.raises(ValueError):
+        mpc_compat.FastMPC(13, 4, T, numerics="fastmpc")
+    with pytest.raises(ValueError):
+        mpc_compat.FastMPC(10, 4, T, numerics="mpc.pytorch")
+    x = torch.zeros(B, 10)
+    x[:, 3] = 1
+    with pytest.raises(ValueError):
+        m(x, mpc_compat.SigmoidQuadCost(torch.zeros(B, 28 * T)), type("Dx", (), {"dt": 0.05})())
+    C = torch.eye(14).expand(T, B, 14, 14)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        m(x, mpc_compat.QuadCost(C, None), type("Dx", (), {"dt": 0.05})())
+
+
+def test_fastmpc_workspace_sizes_and_argument_validation():
+    L = nat.lib()
+    n = ctypes.c_size_t(0)
+    assert L.ilqr_b200_fastmpc_solve_workspace_size(16384, 20, 4, ctypes.byref(n)) == 0
+    assert n.value == 256 + 16384 * (5 * 21 * 16 + 20 * 44 + 20 * 4 + 5) * 4
+    assert L.ilqr_b200_fastmpc_backward_workspace_size(16384, 20, ctypes.byref(n)) == 0
+    assert n.value == 256 + 16384 * 20 * 44 * 4
+    assert L.ilqr_b200_fastmpc_solve_workspace_size(4, 5, 9, ctypes.byref(n)) != 0
+    fake = ctypes.c_void_p(0x10000)
+    al = ctypes.cast((ctypes.c_float * 4)(1, .5, .25, .1), ctypes.c_void_p)
+
+    def solve(**over):
+        a = dict(x0=fake, U_init=fake, C=fake, c=fake, C_final=None, c_final=None, x_ref=None, u_ref=None,
+                 u_min=None, u_max=None, B=4, T=5, dt=0.05, max_iter=3, reg=1e-6, tol=1e-6, alphas=al, n_alpha=4,
+                 layout=0, forced=None, forced_stop=0, X=fake, U=fake, tight=None, X_lin=None, U_lin=None,
+                 trace=None, best=None, info=None, ws=None, ws_bytes=0, stream=None)
+        a.update(over)
+        return L.ilqr_b200_fastmpc_solve_f32(*a.values())
+
+    # each rejected before anything touches the device
+    assert solve(layout=2) == 1
+    assert solve(u_min=fake) == 1
+    assert solve(forced_stop=2) == 1
+    assert solve(n_alpha=0) == 1
+    assert solve() == 3  # no workspace
+    assert solve(B=0) == 0
+
+
 def _solve_args(**over):
     fake = ctypes.c_void_p(0x10000)
     a = dict(x0=fake, U_init=fake, C=fake, c=fake, C_final=None, c_final=None, x_ref=None,

@@ -94,16 +94,11 @@ def test_fastmpc_replay_matches_oracle(name):
     for k in ("X", "U", "X_lin", "U_lin"):
         err = _rel(g[k], r[k])
         assert err.max() <= TOL_XU, (k, float(err.max()), int(err.argmax()))
-    # the box QP's active sets: equal except where a control sits within
-    # rounding of its bound
+    # the box QP's active sets: equal but for rare rounding-level flips of a
+    # control that sits at its bound
     if o["u_min"] is not None:
         diff = g["tight"].astype(bool) != r["tight"]
-        if diff.any():
-            U = r["U_lin"][diff]
-            lo = np.broadcast_to(LO, r["U_lin"].shape)[diff]
-            hi = np.broadcast_to(HI, r["U_lin"].shape)[diff]
-            assert diff.mean() < 0.01, diff.mean()
-            del U, lo, hi
+        assert diff.mean() < 0.01, diff.mean()
     else:
         assert not g["tight"].any()
     # decisions run by the GPU are recorded for every iteration it ran
@@ -182,3 +177,34 @@ def test_fastmpc_invalid_arguments():
         nat.fastmpc_solve(_t(d["x0"]), _t(d["U_init"]), _t(d["C"]), _t(d["c"]), u_min=_t(LO), u_max=None)
     with pytest.raises(RuntimeError):
         nat.fastmpc_solve(_t(d["x0"]), _t(d["U_init"]), _t(d["C"]), _t(d["c"]), alphas=())
+
+
+def test_fastmpc_operator_autograd_equals_entry_points():
+    """MPC(..., numerics="fastmpc") hands QuadCost's [T,B,...] tensors to the
+    time-major entry points; its outputs and autograd gradients equal the
+    batch-major entry points' bit for bit."""
+    import mpc_compat
+    d, o = _case("cfg1_b16_t5")
+    B, T = d["U_init"].shape[:2]
+    lo = _t(LO).view(1, 1, 4).expand(T, B, 4)
+    hi = _t(HI).view(1, 1, 4).expand(T, B, 4)
+    m = mpc_compat.MPC(10, 4, T, u_lower=lo, u_upper=hi, u_init=_t(d["U_init"]).transpose(0, 1), lqr_iter=10,
+                       numerics="fastmpc")
+    x0 = _t(d["x0"]).requires_grad_(True)
+    C = _t(d["C"]).transpose(0, 1).contiguous().requires_grad_(True)
+    c = _t(d["c"]).transpose(0, 1).contiguous().requires_grad_(True)
+    X, U, _ = m(x0, mpc_compat.QuadCost(C, c), type("Dx", (), {"dt": 0.05})())
+    ref = nat.fastmpc_solve(_t(d["x0"]), _t(d["U_init"]), _t(d["C"]), _t(d["c"]), u_min=_t(LO), u_max=_t(HI),
+                            dt=0.05, max_iter=10)
+    assert torch.equal(X.detach().transpose(0, 1), ref["X"])
+    assert torch.equal(U.detach().transpose(0, 1), ref["U"])
+    gX, gU = (_t(a) for a in wl.make_backward_seeds(B, T))
+    ((X * gX.transpose(0, 1)).sum() + (U * gU.transpose(0, 1)).sum()).backward()
+    g = nat.fastmpc_backward(ref["X"], ref["U"], ref["X_lin"], ref["U_lin"], _t(d["C"]), gX, gU, tight=ref["tight"],
+                             dt=0.05)
+    assert torch.equal(x0.grad, g["x0"])
+    assert torch.equal(C.grad.transpose(0, 1), g["C"])
+    assert torch.equal(c.grad.transpose(0, 1), g["c"])
+    with torch.no_grad():
+        Xi, Ui, _ = m(_t(d["x0"]), mpc_compat.QuadCost(C.detach(), c.detach()), type("Dx", (), {"dt": 0.05})())
+    assert torch.equal(Xi, X.detach()) and torch.equal(Ui, U.detach())
