@@ -27,8 +27,11 @@
 // candidates on every later iteration, so it is frozen at its first
 // rejection (its trace repeats that rejection).
 //
-// Arithmetic is fp32 without contraction (the library is compiled with
-// -fmad=false), sums run in index order, as the oracle restates them.
+// Arithmetic is fp32. The matrix-product and cost sums run in index order as
+// fused multiply-adds (the reference build compiles with --use_fast_math,
+// which contracts them too); the oracle rounds each product, so the two
+// differ at the rounding level. The model step and Jacobian entries are
+// evaluated without contraction (the library is compiled with -fmad=false).
 #include <cstdint>
 
 #include "ilqr_b200.h"
@@ -369,14 +372,14 @@ __device__ __forceinline__ void riccati_step(const Group& G, float (&Vr)[NXf], c
     for (int j = 0; j < NXf; ++j) {
       float s = 0.0f;
 #pragma unroll
-      for (int k = 0; k < NXf; ++k) s = s + Vr[k] * sm[S_A + k * 10 + j];
+      for (int k = 0; k < NXf; ++k) s = fmaf(Vr[k], sm[S_A + k * 10 + j], s);
       sm[S_VA + l * 10 + j] = s;
     }
 #pragma unroll
     for (int j = 0; j < NUf; ++j) {
       float s = 0.0f;
 #pragma unroll
-      for (int k = 0; k < NXf; ++k) s = s + Vr[k] * sm[S_B + k * 4 + j];
+      for (int k = 0; k < NXf; ++k) s = fmaf(Vr[k], sm[S_B + k * 4 + j], s);
       sm[S_VB + l * 4 + j] = s;
     }
   }
@@ -388,19 +391,19 @@ __device__ __forceinline__ void riccati_step(const Group& G, float (&Vr)[NXf], c
     for (int j = 0; j < NXf; ++j) {
       float s = cx[j];
 #pragma unroll
-      for (int k = 0; k < NXf; ++k) s = s + sm[S_A + k * 10 + l] * sm[S_VA + k * 10 + j];
+      for (int k = 0; k < NXf; ++k) s = fmaf(sm[S_A + k * 10 + l], sm[S_VA + k * 10 + j], s);
       Qxx[j] = s;
     }
 #pragma unroll
     for (int j = 0; j < NUf; ++j) {
       float s = cx[NXf + j];
 #pragma unroll
-      for (int k = 0; k < NXf; ++k) s = s + sm[S_A + k * 10 + l] * sm[S_VB + k * 4 + j];
+      for (int k = 0; k < NXf; ++k) s = fmaf(sm[S_A + k * 10 + l], sm[S_VB + k * 4 + j], s);
       Qxu[j] = s;
     }
     float s = lxi;
 #pragma unroll
-    for (int k = 0; k < NXf; ++k) s = s + sm[S_A + k * 10 + l] * sm[S_V + k];
+    for (int k = 0; k < NXf; ++k) s = fmaf(sm[S_A + k * 10 + l], sm[S_V + k], s);
     qx = s;
   } else if (urow) {
     const int j = l - NXf;
@@ -408,13 +411,13 @@ __device__ __forceinline__ void riccati_step(const Group& G, float (&Vr)[NXf], c
     for (int m = 0; m < NUf; ++m) {
       float s = cu[m];
 #pragma unroll
-      for (int k = 0; k < NXf; ++k) s = s + sm[S_B + k * 4 + j] * sm[S_VB + k * 4 + m];
+      for (int k = 0; k < NXf; ++k) s = fmaf(sm[S_B + k * 4 + j], sm[S_VB + k * 4 + m], s);
       if (m == j) s = s + reg;
       sm[S_QUU + j * 4 + m] = s;
     }
     float s = luj;
 #pragma unroll
-    for (int k = 0; k < NXf; ++k) s = s + sm[S_B + k * 4 + j] * sm[S_V + k];
+    for (int k = 0; k < NXf; ++k) s = fmaf(sm[S_B + k * 4 + j], sm[S_V + k], s);
     sm[S_QU + j] = s;
   }
   G.sync();
@@ -484,12 +487,12 @@ __device__ __forceinline__ void riccati_step(const Group& G, float (&Vr)[NXf], c
     for (int j = 0; j < NXf; ++j) {
       float s = Qxx[j];
 #pragma unroll
-      for (int m = 0; m < NUf; ++m) s = s + Qxu[m] * sm[S_K + m * 10 + j];
+      for (int m = 0; m < NUf; ++m) s = fmaf(Qxu[m], sm[S_K + m * 10 + j], s);
       Vr[j] = s;
     }
     float s = qx;
 #pragma unroll
-    for (int m = 0; m < NUf; ++m) s = s + Qxu[m] * kk[m];
+    for (int m = 0; m < NUf; ++m) s = fmaf(Qxu[m], kk[m], s);
     sm[S_V + l] = s;
   }
   G.sync();
@@ -508,10 +511,10 @@ __device__ __forceinline__ void cost_rows(const Group& G, const float* __restric
     for (int j = 0; j < Nf; ++j) cx[j] = __ldg(cs + l * Nf + j);
     float a = cx[0] * sm[S_EZ + 0];
 #pragma unroll
-    for (int j = 1; j < NXf; ++j) a = a + cx[j] * sm[S_EZ + j];
+    for (int j = 1; j < NXf; ++j) a = fmaf(cx[j], sm[S_EZ + j], a);
     float b = cx[NXf] * sm[S_EZ + NXf];
 #pragma unroll
-    for (int j = 1; j < NUf; ++j) b = b + cx[NXf + j] * sm[S_EZ + NXf + j];
+    for (int j = 1; j < NUf; ++j) b = fmaf(cx[NXf + j], sm[S_EZ + NXf + j], b);
     lxi = a + b + __ldg(cv + l);
   } else if (l < Nf) {
     const int j = l - NXf;
@@ -519,10 +522,10 @@ __device__ __forceinline__ void cost_rows(const Group& G, const float* __restric
     for (int m = 0; m < NUf; ++m) cu[m] = __ldg(cs + l * Nf + NXf + m);
     float a = __ldg(cs + NXf + j) * sm[S_EZ + 0];
 #pragma unroll
-    for (int k = 1; k < NXf; ++k) a = a + __ldg(cs + k * Nf + NXf + j) * sm[S_EZ + k];
+    for (int k = 1; k < NXf; ++k) a = fmaf(__ldg(cs + k * Nf + NXf + j), sm[S_EZ + k], a);
     float b = cu[0] * sm[S_EZ + NXf];
 #pragma unroll
-    for (int m = 1; m < NUf; ++m) b = b + cu[m] * sm[S_EZ + NXf + m];
+    for (int m = 1; m < NUf; ++m) b = fmaf(cu[m], sm[S_EZ + NXf + m], b);
     luj = a + b + __ldg(cv + l);
   }
 }
@@ -538,7 +541,7 @@ __device__ __forceinline__ void quad_lin(const float* __restrict__ Cm, const flo
   for (int i = 0; i < Nf; ++i) {
     float cz = ld(i * Nf) * z[0];
 #pragma unroll
-    for (int j = 1; j < Nf; ++j) cz = cz + ld(i * Nf + j) * z[j];
+    for (int j = 1; j < Nf; ++j) cz = fmaf(ld(i * Nf + j), z[j], cz);
     const float term = form == 0 ? z[i] * cz : 0.5f * (z[i] * cz);
     const float lt = z[i] * (cv != nullptr ? __ldg(cv + i) : 0.0f);
     sq = i == 0 ? term : sq + term;
@@ -567,7 +570,7 @@ __device__ __forceinline__ void quad_split(const float* __restrict__ Cm, const f
       auto ld = [&](int j) { return Cm != nullptr ? __ldg(row + j) : 0.0f; };
       float cz = ld(0) * z[0];
 #pragma unroll
-      for (int j = 1; j < Nf; ++j) cz = cz + ld(j) * z[j];
+      for (int j = 1; j < Nf; ++j) cz = fmaf(ld(j), z[j], cz);
       float zi = z[0];
 #pragma unroll
       for (int q = 1; q < Nf; ++q) zi = (q == i) ? z[q] : zi;
@@ -594,7 +597,7 @@ __device__ __forceinline__ void quad_split(const float* __restrict__ Cm, const f
 // ---------------------------------------------------------------------------
 
 #ifndef FM_SOLVE_MINB
-#define FM_SOLVE_MINB 2
+#define FM_SOLVE_MINB 4  // 128 registers: at B = 16384, 8.7 ms against 11.1 ms at 2 CTAs per SM
 #endif
 
 // LPC lanes per line-search candidate (4 for up to four step sizes, else 2).
@@ -757,7 +760,7 @@ __global__ void __launch_bounds__(THREADS, FM_SOLVE_MINB) fm_solve_kernel(FmSolv
         for (int i = 0; i < 4; ++i) {
           float du = al * kr[40 + i];
 #pragma unroll
-          for (int j = 0; j < 10; ++j) du = du + kr[i * 10 + j] * dx[j];
+          for (int j = 0; j < 10; ++j) du = fmaf(kr[i * 10 + j], dx[j], du);
           const float v = nr[10 + i] + du;
           u[i] = BOUNDED ? fclamp(v, ulo[i], uhi[i]) : v;
         }
@@ -999,7 +1002,7 @@ __global__ void __launch_bounds__(THREADS) fm_backward_kernel(FmBackwardParams p
     if (l < NUf) {
       float s = kr[40 + l];
 #pragma unroll
-      for (int j = 0; j < NXf; ++j) s = s + kr[l * 10 + j] * sm[S_DX + j];
+      for (int j = 0; j < NXf; ++j) s = fmaf(kr[l * 10 + j], sm[S_DX + j], s);
       sm[S_DU + l] = s;
     }
     // tau = [X_t - x_ref_t; U_t - u_ref_t] at the solution, into S_EZ
@@ -1010,9 +1013,9 @@ __global__ void __launch_bounds__(THREADS) fm_backward_kernel(FmBackwardParams p
     if (l < NXf) {
       float s = 0.0f;
 #pragma unroll
-      for (int j = 0; j < NXf; ++j) s = s + sm[S_A + l * 10 + j] * sm[S_DX + j];
+      for (int j = 0; j < NXf; ++j) s = fmaf(sm[S_A + l * 10 + j], sm[S_DX + j], s);
 #pragma unroll
-      for (int j = 0; j < NUf; ++j) s = s + sm[S_B + l * 4 + j] * sm[S_DU + j];
+      for (int j = 0; j < NUf; ++j) s = fmaf(sm[S_B + l * 4 + j], sm[S_DU + j], s);
       dxn = s;
     }
     if (l < Nf) {

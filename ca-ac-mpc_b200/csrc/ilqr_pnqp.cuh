@@ -29,16 +29,21 @@ __device__ __forceinline__ void solve4_pivot(float (&A)[4][4], float (&b)[4]) {
         r = i;
       }
     }
-    if (r != k) {
+    // row swap with compile-time indices (r is a runtime value; indexing by
+    // it would move A to local memory)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float tmp = A[k][j];
-        A[k][j] = A[r][j];
-        A[r][j] = tmp;
+    for (int i = k + 1; i < 4; ++i) {
+      if (i == r) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float tmp = A[k][j];
+          A[k][j] = A[i][j];
+          A[i][j] = tmp;
+        }
+        const float tb = b[k];
+        b[k] = b[i];
+        b[i] = tb;
       }
-      const float tb = b[k];
-      b[k] = b[r];
-      b[r] = tb;
     }
     float piv = A[k][k];
     if (fabsf(piv) < 1e-10f) piv = piv < 0.0f ? -1e-10f : 1e-10f;

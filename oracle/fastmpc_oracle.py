@@ -30,9 +30,10 @@ reference lines:
   from X - x_ref).
 
 The reference build is not run here (it needs libtorch). Arithmetic is fp32
-with the reference kernels' operation order (sequential sums, no fused
-multiply-add; the reference compiles with --use_fast_math, whose rounding is
-not restated). Pinned pieces: pnqp4 against mpc.pytorch's pnqp (golden
+with the reference kernels' operation order: sums in index order, each product
+rounded. (The reference compiles with --use_fast_math, which contracts
+products into fused multiply-adds, as the B200 kernels do in their matrix
+products; that rounding is not restated, and the parity bars absorb it.) Pinned pieces: pnqp4 against mpc.pytorch's pnqp (golden
 vectors), the Jacobian against central differences of the continuous
 dynamics, and the Riccati pass, line search and adjoint against the closed
 form of linear-quadratic problems (tests/test_oracle_fastmpc.py).

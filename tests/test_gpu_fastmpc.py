@@ -5,8 +5,9 @@ The GPU records its line-search decisions and the iteration at which the
 batch stopped; the oracle replays them (the decisions are rounding-level
 ties in any fp32 implementation) and the remaining arithmetic must agree to
 1e-4 on X, U (relative to the largest magnitude of the element) and 1e-3 on
-the gradients. The kernels and the oracle share operation order; only sinf,
-cosf (CUDA's, within 2 ulp, against the host's) separate them.
+the gradients. The kernels and the oracle share operation order; they differ
+by the kernels' fused multiply-adds in matrix products and by sinf, cosf
+(CUDA's, within 2 ulp, against the host's).
 """
 
 import numpy as np
