@@ -530,31 +530,12 @@ __device__ __forceinline__ void cost_rows(const Group& G, const float* __restric
   }
 }
 
-// 0.5 z^T C z and z^T c summed in index order; form 0: 0.5 * sum(z Cz)
-// (compute_cost), form 1: sum(0.5 * (z Cz)) (line search).
-// A null C or c reads as zeros (the zero terminal cost of the operator).
-__device__ __forceinline__ void quad_lin(const float* __restrict__ Cm, const float* __restrict__ cv,
-                                         const float (&z)[Nf], int form, float& quad, float& lin) {
-  float sq = 0.0f, sl = 0.0f;
-  auto ld = [&](int i) { return Cm != nullptr ? __ldg(Cm + i) : 0.0f; };
-#pragma unroll 2
-  for (int i = 0; i < Nf; ++i) {
-    float cz = ld(i * Nf) * z[0];
-#pragma unroll
-    for (int j = 1; j < Nf; ++j) cz = fmaf(ld(i * Nf + j), z[j], cz);
-    const float term = form == 0 ? z[i] * cz : 0.5f * (z[i] * cz);
-    const float lt = z[i] * (cv != nullptr ? __ldg(cv + i) : 0.0f);
-    sq = i == 0 ? term : sq + term;
-    sl = i == 0 ? lt : sl + lt;
-  }
-  quad = form == 0 ? 0.5f * sq : sq;
-  lin = sl;
-}
-
-// quad_lin split over L lanes: this lane (r of the L lanes starting at warp
-// lane `first`) forms rows r, r + L, ... of C z; the 14 row terms are then
-// gathered by shuffles and summed in index order, so every one of the L lanes
-// returns the sums quad_lin returns.
+// 0.5 z^T C z and z^T c, each summed in index order, with the rows of C z
+// split over L lanes: this lane (r of the L lanes starting at warp lane
+// `first`) forms rows r, r + L, ...; the 14 row terms are gathered by shuffles,
+// so every one of the L lanes returns the same sums. form 0: 0.5 * sum(z Cz)
+// (compute_cost), form 1: sum(0.5 * (z Cz)) (line search). A null C or c
+// reads as zeros (the zero terminal cost of the operator).
 template <int L>
 __device__ __forceinline__ void quad_split(const float* __restrict__ Cm, const float* __restrict__ cv,
                                            const float (&z)[Nf], int r, unsigned gm, int first, int form,
