@@ -209,3 +209,25 @@ def test_fastmpc_operator_autograd_equals_entry_points():
     with torch.no_grad():
         Xi, Ui, _ = m(_t(d["x0"]), mpc_compat.QuadCost(C.detach(), c.detach()), type("Dx", (), {"dt": 0.05})())
     assert torch.equal(Xi, X.detach()) and torch.equal(Ui, U.detach())
+
+
+def test_fastmpc_training_scale_prefix_identity():
+    """At B = 16384, T = 20 every output is finite, and the first 512 elements
+    equal a B = 512 solve bit for bit when both batches ran the same number of
+    iterations (elements share nothing but the batch stop)."""
+    B, T = 16384, 20
+    d = wl.make_inputs(B, T, seed=11)
+    full = nat.fastmpc_solve(_t(d["x0"]), _t(d["U_init"]), _t(d["C"]), _t(d["c"]), u_min=_t(LO), u_max=_t(HI),
+                             dt=0.05, max_iter=5, want_trace=True)
+    part = nat.fastmpc_solve(_t(d["x0"][:512]), _t(d["U_init"][:512]), _t(d["C"][:512]), _t(d["c"][:512]),
+                             u_min=_t(LO), u_max=_t(HI), dt=0.05, max_iter=5, want_trace=True)
+    for k in ("X", "U", "X_lin", "U_lin", "best_cost"):
+        assert torch.isfinite(full[k]).all(), k
+    if int(full["batch_info"][1]) == int(part["batch_info"][1]):
+        for k in ("X", "U", "X_lin", "U_lin", "tight", "trace", "best_cost"):
+            assert torch.equal(full[k][:512], part[k]), k
+    gX, gU = (_t(a) for a in wl.make_backward_seeds(B, T))
+    g = nat.fastmpc_backward(full["X"], full["U"], full["X_lin"], full["U_lin"], _t(d["C"]), gX, gU,
+                             tight=full["tight"])
+    for k in ("x0", "C", "c"):
+        assert torch.isfinite(g[k]).all(), k
