@@ -231,3 +231,25 @@ def test_fastmpc_training_scale_prefix_identity():
                              tight=full["tight"])
     for k in ("x0", "C", "c"):
         assert torch.isfinite(g[k]).all(), k
+
+
+def test_fastmpc_nonfinite_element_is_isolated():
+    """A NaN in one element's costs gives that element a NaN cost: it never
+    improves (U stays clamp(U_init), X its rollout), and its NaN improvement
+    keeps the batch from stopping early, as the reference's batch-wide max does
+    (drone_ilqr_ext.cpp:1029-1049). The other elements stay finite and match
+    the oracle's replay."""
+    d, o = _case("cfg2_b64_t10")
+    d = dict(d, C=d["C"].copy())
+    d["C"][3, 2, 0, 0] = np.nan
+    g = _np(_gpu(d, o))
+    assert g["batch_info"][1] == o["max_iter"] and g["batch_info"][0] == 0
+    U0 = np.minimum(np.maximum(d["U_init"][3], LO), HI)
+    assert np.array_equal(g["U"][3], U0)
+    assert np.isfinite(g["X"][3]).all() and np.isnan(g["best_cost"][3])
+    assert (g["trace"][3] < 0).all()
+    others = np.arange(64) != 3
+    assert np.isfinite(g["X"][others]).all() and np.isfinite(g["U"][others]).all()
+    r = _oracle_replay(d, o, g)
+    for k in ("X", "U"):
+        assert _rel(g[k][others], r[k][others]).max() <= TOL_XU, k
