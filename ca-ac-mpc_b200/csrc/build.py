@@ -4,7 +4,8 @@
 
 Compiles every .cu file in this directory with nvcc for sm_100a
 (-gencode arch=compute_100a,code=sm_100a, -lineinfo, -fmad=false so the model
-arithmetic rounds like the reference's elementwise torch ops) and links them
+arithmetic rounds like the reference's elementwise torch ops; FILE_FLAGS adds
+per-file options) and links them
 into ca-ac-mpc_b200/libilqr_b200.so. Objects are rebuilt only when a source or
 header is newer than the object (make-style), in parallel.
 """
@@ -29,6 +30,11 @@ NVCC = os.environ.get("NVCC", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-fmad=false", "-Xcompiler", "-fPIC,-O2",
          "-I", os.path.join(ROOT, "include"), "-I", HERE]
+# Per-file additions. The FastMPC numerics kernels restate a build compiled
+# with --use_fast_math, whose divisions are the approximate (2-ulp) kind; they
+# use that division too (at B = 16384 the solve takes 5.4 ms instead of 8.5 ms
+# with IEEE division, inside the same parity bars).
+FILE_FLAGS = {"ilqr_fastmpc.cu": ["-prec-div=false"]}
 
 
 def _newer(src_files, target):
@@ -48,8 +54,8 @@ def build(verbose: bool = False) -> str:
     for src in sources:
         obj = os.path.join(OBJ_DIR, os.path.basename(src).replace(".cu", ".o"))
         objs.append(obj)
-        if _newer([src] + headers, obj):
-            cmd = [NVCC, *ARCH, *FLAGS, "-c", src, "-o", obj]
+        if _newer([src, os.path.abspath(__file__)] + headers, obj):
+            cmd = [NVCC, *ARCH, *FLAGS, *FILE_FLAGS.get(os.path.basename(src), []), "-c", src, "-o", obj]
             if verbose:
                 cmd.insert(1, "-Xptxas=-v")
             jobs.append(cmd)

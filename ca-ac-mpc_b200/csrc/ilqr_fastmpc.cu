@@ -28,10 +28,12 @@
 // rejection (its trace repeats that rejection).
 //
 // Arithmetic is fp32. The matrix-product and cost sums run in index order as
-// fused multiply-adds (the reference build compiles with --use_fast_math,
-// which contracts them too); the oracle rounds each product, so the two
-// differ at the rounding level. The model step and Jacobian entries are
-// evaluated without contraction (the library is compiled with -fmad=false).
+// fused multiply-adds, and this file is compiled with -prec-div=false, so
+// divisions (PNQP, the LU, the model step) are the approximate 2-ulp kind: the
+// reference build compiles with --use_fast_math, which does both. The oracle
+// rounds each product and divides exactly, so the two differ at the rounding
+// level. The model step and Jacobian entries are otherwise evaluated without
+// contraction (the library is compiled with -fmad=false).
 #include <cstdint>
 
 #include "ilqr_b200.h"

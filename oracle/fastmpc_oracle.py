@@ -31,9 +31,10 @@ reference lines:
 
 The reference build is not run here (it needs libtorch). Arithmetic is fp32
 with the reference kernels' operation order: sums in index order, each product
-rounded. (The reference compiles with --use_fast_math, which contracts
-products into fused multiply-adds, as the B200 kernels do in their matrix
-products; that rounding is not restated, and the parity bars absorb it.) Pinned pieces: pnqp4 against mpc.pytorch's pnqp (golden
+rounded, divisions exact. (The reference compiles with --use_fast_math, which
+contracts products into fused multiply-adds and makes division approximate,
+as the B200 kernels do; that rounding is not restated, and the parity bars
+absorb it.) Pinned pieces: pnqp4 against mpc.pytorch's pnqp (golden
 vectors), the Jacobian against central differences of the continuous
 dynamics, and the Riccati pass, line search and adjoint against the closed
 form of linear-quadratic problems (tests/test_oracle_fastmpc.py).

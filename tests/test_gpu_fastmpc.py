@@ -6,7 +6,8 @@ batch stopped; the oracle replays them (the decisions are rounding-level
 ties in any fp32 implementation) and the remaining arithmetic must agree to
 1e-4 on X, U (relative to the largest magnitude of the element) and 1e-3 on
 the gradients. The kernels and the oracle share operation order; they differ
-by the kernels' fused multiply-adds in matrix products and by sinf, cosf
+by the kernels' fused multiply-adds in matrix products, their approximate
+(2-ulp) division, as in the reference's fast-math build, and by sinf, cosf
 (CUDA's, within 2 ulp, against the host's).
 """
 
