@@ -56,6 +56,7 @@ constexpr int EPC = EPW * WPC;     // elements per CTA
 constexpr int THREADS = WPC * 32;
 constexpr int REC = 16;            // floats per trajectory record: x[10], u[4], 2 pad
 constexpr int KREC = 44;           // floats per gain record: K[4][10], k[4]
+constexpr unsigned SM_COUNT_FM = 148;  // B200 SMs (the register-tier choice)
 constexpr float MASS = 0.752f;     // drone_kernels.cu:12
 constexpr float G_VAL = -9.8066f;  // drone_kernels.cu:13
 
@@ -579,13 +580,11 @@ __device__ __forceinline__ void quad_split(const float* __restrict__ Cm, const f
 // Solve
 // ---------------------------------------------------------------------------
 
-#ifndef FM_SOLVE_MINB
-#define FM_SOLVE_MINB 4  // 128 registers: at B = 16384, 8.7 ms against 11.1 ms at 2 CTAs per SM
-#endif
-
 // LPC lanes per line-search candidate (4 for up to four step sizes, else 2).
-template <bool BOUNDED, int LPC>
-__global__ void __launch_bounds__(THREADS, FM_SOLVE_MINB) fm_solve_kernel(FmSolveParams p, int it0, int it1) {
+// MINB CTAs per SM: the register tier (2: up to 255 registers, for grids of one
+// 2-CTA wave; 3: 168 registers, for larger grids).
+template <bool BOUNDED, int LPC, int MINB>
+__global__ void __launch_bounds__(THREADS, MINB) fm_solve_kernel(FmSolveParams p, int it0, int it1) {
   if (*(volatile const int32_t*)(p.flags) != 0) return;  // the batch stopped at an earlier check
   __shared__ float smem[EPC * S_ELEM];
   __shared__ uint32_t jtab[36];
@@ -1077,13 +1076,21 @@ cudaError_t launch_solve(FmSolveParams& p, cudaStream_t stream) {
     const int it0 = s * FM_CHECK_PERIOD;
     const int it1 = p.max_iter > 0 ? (it0 + FM_CHECK_PERIOD < p.max_iter ? it0 + FM_CHECK_PERIOD : p.max_iter) : 0;
     const bool wide = p.n_alpha <= GL / 4;
+    // one wave at 2 CTAs per SM runs the fat tier (B = 2048: 0.89 against
+    // 1.01 ms at 4 CTAs per SM); larger grids the 3-CTA tier (B = 16384: 5.35
+    // ms, against 5.45 ms at 4 and 6.22 ms at 2)
+    const bool fat = grid <= 2u * SM_COUNT_FM;
+#define FM_LAUNCH(BD, L)                                                          \
+  (fat ? (fm_solve_kernel<BD, L, 2><<<grid, THREADS, 0, stream>>>(p, it0, it1), 0) \
+       : (fm_solve_kernel<BD, L, 3><<<grid, THREADS, 0, stream>>>(p, it0, it1), 0))
     if (bounded) {
-      if (wide) fm_solve_kernel<true, 4><<<grid, THREADS, 0, stream>>>(p, it0, it1);
-      else fm_solve_kernel<true, 2><<<grid, THREADS, 0, stream>>>(p, it0, it1);
+      if (wide) FM_LAUNCH(true, 4);
+      else FM_LAUNCH(true, 2);
     } else {
-      if (wide) fm_solve_kernel<false, 4><<<grid, THREADS, 0, stream>>>(p, it0, it1);
-      else fm_solve_kernel<false, 2><<<grid, THREADS, 0, stream>>>(p, it0, it1);
+      if (wide) FM_LAUNCH(false, 4);
+      else FM_LAUNCH(false, 2);
     }
+#undef FM_LAUNCH
     if (p.max_iter > 0) fm_check_kernel<<<1, 1024, 0, stream>>>(p, it1);
   }
   const unsigned fgrid = (unsigned)((p.B + 7) / 8);
