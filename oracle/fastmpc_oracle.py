@@ -29,7 +29,9 @@ reference lines:
   617-745 and the assembly of :1092-1256 (grad_x_ref[T] = dX_T, tau built
   from X - x_ref).
 
-The reference build is not run here (it needs libtorch). Arithmetic is fp32
+The reference extension as a whole is not built here (it needs libtorch); its
+CUDA kernels are, from their own sources (oracle/build_fastmpc_ref.py), and the
+GPU tests re-drive them (tests/fastmpc_ref.py). Arithmetic is fp32
 with the reference kernels' operation order: sums in index order, each product
 rounded, divisions exact. (The reference compiles with --use_fast_math, which
 contracts products into fused multiply-adds and makes division approximate,

@@ -1,8 +1,9 @@
 """Pins of the FastMPC-numerics oracle (oracle/fastmpc_oracle.py).
 
-The reference FastMPC build cannot run here (it needs libtorch), so the
-restatement is pinned piece by piece against mathematics the reference code
-implements:
+The reference FastMPC extension cannot be built as a whole here (it needs
+libtorch); its CUDA kernels are checked against the B200 kernels on the GPU
+(tests/test_gpu_fastmpc_reference.py). On the CPU the restatement is pinned
+piece by piece against mathematics the reference code implements:
 - the model: the Jacobian is I + dt times the exact derivative of the
   continuous dynamics (central differences in fp64), and the two step forms
   (rotation matrix and cross product) agree and keep the quaternion unit;
