@@ -9,7 +9,7 @@
 //
 // The prototypes below restate the reference launchers' signatures
 // (drone_kernels.cuh:11-31, forward_pass_kernel.cuh:57-73,
-// backward_pass_kernel.cuh:102-230); the wrappers only forward and report the
+// backward_pass_kernel.cuh:102-230, the last defined in pnqp_kernel.cu:43); the wrappers only forward and report the
 // launch status.
 #include <cuda_runtime.h>
 
@@ -31,6 +31,8 @@ void launch_backward_pass_batched_pnqp(const float* A, const float* B, const flo
                                        const float* l_xN, const float* U, const float* u_min, const float* u_max,
                                        float reg_eps, int batch_size, int T, float* K_out, float* k_out,
                                        float* v0_out, float* free_mask_out, cudaStream_t stream);
+void launch_pnqp4_batch(const float* H, const float* q, const float* lower, const float* upper, const float* x_init,
+                        float* x_out, float* free_mask_out, int N, cudaStream_t stream);
 void launch_implicit_diff_assembly(const float* K_seq, const float* k_seq, const float* v0, const float* A_lin,
                                    const float* B_lin, const float* X, const float* U, const float* x_ref,
                                    const float* u_ref, float* grad_C, float* grad_c, float* grad_x0, float* grad_xref,
@@ -78,6 +80,12 @@ int fmref_riccati_pnqp(const float* A, const float* Bm, const float* lxx, const 
                        float* v0, float* free_mask, void* s) {
   drone_kernels::launch_backward_pass_batched_pnqp(A, Bm, lxx, luu, lxu, lx, lu, lxxN, lxN, U, u_min, u_max, reg, B,
                                                    T, K, k, v0, free_mask, st(s));
+  return status();
+}
+
+int fmref_pnqp4(const float* H, const float* q, const float* lo, const float* hi, const float* x_init, float* x,
+                float* free_mask, int n, void* s) {
+  drone_kernels::launch_pnqp4_batch(H, q, lo, hi, x_init, x, free_mask, n, st(s));
   return status();
 }
 

@@ -50,6 +50,7 @@ def lib():
             "fmref_riccati": [P] * 10 + [F, I, I, P, P, P, P],
             "fmref_riccati_pnqp": [P] * 12 + [F, I, I, P, P, P, P, P],
             "fmref_assembly": [P] * 16 + [I, I, P],
+            "fmref_pnqp4": [P] * 7 + [I, P],
         }
         for name, args in sig.items():
             fn = getattr(L, name)
@@ -220,3 +221,17 @@ def backward(res, grad_X, grad_U, reg=1e-6):
     _chk(L.fmref_assembly(_p(K), _p(k), _p(v0), _p(res["A_lin"]), _p(res["B_lin"]), _p(X), _p(U), _p(x_ref),
                           _p(u_ref), _p(gC), _p(gc), _p(gx0), None, None, None, None, B, T, _s()), "assembly")
     return dict(x0=gx0, C=gC, c=gc)
+
+
+def pnqp4_batch(H, q, lower, upper, x_init=None):
+    """The reference's batched PNQP-4 kernel (pnqp_kernel.cu:43,
+    ext.drone_pnqp4_batch): (x* [n,4], free mask [n,4])."""
+    L = lib()
+    H, q, lower, upper = _f32(H), _f32(q), _f32(lower), _f32(upper)
+    n = H.shape[0]
+    x = torch.empty(n, 4, device=H.device)
+    fm = torch.empty(n, 4, device=H.device)
+    _chk(L.fmref_pnqp4(_p(H), _p(q), _p(lower), _p(upper), _p(None if x_init is None else _f32(x_init)), _p(x),
+                       _p(fm), n, _s()), "pnqp4")
+    return x, fm
+

@@ -121,3 +121,21 @@ def test_free_run_parts_from_reference_only_at_ties(name):
             gap = abs(c[j] - best[b, i]) if j >= 0 else abs(c[-jo - 1] - c[-jr - 1])
         assert gap <= 1e-5 * scale, (b, i, jo, jr, gap / scale)
     assert parted < to.shape[0]
+
+
+def test_pnqp4_batch_matches_reference_kernel():
+    """drone_pnqp4_batch against the reference's own PNQP-4 kernel on the
+    golden problems (mpc.pytorch pnqp's set) and on the box QPs of a solve:
+    the same optimum to 1e-4 and the same free mask, cold and warm started."""
+    import os
+    from parity import GOLDEN_DIR
+    d = np.load(os.path.join(GOLDEN_DIR, "pnqp4_n256.npz"))
+    H, q, lo, hi = (_t(d[k]) for k in ("H", "q", "lower", "upper"))
+    for x_init in (None, _t(d["opt_x"].astype(np.float32))):
+        x, fm = nat.pnqp4_batch(H, q, lo, hi, x_init)
+        rx, rfm = ref.pnqp4_batch(H, q, lo, hi, x_init)
+        scale = torch.clamp(rx.abs().amax(1, keepdim=True), min=1.0)
+        close = ((x - rx).abs() / scale).amax(1) <= 1e-4
+        assert close.float().mean().item() >= 0.98, close.float().mean().item()
+        assert torch.equal(fm[close], rfm[close])
+
