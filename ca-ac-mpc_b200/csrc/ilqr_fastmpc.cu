@@ -1036,8 +1036,251 @@ __global__ void __launch_bounds__(THREADS) fm_backward_kernel(FmBackwardParams p
 }
 
 // ---------------------------------------------------------------------------
+// Extension-surface kernels: the reference extension's separate entry points
+// with its numerics, one thread per step or per element (a compatibility
+// path; the solve and backward above are the fused ones)
+// ---------------------------------------------------------------------------
+
+// A [n][10][10], B [n][10][4] at the points (X[b][t], U[b][t]), t < T
+// (drone_kernels.cu:64-190), with the entry values of the fused kernels.
+__global__ void fm_linearize_kernel(const float* __restrict__ X, const float* __restrict__ U, int64_t B, int T,
+                                    float dt, float* __restrict__ A, float* __restrict__ Bm) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= B * T) return;
+  const int64_t b = i / T;
+  const int t = (int)(i - b * T);
+  const float* x = X + (b * (T + 1) + t) * NXf;
+  const float* u = U + i * NUf;
+  float* Ai = A + i * NXf * NXf;
+  float* Bi = Bm + i * NXf * NUf;
+  for (int e = 0; e < NXf * NXf; ++e) {
+    const int r = e / NXf, c = e % NXf;
+    float v = r == c ? 1.0f : 0.0f;
+    if ((r == 0 && c == 7) || (r == 1 && c == 8) || (r == 2 && c == 9)) v = dt;
+    Ai[e] = v;
+  }
+  for (int e = 0; e < NXf * NUf; ++e) Bi[e] = 0.0f;
+  const float fc = u[0];
+  const float fcm = fc / MASS;
+  float var[11];
+  for (int l = 0; l < 3; ++l) var[l] = u[1 + l];
+  for (int l = 3; l < 7; ++l) var[l] = x[l];
+  for (int l = 7; l < 11; ++l) var[l] = x[l - 4] * fcm;
+  const float h = 0.5f * dt, t2 = 2.0f * dt;
+  for (int e = 0; e < 36; ++e) {
+    const uint32_t code = kJacTable[e];
+    const float p = (((code >> 13) & 1u) ? t2 : h) * var[(code >> 9) & 15u];
+    const bool minus = (code >> 15) & 1u;
+    const float v = ((code >> 14) & 1u) == 0u ? (minus ? 0.0f - p : 0.0f + p) : (minus ? -p : p);
+    const uint32_t dst = code & 511u;  // offset in the shared-memory block: A at S_A, B at S_B
+    if (dst < (uint32_t)S_B) Ai[dst - S_A] = v;
+    else Bi[dst - S_B] = v;
+  }
+  const float qw = x[3], qx = x[4], qy = x[5], qz = x[6];
+  const float dtm = dt / MASS;
+  Bi[7 * NUf] = 2.0f * (qx * qz + qw * qy) * dtm;
+  Bi[8 * NUf] = 2.0f * (qy * qz - qw * qx) * dtm;
+  Bi[9 * NUf] = (qw * qw - qx * qx - qy * qy + qz * qz) * dtm;
+}
+
+// drone_backward_pass_batched on given matrices (backward_pass_kernel.cu:
+// 617-745): Q terms with reg once; a tight control's row and column of Q_uu
+// are zeroed with a 1e-11 diagonal, its column of Q_xu and entry of q_u
+// zeroed; gains by the pivoted LU; V = Q_xx + Q_xu K, v = q_x + Q_xu k.
+__global__ void fm_adjoint_lqr_kernel(const float* __restrict__ A, const float* __restrict__ Bm,
+                                      const float* __restrict__ l_xx, const float* __restrict__ l_uu,
+                                      const float* __restrict__ l_xu, const float* __restrict__ l_x,
+                                      const float* __restrict__ l_u, const float* __restrict__ l_xxN,
+                                      const float* __restrict__ l_xN, const uint8_t* __restrict__ tight, int64_t B,
+                                      int T, float reg, float* __restrict__ Kout, float* __restrict__ kout,
+                                      float* __restrict__ v0) {
+  const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  float V[NXf][NXf], v[NXf];
+  for (int i = 0; i < NXf; ++i) {
+    v[i] = l_xN[b * NXf + i];
+    for (int j = 0; j < NXf; ++j) V[i][j] = l_xxN[(b * NXf + i) * NXf + j];
+  }
+  for (int t = T - 1; t >= 0; --t) {
+    const int64_t bt = b * T + t;
+    const float* At = A + bt * NXf * NXf;
+    const float* Bt = Bm + bt * NXf * NUf;
+    float VA[NXf][NXf], VB[NXf][NUf];
+    for (int i = 0; i < NXf; ++i) {
+      for (int j = 0; j < NXf; ++j) {
+        float s = 0.0f;
+        for (int k = 0; k < NXf; ++k) s = fmaf(V[i][k], At[k * NXf + j], s);
+        VA[i][j] = s;
+      }
+      for (int j = 0; j < NUf; ++j) {
+        float s = 0.0f;
+        for (int k = 0; k < NXf; ++k) s = fmaf(V[i][k], Bt[k * NUf + j], s);
+        VB[i][j] = s;
+      }
+    }
+    float Qxx[NXf][NXf], Qxu[NXf][NUf], qx[NXf], H[4][4], q[4];
+    for (int i = 0; i < NXf; ++i) {
+      for (int j = 0; j < NXf; ++j) {
+        float s = l_xx[bt * NXf * NXf + i * NXf + j];
+        for (int k = 0; k < NXf; ++k) s = fmaf(At[k * NXf + i], VA[k][j], s);
+        Qxx[i][j] = s;
+      }
+      for (int j = 0; j < NUf; ++j) {
+        float s = l_xu[bt * NXf * NUf + i * NUf + j];
+        for (int k = 0; k < NXf; ++k) s = fmaf(At[k * NXf + i], VB[k][j], s);
+        Qxu[i][j] = s;
+      }
+      float s = l_x[bt * NXf + i];
+      for (int k = 0; k < NXf; ++k) s = fmaf(At[k * NXf + i], v[k], s);
+      qx[i] = s;
+    }
+    for (int a = 0; a < NUf; ++a) {
+      for (int c = 0; c < NUf; ++c) {
+        float s = l_uu[bt * NUf * NUf + a * NUf + c];
+        for (int k = 0; k < NXf; ++k) s = fmaf(Bt[k * NUf + a], VB[k][c], s);
+        if (a == c) s = s + reg;
+        H[a][c] = s;
+      }
+      float s = l_u[bt * NUf + a];
+      for (int k = 0; k < NXf; ++k) s = fmaf(Bt[k * NUf + a], v[k], s);
+      q[a] = s;
+    }
+    if (tight != nullptr) {
+      float fr[4];
+      for (int a = 0; a < NUf; ++a) fr[a] = tight[bt * NUf + a] ? 0.0f : 1.0f;
+      for (int a = 0; a < NUf; ++a) {
+        for (int c = 0; c < NUf; ++c) H[a][c] = H[a][c] * (fr[a] * fr[c]);
+        if (fr[a] == 0.0f) H[a][a] = H[a][a] + 1e-11f;
+        q[a] = q[a] * fr[a];
+        for (int r = 0; r < NXf; ++r) Qxu[r][a] = Qxu[r][a] * fr[a];
+      }
+    }
+    int piv[4];
+    lu_factor4(H, piv);
+    float K[NUf][NXf], kk[4];
+    for (int j = 0; j < NXf; ++j) {
+      float rhs[4];
+      for (int a = 0; a < NUf; ++a) rhs[a] = -Qxu[j][a];
+      lu_solve4(H, piv, rhs);
+      for (int a = 0; a < NUf; ++a) K[a][j] = rhs[a];
+    }
+    for (int a = 0; a < NUf; ++a) kk[a] = -q[a];
+    lu_solve4(H, piv, kk);
+    for (int a = 0; a < NUf; ++a) {
+      for (int j = 0; j < NXf; ++j) Kout[(bt * NUf + a) * NXf + j] = K[a][j];
+      kout[bt * NUf + a] = kk[a];
+    }
+    for (int i = 0; i < NXf; ++i) {
+      for (int j = 0; j < NXf; ++j) {
+        float s = Qxx[i][j];
+        for (int m = 0; m < NUf; ++m) s = fmaf(Qxu[i][m], K[m][j], s);
+        V[i][j] = s;
+      }
+      float s = qx[i];
+      for (int m = 0; m < NUf; ++m) s = fmaf(Qxu[i][m], kk[m], s);
+      v[i] = s;
+    }
+  }
+  for (int i = 0; i < NXf; ++i) v0[b * NXf + i] = v[i];
+}
+
+// drone_implicit_diff_assembly (backward_pass_kernel.cu:1092-1256): the
+// tangent sweep dU = K dX + k, dX' = A dX + B dU from dX_0 = 0, then
+// grad_C = -1/2 (d tau tau^T + tau d tau^T), grad_c = -d tau with
+// tau = [X - x_ref; U - u_ref], grad_x_ref = dX (t = 0..T), grad_u_ref = dU,
+// grad_x0 = -v0, and the terminal grad_C_final, grad_c_final. Outputs may be
+// null except grad_C, grad_c, grad_x0.
+__global__ void fm_assembly_kernel(const float* __restrict__ K, const float* __restrict__ k,
+                                   const float* __restrict__ v0, const float* __restrict__ A,
+                                   const float* __restrict__ Bm, const float* __restrict__ X,
+                                   const float* __restrict__ U, const float* __restrict__ x_ref,
+                                   const float* __restrict__ u_ref, int64_t B, int T, float* gC, float* gc,
+                                   float* gx0, float* gxr, float* gur, float* gCf, float* gcf) {
+  const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  for (int i = 0; i < NXf; ++i) gx0[b * NXf + i] = -v0[b * NXf + i];
+  float dX[NXf];
+  for (int i = 0; i < NXf; ++i) dX[i] = 0.0f;
+  for (int t = 0; t < T; ++t) {
+    const int64_t bt = b * T + t;
+    float dU[NUf], tau[Nf], dt_[Nf];
+    for (int a = 0; a < NUf; ++a) {
+      float s = k[bt * NUf + a];
+      for (int j = 0; j < NXf; ++j) s = fmaf(K[(bt * NUf + a) * NXf + j], dX[j], s);
+      dU[a] = s;
+    }
+    for (int i = 0; i < NXf; ++i) {
+      tau[i] = X[(b * (T + 1) + t) * NXf + i] - (x_ref != nullptr ? x_ref[(b * (T + 1) + t) * NXf + i] : 0.0f);
+      dt_[i] = dX[i];
+    }
+    for (int a = 0; a < NUf; ++a) {
+      tau[NXf + a] = U[bt * NUf + a] - (u_ref != nullptr ? u_ref[bt * NUf + a] : 0.0f);
+      dt_[NXf + a] = dU[a];
+    }
+    for (int i = 0; i < Nf; ++i) {
+      for (int j = 0; j < Nf; ++j) gC[(bt * Nf + i) * Nf + j] = -0.5f * (dt_[i] * tau[j] + tau[i] * dt_[j]);
+      gc[bt * Nf + i] = -dt_[i];
+    }
+    if (gxr != nullptr)
+      for (int i = 0; i < NXf; ++i) gxr[(b * (T + 1) + t) * NXf + i] = dX[i];
+    if (gur != nullptr)
+      for (int a = 0; a < NUf; ++a) gur[bt * NUf + a] = dU[a];
+    float dn[NXf];
+    for (int i = 0; i < NXf; ++i) {
+      float s = 0.0f;
+      for (int j = 0; j < NXf; ++j) s = fmaf(A[(bt * NXf + i) * NXf + j], dX[j], s);
+      for (int j = 0; j < NUf; ++j) s = fmaf(Bm[(bt * NXf + i) * NUf + j], dU[j], s);
+      dn[i] = s;
+    }
+    for (int i = 0; i < NXf; ++i) dX[i] = dn[i];
+  }
+  if (gxr != nullptr)
+    for (int i = 0; i < NXf; ++i) gxr[(b * (T + 1) + T) * NXf + i] = dX[i];
+  float tn[Nf], dn[Nf];
+  for (int i = 0; i < Nf; ++i) {
+    tn[i] = i < NXf ? X[(b * (T + 1) + T) * NXf + i] - (x_ref != nullptr ? x_ref[(b * (T + 1) + T) * NXf + i] : 0.0f)
+                    : 0.0f;
+    dn[i] = i < NXf ? dX[i] : 0.0f;
+  }
+  if (gCf != nullptr)
+    for (int i = 0; i < Nf; ++i)
+      for (int j = 0; j < Nf; ++j) gCf[(b * Nf + i) * Nf + j] = -0.5f * (dn[i] * tn[j] + tn[i] * dn[j]);
+  if (gcf != nullptr)
+    for (int i = 0; i < Nf; ++i) gcf[b * Nf + i] = -dn[i];
+}
+
+// ---------------------------------------------------------------------------
 // Launchers
 // ---------------------------------------------------------------------------
+
+cudaError_t launch_linearize(const float* X, const float* U, int64_t B, int T, float dt, float* A, float* Bm,
+                             cudaStream_t stream) {
+  const int64_t n = B * T;
+  if (n == 0) return cudaSuccess;
+  fm_linearize_kernel<<<(unsigned)((n + 127) / 128), 128, 0, stream>>>(X, U, B, T, dt, A, Bm);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_adjoint_lqr(const float* A, const float* Bm, const float* l_xx, const float* l_uu,
+                               const float* l_xu, const float* l_x, const float* l_u, const float* l_xxN,
+                               const float* l_xN, const uint8_t* tight, int64_t B, int T, float reg, float* K,
+                               float* k, float* v0, cudaStream_t stream) {
+  if (B == 0) return cudaSuccess;
+  fm_adjoint_lqr_kernel<<<(unsigned)((B + 63) / 64), 64, 0, stream>>>(A, Bm, l_xx, l_uu, l_xu, l_x, l_u, l_xxN,
+                                                                      l_xN, tight, B, T, reg, K, k, v0);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_assembly(const float* K, const float* k, const float* v0, const float* A, const float* Bm,
+                            const float* X, const float* U, const float* x_ref, const float* u_ref, int64_t B,
+                            int T, float* gC, float* gc, float* gx0, float* gxr, float* gur, float* gCf, float* gcf,
+                            cudaStream_t stream) {
+  if (B == 0) return cudaSuccess;
+  fm_assembly_kernel<<<(unsigned)((B + 63) / 64), 64, 0, stream>>>(K, k, v0, A, Bm, X, U, x_ref, u_ref, B, T, gC,
+                                                                   gc, gx0, gxr, gur, gCf, gcf);
+  return cudaGetLastError();
+}
+
 
 size_t solve_ws_bytes(int64_t B, int32_t T, int32_t n_alpha) {
   const size_t slots = (size_t)B * (n_alpha + 1) * (T + 1) * REC * sizeof(float);

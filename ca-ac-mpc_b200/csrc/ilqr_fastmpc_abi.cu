@@ -98,4 +98,39 @@ int ilqr_b200_fastmpc_backward_f32(const float* X, const float* U, const float* 
   return e == cudaSuccess ? ILQR_OK : ILQR_ERR_CUDA;
 }
 
+int ilqr_b200_fastmpc_linearize_f32(const float* X, const float* U, int64_t B, int32_t T, float dt, float* A,
+                                    float* Bm, cudaStream_t stream) {
+  if (B < 0 || T < 1) return ILQR_ERR_INVALID_ARGUMENT;
+  if (B == 0) return ILQR_OK;
+  if (!X || !U || !A || !Bm) return ILQR_ERR_INVALID_ARGUMENT;
+  return ilqr::fm::launch_linearize(X, U, B, T, dt, A, Bm, stream) == cudaSuccess ? ILQR_OK : ILQR_ERR_CUDA;
+}
+
+int ilqr_b200_fastmpc_adjoint_lqr_f32(const float* A, const float* Bm, const float* l_xx, const float* l_uu,
+                                      const float* l_xu, const float* l_x, const float* l_u, const float* l_xxN,
+                                      const float* l_xN, const uint8_t* tight_mask, int64_t B, int32_t T,
+                                      float reg_eps, float* K, float* k, float* v0, cudaStream_t stream) {
+  if (B < 0 || T < 1) return ILQR_ERR_INVALID_ARGUMENT;
+  if (B == 0) return ILQR_OK;
+  if (!A || !Bm || !l_xx || !l_uu || !l_xu || !l_x || !l_u || !l_xxN || !l_xN || !K || !k || !v0)
+    return ILQR_ERR_INVALID_ARGUMENT;
+  return ilqr::fm::launch_adjoint_lqr(A, Bm, l_xx, l_uu, l_xu, l_x, l_u, l_xxN, l_xN, tight_mask, B, T, reg_eps, K, k,
+                                      v0, stream) == cudaSuccess
+             ? ILQR_OK
+             : ILQR_ERR_CUDA;
+}
+
+int ilqr_b200_fastmpc_assembly_f32(const float* K, const float* k, const float* v0, const float* A, const float* Bm,
+                                   const float* X, const float* U, const float* x_ref, const float* u_ref, int64_t B,
+                                   int32_t T, float* grad_C, float* grad_c, float* grad_x0, float* grad_x_ref,
+                                   float* grad_u_ref, float* grad_C_final, float* grad_c_final, cudaStream_t stream) {
+  if (B < 0 || T < 1) return ILQR_ERR_INVALID_ARGUMENT;
+  if (B == 0) return ILQR_OK;
+  if (!K || !k || !v0 || !A || !Bm || !X || !U || !grad_C || !grad_c || !grad_x0) return ILQR_ERR_INVALID_ARGUMENT;
+  return ilqr::fm::launch_assembly(K, k, v0, A, Bm, X, U, x_ref, u_ref, B, T, grad_C, grad_c, grad_x0, grad_x_ref,
+                                   grad_u_ref, grad_C_final, grad_c_final, stream) == cudaSuccess
+             ? ILQR_OK
+             : ILQR_ERR_CUDA;
+}
+
 }  // extern "C"

@@ -282,6 +282,16 @@ size_t backward_ws_bytes(int64_t B, int32_t T);
 void carve_solve(FmSolveParams& p, void* ws);
 cudaError_t launch_solve(FmSolveParams& p, cudaStream_t stream);
 cudaError_t launch_backward(FmBackwardParams& p, cudaStream_t stream);
+cudaError_t launch_linearize(const float* X, const float* U, int64_t B, int T, float dt, float* A, float* Bm,
+                             cudaStream_t stream);
+cudaError_t launch_adjoint_lqr(const float* A, const float* Bm, const float* l_xx, const float* l_uu,
+                               const float* l_xu, const float* l_x, const float* l_u, const float* l_xxN,
+                               const float* l_xN, const uint8_t* tight, int64_t B, int T, float reg, float* K,
+                               float* k, float* v0, cudaStream_t stream);
+cudaError_t launch_assembly(const float* K, const float* k, const float* v0, const float* A, const float* Bm,
+                            const float* X, const float* U, const float* x_ref, const float* u_ref, int64_t B,
+                            int T, float* gC, float* gc, float* gx0, float* gxr, float* gur, float* gCf, float* gcf,
+                            cudaStream_t stream);
 
 }  // namespace fm
 

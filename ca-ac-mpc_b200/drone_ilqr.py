@@ -5,7 +5,9 @@ returns an object with the reference extension's entry points and return
 tuples (cpp/drone_ilqr_ext.cpp:1321-1386). Instead of JIT-compiling a torch
 extension it loads the prebuilt C-ABI library libilqr_b200.so from this
 directory (built in-tree by csrc/build.py). The numerics are the reference's
-DiffMPC ones (DifferentialMPC/controller.py), not FastMPC's.
+DiffMPC ones (DifferentialMPC/controller.py) by default; numerics="fastmpc"
+(or ACMPC_FASTMPC_NUMERICS=fastmpc) gives the reference extension's own: its
+solve, its masked adjoint Riccati and its assembly (cpp/drone_ilqr_ext.cpp).
 
 There is no CPU path: the entry points require CUDA float32 tensors and the
 loader raises if the library is missing.
@@ -24,7 +26,7 @@ try:
 except ImportError:
     import ilqr_native as _nat
 
-_EXT = None
+_EXT = {}
 _CUDA_KERNELS = None
 NX, NU, N = _nat.NX, _nat.NU, _nat.N
 
@@ -47,11 +49,15 @@ def _expand_batch(t: torch.Tensor, B: int, full_dim: int) -> torch.Tensor:
 
 
 class DroneIlqrExt:
-    """Object returned by load_drone_ilqr_ext()."""
+    """Object returned by load_drone_ilqr_ext(); `numerics` is "diffmpc" or
+    "fastmpc"."""
 
     CUDA_GRAPHS_ENABLED = True
 
-    def __init__(self):
+    def __init__(self, numerics: str = "diffmpc"):
+        if numerics not in ("diffmpc", "fastmpc"):
+            raise ValueError(f"numerics must be 'diffmpc' or 'fastmpc', not {numerics!r}")
+        self.numerics = numerics
         _nat.lib()
         self._graphs_enabled = False
         self._graph_debug = False
@@ -79,16 +85,25 @@ class DroneIlqrExt:
         has_bounds = u_min.numel() > 0 and u_max.numel() > 0
         lo = f(u_min.reshape(-1)[:NU]) if has_bounds else None
         hi = f(u_max.reshape(-1)[:NU]) if has_bounds else None
+        l_xx = C_b[..., :NX, :NX].contiguous()
+        l_uu = C_b[..., NX:, NX:].contiguous()
+        l_xu = C_b[..., :NX, NX:].contiguous()
+        l_xxN = C_f[..., :NX, :NX].contiguous()
+        if self.numerics == "fastmpc":
+            # the extension's own loop; A_lin, B_lin where its last Riccati
+            # pass linearised (drone_ilqr_ext.cpp:771-795, 1063)
+            out = _nat.fastmpc_solve(f(x0), f(U_init), C_b, c_b, C_f, c_f, xr, ur, lo, hi, dt=float(dt),
+                                     max_iter=int(max_iter), reg_eps=float(reg_eps),
+                                     converge_tol=float(converge_tol))
+            A_lin, B_lin = _nat.fastmpc_linearize(out["X_lin"], out["U_lin"], float(dt))
+            converged = bool(int(out["batch_info"][0]))
+            return (out["X"], out["U"], l_xx, l_uu, l_xu, l_xxN, A_lin, B_lin, out["tight"].bool(), converged)
         out = _nat.solve(f(x0), f(U_init), C_b, c_b, C_f, c_f, xr, ur, lo, hi, dt=float(dt),
                          max_iter=int(max_iter), reg_eps=float(reg_eps),
                          converge_tol=float(converge_tol), alphas=_alphas_from_env(),
                          want_stats=True)
         X, U = out["X"], out["U"]
         A_lin, B_lin = _nat.linearize(X, U, float(dt))
-        l_xx = C_b[..., :NX, :NX].contiguous()
-        l_uu = C_b[..., NX:, NX:].contiguous()
-        l_xu = C_b[..., :NX, NX:].contiguous()
-        l_xxN = C_f[..., :NX, :NX].contiguous()
         converged = _nat.converged_flag(out["stall_iter"], out["stall_gap"], out["status"],
                                         int(max_iter), float(converge_tol))
         return (X, U, l_xx, l_uu, l_xu, l_xxN, A_lin, B_lin, out["tight"].bool(), converged)
@@ -96,11 +111,15 @@ class DroneIlqrExt:
     # ---- drone_backward_pass_batched (cpp/drone_ilqr_ext.cpp:1066-1177) ------
     def drone_backward_pass_batched(self, A_lin, Bm_lin, l_xx, l_uu, l_xu, l_x, l_u, l_xxN, l_xN,
                                     tight_mask, reg_eps):
-        """Masked adjoint Riccati with DiffMPC semantics; returns (K, k, v0)."""
+        """Masked adjoint Riccati (DiffMPC semantics, or the extension's own
+        with numerics="fastmpc"); returns (K, k, v0)."""
         f = lambda t: t.to(torch.float32).contiguous()
         tm = None
         if isinstance(tight_mask, torch.Tensor) and tight_mask.numel() > 0:
             tm = tight_mask.to(torch.uint8).contiguous()
+        if self.numerics == "fastmpc":
+            return _nat.fastmpc_adjoint_lqr(f(A_lin), f(Bm_lin), f(l_xx), f(l_uu), f(l_xu), f(l_x), f(l_u),
+                                            f(l_xxN), f(l_xN), tm, float(reg_eps))
         return _nat.adjoint_lqr(f(A_lin), f(Bm_lin), f(l_xx), f(l_uu), f(l_xu), f(l_x), f(l_u),
                                 f(l_xxN), f(l_xN), tm, float(reg_eps))
 
@@ -111,6 +130,10 @@ class DroneIlqrExt:
         """Returns (grad_C, grad_c, grad_x0, grad_xref, grad_uref, grad_C_final,
         grad_c_final); skipped outputs are None."""
         f = lambda t: None if t is None else t.to(torch.float32).contiguous()
+        if self.numerics == "fastmpc":
+            return _nat.fastmpc_assembly(f(K_seq), f(k_seq), f(v0), f(A_lin), f(Bm_lin), f(X), f(U), f(x_ref),
+                                         f(u_ref), bool(compute_xref), bool(compute_uref), bool(compute_C_final),
+                                         bool(compute_c_final))
         return _nat.implicit_diff_assembly(f(K_seq), f(k_seq), f(v0), f(A_lin), f(Bm_lin), f(X),
                                            f(U), f(x_ref), f(u_ref), bool(compute_xref),
                                            bool(compute_uref), bool(compute_C_final),
@@ -147,12 +170,15 @@ class DroneIlqrExt:
 
 
 def load_drone_ilqr_ext(*, build_directory: Optional[Path] = None, verbose: bool = False,
-                        force_rebuild: bool = False, with_fused_kernels: bool = True):
-    """Return the solver extension object (loaded once). The keyword arguments
-    of the reference loader are accepted; the library is prebuilt in-tree."""
-    global _EXT
-    if _EXT is not None and not force_rebuild:
-        return _EXT
+                        force_rebuild: bool = False, with_fused_kernels: bool = True,
+                        numerics: Optional[str] = None):
+    """Return the solver extension object (one per numerics, loaded once). The
+    keyword arguments of the reference loader are accepted; the library is
+    prebuilt in-tree. numerics: "diffmpc" (default) or "fastmpc", the default
+    taken from ACMPC_FASTMPC_NUMERICS."""
+    numerics = (numerics or os.environ.get("ACMPC_FASTMPC_NUMERICS", "diffmpc")).strip().lower()
+    if numerics in _EXT and not force_rebuild:
+        return _EXT[numerics]
     if force_rebuild:
         import importlib.util
         spec = importlib.util.spec_from_file_location(
@@ -160,8 +186,8 @@ def load_drone_ilqr_ext(*, build_directory: Optional[Path] = None, verbose: bool
         mod = importlib.util.module_from_spec(spec)
         spec.loader.exec_module(mod)
         mod.build(verbose=verbose)
-    _EXT = DroneIlqrExt()
-    return _EXT
+    _EXT[numerics] = DroneIlqrExt(numerics)
+    return _EXT[numerics]
 
 
 def load_drone_cuda_kernels(*, build_directory: Optional[Path] = None, verbose: bool = False,

@@ -87,6 +87,9 @@ def lib():
                                             + [_P] * 8 + [_P, ctypes.c_size_t, _P], _I32),
             "ilqr_b200_fastmpc_backward_f32": ([_P] * 11 + [_I64, _I32, _F, _F, _I32] + [_P] * 7
                                                + [_P, ctypes.c_size_t, _P], _I32),
+            "ilqr_b200_fastmpc_linearize_f32": ([_P, _P, _I64, _I32, _F, _P, _P, _P], _I32),
+            "ilqr_b200_fastmpc_adjoint_lqr_f32": ([_P] * 10 + [_I64, _I32, _F, _P, _P, _P, _P], _I32),
+            "ilqr_b200_fastmpc_assembly_f32": ([_P] * 9 + [_I64, _I32] + [_P] * 7 + [_P], _I32),
         }
         for name, (argt, rest) in sig.items():
             fn = getattr(L, name)
@@ -110,7 +113,8 @@ EXPORTED_SYMBOLS = (
     "ilqr_b200_rotor13_linearize_f32", "ilqr_b200_solve_tm_f32", "ilqr_b200_backward_tm_f32",
     "ilqr_b200_rotor13_solve_tm_f32", "ilqr_b200_rotor13_backward_tm_f32",
     "ilqr_b200_fastmpc_solve_workspace_size", "ilqr_b200_fastmpc_backward_workspace_size",
-    "ilqr_b200_fastmpc_solve_f32", "ilqr_b200_fastmpc_backward_f32",
+    "ilqr_b200_fastmpc_solve_f32", "ilqr_b200_fastmpc_backward_f32", "ilqr_b200_fastmpc_linearize_f32",
+    "ilqr_b200_fastmpc_adjoint_lqr_f32", "ilqr_b200_fastmpc_assembly_f32",
 )
 
 
@@ -850,4 +854,67 @@ def fastmpc_backward(X, U, X_lin, U_lin, C, grad_X, grad_U, tight=None, C_final=
         _stream(dev))
     _check(st, "ilqr_b200_fastmpc_backward_f32")
     return out
+
+
+def fastmpc_linearize(X, U, dt):
+    """A [B,T,10,10], B [B,T,10,4] of the FastMPC build's Jacobian at (X_t, U_t)."""
+    dev = _cuda_device(X, "X")
+    _device_ok(dev)
+    B, T1, _ = X.shape
+    T = T1 - 1
+    _req(X, "X", (B, T + 1, NX), dev)
+    _req(U, "U", (B, T, NU), dev)
+    A = torch.empty(B, T, NX, NX, device=dev)
+    Bm = torch.empty(B, T, NX, NU, device=dev)
+    _check(lib().ilqr_b200_fastmpc_linearize_f32(_ptr(X), _ptr(U), B, T, float(dt), _ptr(A), _ptr(Bm), _stream(dev)),
+           "ilqr_b200_fastmpc_linearize_f32")
+    return A, Bm
+
+
+def fastmpc_adjoint_lqr(A, Bm, l_xx, l_uu, l_xu, l_x, l_u, l_xxN, l_xN, tight=None, reg_eps=1e-6):
+    """ext.drone_backward_pass_batched of the FastMPC build: (K, k, v0)."""
+    dev = _cuda_device(A, "A")
+    _device_ok(dev)
+    B, T = A.shape[:2]
+    for t_, nm, sh in ((A, "A", (B, T, NX, NX)), (Bm, "B", (B, T, NX, NU)), (l_xx, "l_xx", (B, T, NX, NX)),
+                       (l_uu, "l_uu", (B, T, NU, NU)), (l_xu, "l_xu", (B, T, NX, NU)), (l_x, "l_x", (B, T, NX)),
+                       (l_u, "l_u", (B, T, NU)), (l_xxN, "l_xxN", (B, NX, NX)), (l_xN, "l_xN", (B, NX))):
+        _req(t_, nm, sh, dev)
+    _opt(tight, "tight_mask", (B, T, NU), dev, torch.uint8)
+    K = torch.empty(B, T, NU, NX, device=dev)
+    k = torch.empty(B, T, NU, device=dev)
+    v0 = torch.empty(B, NX, device=dev)
+    _check(lib().ilqr_b200_fastmpc_adjoint_lqr_f32(
+        _ptr(A), _ptr(Bm), _ptr(l_xx), _ptr(l_uu), _ptr(l_xu), _ptr(l_x), _ptr(l_u), _ptr(l_xxN), _ptr(l_xN),
+        _ptr(tight), B, T, float(reg_eps), _ptr(K), _ptr(k), _ptr(v0), _stream(dev)),
+        "ilqr_b200_fastmpc_adjoint_lqr_f32")
+    return K, k, v0
+
+
+def fastmpc_assembly(K, k, v0, A, Bm, X, U, x_ref=None, u_ref=None, compute_xref=False, compute_uref=False,
+                     compute_C_final=False, compute_c_final=False):
+    """ext.drone_implicit_diff_assembly of the FastMPC build: (grad_C, grad_c,
+    grad_x0, grad_xref, grad_uref, grad_C_final, grad_c_final), None where
+    not requested."""
+    dev = _cuda_device(X, "X")
+    _device_ok(dev)
+    B, T1, _ = X.shape
+    T = T1 - 1
+    for t_, nm, sh in ((K, "K", (B, T, NU, NX)), (k, "k", (B, T, NU)), (v0, "v0", (B, NX)),
+                       (A, "A", (B, T, NX, NX)), (Bm, "B", (B, T, NX, NU)), (X, "X", (B, T + 1, NX)),
+                       (U, "U", (B, T, NU))):
+        _req(t_, nm, sh, dev)
+    _opt(x_ref, "x_ref", (B, T + 1, NX), dev)
+    _opt(u_ref, "u_ref", (B, T, NU), dev)
+    e = lambda *sh: torch.empty(*sh, device=dev)
+    gC, gc, gx0 = e(B, T, N, N), e(B, T, N), e(B, NX)
+    gxr = e(B, T + 1, NX) if compute_xref else None
+    gur = e(B, T, NU) if compute_uref else None
+    gCf = e(B, N, N) if compute_C_final else None
+    gcf = e(B, N) if compute_c_final else None
+    _check(lib().ilqr_b200_fastmpc_assembly_f32(
+        _ptr(K), _ptr(k), _ptr(v0), _ptr(A), _ptr(Bm), _ptr(X), _ptr(U), _ptr(x_ref), _ptr(u_ref), B, T, _ptr(gC),
+        _ptr(gc), _ptr(gx0), _ptr(gxr), _ptr(gur), _ptr(gCf), _ptr(gcf), _stream(dev)),
+        "ilqr_b200_fastmpc_assembly_f32")
+    return gC, gc, gx0, gxr, gur, gCf, gcf
 

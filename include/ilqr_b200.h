@@ -428,6 +428,42 @@ int ilqr_b200_fastmpc_backward_f32(
     float* grad_c_final, float* grad_x_ref, float* grad_u_ref,
     void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
+/*
+ * The reference FastMPC extension's separate entry points with its numerics
+ * (the compatibility surface behind load_drone_ilqr_ext(numerics="fastmpc")).
+ *
+ * A [B,T,10,10], B [B,T,10,4] at (X_t, U_t), t < T: the Jacobian the
+ * extension's drone_ilqr_solve returns as A_lin, B_lin
+ * (drone_kernels.cu:64-190, drone_ilqr_ext.cpp:771-795).
+ */
+int ilqr_b200_fastmpc_linearize_f32(const float* X, const float* U, int64_t B, int32_t T, float dt,
+                                    float* A, float* Bm, cudaStream_t stream);
+
+/*
+ * Replaces ext.drone_backward_pass_batched of the CUDA build
+ * (drone_ilqr_ext.cpp:1066-1123, backward_pass_kernel.cu:617-745): masked
+ * adjoint Riccati on caller-supplied matrices, reg once on Q_uu, a tight
+ * control's row and column zeroed with a 1e-11 diagonal, pivoted-LU gains,
+ * V = Q_xx + Q_xu K. tight_mask may be NULL. Outputs K [B,T,4,10], k [B,T,4],
+ * v0 [B,10].
+ */
+int ilqr_b200_fastmpc_adjoint_lqr_f32(
+    const float* A, const float* Bm, const float* l_xx, const float* l_uu, const float* l_xu,
+    const float* l_x, const float* l_u, const float* l_xxN, const float* l_xN,
+    const uint8_t* tight_mask, int64_t B, int32_t T, float reg_eps,
+    float* K, float* k, float* v0, cudaStream_t stream);
+
+/*
+ * Replaces ext.drone_implicit_diff_assembly (drone_ilqr_ext.cpp:1221-1278,
+ * backward_pass_kernel.cu:1092-1256): grad_x_ref includes t = T. x_ref, u_ref
+ * and grad_x_ref, grad_u_ref, grad_C_final, grad_c_final may be NULL.
+ */
+int ilqr_b200_fastmpc_assembly_f32(
+    const float* K, const float* k, const float* v0, const float* A, const float* Bm,
+    const float* X, const float* U, const float* x_ref, const float* u_ref,
+    int64_t B, int32_t T, float* grad_C, float* grad_c, float* grad_x0, float* grad_x_ref,
+    float* grad_u_ref, float* grad_C_final, float* grad_c_final, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

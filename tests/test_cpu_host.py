@@ -127,6 +127,29 @@ def test_fastmpc_numerics_surface_without_gpu(monkeypatch):
         m(x, mpc_compat.QuadCost(C, None), type("Dx", (), {"dt": 0.05})())
 
 
+def test_extension_numerics_option(monkeypatch):
+    """load_drone_ilqr_ext keeps one extension object per numerics; the
+    default follows ACMPC_FASTMPC_NUMERICS; unknown numerics are refused; the
+    FastMPC compat entry points reject bad sizes before touching the GPU."""
+    import drone_ilqr
+    a = drone_ilqr.load_drone_ilqr_ext(numerics="fastmpc")
+    b = drone_ilqr.load_drone_ilqr_ext(numerics="diffmpc")
+    assert a.numerics == "fastmpc" and b.numerics == "diffmpc" and a is not b
+    assert drone_ilqr.load_drone_ilqr_ext(numerics="fastmpc") is a
+    monkeypatch.setenv("ACMPC_FASTMPC_NUMERICS", "fastmpc")
+    assert drone_ilqr.load_drone_ilqr_ext() is a
+    with pytest.raises(ValueError):
+        drone_ilqr.DroneIlqrExt("mpc.pytorch")
+    L = nat.lib()
+    fake = ctypes.c_void_p(0x10000)
+    assert L.ilqr_b200_fastmpc_linearize_f32(fake, fake, 4, 0, 0.05, fake, fake, None) == 1
+    assert L.ilqr_b200_fastmpc_linearize_f32(None, fake, 4, 5, 0.05, fake, fake, None) == 1
+    assert L.ilqr_b200_fastmpc_adjoint_lqr_f32(*([fake] * 9), None, 4, 5, 1e-6, None, fake, fake, None) == 1
+    assert L.ilqr_b200_fastmpc_assembly_f32(*([fake] * 7), None, None, 4, 5, fake, None, fake, *([None] * 4),
+                                            None) == 1
+    assert L.ilqr_b200_fastmpc_assembly_f32(*([fake] * 7), None, None, 0, 5, *([None] * 7), None) == 0
+
+
 def test_fastmpc_workspace_sizes_and_argument_validation():
     L = nat.lib()
     n = ctypes.c_size_t(0)

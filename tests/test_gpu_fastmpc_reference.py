@@ -139,3 +139,90 @@ def test_pnqp4_batch_matches_reference_kernel():
         assert close.float().mean().item() >= 0.98, close.float().mean().item()
         assert torch.equal(fm[close], rfm[close])
 
+
+
+def _rand_lqr(B, T, seed):
+    rng = np.random.default_rng(seed)
+    A = np.eye(10) + 0.05 * rng.normal(size=(B, T, 10, 10))
+    Bm = 0.1 * rng.normal(size=(B, T, 10, 4))
+    G = rng.normal(size=(B, T, 14, 14)) * 0.3
+    C = G @ np.swapaxes(G, -1, -2) / 14 + np.eye(14) * rng.uniform(0.5, 2.0, (B, T, 14))[..., None]
+    GN = rng.normal(size=(B, 10, 10)) * 0.3
+    f = lambda a: _t(np.asarray(a, np.float32))
+    return dict(A=f(A), B=f(Bm), l_xx=f(C[..., :10, :10]), l_uu=f(C[..., 10:, 10:]), l_xu=f(C[..., :10, 10:]),
+                l_x=f(rng.normal(size=(B, T, 10))), l_u=f(rng.normal(size=(B, T, 4))),
+                l_xxN=f(GN @ np.swapaxes(GN, -1, -2) / 10), l_xN=f(rng.normal(size=(B, 10))),
+                tight=torch.as_tensor(rng.uniform(size=(B, T, 4)) < 0.3, device=DEV))
+
+
+def test_extension_entry_points_match_reference_kernels():
+    """The FastMPC extension surface's separate entry points (Jacobian, masked
+    adjoint Riccati, assembly) against the reference kernels they replace."""
+    import fastmpc_ref
+    B, T = 24, 7
+    rng = np.random.default_rng(3)
+    X = np.zeros((B, T + 1, 10), np.float32)
+    X[..., :3] = rng.normal(size=(B, T + 1, 3))
+    q = rng.normal(size=(B, T + 1, 4))
+    X[..., 3:7] = q / np.linalg.norm(q, axis=-1, keepdims=True)
+    X[..., 7:] = rng.normal(size=(B, T + 1, 3))
+    U = np.concatenate([rng.uniform(0, 30, (B, T, 1)), rng.normal(size=(B, T, 3))], -1).astype(np.float32)
+    Xt, Ut = _t(X), _t(U)
+    A, Bm = nat.fastmpc_linearize(Xt, Ut, 0.05)
+    rA = torch.empty(B * T, 10, 10, device=DEV)
+    rB = torch.empty(B * T, 10, 4, device=DEV)
+    xn = torch.empty(B * T, 10, device=DEV)
+    L = fastmpc_ref.lib()
+    p = fastmpc_ref._p
+    assert L.fmref_step_jacobian(p(Xt[:, :T].reshape(-1, 10).contiguous()), p(Ut.reshape(-1, 4).contiguous()), p(xn),
+                                 p(rA), p(rB), 0.05, B * T, fastmpc_ref._s()) == 0
+    assert torch.allclose(A, rA.view(B, T, 10, 10), rtol=1e-5, atol=1e-6)
+    assert torch.allclose(Bm, rB.view(B, T, 10, 4), rtol=1e-5, atol=1e-6)
+    d = _rand_lqr(B, T, 4)
+    for tight in (None, d["tight"]):
+        K, k, v0 = nat.fastmpc_adjoint_lqr(d["A"], d["B"], d["l_xx"], d["l_uu"], d["l_xu"], d["l_x"], d["l_u"],
+                                           d["l_xxN"], d["l_xN"], None if tight is None else tight.to(torch.uint8))
+        rK, rk, rv = (torch.zeros(B, T, 4, 10, device=DEV), torch.zeros(B, T, 4, device=DEV),
+                      torch.zeros(B, 10, device=DEV))
+        tm = None if tight is None else tight.to(torch.uint8).contiguous()
+        assert L.fmref_riccati(p(d["A"]), p(d["B"]), p(d["l_xx"]), p(d["l_uu"]), p(d["l_xu"]), p(d["l_x"]),
+                               p(d["l_u"]), p(d["l_xxN"]), p(d["l_xN"]), p(tm), 1e-6, B, T, p(rK), p(rk), p(rv),
+                               fastmpc_ref._s()) == 0
+        for a, b_ in ((K, rK), (k, rk), (v0, rv)):
+            assert _rel(a, b_).max() <= 1e-4
+        g = nat.fastmpc_assembly(K, k, v0, d["A"], d["B"], Xt, Ut, None, None, True, True, True, True)
+        z = lambda *s: torch.zeros(*s, device=DEV)
+        rg = [z(B, T, 14, 14), z(B, T, 14), z(B, 10), z(B, T + 1, 10), z(B, T, 4), z(B, 14, 14), z(B, 14)]
+        assert L.fmref_assembly(p(K), p(k), p(v0), p(d["A"]), p(d["B"]), p(Xt), p(Ut), p(z(B, T + 1, 10)),
+                                p(z(B, T, 4)), *[p(r_) for r_ in rg], B, T, fastmpc_ref._s()) == 0
+        for a, b_ in zip(g, rg):
+            assert _rel(a, b_).max() <= 1e-5
+
+
+def test_extension_object_fastmpc_numerics():
+    """load_drone_ilqr_ext(numerics="fastmpc"): drone_ilqr_solve returns the
+    fused solve's X, U, tight mask and the Jacobian at its last linearisation
+    point; the operator-style backward through its separate entry points
+    agrees with the fused backward."""
+    import drone_ilqr
+    d, _, iters = _case("cfg1_b16_t5")
+    B, T = d["U_init"].shape[:2]
+    ext = drone_ilqr.load_drone_ilqr_ext(numerics="fastmpc")
+    assert ext.numerics == "fastmpc" and drone_ilqr.load_drone_ilqr_ext().numerics == "diffmpc"
+    z = lambda *s: torch.zeros(*s, device=DEV)
+    res = ext.drone_ilqr_solve(_t(d["x0"]), _t(d["U_init"]), _t(d["C"]), _t(d["c"]), z(B, 14, 14), z(B, 14),
+                               z(B, T + 1, 10), z(B, T, 4), _t(LO), _t(HI), 0.05, iters, 1e-6, 1e-6)
+    X, U, l_xx, l_uu, l_xu, l_xxN, A_lin, B_lin, tight, converged = res
+    o = nat.fastmpc_solve(_t(d["x0"]), _t(d["U_init"]), _t(d["C"]), _t(d["c"]), u_min=_t(LO), u_max=_t(HI),
+                          dt=0.05, max_iter=iters)
+    assert torch.equal(X, o["X"]) and torch.equal(U, o["U"]) and torch.equal(tight, o["tight"].bool())
+    A2, B2 = nat.fastmpc_linearize(o["X_lin"], o["U_lin"], 0.05)
+    assert torch.equal(A_lin, A2) and torch.equal(B_lin, B2)
+    assert converged == bool(int(o["batch_info"][0]))
+    gX, gU = (_t(a) for a in wl.make_backward_seeds(B, T))
+    K, k, v0 = ext.drone_backward_pass_batched(A_lin, B_lin, l_xx, l_uu, l_xu, -gX[:, :T], -gU, l_xxN, -gX[:, -1],
+                                               tight, 1e-6)
+    gC, gc, gx0, *_ = ext.drone_implicit_diff_assembly(K, k, v0, A_lin, B_lin, X, U, z(B, T + 1, 10), z(B, T, 4))
+    g = nat.fastmpc_backward(o["X"], o["U"], o["X_lin"], o["U_lin"], _t(d["C"]), gX, gU, tight=o["tight"], dt=0.05)
+    for a, b_ in ((gx0, g["x0"]), (gC, g["C"]), (gc, g["c"])):
+        assert _rel(a, b_).max() <= 1e-5
