@@ -71,13 +71,43 @@ class Clocks:
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
+    # NVML clocks-event reason bits: sw_power_cap, hw_slowdown,
+    # sw_thermal_slowdown, hw_thermal_slowdown (nvml.h)
+    NVML_BITS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+                 ("sw_power_cap", 0x4))
+
+    def __init__(self, index: int, pci=None):
         self.index = index
         self.samples = []
         self._stop = threading.Event()
         self._t = None
+        self._nvml = None
+        if pci is not None:
+            try:  # read-only NVML queries, every 2 ms: several samples even in a short timed region
+                import pynvml
+                pynvml.nvmlInit()
+                self._nvml = (pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(pci))
+            except Exception:
+                self._nvml = None
+
+    def _run_nvml(self):
+        nv, h = self._nvml
+        reasons_fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                r = reasons_fn(h)
+                self.samples.append([str(self.index), str(sm), str(mx), "", ""]
+                                    + ["Active" if r & bit else "Not Active" for _, bit in self.NVML_BITS])
+            except Exception:
+                pass
+            self._stop.wait(0.002)
 
     def _run(self):
+        if self._nvml is not None:
+            return self._run_nvml()
         while not self._stop.is_set():
             try:
                 out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
@@ -108,7 +138,7 @@ class Clocks:
                           if len(s) > 5 + i and s[5 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(self.samples)}
+                "samples": len(self.samples), "source": "nvml" if self._nvml is not None else "nvidia-smi"}
 
 
 # ---------------------------------------------------------------------------
@@ -236,6 +266,15 @@ def time_streaming(torch, dev, stream, host, compute, warm, steps, barrier):
     return e0.elapsed_time(e1) * 1e-3
 
 
+def gpu_pci_bus_id(torch, dev_index):
+    """NVML PCI bus id of a CUDA device (None if torch does not report it)."""
+    try:
+        pr = torch.cuda.get_device_properties(dev_index)
+        return f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+    except Exception:
+        return None
+
+
 def bind_to_gpu_numa_node(torch, dev_index):
     """Pin this process to the host CPUs NVML reports as local to its GPU, so
     the pinned host buffers of the end-to-end measurement are allocated and
@@ -321,7 +360,7 @@ def run_ours(args):
     barrier()
     timings = [(ev(), ev(), ev()) for _ in range(args.steps)]
     t_start, t_end = ev(), ev()
-    with Clocks(local) as clk:
+    with Clocks(local, gpu_pci_bus_id(torch, dev.index)) as clk:
         barrier()
         t_start.record(stream)
         for i in range(args.steps):
