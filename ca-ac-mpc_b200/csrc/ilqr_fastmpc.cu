@@ -1309,6 +1309,13 @@ void carve_solve(FmSolveParams& p, void* ws) {
   p.state.imp = p.state.best + p.B;
 }
 
+// One solve segment in the register tier chosen by the caller.
+template <bool BOUNDED, int LPC>
+void launch_segment(const FmSolveParams& p, unsigned grid, bool fat, int it0, int it1, cudaStream_t stream) {
+  if (fat) fm_solve_kernel<BOUNDED, LPC, 2><<<grid, THREADS, 0, stream>>>(p, it0, it1);
+  else fm_solve_kernel<BOUNDED, LPC, 3><<<grid, THREADS, 0, stream>>>(p, it0, it1);
+}
+
 cudaError_t launch_solve(FmSolveParams& p, cudaStream_t stream) {
   cudaError_t e = cudaMemsetAsync(p.flags, 0, 256, stream);
   if (e != cudaSuccess || p.B == 0) return e;
@@ -1323,17 +1330,13 @@ cudaError_t launch_solve(FmSolveParams& p, cudaStream_t stream) {
     // 1.01 ms at 4 CTAs per SM); larger grids the 3-CTA tier (B = 16384: 5.35
     // ms, against 5.45 ms at 4 and 6.22 ms at 2)
     const bool fat = grid <= 2u * SM_COUNT_FM;
-#define FM_LAUNCH(BD, L)                                                          \
-  (fat ? (fm_solve_kernel<BD, L, 2><<<grid, THREADS, 0, stream>>>(p, it0, it1), 0) \
-       : (fm_solve_kernel<BD, L, 3><<<grid, THREADS, 0, stream>>>(p, it0, it1), 0))
     if (bounded) {
-      if (wide) FM_LAUNCH(true, 4);
-      else FM_LAUNCH(true, 2);
+      if (wide) launch_segment<true, 4>(p, grid, fat, it0, it1, stream);
+      else launch_segment<true, 2>(p, grid, fat, it0, it1, stream);
     } else {
-      if (wide) FM_LAUNCH(false, 4);
-      else FM_LAUNCH(false, 2);
+      if (wide) launch_segment<false, 4>(p, grid, fat, it0, it1, stream);
+      else launch_segment<false, 2>(p, grid, fat, it0, it1, stream);
     }
-#undef FM_LAUNCH
     if (p.max_iter > 0) fm_check_kernel<<<1, 1024, 0, stream>>>(p, it1);
   }
   const unsigned fgrid = (unsigned)((p.B + 7) / 8);
