@@ -254,3 +254,17 @@ def test_fastmpc_nonfinite_element_is_isolated():
     r = _oracle_replay(d, o, g)
     for k in ("X", "U"):
         assert _rel(g[k][others], r[k][others]).max() <= TOL_XU, k
+
+
+@pytest.mark.parametrize("alphas", [(1.0,), (1.0, 0.7, 0.5, 0.3, 0.2, 0.1), (1.0, 0.9, 0.8, 0.6, 0.4, 0.3, 0.2, 0.1)])
+def test_fastmpc_step_size_counts(alphas):
+    """One step size, and more than four (two lanes per candidate instead of
+    four): the replayed oracle agrees as for the reference grid."""
+    d, o = _case("cfg2_b64_t10")
+    g = _np(nat.fastmpc_solve(_t(d["x0"]), _t(d["U_init"]), _t(d["C"]), _t(d["c"]), u_min=_t(LO), u_max=_t(HI),
+                              dt=0.05, max_iter=6, alphas=alphas, want_trace=True))
+    r = O.fm_solve(d["x0"], d["U_init"], d["C"], d["c"], u_min=LO, u_max=HI, dt=0.05, max_iter=6, alphas=alphas,
+                   forced=g["trace"].astype(np.int64), forced_stop=int(g["batch_info"][1]))
+    for k in ("X", "U", "X_lin", "U_lin"):
+        assert _rel(g[k], r[k]).max() <= TOL_XU, k
+    assert g["trace"].max() < len(alphas)
