@@ -216,6 +216,35 @@ class SigmoidQuadCost(NamedTuple):
         return _nat.SigmoidCostSpec(self.eps, self.range_q, self.range_p, self.mass, self.range_pt)
 
 
+def _sigmoid_index(T: int, device) -> Tensor:
+    """[T, 14] positions in x_q / x_p of each tau entry: _build_cost_tensors
+    (training_modules/mlp_mpc_policy_diffmpc.py:204-243) slices the sigmoid
+    output into blocks of T steps, p (3), q (4), v (3), w (3), thrust (1), and
+    lists them in tau order p, q, v, thrust, w."""
+    t = torch.arange(T, device=device)
+    cols = [3 * t + i for i in range(3)] + [3 * T + 4 * t + i for i in range(4)]
+    cols += [7 * T + 3 * t + i for i in range(3)] + [13 * T + t] + [10 * T + 3 * t + i for i in range(3)]
+    return torch.stack(cols, dim=1)
+
+
+def _sigmoid_to_dense_tm(sc: Tensor, T: int, spec) -> tuple:
+    """Dense time-major C [T,B,14,14] (diagonal) and c [T,B,14] from the
+    policy's sigmoid output [B, 28 T], differentiable, with
+    _build_cost_tensors' operations (mlp_mpc_policy_diffmpc.py:194-247):
+    x_q = s * range_q + eps on the diagonal, c = (x_p - 0.5) * range_p, and
+    for the thrust entry c = -(x_p * range_pt + eps). For the FastMPC numerics
+    mode, whose kernels read dense costs."""
+    idx = _sigmoid_index(T, sc.device)
+    x_q = sc[:, :14 * T] * spec.range_q + spec.eps
+    x_p = sc[:, 14 * T:]
+    xp = x_p[:, idx]
+    c = (xp - 0.5) * spec.range_p
+    c_thrust = -(xp[..., 10] * spec.range_pt + spec.eps)
+    c = torch.cat([c[..., :10], c_thrust.unsqueeze(-1), c[..., 11:]], dim=-1)
+    C = torch.diag_embed(x_q[:, idx])
+    return C.transpose(0, 1).contiguous(), c.transpose(0, 1).contiguous()
+
+
 class SigmoidMPCFunction(torch.autograd.Function):
     """DroneMPCFunction for SigmoidQuadCost: forward(x0 [B,10],
     sigmoid_cost [B,28T], solver_cfg) -> (X, U); backward returns the
@@ -294,8 +323,8 @@ class FastMPC(nn.Module):
     n_state selects the model: 10 is the reference's CTBR quadrotor, 13 the
     rotor-thrust rigid body (four rotor thrusts in [0, 1]; dense QuadCost only).
     numerics: "diffmpc" (default) or "fastmpc" (the reference FastMPC build's
-    own numerics; 10-state model, dense QuadCost; ACMPC_FASTMPC_NUMERICS sets
-    the default).
+    own numerics; 10-state model; a SigmoidQuadCost is turned into the dense
+    costs the policy would build; ACMPC_FASTMPC_NUMERICS sets the default).
     """
 
     def __init__(self, n_state: int, n_ctrl: int, T: int, u_lower: Optional[Tensor] = None,
@@ -370,8 +399,11 @@ class FastMPC(nn.Module):
         if sigm and r13:
             raise ValueError("SigmoidQuadCost builds the 10-state policy's costs; use QuadCost with n_state=13")
         if sigm and self.numerics == "fastmpc":
-            raise ValueError("the FastMPC numerics mode takes QuadCost")
-        if not sigm:
+            # the FastMPC kernels read dense costs: build the policy's C, c on
+            # the device (autograd carries the gradient back to the sigmoid output)
+            C_tb, c_tb = _sigmoid_to_dense_tm(cost.sigmoid_cost.to(torch.float32), T, cost.spec())
+            sigm = False
+        elif not sigm:
             C_tb, c_tb = _normalize_cost_tm(cost.C, cost.c, B, T, n, device, dtype)
         u_min, u_max = self._get_bounds(device, dtype)
         U_init = _normalize_init(self.u_init, B, T, nu, device, dtype, nx)

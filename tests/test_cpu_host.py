@@ -107,7 +107,8 @@ def test_rotor13_surface_without_gpu():
 def test_fastmpc_numerics_surface_without_gpu(monkeypatch):
     """numerics="fastmpc" (or ACMPC_FASTMPC_NUMERICS) selects the reference
     FastMPC build's numerics: its step sizes by default, the 10-state model
-    only, QuadCost only, and no CPU path."""
+    only, and no CPU path; SigmoidQuadCost is turned into the policy's dense
+    costs (bit for bit the policy's construction)."""
     B, T = 2, 3
     m = mpc_compat.FastMPC(10, 4, T, lqr_iter=2, numerics="fastmpc")
     assert m.numerics == "fastmpc" and m._alphas() == nat.FASTMPC_ALPHAS == (1.0, 0.5, 0.25, 0.1)
@@ -120,11 +121,14 @@ def test_fastmpc_numerics_surface_without_gpu(monkeypatch):
         mpc_compat.FastMPC(10, 4, T, numerics="mpc.pytorch")
     x = torch.zeros(B, 10)
     x[:, 3] = 1
-    with pytest.raises(ValueError):
-        m(x, mpc_compat.SigmoidQuadCost(torch.zeros(B, 28 * T)), type("Dx", (), {"dt": 0.05})())
     C = torch.eye(14).expand(T, B, 14, 14)
     with pytest.raises(RuntimeError, match="CUDA"):
         m(x, mpc_compat.QuadCost(C, None), type("Dx", (), {"dt": 0.05})())
+    rng = np.random.default_rng(0)
+    sc = rng.uniform(size=(B, 28 * T)).astype(np.float32)
+    Ct, ct = mpc_compat._sigmoid_to_dense_tm(torch.from_numpy(sc), T, nat.SigmoidCostSpec())
+    Cr, cr = O.sigmoid_costs(sc, T)
+    assert np.array_equal(Ct.transpose(0, 1).numpy(), Cr) and np.array_equal(ct.transpose(0, 1).numpy(), cr)
 
 
 def test_extension_numerics_option(monkeypatch):

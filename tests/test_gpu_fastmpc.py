@@ -268,3 +268,30 @@ def test_fastmpc_step_size_counts(alphas):
     for k in ("X", "U", "X_lin", "U_lin"):
         assert _rel(g[k], r[k]).max() <= TOL_XU, k
     assert g["trace"].max() < len(alphas)
+
+
+def test_fastmpc_operator_takes_sigmoid_costs():
+    """MPC(..., numerics="fastmpc") with SigmoidQuadCost solves the dense costs
+    the policy would build, and autograd returns their gradient carried back
+    through the construction to the sigmoid output."""
+    import mpc_compat
+    B, T = 16, 5
+    d = wl.make_inputs(B, T, seed=7)
+    sc = np.random.default_rng(8).uniform(0.0, 1e-3, (B, 28 * T)).astype(np.float32)
+    C, c = O.sigmoid_costs(sc, T)
+    lo = _t(LO).view(1, 1, 4).expand(T, B, 4)
+    hi = _t(HI).view(1, 1, 4).expand(T, B, 4)
+    m = mpc_compat.MPC(10, 4, T, u_lower=lo, u_upper=hi, lqr_iter=6, numerics="fastmpc")
+    dx = type("Dx", (), {"dt": 0.05})()
+    gX, gU = (_t(a) for a in wl.make_backward_seeds(B, T))
+    s = _t(sc).requires_grad_(True)
+    X, U, _ = m(_t(d["x0"]), mpc_compat.SigmoidQuadCost(s), dx)
+    ((X * gX.transpose(0, 1)).sum() + (U * gU.transpose(0, 1)).sum()).backward()
+    Cd = _t(C).transpose(0, 1).contiguous().requires_grad_(True)
+    cd = _t(c).transpose(0, 1).contiguous().requires_grad_(True)
+    X2, U2, _ = m(_t(d["x0"]), mpc_compat.QuadCost(Cd, cd), dx)
+    ((X2 * gX.transpose(0, 1)).sum() + (U2 * gU.transpose(0, 1)).sum()).backward()
+    assert torch.equal(X, X2) and torch.equal(U, U2)
+    want = O.sigmoid_cost_grad(Cd.grad.transpose(0, 1).cpu().numpy(), cd.grad.transpose(0, 1).cpu().numpy(), T)
+    got = s.grad.cpu().numpy()
+    assert np.allclose(got, want, rtol=1e-6, atol=1e-6 * np.abs(want).max())
