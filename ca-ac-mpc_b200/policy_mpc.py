@@ -36,12 +36,13 @@ class PolicyMPC:
 
     Constants follow DroneDx (drone.py:166-203): mass, thrust_max per rotor,
     omega_max; the control box is [4 thrust_min, -omega_max] ..
-    [4 thrust_max, omega_max] (mlp_mpc_policy_diffmpc.py:166-177)."""
+    [4 thrust_max, omega_max] (mlp_mpc_policy_diffmpc.py:166-177). numerics:
+    as FastMPC's ("diffmpc" by default, or "fastmpc")."""
 
     def __init__(self, T: int, dt: float, lqr_iter: Optional[int] = None, eps: float = 0.1,
                  alphas=None, mass: float = 0.752, thrust_min: float = 0.0, thrust_max: float = 8.5,
                  omega_max=(10.0, 10.0, 4.0), grad_mode: str = "diff", chunk: Optional[int] = None,
-                 device=None):
+                 device=None, numerics: Optional[str] = None):
         self.T = int(T)
         self.dt = float(dt)
         self.lqr_iter = int(os.environ.get("ACMPC_MPC_MAX_ITER", "1")) if lqr_iter is None else int(lqr_iter)
@@ -57,7 +58,7 @@ class PolicyMPC:
         hi = torch.tensor([4.0 * thrust_max, omega_max[0], omega_max[1], omega_max[2]], device=self.device)
         self.solver = mpc_compat.FastMPC(10, 4, self.T, u_lower=lo.view(1, 1, 4).expand(self.T, 1, 4),
                                          u_upper=hi.view(1, 1, 4).expand(self.T, 1, 4),
-                                         lqr_iter=self.lqr_iter, eps=self.eps, alphas=alphas)
+                                         lqr_iter=self.lqr_iter, eps=self.eps, alphas=alphas, numerics=numerics)
         self._dx = type("Dx", (), {"dt": self.dt})()
         self.u_prev: Optional[Tensor] = None
         self.predictions: Optional[Tensor] = None

@@ -17,7 +17,7 @@ DEV = "cuda:0"
 T, DT, MASS = 10, 0.05, 0.752
 
 
-def _reference_loop(sc, states, u_prev, chunk, lqr_iter, eps):
+def _reference_loop(sc, states, u_prev, chunk, lqr_iter, eps, numerics=None):
     """forward_actor's loop: per chunk, dense C, c from the sigmoid output,
     U_init from the warm start (or hover), FastMPC solve; then the warm start
     update and the action normalisation."""
@@ -25,7 +25,8 @@ def _reference_loop(sc, states, u_prev, chunk, lqr_iter, eps):
     lo = torch.tensor([0.0, -10.0, -10.0, -4.0], device=DEV)
     hi = torch.tensor([34.0, 10.0, 10.0, 4.0], device=DEV)
     mpc = mpc_compat.FastMPC(10, 4, T, u_lower=lo.view(1, 1, 4).expand(T, 1, 4),
-                             u_upper=hi.view(1, 1, 4).expand(T, 1, 4), lqr_iter=lqr_iter, eps=eps)
+                             u_upper=hi.view(1, 1, 4).expand(T, 1, 4), lqr_iter=lqr_iter, eps=eps,
+                             numerics=numerics)
     dx = type("Dx", (), {"dt": DT})()
     nom_u = torch.zeros(B, T, 4, device=DEV)
     naninf = 0
@@ -82,3 +83,24 @@ def test_actor_gradient_reaches_the_policy_output():
     pm_stop = policy_mpc.PolicyMPC(T, DT, lqr_iter=2, eps=0.1, grad_mode="stop", device=DEV)
     act2 = pm_stop.actor(sc, states)
     assert not act2.requires_grad
+
+
+def test_actor_fastmpc_numerics_matches_chunked_loop():
+    """PolicyMPC(numerics="fastmpc"): with fewer than four iterations the batch
+    stop is never read early, so the elements are independent and the one-call
+    actor equals the chunked loop on the FastMPC numerics."""
+    B = 21
+    rng = np.random.default_rng(9)
+    inp = wl.make_inputs(B, T, seed=10)
+    states = torch.from_numpy(inp["x0"]).to(DEV)
+    pm = policy_mpc.PolicyMPC(T, DT, lqr_iter=3, eps=0.1, chunk=8, device=DEV, numerics="fastmpc")
+    assert pm.solver.numerics == "fastmpc"
+    sc = torch.from_numpy((1 / (1 + np.exp(-rng.normal(0, 1.5, (B, 28 * T))))).astype(np.float32)).to(DEV)
+    u_prev = torch.zeros(B, 4, device=DEV)
+    u_prev[:, 0] = MASS * 9.8066
+    with torch.no_grad():
+        act = pm.actor(sc, states)
+    ref_act, ref_u_prev, _ = _reference_loop(sc, states, u_prev, 8, 3, 0.1, numerics="fastmpc")
+    assert torch.equal(act, ref_act)
+    assert torch.equal(pm.u_prev, ref_u_prev)
+
