@@ -80,6 +80,7 @@ class Clocks:
         self.index = index
         self.samples = []
         self._stop = threading.Event()
+        self._first = threading.Event()
         self._t = None
         self._nvml = None
         if pci is not None:
@@ -90,19 +91,23 @@ class Clocks:
             except Exception:
                 self._nvml = None
 
-    def _run_nvml(self):
+    def _sample_nvml(self):
         nv, h = self._nvml
-        reasons_fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
-            nv.nvmlDeviceGetCurrentClocksThrottleReasons
-        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        try:
+            reasons_fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+            r = reasons_fn(h)
+            self.samples.append([str(self.index), str(sm), str(mx), "", ""]
+                                + ["Active" if r & bit else "Not Active" for _, bit in self.NVML_BITS])
+        except Exception:
+            pass
+
+    def _run_nvml(self):
         while not self._stop.is_set():
-            try:
-                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
-                r = reasons_fn(h)
-                self.samples.append([str(self.index), str(sm), str(mx), "", ""]
-                                    + ["Active" if r & bit else "Not Active" for _, bit in self.NVML_BITS])
-            except Exception:
-                pass
+            self._sample_nvml()
+            self._first.set()
             self._stop.wait(0.002)
 
     def _run(self):
@@ -117,14 +122,20 @@ class Clocks:
                     self.samples.append([x.strip() for x in out.split(",")])
             except Exception:
                 pass
+            self._first.set()
             self._stop.wait(0.2)
 
     def __enter__(self):
+        # the first sample is taken before the timed region opens and a last
+        # one when it closes, so even a region of a few milliseconds has two
         self._t = threading.Thread(target=self._run, daemon=True)
         self._t.start()
+        self._first.wait(6.0)
         return self
 
     def __exit__(self, *a):
+        if self._nvml is not None:
+            self._sample_nvml()
         self._stop.set()
         self._t.join(timeout=10)
 
