@@ -1,0 +1,92 @@
+"""Pin the FastMPC oracle to the reference FastMPC extension's CUDA build:
+golden vectors made by running the reference's own kernels
+(tests/golden/make_fastmpc_golden.py). CPU only.
+
+With the reference's recorded decisions and batch stop replayed, the oracle's
+X and U agree to 1e-5 (relative to the element's largest magnitude), its tight
+mask exactly and its gradients of x0, C, c to 1e-4: a tenth of the device
+kernels' parity bars (1e-4, 1e-3). The reference kernels are built with fast
+math (FMA contraction, approximate division and square root), the oracle in
+plain fp32 numpy, so the bars are tolerances, not bit identity. Free-running,
+every decision where the oracle parts from the reference is a near-tie in the
+reference's own candidate costs.
+"""
+
+import glob
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+CASES = sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "fm_ref_*.npz")))
+
+pytestmark = pytest.mark.skipif(not CASES, reason="no FastMPC golden fixtures")
+
+
+def _load(name):
+    return dict(np.load(os.path.join(GOLDEN, name + ".npz")))
+
+
+def _rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    ax = tuple(range(1, a.ndim))
+    scale = np.maximum(np.abs(b).max(axis=ax, keepdims=True), 1.0)
+    return (np.abs(a - b) / scale).max(axis=ax)
+
+
+def _solve(d, **kw):
+    box = dict(u_min=d["u_min"], u_max=d["u_max"]) if bool(d["boxed"]) else {}
+    return O.fm_solve(d["x0"], d["U_init"], d["C"], d["c"], dt=float(d["dt"]), max_iter=int(d["max_iter"]),
+                      **box, **kw)
+
+
+def test_fixture_set_complete():
+    assert len(CASES) == 6, CASES
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_oracle_replay_matches_reference_kernels(name):
+    d = _load(name)
+    r = _solve(d, forced=d["ref_trace"], forced_stop=int(d["ref_iters"]))
+    assert r["iters_run"] == int(d["ref_iters"])
+    assert r["converged"] == bool(d["ref_converged"])
+    for k in ("X", "U"):
+        err = _rel(r[k], d["ref_" + k])
+        assert err.max() <= 1e-5, (k, float(err.max()), int(err.argmax()))
+    assert np.array_equal(r["tight"], d["ref_tight"])
+    g = O.fm_backward(r["X"], r["U"], r["X_lin"], r["U_lin"], d["C"], d["gX"], d["gU"], r["tight"],
+                      dt=float(d["dt"]))
+    for k in ("x0", "C", "c"):
+        err = _rel(g[k], d["ref_" + k])
+        assert err.max() <= 1e-4, (k, float(err.max()), int(err.argmax()))
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_oracle_free_run_parts_from_reference_only_at_ties(name):
+    d = _load(name)
+    r = _solve(d)
+    n = min(r["iters_run"], int(d["ref_iters"]))
+    to, tr = r["trace"][:, :n], d["ref_trace"][:, :n].astype(np.int64)
+    costs = d["ref_costs"][:, :n].astype(np.float64)
+    best = d["ref_best_before"][:, :n].astype(np.float64)
+    err = _rel(r["U"], d["ref_U"])
+    for b in range(to.shape[0]):
+        diff = np.nonzero(to[b] != tr[b])[0]
+        if diff.size == 0:
+            if r["iters_run"] == int(d["ref_iters"]):
+                assert err[b] <= 1e-4, (b, err[b])
+            continue
+        i = diff[0]
+        c = costs[b, i]
+        scale = max(np.abs(c).max(), abs(best[b, i]), 1e-30)
+        jo, jr = to[b, i], tr[b, i]
+        if jo >= 0 and jr >= 0:
+            gap = abs(c[jo] - c[jr])
+        else:
+            j = jo if jo >= 0 else jr
+            gap = abs(c[j] - best[b, i]) if j >= 0 else abs(c[-jo - 1] - c[-jr - 1])
+        assert gap <= 1e-5 * scale, (b, i, jo, jr, gap / scale)
