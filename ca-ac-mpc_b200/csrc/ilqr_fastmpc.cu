@@ -12,7 +12,8 @@
 //   J   A_t, B_t entries from the linearisation point (a 36-entry table, three
 //       per lane, plus the thrust column), cost rows from C
 //   P1  (V A)_i., (V B)_i.
-//   P2  Q_xx,i. = C_xx,i. + A_.i^T (V A); Q_xu,i.; q_x,i; Q_uu,j.; q_u,j
+//   P2  Q_xx,i. = C_xx,i. + A_.i^T (V A); Q_xu,i.; q_x,i; q_u,j on lane
+//       10 + j; Q_uu entry (l / 4, l % 4) on lane l of all 16
 //   P3  every lane solves the step's box QP with PNQP-4 (same inputs, same
 //       answer), masks Q_uu, Q_xu, q_u with its free mask, factors Q_uu by
 //       the reference's pivoted LU and solves its column of K; k likewise
@@ -355,14 +356,20 @@ __device__ __forceinline__ void load_point(const Group& G, const float* rec, con
   G.sync();
 }
 
+// C_uu entry (l / 4, l % 4) of a step's 14x14 cost block, for group lane l.
+__device__ __forceinline__ float quu_entry(const float* __restrict__ cs, int l) {
+  return __ldg(cs + (NXf + (l >> 2)) * Nf + NXf + (l & 3));
+}
+
 // One Riccati step (P1..P4) on the A_t, B_t and Q inputs already set up.
 //   lane i < 10: Vr = V row i, cx = C row i (l_xx row, l_xu row), lxi = l_x,i
-//   lane 10 + j: cu = C_uu row j, luj = l_u,j
+//   lane 10 + j: luj = l_u,j
+//   every lane l: cq = C_uu entry (l / 4, l % 4) (quu_entry)
 // MODE 0: unmasked; 1: PNQP free mask (forward solve); 2: tight mask
 // (adjoint). Outputs K_t, k_t into the gain record and (MODE 1) the free mask.
 template <int MODE>
 __device__ __forceinline__ void riccati_step(const Group& G, float (&Vr)[NXf], const float (&cx)[Nf], float lxi,
-                                            const float (&cu)[NUf], float luj, float reg, const float* umin,
+                                            float cq, float luj, float reg, const float* umin,
                                             const float* umax, const uint8_t* tight_row, float* krec,
                                             float* fm_row) {
   float* sm = G.sm;
@@ -410,18 +417,18 @@ __device__ __forceinline__ void riccati_step(const Group& G, float (&Vr)[NXf], c
     qx = s;
   } else if (urow) {
     const int j = l - NXf;
-#pragma unroll
-    for (int m = 0; m < NUf; ++m) {
-      float s = cu[m];
-#pragma unroll
-      for (int k = 0; k < NXf; ++k) s = fmaf(sm[S_B + k * 4 + j], sm[S_VB + k * 4 + m], s);
-      if (m == j) s = s + reg;
-      sm[S_QUU + j * 4 + m] = s;
-    }
     float s = luj;
 #pragma unroll
     for (int k = 0; k < NXf; ++k) s = fmaf(sm[S_B + k * 4 + j], sm[S_V + k], s);
     sm[S_QU + j] = s;
+  }
+  {  // Q_uu entry (j, m) = (l / 4, l % 4) on every lane: 16 entries, 16 lanes
+    const int j = l >> 2, m = l & 3;
+    float s = cq;
+#pragma unroll
+    for (int k = 0; k < NXf; ++k) s = fmaf(sm[S_B + k * 4 + j], sm[S_VB + k * 4 + m], s);
+    if (m == j) s = s + reg;
+    sm[S_QUU + l] = s;
   }
   G.sync();
   // P3: mask, factor, gains
@@ -713,7 +720,7 @@ __global__ void __launch_bounds__(THREADS, MINB) fm_solve_kernel(FmSolveParams p
       jacobian(G, jtab, p.dt);
       float cx[Nf], cu[NUf], lxi = 0.0f, luj = 0.0f;
       cost_rows(G, Cstep(t), cstep(t), cx, lxi, cu, luj);
-      riccati_step<BOUNDED ? 1 : 0>(G, Vr, cx, lxi, cu, luj, p.reg, p.u_min, p.u_max, nullptr,
+      riccati_step<BOUNDED ? 1 : 0>(G, Vr, cx, lxi, quu_entry(Cstep(t), l), luj, p.reg, p.u_min, p.u_max, nullptr,
                                     kw + (int64_t)t * KREC, BOUNDED ? fmw + t * NUf : nullptr);
     }
     // ---- line search: candidate a on lanes a*LPC .. a*LPC + LPC - 1 ----
@@ -954,21 +961,20 @@ __global__ void __launch_bounds__(THREADS) fm_backward_kernel(FmBackwardParams p
     load_lin(t);
     jacobian(G, jtab, p.dt);
     const float* cs = Cb + (int64_t)t * p.cost_tstride * NN;
-    float cx[Nf], cu[NUf], lxi = 0.0f, luj = 0.0f;
+    float cx[Nf], lxi = 0.0f, luj = 0.0f;
     if (l < NXf) {
 #pragma unroll
       for (int j = 0; j < Nf; ++j) cx[j] = __ldg(cs + l * Nf + j);
       lxi = -gX[t * NXf + l];
     } else if (l < Nf) {
-#pragma unroll
-      for (int m = 0; m < NUf; ++m) cu[m] = __ldg(cs + l * Nf + NXf + m);
       luj = -gU[t * NUf + l - NXf];
     }
+    const float cq = quu_entry(cs, l);
     if (p.tight != nullptr) {
-      riccati_step<2>(G, Vr, cx, lxi, cu, luj, p.reg, nullptr, nullptr, p.tight + (b * (int64_t)T + t) * NUf,
+      riccati_step<2>(G, Vr, cx, lxi, cq, luj, p.reg, nullptr, nullptr, p.tight + (b * (int64_t)T + t) * NUf,
                       kw + (int64_t)t * KREC, nullptr);
     } else {
-      riccati_step<0>(G, Vr, cx, lxi, cu, luj, p.reg, nullptr, nullptr, nullptr, kw + (int64_t)t * KREC, nullptr);
+      riccati_step<0>(G, Vr, cx, lxi, cq, luj, p.reg, nullptr, nullptr, nullptr, kw + (int64_t)t * KREC, nullptr);
     }
   }
   if (p.grad_x0 != nullptr && l < NXf) p.grad_x0[b * NXf + l] = -sm[S_V + l];
