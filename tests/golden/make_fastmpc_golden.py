@@ -42,6 +42,7 @@ def cases():
         ("fm_ref_dense_b8_t6", dict(d, C=dense["C"], c=dense["c"]), True, 6),
         ("fm_ref_nobox_b8_t5", wl.make_inputs(8, 5, seed=5), False, 5),
         ("fm_ref_ragged_b13_t7", wl.make_inputs(13, 7, seed=6, r=15.0), True, 9),
+        ("fm_ref_cfg5_b8_t50", wl.make_inputs(8, 50, seed=7, r=15.0), True, 8),
     ]
 
 

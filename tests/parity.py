@@ -169,3 +169,44 @@ def within_rounding(a, ref32, exact64, spread, tol):
     e32 = rel_per_elem(a, ref32)
     bad = (e64 > np.maximum(tol, SPREAD_FACTOR * spread)) | ((spread <= WELL_CONDITIONED) & (e32 > tol))
     return [(int(b), float(e64[b]), float(e32[b]), float(spread[b])) for b in np.nonzero(bad)[0]]
+
+
+# Long horizons in the FastMPC numerics mode (T = 50): for some elements a
+# 1e-7 relative change of C -- about one ulp -- moves the replayed solution by
+# 1e-4 or more, so two fp32 implementations of the same decisions differ by
+# that much. The bar there is per element: the plain bar, or CONDITION_FACTOR
+# times the oracle's own sensitivity to that noise, whichever is larger.
+CONDITION_NOISE = 1e-7
+CONDITION_FACTOR = 10.0
+
+
+def fm_condition_spread(d, trace, stop, u_min, u_max, dt, max_iter, grad_seeds=None, n=2, seed=0):
+    """Per-element sensitivity of the FastMPC oracle's replayed solution to
+    rounding-sized noise: the largest relative change of X and U (and, given
+    grad_seeds = (dL/dX, dL/dU), of the x0, C, c gradients) over n replays with
+    C scaled entrywise by 1 + CONDITION_NOISE N(0, 1)."""
+    import oracle as O
+    kw = dict(u_min=u_min, u_max=u_max, dt=dt, max_iter=max_iter, forced=trace, forced_stop=stop)
+
+    def run(C):
+        r = O.fm_solve(d["x0"], d["U_init"], C, d["c"], **kw)
+        out = {"X": r["X"], "U": r["U"]}
+        if grad_seeds is not None:
+            tight = r["tight"] if u_min is not None else None
+            g = O.fm_backward(r["X"], r["U"], r["X_lin"], r["U_lin"], C, grad_seeds[0], grad_seeds[1], tight, dt=dt)
+            out.update({k: g[k] for k in ("x0", "C", "c")})
+        return out
+
+    base = run(d["C"])
+    rng = np.random.default_rng(seed)
+    spread = {k: np.zeros(len(d["x0"])) for k in base}
+    for _ in range(n):
+        C = (d["C"] * (1.0 + CONDITION_NOISE * rng.standard_normal(d["C"].shape))).astype(np.float32)
+        p = run(C)
+        for k in base:
+            a = np.asarray(p[k], np.float64)
+            b = np.asarray(base[k], np.float64)
+            ax = tuple(range(1, a.ndim))
+            s = (np.abs(a - b) / np.maximum(np.abs(b).max(axis=ax, keepdims=True), 1.0)).max(axis=ax)
+            spread[k] = np.maximum(spread[k], s)
+    return spread

@@ -54,9 +54,13 @@ def _case(name):
     if name == "ragged_b13_t7":
         d = wl.make_inputs(13, 7, seed=6, r=15.0)
         return d, dict(u_min=LO, u_max=HI, max_iter=9, dt=0.05)
+    if name == "cfg5_b8_t50":
+        d = wl.make_inputs(8, 50, seed=7, r=15.0)
+        return d, dict(u_min=LO, u_max=HI, max_iter=8, dt=0.05)
     raise KeyError(name)
 
 
+# cfg5_b8_t50 (long horizon) is checked against the problem's conditioning instead
 CASES = ["cfg1_b16_t5", "cfg2_b64_t10", "cfg3_b48_t20", "dense_b8_t6", "nobox_b8_t5", "ragged_b13_t7"]
 
 
@@ -126,6 +130,34 @@ def test_fastmpc_backward_matches_oracle(name):
         got = gg[k].cpu().numpy()
         err = _rel(got, r[k])
         assert err.max() <= TOL_GRAD, (k, float(err.max()), int(err.argmax()))
+
+
+def test_long_horizon_within_conditioning():
+    """T = 50, targets at 15 m (28 % of controls tight), 8 iterations. With the
+    decisions replayed, X and U agree with the oracle, and the gradients at each
+    side's solution agree, to the plain bars or to CONDITION_FACTOR times the
+    oracle's own response to 1e-7 noise in C, per element."""
+    from parity import CONDITION_FACTOR, fm_condition_spread
+    d, o = _case("cfg5_b8_t50")
+    sol = _gpu(d, o)
+    g = _np(sol)
+    stop = int(g["batch_info"][1])
+    r = _oracle_replay(d, o, g)
+    B, T = d["U_init"].shape[:2]
+    gX, gU = wl.make_backward_seeds(B, T)
+    sp = fm_condition_spread(d, g["trace"].astype(np.int64), stop, o["u_min"], o["u_max"], o["dt"], o["max_iter"],
+                             grad_seeds=(gX, gU))
+    for k in ("X", "U"):
+        err = _rel(g[k], r[k])
+        bad = np.nonzero(err > np.maximum(TOL_XU, CONDITION_FACTOR * sp[k]))[0]
+        assert bad.size == 0, (k, [(int(b), float(err[b]), float(sp[k][b])) for b in bad])
+    gg = nat.fastmpc_backward(sol["X"], sol["U"], sol["X_lin"], sol["U_lin"], _t(d["C"]), _t(gX), _t(gU),
+                              tight=sol["tight"], dt=o["dt"])
+    rg = O.fm_backward(r["X"], r["U"], r["X_lin"], r["U_lin"], d["C"], gX, gU, r["tight"], dt=o["dt"])
+    for k in ("x0", "C", "c"):
+        err = _rel(gg[k].cpu().numpy(), rg[k])
+        bad = np.nonzero(err > np.maximum(TOL_GRAD, CONDITION_FACTOR * sp[k]))[0]
+        assert bad.size == 0, (k, [(int(b), float(err[b]), float(sp[k][b])) for b in bad])
 
 
 def test_fastmpc_time_major_is_bit_identical():

@@ -53,9 +53,12 @@ def _case(name):
         return wl.make_inputs(8, 5, seed=5), False, 5
     if name == "ragged_b13_t7":
         return wl.make_inputs(13, 7, seed=6, r=15.0), True, 9
+    if name == "cfg5_b8_t50":
+        return wl.make_inputs(8, 50, seed=7, r=15.0), True, 8
     raise KeyError(name)
 
 
+# cfg5_b8_t50 (long horizon) is checked against the problem's conditioning instead
 CASES = ["cfg1_b16_t5", "cfg2_b64_t10", "cfg3_b48_t20", "dense_b8_t6", "nobox_b8_t5", "ragged_b13_t7"]
 
 
@@ -83,6 +86,33 @@ def test_fastmpc_matches_reference_kernels(name):
     for k in ("x0", "C", "c"):
         err = _rel(g[k], rg[k])
         assert err.max() <= 1e-3, (k, float(err.max()), int(err.argmax()))
+
+
+def test_long_horizon_within_conditioning():
+    """T = 50, targets at 15 m, 8 iterations, against the reference kernels
+    replaying the B200 solve's decisions. Per element, X, U and the gradients
+    agree to the plain bars or to CONDITION_FACTOR times the oracle's own
+    response to 1e-7 noise in C, whichever is larger."""
+    from parity import CONDITION_FACTOR, fm_condition_spread
+    d, boxed, iters = _case("cfg5_b8_t50")
+    ours = nat.fastmpc_solve(_t(d["x0"]), _t(d["U_init"]), _t(d["C"]), _t(d["c"]), u_min=_t(LO), u_max=_t(HI),
+                             dt=0.05, max_iter=iters, want_trace=True)
+    run = int(ours["batch_info"][1])
+    r = ref.solve(_t(d["x0"]), _t(d["U_init"]), _t(d["C"]), _t(d["c"]), _t(LO), _t(HI), dt=0.05, max_iter=iters,
+                  forced=ours["trace"].long(), forced_stop=run)
+    assert r["iters"] == run
+    B, T = d["U_init"].shape[:2]
+    gXn, gUn = wl.make_backward_seeds(B, T)
+    sp = fm_condition_spread(d, ours["trace"].long().cpu().numpy(), run, LO, HI, 0.05, iters, grad_seeds=(gXn, gUn))
+    g = nat.fastmpc_backward(ours["X"], ours["U"], ours["X_lin"], ours["U_lin"], _t(d["C"]), _t(gXn), _t(gUn),
+                             tight=ours["tight"], dt=0.05)
+    rg = ref.backward(r, _t(gXn), _t(gUn))
+    pairs = [("X", ours["X"], r["X"], 1e-4), ("U", ours["U"], r["U"], 1e-4)]
+    pairs += [(k, g[k], rg[k], 1e-3) for k in ("x0", "C", "c")]
+    for k, a, b_, tol in pairs:
+        err = _rel(a, b_)
+        bad = np.nonzero(err > np.maximum(tol, CONDITION_FACTOR * sp[k]))[0]
+        assert bad.size == 0, (k, [(int(i), float(err[i]), float(sp[k][i])) for i in bad])
 
 
 @pytest.mark.parametrize("name", ["cfg1_b16_t5", "cfg2_b64_t10", "cfg3_b48_t20"])

@@ -21,9 +21,12 @@ import pytest
 import oracle as O
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
-CASES = sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "fm_ref_*.npz")))
+ALL = sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "fm_ref_*.npz")))
+# the long-horizon case (T = 50) is checked against the problem's conditioning
+LONG = [n for n in ALL if n.endswith("_t50")]
+CASES = [n for n in ALL if n not in LONG]
 
-pytestmark = pytest.mark.skipif(not CASES, reason="no FastMPC golden fixtures")
+pytestmark = pytest.mark.skipif(not ALL, reason="no FastMPC golden fixtures")
 
 
 def _load(name):
@@ -45,7 +48,30 @@ def _solve(d, **kw):
 
 
 def test_fixture_set_complete():
-    assert len(CASES) == 6, CASES
+    assert len(CASES) == 6 and len(LONG) == 1, ALL
+
+
+@pytest.mark.parametrize("name", LONG)
+def test_oracle_long_horizon_within_conditioning(name):
+    """T = 50, targets at 15 m, 8 iterations: with the reference's decisions
+    replayed, X, U and the gradients agree per element to the device bars (1e-4,
+    1e-3) or to CONDITION_FACTOR times the oracle's own response to 1e-7 noise
+    in C, whichever is larger; the tight masks agree exactly."""
+    from parity import CONDITION_FACTOR, fm_condition_spread
+    d = _load(name)
+    stop = int(d["ref_iters"])
+    r = _solve(d, forced=d["ref_trace"], forced_stop=stop)
+    assert r["iters_run"] == stop
+    assert np.array_equal(r["tight"], d["ref_tight"])
+    g = O.fm_backward(r["X"], r["U"], r["X_lin"], r["U_lin"], d["C"], d["gX"], d["gU"], r["tight"],
+                      dt=float(d["dt"]))
+    sp = fm_condition_spread(d, d["ref_trace"].astype(np.int64), stop, d["u_min"], d["u_max"], float(d["dt"]),
+                             int(d["max_iter"]), grad_seeds=(d["gX"], d["gU"]))
+    pairs = [("X", r["X"], 1e-4), ("U", r["U"], 1e-4)] + [(k, g[k], 1e-3) for k in ("x0", "C", "c")]
+    for k, a, tol in pairs:
+        err = _rel(a, d["ref_" + k])
+        bad = np.nonzero(err > np.maximum(tol, CONDITION_FACTOR * sp[k]))[0]
+        assert bad.size == 0, (k, [(int(b), float(err[b]), float(sp[k][b])) for b in bad])
 
 
 @pytest.mark.parametrize("name", CASES)
