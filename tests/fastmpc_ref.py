@@ -15,7 +15,8 @@ around them:
   1066-1123) and drone_implicit_diff_assembly (:1221-1278).
 
 A recorded decision trace can be replayed, as for the oracles. Only the GPU
-parity tests import this module.
+parity tests and the fixture generator tests/golden/make_fastmpc_golden.py
+import this module.
 """
 
 from __future__ import annotations
