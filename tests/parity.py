@@ -180,11 +180,31 @@ CONDITION_NOISE = 1e-7
 CONDITION_FACTOR = 10.0
 
 
+def condition_spread(run, C, measure, n=2, seed=0):
+    """Per-element sensitivity of run(C) -> dict of arrays to rounding-sized
+    noise: the largest measure(perturbed, unperturbed) over n runs with C
+    scaled entrywise by 1 + CONDITION_NOISE N(0, 1)."""
+    base = run(C)
+    rng = np.random.default_rng(seed)
+    spread = {k: np.zeros(len(np.asarray(v))) for k, v in base.items()}
+    for _ in range(n):
+        p = run((C * (1.0 + CONDITION_NOISE * rng.standard_normal(C.shape))).astype(np.float32))
+        for k in base:
+            spread[k] = np.maximum(spread[k], measure(p[k], base[k]))
+    return spread
+
+
+def _rel_floor1(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    ax = tuple(range(1, a.ndim))
+    return (np.abs(a - b) / np.maximum(np.abs(b).max(axis=ax, keepdims=True), 1.0)).max(axis=ax)
+
+
 def fm_condition_spread(d, trace, stop, u_min, u_max, dt, max_iter, grad_seeds=None, n=2, seed=0):
-    """Per-element sensitivity of the FastMPC oracle's replayed solution to
-    rounding-sized noise: the largest relative change of X and U (and, given
-    grad_seeds = (dL/dX, dL/dU), of the x0, C, c gradients) over n replays with
-    C scaled entrywise by 1 + CONDITION_NOISE N(0, 1)."""
+    """condition_spread of the FastMPC oracle's replayed solution: X and U
+    (and, given grad_seeds = (dL/dX, dL/dU), the x0, C, c gradients), measured
+    relative to the element's largest magnitude or 1."""
     import oracle as O
     kw = dict(u_min=u_min, u_max=u_max, dt=dt, max_iter=max_iter, forced=trace, forced_stop=stop)
 
@@ -197,16 +217,20 @@ def fm_condition_spread(d, trace, stop, u_min, u_max, dt, max_iter, grad_seeds=N
             out.update({k: g[k] for k in ("x0", "C", "c")})
         return out
 
-    base = run(d["C"])
-    rng = np.random.default_rng(seed)
-    spread = {k: np.zeros(len(d["x0"])) for k in base}
-    for _ in range(n):
-        C = (d["C"] * (1.0 + CONDITION_NOISE * rng.standard_normal(d["C"].shape))).astype(np.float32)
-        p = run(C)
-        for k in base:
-            a = np.asarray(p[k], np.float64)
-            b = np.asarray(base[k], np.float64)
-            ax = tuple(range(1, a.ndim))
-            s = (np.abs(a - b) / np.maximum(np.abs(b).max(axis=ax, keepdims=True), 1.0)).max(axis=ax)
-            spread[k] = np.maximum(spread[k], s)
-    return spread
+    return condition_spread(run, d["C"], _rel_floor1, n, seed)
+
+
+def diffmpc_condition_spread(d, trace, n=2, seed=0):
+    """condition_spread of the DiffMPC oracle replaying `trace` on a golden
+    case: X, U and the GRAD_KEYS gradients at each replayed solution, measured
+    by rel_per_elem."""
+    import oracle as O
+    kw = case_kwargs(d)
+
+    def run(C):
+        r = O.solve(d["x0"], d["U_init"], C, d["c"], forced=trace, **kw)
+        g = O.backward(r["X"], r["U"], C, kw["C_f"], kw["x_ref"], kw["u_ref"], r["tight"], d["gX"], d["gU"],
+                       kw["dt"], kw["reg"])
+        return dict({"X": r["X"], "U": r["U"]}, **{k: g[k] for k in GRAD_KEYS})
+
+    return condition_spread(run, d["C"], rel_per_elem, n, seed)

@@ -116,6 +116,23 @@ def test_long_horizon_never_improving_elements_exact():
     assert np.array_equal(r["U"][never], d["ref_U"][never])
 
 
+def test_long_horizon_within_conditioning():
+    """T=50, 15 m targets, every element: replaying the reference's decisions,
+    X, U and the gradients at the GPU's solution agree with the reference to
+    the plain bars or to CONDITION_FACTOR times the oracle's own response to
+    1e-7 noise in C, per element."""
+    from parity import CONDITION_FACTOR, diffmpc_condition_spread, rel_per_elem
+    d = load("cfg5_b16_t50")
+    r, kw = gpu_solve(d, forced=d["ref_trace"])
+    gg = gpu_backward(d, r["X"], r["U"], r["tight"], kw)
+    sp = diffmpc_condition_spread(d, d["ref_trace"])
+    pairs = [("X", r["X"], TOL_XU), ("U", r["U"], TOL_XU)] + [(k, gg[k], TOL_GRAD) for k in GRAD_KEYS]
+    for k, a, tol in pairs:
+        err = rel_per_elem(a, d["ref_" + k])
+        bad = np.nonzero(err > np.maximum(tol, CONDITION_FACTOR * sp[k]))[0]
+        assert bad.size == 0, (k, [(int(b), float(err[b]), float(sp[k][b])) for b in bad])
+
+
 def _dx():
     return type("Dx", (), {"dt": wl.DT})()
 

@@ -94,6 +94,24 @@ def test_long_horizon_stress_case():
     assert np.all(free["best_cost"] <= x0c)
 
 
+def test_long_horizon_within_conditioning():
+    """T=50, 15 m targets, every element: with the reference's decisions
+    replayed, the oracle's X, U and gradients agree with the reference to the
+    plain bars or to CONDITION_FACTOR times the oracle's own response to 1e-7
+    noise in C, per element. On the ill-conditioned elements that response is
+    O(1), and the oracle-reference difference is below it."""
+    from parity import CONDITION_FACTOR, diffmpc_condition_spread
+    d = load("cfg5_b16_t50")
+    r, kw = _solve(d, forced=d["ref_trace"])
+    g = _backward(d, r["X"], r["U"], r["tight"], kw)
+    sp = diffmpc_condition_spread(d, d["ref_trace"])
+    pairs = [("X", r["X"], TOL_XU), ("U", r["U"], TOL_XU)] + [(k, g[k], TOL_GRAD) for k in GRAD_KEYS]
+    for k, a, tol in pairs:
+        err = rel_per_elem(a, d["ref_" + k])
+        bad = np.nonzero(err > np.maximum(tol, CONDITION_FACTOR * sp[k]))[0]
+        assert bad.size == 0, (k, [(int(b), float(err[b]), float(sp[k][b])) for b in bad])
+
+
 @pytest.mark.parametrize("name", ["cfg1_b16_t5", "cfg3_b16_t20"])
 def test_per_element_freeze_equals_batch_loop(name):
     """Freezing each element at its first rejection gives the same X, U as
