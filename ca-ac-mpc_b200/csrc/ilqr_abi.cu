@@ -81,13 +81,15 @@ int ilqr_b200_check_device(int device) {
 }
 
 int ilqr_b200_solve_workspace_size(int64_t B, int32_t T, size_t* bytes) {
-  if (bytes == nullptr || B < 0 || T < 1) return ILQR_ERR_INVALID_ARGUMENT;
+  if (bytes == nullptr || B < 0 || B > ILQR_MAX_BATCH || T < 1 || T > ILQR_MAX_HORIZON)
+    return ILQR_ERR_INVALID_ARGUMENT;
   *bytes = (size_t)(ilqr::solve_ws_fields(T) * ilqr::ws_stride(B)) * sizeof(float);
   return ILQR_OK;
 }
 
 int ilqr_b200_backward_workspace_size(int64_t B, int32_t T, size_t* bytes) {
-  if (bytes == nullptr || B < 0 || T < 1) return ILQR_ERR_INVALID_ARGUMENT;
+  if (bytes == nullptr || B < 0 || B > ILQR_MAX_BATCH || T < 1 || T > ILQR_MAX_HORIZON)
+    return ILQR_ERR_INVALID_ARGUMENT;
   *bytes = (size_t)(ilqr::backward_ws_fields(T) * ilqr::ws_stride(B)) * sizeof(float);
   return ILQR_OK;
 }
@@ -122,7 +124,7 @@ int solve_impl(const float* x0, const float* U_init, const float* C, const float
     if (recs * ilqr::ws_stride(B) >= ((int64_t)1 << 32)) return ILQR_ERR_INVALID_ARGUMENT;
   }
   size_t need = 0;
-  ilqr_b200_solve_workspace_size(B, T, &need);
+  if (const int q = ilqr_b200_solve_workspace_size(B, T, &need); q != ILQR_OK) return q;
   if (workspace == nullptr || workspace_bytes < need) return ILQR_ERR_WORKSPACE;
   ilqr::SolveParams p{};
   p.x0 = x0; p.U_init = U_init; p.c = c; p.C_f = C_final; p.c_f = c_final;
@@ -162,7 +164,7 @@ int backward_impl(const float* X, const float* U, const float* C, const float* C
     if (!aligned16(C) || (grad_C != nullptr && !aligned16(grad_C))) return ILQR_ERR_MISALIGNED;
   }
   size_t need = 0;
-  ilqr_b200_backward_workspace_size(B, T, &need);
+  if (const int q = ilqr_b200_backward_workspace_size(B, T, &need); q != ILQR_OK) return q;
   if (workspace == nullptr || workspace_bytes < need) return ILQR_ERR_WORKSPACE;
   ilqr::BackwardParams p{};
   p.X = X; p.U = U; p.C_f = C_final; p.x_ref = x_ref; p.u_ref = u_ref; p.tight = tight_mask;

@@ -20,14 +20,16 @@ void cost_strides(int64_t B, int32_t T, int32_t layout, int64_t& bs, int64_t& ts
 extern "C" {
 
 int ilqr_b200_fastmpc_solve_workspace_size(int64_t B, int32_t T, int32_t n_alpha, size_t* bytes) {
-  if (bytes == nullptr || B < 0 || T < 1 || n_alpha < 1 || n_alpha > ILQR_MAX_ALPHAS)
+  if (bytes == nullptr || B < 0 || B > ILQR_MAX_BATCH || T < 1 || T > ILQR_MAX_HORIZON || n_alpha < 1 ||
+      n_alpha > ILQR_MAX_ALPHAS)
     return ILQR_ERR_INVALID_ARGUMENT;
   *bytes = ilqr::fm::solve_ws_bytes(B, T, n_alpha);
   return ILQR_OK;
 }
 
 int ilqr_b200_fastmpc_backward_workspace_size(int64_t B, int32_t T, size_t* bytes) {
-  if (bytes == nullptr || B < 0 || T < 1) return ILQR_ERR_INVALID_ARGUMENT;
+  if (bytes == nullptr || B < 0 || B > ILQR_MAX_BATCH || T < 1 || T > ILQR_MAX_HORIZON)
+    return ILQR_ERR_INVALID_ARGUMENT;
   *bytes = ilqr::fm::backward_ws_bytes(B, T);
   return ILQR_OK;
 }
@@ -49,7 +51,7 @@ int ilqr_b200_fastmpc_solve_f32(const float* x0, const float* U_init, const floa
   if (B == 0) return ILQR_OK;
   if (!x0 || !U_init || !C || !c || !X || !U) return ILQR_ERR_INVALID_ARGUMENT;
   size_t need = 0;
-  ilqr_b200_fastmpc_solve_workspace_size(B, T, n_alpha, &need);
+  if (const int q = ilqr_b200_fastmpc_solve_workspace_size(B, T, n_alpha, &need); q != ILQR_OK) return q;
   if (workspace == nullptr || workspace_bytes < need) return ILQR_ERR_WORKSPACE;
   if (!aligned16_fm(workspace)) return ILQR_ERR_MISALIGNED;
   ilqr::fm::FmSolveParams p;
@@ -82,7 +84,7 @@ int ilqr_b200_fastmpc_backward_f32(const float* X, const float* U, const float* 
   if (B == 0) return ILQR_OK;
   if (!X || !U || !X_lin || !U_lin || !C || !grad_X || !grad_U) return ILQR_ERR_INVALID_ARGUMENT;
   size_t need = 0;
-  ilqr_b200_fastmpc_backward_workspace_size(B, T, &need);
+  if (const int q = ilqr_b200_fastmpc_backward_workspace_size(B, T, &need); q != ILQR_OK) return q;
   if (workspace == nullptr || workspace_bytes < need) return ILQR_ERR_WORKSPACE;
   if (!aligned16_fm(workspace)) return ILQR_ERR_MISALIGNED;
   ilqr::fm::FmBackwardParams p;

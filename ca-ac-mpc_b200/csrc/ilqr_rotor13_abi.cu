@@ -31,14 +31,16 @@ int r13_backward_impl(const float* X, const float* U, const float* C, const floa
 extern "C" {
 
 int ilqr_b200_rotor13_solve_workspace_size(int64_t B, int32_t T, int32_t n_alpha, size_t* bytes) {
-  if (bytes == nullptr || B < 0 || T < 1 || n_alpha < 1 || n_alpha > ILQR_MAX_ALPHAS)
+  if (bytes == nullptr || B < 0 || B > ILQR_MAX_BATCH || T < 1 || T > ILQR_MAX_HORIZON || n_alpha < 1 ||
+      n_alpha > ILQR_MAX_ALPHAS)
     return ILQR_ERR_INVALID_ARGUMENT;
   *bytes = (size_t)(ilqr::dense_solve_ws_fields(T, n_alpha) * B) * sizeof(float);
   return ILQR_OK;
 }
 
 int ilqr_b200_rotor13_backward_workspace_size(int64_t B, int32_t T, size_t* bytes) {
-  if (bytes == nullptr || B < 0 || T < 1) return ILQR_ERR_INVALID_ARGUMENT;
+  if (bytes == nullptr || B < 0 || B > ILQR_MAX_BATCH || T < 1 || T > ILQR_MAX_HORIZON)
+    return ILQR_ERR_INVALID_ARGUMENT;
   *bytes = (size_t)(ilqr::dense_backward_ws_fields(T) * B) * sizeof(float);
   return ILQR_OK;
 }
@@ -112,7 +114,7 @@ int r13_solve_impl(const float* x0, const float* U_init, const float* C, const f
   if (B == 0) return ILQR_OK;
   if (!x0 || !U_init || !C || !c || !X || !U) return ILQR_ERR_INVALID_ARGUMENT;
   size_t need = 0;
-  ilqr_b200_rotor13_solve_workspace_size(B, T, n_alpha, &need);
+  if (const int q = ilqr_b200_rotor13_solve_workspace_size(B, T, n_alpha, &need); q != ILQR_OK) return q;
   if (workspace == nullptr || workspace_bytes < need) return ILQR_ERR_WORKSPACE;
   if (!aligned16_13(workspace)) return ILQR_ERR_MISALIGNED;
   ilqr::DenseSolveParams p{};
@@ -141,7 +143,7 @@ int r13_backward_impl(const float* X, const float* U, const float* C, const floa
   if (B == 0) return ILQR_OK;
   if (!X || !U || !C || !grad_X || !grad_U) return ILQR_ERR_INVALID_ARGUMENT;
   size_t need = 0;
-  ilqr_b200_rotor13_backward_workspace_size(B, T, &need);
+  if (const int q = ilqr_b200_rotor13_backward_workspace_size(B, T, &need); q != ILQR_OK) return q;
   if (workspace == nullptr || workspace_bytes < need) return ILQR_ERR_WORKSPACE;
   if (!aligned16_13(workspace)) return ILQR_ERR_MISALIGNED;
   ilqr::DenseBackwardParams p{};

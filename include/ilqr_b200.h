@@ -32,6 +32,11 @@ extern "C" {
 #define ILQR_N 14
 #define ILQR_MAX_ALPHAS 8
 #define ILQR_TRACE_NOT_RUN (-128)
+/* Largest batch and horizon any entry point accepts. The workspace-size
+ * queries reject larger ones with ILQR_ERR_INVALID_ARGUMENT before any size
+ * arithmetic, so no byte count can wrap around. */
+#define ILQR_MAX_BATCH ((int64_t)2147483647)
+#define ILQR_MAX_HORIZON 65536
 
 typedef enum {
   ILQR_OK = 0,

@@ -6,7 +6,7 @@ copied) with the CUDA flags its builder gives them (drone_ilqr.py: -O3
 also leave out the file's standalone torch bindings), plus the extern "C" shim
 in oracle/fastmpc_ref/shim.cu.
 
-    python oracle/build_fastmpc_ref.py [reference_root]
+    python oracle/build_fastmpc_ref.py <reference root>
 
 Runs only where the reference tree exists (the build container); the built
 library travels with the repository to the GPU machine, where the parity
@@ -28,7 +28,7 @@ FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "--use_fast_math",
          "-DDRONE_ILQR_USE_PNQP", "-DDRONE_ILQR_USE_CUDA_KERNELS"]
 
 
-def build(reference_root: str = "/root/reference") -> str | None:
+def build(reference_root: str) -> str | None:
     cpp = os.path.join(reference_root, "differentialMPCPerformance", "cpp")
     if not all(os.path.exists(os.path.join(cpp, s)) for s in SOURCES):
         print(f"reference FastMPC sources not found under {cpp}; oracle/_ref not built")
@@ -46,4 +46,6 @@ def build(reference_root: str = "/root/reference") -> str | None:
 
 
 if __name__ == "__main__":
-    print(build(*sys.argv[1:]))
+    if len(sys.argv) != 2:
+        sys.exit("usage: python oracle/build_fastmpc_ref.py <reference root>")
+    print(build(sys.argv[1]))

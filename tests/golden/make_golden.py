@@ -2,7 +2,7 @@
 
 Run in the build container, where the reference source tree is available:
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py --ref <reference root>
 
 It imports the reference's DifferentialMPC package and DroneDx model from
 their source tree (a stand-in module replaces matplotlib, which drone.py
@@ -282,7 +282,7 @@ def make_dynamics(drone):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="root of the reference source tree")
     ap.add_argument("--only", nargs="*")
     args = ap.parse_args()
     drone, DM = import_reference(args.ref)

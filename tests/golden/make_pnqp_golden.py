@@ -5,7 +5,7 @@ mpc.pytorch's pnqp (acmpc_public-master/mpc.pytorch/mpc/pnqp.py:5-84), run
 here on CPU in float64 with more iterations so that its x* is the converged
 optimum (unique: H is positive definite). Writes pnqp4_n256.npz.
 
-Usage: python tests/golden/make_pnqp_golden.py [--ref /root/reference]
+Usage: python tests/golden/make_pnqp_golden.py --ref <reference root>
 """
 import argparse
 import os
@@ -18,7 +18,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="root of the reference source tree")
     args = ap.parse_args()
     sys.path.insert(0, os.path.join(args.ref, "acmpc_public-master", "mpc.pytorch"))
     import torch

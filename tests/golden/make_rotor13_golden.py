@@ -12,7 +12,7 @@ in the reference ("model unpinned by the reference"). The model is the one
 oracle/rotor13_model.py restates in numpy (same expressions, same order).
 
 Run in the build container (it imports the reference from its source tree):
-    python tests/golden/make_rotor13_golden.py [--ref /root/reference]
+    python tests/golden/make_rotor13_golden.py --ref <reference root>
 """
 
 from __future__ import annotations
@@ -165,7 +165,7 @@ def make_dynamics():
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="root of the reference source tree")
     ap.add_argument("--only", nargs="*")
     args = ap.parse_args()
     _, DM = import_reference(args.ref)

@@ -51,6 +51,32 @@ def test_workspace_sizes():
     assert L.ilqr_b200_solve_workspace_size(4, 0, ctypes.byref(n)) == 1
 
 
+def test_size_limits_reject_before_the_byte_count_can_wrap():
+    """B beyond ILQR_MAX_BATCH or T beyond ILQR_MAX_HORIZON is rejected by
+    every workspace query (B = 2^61 at T = 20 would wrap the byte count to
+    0), and so by every entry point that sizes its workspace with them."""
+    L = nat.lib()
+    n = ctypes.c_size_t(12345)
+    big_b, big_t = (1 << 61), 65537
+    assert L.ilqr_b200_solve_workspace_size(2**31 - 1, 20, ctypes.byref(n)) == 0
+    assert n.value > 0
+    for q in (L.ilqr_b200_solve_workspace_size, L.ilqr_b200_backward_workspace_size,
+              L.ilqr_b200_rotor13_backward_workspace_size, L.ilqr_b200_fastmpc_backward_workspace_size):
+        assert q(big_b, 20, ctypes.byref(n)) == 1
+        assert q(2**31, 20, ctypes.byref(n)) == 1
+        assert q(16, big_t, ctypes.byref(n)) == 1
+    for q in (L.ilqr_b200_rotor13_solve_workspace_size, L.ilqr_b200_fastmpc_solve_workspace_size):
+        assert q(big_b, 20, 5, ctypes.byref(n)) == 1
+        assert q(16, big_t, 5, ctypes.byref(n)) == 1
+    # the entry points return that status instead of passing a wrapped size
+    assert L.ilqr_b200_solve_f32(*_solve_args(B=big_b)) == 1
+    f = L.ilqr_b200_solve_f32_noalloc
+    P, I64, I32, F = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_float
+    f.argtypes = [P] * 10 + [I64, I32, F, I32, F, F, P, I32, P] + [P] * 9 + [P]
+    f.restype = I32
+    assert f(*(_solve_args(B=big_b)[:-3] + [None])) == 1
+
+
 def test_rotor13_workspace_sizes():
     """Rotor13 solve: (n_alpha + 1) slots of (T + 1) records of 20 floats plus
     K_t columns and k_t ([T][14] float4) per element; backward: the gains."""
