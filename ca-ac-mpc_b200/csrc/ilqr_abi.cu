@@ -53,6 +53,16 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 int cuda_status(cudaError_t e) { return e == cudaSuccess ? ILQR_OK : ILQR_ERR_CUDA; }
 
+// ILQR_B200_LAYOUT=team|pair forces one kernel layout of the 10-state solve
+// and backward (both give the same bits; the default picks by batch size).
+int layout_from_env() {
+  const char* v = std::getenv("ILQR_B200_LAYOUT");
+  if (v == nullptr) return ilqr::LAYOUT_AUTO;
+  if (std::strcmp(v, "team") == 0) return ilqr::LAYOUT_TEAM;
+  if (std::strcmp(v, "pair") == 0) return ilqr::LAYOUT_PAIR;
+  return ilqr::LAYOUT_AUTO;
+}
+
 }  // namespace
 
 extern "C" {
@@ -141,6 +151,10 @@ int solve_impl(const float* x0, const float* U_init, const float* C, const float
   p.sig = sig;
   p.c_bstride = time_major ? ilqr::NT : (int64_t)T * ilqr::NT;
   p.c_tstride = time_major ? B * ilqr::NT : ilqr::NT;
+  p.C = C;
+  p.C_bstride = time_major ? 1 : (int64_t)T;
+  p.C_tstride = time_major ? B : 1;
+  p.layout = layout_from_env();
   CUtensorMap tmC;
   std::memset(&tmC, 0, sizeof(tmC));  // never read in sigmoid mode (no pass copies C)
   if (sig.p == nullptr) {
@@ -177,6 +191,11 @@ int backward_impl(const float* X, const float* U, const float* C, const float* C
   p.g_sig = grad_sig;
   p.gc_bstride = time_major ? ilqr::NT : (int64_t)T * ilqr::NT;
   p.gc_tstride = time_major ? B * ilqr::NT : ilqr::NT;
+  p.C = C;
+  p.g_C = p.write_gC ? grad_C : nullptr;
+  p.C_bstride = time_major ? 1 : (int64_t)T;
+  p.C_tstride = time_major ? B : 1;
+  p.layout = layout_from_env();
   CUtensorMap tmC, tmG;
   std::memset(&tmC, 0, sizeof(tmC));  // never read in sigmoid mode
   std::memset(&tmG, 0, sizeof(tmG));

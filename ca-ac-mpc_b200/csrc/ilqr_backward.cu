@@ -13,6 +13,7 @@
 //      split across the team, written into the shared-memory slab and stored
 //      with one TMA bulk tensor store per step for the warp's six elements.
 #include "ilqr_kernels.h"
+#include "ilqr_pair.cuh"
 #include "ilqr_team.cuh"
 
 namespace ilqr {
@@ -254,12 +255,220 @@ __global__ void __launch_bounds__(32, MINB) backward_kernel(const __grid_constan
   }
 }
 
+
+// Bulk copy of `bytes` (a multiple of 16) from shared to global memory,
+// completion tracked by the issuing thread's bulk groups.
+__device__ __forceinline__ void bulk_store(float* dst, const float* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_u32(src)),
+               "r"(bytes)
+               : "memory");
+}
+
+// The pair layout of the same backward (ilqr_pair.cuh): one element per
+// half-warp; lane i < 10 owns row i of V in the masked Riccati pass, lane
+// i < 14 row i of grad_C[b, t] in the sweep. grad_C rows go to a
+// double-buffered staging block in shared memory and each block is stored
+// with one bulk copy (784 contiguous bytes). Same formulas and order as the
+// team kernel, so the same bits.
+template <int MINB>
+__global__ void __launch_bounds__(32, MINB) backward_pair_kernel(const BackwardParams p) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int lane = threadIdx.x;
+  const int h = lane >> 4, i = lane & (HALF - 1);
+  const int64_t b0 = (int64_t)blockIdx.x * EPWP;
+  const int64_t b = b0 + h;
+  const bool valid = b < p.B;
+  const int64_t bw = valid ? b : b0;
+  const int T = p.T;
+  const float dt = p.dt;
+  float* sh = reinterpret_cast<float*>(smem) + h * PAREA;
+  auto kcol = [&](int t, int j) {
+    return reinterpret_cast<float4*>(p.ws + ((size_t)(t * NX + j) * (size_t)p.S + (size_t)bw) * 4);
+  };
+  auto kff = [&](int t) {
+    return reinterpret_cast<float4*>(p.ws + ((size_t)T * NX * (size_t)p.S + (size_t)t * p.S + (size_t)bw) * 4);
+  };
+  auto f4 = [](const float (&v)[NU]) { return make_float4(v[0], v[1], v[2], v[3]); };
+  auto ld = [&](const float* q, int64_t k) { return valid ? __ldg(q + k) : 0.0f; };
+  const float* Xb = p.X + b * (int64_t)(T + 1) * NX;
+  const float* Ub = p.U + b * (int64_t)T * NU;
+  const float* gXb = p.gX + b * (int64_t)(T + 1) * NX;
+  const float* gUb = p.gU + b * (int64_t)T * NU;
+  const float* Cf = (p.C_f != nullptr && valid) ? p.C_f + b * CBLK : nullptr;
+  const int ri = i < NX ? i : 0;
+
+  // ---- 1. masked adjoint Riccati, V_T = C_f[:nx,:nx], v_T = -dL/dX_T --------
+  float Vr[NX];
+  float vr = -ld(gXb, T * NX + ri);
+#pragma unroll
+  for (int j = 0; j < NX; ++j) Vr[j] = Cf ? __ldg(Cf + ri * NT + j) : 0.0f;
+  const bool sigm = p.sig.p != nullptr;
+  const float* sgrow = sigm ? p.sig.p + bw * (int64_t)(2 * NT) * T : nullptr;
+  PairCPipe cpipe{sigm ? nullptr : p.C + bw * p.C_bstride * CBLK, p.C_tstride, sh + PC0, i};
+  if (sigm) {
+    for (int f = i; f < CBLK; f += HALF) sh[PC0 + f] = 0.0f;
+    __syncwarp();
+  } else {
+    cpipe.issue(T - 1);
+  }
+  for (int t = T - 1; t >= 0; --t) {
+    float xb[NX], ub[NU];
+#pragma unroll
+    for (int k = 0; k < NX; ++k) xb[k] = ld(Xb, t * NX + k);
+#pragma unroll
+    for (int a = 0; a < NU; ++a) ub[a] = ld(Ub, t * NU + a);
+    const float lx = i < NX ? -ld(gXb, t * NX + i) : (i < NT ? -ld(gUb, t * NU + (i - NX)) : 0.0f);
+    uint32_t tight = 0;
+    if (p.tight != nullptr && valid) {
+#pragma unroll
+      for (int a = 0; a < NU; ++a) tight |= (p.tight[(b * T + t) * NU + a] != 0 ? 1u : 0u) << a;
+    }
+    if (sigm) {
+      if (i < NT) sh[PC0 + i * (NT + 1)] = sig_diag(p.sig, sgrow, T, t, i);
+    } else if (t > 0) {
+      cpipe.issue(t - 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    const Jac J = drone_jac(xb, ub, dt);
+    __syncwarp();
+    float Kr[NU];
+    pair_riccati<true>(Vr, vr, J, sigm ? sh + PC0 : cpipe.block(t), lx, p.reg, tight, i, valid, sh, Kr);
+    if (valid) {
+      if (i < NX) *kcol(t, i) = f4(Kr);
+      if (i == NX) *kff(t) = f4(Kr);
+    }
+  }
+  if (valid && p.g_x0 != nullptr && i < NX) p.g_x0[b * NX + i] = -vr;
+  __syncwarp();
+
+  // ---- 2. tangent sweep and gradient assembly -------------------------------
+  // grad_C[b, t] staging: two blocks of 196 floats at the start of the area
+  // (the C_t buffers, free now); block t goes out with one bulk copy by lane 0
+  // of the half, and block t - 2's copy must have read its buffer first.
+  float dx[NX];
+#pragma unroll
+  for (int k = 0; k < NX; ++k) dx[k] = 0.0f;
+  const bool wgc = p.write_gC && valid;
+  float* gCb = wgc ? p.g_C + b * p.C_bstride * CBLK : nullptr;
+  for (int t = 0; t < T; ++t) {
+    float z[NT], du[NU];
+#pragma unroll
+    for (int k = 0; k < NX; ++k) z[k] = ld(Xb, t * NX + k);
+#pragma unroll
+    for (int a = 0; a < NU; ++a) z[NX + a] = ld(Ub, t * NU + a);
+    {
+      float4 c = *kcol(t, 0);
+      float acc[NU] = {c.x * dx[0], c.y * dx[0], c.z * dx[0], c.w * dx[0]};
+#pragma unroll
+      for (int j = 1; j < NX; ++j) {
+        c = *kcol(t, j);
+        acc[0] = fmaf(c.x, dx[j], acc[0]);
+        acc[1] = fmaf(c.y, dx[j], acc[1]);
+        acc[2] = fmaf(c.z, dx[j], acc[2]);
+        acc[3] = fmaf(c.w, dx[j], acc[3]);
+      }
+      const float4 kk = *kff(t);
+      du[0] = acc[0] + kk.x;
+      du[1] = acc[1] + kk.y;
+      du[2] = acc[2] + kk.z;
+      du[3] = acc[3] + kk.w;
+    }
+    float dtau[NT];
+#pragma unroll
+    for (int k = 0; k < NX; ++k) dtau[k] = dx[k];
+#pragma unroll
+    for (int a = 0; a < NU; ++a) dtau[NX + a] = du[a];
+    const int ti = i < NT ? i : 0;
+    const float di = dtau[ti], zi = z[ti];
+    if (p.write_gC) {  // (uniform across the warp; a half without an element stages but never stores)
+      float* stg = sh + PC0 + (t & 1) * CBLK;
+      if (t >= 2) {
+        if (wgc && i == 0) bulk_wait_read<1>();  // the copy of block t - 2 has read this buffer
+        __syncwarp();
+      }
+      // grad_C = -1/2 (dtau (x) z + z (x) dtau), z = [X_t; U_t] (controller.py:87-96)
+      if (i < NT) {
+        float2* row = reinterpret_cast<float2*>(stg + i * NT);
+#pragma unroll
+        for (int j = 0; j < NT; j += 2) {
+          const float g0 = -0.5f * (di * z[j] + zi * dtau[j]);
+          const float g1 = -0.5f * (di * z[j + 1] + zi * dtau[j + 1]);
+          row[j / 2] = make_float2(g0, g1);
+        }
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (wgc && i == 0) {
+        bulk_store(gCb + (int64_t)t * p.C_tstride * CBLK, stg, CBLK * 4u);
+        bulk_commit();
+      }
+    }
+    if (valid && i < NT) {
+      if (sigm && p.g_sig != nullptr) {
+        float* gq = p.g_sig + b * (int64_t)(2 * NT) * T;
+        const float gii = -0.5f * (di * zi + zi * di);
+        const int off = sig_off(T, t, i);
+        gq[off] = gii * p.sig.range_q;
+        const float gc = -di;
+        gq[14 * T + off] = i == NX ? (-gc) * p.sig.range_pt : gc * p.sig.range_p;
+      }
+      if (p.g_c != nullptr) p.g_c[b * p.gc_bstride + t * p.gc_tstride + i] = -di;
+      if (i < NX && p.g_xref != nullptr) p.g_xref[(b * (T + 1) + t) * NX + i] = di;
+      if (i >= NX && p.g_uref != nullptr) p.g_uref[(b * T + t) * NU + (i - NX)] = di;
+    }
+    float xs[NX], us[NU];
+#pragma unroll
+    for (int k = 0; k < NX; ++k) xs[k] = z[k];
+#pragma unroll
+    for (int a = 0; a < NU; ++a) us[a] = z[NX + a];
+    const Jac J = drone_jac(xs, us, dt);
+    float nd[NX];
+    jac_apply(J, dx, du, nd);
+#pragma unroll
+    for (int k = 0; k < NX; ++k) dx[k] = nd[k];
+  }
+  if (wgc && i == 0) bulk_wait<0>();
+  __syncwarp();
+  if (!valid) return;
+  if (p.g_xref != nullptr && i < NX) p.g_xref[(b * (T + 1) + T) * NX + i] = 0.0f;
+  if (p.g_Cf != nullptr || p.g_cf != nullptr) {
+    float ev[NX];
+#pragma unroll
+    for (int k = 0; k < NX; ++k)
+      ev[k] = ld(Xb, T * NX + k) - (p.x_ref != nullptr ? __ldg(p.x_ref + (b * (T + 1) + T) * NX + k) : 0.0f);
+    if (p.g_Cf != nullptr) {
+      for (int f = i; f < CBLK; f += HALF) {
+        const int r = f / NT, j = f - r * NT;
+        float g = 0.0f;
+        if (r < NX && j < NX) {
+          float dr = 0.0f, dj = 0.0f, er = 0.0f, ej = 0.0f;
+#pragma unroll
+          for (int q = 0; q < NX; ++q) {
+            if (q == r) { dr = dx[q]; er = ev[q]; }
+            if (q == j) { dj = dx[q]; ej = ev[q]; }
+          }
+          g = -0.5f * (dr * ej + er * dj);
+        }
+        p.g_Cf[b * CBLK + f] = g;
+      }
+    }
+    if (p.g_cf != nullptr && i < NT) p.g_cf[b * NT + i] = i < NX ? -dx[i] : 0.0f;
+  }
+}
+
 }  // namespace
 
 size_t backward_smem_bytes() { return (size_t)EPW * CBLK * 4 + (size_t)EPW * XS * 4 + sizeof(uint64_t); }
 
 cudaError_t launch_backward(const CUtensorMap& tmC, const CUtensorMap& tmG, const BackwardParams& p,
                             cudaStream_t stream) {
+  if (p.layout == LAYOUT_PAIR || (p.layout == LAYOUT_AUTO && p.B <= PAIR_MAX_B)) {
+    const unsigned pgrid = (unsigned)((p.B + EPWP - 1) / EPWP);
+    backward_pair_kernel<8><<<pgrid, WARP, (size_t)EPWP * PAREA * sizeof(float), stream>>>(p);
+    return cudaGetLastError();
+  }
   const size_t smem = backward_smem_bytes();
   const unsigned grid = (unsigned)((p.B + EPW - 1) / EPW);
   const int tier = pick_tier(grid);

@@ -53,7 +53,20 @@ struct SolveParams {
   // for batch-major costs [B, T, 14], 14 / B * 14 for time-major [T, B, 14]
   int64_t c_bstride;
   int64_t c_tstride;
+  // The pair layout (two elements per warp) copies C blocks with cp.async:
+  // C itself and the blocks between consecutive elements / steps (T, 1)
+  // batch-major, (1, B) time-major.
+  const float* C;
+  int64_t C_bstride;
+  int64_t C_tstride;
+  int layout;  // LAYOUT_AUTO, LAYOUT_TEAM or LAYOUT_PAIR
 };
+
+// Kernel layouts of the 10-state solve and backward. TEAM: six elements per
+// warp, five lanes each (ilqr_team.cuh); PAIR: two elements per warp,
+// sixteen lanes each (ilqr_pair.cuh). Both compute the same bits; AUTO picks
+// PAIR for batches up to PAIR_MAX_B.
+constexpr int LAYOUT_AUTO = 0, LAYOUT_TEAM = 1, LAYOUT_PAIR = 2;
 
 struct BackwardParams {
   const float* X;
@@ -81,6 +94,11 @@ struct BackwardParams {
   float* g_sig;     // [B, 28 T] gradient of the parameters (sigmoid mode)
   int64_t gc_bstride;  // layout of grad_c, as SolveParams::c_bstride / c_tstride
   int64_t gc_tstride;
+  const float* C;      // pair layout: C and grad_C blocks, strides as SolveParams::C_bstride
+  float* g_C;
+  int64_t C_bstride;
+  int64_t C_tstride;
+  int layout;
 };
 
 // Solve workspace, in floats, element-interleaved with stride S (the record

@@ -1,0 +1,307 @@
+// ilqr_pair.cuh -- one batch element per half-warp (16 lanes, 2 elements per warp).
+//
+// The team layout (ilqr_team.cuh) packs six elements into a warp, which
+// keeps the instruction count per element low but leaves a small batch with
+// too few warps: at B = 2048 it makes 342 warps for 592 schedulers, and each
+// element's iterations run as one long serial chain. This layout gives an
+// element sixteen lanes: lane i < 10 owns row i of V, lanes 10..13 the four
+// control rows, and every phase of a Riccati step spreads over them, so the
+// chain per step is several times shorter.
+//
+// Each output is computed with exactly the operations, in exactly the order,
+// of the team kernels, so both layouts give the same bits (for finite
+// values: a product with an exact zero coefficient adds a zero here where
+// the team formula leaves the term out). To keep every phase one
+// instruction stream, each row r in 0..13 of the products A^T Y (Y = V A,
+// V B, v) and B^T Y is written in one form,
+//     out = base + fmaf(c7, Y[own], sum_s c[s] Y[3 + s]),   s = 0..6,
+// the sum accumulated from 0 in index order (pair_coef gives c, c7, own):
+//   rows 3..6   column of A at quaternion row r (c7 = 0)
+//   row 0       c = 0, c7 = 1, own = 0
+//   rows 1, 2   c = 0, c7 = 1, own = r            (position: Y[r])
+//   rows 7..9   c[r-3] = 1, c7 = dt, own = r - 7  (velocity: Y[r] + dt Y[p])
+//   row 10      c[4..6] = B's thrust column       (Q_uu / q_u row of the thrust)
+//   rows 11..13 c[0..3] = B's body-rate column    (Q_uu / q_u rows of the rates)
+#pragma once
+
+#include "ilqr_device.cuh"
+#include "ilqr_kernels.h"
+#include "ilqr_team.cuh"
+
+namespace ilqr {
+
+constexpr int HALF = 16;   // lanes per element
+constexpr int EPWP = 2;    // elements per warp
+// Batches up to this size run in the pair layout by default.
+constexpr int64_t PAIR_MAX_B = 2048;
+
+// Per-element shared-memory area (floats; float4 fields 16-byte aligned).
+constexpr int PC0 = 0;       // [2][196] C_t blocks (double buffer; diagonal mode uses block 0)
+constexpr int PVAT = 392;    // [10][12] columns of V A: VAT[c][vat_pos(r)]
+constexpr int PVB = 512;     // [10][4]  rows of V B
+constexpr int PV = 552;      // [12]     v
+constexpr int PQUU = 564;    // [4][4]   Q_uu rows (reg added once)
+constexpr int PQU = 580;     // [4]      q_u
+constexpr int PKC = 584;     // [10][4]  K columns (the four gains of state c)
+constexpr int PKF = 624;     // [4]      k
+constexpr int PQXU = 628;    // [10][4]  Q_xu rows
+constexpr int PS = 668;      // [16]     rowdots s_i = (C_t tau)_i (first-pass objective)
+constexpr int PCV = 684;     // [16]     c_t
+constexpr int PSV = 700;     // [32]     SVD fallback: Q, its inverse
+constexpr int PAREA = 752;   // floats per element (= 16 mod 32: the two elements use opposite bank halves)
+
+// Position of row r of V A inside a column of VAT: rows 3..9 first (two
+// aligned float4 loads give them), then rows 0..2.
+__device__ __forceinline__ int vat_pos(int r) { return r >= 3 ? r - 3 : r + 7; }
+
+// Coefficients of row r (0..13) in the form of the header comment.
+__device__ __forceinline__ void pair_coef(const Jac& J, int r, float (&c)[7], float& c7, int& own) {
+  const float z = 0.0f;
+  float cc[8];
+  coef_a(J, (r >= 3 && r <= 6) ? r - 3 : 4, cc);  // rows 3..6; m = 4 gives zeros and cc[7] = 1
+#pragma unroll
+  for (int s = 0; s < 7; ++s) c[s] = (r >= 3 && r <= 6) ? cc[s] : z;
+  c7 = (r <= 6) ? cc[7] : z;  // rows 0..2: 1; rows 3..6: 0
+  own = r < 3 ? r : (r <= 6 ? r : (r < NX ? r - 7 : 0));
+  if (r >= 7 && r < NX) {
+#pragma unroll
+    for (int s = 4; s < 7; ++s) c[s] = (s == r - 3) ? 1.0f : z;
+    c7 = J.dt;
+  }
+  if (r == NX) {
+    c[4] = J.bv0;
+    c[5] = J.bv1;
+    c[6] = J.bv2;
+  }
+  if (r > NX) {
+    const int kk = r - NX - 1;
+#pragma unroll
+    for (int mm = 0; mm < 4; ++mm) c[mm] = kk == 0 ? bqw(J, mm, 0) : (kk == 1 ? bqw(J, mm, 1) : bqw(J, mm, 2));
+  }
+}
+
+// One Riccati step for an element's half-warp; the same recursion and
+// operation order as team_riccati (ilqr_team.cuh), forward or masked.
+// Lane i < 10: Vr, vr = row i of V and v_i (in V_{t+1}, out V_t). lx: lane
+// i < 10 the gradient term of row i, lane 10 + a that of control a. Ce: the
+// element's C_t block in shared memory. sh: the element's area. On return
+// lane i < 10 holds column i of K in Kr (the four gains of state i), lane 10
+// holds k. Every lane returns whether the Cholesky succeeded (the same in all
+// lanes of the half). Ends with a warp sync: C_t and the area are free.
+template <bool MASKED>
+__device__ __forceinline__ bool pair_riccati(float (&Vr)[NX], float& vr, const Jac& J, const float* __restrict__ Ce,
+                                             float lx, float reg, uint32_t tight, int i, bool live,
+                                             float* __restrict__ sh, float (&Kr)[NU]) {
+  // ---- rows of V A (as columns of VAT), V B and v ----------------------------
+  if (i < NX) {
+    float va[NX], vb[NU];
+    row_VA_VB(J, Vr, va, vb);
+    const int ps = vat_pos(i);
+#pragma unroll
+    for (int c = 0; c < NX; ++c) sh[PVAT + c * 12 + ps] = va[c];
+    *reinterpret_cast<float4*>(sh + PVB + 4 * i) = make_float4(vb[0], vb[1], vb[2], vb[3]);
+    sh[PV + i] = vr;
+  }
+  __syncwarp();
+
+  // ---- Q_xu rows and q_x (lanes 0..9), Q_uu rows and q_u (lanes 10..13) -------
+  const int r = i < NT ? i : NT - 1;
+  float c[7], c7;
+  int own;
+  pair_coef(J, r, c, c7, own);
+  float Qr[NU], qr;
+  {
+    float4 acc4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    float accv = 0.0f;
+#pragma unroll
+    for (int s = 0; s < 7; ++s) {
+      const float4 y = *reinterpret_cast<const float4*>(sh + PVB + 4 * (3 + s));
+      acc4.x = fmaf(c[s], y.x, acc4.x);
+      acc4.y = fmaf(c[s], y.y, acc4.y);
+      acc4.z = fmaf(c[s], y.z, acc4.z);
+      acc4.w = fmaf(c[s], y.w, acc4.w);
+      accv = fmaf(c[s], sh[PV + 3 + s], accv);
+    }
+    const float4 o = *reinterpret_cast<const float4*>(sh + PVB + 4 * own);
+    const float* Cr = Ce + r * NT + NX;
+    Qr[0] = Cr[0] + fmaf(c7, o.x, acc4.x);
+    Qr[1] = Cr[1] + fmaf(c7, o.y, acc4.y);
+    Qr[2] = Cr[2] + fmaf(c7, o.z, acc4.z);
+    Qr[3] = Cr[3] + fmaf(c7, o.w, acc4.w);
+    if (r >= NX) {
+#pragma unroll
+      for (int a = 0; a < NU; ++a) Qr[a] = Qr[a] + (r - NX == a ? reg : 0.0f);
+    }
+    qr = lx + fmaf(c7, sh[PV + own], accv);
+  }
+  if (i >= NX && i < NT) {
+    *reinterpret_cast<float4*>(sh + PQUU + 4 * (i - NX)) = make_float4(Qr[0], Qr[1], Qr[2], Qr[3]);
+    sh[PQU + i - NX] = qr;
+  }
+  if (i < NX) *reinterpret_cast<float4*>(sh + PQXU + 4 * i) = make_float4(Qr[0], Qr[1], Qr[2], Qr[3]);
+  __syncwarp();
+
+  // ---- gains: every lane factors Q_uu, lane i < 10 solves column i of K,
+  // lane 10 solves k ----------------------------------------------------------
+  float Quu[NU][NU], qu[NU];
+#pragma unroll
+  for (int a = 0; a < NU; ++a) {
+    const float4 q4 = *reinterpret_cast<const float4*>(sh + PQUU + 4 * a);
+    Quu[a][0] = q4.x; Quu[a][1] = q4.y; Quu[a][2] = q4.z; Quu[a][3] = q4.w;
+  }
+  {
+    const float4 q4 = *reinterpret_cast<const float4*>(sh + PQU);
+    qu[0] = q4.x; qu[1] = q4.y; qu[2] = q4.z; qu[3] = q4.w;
+  }
+  bool ok;
+  Chol4 L;
+  float* sv = sh + PSV;
+  {
+    float Qs[NU][NU];
+#pragma unroll
+    for (int a = 0; a < NU; ++a)
+#pragma unroll
+      for (int b = 0; b < NU; ++b) {
+        if (MASKED) {
+          const bool ta = (tight >> a) & 1u, tb = (tight >> b) & 1u;
+          float val = (ta || tb) ? 0.0f : Quu[a][b];
+          if (a == b && ta) val = val + 1.0f;
+          Qs[a][b] = val + (a == b ? 1e-8f * reg : 0.0f);
+        } else {
+          Qs[a][b] = Quu[a][b] + (a == b ? reg : 0.0f);
+        }
+      }
+    // A half without an element never takes the SVD path.
+    ok = chol4(Qs, L) || !live;
+    if (!ok) {
+      // every lane of the half forms the same inverse; identical writes
+#pragma unroll
+      for (int a = 0; a < NU; ++a)
+#pragma unroll
+        for (int b = 0; b < NU; ++b) sv[a * NU + b] = Qs[a][b];
+      svd_inverse4(sv, sv + NU * NU);
+    }
+  }
+  if (__any_sync(FULL, !ok)) __syncwarp();  // every fallback inverse of the warp is written
+  auto msk = [&](int a, float v) { return (MASKED && ((tight >> a) & 1u)) ? 0.0f : v; };
+  {
+    float rhs[NU], sol[NU];
+#pragma unroll
+    for (int a = 0; a < NU; ++a) rhs[a] = msk(a, i < NX ? Qr[a] : qu[a]);
+    if (ok) {
+      chol4_solve(L, rhs, sol);
+    } else {
+      const float* Mi = sv + NU * NU;
+#pragma unroll
+      for (int a = 0; a < NU; ++a) {
+        float acc = Mi[a * NU] * rhs[0];
+#pragma unroll
+        for (int b = 1; b < NU; ++b) acc = fmaf(Mi[a * NU + b], rhs[b], acc);
+        sol[a] = acc;
+      }
+    }
+#pragma unroll
+    for (int a = 0; a < NU; ++a) Kr[a] = -sol[a];
+  }
+  if (i < NX) *reinterpret_cast<float4*>(sh + PKC + 4 * i) = make_float4(Kr[0], Kr[1], Kr[2], Kr[3]);
+  if (i == NX) *reinterpret_cast<float4*>(sh + PKF) = make_float4(Kr[0], Kr[1], Kr[2], Kr[3]);
+  // W_r = K_r^T Q_uu + Q_xu[r] (team_riccati's wrow)
+  float Wr[NU];
+#pragma unroll
+  for (int a = 0; a < NU; ++a) {
+    float acc = Kr[0] * Quu[0][a];
+#pragma unroll
+    for (int b = 1; b < NU; ++b) acc = fmaf(Kr[b], Quu[b][a], acc);
+    Wr[a] = acc + Qr[a];
+  }
+  __syncwarp();  // K columns and k of the element are in the area
+
+  // ---- value update for row i ---------------------------------------------
+  float k[NU];
+  {
+    const float4 k4 = *reinterpret_cast<const float4*>(sh + PKF);
+    k[0] = k4.x; k[1] = k4.y; k[2] = k4.z; k[3] = k4.w;
+  }
+  if (i < NX) {
+    if (MASKED) {
+      float w[NU];
+#pragma unroll
+      for (int a = 0; a < NU; ++a) {
+        float acc = Quu[a][0] * k[0];
+#pragma unroll
+        for (int b = 1; b < NU; ++b) acc = fmaf(Quu[a][b], k[b], acc);
+        w[a] = acc + qu[a];
+      }
+      float t2 = Kr[0] * w[0];
+#pragma unroll
+      for (int a = 1; a < NU; ++a) t2 = fmaf(Kr[a], w[a], t2);
+      float t3 = Qr[0] * k[0];
+#pragma unroll
+      for (int a = 1; a < NU; ++a) t3 = fmaf(Qr[a], k[a], t3);
+      vr = (qr + t2) + t3;
+    } else {
+      float t1 = Wr[0] * k[0];
+#pragma unroll
+      for (int a = 1; a < NU; ++a) t1 = fmaf(Wr[a], k[a], t1);
+      float t2 = Kr[0] * qu[0];
+#pragma unroll
+      for (int a = 1; a < NU; ++a) t2 = fmaf(Kr[a], qu[a], t2);
+      vr = (qr + t1) + t2;
+    }
+    // V[i][cc] = (Q_xx[i][cc] + W_i K_cc) + K_i Q_xu[cc], Q_xx[i][cc] from the
+    // columns of V A in the form of the header comment
+    const int po = vat_pos(own);
+    const float* Ci = Ce + i * NT;
+#pragma unroll
+    for (int cc = 0; cc < NX; ++cc) {
+      const float* col = sh + PVAT + cc * 12;
+      const float4 y0 = *reinterpret_cast<const float4*>(col);
+      const float4 y1 = *reinterpret_cast<const float4*>(col + 4);
+      const float y[7] = {y0.x, y0.y, y0.z, y0.w, y1.x, y1.y, y1.z};
+      float acc = 0.0f;
+#pragma unroll
+      for (int s = 0; s < 7; ++s) acc = fmaf(c[s], y[s], acc);
+      const float q = Ci[cc] + fmaf(c7, col[po], acc);
+      const float4 k4 = *reinterpret_cast<const float4*>(sh + PKC + 4 * cc);
+      const float4 q4 = *reinterpret_cast<const float4*>(sh + PQXU + 4 * cc);
+      float t1 = Wr[0] * k4.x;
+      t1 = fmaf(Wr[1], k4.y, t1);
+      t1 = fmaf(Wr[2], k4.z, t1);
+      t1 = fmaf(Wr[3], k4.w, t1);
+      float t2 = Kr[0] * q4.x;
+      t2 = fmaf(Kr[1], q4.y, t2);
+      t2 = fmaf(Kr[2], q4.z, t2);
+      t2 = fmaf(Kr[3], q4.w, t2);
+      Vr[cc] = (q + t1) + t2;
+    }
+  }
+  __syncwarp();  // C_t and the area are no longer read
+  return ok;
+}
+
+// Sum of x over lanes base .. base + 4 in that order (team_sum's order).
+__device__ __forceinline__ float pair_sum5(float x, int base) {
+  float s = __shfl_sync(FULL, x, base);
+#pragma unroll
+  for (int j = 1; j < TEAM; ++j) s += __shfl_sync(FULL, x, base + j);
+  return s;
+}
+
+// Double-buffered cp.async stream of one element's C_t blocks (16 lanes,
+// 49 copies of 16 bytes per block). issue(t) copies block t into buffer
+// t & 1; each lane commits one group per issue.
+struct PairCPipe {
+  const float* Cb;   // C block of (element, t) at Cb + t * tstride * CBLK
+  int64_t tstride;
+  float* buf;        // the element's area + PC0
+  int i;
+  __device__ __forceinline__ void issue(int t) {
+    const float* src = Cb + (int64_t)t * tstride * CBLK;
+    float* dst = buf + (t & 1) * CBLK;
+    for (int q = i; q < CBLK / 4; q += HALF) cp_async16(dst + 4 * q, src + 4 * q);
+    cp_async_commit();
+  }
+  __device__ __forceinline__ float* block(int t) const { return buf + (t & 1) * CBLK; }
+};
+
+}  // namespace ilqr

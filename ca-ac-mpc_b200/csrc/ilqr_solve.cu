@@ -33,6 +33,7 @@
 // The initial objective (controller.py:308) is accumulated during the first
 // Riccati pass, which reads the same C_t blocks.
 #include "ilqr_kernels.h"
+#include "ilqr_pair.cuh"
 #include "ilqr_team.cuh"
 
 namespace ilqr {
@@ -668,6 +669,397 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
   }
 }
 
+
+// The pair layout of the same solve (ilqr_pair.cuh): one element per
+// half-warp. Lane i < 10 owns row i of V through the Riccati pass; the line
+// search runs step size j on lane j of the half (up to eight at once); C_t
+// blocks stream through a cp.async double buffer. Workspace records, the
+// candidate slots and every formula are the team kernel's, so the results
+// are the same bits.
+template <bool HAS_REF, int MINB>
+__global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams p) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int lane = threadIdx.x;
+  const int h = lane >> 4, i = lane & (HALF - 1);
+  const int base = h * HALF;
+  const int64_t b0 = (int64_t)blockIdx.x * EPWP;
+  const int64_t b = b0 + h;
+  const bool valid = b < p.B;
+  const int64_t bw = valid ? b : b0;  // workspace record read by this half (never written when !valid)
+  const int T = p.T;
+  const float dt = p.dt;
+  const SolveWs W{p, (uint32_t)bw};
+  float* sh = reinterpret_cast<float*>(smem) + h * PAREA;
+
+  const bool bounds = p.has_bounds != 0;
+  const float* lo = bounds ? p.u_min : nullptr;
+  const float* hi = bounds ? p.u_max : nullptr;
+  const float* cb = p.c != nullptr ? p.c + b * p.c_bstride : nullptr;
+  const float* xrb = (HAS_REF && p.x_ref != nullptr) ? p.x_ref + b * (int64_t)(T + 1) * NX : nullptr;
+  const float* urb = (HAS_REF && p.u_ref != nullptr) ? p.u_ref + b * (int64_t)T * NU : nullptr;
+  auto xref = [&](int t, int k) { return (HAS_REF && xrb != nullptr) ? ldg_or0(xrb + t * NX + k, valid) : 0.0f; };
+  auto uref = [&](int t, int a) { return (HAS_REF && urb != nullptr) ? ldg_or0(urb + t * NU + a, valid) : 0.0f; };
+  const float* Cf = (p.C_f != nullptr && valid) ? p.C_f + b * CBLK : nullptr;
+  const float* cf = (p.c_f != nullptr && valid) ? p.c_f + b * NT : nullptr;
+  auto load_x0 = [&](float (&x)[NX]) {
+#pragma unroll
+    for (int k = 0; k < NX; ++k) x[k] = ldg_or0(p.x0 + b * NX + k, valid);
+  };
+  const bool writer = valid && i == 0;
+  if (p.trace != nullptr && writer)
+    for (int it = 0; it < p.max_iter; ++it) p.trace[b * p.max_iter + it] = (int8_t)-128;
+
+  // ---- initial open-loop rollout with U_init into slot 0 -----------------------
+  {
+    float x[NX];
+    load_x0(x);
+    for (int t = 0; t < T; ++t) {
+      float u[NU];
+#pragma unroll
+      for (int a = 0; a < NU; ++a) u[a] = ldg_or0(p.U_init + (b * T + t) * NU + a, valid);
+      if (writer) store_rec(W.rec(0, t), x, u);
+      float xn[NX];
+      drone_step(x, u, dt, xn);
+#pragma unroll
+      for (int k = 0; k < NX; ++k) x[k] = xn[k];
+    }
+    if (writer) store_rec_x(W.rec(0, T), x);
+  }
+  __syncwarp();
+
+  const bool sigm = p.sig.p != nullptr;
+  const float* sgrow = sigm ? p.sig.p + bw * (int64_t)(2 * NT) * T : nullptr;
+  PairCPipe cpipe{sigm ? nullptr : p.C + bw * p.C_bstride * CBLK, p.C_tstride, sh + PC0, i};
+  bool diag = sigm;
+  bool offd = false;
+  if (sigm) {
+    for (int f = i; f < CBLK; f += HALF) sh[PC0 + f] = 0.0f;
+    __syncwarp();
+  }
+  int nom = 0;
+  uint32_t status = 0;
+  bool active = valid;
+  int iters = 0;
+  int stall_iter = p.max_iter;
+  float stall_gap = 0.0f;
+  float best = 0.0f;
+  const int ri = i < NX ? i : 0;  // V row of this lane (lanes >= 10 carry a copy of row 0, unused)
+  const int ti = i < NT ? i : 0;  // tau / c entry of this lane
+
+  const int n_loop = p.max_iter > 0 ? p.max_iter : 1;
+  for (int it = 0; it < n_loop; ++it) {
+    const bool cost_only = it >= p.max_iter;
+    if (!cost_only && p.forced != nullptr && active && p.forced[b * p.max_iter + it] == (int8_t)-128)
+      active = false;
+    if (!__any_sync(FULL, active) && it > 0) break;
+
+    // ---- backward Riccati pass ----------------------------------------------------
+    float Vr[NX], vr;
+    {
+      float xT[NX], tn[NX];
+      load_rec_x(W.rec(nom, T), xT);
+#pragma unroll
+      for (int k = 0; k < NX; ++k) tn[k] = xT[k] - xref(T, k);
+      float acc = 0.0f;
+#pragma unroll
+      for (int j = 0; j < NX; ++j) {
+        Vr[j] = Cf ? __ldg(Cf + ri * NT + j) : 0.0f;
+        acc = fmaf(Vr[j], tn[j], acc);
+      }
+      vr = acc + (cf ? __ldg(cf + ri) : 0.0f);
+    }
+    bool fallback = false;
+    float cost_q = 0.0f, cost_l = 0.0f;
+    const bool first = (it == 0);
+    if (!diag) cpipe.issue(T - 1);
+    for (int t = T - 1; t >= 0; --t) {
+      float xb[NX], ub[NU], tau[NT];
+      load_rec(W.rec(nom, t), xb, ub);
+      float cv;  // c_t entry ti: from the input on the first pass, from the cost record afterwards
+      if (first && sigm) cv = sig_c(p.sig, sgrow, T, t, ti);
+      else if (first) cv = ldg_or0(cb + t * p.c_tstride + ti, valid);
+      else cv = W.cvec(t)[ti];
+      if (!diag) {
+        if (t > 0) {
+          cpipe.issue(t - 1);
+          cp_async_wait<1>();
+        } else {
+          cp_async_wait<0>();
+        }
+      } else if (first && sigm) {
+        if (i < NT) {
+          const float dv = sig_diag(p.sig, sgrow, T, t, i);
+          sh[PC0 + i * (NT + 1)] = dv;
+          if (valid) W.diag(t)[i] = dv;
+        }
+      } else {
+        if (i < NT) sh[PC0 + i * (NT + 1)] = W.diag(t)[i];
+      }
+      __syncwarp();
+      const float* Ce = diag ? sh + PC0 : cpipe.block(t);
+#pragma unroll
+      for (int k = 0; k < NX; ++k) tau[k] = xb[k] - xref(t, k);
+#pragma unroll
+      for (int a = 0; a < NU; ++a) tau[NX + a] = ub[a] - uref(t, a);
+      // quadraticize: l_tau = C tau + c, row ti
+      float sdot;
+      {
+        const float* Cr = Ce + ti * NT;
+        sdot = Cr[0] * tau[0];
+#pragma unroll
+        for (int j = 1; j < NT; ++j) sdot = fmaf(Cr[j], tau[j], sdot);
+      }
+      const float lx = sdot + cv;
+      if (first) {
+        if (i < NT) {
+          sh[PS + i] = sdot;
+          sh[PCV + i] = cv;
+          if (valid) W.cvec(t)[i] = cv;
+        }
+        if (p.diag_cache && valid && !sigm) {
+          const float4* c4 = reinterpret_cast<const float4*>(Ce);
+          for (int q = i; q < CBLK / 4; q += HALF) {
+            const float4 v = c4[q];
+            const int f = 4 * q;
+            offd |= (v.x != 0.0f && f % (NT + 1) != 0) || (v.y != 0.0f && (f + 1) % (NT + 1) != 0) ||
+                    (v.z != 0.0f && (f + 2) % (NT + 1) != 0) || (v.w != 0.0f && (f + 3) % (NT + 1) != 0);
+          }
+          if (i < NT) W.diag(t)[i] = Ce[i * (NT + 1)];
+        }
+      }
+      const Jac J = drone_jac(xb, ub, dt);
+      __syncwarp();
+      if (first && i < TEAM) {
+        // the initial objective, accumulated as the team kernel's lane m = i does
+        const int ra = row_a(i), rb = row_b(i), ru = NX + (i < NU ? i : 0);
+        const float sa = sh[PS + ra], sb = sh[PS + rb], su = sh[PS + ru];
+        const float ca_ = sh[PCV + ra], cb_ = sh[PCV + rb], cu = sh[PCV + ru];
+        const float ta = tau[ra], tb = tau[rb], tu = tau[ru];
+        cost_q += fmaf(ta, sa, tb * sb) + (i < NU ? tu * su : 0.0f);
+        cost_l += fmaf(ca_, ta, cb_ * tb) + (i < NU ? cu * tu : 0.0f);
+      }
+      float Kr[NU];
+      if (!pair_riccati<false>(Vr, vr, J, Ce, lx, p.reg, 0u, i, valid, sh, Kr)) fallback = true;
+      if (valid) {
+        if (i < NX) *W.kcol(t, i) = f4(Kr);
+        if (i == NX) *W.kff(t) = f4(Kr);
+      }
+    }
+    if (first && p.diag_cache && !sigm) {
+      diag = !__any_sync(FULL, offd);
+      if (diag) {  // off-diagonal entries of the rebuilt block stay zero from here on
+        for (int f = i; f < CBLK; f += HALF) sh[PC0 + f] = 0.0f;
+        __syncwarp();
+      }
+    }
+    if (fallback && active) status |= ELEM_CHOL_FALLBACK;
+    if (first) {
+      float xT[NX], tn[NX];
+      load_rec_x(W.rec(nom, T), xT);
+#pragma unroll
+      for (int k = 0; k < NX; ++k) tn[k] = xT[k] - xref(T, k);
+      best = (0.5f * pair_sum5(cost_q, base) + pair_sum5(cost_l, base)) + terminal_cost(Cf, cf, tn);
+    }
+    __syncwarp();
+    if (cost_only) break;
+
+    // ---- grid line search: lane j of the half = step size j ----------------------
+    int jbest = 0;
+    float cmin = 0.0f;
+    bool have = false, nan_seen = false;
+    float cand[ILQR_MAX_ALPHAS_DEV];
+    {
+      const int j = i;
+      const float al = (j < p.n_alpha) ? p.alphas[j] : 0.0f;
+      const bool keep = valid && j < p.n_alpha && j < SOLVE_SLOTS - 1;
+      const int cs = j < nom ? j : j + 1;
+      float x[NX], sq = 0.0f, sl = 0.0f;
+      load_x0(x);
+      if (!diag) cpipe.issue(0);
+      for (int t = 0; t < T; ++t) {
+        if (!diag) {
+          if (t + 1 < T) {
+            cpipe.issue(t + 1);
+            cp_async_wait<1>();
+          } else {
+            cp_async_wait<0>();
+          }
+          __syncwarp();
+        }
+        float xb[NX], ub[NU], kt[NU], u[NU];
+        load_rec(W.rec(nom, t), xb, ub);
+        {
+          const float4 k4 = *W.kff(t);
+          kt[0] = k4.x; kt[1] = k4.y; kt[2] = k4.z; kt[3] = k4.w;
+        }
+        candidate_u(x, xb, ub, [&](int jj) { return *W.kcol(t, jj); }, kt, al, lo, hi, u);
+        if (keep) store_rec(W.rec(cs, t), x, u);
+        float tau[NT];
+#pragma unroll
+        for (int k = 0; k < NX; ++k) tau[k] = x[k] - xref(t, k);
+#pragma unroll
+        for (int a = 0; a < NU; ++a) tau[NX + a] = u[a] - uref(t, a);
+        const float* cost_t = W.diag(t);
+        float l;
+        {
+          const float4* c4 = reinterpret_cast<const float4*>(cost_t + 16);
+          const float4 h0 = c4[0], h1 = c4[1], h2 = c4[2], h3 = c4[3];
+          const float cvv[NT] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z,
+                                 h1.w, h2.x, h2.y, h2.z, h2.w, h3.x, h3.y};
+          l = cvv[0] * tau[0];
+#pragma unroll
+          for (int jj = 1; jj < NT; ++jj) l = fmaf(cvv[jj], tau[jj], l);
+        }
+        float q = 0.0f;
+        if (diag) {
+          const float4* d4 = reinterpret_cast<const float4*>(cost_t);
+          const float4 g0 = d4[0], g1 = d4[1], g2 = d4[2], g3 = d4[3];
+          const float dgv[NT] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z,
+                                 g1.w, g2.x, g2.y, g2.z, g2.w, g3.x, g3.y};
+#pragma unroll
+          for (int k = 0; k < NT; ++k) q = fmaf(tau[k], dgv[k] * tau[k], q);
+          if (!isfinite(q)) {
+            bool nonfinite = false;
+#pragma unroll
+            for (int k = 0; k < NT; ++k) nonfinite |= !isfinite(tau[k]);
+            if (nonfinite) q = __int_as_float(0x7fffffff);
+          }
+        } else {
+          const float* Ce = cpipe.block(t);
+#pragma unroll
+          for (int k = 0; k < NT; ++k) {
+            const float2* r2 = reinterpret_cast<const float2*>(Ce + k * NT);
+            float r = 0.0f;
+#pragma unroll
+            for (int jj = 0; jj < NT / 2; ++jj) {
+              const float2 c2 = r2[jj];
+              r = (jj == 0) ? c2.x * tau[0] : fmaf(c2.x, tau[2 * jj], r);
+              r = fmaf(c2.y, tau[2 * jj + 1], r);
+            }
+            q = fmaf(tau[k], r, q);
+          }
+          __syncwarp();  // block t is read; the next issue may overwrite it
+        }
+        sq += q;
+        sl += l;
+        float xn[NX];
+        drone_step(x, u, dt, xn);
+#pragma unroll
+        for (int k = 0; k < NX; ++k) x[k] = xn[k];
+      }
+      if (keep) store_rec_x(W.rec(cs, T), x);
+      float tn[NX];
+#pragma unroll
+      for (int k = 0; k < NX; ++k) tn[k] = x[k] - xref(T, k);
+      const float mine = (0.5f * sq + sl) + terminal_cost(Cf, cf, tn);
+#pragma unroll
+      for (int jj = 0; jj < ILQR_MAX_ALPHAS_DEV; ++jj) {
+        const float cj = __shfl_sync(FULL, mine, base + jj);
+        if (jj >= p.n_alpha) continue;
+        cand[jj] = cj;
+        if (!nan_seen) {
+          if (cj != cj) {
+            nan_seen = true;
+            jbest = jj;
+            cmin = cj;
+          } else if (!have || cj < cmin) {
+            have = true;
+            jbest = jj;
+            cmin = cj;
+          }
+        }
+      }
+    }
+
+    // ---- decision ---------------------------------------------------------------
+    bool accept = false;
+    int jsel = jbest;
+    if (active) {
+      ++iters;
+      if (p.forced != nullptr) {
+        const int8_t d = p.forced[b * p.max_iter + it];
+        if (d >= 0 && d < p.n_alpha) {
+          accept = true;
+          jsel = d;
+        }
+      } else {
+        accept = cmin < best;
+      }
+      if (p.trace != nullptr && writer) p.trace[b * p.max_iter + it] = (int8_t)(accept ? jsel : -(jbest + 1));
+      if (!accept && stall_iter == p.max_iter) {
+        stall_iter = it;
+        stall_gap = fabsf(cmin - best);
+      }
+      if (accept) best = cand[jsel];
+      if (!accept && p.forced == nullptr) active = false;
+    }
+    const bool rerun = accept && jsel >= SOLVE_SLOTS - 1;
+    if (accept && !rerun) nom = jsel < nom ? jsel : jsel + 1;
+    if (__any_sync(FULL, rerun)) {
+      const int dst = nom == 0 ? 1 : 0;
+      if (rerun && writer) {
+        const float al = p.alphas[jsel];
+        float x[NX];
+        load_x0(x);
+        for (int t = 0; t < T; ++t) {
+          float xb[NX], ub[NU], kt[NU], u[NU];
+          load_rec(W.rec(nom, t), xb, ub);
+          const float4 k4 = *W.kff(t);
+          kt[0] = k4.x; kt[1] = k4.y; kt[2] = k4.z; kt[3] = k4.w;
+          candidate_u(x, xb, ub, [&](int jj) { return *W.kcol(t, jj); }, kt, al, lo, hi, u);
+          store_rec(W.rec(dst, t), x, u);
+          float xn[NX];
+          drone_step(x, u, dt, xn);
+#pragma unroll
+          for (int k = 0; k < NX; ++k) x[k] = xn[k];
+        }
+        store_rec_x(W.rec(dst, T), x);
+      }
+      if (rerun) nom = dst;
+      __syncwarp();
+    }
+  }
+
+  // ---- outputs (the 16 lanes of the half split the writes) ------------------------
+  bool finite = true;
+  if (valid) {
+    const float* nrec = reinterpret_cast<const float*>(W.rec(nom, 0));
+    const int64_t rstride = p.S * TRJ_REC;
+    for (int f = i; f < (T + 1) * NX; f += HALF) {
+      const int t = f / NX, k = f - t * NX;
+      const float xv = nrec[t * rstride + k];
+      finite &= isfinite(xv);
+      p.X[b * (T + 1) * NX + f] = xv;
+    }
+    for (int f = i; f < T * NU; f += HALF) {
+      const int t = f / NU, a = f - t * NU;
+      const float uv = nrec[t * rstride + NX + a];
+      finite &= isfinite(uv);
+      p.U[b * T * NU + f] = uv;
+      if (p.tight != nullptr) {
+        bool tt = false;
+        if (bounds) {
+          const float l_ = __ldg(lo + a), h_ = __ldg(hi + a);
+          const float e0 = fabsf(uv - l_), e1 = fabsf(uv - h_);
+          tt = (uv == l_) || (isfinite(e0) && e0 <= 1e-7f + fabsf(1e-5f * l_)) || (uv == h_) ||
+               (isfinite(e1) && e1 <= 1e-7f + fabsf(1e-5f * h_));
+        }
+        p.tight[b * T * NU + f] = tt ? 1 : 0;
+      }
+    }
+  }
+  const unsigned bad = __ballot_sync(FULL, !finite);
+  if ((bad >> base) & 0xffffu) status |= ELEM_NONFINITE;
+  if (diag) status |= ELEM_DIAG_COST;
+  if (writer) {
+    if (p.iters) p.iters[b] = iters;
+    if (p.status) p.status[b] = status;
+    if (p.best_cost) p.best_cost[b] = best;
+    if (p.stall_iter) p.stall_iter[b] = stall_iter;
+    if (p.stall_gap) p.stall_gap[b] = stall_gap;
+  }
+}
+
 }  // namespace
 
 size_t solve_smem_bytes(int tier) {
@@ -677,9 +1069,18 @@ size_t solve_smem_bytes(int tier) {
   return base + sizeof(uint64_t);
 }
 
+size_t solve_pair_smem_bytes() { return (size_t)EPWP * PAREA * sizeof(float); }
+
 cudaError_t launch_solve(const CUtensorMap& tmC, const SolveParams& p, cudaStream_t stream) {
-  const unsigned grid = (unsigned)((p.B + EPW - 1) / EPW);
   const bool ref = p.x_ref != nullptr || p.u_ref != nullptr;
+  if (p.layout == LAYOUT_PAIR || (p.layout == LAYOUT_AUTO && p.B <= PAIR_MAX_B)) {
+    const unsigned pgrid = (unsigned)((p.B + EPWP - 1) / EPWP);
+    const size_t psmem = solve_pair_smem_bytes();
+    if (ref) solve_pair_kernel<true, 8><<<pgrid, WARP, psmem, stream>>>(p);
+    else solve_pair_kernel<false, 8><<<pgrid, WARP, psmem, stream>>>(p);
+    return cudaGetLastError();
+  }
+  const unsigned grid = (unsigned)((p.B + EPW - 1) / EPW);
   const int tier = pick_tier(grid);
   const size_t smem = solve_smem_bytes(tier);
   if (ref) {

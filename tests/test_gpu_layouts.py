@@ -1,0 +1,138 @@
+"""The two kernel layouts of the 10-state solve and backward give the same
+bits: the team layout (six elements per warp, five lanes each) and the pair
+layout (two elements per warp, sixteen lanes each; the default for small
+batches). ILQR_B200_LAYOUT forces one layout; every output of the solve
+(X, U, tight mask, decision trace, iterations, best cost, stall record, the
+status bits other than the diagonal-cost flag, which depends on which
+elements share a warp) and every gradient of the backward are compared bit
+for bit, on the golden cases (dense and asymmetric costs with terminal cost
+and references, no box, an indefinite Q_uu that takes the SVD fallback),
+an odd training-scale batch, a non-finite element, seven step sizes with
+re-run candidates, sigmoid costs and the time-major layout."""
+
+import numpy as np
+import pytest
+import torch
+
+import ilqr_native as nat
+import ilqr_workload as wl
+from parity import case_kwargs, load
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+DIAG_BIT = 8
+NEED = ("x0", "C", "c", "C_final", "c_final", "x_ref", "u_ref")
+
+
+def g(a, dtype=torch.float32):
+    return None if a is None else torch.as_tensor(np.ascontiguousarray(a)).to(DEV, dtype)
+
+
+def _eq(a, b, key):
+    a, b = a.cpu().numpy(), b.cpu().numpy()
+    if key == "status":
+        a, b = a & ~DIAG_BIT, b & ~DIAG_BIT
+    assert a.shape == b.shape, key
+    assert np.array_equal(a, b, equal_nan=a.dtype.kind == "f"), key
+
+
+def _both(monkeypatch, fn):
+    out = {}
+    for layout in ("team", "pair"):
+        monkeypatch.setenv("ILQR_B200_LAYOUT", layout)
+        out[layout] = fn()
+        torch.cuda.synchronize()
+    monkeypatch.delenv("ILQR_B200_LAYOUT")
+    return out["team"], out["pair"]
+
+
+def _solve_and_backward(d, kw, forced=None, time_major=False):
+    C, c = g(d["C"]), g(d["c"])
+    gX, gU = g(d["gX"]), g(d["gU"])
+    if time_major:
+        C, c = C.transpose(0, 1).contiguous(), c.transpose(0, 1).contiguous()
+    s = nat.solve(g(d["x0"]), g(d["U_init"]), C, c, g(kw["C_f"]), g(kw["c_f"]), g(kw["x_ref"]), g(kw["u_ref"]),
+                  g(kw["u_min"]), g(kw["u_max"]), dt=kw["dt"], max_iter=kw["max_iter"], reg_eps=kw["reg"],
+                  alphas=kw["alphas"], forced_trace=g(forced, torch.int8), want_trace=True, want_stats=True,
+                  time_major=time_major)
+    r = nat.backward(s["X"], s["U"], C, gX, gU, C_final=g(kw["C_f"]), x_ref=g(kw["x_ref"]),
+                     u_ref=g(kw["u_ref"]), tight=s["tight"], dt=kw["dt"], reg_eps=kw["reg"],
+                     need=NEED if kw["C_f"] is not None or kw["x_ref"] is not None else ("x0", "C", "c"),
+                     time_major=time_major)
+    return s, r
+
+
+def _check(a, b):
+    (sa, ra), (sb, rb) = a, b
+    assert set(sa) == set(sb)
+    for k in sa:
+        _eq(sa[k], sb[k], k)
+    for k in ra:
+        _eq(ra[k], rb[k], "grad_" + k)
+
+
+@pytest.mark.parametrize("name", ["cfg1_b16_t5", "cfg3_b16_t20", "dense_b8_t6", "asym_b8_t4", "nobox_b8_t5",
+                                  "indef_b8_t4", "b1_t1"])
+def test_golden_cases_same_bits(monkeypatch, name):
+    d = load(name)
+    kw = case_kwargs(d)
+    _check(*_both(monkeypatch, lambda: _solve_and_backward(d, kw)))
+
+
+@pytest.mark.parametrize("time_major", [False, True])
+def test_odd_training_batch_same_bits(monkeypatch, time_major):
+    """B = 45 at the training-scale horizon: the last warp of either layout is
+    ragged, and one element starts at an infinite position."""
+    cfg, inp = wl.config_inputs("rollout_b16384_t20", B=45)
+    inp["x0"][31, 0] = np.inf
+    gX, gU = wl.make_backward_seeds(45, cfg["T"])
+    d = dict(inp, gX=gX, gU=gU)
+    kw = dict(C_f=None, c_f=None, x_ref=None, u_ref=None, u_min=wl.U_MIN, u_max=wl.U_MAX, dt=wl.DT,
+              max_iter=cfg["max_iter"], reg=wl.REG_EPS, alphas=cfg["alphas"])
+    team, pair = _both(monkeypatch, lambda: _solve_and_backward(d, kw, time_major=time_major))
+    _check(team, pair)
+    assert not np.isfinite(pair[0]["X"][31].cpu().numpy()).all()
+
+
+@pytest.mark.parametrize("forced", [False, True])
+def test_seven_step_sizes_same_bits(monkeypatch, forced):
+    d = dict(load("cfg3_b16_t20"))
+    kw = case_kwargs(d)
+    kw["alphas"] = (1.0, 0.8, 0.6, 0.5, 0.3, 0.2, 0.1)
+    trace = None
+    if forced:
+        trace = np.tile(np.array([[5, 6, 0, -1, 6]], np.int8), (16, 1))[:, : kw["max_iter"]]
+    _check(*_both(monkeypatch, lambda: _solve_and_backward(d, kw, forced=trace)))
+
+
+def test_sigmoid_costs_same_bits(monkeypatch):
+    d = load("sigmoid_b16_t10")
+    spec = nat.SigmoidCostSpec(float(d["cost_eps"]), float(d["range_q"]), float(d["range_p"]),
+                               range_pt=float(d["range_pt"]))
+    sc = g(d["sigmoid_cost"])
+    lo, hi = g(wl.U_MIN), g(wl.U_MAX)
+
+    def run():
+        s = nat.solve_sigmoid(g(d["x0"]), g(d["U_init"]), sc, spec, lo, hi, dt=float(d["dt"]),
+                              max_iter=int(d["max_iter"]), reg_eps=float(d["reg"]),
+                              alphas=tuple(float(a) for a in d["alphas"]), want_trace=True, want_stats=True)
+        r = nat.backward_sigmoid(s["X"], s["U"], sc, g(d["gX"]), g(d["gU"]), spec, tight=s["tight"],
+                                 dt=float(d["dt"]), reg_eps=float(d["reg"]))
+        return s, r
+
+    _check(*_both(monkeypatch, run))
+
+
+def test_default_layout_by_batch(monkeypatch):
+    """The default picks the pair layout up to PAIR_MAX_B and the team layout
+    above; the first elements of a batch just above the limit equal those of
+    a batch just below it (prefix independence across the two layouts)."""
+    cfg, inp = wl.config_inputs("rollout_b16384_t20", B=2052)
+    t = {k: g(v) for k, v in inp.items()}
+    kw = dict(dt=wl.DT, max_iter=cfg["max_iter"], alphas=cfg["alphas"], want_trace=True)
+    lo, hi = g(wl.U_MIN), g(wl.U_MAX)
+    big = nat.solve(t["x0"], t["U_init"], t["C"], t["c"], None, None, None, None, lo, hi, **kw)
+    small = nat.solve(*(t[k][:2048].contiguous() for k in ("x0", "U_init", "C", "c")), None, None, None, None,
+                      lo, hi, **kw)
+    for k in ("X", "U", "tight", "trace"):
+        assert torch.equal(big[k][:2048], small[k]), k

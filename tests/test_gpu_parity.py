@@ -302,12 +302,15 @@ def test_training_scale_properties(B, T, iters):
         assert torch.equal(2 * g1[k], g2[k]), k
 
 
-def test_diag_cost_cache_identical_to_dense_path(monkeypatch):
+@pytest.mark.parametrize("layout", ["team", "pair"])
+def test_diag_cost_cache_identical_to_dense_path(monkeypatch, layout):
     """Diagonal C blocks are detected in the first pass and later passes read
     only their diagonals. Every result must equal the dense path's
-    (ILQR_B200_DIAG_CACHE=0): here with one warp of six elements holding a
-    single off-diagonal entry (that warp stays dense) and one element that
-    starts at an infinite position (the quadratic form's 0 * inf = NaN rule)."""
+    (ILQR_B200_DIAG_CACHE=0): here with one warp (six elements in the team
+    layout, two in the pair layout) holding a single off-diagonal entry (that
+    warp stays dense) and one element that starts at an infinite position (the
+    quadratic form's 0 * inf = NaN rule)."""
+    monkeypatch.setenv("ILQR_B200_LAYOUT", layout)
     cfg, inp = wl.config_inputs("rollout_b16384_t20", B=96)
     inp["C"][7, 3, 2, 5] = inp["C"][7, 3, 5, 2] = np.float32(1e-3)
     inp["x0"][20, 0] = np.inf
@@ -320,7 +323,7 @@ def test_diag_cost_cache_identical_to_dense_path(monkeypatch):
     diag_bit = 8
     assert not (off["status"] & diag_bit).any()
     warp_dense = np.zeros(96, bool)
-    warp_dense[6:12] = True
+    warp_dense[6:12 if layout == "team" else 8] = True
     assert ((on["status"] & diag_bit) != 0).tolist() == (~warp_dense).tolist()
     assert not np.isfinite(off["X"][20]).all()
     for k in on:
