@@ -1,10 +1,13 @@
 """Batch sharding across ranks (one process per GPU).
 
 Batch elements are independent iLQR problems, so rank r of W solves the
-contiguous slice [lo, hi) of the batch with no communication; the only
-collective is one all-gather of the first controls U[:, 0, :] (the actions
-the policy consumes) after the solve, through torch.distributed (NCCL on
-GPUs, gloo on CPU).
+contiguous slice [lo, hi) of the batch with no communication. After the
+solve, the results the caller consumes are gathered over torch.distributed
+(NCCL on GPUs, gloo on CPU): the first controls U[:, 0, :] (the actions the
+policy steps with) and, after the backward, the gradients (dL/dx0 by
+default; dL/dc or dL/dC on request). The reference has no multi-GPU path; its
+caller solves the whole batch in one process
+(acmpc_public-master/training_modules/mlp_mpc_policy_diffmpc.py:324-399).
 """
 
 from __future__ import annotations
@@ -22,18 +25,36 @@ def shard_bounds(B: int, rank: int, world: int):
     return lo, hi
 
 
-def gather_first_actions(U_local: torch.Tensor, B: int, group=None) -> torch.Tensor:
-    """All-gather U_local[:, 0, :] from every rank into a [B, nu] tensor
-    (shards padded to equal length for all_gather_into_tensor)."""
+def gather_rows(x_local: torch.Tensor, B: int, group=None) -> torch.Tensor:
+    """All-gather the per-element rows x_local [hi - lo, ...] of every rank's
+    shard into one [B, ...] tensor, in batch order. Shards are padded to
+    equal length for all_gather_into_tensor; every rank receives the result
+    (rank 0 is the consumer)."""
     world = dist.get_world_size(group)
-    nu = U_local.shape[-1]
+    tail = tuple(x_local.shape[1:])
+    width = 1
+    for d in tail:
+        width *= d
     per = (B + world - 1) // world
-    buf = torch.zeros(per, nu, device=U_local.device, dtype=U_local.dtype)
-    buf[: U_local.shape[0]] = U_local[:, 0, :]
-    out = torch.empty(per * world, nu, device=U_local.device, dtype=U_local.dtype)
+    buf = torch.zeros(per, width, device=x_local.device, dtype=x_local.dtype)
+    buf[: x_local.shape[0]] = x_local.reshape(x_local.shape[0], width)
+    out = torch.empty(per * world, width, device=x_local.device, dtype=x_local.dtype)
     dist.all_gather_into_tensor(out, buf, group=group)
     parts = []
     for r in range(world):
         lo, hi = shard_bounds(B, r, world)
         parts.append(out[r * per: r * per + (hi - lo)])
-    return torch.cat(parts, 0)
+    return torch.cat(parts, 0).reshape((B,) + tail)
+
+
+def gather_first_actions(U_local: torch.Tensor, B: int, group=None) -> torch.Tensor:
+    """All-gather U_local[:, 0, :] from every rank into a [B, nu] tensor."""
+    return gather_rows(U_local[:, 0, :], B, group)
+
+
+def gather_gradients(grads: dict, B: int, keys=("x0",), group=None) -> dict:
+    """All-gather the per-element gradients `keys` of a rank's backward
+    (the dict ilqr_native.backward returns, batch-major) into [B, ...]
+    tensors: dL/dx0 [B, 10] by default, "c" [B, T, 14] or "C" [B, T, 14, 14]
+    when the consumer lives on rank 0."""
+    return {k: gather_rows(grads[k], B, group) for k in keys}

@@ -1,7 +1,8 @@
 """Multi-rank batch sharding on CPU (gloo, world size 2): each rank solves its
-contiguous shard with the oracle, the first actions are all-gathered with the
-same helper the GPU benchmark uses, and the gathered result equals the
-single-process solve bit for bit (batch elements are independent)."""
+contiguous shard with the oracle and runs the backward, the first actions
+and the gradients (dL/dx0, dL/dc) are all-gathered with the same helpers the
+GPU benchmark uses, and the gathered results equal the single-process solve
+and backward bit for bit (batch elements are independent)."""
 
 import os
 import socket
@@ -39,8 +40,13 @@ def _worker(rank, world, port, B, T, q):
         r = O.solve(inp["x0"][lo:hi], inp["U_init"][lo:hi], inp["C"][lo:hi], inp["c"][lo:hi],
                     u_min=wl.U_MIN, u_max=wl.U_MAX, dt=wl.DT, max_iter=3)
         acts = sh.gather_first_actions(torch.from_numpy(r["U"]), B)
+        gX, gU = wl.make_backward_seeds(B, T)
+        gr = O.backward(r["X"], r["U"], inp["C"][lo:hi], None, None, None, r["tight"], gX[lo:hi], gU[lo:hi],
+                        wl.DT, wl.REG_EPS)
+        gg = sh.gather_gradients({"x0": torch.from_numpy(gr["grad_x0"]), "c": torch.from_numpy(gr["grad_c"])},
+                                 B, keys=("x0", "c"))
         if rank == 0:
-            q.put(acts.numpy())
+            q.put((acts.numpy(), gg["x0"].numpy(), gg["c"].numpy()))
     finally:
         dist.destroy_process_group()
 
@@ -64,7 +70,7 @@ def test_gloo_two_ranks_match_single_process(B):
     procs = [ctx.Process(target=_worker, args=(r, 2, port, B, T, q)) for r in range(2)]
     for p in procs:
         p.start()
-    got = q.get(timeout=300)
+    got, gx0, gc = q.get(timeout=300)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
@@ -72,3 +78,8 @@ def test_gloo_two_ranks_match_single_process(B):
     ref = O.solve(inp["x0"], inp["U_init"], inp["C"], inp["c"], u_min=wl.U_MIN, u_max=wl.U_MAX,
                   dt=wl.DT, max_iter=3)
     assert np.array_equal(got, ref["U"][:, 0, :])
+    gX, gU = wl.make_backward_seeds(B, T)
+    gr = O.backward(ref["X"], ref["U"], inp["C"], None, None, None, ref["tight"], gX, gU, wl.DT, wl.REG_EPS)
+    assert gx0.shape == (B, 10) and gc.shape == (B, T, 14)
+    assert np.array_equal(gx0, gr["grad_x0"])
+    assert np.array_equal(gc, gr["grad_c"])
