@@ -4,21 +4,30 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 One step = one forward solve (all iLQR iterations) plus the implicit-diff
-backward of a batch of 16384 quadrotor MPC problems with horizon 20 and
-5 iterations (the training-scale rollout workload), each GPU solving its own
-batch (weak scaling; for N > 1 the first actions are all-gathered over NCCL
-inside the step). Prints one JSON line on rank 0.
+backward of a global batch of 16384 quadrotor MPC problems with horizon 20
+and 5 iterations (the training-scale rollout workload). With N ranks the
+batch is sharded by rank (rank r solves the contiguous slice
+shard_bounds(16384, r, N)) and the first actions and dL/dx0 are all-gathered
+over NCCL inside the step (strong scaling). Rank 0 prints one JSON line; the
+larger sections (rotor13 model, FastMPC numerics, sigmoid costs, policy
+actor step) go to earlier lines that start with "#section".
 
-  value  whole-job solves/s with inputs resident in HBM (device time, max over
-         ranks); inputs (257 MB of cost blocks per GPU) exceed the 126 MB L2.
+  value  global-batch solves/s with inputs resident in HBM (device time, max
+         over ranks); the cost blocks (257 MB) exceed the 126 MB L2.
   e2e    the same through the reference-facing operator
          (mpc_compat.MPC(...)(x_init, QuadCost(C, c), dx) + autograd backward)
          with host buffers: every step copies its inputs from pinned host
          memory and reads the actions and dL/dx0 back.
-  --impl reference: the reference's CPU algorithm (the CPU oracle, a numpy
-         restatement of DiffMPC) on all host cores, over a bounded sample.
+  cpu_baseline  the reference DiffMPC solver itself (staged from the
+         reference's sources into oracle/_ref/diffmpc) on the host cores,
+         one process per core, over a bounded sample; the numpy port of it
+         beside it.
+  fastmpc_ref_cuda  the reference FastMPC extension's own CUDA kernels
+         (oracle/_ref/libfastmpc_ref.so) through a torch restatement of its
+         host loop, on the same inputs and GPU.
+  --impl reference: the reference's CPU solver on all host cores (DiffMPC
+         itself when staged, else the numpy port), over a bounded sample.
 """
-
 from __future__ import annotations
 
 import argparse
@@ -59,7 +68,13 @@ def _args():
                          "(both models, 1 GPU, device-resident)")
     ap.add_argument("--latency-reps", type=int, default=200)
     ap.add_argument("--batch", type=int, default=None,
-                    help="elements per GPU (default: the workload's 16384); for profiling runs")
+                    help="global batch (default: the workload's 16384); for profiling runs")
+    ap.add_argument("--no-ref-baselines", action="store_true",
+                    help="skip the reference FastMPC CUDA build and the DiffMPC CPU baseline")
+    ap.add_argument("--no-weak", action="store_true",
+                    help="skip the weak-scaling figure (16384 elements per rank) of runs with N > 1")
+    ap.add_argument("--no-inference", action="store_true",
+                    help="skip the sharded inference configuration (B=262144, T=10) of runs with N > 1")
     return ap.parse_args()
 
 
@@ -153,11 +168,24 @@ class Clocks:
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline: the oracle (numpy restatement of DiffMPC) over host cores
+# Shared config and the reference's CPU solver (baseline leg, reference arm)
 # ---------------------------------------------------------------------------
-def cpu_oracle_rate(workers: int, chunk: int = 1024, reps: int = 1):
+def headline_config(world: int):
+    """The config object of the benchmark line, shared by both arms."""
+    import ilqr_workload as wl
+    cfg = wl.CONFIGS[WORKLOAD]
+    return {"workload": WORKLOAD, "B": cfg["B"], "T": cfg["T"], "iters": cfg["max_iter"],
+            "alphas": list(cfg["alphas"]), "dt": wl.DT, "control_box": True,
+            "parallelism": f"batch sharded by rank over {world}",
+            "l2": "inputs > L2 (C 257 MB), no flush"}
+
+
+def cpu_rate(impl: str, workers: int, chunk: int, reps: int = 1):
+    """Element solves/s of the reference's CPU solver ("reference": DiffMPC
+    itself, "port": its numpy restatement) over `workers` spawned processes
+    of `chunk` elements each (best of `reps`)."""
     from oracle.cpu_pool import OraclePool
-    pool = OraclePool(workers, ROOT, PKG)
+    pool = OraclePool(workers, ROOT, PKG, impl)
     try:
         best = None
         for _ in range(reps):
@@ -168,15 +196,26 @@ def cpu_oracle_rate(workers: int, chunk: int = 1024, reps: int = 1):
         pool.close()
 
 
+def diffmpc_staged() -> bool:
+    from oracle import diffmpc_ref
+    return diffmpc_ref.available()
+
+
 def run_reference(args):
+    """The reference's own CPU implementation of the path on the host cores:
+    DiffMPC itself (one single-threaded process per core, 256-element chunks)
+    when its sources are staged in oracle/_ref/diffmpc, else the numpy port.
+    Only rank 0 works; the other ranks exit."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     import ilqr_workload as wl
     cores = len(os.sched_getaffinity(0))
     from oracle.cpu_pool import OraclePool
-    pool = OraclePool(cores, ROOT, PKG)
-    chunk = 1024
+    impl = "reference" if diffmpc_staged() else "port"
+    chunk = 256 if impl == "reference" else 1024
+    pool = OraclePool(cores, ROOT, PKG, impl)
     try:
         for _ in range(args.warmup):
             pool.run(WORKLOAD, cores, chunk)
@@ -190,17 +229,16 @@ def run_reference(args):
     cfg = wl.CONFIGS[WORKLOAD]
     step = statistics.mean(times)
     value = n / step
-    sample = (f"{n} of {cfg['B']} elements per step ({cores} workers x {chunk}), T={cfg['T']}, "
-              f"{cfg['max_iter']} iterations, fwd+bwd")
+    what = "DiffMPC itself" if impl == "reference" else "numpy port of DiffMPC"
+    sample = f"{n} of {cfg['B']} elements/step, {cores} procs x {chunk}, {what}"
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "solves/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": step * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, reference value ranges)",
-        "config": {"workload": WORKLOAD, "B": cfg["B"], "T": cfg["T"], "iters": cfg["max_iter"],
-                   "alphas": list(cfg["alphas"]), "control_box": True},
-        "cpu_baseline": {"value": value, "unit": "solves/s", "cores": cores, "kind": "port",
-                         "sample": sample},
+        "ms_per_step": step * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+        "config": headline_config(world),
+        "cpu_baseline": {"value": value, "unit": "solves/s", "cores": cores,
+                         "kind": "reference" if impl == "reference" else "port", "sample": sample},
         "e2e": {"value": value, "unit": "solves/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -309,6 +347,57 @@ def bind_to_gpu_numa_node(torch, dev_index):
         return None
 
 
+def shard_inputs(wl, B_glob, T, lo, hi, cfg, seed=0):
+    """Inputs of elements [lo, hi) of the seeded global batch (the block
+    generators make any 1024-aligned slice directly; other slices are cut
+    from the generated prefix)."""
+    if lo % wl.BLOCK == 0:
+        return wl.make_inputs(hi - lo, T, seed=seed, target=cfg["target"], r=cfg["r"], offset=lo)
+    full = wl.make_inputs(hi, T, seed=seed, target=cfg["target"], r=cfg["r"])
+    return {k: v[lo:hi] for k, v in full.items()}
+
+
+def kernel_source_sha(names):
+    """Short hash of the kernel sources a committed profile describes."""
+    import hashlib
+    h = hashlib.sha256()
+    for n in names:
+        with open(os.path.join(PKG, "csrc", n), "rb") as f:
+            h.update(f.read())
+    return h.hexdigest()[:16]
+
+
+def solve_variant(B: int) -> str:
+    """The solve kernel a batch of B elements launches (the library's own
+    choice): the pair layout up to 2048 elements, else the team layout's
+    register tier, the fattest whose residency fits the grid in one wave."""
+    if B <= 2048:
+        return "pair"
+    grid = (B + 5) // 6
+    tier = 8 if grid <= 148 * 8 else (12 if grid <= 148 * 12 else 19)
+    return f"team_tier{tier}"
+
+
+SOLVE_SOURCES = ("ilqr_solve.cu", "ilqr_team.cuh", "ilqr_pair.cuh", "ilqr_device.cuh")
+
+
+def committed_traffic(variant: str, B: int, T: int):
+    """DRAM bytes per launch of this solve variant from the committed ncu
+    summary (profiles/solve_kernel_traffic.json), scaled to B elements. Only
+    returned while the kernel sources still hash to the captured ones; else
+    (None, why)."""
+    try:
+        prof = json.load(open(os.path.join(ROOT, "profiles", "solve_kernel_traffic.json")))
+    except Exception:
+        return None, "no committed capture"
+    e = prof.get(f"{variant}_t{T}")
+    if e is None:
+        return None, f"no capture of {variant} at T={T}"
+    if e.get("source_sha") != kernel_source_sha(SOLVE_SOURCES):
+        return None, f"capture of {variant} is stale (kernel sources changed)"
+    return e["dram_bytes_per_launch"] * B / e["B"], f"{e['summary']} (B={e['B']}, scaled per element)"
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -333,13 +422,17 @@ def run_ours(args):
                                 device_id=dev)
 
     cfg = wl.CONFIGS[WORKLOAD]
-    B, T, iters, alphas = cfg["B"], cfg["T"], cfg["max_iter"], cfg["alphas"]
+    B_glob, T, iters, alphas = cfg["B"], cfg["T"], cfg["max_iter"], cfg["alphas"]
     if args.batch is not None:
-        B = args.batch
-    inp = wl.make_inputs(B, T, seed=rank, target=cfg["target"], r=cfg["r"])
-    gXn, gUn = wl.make_backward_seeds(B, T, seed=1 + rank)
-    d = {k: torch.from_numpy(v).to(dev) for k, v in inp.items()}
-    gX, gU = torch.from_numpy(gXn).to(dev), torch.from_numpy(gUn).to(dev)
+        B_glob = args.batch
+    # The global batch is one seeded set of problems; rank r solves the
+    # contiguous slice shard_bounds(B_glob, r, world) of it.
+    s_lo, s_hi = ilqr_shard.shard_bounds(B_glob, rank, world)
+    B = s_hi - s_lo
+    inp = shard_inputs(wl, B_glob, T, s_lo, s_hi, cfg)
+    gXn, gUn = (a[s_lo:s_hi] for a in wl.make_backward_seeds(B_glob, T, seed=1))
+    d = {k: torch.from_numpy(np.ascontiguousarray(v)).to(dev) for k, v in inp.items()}
+    gX, gU = torch.from_numpy(np.ascontiguousarray(gXn)).to(dev), torch.from_numpy(np.ascontiguousarray(gUn)).to(dev)
     lo, hi = torch.from_numpy(wl.U_MIN).to(dev), torch.from_numpy(wl.U_MAX).to(dev)
 
     stream = torch.cuda.current_stream(dev)
@@ -357,7 +450,11 @@ def run_ours(args):
         if timing is not None:
             timing[2].record(stream)
         if world > 1:
-            ilqr_shard.gather_first_actions(out["U"], B * world)
+            # actions and dL/dx0 of every shard to rank 0 (all-gather over NCCL)
+            ilqr_shard.gather_first_actions(out["U"], B_glob)
+            ilqr_shard.gather_gradients(g, B_glob, keys=("x0",))
+        if timing is not None:
+            timing[3].record(stream)
         return out, g
 
     def barrier():
@@ -365,11 +462,18 @@ def run_ours(args):
             dist.barrier()
         torch.cuda.synchronize()
 
+    def max_over_ranks(x):
+        if world > 1:
+            t = torch.tensor([x], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+        return x
+
     # ---- device-resident throughput ---------------------------------------
     for _ in range(max(3, args.warmup)):
         step()
     barrier()
-    timings = [(ev(), ev(), ev()) for _ in range(args.steps)]
+    timings = [(ev(), ev(), ev(), ev()) for _ in range(args.steps)]
     t_start, t_end = ev(), ev()
     with Clocks(local, gpu_pci_bus_id(torch, dev.index)) as clk:
         barrier()
@@ -378,15 +482,12 @@ def run_ours(args):
             step(timings[i])
         t_end.record(stream)
         barrier()
-    elapsed = t_start.elapsed_time(t_end) * 1e-3
-    solve_ms = [a.elapsed_time(b) for a, b, _ in timings]
-    bwd_ms = [b.elapsed_time(c) for _, b, c in timings]
-    if world > 1:
-        t = torch.tensor([elapsed], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed = float(t.item())
+    elapsed = max_over_ranks(t_start.elapsed_time(t_end) * 1e-3)
+    solve_ms = [a.elapsed_time(b) for a, b, _, _ in timings]
+    bwd_ms = [b.elapsed_time(c) for _, b, c, _ in timings]
+    gather_ms = max_over_ranks(statistics.mean(c.elapsed_time(e) for _, _, c, e in timings))
     per_step = elapsed / args.steps
-    value = world * B / per_step
+    value = B_glob / per_step
 
     # ---- algorithmic counts for the roofline (same inputs -> same iterations)
     st = nat.solve(d["x0"], d["U_init"], d["C"], d["c"], None, None, None, None, lo, hi, dt=wl.DT,
@@ -409,17 +510,12 @@ def run_ours(args):
     hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
     t_solve = statistics.mean(solve_ms) * 1e-3
     t_bwd = statistics.mean(bwd_ms) * 1e-3
-    traffic, traffic_src = None, None
-    try:
-        prof = json.load(open(os.path.join(ROOT, "profiles", "solve_kernel_traffic.json")))
-        traffic = prof.get(WORKLOAD, {}).get("dram_bytes_per_launch")
-        traffic_src = prof.get(WORKLOAD, {}).get("source")
-    except Exception:
-        pass
+    variant = solve_variant(B)
+    traffic, traffic_note = committed_traffic(variant, B, T)
     roofline = {
-        "bound": "fp32", "kernel": "solve_kernel (fused forward iLQR)",
+        "bound": "fp32", "kernel": f"solve ({variant})",
         "achieved": f_solve / t_solve / 1e12, "peak": peak_fp32, "unit": "TFLOP/s",
-        "frac": f_solve / t_solve / 1e12 / peak_fp32, "traffic": traffic, "traffic_source": traffic_src,
+        "frac": f_solve / t_solve / 1e12 / peak_fp32, "traffic": traffic, "traffic_source": traffic_note,
         "peak_source": "measured FMA probe on this GPU (no FP32 figure in MEASURED_PEAKS.json)",
         "algorithmic_flops_per_launch": f_solve, "mean_launch_ms": t_solve * 1e3,
         "flop_count": "dense per-unit counts: T [I (10.3k + 0.66k n_alpha) + 1.0k] per element (ilqr_costmodel)",
@@ -446,8 +542,8 @@ def run_ours(args):
         h_c = pin(np.transpose(inp["c"], (1, 0, 2)))
         h_gX = pin(np.transpose(gXn, (1, 0, 2)))
         h_gU = pin(np.transpose(gUn, (1, 0, 2)))
-        h_act = torch.empty(B * world, 4).pin_memory()
-        h_gx0 = torch.empty(B, 10).pin_memory()
+        h_act = torch.empty(B_glob, 4).pin_memory()
+        h_gx0 = torch.empty(B_glob, 10).pin_memory()
         mpc = mpc_compat.MPC(10, 4, T, u_lower=lo.view(1, 1, 4).expand(T, 1, 4),
                              u_upper=hi.view(1, 1, 4).expand(T, 1, 4), lqr_iter=iters,
                              eps=wl.REG_EPS, alphas=alphas)
@@ -462,10 +558,12 @@ def run_ours(args):
             x, u, _ = mpc(x0, mpc_compat.QuadCost(C, c), dyn)
             ((x * gx).sum() + (u * gu).sum()).backward()
             act = u[0].detach()
+            gx0 = x0.grad
             if world > 1:
-                act = ilqr_shard.gather_first_actions(u.detach().permute(1, 0, 2).contiguous(), B * world)
+                act = ilqr_shard.gather_first_actions(u.detach().permute(1, 0, 2).contiguous(), B_glob)
+                gx0 = ilqr_shard.gather_rows(gx0, B_glob)
             h_act.copy_(act, non_blocking=True)
-            h_gx0.copy_(x0.grad, non_blocking=True)
+            h_gx0.copy_(gx0, non_blocking=True)
 
         for _ in range(max(3, args.warmup)):
             e2e_step()
@@ -492,10 +590,12 @@ def run_ours(args):
             x, u, _ = mpc(x0, mpc_compat.QuadCost(C, c), dyn)
             ((x * bgx).sum() + (u * bgu).sum()).backward()
             act = u[0].detach()
+            gx0 = x0.grad
             if world > 1:
-                act = ilqr_shard.gather_first_actions(u.detach().permute(1, 0, 2).contiguous(), B * world)
+                act = ilqr_shard.gather_first_actions(u.detach().permute(1, 0, 2).contiguous(), B_glob)
+                gx0 = ilqr_shard.gather_rows(gx0, B_glob)
             h_act.copy_(act, non_blocking=True)
-            h_gx0.copy_(x0.grad, non_blocking=True)
+            h_gx0.copy_(gx0, non_blocking=True)
 
         el = time_streaming(torch, dev, stream, host, e2e_compute, max(3, args.warmup), args.steps, barrier)
 
@@ -522,14 +622,14 @@ def run_ours(args):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             el = float(t.item())
         h2d = sum(t.numel() * 4 for t in host)
-        e2e = {"value": world * B / (el / args.steps), "unit": "solves/s",
+        e2e = {"value": B_glob / (el / args.steps), "unit": "solves/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": (h_act.numel() + h_gx0.numel()) * 4,
                "ms_per_step": el / args.steps * 1e3,
                "path": "mpc_compat.MPC(...)(x_init, QuadCost(C, c), dx) + autograd backward",
                "streaming": "inputs of step k+1 copied on a second stream while step k computes (double buffer)",
-               "sequential": {"value": world * B / (el_seq / args.steps), "ms_per_step": el_seq / args.steps * 1e3,
+               "sequential": {"value": B_glob / (el_seq / args.steps), "ms_per_step": el_seq / args.steps * 1e3,
                               "note": "copies and compute of each step back to back on one stream"},
-               "operator_device_resident": {"value": world * B / (el_dev / args.steps),
+               "operator_device_resident": {"value": B_glob / (el_dev / args.steps),
                                             "ms_per_step": el_dev / args.steps * 1e3,
                                             "note": "the same operator call and backward on device tensors"}}
 
@@ -588,7 +688,7 @@ def run_ours(args):
     # Same batch, horizon, iterations and model; the costs are the diagonal
     # ones the policy builds from its sigmoid output, built inside the kernels.
     sig = None
-    if not args.no_sigmoid:
+    if not args.no_sigmoid and world == 1:
         rng = np.random.default_rng(100 + rank)
         scn = (1.0 / (1.0 + np.exp(-rng.normal(0.0, 1.5, (B, 28 * T))))).astype(np.float32)
         sc = torch.from_numpy(scn).to(dev)
@@ -690,7 +790,7 @@ def run_ours(args):
     # built with a Python loop over t, one host read per chunk. Both run on
     # this solver, without gradients (evaluation), rank 0 only.
     actor = None
-    if rank == 0 and not args.no_sigmoid:
+    if rank == 0 and not args.no_sigmoid and world == 1:
         import policy_mpc
         pm = policy_mpc.PolicyMPC(T, wl.DT, lqr_iter=iters, eps=wl.REG_EPS, alphas=alphas, device=dev)
         sc_all = sc
@@ -755,7 +855,7 @@ def run_ours(args):
     # The benchmark configurations' rigid body (four rotor thrusts in [0, 1]),
     # same batch, horizon, iterations and step sizes, dense C [B,T,17,17].
     r13 = None
-    if not args.no_rotor13:
+    if not args.no_rotor13 and world == 1:
         ri = wl.make_rotor13_inputs(B, T, seed=rank, target=cfg["target"], r=cfg["r"])
         rd = {k: torch.from_numpy(v).to(dev) for k, v in ri.items()}
         rgXn, rgUn = wl.make_backward_seeds(B, T, seed=1 + rank, nx=wl.NX13)
@@ -900,7 +1000,7 @@ def run_ours(args):
     # convergence. Device-resident solve + backward, then the operator call
     # MPC(..., numerics="fastmpc") with autograd on the same device tensors.
     fmr = None
-    if not args.no_fastmpc:
+    if not args.no_fastmpc and world == 1:
         fm_alphas = nat.FASTMPC_ALPHAS
         fm_tim = [(ev(), ev(), ev()) for _ in range(args.steps)]
         fm_info = []
@@ -970,42 +1070,138 @@ def run_ours(args):
                                             "ms_per_step": fop / args.steps * 1e3,
                                             "path": "mpc_compat.MPC(..., numerics='fastmpc') + autograd"}}
 
-    # ---- CPU baseline (rank 0, N=1) ------------------------------------------
-    cpu = None
+    # ---- weak scaling: every rank its own 16384 elements (N > 1) ----------------
+    weak = None
+    if world > 1 and not args.no_weak:
+        Bw = cfg["B"]
+        wi = wl.make_inputs(Bw, T, seed=100 + rank, target=cfg["target"], r=cfg["r"])
+        wd = {k: torch.from_numpy(v).to(dev) for k, v in wi.items()}
+        wgX, wgU = (torch.from_numpy(a).to(dev) for a in wl.make_backward_seeds(Bw, T, seed=200 + rank))
+
+        def wstep():
+            o = nat.solve(wd["x0"], wd["U_init"], wd["C"], wd["c"], None, None, None, None, lo, hi,
+                          dt=wl.DT, max_iter=iters, reg_eps=wl.REG_EPS, alphas=alphas)
+            gw = nat.backward(o["X"], o["U"], wd["C"], wgX, wgU, tight=o["tight"], dt=wl.DT,
+                              reg_eps=wl.REG_EPS, need=("x0", "C", "c"))
+            ilqr_shard.gather_first_actions(o["U"], Bw * world)
+            ilqr_shard.gather_gradients(gw, Bw * world, keys=("x0",))
+
+        for _ in range(max(3, args.warmup)):
+            wstep()
+        barrier()
+        e0, e1 = ev(), ev()
+        e0.record(stream)
+        for _ in range(args.steps):
+            wstep()
+        e1.record(stream)
+        barrier()
+        wel = max_over_ranks(e0.elapsed_time(e1) * 1e-3) / args.steps
+        weak = {"value": float(f"{world * Bw / wel:.5g}"), "ms": float(f"{wel * 1e3:.4g}"), "B_per_gpu": Bw}
+        del wd, wgX, wgU
+        torch.cuda.empty_cache()
+
+    # ---- the inference configuration sharded over the ranks (N > 1) -------------
+    infer = None
+    if world > 1 and not args.no_inference:
+        c4 = wl.CONFIGS["inference_b262144_t10"]
+        B4, T4 = c4["B"], c4["T"]
+        i_lo, i_hi = ilqr_shard.shard_bounds(B4, rank, world)
+        ii = shard_inputs(wl, B4, T4, i_lo, i_hi, c4)
+        idv = {k: torch.from_numpy(np.ascontiguousarray(v)).to(dev) for k, v in ii.items()}
+
+        def icall():
+            o = nat.solve(idv["x0"], idv["U_init"], idv["C"], idv["c"], None, None, None, None, lo, hi,
+                          dt=wl.DT, max_iter=c4["max_iter"], reg_eps=wl.REG_EPS, alphas=c4["alphas"])
+            return ilqr_shard.gather_first_actions(o["U"], B4)
+
+        for _ in range(3):
+            icall()
+        barrier()
+        reps = 5
+        e0, e1 = ev(), ev()
+        e0.record(stream)
+        for _ in range(reps):
+            icall()
+        e1.record(stream)
+        barrier()
+        iel = max_over_ranks(e0.elapsed_time(e1) * 1e-3) / reps
+        infer = {"value": float(f"{B4 / iel:.5g}"), "ms": float(f"{iel * 1e3:.4g}"), "B": B4, "T": T4,
+                 "iters": c4["max_iter"]}
+        del idv
+        torch.cuda.empty_cache()
+
+    # ---- the reference FastMPC extension's CUDA kernels (rank 0, N=1) ------------
+    fm_ref = None
+    if rank == 0 and world == 1 and not args.no_ref_baselines:
+        from oracle import fastmpc_ref_cuda as fref
+        if fref.available():
+            def fref_step():
+                r_ = fref.solve(d["x0"], d["U_init"], d["C"], d["c"], lo, hi, dt=wl.DT, max_iter=iters,
+                                reg=wl.REG_EPS)
+                fref.backward(r_, gX, gU, reg=wl.REG_EPS)
+
+            for _ in range(2):
+                fref_step()
+            torch.cuda.synchronize()
+            reps = 5
+            e0, e1 = ev(), ev()
+            e0.record(stream)
+            for _ in range(reps):
+                fref_step()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            fms = e0.elapsed_time(e1) / reps
+            fm_ref = {"value": B / (fms * 1e-3), "ms": fms,
+                      "what": "reference FastMPC CUDA kernels (oracle/_ref) via its restated host loop, "
+                              "same inputs, fwd+bwd"}
+
+    # ---- CPU baselines (rank 0, N=1): DiffMPC itself and the numpy port ----------
+    cpu = port = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         os.sched_setaffinity(0, all_cpus)  # the CPU baseline uses every host core
         cores = len(os.sched_getaffinity(0))
-        rate, n, t = cpu_oracle_rate(cores)
-        cpu = {"value": rate, "unit": "solves/s", "cores": cores, "kind": "port",
-               "sample": f"{n} elements of {WORKLOAD} (T={T}, {iters} iterations, fwd+bwd), "
-                         f"{cores} spawned workers x 1024, oracle = numpy restatement of DiffMPC"}
+        rate_p, n_p, _ = cpu_rate("port", cores, 1024)
+        port = {"value": rate_p, "cores": cores, "sample": f"{n_p} elements, {cores} procs x 1024"}
+        if not args.no_ref_baselines and diffmpc_staged():
+            rate, n, _ = cpu_rate("reference", cores, 256)
+            cpu = {"value": rate, "unit": "solves/s", "cores": cores, "kind": "reference",
+                   "sample": f"DiffMPC itself, fwd+bwd, {n} of {B} elements, {cores} procs x 256"}
+        else:
+            cpu = {"value": rate_p, "unit": "solves/s", "cores": cores, "kind": "port",
+                   "sample": f"numpy port, fwd+bwd, {n_p} of {B} elements, {cores} procs x 1024"}
 
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
+    # the bulky sections, each on a line of its own before the benchmark line
+    for name, sec in (("roofline", roofline), ("e2e", e2e), ("latency_b16_t5", lat),
+                      ("policy_sigmoid_cost", sig), ("policy_actor_step", actor), ("rotor13", r13),
+                      ("fastmpc_numerics", fmr)):
+        if sec is not None:
+            print(f"#section {name} " + json.dumps(sec), flush=True)
+    rnd = lambda x, k=4: None if x is None else float(f"{x:.{k}g}")
     line = {
         "metric": METRIC, "value": value, "unit": "solves/s", "n_gpus": world,
         "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": per_step * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded; reference value ranges, dense C stored [B,T,14,14])",
-        "config": {"workload": WORKLOAD, "B_per_gpu": B, "T": T, "iters": iters,
-                   "alphas": list(alphas), "control_box": [wl.U_MIN.tolist(), wl.U_MAX.tolist()],
-                   "dt": wl.DT, "parallelism": f"batch sharded, {world} rank(s)",
-                   "l2": "inputs larger than L2 (C alone 257 MB per GPU), no flush",
-                   "host_affinity": (f"{len(numa_cpus)} CPUs local to the GPU (NVML)" if numa_cpus
-                                     else "unchanged"),
-                   "per_step": "fused solve kernel + fused backward kernel"
-                               + (" + NCCL all-gather of first actions" if world > 1 else "")},
-        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded)",
+        "config": headline_config(world),
+        "roofline": {"bound": "fp32", "achieved": rnd(roofline["achieved"]), "peak": rnd(roofline["peak"]),
+                     "unit": "TFLOP/s", "frac": rnd(roofline["frac"]), "traffic": traffic,
+                     "kernel": roofline["kernel"], "B": B},
+        "cpu_baseline": cpu,
+        "e2e": None if e2e is None else {k: e2e[k] for k in ("value", "unit", "h2d_bytes_per_step",
+                                                             "d2h_bytes_per_step")},
         "gpu_launches": 2 * args.steps, "clocks": clk.summary(),
-        "latency_b16_t5": lat,
-        "policy_sigmoid_cost": sig,
-        "policy_actor_step": actor,
-        "rotor13": r13,
-        "fastmpc_numerics": fmr,
-        "kernel_ms": {"solve_mean": statistics.mean(solve_ms), "backward_mean": statistics.mean(bwd_ms)},
+        "latency_b16_t5_p50_us": None if lat is None else rnd(lat["p50_us"]),
+        "kernel_ms": {"solve": rnd(statistics.mean(solve_ms)), "bwd": rnd(statistics.mean(bwd_ms)),
+                      "gather": rnd(gather_ms) if world > 1 else None},
+        "weak_b16384_per_gpu": weak,
+        "inference_b262144_t10": infer,
+        "fastmpc_ref_cuda": None if fm_ref is None else {"value": rnd(fm_ref["value"]), "ms": rnd(fm_ref["ms"])},
+        "cpu_port": None if port is None else {"value": rnd(port["value"]), "cores": port["cores"]},
     }
     print(json.dumps(line), flush=True)
 

@@ -31,7 +31,7 @@ reference lines:
 
 The reference extension as a whole is not built here (it needs libtorch); its
 CUDA kernels are, from their own sources (oracle/build_fastmpc_ref.py), and the
-GPU tests re-drive them (tests/fastmpc_ref.py). Arithmetic is fp32
+GPU tests re-drive them (oracle/fastmpc_ref_cuda.py). Arithmetic is fp32
 with the reference kernels' operation order: sums in index order, each product
 rounded, divisions exact. (The reference compiles with --use_fast_math, which
 contracts products into fused multiply-adds and makes division approximate,

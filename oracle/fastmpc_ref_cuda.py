@@ -1,4 +1,4 @@
-"""TEST INFRASTRUCTURE ONLY -- the reference FastMPC extension's CUDA build,
+"""TEST AND BASELINE INFRASTRUCTURE ONLY -- the reference FastMPC extension's CUDA build,
 re-executed on the GPU: its own kernels (oracle/_ref/libfastmpc_ref.so, built
 from the reference's sources with its own flags by
 oracle/build_fastmpc_ref.py) driven by a torch restatement of the host code
@@ -15,8 +15,9 @@ around them:
   1066-1123) and drone_implicit_diff_assembly (:1221-1278).
 
 A recorded decision trace can be replayed, as for the oracles. Only the GPU
-parity tests and the fixture generator tests/golden/make_fastmpc_golden.py
-import this module.
+parity tests, the fixture generator tests/golden/make_fastmpc_golden.py and
+the benchmark's reference-baseline leg (which times the existing FastMPC
+CUDA build beside the product) import this module.
 """
 
 from __future__ import annotations

@@ -1,7 +1,7 @@
 """Generate the FastMPC golden fixtures (fm_ref_*.npz) by running the
 reference FastMPC extension's CUDA build: its own kernels, compiled from the
 reference sources into oracle/_ref/libfastmpc_ref.so by
-oracle/build_fastmpc_ref.py, driven by tests/fastmpc_ref.py (the restated host
+oracle/build_fastmpc_ref.py, driven by oracle/fastmpc_ref_cuda.py (the restated host
 loop of drone_ilqr_solve, differentialMPCPerformance/cpp/drone_ilqr_ext.cpp:
 664-1064, and of the operator's CUDA backward, differentialMPCPerformance/
 mpc_compat.py:217-258). Needs a GPU.
@@ -21,9 +21,9 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-sys.path[:0] = [os.path.join(ROOT, "tests"), os.path.join(ROOT, "ca-ac-mpc_b200")]
+sys.path[:0] = [ROOT, os.path.join(ROOT, "tests"), os.path.join(ROOT, "ca-ac-mpc_b200")]
 
-import fastmpc_ref as ref  # noqa: E402
+from oracle import fastmpc_ref_cuda as ref  # noqa: E402
 import ilqr_workload as wl  # noqa: E402
 
 LO = np.array([0.0, -10.0, -10.0, -4.0], np.float32)

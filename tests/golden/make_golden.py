@@ -186,7 +186,7 @@ CASES = {
     "cfg1_b16_t5": ("latency_b16_t5", 16, None, None, None, True, None),
     "cfg2_b32_t10": ("b1024_t10", 32, None, None, None, True, None),
     "cfg3_b16_t20": ("rollout_b16384_t20", 16, None, None, None, True, None),
-    "cfg5_b16_t50": ("stress_b65536_t50", 16, None, None, None, True, None),
+    "cfg5_b64_t50": ("stress_b65536_t50", 64, None, None, None, True, None),
     "dense_b8_t6": (None, 8, 6, 6, (1.0, 0.8, 0.5, 0.2, 0.1), True, "dense"),
     "asym_b8_t4": (None, 8, 4, 5, (1.0, 0.8, 0.5, 0.2, 0.1), True, "asym"),
     "nobox_b8_t5": (None, 8, 5, 6, (1.0, 0.8, 0.5, 0.2, 0.1), False, None),

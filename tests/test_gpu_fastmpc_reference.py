@@ -1,6 +1,6 @@
 """The FastMPC numerics mode against the reference's own CUDA kernels.
 
-tests/fastmpc_ref.py re-executes the reference FastMPC extension's CUDA build
+oracle/fastmpc_ref_cuda.py re-executes the reference FastMPC extension's CUDA build
 on the GPU: its kernels, compiled from the reference sources with its own
 flags (--use_fast_math) into oracle/_ref/, driven by a torch restatement of
 its host loop. The B200 solve records its line-search decisions and batch
@@ -14,7 +14,7 @@ import numpy as np
 import pytest
 import torch
 
-import fastmpc_ref as ref
+from oracle import fastmpc_ref_cuda as ref
 import ilqr_native as nat
 import ilqr_workload as wl
 
@@ -188,7 +188,7 @@ def _rand_lqr(B, T, seed):
 def test_extension_entry_points_match_reference_kernels():
     """The FastMPC extension surface's separate entry points (Jacobian, masked
     adjoint Riccati, assembly) against the reference kernels they replace."""
-    import fastmpc_ref
+    from oracle import fastmpc_ref_cuda as fastmpc_ref
     B, T = 24, 7
     rng = np.random.default_rng(3)
     X = np.zeros((B, T + 1, 10), np.float32)

@@ -109,7 +109,7 @@ def test_chol_fallback_path():
 
 
 def test_long_horizon_never_improving_elements_exact():
-    d = load("cfg5_b16_t50")
+    d = load("cfg5_b64_t50")
     r, _ = gpu_solve(d, forced=d["ref_trace"])
     never = d["ref_trace"].max(axis=1) < 0
     assert max_rel(r["X"][never], d["ref_X"][never]) <= 1e-6
@@ -117,20 +117,38 @@ def test_long_horizon_never_improving_elements_exact():
 
 
 def test_long_horizon_within_conditioning():
-    """T=50, 15 m targets, every element: replaying the reference's decisions,
-    X, U and the gradients at the GPU's solution agree with the reference to
-    the plain bars or to CONDITION_FACTOR times the oracle's own response to
-    1e-7 noise in C, per element."""
+    """T=50, 15 m targets, every element, replaying the reference's decisions.
+    Where the problem is well conditioned (CONDITION_FACTOR times the oracle's
+    own response to 1e-7 noise in C stays below COND_CAP), X, U and the
+    gradients at the GPU's solution agree with the reference to the plain bars
+    or to that multiple of the response, per element. Where it does not, one
+    ulp of noise moves the answer by more than COND_CAP, so no fp32 run pins
+    another: those elements are not compared with the reference's fp32 run but
+    with the oracle's fp64 replay of the same decisions, and the GPU's error
+    there must stay within ROUNDING_FACTOR times the larger fp32 error of the
+    two other realisations of the same arithmetic (the reference's fp32 run
+    and the oracle's)."""
     from parity import CONDITION_FACTOR, diffmpc_condition_spread, rel_per_elem
-    d = load("cfg5_b16_t50")
+    COND_CAP, ROUNDING_FACTOR = 0.05, 30.0
+    d = load("cfg5_b64_t50")
     r, kw = gpu_solve(d, forced=d["ref_trace"])
     gg = gpu_backward(d, r["X"], r["U"], r["tight"], kw)
     sp = diffmpc_condition_spread(d, d["ref_trace"])
+    o32 = O.solve(d["x0"], d["U_init"], d["C"], d["c"], forced=d["ref_trace"], **kw)
+    o64 = O.solve(d["x0"], d["U_init"], d["C"], d["c"], forced=d["ref_trace"], dtype=np.float64, **kw)
     pairs = [("X", r["X"], TOL_XU), ("U", r["U"], TOL_XU)] + [(k, gg[k], TOL_GRAD) for k in GRAD_KEYS]
+    ill = np.zeros(len(d["x0"]), bool)
+    for k, a, tol in pairs:
+        ill |= CONDITION_FACTOR * sp[k] > COND_CAP
     for k, a, tol in pairs:
         err = rel_per_elem(a, d["ref_" + k])
-        bad = np.nonzero(err > np.maximum(tol, CONDITION_FACTOR * sp[k]))[0]
+        bad = np.nonzero(~ill & (err > np.maximum(tol, CONDITION_FACTOR * sp[k])))[0]
         assert bad.size == 0, (k, [(int(b), float(err[b]), float(sp[k][b])) for b in bad])
+    for k in ("X", "U"):
+        e_gpu = rel_per_elem(r[k], o64[k])
+        e_o32 = np.maximum(rel_per_elem(o32[k], o64[k]), rel_per_elem(d["ref_" + k], o64[k]))
+        bad = np.nonzero(ill & (e_gpu > np.maximum(TOL_XU, ROUNDING_FACTOR * e_o32)))[0]
+        assert bad.size == 0, (k, [(int(b), float(e_gpu[b]), float(e_o32[b])) for b in bad])
 
 
 def _dx():
@@ -279,11 +297,73 @@ def test_empty_batch():
     assert out["X"].shape == (0, 4, 10)
 
 
+def sample_indices(B, n=512, tail=8):
+    """A strided sample of n elements of a batch of B that touches every
+    1024-element block, lands at varying positions inside warps, and includes
+    the last `tail` elements (the ragged last warp)."""
+    stride = max(1, B // n)
+    j = np.arange(n)
+    idx = j * stride + (7 * j) % stride
+    return np.unique(np.concatenate([idx[idx < B], np.arange(max(0, B - tail), B)]))
+
+
+def replay_sample(cfg, inp, res, grads, gX, gU, idx, cond_capped=False):
+    """The oracle replays the GPU's own decisions on the sampled elements: X, U
+    within 1e-4 of the GPU's, and the oracle's backward at the GPU's solution
+    within 1e-3 of the GPU's gradients. cond_capped (long horizons): the bar
+    is per element the plain one or CONDITION_FACTOR times the oracle's
+    response to 1e-7 noise in C where that stays below 0.05; the rest (one ulp
+    moves them further) are compared with the oracle's fp64 replay, within 30
+    times the oracle's own fp32 error."""
+    from parity import CONDITION_FACTOR, condition_spread, rel_per_elem
+    sl = {k: np.ascontiguousarray(v[idx]) for k, v in inp.items()}
+    tr = res["trace"][idx].cpu().numpy()
+    X, U = res["X"][idx].cpu().numpy(), res["U"][idx].cpu().numpy()
+    tight = res["tight"][idx].cpu().numpy()
+    kw = dict(u_min=wl.U_MIN, u_max=wl.U_MAX, dt=wl.DT, max_iter=cfg["max_iter"], alphas=cfg["alphas"], forced=tr)
+
+    def run(C):
+        o_ = O.solve(sl["x0"], sl["U_init"], C, sl["c"], **kw)
+        out = {"X": o_["X"], "U": o_["U"]}
+        if grads is not None:
+            g_ = O.backward(X, U, C, None, None, None, tight, gX[idx], gU[idx], wl.DT, wl.REG_EPS)
+            out.update({k: g_["grad_" + k] for k in grads})
+        return out
+
+    o = run(sl["C"])
+    gpu = {"X": X, "U": U}
+    if grads is not None:
+        gpu.update({k: grads[k][idx].cpu().numpy() for k in grads})
+    if not cond_capped:
+        for k in gpu:
+            tol = TOL_XU if k in ("X", "U") else TOL_GRAD
+            assert max_rel(gpu[k], o[k]) <= tol, (k, max_rel(gpu[k], o[k]))
+        return
+    sp = condition_spread(run, sl["C"], rel_per_elem)
+    ill = np.zeros(len(idx), bool)
+    for k in gpu:
+        ill |= CONDITION_FACTOR * sp[k] > 0.05
+    for k in gpu:
+        tol = TOL_XU if k in ("X", "U") else TOL_GRAD
+        err = rel_per_elem(gpu[k], o[k])
+        bad = np.nonzero(~ill & (err > np.maximum(tol, CONDITION_FACTOR * sp[k])))[0]
+        assert bad.size == 0, (k, [(int(idx[b]), float(err[b]), float(sp[k][b])) for b in bad])
+    if ill.any():
+        o64 = O.solve(sl["x0"], sl["U_init"], sl["C"], sl["c"], dtype=np.float64, **kw)
+        for k in ("X", "U"):
+            e_gpu, e_o32 = rel_per_elem(gpu[k], o64[k]), rel_per_elem(o[k], o64[k])
+            bad = np.nonzero(ill & (e_gpu > np.maximum(TOL_XU, 30.0 * e_o32)))[0]
+            assert bad.size == 0, (k, [(int(idx[b]), float(e_gpu[b]), float(e_o32[b])) for b in bad])
+
+
 @pytest.mark.parametrize("B,T,iters", [(16384, 20, 5)])
 def test_training_scale_properties(B, T, iters):
     """Full training-scale batch: deterministic, finite, its first 16 elements
     equal the 16-element solve (which the replay tests pin to the reference),
-    and the backward is exactly linear in the upstream gradient (x2 scaling)."""
+    the backward is exactly linear in the upstream gradient (x2 scaling), and
+    a strided sample of 520 elements (every 1024-block, the ragged last warp)
+    is replayed by the oracle from the GPU's own decisions: X, U within 1e-4
+    and the gradients within 1e-3."""
     cfg, inp = wl.config_inputs("rollout_b16384_t20", B=B)
     t = {k: g(v) for k, v in inp.items()}
     args = (t["x0"], t["U_init"], t["C"], t["c"], None, None, None, None, g(wl.U_MIN), g(wl.U_MAX))
@@ -300,6 +380,7 @@ def test_training_scale_properties(B, T, iters):
     g2 = nat.backward(a["X"], a["U"], t["C"], g(2 * gX), g(2 * gU), tight=a["tight"], dt=wl.DT)
     for k in g1:
         assert torch.equal(2 * g1[k], g2[k]), k
+    replay_sample(cfg, inp, a, g1, gX, gU, sample_indices(B))
 
 
 @pytest.mark.parametrize("layout", ["team", "pair"])
@@ -469,18 +550,21 @@ def test_captured_solve_equals_eager_calls(sigmoid):
 def test_full_size_configs(name):
     """The largest configurations run at full size (many waves of CTAs, 2-3 GB
     of costs): finite results, the first 16 elements equal to a 16-element
-    solve of the same inputs, and for the stress case a backward that is
-    linear in the upstream gradient."""
+    solve of the same inputs, for the stress case a backward that is linear
+    in the upstream gradient, and a strided sample of about 520 elements
+    replayed by the oracle from the GPU's own decisions (for the T=50 stress
+    case with the conditioning-capped bar of replay_sample)."""
     cfg, inp = wl.config_inputs(name)
     B, T = cfg["B"], cfg["T"]
     lo, hi = g(wl.U_MIN), g(wl.U_MAX)
     t = {k: g(v) for k, v in inp.items()}
     kw = dict(dt=wl.DT, max_iter=cfg["max_iter"], alphas=cfg["alphas"])
-    a = nat.solve(t["x0"], t["U_init"], t["C"], t["c"], None, None, None, None, lo, hi, **kw)
+    a = nat.solve(t["x0"], t["U_init"], t["C"], t["c"], None, None, None, None, lo, hi, want_trace=True, **kw)
     assert torch.isfinite(a["X"]).all() and torch.isfinite(a["U"]).all()
     s = nat.solve(*(t[k][:16].contiguous() for k in ("x0", "U_init", "C", "c")), None, None, None, None,
                   lo, hi, **kw)
     assert torch.equal(a["X"][:16], s["X"]) and torch.equal(a["U"][:16], s["U"])
+    g1 = gX = gU = None
     if cfg["backward"]:
         gX, gU = wl.make_backward_seeds(B, T)
         g1 = nat.backward(a["X"], a["U"], t["C"], g(gX), g(gU), tight=a["tight"], dt=wl.DT, need=("x0", "c"))
@@ -489,6 +573,8 @@ def test_full_size_configs(name):
         for k in g1:
             assert torch.isfinite(g1[k]).all()
             assert torch.equal(2 * g1[k], g2[k]), k
+    del t
+    replay_sample(cfg, inp, a, g1, gX, gU, sample_indices(B), cond_capped=T >= 50)
 
 
 def test_pnqp4_batch_matches_oracle_and_optimum():

@@ -81,7 +81,7 @@ def test_long_horizon_stress_case():
     keep the hover trajectory and match exactly; the others are rounding-
     dominated in the reference itself (its fp32 and fp64 runs differ by O(1)),
     so only monotone improvement is asserted for them."""
-    d = load("cfg5_b16_t50")
+    d = load("cfg5_b64_t50")
     r, kw = _solve(d, forced=d["ref_trace"])
     never = d["ref_trace"].max(axis=1) < 0
     assert never.any()
@@ -90,26 +90,41 @@ def test_long_horizon_stress_case():
     free, _ = _solve(d)
     x0c = O.objective(O.rollout(d["x0"], d["U_init"], kw["dt"]), d["U_init"],
                       np.zeros_like(d["ref_X"]), np.zeros_like(d["U_init"]), d["C"], d["c"],
-                      np.zeros((16, 14, 14), np.float32), np.zeros((16, 14), np.float32))
+                      np.zeros((len(d["x0"]), 14, 14), np.float32), np.zeros((len(d["x0"]), 14), np.float32))
     assert np.all(free["best_cost"] <= x0c)
 
 
 def test_long_horizon_within_conditioning():
-    """T=50, 15 m targets, every element: with the reference's decisions
-    replayed, the oracle's X, U and gradients agree with the reference to the
-    plain bars or to CONDITION_FACTOR times the oracle's own response to 1e-7
-    noise in C, per element. On the ill-conditioned elements that response is
-    O(1), and the oracle-reference difference is below it."""
+    """T=50, 15 m targets, the first 64 elements of the stress workload, with
+    the reference's decisions replayed. Where the problem is well conditioned
+    (CONDITION_FACTOR times the oracle's own response to 1e-7 noise in C stays
+    below COND_CAP), the oracle's X, U and gradients agree with the
+    reference's to the plain bars or to that multiple of the response, per
+    element. Where one ulp of noise moves the answer by more than COND_CAP,
+    fp32 runs do not pin one another: there the oracle's fp32 error against
+    its own fp64 replay of the same decisions must stay within
+    ROUNDING_FACTOR times the reference's fp32 error against that replay."""
     from parity import CONDITION_FACTOR, diffmpc_condition_spread
-    d = load("cfg5_b16_t50")
+    COND_CAP, ROUNDING_FACTOR = 0.05, 30.0
+    d = load("cfg5_b64_t50")
     r, kw = _solve(d, forced=d["ref_trace"])
     g = _backward(d, r["X"], r["U"], r["tight"], kw)
     sp = diffmpc_condition_spread(d, d["ref_trace"])
     pairs = [("X", r["X"], TOL_XU), ("U", r["U"], TOL_XU)] + [(k, g[k], TOL_GRAD) for k in GRAD_KEYS]
+    ill = np.zeros(len(d["x0"]), bool)
+    for k, a, tol in pairs:
+        ill |= CONDITION_FACTOR * sp[k] > COND_CAP
     for k, a, tol in pairs:
         err = rel_per_elem(a, d["ref_" + k])
-        bad = np.nonzero(err > np.maximum(tol, CONDITION_FACTOR * sp[k]))[0]
+        bad = np.nonzero(~ill & (err > np.maximum(tol, CONDITION_FACTOR * sp[k])))[0]
         assert bad.size == 0, (k, [(int(b), float(err[b]), float(sp[k][b])) for b in bad])
+    if ill.any():
+        o64, _ = _solve(d, forced=d["ref_trace"], dtype=np.float64)
+        for k in ("X", "U"):
+            e_o = rel_per_elem(r[k], o64[k])
+            e_ref = rel_per_elem(d["ref_" + k], o64[k])
+            bad = np.nonzero(ill & (e_o > np.maximum(TOL_XU, ROUNDING_FACTOR * e_ref)))[0]
+            assert bad.size == 0, (k, [(int(b), float(e_o[b]), float(e_ref[b])) for b in bad])
 
 
 @pytest.mark.parametrize("name", ["cfg1_b16_t5", "cfg3_b16_t20"])
