@@ -256,6 +256,15 @@ __global__ void __launch_bounds__(32, MINB) backward_kernel(const __grid_constan
 }
 
 
+__device__ __forceinline__ void load_rec4(const float* r, float (&x)[NX], float (&u)[NU]) {
+  const float4* q = reinterpret_cast<const float4*>(r);
+  const float4 a = q[0], c = q[1], d = q[2], e = q[3];
+  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+  x[4] = c.x; x[5] = c.y; x[6] = c.z; x[7] = c.w;
+  x[8] = d.x; x[9] = d.y; u[0] = d.z; u[1] = d.w;
+  u[2] = e.x; u[3] = e.y;
+}
+
 // Bulk copy of `bytes` (a multiple of 16) from shared to global memory,
 // completion tracked by the issuing thread's bulk groups.
 __device__ __forceinline__ void bulk_store(float* dst, const float* src, uint32_t bytes) {
@@ -281,13 +290,12 @@ __global__ void __launch_bounds__(32, MINB) backward_pair_kernel(const BackwardP
   const int64_t bw = valid ? b : b0;
   const int T = p.T;
   const float dt = p.dt;
-  float* sh = reinterpret_cast<float*>(smem) + h * PAREA;
-  auto kcol = [&](int t, int j) {
-    return reinterpret_cast<float4*>(p.ws + ((size_t)(t * NX + j) * (size_t)p.S + (size_t)bw) * 4);
-  };
-  auto kff = [&](int t) {
-    return reinterpret_cast<float4*>(p.ws + ((size_t)T * NX * (size_t)p.S + (size_t)t * p.S + (size_t)bw) * 4);
-  };
+  float* sh = reinterpret_cast<float*>(smem) + h * pair_area(T, PREC_F + PJT_F + PKS_F);
+  float* REC = sh + PBASE;         // [T][16] X_t, U_t
+  float* JT = REC + PREC_F * T;    // [T][32] Jacobian tables
+  float* KS = JT + PJT_F * T;      // [T][44] K columns, then k
+  int own;
+  const uint64_t coffs = pair_coef_offsets(i < NT ? i : NT - 1, own);
   auto f4 = [](const float (&v)[NU]) { return make_float4(v[0], v[1], v[2], v[3]); };
   auto ld = [&](const float* q, int64_t k) { return valid ? __ldg(q + k) : 0.0f; };
   const float* Xb = p.X + b * (int64_t)(T + 1) * NX;
@@ -307,16 +315,25 @@ __global__ void __launch_bounds__(32, MINB) backward_pair_kernel(const BackwardP
   PairCPipe cpipe{sigm ? nullptr : p.C + bw * p.C_bstride * CBLK, p.C_tstride, sh + PC0, i};
   if (sigm) {
     for (int f = i; f < CBLK; f += HALF) sh[PC0 + f] = 0.0f;
-    __syncwarp();
   } else {
     cpipe.issue(T - 1);
   }
-  for (int t = T - 1; t >= 0; --t) {
+  // prologue: every step's (X_t, U_t) and Jacobian table, a step per lane
+  for (int t = i; t < T; t += HALF) {
     float xb[NX], ub[NU];
 #pragma unroll
     for (int k = 0; k < NX; ++k) xb[k] = ld(Xb, t * NX + k);
 #pragma unroll
     for (int a = 0; a < NU; ++a) ub[a] = ld(Ub, t * NU + a);
+    float4* d4 = reinterpret_cast<float4*>(REC + PREC_F * t);
+    d4[0] = make_float4(xb[0], xb[1], xb[2], xb[3]);
+    d4[1] = make_float4(xb[4], xb[5], xb[6], xb[7]);
+    d4[2] = make_float4(xb[8], xb[9], ub[0], ub[1]);
+    d4[3] = make_float4(ub[2], ub[3], 0.0f, 0.0f);
+    jtab_write(JT + PJT_F * t, drone_jac(xb, ub, dt));
+  }
+  __syncwarp();
+  for (int t = T - 1; t >= 0; --t) {
     const float lx = i < NX ? -ld(gXb, t * NX + i) : (i < NT ? -ld(gUb, t * NU + (i - NX)) : 0.0f);
     uint32_t tight = 0;
     if (p.tight != nullptr && valid) {
@@ -331,14 +348,15 @@ __global__ void __launch_bounds__(32, MINB) backward_pair_kernel(const BackwardP
     } else {
       cp_async_wait<0>();
     }
-    const Jac J = drone_jac(xb, ub, dt);
+    const float* jt = JT + PJT_F * t;
+    const Jac J = jtab_read(jt);
+    float cf_[7], c7;
+    pair_coef_load(jt, coffs, cf_, c7);
     __syncwarp();
     float Kr[NU];
-    pair_riccati<true>(Vr, vr, J, sigm ? sh + PC0 : cpipe.block(t), lx, p.reg, tight, i, valid, sh, Kr);
-    if (valid) {
-      if (i < NX) *kcol(t, i) = f4(Kr);
-      if (i == NX) *kff(t) = f4(Kr);
-    }
+    pair_riccati<true>(Vr, vr, J, cf_, c7, own, sigm ? sh + PC0 : cpipe.block(t), lx, p.reg, tight, i, valid, sh,
+                       Kr);
+    if (i <= NX) *reinterpret_cast<float4*>(KS + PKS_F * t + 4 * i) = f4(Kr);
   }
   if (valid && p.g_x0 != nullptr && i < NX) p.g_x0[b * NX + i] = -vr;
   __syncwarp();
@@ -354,22 +372,27 @@ __global__ void __launch_bounds__(32, MINB) backward_pair_kernel(const BackwardP
   float* gCb = wgc ? p.g_C + b * p.C_bstride * CBLK : nullptr;
   for (int t = 0; t < T; ++t) {
     float z[NT], du[NU];
-#pragma unroll
-    for (int k = 0; k < NX; ++k) z[k] = ld(Xb, t * NX + k);
-#pragma unroll
-    for (int a = 0; a < NU; ++a) z[NX + a] = ld(Ub, t * NU + a);
     {
-      float4 c = *kcol(t, 0);
+      float xz[NX], uz[NU];
+      load_rec4(REC + PREC_F * t, xz, uz);
+#pragma unroll
+      for (int k = 0; k < NX; ++k) z[k] = xz[k];
+#pragma unroll
+      for (int a = 0; a < NU; ++a) z[NX + a] = uz[a];
+    }
+    const float4* ks = reinterpret_cast<const float4*>(KS + PKS_F * t);
+    {
+      float4 c = ks[0];
       float acc[NU] = {c.x * dx[0], c.y * dx[0], c.z * dx[0], c.w * dx[0]};
 #pragma unroll
       for (int j = 1; j < NX; ++j) {
-        c = *kcol(t, j);
+        c = ks[j];
         acc[0] = fmaf(c.x, dx[j], acc[0]);
         acc[1] = fmaf(c.y, dx[j], acc[1]);
         acc[2] = fmaf(c.z, dx[j], acc[2]);
         acc[3] = fmaf(c.w, dx[j], acc[3]);
       }
-      const float4 kk = *kff(t);
+      const float4 kk = ks[NX];
       du[0] = acc[0] + kk.x;
       du[1] = acc[1] + kk.y;
       du[2] = acc[2] + kk.z;
@@ -418,12 +441,7 @@ __global__ void __launch_bounds__(32, MINB) backward_pair_kernel(const BackwardP
       if (i < NX && p.g_xref != nullptr) p.g_xref[(b * (T + 1) + t) * NX + i] = di;
       if (i >= NX && p.g_uref != nullptr) p.g_uref[(b * T + t) * NU + (i - NX)] = di;
     }
-    float xs[NX], us[NU];
-#pragma unroll
-    for (int k = 0; k < NX; ++k) xs[k] = z[k];
-#pragma unroll
-    for (int a = 0; a < NU; ++a) us[a] = z[NX + a];
-    const Jac J = drone_jac(xs, us, dt);
+    const Jac J = jtab_read(JT + PJT_F * t);
     float nd[NX];
     jac_apply(J, dx, du, nd);
 #pragma unroll
@@ -464,9 +482,12 @@ size_t backward_smem_bytes() { return (size_t)EPW * CBLK * 4 + (size_t)EPW * XS 
 
 cudaError_t launch_backward(const CUtensorMap& tmC, const CUtensorMap& tmG, const BackwardParams& p,
                             cudaStream_t stream) {
-  if (p.layout == LAYOUT_PAIR || (p.layout == LAYOUT_AUTO && p.B <= PAIR_MAX_B)) {
+  if (p.T <= PAIR_MAX_T && (p.layout == LAYOUT_PAIR || (p.layout == LAYOUT_AUTO && p.B <= PAIR_MAX_B))) {
     const unsigned pgrid = (unsigned)((p.B + EPWP - 1) / EPWP);
-    backward_pair_kernel<8><<<pgrid, WARP, (size_t)EPWP * PAREA * sizeof(float), stream>>>(p);
+    const size_t psmem = (size_t)EPWP * pair_area(p.T, PREC_F + PJT_F + PKS_F) * sizeof(float);
+    const cudaError_t e = allow_smem(backward_pair_kernel<8>, psmem);
+    if (e != cudaSuccess) return e;
+    backward_pair_kernel<8><<<pgrid, WARP, psmem, stream>>>(p);
     return cudaGetLastError();
   }
   const size_t smem = backward_smem_bytes();

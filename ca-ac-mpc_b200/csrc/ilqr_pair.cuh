@@ -32,8 +32,10 @@ namespace ilqr {
 
 constexpr int HALF = 16;   // lanes per element
 constexpr int EPWP = 2;    // elements per warp
-// Batches up to this size run in the pair layout by default.
+// Batches up to this size (and horizons up to PAIR_MAX_T, whose per-step
+// tables fit in shared memory) run in the pair layout by default.
 constexpr int64_t PAIR_MAX_B = 2048;
+constexpr int PAIR_MAX_T = 64;
 
 // Per-element shared-memory area (floats; float4 fields 16-byte aligned).
 constexpr int PC0 = 0;       // [2][196] C_t blocks (double buffer; diagonal mode uses block 0)
@@ -48,13 +50,52 @@ constexpr int PQXU = 628;    // [10][4]  Q_xu rows
 constexpr int PS = 668;      // [16]     rowdots s_i = (C_t tau)_i (first-pass objective)
 constexpr int PCV = 684;     // [16]     c_t
 constexpr int PSV = 700;     // [32]     SVD fallback: Q, its inverse
-constexpr int PAREA = 752;   // floats per element (= 16 mod 32: the two elements use opposite bank halves)
+constexpr int PBASE = 752;   // end of the fixed part of the area
+// Per-step tables after the fixed part (floats per step): the nominal record
+// (x, u; 16), the Jacobian table (32, below), the gains (ten K columns and k;
+// 44) and, in the solve, the cost record (diag C_t, c_t; 32).
+constexpr int PREC_F = 16, PJT_F = 32, PKS_F = 44, PCR_F = 32;
+// Floats per element: the fixed part and `per_t` floats per step, rounded so
+// that the two elements' areas start 16 floats apart modulo the 32 banks.
+__host__ __device__ __forceinline__ int pair_area(int T, int per_t) {
+  const int n = PBASE + per_t * T;
+  return (n + 31) / 32 * 32 + 16;
+}
+
+// Jacobian table of one step (32 floats): the fields of Jac and their
+// negatives, so that every coefficient of pair_coef is one entry:
+//   [0..3] dt h0 h1 h2   [4..7] g0..g3   [8..11] e0..e3   [12..15] bv0 bv1 bv2 1
+//   [16..19] 0 -h0 -h1 -h2   [20..23] -g0..-g3   [24..27] -e0..-e3   [28..31] -bv0 -bv1 -bv2 0
+__device__ __forceinline__ void jtab_write(float* jt, const Jac& J) {
+  float4* q = reinterpret_cast<float4*>(jt);
+  q[0] = make_float4(J.dt, J.h0, J.h1, J.h2);
+  q[1] = make_float4(J.g0, J.g1, J.g2, J.g3);
+  q[2] = make_float4(J.e0, J.e1, J.e2, J.e3);
+  q[3] = make_float4(J.bv0, J.bv1, J.bv2, 1.0f);
+  q[4] = make_float4(0.0f, -J.h0, -J.h1, -J.h2);
+  q[5] = make_float4(-J.g0, -J.g1, -J.g2, -J.g3);
+  q[6] = make_float4(-J.e0, -J.e1, -J.e2, -J.e3);
+  q[7] = make_float4(-J.bv0, -J.bv1, -J.bv2, 0.0f);
+}
+__device__ __forceinline__ Jac jtab_read(const float* jt) {
+  const float4* q = reinterpret_cast<const float4*>(jt);
+  const float4 a = q[0], b = q[1], c = q[2], d = q[3];
+  Jac J;
+  J.dt = a.x; J.h0 = a.y; J.h1 = a.z; J.h2 = a.w;
+  J.g0 = b.x; J.g1 = b.y; J.g2 = b.z; J.g3 = b.w;
+  J.e0 = c.x; J.e1 = c.y; J.e2 = c.z; J.e3 = c.w;
+  J.bv0 = d.x; J.bv1 = d.y; J.bv2 = d.z;
+  return J;
+}
 
 // Position of row r of V A inside a column of VAT: rows 3..9 first (two
 // aligned float4 loads give them), then rows 0..2.
 __device__ __forceinline__ int vat_pos(int r) { return r >= 3 ? r - 3 : r + 7; }
 
 // Coefficients of row r (0..13) in the form of the header comment.
+// (Evaluated once per kernel on a probe Jacobian whose fields are distinct
+// small integers, to find which Jacobian-table entry each coefficient is;
+// pair_coef_offsets.)
 __device__ __forceinline__ void pair_coef(const Jac& J, int r, float (&c)[7], float& c7, int& own) {
   const float z = 0.0f;
   float cc[8];
@@ -80,8 +121,40 @@ __device__ __forceinline__ void pair_coef(const Jac& J, int r, float (&c)[7], fl
   }
 }
 
+// Jacobian-table offsets of row r's coefficients c[0..6] and c7 (5 bits
+// each, packed), found by evaluating pair_coef on a probe whose fields are
+// the codes 2..16: a coefficient 0 is entry 16, 1 is entry 15, field k is
+// entry k and its negative entry 16 + k.
+__device__ __forceinline__ uint64_t pair_coef_offsets(int r, int& own) {
+  Jac P;
+  P.dt = 2.0f; P.h0 = 3.0f; P.h1 = 4.0f; P.h2 = 5.0f;
+  P.g0 = 6.0f; P.g1 = 7.0f; P.g2 = 8.0f; P.g3 = 9.0f;
+  P.e0 = 10.0f; P.e1 = 11.0f; P.e2 = 12.0f; P.e3 = 13.0f;
+  P.bv0 = 14.0f; P.bv1 = 15.0f; P.bv2 = 16.0f;
+  float c[7], c7;
+  pair_coef(P, r, c, c7, own);
+  auto off = [](float v) -> uint64_t {
+    const int k = (int)fabsf(v) - 2;
+    return v == 0.0f ? 16u : (v == 1.0f ? 15u : (v > 0.0f ? (uint64_t)k : (uint64_t)(16 + k)));
+  };
+  uint64_t o = 0;
+#pragma unroll
+  for (int s = 0; s < 7; ++s) o |= off(c[s]) << (5 * s);
+  o |= off(c7) << 35;
+  return o;
+}
+
+// Row coefficients of one step from its Jacobian table.
+__device__ __forceinline__ void pair_coef_load(const float* jt, uint64_t offs, float (&c)[7], float& c7) {
+#pragma unroll
+  for (int s = 0; s < 7; ++s) c[s] = jt[(offs >> (5 * s)) & 31u];
+  c7 = jt[(offs >> 35) & 31u];
+}
+
 // One Riccati step for an element's half-warp; the same recursion and
 // operation order as team_riccati (ilqr_team.cuh), forward or masked.
+// c, c7, own: the coefficients of this lane's row (pair_coef, through the
+// step's Jacobian table; lanes 14, 15 carry row 13's).
 // Lane i < 10: Vr, vr = row i of V and v_i (in V_{t+1}, out V_t). lx: lane
 // i < 10 the gradient term of row i, lane 10 + a that of control a. Ce: the
 // element's C_t block in shared memory. sh: the element's area. On return
@@ -89,9 +162,10 @@ __device__ __forceinline__ void pair_coef(const Jac& J, int r, float (&c)[7], fl
 // holds k. Every lane returns whether the Cholesky succeeded (the same in all
 // lanes of the half). Ends with a warp sync: C_t and the area are free.
 template <bool MASKED>
-__device__ __forceinline__ bool pair_riccati(float (&Vr)[NX], float& vr, const Jac& J, const float* __restrict__ Ce,
-                                             float lx, float reg, uint32_t tight, int i, bool live,
-                                             float* __restrict__ sh, float (&Kr)[NU]) {
+__device__ __forceinline__ bool pair_riccati(float (&Vr)[NX], float& vr, const Jac& J, const float (&c)[7], float c7,
+                                             int own, const float* __restrict__ Ce, float lx, float reg,
+                                             uint32_t tight, int i, bool live, float* __restrict__ sh,
+                                             float (&Kr)[NU]) {
   // ---- rows of V A (as columns of VAT), V B and v ----------------------------
   if (i < NX) {
     float va[NX], vb[NU];
@@ -106,9 +180,6 @@ __device__ __forceinline__ bool pair_riccati(float (&Vr)[NX], float& vr, const J
 
   // ---- Q_xu rows and q_x (lanes 0..9), Q_uu rows and q_u (lanes 10..13) -------
   const int r = i < NT ? i : NT - 1;
-  float c[7], c7;
-  int own;
-  pair_coef(J, r, c, c7, own);
   float Qr[NU], qr;
   {
     float4 acc4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
@@ -277,6 +348,13 @@ __device__ __forceinline__ bool pair_riccati(float (&Vr)[NX], float& vr, const J
   }
   __syncwarp();  // C_t and the area are no longer read
   return ok;
+}
+
+// Raise a kernel's dynamic shared-memory limit to `bytes` (above the default
+// 48 KB the launch needs it; harmless below).
+template <class K>
+inline cudaError_t allow_smem(K kernel, size_t bytes) {
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
 
 // Sum of x over lanes base .. base + 4 in that order (team_sum's order).

@@ -676,6 +676,16 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
 // blocks stream through a cp.async double buffer. Workspace records, the
 // candidate slots and every formula are the team kernel's, so the results
 // are the same bits.
+//
+// Per-step tables in shared memory keep the serial chain of each step short:
+// at the start of every Riccati pass the sixteen lanes load the nominal
+// records of all steps and evaluate all the Jacobians at once (drone_jac into
+// a Jacobian table, one step per lane and round); the pass then reads its
+// step's record and Jacobian from shared memory and each lane picks its row
+// coefficients from the table by offsets fixed at kernel start. The pass
+// also leaves the gains and the cost records of every step in shared memory,
+// so the line search that follows loads nothing from global memory but the
+// dense cost blocks.
 template <bool HAS_REF, int MINB>
 __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -689,7 +699,13 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
   const int T = p.T;
   const float dt = p.dt;
   const SolveWs W{p, (uint32_t)bw};
-  float* sh = reinterpret_cast<float*>(smem) + h * PAREA;
+  float* sh = reinterpret_cast<float*>(smem) + h * pair_area(T, PREC_F + PJT_F + PKS_F + PCR_F);
+  float* REC = sh + PBASE;                  // [T][16] nominal x_t, u_t
+  float* JT = REC + PREC_F * T;             // [T][32] Jacobian tables
+  float* KS = JT + PJT_F * T;               // [T][44] K columns (4 each), then k
+  float* CR = KS + PKS_F * T;               // [T][32] diag(C_t) at 0, c_t at 16
+  int own;
+  const uint64_t coffs = pair_coef_offsets(i < NT ? i : NT - 1, own);
 
   const bool bounds = p.has_bounds != 0;
   const float* lo = bounds ? p.u_min : nullptr;
@@ -772,13 +788,25 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
     float cost_q = 0.0f, cost_l = 0.0f;
     const bool first = (it == 0);
     if (!diag) cpipe.issue(T - 1);
+    // prologue: every step's nominal record and Jacobian table (a step per lane)
+    for (int t = i; t < T; t += HALF) {
+      float xb[NX], ub[NU];
+      const float4* r4 = W.rec(nom, t);
+      const float4 q0 = r4[0], q1 = r4[1], q2 = r4[2], q3 = r4[3];
+      float4* d4 = reinterpret_cast<float4*>(REC + PREC_F * t);
+      d4[0] = q0; d4[1] = q1; d4[2] = q2; d4[3] = q3;
+      load_rec(reinterpret_cast<const float4*>(d4), xb, ub);
+      jtab_write(JT + PJT_F * t, drone_jac(xb, ub, dt));
+    }
+    __syncwarp();
     for (int t = T - 1; t >= 0; --t) {
       float xb[NX], ub[NU], tau[NT];
-      load_rec(W.rec(nom, t), xb, ub);
+      load_rec(reinterpret_cast<const float4*>(REC + PREC_F * t), xb, ub);
+      float* cr = CR + PCR_F * t;
       float cv;  // c_t entry ti: from the input on the first pass, from the cost record afterwards
       if (first && sigm) cv = sig_c(p.sig, sgrow, T, t, ti);
       else if (first) cv = ldg_or0(cb + t * p.c_tstride + ti, valid);
-      else cv = W.cvec(t)[ti];
+      else cv = cr[16 + ti];
       if (!diag) {
         if (t > 0) {
           cpipe.issue(t - 1);
@@ -790,10 +818,11 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
         if (i < NT) {
           const float dv = sig_diag(p.sig, sgrow, T, t, i);
           sh[PC0 + i * (NT + 1)] = dv;
+          cr[i] = dv;
           if (valid) W.diag(t)[i] = dv;
         }
       } else {
-        if (i < NT) sh[PC0 + i * (NT + 1)] = W.diag(t)[i];
+        if (i < NT) sh[PC0 + i * (NT + 1)] = cr[i];
       }
       __syncwarp();
       const float* Ce = diag ? sh + PC0 : cpipe.block(t);
@@ -814,20 +843,27 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
         if (i < NT) {
           sh[PS + i] = sdot;
           sh[PCV + i] = cv;
+          cr[16 + i] = cv;
           if (valid) W.cvec(t)[i] = cv;
         }
-        if (p.diag_cache && valid && !sigm) {
-          const float4* c4 = reinterpret_cast<const float4*>(Ce);
-          for (int q = i; q < CBLK / 4; q += HALF) {
-            const float4 v = c4[q];
-            const int f = 4 * q;
-            offd |= (v.x != 0.0f && f % (NT + 1) != 0) || (v.y != 0.0f && (f + 1) % (NT + 1) != 0) ||
-                    (v.z != 0.0f && (f + 2) % (NT + 1) != 0) || (v.w != 0.0f && (f + 3) % (NT + 1) != 0);
+        if (!sigm) {
+          if (i < NT) cr[i] = Ce[i * (NT + 1)];
+          if (p.diag_cache && valid) {
+            const float4* c4 = reinterpret_cast<const float4*>(Ce);
+            for (int q = i; q < CBLK / 4; q += HALF) {
+              const float4 v = c4[q];
+              const int f = 4 * q;
+              offd |= (v.x != 0.0f && f % (NT + 1) != 0) || (v.y != 0.0f && (f + 1) % (NT + 1) != 0) ||
+                      (v.z != 0.0f && (f + 2) % (NT + 1) != 0) || (v.w != 0.0f && (f + 3) % (NT + 1) != 0);
+            }
+            if (i < NT) W.diag(t)[i] = Ce[i * (NT + 1)];
           }
-          if (i < NT) W.diag(t)[i] = Ce[i * (NT + 1)];
         }
       }
-      const Jac J = drone_jac(xb, ub, dt);
+      const float* jt = JT + PJT_F * t;
+      const Jac J = jtab_read(jt);
+      float cf_[7], c7;
+      pair_coef_load(jt, coffs, cf_, c7);
       __syncwarp();
       if (first && i < TEAM) {
         // the initial objective, accumulated as the team kernel's lane m = i does
@@ -839,7 +875,8 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
         cost_l += fmaf(ca_, ta, cb_ * tb) + (i < NU ? cu * tu : 0.0f);
       }
       float Kr[NU];
-      if (!pair_riccati<false>(Vr, vr, J, Ce, lx, p.reg, 0u, i, valid, sh, Kr)) fallback = true;
+      if (!pair_riccati<false>(Vr, vr, J, cf_, c7, own, Ce, lx, p.reg, 0u, i, valid, sh, Kr)) fallback = true;
+      if (i <= NX) *reinterpret_cast<float4*>(KS + PKS_F * t + 4 * i) = f4(Kr);
       if (valid) {
         if (i < NX) *W.kcol(t, i) = f4(Kr);
         if (i == NX) *W.kff(t) = f4(Kr);
@@ -887,19 +924,20 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
           __syncwarp();
         }
         float xb[NX], ub[NU], kt[NU], u[NU];
-        load_rec(W.rec(nom, t), xb, ub);
+        load_rec(reinterpret_cast<const float4*>(REC + PREC_F * t), xb, ub);
+        const float4* ks = reinterpret_cast<const float4*>(KS + PKS_F * t);
         {
-          const float4 k4 = *W.kff(t);
+          const float4 k4 = ks[NX];
           kt[0] = k4.x; kt[1] = k4.y; kt[2] = k4.z; kt[3] = k4.w;
         }
-        candidate_u(x, xb, ub, [&](int jj) { return *W.kcol(t, jj); }, kt, al, lo, hi, u);
+        candidate_u(x, xb, ub, [&](int jj) { return ks[jj]; }, kt, al, lo, hi, u);
         if (keep) store_rec(W.rec(cs, t), x, u);
         float tau[NT];
 #pragma unroll
         for (int k = 0; k < NX; ++k) tau[k] = x[k] - xref(t, k);
 #pragma unroll
         for (int a = 0; a < NU; ++a) tau[NX + a] = u[a] - uref(t, a);
-        const float* cost_t = W.diag(t);
+        const float* cost_t = CR + PCR_F * t;
         float l;
         {
           const float4* c4 = reinterpret_cast<const float4*>(cost_t + 16);
@@ -1069,13 +1107,17 @@ size_t solve_smem_bytes(int tier) {
   return base + sizeof(uint64_t);
 }
 
-size_t solve_pair_smem_bytes() { return (size_t)EPWP * PAREA * sizeof(float); }
+size_t solve_pair_smem_bytes(int T) {
+  return (size_t)EPWP * pair_area(T, PREC_F + PJT_F + PKS_F + PCR_F) * sizeof(float);
+}
 
 cudaError_t launch_solve(const CUtensorMap& tmC, const SolveParams& p, cudaStream_t stream) {
   const bool ref = p.x_ref != nullptr || p.u_ref != nullptr;
-  if (p.layout == LAYOUT_PAIR || (p.layout == LAYOUT_AUTO && p.B <= PAIR_MAX_B)) {
+  if (p.T <= PAIR_MAX_T && (p.layout == LAYOUT_PAIR || (p.layout == LAYOUT_AUTO && p.B <= PAIR_MAX_B))) {
     const unsigned pgrid = (unsigned)((p.B + EPWP - 1) / EPWP);
-    const size_t psmem = solve_pair_smem_bytes();
+    const size_t psmem = solve_pair_smem_bytes(p.T);
+    cudaError_t e = ref ? allow_smem(solve_pair_kernel<true, 8>, psmem) : allow_smem(solve_pair_kernel<false, 8>, psmem);
+    if (e != cudaSuccess) return e;
     if (ref) solve_pair_kernel<true, 8><<<pgrid, WARP, psmem, stream>>>(p);
     else solve_pair_kernel<false, 8><<<pgrid, WARP, psmem, stream>>>(p);
     return cudaGetLastError();
