@@ -290,10 +290,11 @@ __global__ void __launch_bounds__(32, MINB) backward_pair_kernel(const BackwardP
   const int64_t bw = valid ? b : b0;
   const int T = p.T;
   const float dt = p.dt;
-  float* sh = reinterpret_cast<float*>(smem) + h * pair_area(T, PREC_F + PJT_F + PKS_F);
+  float* sh = reinterpret_cast<float*>(smem) + h * pair_area(T, PREC_F + PJT_F + PKS_F + PLX_F);
   float* REC = sh + PBASE;         // [T][16] X_t, U_t
   float* JT = REC + PREC_F * T;    // [T][32] Jacobian tables
   float* KS = JT + PJT_F * T;      // [T][44] K columns, then k
+  float* LX = KS + PKS_F * T;      // [T][16] -dL/dX_t (10), -dL/dU_t (4), the tight bits
   int own;
   const uint64_t coffs = pair_coef_offsets(i < NT ? i : NT - 1, own);
   auto f4 = [](const float (&v)[NU]) { return make_float4(v[0], v[1], v[2], v[3]); };
@@ -331,15 +332,23 @@ __global__ void __launch_bounds__(32, MINB) backward_pair_kernel(const BackwardP
     d4[2] = make_float4(xb[8], xb[9], ub[0], ub[1]);
     d4[3] = make_float4(ub[2], ub[3], 0.0f, 0.0f);
     jtab_write(JT + PJT_F * t, drone_jac(xb, ub, dt));
+    float* lxt = LX + PLX_F * t;
+#pragma unroll
+    for (int k = 0; k < NX; ++k) lxt[k] = -ld(gXb, t * NX + k);
+#pragma unroll
+    for (int a = 0; a < NU; ++a) lxt[NX + a] = -ld(gUb, t * NU + a);
+    uint32_t tb = 0;
+    if (p.tight != nullptr && valid) {
+#pragma unroll
+      for (int a = 0; a < NU; ++a) tb |= (p.tight[(b * T + t) * NU + a] != 0 ? 1u : 0u) << a;
+    }
+    lxt[NT] = __uint_as_float(tb);
   }
   __syncwarp();
   for (int t = T - 1; t >= 0; --t) {
-    const float lx = i < NX ? -ld(gXb, t * NX + i) : (i < NT ? -ld(gUb, t * NU + (i - NX)) : 0.0f);
-    uint32_t tight = 0;
-    if (p.tight != nullptr && valid) {
-#pragma unroll
-      for (int a = 0; a < NU; ++a) tight |= (p.tight[(b * T + t) * NU + a] != 0 ? 1u : 0u) << a;
-    }
+    const float* lxt = LX + PLX_F * t;
+    const float lx = i < NT ? lxt[i] : 0.0f;
+    const uint32_t tight = __float_as_uint(lxt[NT]);
     if (sigm) {
       if (i < NT) sh[PC0 + i * (NT + 1)] = sig_diag(p.sig, sgrow, T, t, i);
     } else if (t > 0) {
@@ -484,7 +493,7 @@ cudaError_t launch_backward(const CUtensorMap& tmC, const CUtensorMap& tmG, cons
                             cudaStream_t stream) {
   if (p.T <= PAIR_MAX_T && (p.layout == LAYOUT_PAIR || (p.layout == LAYOUT_AUTO && p.B <= PAIR_MAX_B))) {
     const unsigned pgrid = (unsigned)((p.B + EPWP - 1) / EPWP);
-    const size_t psmem = (size_t)EPWP * pair_area(p.T, PREC_F + PJT_F + PKS_F) * sizeof(float);
+    const size_t psmem = (size_t)EPWP * pair_area(p.T, PREC_F + PJT_F + PKS_F + PLX_F) * sizeof(float);
     const cudaError_t e = allow_smem(backward_pair_kernel<8>, psmem);
     if (e != cudaSuccess) return e;
     backward_pair_kernel<8><<<pgrid, WARP, psmem, stream>>>(p);

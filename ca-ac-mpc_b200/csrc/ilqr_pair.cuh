@@ -41,7 +41,7 @@ constexpr int PAIR_MAX_T = 64;
 constexpr int PC0 = 0;       // [2][196] C_t blocks (double buffer; diagonal mode uses block 0)
 constexpr int PVAT = 392;    // [10][12] columns of V A: VAT[c][vat_pos(r)]
 constexpr int PVB = 512;     // [10][4]  rows of V B
-constexpr int PV = 552;      // [12]     v
+constexpr int PV = 552;      // [12]     v (v_k at PV + 1 + k: v[3..6], v[7..9] are aligned float4s)
 constexpr int PQUU = 564;    // [4][4]   Q_uu rows (reg added once)
 constexpr int PQU = 580;     // [4]      q_u
 constexpr int PKC = 584;     // [10][4]  K columns (the four gains of state c)
@@ -55,6 +55,8 @@ constexpr int PBASE = 752;   // end of the fixed part of the area
 // (x, u; 16), the Jacobian table (32, below), the gains (ten K columns and k;
 // 44) and, in the solve, the cost record (diag C_t, c_t; 32).
 constexpr int PREC_F = 16, PJT_F = 32, PKS_F = 44, PCR_F = 32;
+// The backward's per-step gradient terms (-dL/dX_t, -dL/dU_t, tight bits; 16).
+constexpr int PLX_F = 16;
 // Floats per element: the fixed part and `per_t` floats per step, rounded so
 // that the two elements' areas start 16 floats apart modulo the 32 banks.
 __host__ __device__ __forceinline__ int pair_area(int T, int per_t) {
@@ -174,7 +176,7 @@ __device__ __forceinline__ bool pair_riccati(float (&Vr)[NX], float& vr, const J
 #pragma unroll
     for (int c = 0; c < NX; ++c) sh[PVAT + c * 12 + ps] = va[c];
     *reinterpret_cast<float4*>(sh + PVB + 4 * i) = make_float4(vb[0], vb[1], vb[2], vb[3]);
-    sh[PV + i] = vr;
+    sh[PV + 1 + i] = vr;
   }
   __syncwarp();
 
@@ -184,6 +186,9 @@ __device__ __forceinline__ bool pair_riccati(float (&Vr)[NX], float& vr, const J
   {
     float4 acc4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     float accv = 0.0f;
+    const float4 v36 = *reinterpret_cast<const float4*>(sh + PV + 4);
+    const float4 v79 = *reinterpret_cast<const float4*>(sh + PV + 8);
+    const float vs[7] = {v36.x, v36.y, v36.z, v36.w, v79.x, v79.y, v79.z};
 #pragma unroll
     for (int s = 0; s < 7; ++s) {
       const float4 y = *reinterpret_cast<const float4*>(sh + PVB + 4 * (3 + s));
@@ -191,19 +196,20 @@ __device__ __forceinline__ bool pair_riccati(float (&Vr)[NX], float& vr, const J
       acc4.y = fmaf(c[s], y.y, acc4.y);
       acc4.z = fmaf(c[s], y.z, acc4.z);
       acc4.w = fmaf(c[s], y.w, acc4.w);
-      accv = fmaf(c[s], sh[PV + 3 + s], accv);
+      accv = fmaf(c[s], vs[s], accv);
     }
     const float4 o = *reinterpret_cast<const float4*>(sh + PVB + 4 * own);
-    const float* Cr = Ce + r * NT + NX;
-    Qr[0] = Cr[0] + fmaf(c7, o.x, acc4.x);
-    Qr[1] = Cr[1] + fmaf(c7, o.y, acc4.y);
-    Qr[2] = Cr[2] + fmaf(c7, o.z, acc4.z);
-    Qr[3] = Cr[3] + fmaf(c7, o.w, acc4.w);
+    const float2* Cr = reinterpret_cast<const float2*>(Ce + r * NT + NX);
+    const float2 cr0 = Cr[0], cr1 = Cr[1];
+    Qr[0] = cr0.x + fmaf(c7, o.x, acc4.x);
+    Qr[1] = cr0.y + fmaf(c7, o.y, acc4.y);
+    Qr[2] = cr1.x + fmaf(c7, o.z, acc4.z);
+    Qr[3] = cr1.y + fmaf(c7, o.w, acc4.w);
     if (r >= NX) {
 #pragma unroll
       for (int a = 0; a < NU; ++a) Qr[a] = Qr[a] + (r - NX == a ? reg : 0.0f);
     }
-    qr = lx + fmaf(c7, sh[PV + own], accv);
+    qr = lx + fmaf(c7, sh[PV + 1 + own], accv);
   }
   if (i >= NX && i < NT) {
     *reinterpret_cast<float4*>(sh + PQUU + 4 * (i - NX)) = make_float4(Qr[0], Qr[1], Qr[2], Qr[3]);
@@ -322,7 +328,16 @@ __device__ __forceinline__ bool pair_riccati(float (&Vr)[NX], float& vr, const J
     // V[i][cc] = (Q_xx[i][cc] + W_i K_cc) + K_i Q_xu[cc], Q_xx[i][cc] from the
     // columns of V A in the form of the header comment
     const int po = vat_pos(own);
-    const float* Ci = Ce + i * NT;
+    float Ci[NX];
+    {
+      const float2* c2 = reinterpret_cast<const float2*>(Ce + i * NT);
+#pragma unroll
+      for (int q = 0; q < NX / 2; ++q) {
+        const float2 v = c2[q];
+        Ci[2 * q] = v.x;
+        Ci[2 * q + 1] = v.y;
+      }
+    }
 #pragma unroll
     for (int cc = 0; cc < NX; ++cc) {
       const float* col = sh + PVAT + cc * 12;

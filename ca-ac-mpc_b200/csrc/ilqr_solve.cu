@@ -175,6 +175,49 @@ __device__ __forceinline__ void candidate_u(const float (&x)[NX], const float (&
   }
 }
 
+// candidate_u with the box in registers (the same operations).
+template <class KCol>
+__device__ __forceinline__ void candidate_u_reg(const float (&x)[NX], const float (&xb)[NX], const float (&ub)[NU],
+                                                KCol&& kcol, const float (&kt)[NU], float al, bool bounds,
+                                                const float (&lo)[NU], const float (&hi)[NU], float (&u)[NU]) {
+  float dx[NX];
+#pragma unroll
+  for (int i = 0; i < NX; ++i) dx[i] = x[i] - xb[i];
+  float kd[NU];
+  {
+    const float4 c = kcol(0);
+    kd[0] = c.x * dx[0];
+    kd[1] = c.y * dx[0];
+    kd[2] = c.z * dx[0];
+    kd[3] = c.w * dx[0];
+  }
+#pragma unroll
+  for (int j = 1; j < NX; ++j) {
+    const float4 c = kcol(j);
+    kd[0] = fmaf(c.x, dx[j], kd[0]);
+    kd[1] = fmaf(c.y, dx[j], kd[1]);
+    kd[2] = fmaf(c.z, dx[j], kd[2]);
+    kd[3] = fmaf(c.w, dx[j], kd[3]);
+  }
+#pragma unroll
+  for (int a = 0; a < NU; ++a) {
+    float v = ub[a] + (al * kt[a] + al * kd[a]);
+    if (bounds) v = clamp_nan(v, lo[a], hi[a]);
+    u[a] = v;
+  }
+}
+
+// Whether flat index f (< 196) of a C block is on its diagonal (15 i):
+// f / 15 as (f * 2185) >> 15, exact for these f, without a division.
+__device__ __forceinline__ bool on_diag(int f) { return f == ((f * 2185) >> 15) * (NT + 1); }
+
+// Whether the four floats at flat indices f .. f + 3 of a C block hold a
+// nonzero off the diagonal.
+__device__ __forceinline__ bool offdiag_nonzero(const float4 v, int f) {
+  return (v.x != 0.0f && !on_diag(f)) || (v.y != 0.0f && !on_diag(f + 1)) || (v.z != 0.0f && !on_diag(f + 2)) ||
+         (v.w != 0.0f && !on_diag(f + 3));
+}
+
 __device__ __forceinline__ float pick(const float (&v)[NT], int i) {
   float r = v[0];
 #pragma unroll
@@ -404,12 +447,7 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
           // the team scans the block for off-diagonal nonzeros (the diagonal
           // sits at flat index 15 i) and keeps a copy of the diagonal
           const float4* c4 = reinterpret_cast<const float4*>(Ce);
-          for (int q = m; q < CBLK / 4; q += TEAM) {
-            const float4 v = c4[q];
-            const int f = 4 * q;
-            offd |= (v.x != 0.0f && f % (NT + 1) != 0) || (v.y != 0.0f && (f + 1) % (NT + 1) != 0) ||
-                    (v.z != 0.0f && (f + 2) % (NT + 1) != 0) || (v.w != 0.0f && (f + 3) % (NT + 1) != 0);
-          }
+          for (int q = m; q < CBLK / 4; q += TEAM) offd |= offdiag_nonzero(c4[q], 4 * q);
           float* dgt = W.diag(t);
 #pragma unroll
           for (int s3 = 0; s3 < 3; ++s3)
@@ -710,6 +748,12 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
   const bool bounds = p.has_bounds != 0;
   const float* lo = bounds ? p.u_min : nullptr;
   const float* hi = bounds ? p.u_max : nullptr;
+  float blo[NU], bhi[NU];  // the box, in registers for the line search
+#pragma unroll
+  for (int a = 0; a < NU; ++a) {
+    blo[a] = bounds ? __ldg(lo + a) : 0.0f;
+    bhi[a] = bounds ? __ldg(hi + a) : 0.0f;
+  }
   const float* cb = p.c != nullptr ? p.c + b * p.c_bstride : nullptr;
   const float* xrb = (HAS_REF && p.x_ref != nullptr) ? p.x_ref + b * (int64_t)(T + 1) * NX : nullptr;
   const float* urb = (HAS_REF && p.u_ref != nullptr) ? p.u_ref + b * (int64_t)T * NU : nullptr;
@@ -727,12 +771,19 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
 
   // ---- initial open-loop rollout with U_init into slot 0 -----------------------
   {
+    // U_init of every step into the record table first (a step per lane)
+    for (int t = i; t < T; t += HALF) {
+      float* r = REC + PREC_F * t;
+#pragma unroll
+      for (int a = 0; a < NU; ++a) r[NX + a] = ldg_or0(p.U_init + (b * T + t) * NU + a, valid);
+    }
+    __syncwarp();
     float x[NX];
     load_x0(x);
     for (int t = 0; t < T; ++t) {
       float u[NU];
 #pragma unroll
-      for (int a = 0; a < NU; ++a) u[a] = ldg_or0(p.U_init + (b * T + t) * NU + a, valid);
+      for (int a = 0; a < NU; ++a) u[a] = REC[PREC_F * t + NX + a];
       if (writer) store_rec(W.rec(0, t), x, u);
       float xn[NX];
       drone_step(x, u, dt, xn);
@@ -797,29 +848,27 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
       d4[0] = q0; d4[1] = q1; d4[2] = q2; d4[3] = q3;
       load_rec(reinterpret_cast<const float4*>(d4), xb, ub);
       jtab_write(JT + PJT_F * t, drone_jac(xb, ub, dt));
+      if (first) {  // c_t (and, from policy parameters, diag C_t) into the step's cost record
+        float* cr = CR + PCR_F * t;
+#pragma unroll
+        for (int k = 0; k < NT; ++k) {
+          cr[16 + k] = sigm ? sig_c(p.sig, sgrow, T, t, k) : ldg_or0(cb + t * p.c_tstride + k, valid);
+          if (sigm) cr[k] = sig_diag(p.sig, sgrow, T, t, k);
+        }
+      }
     }
     __syncwarp();
     for (int t = T - 1; t >= 0; --t) {
       float xb[NX], ub[NU], tau[NT];
       load_rec(reinterpret_cast<const float4*>(REC + PREC_F * t), xb, ub);
       float* cr = CR + PCR_F * t;
-      float cv;  // c_t entry ti: from the input on the first pass, from the cost record afterwards
-      if (first && sigm) cv = sig_c(p.sig, sgrow, T, t, ti);
-      else if (first) cv = ldg_or0(cb + t * p.c_tstride + ti, valid);
-      else cv = cr[16 + ti];
+      const float cv = cr[16 + ti];  // c_t entry ti
       if (!diag) {
         if (t > 0) {
           cpipe.issue(t - 1);
           cp_async_wait<1>();
         } else {
           cp_async_wait<0>();
-        }
-      } else if (first && sigm) {
-        if (i < NT) {
-          const float dv = sig_diag(p.sig, sgrow, T, t, i);
-          sh[PC0 + i * (NT + 1)] = dv;
-          cr[i] = dv;
-          if (valid) W.diag(t)[i] = dv;
         }
       } else {
         if (i < NT) sh[PC0 + i * (NT + 1)] = cr[i];
@@ -833,30 +882,28 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
       // quadraticize: l_tau = C tau + c, row ti
       float sdot;
       {
-        const float* Cr = Ce + ti * NT;
-        sdot = Cr[0] * tau[0];
+        const float2* Cr = reinterpret_cast<const float2*>(Ce + ti * NT);
+        float2 c2 = Cr[0];
+        sdot = c2.x * tau[0];
+        sdot = fmaf(c2.y, tau[1], sdot);
 #pragma unroll
-        for (int j = 1; j < NT; ++j) sdot = fmaf(Cr[j], tau[j], sdot);
+        for (int j = 1; j < NT / 2; ++j) {
+          c2 = Cr[j];
+          sdot = fmaf(c2.x, tau[2 * j], sdot);
+          sdot = fmaf(c2.y, tau[2 * j + 1], sdot);
+        }
       }
       const float lx = sdot + cv;
       if (first) {
         if (i < NT) {
           sh[PS + i] = sdot;
           sh[PCV + i] = cv;
-          cr[16 + i] = cv;
-          if (valid) W.cvec(t)[i] = cv;
         }
         if (!sigm) {
           if (i < NT) cr[i] = Ce[i * (NT + 1)];
           if (p.diag_cache && valid) {
             const float4* c4 = reinterpret_cast<const float4*>(Ce);
-            for (int q = i; q < CBLK / 4; q += HALF) {
-              const float4 v = c4[q];
-              const int f = 4 * q;
-              offd |= (v.x != 0.0f && f % (NT + 1) != 0) || (v.y != 0.0f && (f + 1) % (NT + 1) != 0) ||
-                      (v.z != 0.0f && (f + 2) % (NT + 1) != 0) || (v.w != 0.0f && (f + 3) % (NT + 1) != 0);
-            }
-            if (i < NT) W.diag(t)[i] = Ce[i * (NT + 1)];
+            for (int q = i; q < CBLK / 4; q += HALF) offd |= offdiag_nonzero(c4[q], 4 * q);
           }
         }
       }
@@ -877,10 +924,6 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
       float Kr[NU];
       if (!pair_riccati<false>(Vr, vr, J, cf_, c7, own, Ce, lx, p.reg, 0u, i, valid, sh, Kr)) fallback = true;
       if (i <= NX) *reinterpret_cast<float4*>(KS + PKS_F * t + 4 * i) = f4(Kr);
-      if (valid) {
-        if (i < NX) *W.kcol(t, i) = f4(Kr);
-        if (i == NX) *W.kff(t) = f4(Kr);
-      }
     }
     if (first && p.diag_cache && !sigm) {
       diag = !__any_sync(FULL, offd);
@@ -930,7 +973,7 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
           const float4 k4 = ks[NX];
           kt[0] = k4.x; kt[1] = k4.y; kt[2] = k4.z; kt[3] = k4.w;
         }
-        candidate_u(x, xb, ub, [&](int jj) { return ks[jj]; }, kt, al, lo, hi, u);
+        candidate_u_reg(x, xb, ub, [&](int jj) { return ks[jj]; }, kt, al, bounds, blo, bhi, u);
         if (keep) store_rec(W.rec(cs, t), x, u);
         float tau[NT];
 #pragma unroll
@@ -1041,10 +1084,11 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
         load_x0(x);
         for (int t = 0; t < T; ++t) {
           float xb[NX], ub[NU], kt[NU], u[NU];
-          load_rec(W.rec(nom, t), xb, ub);
-          const float4 k4 = *W.kff(t);
+          load_rec(reinterpret_cast<const float4*>(REC + PREC_F * t), xb, ub);
+          const float4* ks = reinterpret_cast<const float4*>(KS + PKS_F * t);
+          const float4 k4 = ks[NX];
           kt[0] = k4.x; kt[1] = k4.y; kt[2] = k4.z; kt[3] = k4.w;
-          candidate_u(x, xb, ub, [&](int jj) { return *W.kcol(t, jj); }, kt, al, lo, hi, u);
+          candidate_u_reg(x, xb, ub, [&](int jj) { return ks[jj]; }, kt, al, bounds, blo, bhi, u);
           store_rec(W.rec(dst, t), x, u);
           float xn[NX];
           drone_step(x, u, dt, xn);
