@@ -450,9 +450,8 @@ def run_ours(args):
         if timing is not None:
             timing[2].record(stream)
         if world > 1:
-            # actions and dL/dx0 of every shard to rank 0 (all-gather over NCCL)
-            ilqr_shard.gather_first_actions(out["U"], B_glob)
-            ilqr_shard.gather_gradients(g, B_glob, keys=("x0",))
+            # actions and dL/dx0 of every shard to rank 0 (one all-gather over NCCL)
+            ilqr_shard.gather_actions_and_gradients(out["U"], g, B_glob, keys=("x0",))
         if timing is not None:
             timing[3].record(stream)
         return out, g
@@ -560,8 +559,8 @@ def run_ours(args):
             act = u[0].detach()
             gx0 = x0.grad
             if world > 1:
-                act = ilqr_shard.gather_first_actions(u.detach().permute(1, 0, 2).contiguous(), B_glob)
-                gx0 = ilqr_shard.gather_rows(gx0, B_glob)
+                act, gg = ilqr_shard.gather_actions_and_gradients(u.detach().permute(1, 0, 2), {"x0": gx0}, B_glob)
+                gx0 = gg["x0"]
             h_act.copy_(act, non_blocking=True)
             h_gx0.copy_(gx0, non_blocking=True)
 
@@ -592,8 +591,8 @@ def run_ours(args):
             act = u[0].detach()
             gx0 = x0.grad
             if world > 1:
-                act = ilqr_shard.gather_first_actions(u.detach().permute(1, 0, 2).contiguous(), B_glob)
-                gx0 = ilqr_shard.gather_rows(gx0, B_glob)
+                act, gg = ilqr_shard.gather_actions_and_gradients(u.detach().permute(1, 0, 2), {"x0": gx0}, B_glob)
+                gx0 = gg["x0"]
             h_act.copy_(act, non_blocking=True)
             h_gx0.copy_(gx0, non_blocking=True)
 
@@ -1083,8 +1082,7 @@ def run_ours(args):
                           dt=wl.DT, max_iter=iters, reg_eps=wl.REG_EPS, alphas=alphas)
             gw = nat.backward(o["X"], o["U"], wd["C"], wgX, wgU, tight=o["tight"], dt=wl.DT,
                               reg_eps=wl.REG_EPS, need=("x0", "C", "c"))
-            ilqr_shard.gather_first_actions(o["U"], Bw * world)
-            ilqr_shard.gather_gradients(gw, Bw * world, keys=("x0",))
+            ilqr_shard.gather_actions_and_gradients(o["U"], gw, Bw * world, keys=("x0",))
 
         for _ in range(max(3, args.warmup)):
             wstep()

@@ -52,6 +52,26 @@ def gather_first_actions(U_local: torch.Tensor, B: int, group=None) -> torch.Ten
     return gather_rows(U_local[:, 0, :], B, group)
 
 
+def gather_actions_and_gradients(U_local: torch.Tensor, grads: dict, B: int, keys=("x0",), group=None):
+    """gather_first_actions and gather_gradients in one collective: the
+    first controls and the per-element gradients `keys` are packed into one
+    [hi - lo, nu + sum of widths] buffer per rank, all-gathered once, and
+    unpacked. Returns (actions [B, nu], dict of [B, ...] gradients)."""
+    parts = [U_local[:, 0, :]] + [grads[k].reshape(grads[k].shape[0], -1) for k in keys]
+    packed = gather_rows(torch.cat(parts, 1), B, group)
+    nu = U_local.shape[-1]
+    acts = packed[:, :nu]
+    out, col = {}, nu
+    for k in keys:
+        tail = tuple(grads[k].shape[1:])
+        width = 1
+        for d in tail:
+            width *= d
+        out[k] = packed[:, col:col + width].reshape((B,) + tail)
+        col += width
+    return acts, out
+
+
 def gather_gradients(grads: dict, B: int, keys=("x0",), group=None) -> dict:
     """All-gather the per-element gradients `keys` of a rank's backward
     (the dict ilqr_native.backward returns, batch-major) into [B, ...]

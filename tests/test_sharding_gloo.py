@@ -43,8 +43,10 @@ def _worker(rank, world, port, B, T, q):
         gX, gU = wl.make_backward_seeds(B, T)
         gr = O.backward(r["X"], r["U"], inp["C"][lo:hi], None, None, None, r["tight"], gX[lo:hi], gU[lo:hi],
                         wl.DT, wl.REG_EPS)
-        gg = sh.gather_gradients({"x0": torch.from_numpy(gr["grad_x0"]), "c": torch.from_numpy(gr["grad_c"])},
-                                 B, keys=("x0", "c"))
+        gl = {"x0": torch.from_numpy(gr["grad_x0"]), "c": torch.from_numpy(gr["grad_c"])}
+        gg = sh.gather_gradients(gl, B, keys=("x0", "c"))
+        acts2, gg2 = sh.gather_actions_and_gradients(torch.from_numpy(r["U"]), gl, B, keys=("x0", "c"))
+        assert torch.equal(acts2, acts) and torch.equal(gg2["x0"], gg["x0"]) and torch.equal(gg2["c"], gg["c"])
         if rank == 0:
             q.put((acts.numpy(), gg["x0"].numpy(), gg["c"].numpy()))
     finally:
