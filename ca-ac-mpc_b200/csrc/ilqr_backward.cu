@@ -494,7 +494,7 @@ cudaError_t launch_backward(const CUtensorMap& tmC, const CUtensorMap& tmG, cons
   if (p.T <= PAIR_MAX_T && (p.layout == LAYOUT_PAIR || (p.layout == LAYOUT_AUTO && p.B <= PAIR_MAX_B))) {
     const unsigned pgrid = (unsigned)((p.B + EPWP - 1) / EPWP);
     const size_t psmem = (size_t)EPWP * pair_area(p.T, PREC_F + PJT_F + PKS_F + PLX_F) * sizeof(float);
-    const cudaError_t e = allow_smem(backward_pair_kernel<8>, psmem);
+    const cudaError_t e = allow_smem<backward_pair_kernel<8>>(psmem);
     if (e != cudaSuccess) return e;
     backward_pair_kernel<8><<<pgrid, WARP, psmem, stream>>>(p);
     return cudaGetLastError();

@@ -24,6 +24,8 @@
 //   rows 11..13 c[0..3] = B's body-rate column    (Q_uu / q_u rows of the rates)
 #pragma once
 
+#include <atomic>
+
 #include "ilqr_device.cuh"
 #include "ilqr_kernels.h"
 #include "ilqr_team.cuh"
@@ -367,9 +369,15 @@ __device__ __forceinline__ bool pair_riccati(float (&Vr)[NX], float& vr, const J
 
 // Raise a kernel's dynamic shared-memory limit to `bytes` (above the default
 // 48 KB the launch needs it; harmless below).
-template <class K>
-inline cudaError_t allow_smem(K kernel, size_t bytes) {
-  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+// Set once per kernel and size (a later, larger request sets it again), so
+// that launches recorded into a CUDA graph call no attribute setter.
+template <auto Kernel>
+inline cudaError_t allow_smem(size_t bytes) {
+  static std::atomic<size_t> granted{0};  // one per kernel
+  if (bytes <= granted.load()) return cudaSuccess;
+  const cudaError_t e = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e == cudaSuccess) granted.store(bytes);
+  return e;
 }
 
 // Sum of x over lanes base .. base + 4 in that order (team_sum's order).

@@ -1160,7 +1160,7 @@ cudaError_t launch_solve(const CUtensorMap& tmC, const SolveParams& p, cudaStrea
   if (p.T <= PAIR_MAX_T && (p.layout == LAYOUT_PAIR || (p.layout == LAYOUT_AUTO && p.B <= PAIR_MAX_B))) {
     const unsigned pgrid = (unsigned)((p.B + EPWP - 1) / EPWP);
     const size_t psmem = solve_pair_smem_bytes(p.T);
-    cudaError_t e = ref ? allow_smem(solve_pair_kernel<true, 8>, psmem) : allow_smem(solve_pair_kernel<false, 8>, psmem);
+    cudaError_t e = ref ? allow_smem<solve_pair_kernel<true, 8>>(psmem) : allow_smem<solve_pair_kernel<false, 8>>(psmem);
     if (e != cudaSuccess) return e;
     if (ref) solve_pair_kernel<true, 8><<<pgrid, WARP, psmem, stream>>>(p);
     else solve_pair_kernel<false, 8><<<pgrid, WARP, psmem, stream>>>(p);
