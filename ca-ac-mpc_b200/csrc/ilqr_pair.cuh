@@ -171,14 +171,18 @@ __device__ __forceinline__ bool pair_riccati(float (&Vr)[NX], float& vr, const J
                                              uint32_t tight, int i, bool live, float* __restrict__ sh,
                                              float (&Kr)[NU]) {
   // ---- rows of V A (as columns of VAT), V B and v ----------------------------
-  if (i < NX) {
+  // (Lanes 10..15 run every phase on a stand-in row, which keeps the warp in
+  // one instruction stream; only the lanes of real rows store.)
+  {
     float va[NX], vb[NU];
     row_VA_VB(J, Vr, va, vb);
-    const int ps = vat_pos(i);
+    if (i < NX) {
+      const int ps = vat_pos(i);
 #pragma unroll
-    for (int c = 0; c < NX; ++c) sh[PVAT + c * 12 + ps] = va[c];
-    *reinterpret_cast<float4*>(sh + PVB + 4 * i) = make_float4(vb[0], vb[1], vb[2], vb[3]);
-    sh[PV + 1 + i] = vr;
+      for (int c = 0; c < NX; ++c) sh[PVAT + c * 12 + ps] = va[c];
+      *reinterpret_cast<float4*>(sh + PVB + 4 * i) = make_float4(vb[0], vb[1], vb[2], vb[3]);
+      sh[PV + 1 + i] = vr;
+    }
   }
   __syncwarp();
 
@@ -301,7 +305,7 @@ __device__ __forceinline__ bool pair_riccati(float (&Vr)[NX], float& vr, const J
     const float4 k4 = *reinterpret_cast<const float4*>(sh + PKF);
     k[0] = k4.x; k[1] = k4.y; k[2] = k4.z; k[3] = k4.w;
   }
-  if (i < NX) {
+  {
     if (MASKED) {
       float w[NU];
 #pragma unroll
@@ -332,7 +336,7 @@ __device__ __forceinline__ bool pair_riccati(float (&Vr)[NX], float& vr, const J
     const int po = vat_pos(own);
     float Ci[NX];
     {
-      const float2* c2 = reinterpret_cast<const float2*>(Ce + i * NT);
+      const float2* c2 = reinterpret_cast<const float2*>(Ce + (i < NX ? i : NX - 1) * NT);
 #pragma unroll
       for (int q = 0; q < NX / 2; ++q) {
         const float2 v = c2[q];
