@@ -212,10 +212,26 @@ __device__ __forceinline__ void candidate_u_reg(const float (&x)[NX], const floa
 __device__ __forceinline__ bool on_diag(int f) { return f == ((f * 2185) >> 15) * (NT + 1); }
 
 // Whether the four floats at flat indices f .. f + 3 of a C block hold a
-// nonzero off the diagonal.
+// nonzero off the diagonal (bitwise, so that no lane branches).
 __device__ __forceinline__ bool offdiag_nonzero(const float4 v, int f) {
-  return (v.x != 0.0f && !on_diag(f)) || (v.y != 0.0f && !on_diag(f + 1)) || (v.z != 0.0f && !on_diag(f + 2)) ||
-         (v.w != 0.0f && !on_diag(f + 3));
+  return ((v.x != 0.0f) & !on_diag(f)) | ((v.y != 0.0f) & !on_diag(f + 1)) | ((v.z != 0.0f) & !on_diag(f + 2)) |
+         ((v.w != 0.0f) & !on_diag(f + 3));
+}
+
+// A lane's share of the scan of one C block for off-diagonal nonzeros: the
+// chunks of four floats q0, q0 + stride, ..., a fixed unrolled count with a
+// guard, so that lanes with one chunk fewer do not diverge.
+template <int STRIDE>
+__device__ __forceinline__ bool scan_offdiag(const float* blk, int q0) {
+  const float4* c4 = reinterpret_cast<const float4*>(blk);
+  bool nz = false;
+#pragma unroll
+  for (int r = 0; r < (CBLK / 4 + STRIDE - 1) / STRIDE; ++r) {
+    const int q = q0 + STRIDE * r;
+    const float4 v = c4[q < CBLK / 4 ? q : 0];
+    nz |= (q < CBLK / 4) & offdiag_nonzero(v, 4 * q);
+  }
+  return nz;
 }
 
 __device__ __forceinline__ float pick(const float (&v)[NT], int i) {
@@ -446,8 +462,7 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
         if (p.diag_cache && valid && !sigm) {  // (mirror lanes check too; only owners write)
           // the team scans the block for off-diagonal nonzeros (the diagonal
           // sits at flat index 15 i) and keeps a copy of the diagonal
-          const float4* c4 = reinterpret_cast<const float4*>(Ce);
-          for (int q = m; q < CBLK / 4; q += TEAM) offd |= offdiag_nonzero(c4[q], 4 * q);
+          offd |= scan_offdiag<TEAM>(Ce, m);
           float* dgt = W.diag(t);
 #pragma unroll
           for (int s3 = 0; s3 < 3; ++s3)
@@ -769,7 +784,19 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
   if (p.trace != nullptr && writer)
     for (int it = 0; it < p.max_iter; ++it) p.trace[b * p.max_iter + it] = (int8_t)-128;
 
-  // ---- initial open-loop rollout with U_init into slot 0 -----------------------
+  const bool sigm = p.sig.p != nullptr;
+  const float* sgrow = sigm ? p.sig.p + bw * (int64_t)(2 * NT) * T : nullptr;
+  // c_t (and, from policy parameters, diag C_t) of every step into the cost
+  // records, all (t, k) at once; the loads complete behind the rollout below
+#pragma unroll 4
+  for (int f = i; f < T * NT; f += HALF) {
+    const int t = f / NT, k = f - t * NT;
+    float* cr = CR + PCR_F * t;
+    cr[16 + k] = sigm ? sig_c(p.sig, sgrow, T, t, k) : ldg_or0(cb + t * p.c_tstride + k, valid);
+    if (sigm) cr[k] = sig_diag(p.sig, sgrow, T, t, k);
+  }
+
+  // ---- initial open-loop rollout with U_init into slot 0 (and the record table)
   {
     // U_init of every step into the record table first (a step per lane)
     for (int t = i; t < T; t += HALF) {
@@ -785,6 +812,7 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
 #pragma unroll
       for (int a = 0; a < NU; ++a) u[a] = REC[PREC_F * t + NX + a];
       if (writer) store_rec(W.rec(0, t), x, u);
+      if (i == 0) store_rec(reinterpret_cast<float4*>(REC + PREC_F * t), x, u);
       float xn[NX];
       drone_step(x, u, dt, xn);
 #pragma unroll
@@ -794,8 +822,6 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
   }
   __syncwarp();
 
-  const bool sigm = p.sig.p != nullptr;
-  const float* sgrow = sigm ? p.sig.p + bw * (int64_t)(2 * NT) * T : nullptr;
   PairCPipe cpipe{sigm ? nullptr : p.C + bw * p.C_bstride * CBLK, p.C_tstride, sh + PC0, i};
   bool diag = sigm;
   bool offd = false;
@@ -839,23 +865,18 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
     float cost_q = 0.0f, cost_l = 0.0f;
     const bool first = (it == 0);
     if (!diag) cpipe.issue(T - 1);
-    // prologue: every step's nominal record and Jacobian table (a step per lane)
+    // prologue: every step's nominal record (already in the table on the
+    // first pass: the initial rollout wrote it) and Jacobian table, a step per lane
     for (int t = i; t < T; t += HALF) {
       float xb[NX], ub[NU];
-      const float4* r4 = W.rec(nom, t);
-      const float4 q0 = r4[0], q1 = r4[1], q2 = r4[2], q3 = r4[3];
       float4* d4 = reinterpret_cast<float4*>(REC + PREC_F * t);
-      d4[0] = q0; d4[1] = q1; d4[2] = q2; d4[3] = q3;
+      if (!first) {
+        const float4* r4 = W.rec(nom, t);
+        const float4 q0 = r4[0], q1 = r4[1], q2 = r4[2], q3 = r4[3];
+        d4[0] = q0; d4[1] = q1; d4[2] = q2; d4[3] = q3;
+      }
       load_rec(reinterpret_cast<const float4*>(d4), xb, ub);
       jtab_write(JT + PJT_F * t, drone_jac(xb, ub, dt));
-      if (first) {  // c_t (and, from policy parameters, diag C_t) into the step's cost record
-        float* cr = CR + PCR_F * t;
-#pragma unroll
-        for (int k = 0; k < NT; ++k) {
-          cr[16 + k] = sigm ? sig_c(p.sig, sgrow, T, t, k) : ldg_or0(cb + t * p.c_tstride + k, valid);
-          if (sigm) cr[k] = sig_diag(p.sig, sgrow, T, t, k);
-        }
-      }
     }
     __syncwarp();
     for (int t = T - 1; t >= 0; --t) {
@@ -902,8 +923,7 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
         if (!sigm) {
           if (i < NT) cr[i] = Ce[i * (NT + 1)];
           if (p.diag_cache && valid) {
-            const float4* c4 = reinterpret_cast<const float4*>(Ce);
-            for (int q = i; q < CBLK / 4; q += HALF) offd |= offdiag_nonzero(c4[q], 4 * q);
+            offd |= scan_offdiag<HALF>(Ce, i);
           }
         }
       }
@@ -1107,12 +1127,14 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
   if (valid) {
     const float* nrec = reinterpret_cast<const float*>(W.rec(nom, 0));
     const int64_t rstride = p.S * TRJ_REC;
+#pragma unroll 4
     for (int f = i; f < (T + 1) * NX; f += HALF) {
       const int t = f / NX, k = f - t * NX;
       const float xv = nrec[t * rstride + k];
       finite &= isfinite(xv);
       p.X[b * (T + 1) * NX + f] = xv;
     }
+#pragma unroll 4
     for (int f = i; f < T * NU; f += HALF) {
       const int t = f / NU, a = f - t * NU;
       const float uv = nrec[t * rstride + NX + a];
