@@ -276,6 +276,23 @@ static __device__ __noinline__ void svd_inverse4(const float* M, float* Mi) {
 }
 
 // --------------------------------------------------------------------------
+// Packed FP32 (sm_100): one instruction works on a pair of floats held in a
+// 64-bit register pair; each component rounds exactly as fmaf / __fadd_rn /
+// __fmul_rn, so a pair of independent scalar operations becomes one
+// instruction with the same bits. One exception, measured on B200: a packed
+// multiply whose result feeds a packed add can be fused by the code
+// generator into one packed FMA (a single rounding), even with -fmad=false
+// and even from inline PTX with .rn. The kernels therefore never feed mul2
+// into add2; a packed product only starts an FMA chain (as the addend of
+// fma2, where no fusion is possible).
+// --------------------------------------------------------------------------
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 dup2(float a) { return make_float2(a, a); }
+__device__ __forceinline__ float2 ld2(const float* p) { return *reinterpret_cast<const float2*>(p); }
+
+// --------------------------------------------------------------------------
 // cp.async: 16-byte global -> shared copies that complete in the background
 // --------------------------------------------------------------------------
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {

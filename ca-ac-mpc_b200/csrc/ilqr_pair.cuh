@@ -25,6 +25,7 @@
 #pragma once
 
 #include <atomic>
+#include <type_traits>
 
 #include "ilqr_device.cuh"
 #include "ilqr_kernels.h"
@@ -40,18 +41,20 @@ constexpr int64_t PAIR_MAX_B = 2048;
 constexpr int PAIR_MAX_T = 64;
 
 // Per-element shared-memory area (floats; float4 fields 16-byte aligned).
+// Matrices are row-major with rows of 12 floats, so that a float4 load gives
+// four columns of a row: two packed pairs.
 constexpr int PC0 = 0;       // [2][196] C_t blocks (double buffer; diagonal mode uses block 0)
-constexpr int PVAT = 392;    // [10][12] columns of V A: VAT[c][vat_pos(r)]
+constexpr int PVA = 392;     // [10][12] rows of V A
 constexpr int PVB = 512;     // [10][4]  rows of V B
 constexpr int PV = 552;      // [12]     v (v_k at PV + 1 + k: v[3..6], v[7..9] are aligned float4s)
 constexpr int PQUU = 564;    // [4][4]   Q_uu rows (reg added once)
 constexpr int PQU = 580;     // [4]      q_u
-constexpr int PKC = 584;     // [10][4]  K columns (the four gains of state c)
-constexpr int PKF = 624;     // [4]      k
-constexpr int PQXU = 628;    // [10][4]  Q_xu rows
-constexpr int PS = 668;      // [16]     rowdots s_i = (C_t tau)_i (first-pass objective)
-constexpr int PCV = 684;     // [16]     c_t
-constexpr int PSV = 700;     // [32]     SVD fallback: Q, its inverse
+constexpr int PKR = 584;     // [4][12]  rows of K (gain a of every state)
+constexpr int PKF = 632;     // [4]      k
+constexpr int PQUX = 636;    // [4][12]  rows of Q_ux (Q_xu[c][a] at PQUX + 12 a + c)
+constexpr int PS = 684;      // [16]     rowdots s_i = (C_t tau)_i (first-pass objective)
+constexpr int PCV = 700;     // [16]     c_t
+constexpr int PSV = 716;     // [32]     SVD fallback: Q, its inverse
 constexpr int PBASE = 752;   // end of the fixed part of the area
 // Per-step tables after the fixed part (floats per step): the nominal record
 // (x, u; 16), the Jacobian table (32, below), the gains (ten K columns and k;
@@ -91,10 +94,6 @@ __device__ __forceinline__ Jac jtab_read(const float* jt) {
   J.bv0 = d.x; J.bv1 = d.y; J.bv2 = d.z;
   return J;
 }
-
-// Position of row r of V A inside a column of VAT: rows 3..9 first (two
-// aligned float4 loads give them), then rows 0..2.
-__device__ __forceinline__ int vat_pos(int r) { return r >= 3 ? r - 3 : r + 7; }
 
 // Coefficients of row r (0..13) in the form of the header comment.
 // (Evaluated once per kernel on a probe Jacobian whose fields are distinct
@@ -177,9 +176,10 @@ __device__ __forceinline__ bool pair_riccati(float (&Vr)[NX], float& vr, const J
     float va[NX], vb[NU];
     row_VA_VB(J, Vr, va, vb);
     if (i < NX) {
-      const int ps = vat_pos(i);
-#pragma unroll
-      for (int c = 0; c < NX; ++c) sh[PVAT + c * 12 + ps] = va[c];
+      float* row = sh + PVA + 12 * i;
+      *reinterpret_cast<float4*>(row) = make_float4(va[0], va[1], va[2], va[3]);
+      *reinterpret_cast<float4*>(row + 4) = make_float4(va[4], va[5], va[6], va[7]);
+      *reinterpret_cast<float2*>(row + 8) = make_float2(va[8], va[9]);
       *reinterpret_cast<float4*>(sh + PVB + 4 * i) = make_float4(vb[0], vb[1], vb[2], vb[3]);
       sh[PV + 1 + i] = vr;
     }
@@ -188,40 +188,44 @@ __device__ __forceinline__ bool pair_riccati(float (&Vr)[NX], float& vr, const J
 
   // ---- Q_xu rows and q_x (lanes 0..9), Q_uu rows and q_u (lanes 10..13) -------
   const int r = i < NT ? i : NT - 1;
+  // the row's coefficients as packed pairs (the same value in both halves)
+  float2 c2[7];
+#pragma unroll
+  for (int s = 0; s < 7; ++s) c2[s] = dup2(c[s]);
+  const float2 c72 = dup2(c7);
   float Qr[NU], qr;
   {
-    float4 acc4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    float2 acc01 = make_float2(0.0f, 0.0f), acc23 = make_float2(0.0f, 0.0f);
     float accv = 0.0f;
     const float4 v36 = *reinterpret_cast<const float4*>(sh + PV + 4);
     const float4 v79 = *reinterpret_cast<const float4*>(sh + PV + 8);
     const float vs[7] = {v36.x, v36.y, v36.z, v36.w, v79.x, v79.y, v79.z};
 #pragma unroll
     for (int s = 0; s < 7; ++s) {
-      const float4 y = *reinterpret_cast<const float4*>(sh + PVB + 4 * (3 + s));
-      acc4.x = fmaf(c[s], y.x, acc4.x);
-      acc4.y = fmaf(c[s], y.y, acc4.y);
-      acc4.z = fmaf(c[s], y.z, acc4.z);
-      acc4.w = fmaf(c[s], y.w, acc4.w);
+      const float* y = sh + PVB + 4 * (3 + s);
+      acc01 = fma2(c2[s], ld2(y), acc01);
+      acc23 = fma2(c2[s], ld2(y + 2), acc23);
       accv = fmaf(c[s], vs[s], accv);
     }
-    const float4 o = *reinterpret_cast<const float4*>(sh + PVB + 4 * own);
-    const float2* Cr = reinterpret_cast<const float2*>(Ce + r * NT + NX);
-    const float2 cr0 = Cr[0], cr1 = Cr[1];
-    Qr[0] = cr0.x + fmaf(c7, o.x, acc4.x);
-    Qr[1] = cr0.y + fmaf(c7, o.y, acc4.y);
-    Qr[2] = cr1.x + fmaf(c7, o.z, acc4.z);
-    Qr[3] = cr1.y + fmaf(c7, o.w, acc4.w);
+    const float* o = sh + PVB + 4 * own;
+    const float* Cr = Ce + r * NT + NX;
+    float2 q01 = add2(ld2(Cr), fma2(c72, ld2(o), acc01));
+    float2 q23 = add2(ld2(Cr + 2), fma2(c72, ld2(o + 2), acc23));
     if (r >= NX) {
-#pragma unroll
-      for (int a = 0; a < NU; ++a) Qr[a] = Qr[a] + (r - NX == a ? reg : 0.0f);
+      q01 = add2(q01, make_float2(r - NX == 0 ? reg : 0.0f, r - NX == 1 ? reg : 0.0f));
+      q23 = add2(q23, make_float2(r - NX == 2 ? reg : 0.0f, r - NX == 3 ? reg : 0.0f));
     }
+    Qr[0] = q01.x; Qr[1] = q01.y; Qr[2] = q23.x; Qr[3] = q23.y;
     qr = lx + fmaf(c7, sh[PV + 1 + own], accv);
   }
   if (i >= NX && i < NT) {
     *reinterpret_cast<float4*>(sh + PQUU + 4 * (i - NX)) = make_float4(Qr[0], Qr[1], Qr[2], Qr[3]);
     sh[PQU + i - NX] = qr;
   }
-  if (i < NX) *reinterpret_cast<float4*>(sh + PQXU + 4 * i) = make_float4(Qr[0], Qr[1], Qr[2], Qr[3]);
+  if (i < NX) {
+#pragma unroll
+    for (int a = 0; a < NU; ++a) sh[PQUX + 12 * a + i] = Qr[a];
+  }
   __syncwarp();
 
   // ---- gains: every lane factors Q_uu, lane i < 10 solves column i of K,
@@ -286,7 +290,10 @@ __device__ __forceinline__ bool pair_riccati(float (&Vr)[NX], float& vr, const J
 #pragma unroll
     for (int a = 0; a < NU; ++a) Kr[a] = -sol[a];
   }
-  if (i < NX) *reinterpret_cast<float4*>(sh + PKC + 4 * i) = make_float4(Kr[0], Kr[1], Kr[2], Kr[3]);
+  if (i < NX) {
+#pragma unroll
+    for (int a = 0; a < NU; ++a) sh[PKR + 12 * a + i] = Kr[a];
+  }
   if (i == NX) *reinterpret_cast<float4*>(sh + PKF) = make_float4(Kr[0], Kr[1], Kr[2], Kr[3]);
   // W_r = K_r^T Q_uu + Q_xu[r] (team_riccati's wrow)
   float Wr[NU];
@@ -332,40 +339,45 @@ __device__ __forceinline__ bool pair_riccati(float (&Vr)[NX], float& vr, const J
       vr = (qr + t1) + t2;
     }
     // V[i][cc] = (Q_xx[i][cc] + W_i K_cc) + K_i Q_xu[cc], Q_xx[i][cc] from the
-    // columns of V A in the form of the header comment
-    const int po = vat_pos(own);
-    float Ci[NX];
-    {
-      const float2* c2 = reinterpret_cast<const float2*>(Ce + (i < NX ? i : NX - 1) * NT);
+    // rows of V A in the form of the header comment; packed pairs of columns
+    // (cc, cc + 1), every sum in the order of the scalar formula.
+    const float* Crow = Ce + (i < NX ? i : NX - 1) * NT;
+    float2 w2[NU], kr2[NU];
 #pragma unroll
-      for (int q = 0; q < NX / 2; ++q) {
-        const float2 v = c2[q];
-        Ci[2 * q] = v.x;
-        Ci[2 * q + 1] = v.y;
+    for (int a = 0; a < NU; ++a) {
+      w2[a] = dup2(Wr[a]);
+      kr2[a] = dup2(Kr[a]);
+    }
+    // columns c0 .. c0 + 2 NP - 1 (NP packed pairs)
+    auto cols = [&](auto np_tag, int c0) {
+      constexpr int NP = decltype(np_tag)::value;
+      float2 acc[NP];
+#pragma unroll
+      for (int h = 0; h < NP; ++h) acc[h] = make_float2(0.0f, 0.0f);
+#pragma unroll
+      for (int s = 0; s < 7; ++s) {
+        const float* y = sh + PVA + 12 * (3 + s) + c0;
+#pragma unroll
+        for (int h = 0; h < NP; ++h) acc[h] = fma2(c2[s], ld2(y + 2 * h), acc[h]);
       }
-    }
 #pragma unroll
-    for (int cc = 0; cc < NX; ++cc) {
-      const float* col = sh + PVAT + cc * 12;
-      const float4 y0 = *reinterpret_cast<const float4*>(col);
-      const float4 y1 = *reinterpret_cast<const float4*>(col + 4);
-      const float y[7] = {y0.x, y0.y, y0.z, y0.w, y1.x, y1.y, y1.z};
-      float acc = 0.0f;
+      for (int h = 0; h < NP; ++h) {
+        const int cc = c0 + 2 * h;
+        const float2 q = add2(ld2(Crow + cc), fma2(c72, ld2(sh + PVA + 12 * own + cc), acc[h]));
+        float2 t1 = mul2(w2[0], ld2(sh + PKR + cc));
 #pragma unroll
-      for (int s = 0; s < 7; ++s) acc = fmaf(c[s], y[s], acc);
-      const float q = Ci[cc] + fmaf(c7, col[po], acc);
-      const float4 k4 = *reinterpret_cast<const float4*>(sh + PKC + 4 * cc);
-      const float4 q4 = *reinterpret_cast<const float4*>(sh + PQXU + 4 * cc);
-      float t1 = Wr[0] * k4.x;
-      t1 = fmaf(Wr[1], k4.y, t1);
-      t1 = fmaf(Wr[2], k4.z, t1);
-      t1 = fmaf(Wr[3], k4.w, t1);
-      float t2 = Kr[0] * q4.x;
-      t2 = fmaf(Kr[1], q4.y, t2);
-      t2 = fmaf(Kr[2], q4.z, t2);
-      t2 = fmaf(Kr[3], q4.w, t2);
-      Vr[cc] = (q + t1) + t2;
-    }
+        for (int a = 1; a < NU; ++a) t1 = fma2(w2[a], ld2(sh + PKR + 12 * a + cc), t1);
+        float2 t2 = mul2(kr2[0], ld2(sh + PQUX + cc));
+#pragma unroll
+        for (int a = 1; a < NU; ++a) t2 = fma2(kr2[a], ld2(sh + PQUX + 12 * a + cc), t2);
+        const float2 v = add2(add2(q, t1), t2);
+        Vr[cc] = v.x;
+        Vr[cc + 1] = v.y;
+      }
+    };
+    cols(std::integral_constant<int, 2>{}, 0);
+    cols(std::integral_constant<int, 2>{}, 4);
+    cols(std::integral_constant<int, 1>{}, 8);
   }
   __syncwarp();  // C_t and the area are no longer read
   return ok;

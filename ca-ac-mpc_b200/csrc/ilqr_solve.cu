@@ -143,36 +143,45 @@ __device__ __forceinline__ float clamp_nan(float v, float lo, float hi) {
 // u = U_t + a k_t + a (K_t (x - X_t)), then max(., u_min), min(., u_max).
 // kcol(j) returns column j of K_t (the four gains of state j); each row of
 // K_t (x - X_t) is accumulated over j in index order.
+// The unclamped candidate ub + (a k + a (K dx)). K dx runs as packed FMA
+// chains (controls 0, 1 and 2, 3), in the scalar formula's order; the rest
+// stays scalar: a packed multiply whose product feeds a packed add may be
+// fused into one packed FMA by the code generator, which rounds once
+// instead of twice (measured on B200), so no packed product here ends in an add.
+template <class KCol>
+__device__ __forceinline__ void candidate_raw(const float (&x)[NX], const float (&xb)[NX], const float (&ub)[NU],
+                                              KCol&& kcol, const float (&kt)[NU], float al, float (&v)[NU]) {
+  float dx[NX];
+#pragma unroll
+  for (int i = 0; i < NX; ++i) dx[i] = x[i] - xb[i];
+  float2 kd01, kd23;
+  {
+    const float4 c = kcol(0);
+    const float2 d = dup2(dx[0]);
+    kd01 = mul2(make_float2(c.x, c.y), d);
+    kd23 = mul2(make_float2(c.z, c.w), d);
+  }
+#pragma unroll
+  for (int j = 1; j < NX; ++j) {
+    const float4 c = kcol(j);
+    const float2 d = dup2(dx[j]);
+    kd01 = fma2(make_float2(c.x, c.y), d, kd01);
+    kd23 = fma2(make_float2(c.z, c.w), d, kd23);
+  }
+  const float kd[NU] = {kd01.x, kd01.y, kd23.x, kd23.y};
+#pragma unroll
+  for (int a = 0; a < NU; ++a) v[a] = ub[a] + (al * kt[a] + al * kd[a]);
+}
+
 template <class KCol>
 __device__ __forceinline__ void candidate_u(const float (&x)[NX], const float (&xb)[NX], const float (&ub)[NU],
                                             KCol&& kcol, const float (&kt)[NU], float al,
                                             const float* __restrict__ lo, const float* __restrict__ hi,
                                             float (&u)[NU]) {
-  float dx[NX];
+  float v[NU];
+  candidate_raw(x, xb, ub, kcol, kt, al, v);
 #pragma unroll
-  for (int i = 0; i < NX; ++i) dx[i] = x[i] - xb[i];
-  float kd[NU];
-  {
-    const float4 c = kcol(0);
-    kd[0] = c.x * dx[0];
-    kd[1] = c.y * dx[0];
-    kd[2] = c.z * dx[0];
-    kd[3] = c.w * dx[0];
-  }
-#pragma unroll
-  for (int j = 1; j < NX; ++j) {
-    const float4 c = kcol(j);
-    kd[0] = fmaf(c.x, dx[j], kd[0]);
-    kd[1] = fmaf(c.y, dx[j], kd[1]);
-    kd[2] = fmaf(c.z, dx[j], kd[2]);
-    kd[3] = fmaf(c.w, dx[j], kd[3]);
-  }
-#pragma unroll
-  for (int a = 0; a < NU; ++a) {
-    float v = ub[a] + (al * kt[a] + al * kd[a]);
-    if (lo != nullptr) v = clamp_nan(v, __ldg(lo + a), __ldg(hi + a));
-    u[a] = v;
-  }
+  for (int a = 0; a < NU; ++a) u[a] = lo != nullptr ? clamp_nan(v[a], __ldg(lo + a), __ldg(hi + a)) : v[a];
 }
 
 // candidate_u with the box in registers (the same operations).
@@ -180,31 +189,10 @@ template <class KCol>
 __device__ __forceinline__ void candidate_u_reg(const float (&x)[NX], const float (&xb)[NX], const float (&ub)[NU],
                                                 KCol&& kcol, const float (&kt)[NU], float al, bool bounds,
                                                 const float (&lo)[NU], const float (&hi)[NU], float (&u)[NU]) {
-  float dx[NX];
+  float v[NU];
+  candidate_raw(x, xb, ub, kcol, kt, al, v);
 #pragma unroll
-  for (int i = 0; i < NX; ++i) dx[i] = x[i] - xb[i];
-  float kd[NU];
-  {
-    const float4 c = kcol(0);
-    kd[0] = c.x * dx[0];
-    kd[1] = c.y * dx[0];
-    kd[2] = c.z * dx[0];
-    kd[3] = c.w * dx[0];
-  }
-#pragma unroll
-  for (int j = 1; j < NX; ++j) {
-    const float4 c = kcol(j);
-    kd[0] = fmaf(c.x, dx[j], kd[0]);
-    kd[1] = fmaf(c.y, dx[j], kd[1]);
-    kd[2] = fmaf(c.z, dx[j], kd[2]);
-    kd[3] = fmaf(c.w, dx[j], kd[3]);
-  }
-#pragma unroll
-  for (int a = 0; a < NU; ++a) {
-    float v = ub[a] + (al * kt[a] + al * kd[a]);
-    if (bounds) v = clamp_nan(v, lo[a], hi[a]);
-    u[a] = v;
-  }
+  for (int a = 0; a < NU; ++a) u[a] = bounds ? clamp_nan(v[a], lo[a], hi[a]) : v[a];
 }
 
 // Whether flat index f (< 196) of a C block is on its diagonal (15 i):

@@ -30,8 +30,8 @@ constexpr int X_VA = 0;       // [10][10] rows of V A
 constexpr int X_VB = 100;     // [10][4]  rows of V B
 constexpr int X_V = 140;      // [10]     v
 constexpr int X_LU = 152;     // [4]      l_u
-constexpr int X_K = 100;      // [10][4]  K transposed: column c of K at X_K + 4c (over V B)
-constexpr int X_QXU = 140;    // [10][4]  Q_xu rows (over v, l_u)
+constexpr int X_K = 100;      // [4][10]  K: gain row a at X_K + 10a (over V B)
+constexpr int X_QXU = 140;    // [4][10]  Q_ux: Q_xu[c][a] at X_QXU + 10a + c (over v, l_u)
 constexpr uint32_t TSLAB_BYTES = EPW * CBLK * 4u;  // bytes one TMA box delivers
 
 // Register tiers. Each kernel is compiled for three minimum residencies
@@ -77,6 +77,8 @@ __device__ __forceinline__ float sig_c(const SigmoidCost& s, const float* q, int
 struct DenseC {
   const float* Ct;
   __device__ __forceinline__ float operator()(int i, int j) const { return Ct[i * NT + j]; }
+  // entries (i, j) and (i, j + 1); j even (8-byte aligned: NT is even)
+  __device__ __forceinline__ float2 pair(int i, int j) const { return ld2(Ct + i * NT + j); }
 };
 
 // Coefficients A[k][RA] for k = 3..9 and the own-row coefficient, for lane m.
@@ -176,32 +178,39 @@ __device__ __forceinline__ bool team_riccati(float (&Va)[NX], float (&Vb)[NX], f
   coef_a(J, m, ca);
   const float cb = (m >= 2) ? J.dt : 0.0f;
   const int pb = (m >= 2) ? m - 2 : 0;
+  // Coefficients as packed pairs (the same value in both halves): every
+  // product below pairs two columns of one row.
+  float2 c2[8];
+#pragma unroll
+  for (int s = 0; s < 8; ++s) c2[s] = dup2(ca[s]);
+  const float2 cb2 = dup2(cb);
   float Qxa[NU], Qxb[NU], qxa, qxb;
   {
     // RA: sum over rows 3..9 of V B (and v), then the own row.
-    float4 acc4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    float2 acc01 = make_float2(0.0f, 0.0f), acc23 = make_float2(0.0f, 0.0f);
     float accv = 0.0f;
 #pragma unroll
     for (int s = 0; s < 7; ++s) {
-      const float4 r = *reinterpret_cast<const float4*>(xc + X_VB + (3 + s) * NU);
-      acc4.x = fmaf(ca[s], r.x, acc4.x);
-      acc4.y = fmaf(ca[s], r.y, acc4.y);
-      acc4.z = fmaf(ca[s], r.z, acc4.z);
-      acc4.w = fmaf(ca[s], r.w, acc4.w);
+      const float* r = xc + X_VB + (3 + s) * NU;
+      acc01 = fma2(c2[s], ld2(r), acc01);
+      acc23 = fma2(c2[s], ld2(r + 2), acc23);
       accv = fmaf(ca[s], xc[X_V + 3 + s], accv);
     }
     {
-      const float4 own = *reinterpret_cast<const float4*>(xc + X_VB + ra * NU);
-      Qxa[0] = Ct(ra, NX + 0) + fmaf(ca[7], own.x, acc4.x);
-      Qxa[1] = Ct(ra, NX + 1) + fmaf(ca[7], own.y, acc4.y);
-      Qxa[2] = Ct(ra, NX + 2) + fmaf(ca[7], own.z, acc4.z);
-      Qxa[3] = Ct(ra, NX + 3) + fmaf(ca[7], own.w, acc4.w);
+      const float* own = xc + X_VB + ra * NU;
+      const float2 q01 = add2(Ct.pair(ra, NX), fma2(c2[7], ld2(own), acc01));
+      const float2 q23 = add2(Ct.pair(ra, NX + 2), fma2(c2[7], ld2(own + 2), acc23));
+      Qxa[0] = q01.x; Qxa[1] = q01.y; Qxa[2] = q23.x; Qxa[3] = q23.y;
     }
     qxa = lxa + fmaf(ca[7], va_, accv);
     // RB: own row plus cb times row pb.
-#pragma unroll
-    for (int a = 0; a < NU; ++a)
-      Qxb[a] = Ct(rb, NX + a) + fmaf(cb, xc[X_VB + pb * NU + a], xc[X_VB + rb * NU + a]);
+    {
+      const float* pr = xc + X_VB + pb * NU;
+      const float* own = xc + X_VB + rb * NU;
+      const float2 q01 = add2(Ct.pair(rb, NX), fma2(cb2, ld2(pr), ld2(own)));
+      const float2 q23 = add2(Ct.pair(rb, NX + 2), fma2(cb2, ld2(pr + 2), ld2(own + 2)));
+      Qxb[0] = q01.x; Qxb[1] = q01.y; Qxb[2] = q23.x; Qxb[3] = q23.y;
+    }
     qxb = lxb + fmaf(cb, xc[X_V + pb], vb_);
   }
   float Quu[NU][NU], qu[NU];
@@ -209,21 +218,22 @@ __device__ __forceinline__ bool team_riccati(float (&Va)[NX], float (&Vb)[NX], f
     // Q_uu = l_uu + B^T (V B) + reg I: B^T rows are bv over the velocity rows
     // (first control) and 0.5 dt Xi(q) over the quaternion rows (body rates);
     // accumulated row by row of V B in index order.
-    float acc[NU][NU];
+    // (columns paired: acc[a][h] holds columns 2h, 2h + 1 of row a)
+    float2 acc[NU][2];
 #pragma unroll
     for (int s = 0; s < 7; ++s) {
-      const float4 r4 = *reinterpret_cast<const float4*>(xc + X_VB + (3 + s) * NU);
-      const float r[NU] = {r4.x, r4.y, r4.z, r4.w};
+      const float* r = xc + X_VB + (3 + s) * NU;
 #pragma unroll
-      for (int b = 0; b < NU; ++b) {
+      for (int h = 0; h < 2; ++h) {
+        const float2 rh = ld2(r + 2 * h);
         if (s >= 4) {
-          const float cf = bvf(J, s - 4);
-          acc[0][b] = (s == 4) ? cf * r[b] : fmaf(cf, r[b], acc[0][b]);
+          const float2 cf = dup2(bvf(J, s - 4));
+          acc[0][h] = (s == 4) ? mul2(cf, rh) : fma2(cf, rh, acc[0][h]);
         } else {
 #pragma unroll
           for (int kk = 0; kk < 3; ++kk) {
-            const float cf = bqw(J, s, kk);
-            acc[1 + kk][b] = (s == 0) ? cf * r[b] : fmaf(cf, r[b], acc[1 + kk][b]);
+            const float2 cf = dup2(bqw(J, s, kk));
+            acc[1 + kk][h] = (s == 0) ? mul2(cf, rh) : fma2(cf, rh, acc[1 + kk][h]);
           }
         }
       }
@@ -231,8 +241,12 @@ __device__ __forceinline__ bool team_riccati(float (&Va)[NX], float (&Vb)[NX], f
 #pragma unroll
     for (int a = 0; a < NU; ++a)
 #pragma unroll
-      for (int b = 0; b < NU; ++b)
-        Quu[a][b] = (Ct(NX + a, NX + b) + acc[a][b]) + (a == b ? reg : 0.0f);
+      for (int h = 0; h < 2; ++h) {
+        const float2 rg = make_float2(a == 2 * h ? reg : 0.0f, a == 2 * h + 1 ? reg : 0.0f);
+        const float2 q = add2(add2(Ct.pair(NX + a, NX + 2 * h), acc[a][h]), rg);
+        Quu[a][2 * h] = q.x;
+        Quu[a][2 * h + 1] = q.y;
+      }
     float vq[7];
 #pragma unroll
     for (int s = 0; s < 7; ++s) vq[s] = xc[X_V + 3 + s];
@@ -324,10 +338,13 @@ __device__ __forceinline__ bool team_riccati(float (&Va)[NX], float (&Vb)[NX], f
   }
   if (any_fallback) __syncwarp();  // the fallback inverses are read; K goes over them
   // K columns and Q_xu rows -> exchange (over V B, v, l_u)
-  *reinterpret_cast<float4*>(xc + X_K + ra * NU) = make_float4(Ka[0], Ka[1], Ka[2], Ka[3]);
-  *reinterpret_cast<float4*>(xc + X_K + rb * NU) = make_float4(Kb[0], Kb[1], Kb[2], Kb[3]);
-  *reinterpret_cast<float4*>(xc + X_QXU + ra * NU) = make_float4(Qxa[0], Qxa[1], Qxa[2], Qxa[3]);
-  *reinterpret_cast<float4*>(xc + X_QXU + rb * NU) = make_float4(Qxb[0], Qxb[1], Qxb[2], Qxb[3]);
+#pragma unroll
+  for (int a = 0; a < NU; ++a) {
+    xc[X_K + a * NX + ra] = Ka[a];
+    xc[X_K + a * NX + rb] = Kb[a];
+    xc[X_QXU + a * NX + ra] = Qxa[a];
+    xc[X_QXU + a * NX + rb] = Qxb[a];
+  }
 
   // ---- value update for my rows -------------------------------------------------
   // (K^T Q_uu) K + Q_xu K is formed as (K^T Q_uu + Q_xu) K: one 4-term
@@ -376,47 +393,48 @@ __device__ __forceinline__ bool team_riccati(float (&Va)[NX], float (&Vb)[NX], f
   va_ = vrow(Ka, Qxa, Wa, qxa);
   vb_ = vrow(Kb, Qxb, Wb, qxb);
   __syncwarp();  // K and Q_xu rows of the whole team are in the exchange
-  // Q_xx entries of my rows are formed column by column here (A^T (V A) from
-  // the V A rows still in the exchange, plus l_xx), then
-  // V[r][c] = (Q_xx[r][c] + W_r K_c) + K_r Q_xu[c].
+  // Q_xx entries of my rows are formed two columns at a time here (A^T (V A)
+  // from the V A rows still in the exchange, plus l_xx), then
+  // V[r][c] = (Q_xx[r][c] + W_r K_c) + K_r Q_xu[c], every sum in the order
+  // of the scalar formulas (packed pairs: columns c, c + 1).
+  {
+    float2 wa[NU], wb[NU], ka[NU], kb[NU];
 #pragma unroll
-  for (int c = 0; c < NX; c += 2) {
-    float2 qa = make_float2(0.0f, 0.0f);
-#pragma unroll
-    for (int s = 0; s < 7; ++s) {
-      const float2 r = *reinterpret_cast<const float2*>(xc + X_VA + (3 + s) * NX + c);
-      qa.x = fmaf(ca[s], r.x, qa.x);
-      qa.y = fmaf(ca[s], r.y, qa.y);
-    }
-    {
-      const float2 own = *reinterpret_cast<const float2*>(xc + X_VA + ra * NX + c);
-      qa.x = Ct(ra, c) + fmaf(ca[7], own.x, qa.x);
-      qa.y = Ct(ra, c + 1) + fmaf(ca[7], own.y, qa.y);
-    }
-    float2 qb;
-    {
-      const float2 pr = *reinterpret_cast<const float2*>(xc + X_VA + pb * NX + c);
-      const float2 own = *reinterpret_cast<const float2*>(xc + X_VA + rb * NX + c);
-      qb.x = Ct(rb, c) + fmaf(cb, pr.x, own.x);
-      qb.y = Ct(rb, c + 1) + fmaf(cb, pr.y, own.y);
+    for (int a = 0; a < NU; ++a) {
+      wa[a] = dup2(Wa[a]);
+      wb[a] = dup2(Wb[a]);
+      ka[a] = dup2(Ka[a]);
+      kb[a] = dup2(Kb[a]);
     }
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const float4 k4 = *reinterpret_cast<const float4*>(xc + X_K + (c + h) * NU);
-      const float4 q4 = *reinterpret_cast<const float4*>(xc + X_QXU + (c + h) * NU);
-      auto entry = [&](float q, const float (&Wr)[NU], const float (&Kr)[NU]) {
-        float t1 = Wr[0] * k4.x;
-        t1 = fmaf(Wr[1], k4.y, t1);
-        t1 = fmaf(Wr[2], k4.z, t1);
-        t1 = fmaf(Wr[3], k4.w, t1);
-        float t2 = Kr[0] * q4.x;
-        t2 = fmaf(Kr[1], q4.y, t2);
-        t2 = fmaf(Kr[2], q4.z, t2);
-        t2 = fmaf(Kr[3], q4.w, t2);
-        return (q + t1) + t2;
+    for (int c = 0; c < NX; c += 2) {
+      float2 qa = make_float2(0.0f, 0.0f);
+#pragma unroll
+      for (int s = 0; s < 7; ++s) qa = fma2(c2[s], ld2(xc + X_VA + (3 + s) * NX + c), qa);
+      qa = add2(Ct.pair(ra, c), fma2(c2[7], ld2(xc + X_VA + ra * NX + c), qa));
+      const float2 qb = add2(Ct.pair(rb, c), fma2(cb2, ld2(xc + X_VA + pb * NX + c), ld2(xc + X_VA + rb * NX + c)));
+      float2 kp[NU], qp[NU];
+#pragma unroll
+      for (int a = 0; a < NU; ++a) {
+        kp[a] = ld2(xc + X_K + a * NX + c);
+        qp[a] = ld2(xc + X_QXU + a * NX + c);
+      }
+      auto entry = [&](float2 q, const float2 (&Wr)[NU], const float2 (&Kr)[NU]) {
+        float2 t1 = mul2(Wr[0], kp[0]);
+        t1 = fma2(Wr[1], kp[1], t1);
+        t1 = fma2(Wr[2], kp[2], t1);
+        t1 = fma2(Wr[3], kp[3], t1);
+        float2 t2 = mul2(Kr[0], qp[0]);
+        t2 = fma2(Kr[1], qp[1], t2);
+        t2 = fma2(Kr[2], qp[2], t2);
+        t2 = fma2(Kr[3], qp[3], t2);
+        return add2(add2(q, t1), t2);
       };
-      Va[c + h] = entry(h ? qa.y : qa.x, Wa, Ka);
-      Vb[c + h] = entry(h ? qb.y : qb.x, Wb, Kb);
+      const float2 va2 = entry(qa, wa, ka), vb2 = entry(qb, wb, kb);
+      Va[c] = va2.x;
+      Va[c + 1] = va2.y;
+      Vb[c] = vb2.x;
+      Vb[c + 1] = vb2.y;
     }
   }
   after_c();  // syncs the warp: C_t and the exchange area are no longer read
