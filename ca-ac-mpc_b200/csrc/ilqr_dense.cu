@@ -43,21 +43,24 @@ constexpr int SM_COUNT = 148;      // B200 SMs (the launch's one-wave test)
 // Shared memory of one element (floats). The block size is an odd multiple
 // of 16 floats, so the two elements of a warp use opposite halves of the
 // banks for the same offsets.
-constexpr int S_V = 0;       // V [13][13]
-constexpr int S_A = 172;     // A_t [13][13]
-constexpr int S_B = 344;     // B_t [13][4]
-constexpr int S_VB = 396;    // V B [13][4]
-constexpr int S_K = 448;     // K_t [4][13]
-constexpr int S_M = 500;     // Q_uu K + Q_ux [4][13]
-constexpr int S_VV = 552;    // v [13]
-constexpr int S_Z = 568;     // nominal x_t, u_t [20]
-constexpr int S_QUU = 588;   // Q_uu [4][4] (regularised once)
-constexpr int S_QU = 604;    // q_u [4]
-constexpr int S_KF = 608;    // k_t [4]
-constexpr int S_MK = 612;    // Q_uu k + q_u [4]
-constexpr int S_SVD = 616;   // SVD fallback: matrix [16], inverse [16]
-constexpr int S_TAU = 656;   // per-lane tau scratch of the rollouts [16][17]
-constexpr int S_LS2 = 928;   // second rollout staging buffer (the first is at 0)
+// V, A_t, K_t and M have rows of LDM = 14 floats (13 used), so that two
+// adjacent columns of a row are one 8-byte load: a packed pair.
+constexpr int LDM = 14;
+constexpr int S_V = 0;       // V [13][14]
+constexpr int S_A = 184;     // A_t [13][14]
+constexpr int S_B = 368;     // B_t [13][4]
+constexpr int S_VB = 420;    // V B [13][4]
+constexpr int S_K = 472;     // K_t [4][14]
+constexpr int S_M = 528;     // Q_uu K + Q_ux [4][14]
+constexpr int S_VV = 584;    // v [13]
+constexpr int S_Z = 600;     // nominal x_t, u_t [20]
+constexpr int S_QUU = 620;   // Q_uu [4][4] (regularised once)
+constexpr int S_QU = 636;    // q_u [4]
+constexpr int S_KF = 640;    // k_t [4]
+constexpr int S_MK = 644;    // Q_uu k + q_u [4]
+constexpr int S_SVD = 648;   // SVD fallback: matrix [16], inverse [16]
+constexpr int S_TAU = 680;   // per-lane tau scratch of the rollouts [16][17]
+constexpr int S_LS2 = 952;   // second rollout staging buffer (the first is at 0)
 constexpr int S_ELEM = 1360; // floats per element in the solve (85 x 16)
 constexpr int S_STG = 944;   // backward: two buffers staging a step's inputs
 constexpr int S_ELEM_BWD = 1616;  // floats per element in the backward (101 x 16)
@@ -268,26 +271,40 @@ __device__ __forceinline__ bool riccati_step(float* sm, int g, bool rowx, bool l
   // ---- P1 ---------------------------------------------------------------
   float acol[NX];
 #pragma unroll
-  for (int k = 0; k < NX; ++k) acol[k] = rowx ? sm[S_A + k * NX + g] : 0.0f;
+  for (int k = 0; k < NX; ++k) acol[k] = rowx ? sm[S_A + k * LDM + g] : 0.0f;
   float w[NX];
   float qx = 0.0f;
+  // the column of A as packed pairs (the same value in both halves)
+  float2 ac2[NX];
+#pragma unroll
+  for (int k = 0; k < NX; ++k) ac2[k] = dup2(acol[k]);
   if (rowx) {
-    float vb[NU];
+    {
+      // (V B)_g. over the two column pairs of B
+      float2 vb[2];
 #pragma unroll
-    for (int a = 0; a < NU; ++a) {
-      float s = Vr[B_ROW0] * sm[S_B + B_ROW0 * NU + a];
+      for (int h = 0; h < 2; ++h) {
+        float2 s = mul2(dup2(Vr[B_ROW0]), ld2(sm + S_B + B_ROW0 * NU + 2 * h));
 #pragma unroll
-      for (int k = B_ROW0 + 1; k < NX; ++k) s = fmaf(Vr[k], sm[S_B + k * NU + a], s);
-      vb[a] = s;
+        for (int k = B_ROW0 + 1; k < NX; ++k) s = fma2(dup2(Vr[k]), ld2(sm + S_B + k * NU + 2 * h), s);
+        vb[h] = s;
+      }
+      *reinterpret_cast<float4*>(sm + S_VB + g * NU) = make_float4(vb[0].x, vb[0].y, vb[1].x, vb[1].y);
     }
+    // w = (A^T V)_g. by column pairs (j, j + 1), column 12 alone
 #pragma unroll
-    for (int a = 0; a < NU; ++a) sm[S_VB + g * NU + a] = vb[a];
+    for (int j = 0; j < NX - 1; j += 2) {
+      float2 s = mul2(ac2[0], ld2(sm + S_V + j));
 #pragma unroll
-    for (int j = 0; j < NX; ++j) {
-      float s = acol[0] * sm[S_V + j];
+      for (int k = 1; k < NX; ++k) s = fma2(ac2[k], ld2(sm + S_V + k * LDM + j), s);
+      w[j] = s.x;
+      w[j + 1] = s.y;
+    }
+    {
+      float s = acol[0] * sm[S_V + NX - 1];
 #pragma unroll
-      for (int k = 1; k < NX; ++k) s = fmaf(acol[k], sm[S_V + k * NX + j], s);
-      w[j] = s;
+      for (int k = 1; k < NX; ++k) s = fmaf(acol[k], sm[S_V + k * LDM + NX - 1], s);
+      w[NX - 1] = s;
     }
     float s = acol[0] * sm[S_VV];
 #pragma unroll
@@ -307,22 +324,23 @@ __device__ __forceinline__ bool riccati_step(float* sm, int g, bool rowx, bool l
 #pragma unroll
     for (int j = 0; j < NX; ++j) {
       const int k0 = a_col_row(j, 0);
-      float s = w[k0] * sm[S_A + k0 * NX + j];
+      float s = w[k0] * sm[S_A + k0 * LDM + j];
 #pragma unroll
       for (int m = 1; m < 7; ++m) {
         if (m < a_col_nnz(j)) {
           const int k = a_col_row(j, m);
-          s = fmaf(w[k], sm[S_A + k * NX + j], s);
+          s = fmaf(w[k], sm[S_A + k * LDM + j], s);
         }
       }
       qxx[j] = in.cxx[j] + s;
     }
 #pragma unroll
-    for (int a = 0; a < NU; ++a) {
-      float s = acol[0] * sm[S_VB + a];
+    for (int h = 0; h < 2; ++h) {
+      float2 s = mul2(ac2[0], ld2(sm + S_VB + 2 * h));
 #pragma unroll
-      for (int k = 1; k < NX; ++k) s = fmaf(acol[k], sm[S_VB + k * NU + a], s);
-      qxu[a] = in.cxu[a] + s;
+      for (int k = 1; k < NX; ++k) s = fma2(ac2[k], ld2(sm + S_VB + k * NU + 2 * h), s);
+      qxu[2 * h] = in.cxu[2 * h] + s.x;
+      qxu[2 * h + 1] = in.cxu[2 * h + 1] + s.y;
     }
   }
   {
@@ -415,14 +433,14 @@ __device__ __forceinline__ bool riccati_step(float* sm, int g, bool rowx, bool l
 #pragma unroll
     for (int a = 0; a < NU; ++a) {
       Kc[a] = sol[a];
-      sm[S_K + a * NX + g] = sol[a];
+      sm[S_K + a * LDM + g] = sol[a];
     }
 #pragma unroll
     for (int a = 0; a < NU; ++a) {
       float s = Q[a][0] * sol[0];
 #pragma unroll
       for (int b = 1; b < NU; ++b) s = fmaf(Q[a][b], sol[b], s);
-      sm[S_M + a * NX + g] = s + qxu[a];
+      sm[S_M + a * LDM + g] = s + qxu[a];
     }
   } else if (g == NX) {
 #pragma unroll
@@ -441,14 +459,30 @@ __device__ __forceinline__ bool riccati_step(float* sm, int g, bool rowx, bool l
   __syncwarp(wmask);
   // ---- P4: V, v -----------------------------------------------------------
   if (rowx) {
+    float2 kc2[NU], qu2[NU];
 #pragma unroll
-    for (int j = 0; j < NX; ++j) {
-      float s = qxx[j];
+    for (int a = 0; a < NU; ++a) {
+      kc2[a] = dup2(Kc[a]);
+      qu2[a] = dup2(qxu[a]);
+    }
+    // column pairs (j, j + 1), column 12 alone
 #pragma unroll
-      for (int a = 0; a < NU; ++a) s = fmaf(Kc[a], sm[S_M + a * NX + j], s);
+    for (int j = 0; j < NX - 1; j += 2) {
+      float2 s = make_float2(qxx[j], qxx[j + 1]);
 #pragma unroll
-      for (int a = 0; a < NU; ++a) s = fmaf(qxu[a], sm[S_K + a * NX + j], s);
-      Vr[j] = s;
+      for (int a = 0; a < NU; ++a) s = fma2(kc2[a], ld2(sm + S_M + a * LDM + j), s);
+#pragma unroll
+      for (int a = 0; a < NU; ++a) s = fma2(qu2[a], ld2(sm + S_K + a * LDM + j), s);
+      Vr[j] = s.x;
+      Vr[j + 1] = s.y;
+    }
+    {
+      float s = qxx[NX - 1];
+#pragma unroll
+      for (int a = 0; a < NU; ++a) s = fmaf(Kc[a], sm[S_M + a * LDM + NX - 1], s);
+#pragma unroll
+      for (int a = 0; a < NU; ++a) s = fmaf(qxu[a], sm[S_K + a * LDM + NX - 1], s);
+      Vr[NX - 1] = s;
     }
     float s = qx;
 #pragma unroll
@@ -457,7 +491,7 @@ __device__ __forceinline__ bool riccati_step(float* sm, int g, bool rowx, bool l
     for (int a = 0; a < NU; ++a) s = fmaf(qxu[a], sm[S_KF + a], s);
     vi = s;
 #pragma unroll
-    for (int j = 0; j < NX; ++j) sm[S_V + g * NX + j] = Vr[j];
+    for (int j = 0; j < NX; ++j) sm[S_V + g * LDM + j] = Vr[j];
     sm[S_VV + g] = vi;
   }
   return fb;
@@ -466,7 +500,7 @@ __device__ __forceinline__ bool riccati_step(float* sm, int g, bool rowx, bool l
 // Lane g writes row g of A_t, B_t (state-row lanes) at the state and control
 // z = [x_t (13); u_t (4)].
 __device__ __forceinline__ void jacobian_rows(float* sm, const float* z, int g, float dt) {
-  if (g < NX) jac_row(g, z, z + NX, dt, sm + S_A + g * NX, sm + S_B + g * NU);
+  if (g < NX) jac_row(g, z, z + NX, dt, sm + S_A + g * LDM, sm + S_B + g * NU);
 }
 
 // v[i] for a lane-dependent i, without a dynamically indexed local array.
@@ -697,7 +731,7 @@ __global__ void __launch_bounds__(THREADS, MINB) dense_solve_kernel(DenseSolvePa
         }
         vi = s + (cf ? __ldg(cf + g) : 0.0f);
 #pragma unroll
-        for (int j = 0; j < NX; ++j) sm[S_V + g * NX + j] = Vr[j];
+        for (int j = 0; j < NX; ++j) sm[S_V + g * LDM + j] = Vr[j];
         sm[S_VV + g] = vi;
       }
     }
@@ -881,7 +915,7 @@ __global__ void __launch_bounds__(THREADS, 4) dense_backward_kernel(DenseBackwar
 #pragma unroll
     for (int j = 0; j < NX; ++j) {
       Vr[j] = Cf ? __ldg(Cf + g * NT + j) : 0.0f;
-      sm[S_V + g * NX + j] = Vr[j];
+      sm[S_V + g * LDM + j] = Vr[j];
     }
     vi = -__ldg(gX + T * NX + g);
     sm[S_VV + g] = vi;
@@ -998,9 +1032,9 @@ __global__ void __launch_bounds__(THREADS, 4) dense_backward_kernel(DenseBackwar
     // dX_{t+1}, row g (A_t row g was written by this lane)
     float dxn = 0.0f;
     if (rowx) {
-      float s = sm[S_A + g * NX] * dx[0];
+      float s = sm[S_A + g * LDM] * dx[0];
 #pragma unroll
-      for (int k = 1; k < NX; ++k) s = fmaf(sm[S_A + g * NX + k], dx[k], s);
+      for (int k = 1; k < NX; ++k) s = fmaf(sm[S_A + g * LDM + k], dx[k], s);
       float sb = sm[S_B + g * NU] * du[0];
 #pragma unroll
       for (int a = 1; a < NU; ++a) sb = fmaf(sm[S_B + g * NU + a], du[a], sb);
