@@ -36,10 +36,18 @@ def gather_rows(x_local: torch.Tensor, B: int, group=None) -> torch.Tensor:
     for d in tail:
         width *= d
     per = (B + world - 1) // world
-    buf = torch.zeros(per, width, device=x_local.device, dtype=x_local.dtype)
-    buf[: x_local.shape[0]] = x_local.reshape(x_local.shape[0], width)
+    even = B % world == 0
+    if even and x_local.is_contiguous():
+        # equal shards: the rank's rows are sent as they are and the gathered
+        # buffer is already in batch order (no padding, no reassembly copy)
+        buf = x_local.reshape(per, width)
+    else:
+        buf = torch.zeros(per, width, device=x_local.device, dtype=x_local.dtype)
+        buf[: x_local.shape[0]] = x_local.reshape(x_local.shape[0], width)
     out = torch.empty(per * world, width, device=x_local.device, dtype=x_local.dtype)
     dist.all_gather_into_tensor(out, buf, group=group)
+    if even:
+        return out.reshape((B,) + tail)
     parts = []
     for r in range(world):
         lo, hi = shard_bounds(B, r, world)
