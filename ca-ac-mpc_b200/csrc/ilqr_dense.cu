@@ -522,7 +522,7 @@ __device__ __forceinline__ float pick(const float (&v)[N], int i) {
 // that 3 (168 registers, about 90 B of spills) is, by the extra warps per SM.
 template <int MINB>
 __global__ void __launch_bounds__(THREADS, MINB) dense_solve_kernel(DenseSolveParams p) {
-  extern __shared__ float smem[];
+  extern __shared__ __align__(16) float smem[];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int e = lane >> 4;   // element slot of the warp
@@ -885,7 +885,7 @@ __global__ void __launch_bounds__(THREADS, MINB) dense_solve_kernel(DenseSolvePa
 // 4 CTAs per SM (128 registers, 16 B of spills) against 3 (161, none): 4 % faster
 // at B=16384, the same for small grids.
 __global__ void __launch_bounds__(THREADS, 4) dense_backward_kernel(DenseBackwardParams p) {
-  extern __shared__ float smem[];
+  extern __shared__ __align__(16) float smem[];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int e = lane >> 4;

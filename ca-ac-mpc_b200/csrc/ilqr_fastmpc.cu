@@ -38,6 +38,7 @@
 #include <cstdint>
 
 #include "ilqr_b200.h"
+#include "ilqr_device.cuh"
 #include "ilqr_kernels.h"
 #include "ilqr_pnqp.cuh"
 
@@ -376,40 +377,51 @@ __device__ __forceinline__ void riccati_step(const Group& G, float (&Vr)[NXf], c
   const int l = G.l;
   const bool xrow = l < NXf;
   const bool urow = l >= NXf && l < Nf;
+  // The matrix products run two columns per packed FP32 instruction (the
+  // same sums in the same order; rows of A, B, V A, V B and K start on even
+  // offsets, so a column pair is one 8-byte shared load).
   // P1: (V A)_i., (V B)_i.
   if (xrow) {
+    float2 v2[NXf];
 #pragma unroll
-    for (int j = 0; j < NXf; ++j) {
-      float s = 0.0f;
+    for (int k = 0; k < NXf; ++k) v2[k] = dup2(Vr[k]);
 #pragma unroll
-      for (int k = 0; k < NXf; ++k) s = fmaf(Vr[k], sm[S_A + k * 10 + j], s);
-      sm[S_VA + l * 10 + j] = s;
+    for (int j = 0; j < NXf; j += 2) {
+      float2 s = make_float2(0.0f, 0.0f);
+#pragma unroll
+      for (int k = 0; k < NXf; ++k) s = fma2(v2[k], ld2(sm + S_A + k * 10 + j), s);
+      *reinterpret_cast<float2*>(sm + S_VA + l * 10 + j) = s;
     }
 #pragma unroll
-    for (int j = 0; j < NUf; ++j) {
-      float s = 0.0f;
+    for (int j = 0; j < NUf; j += 2) {
+      float2 s = make_float2(0.0f, 0.0f);
 #pragma unroll
-      for (int k = 0; k < NXf; ++k) s = fmaf(Vr[k], sm[S_B + k * 4 + j], s);
-      sm[S_VB + l * 4 + j] = s;
+      for (int k = 0; k < NXf; ++k) s = fma2(v2[k], ld2(sm + S_B + k * 4 + j), s);
+      *reinterpret_cast<float2*>(sm + S_VB + l * 4 + j) = s;
     }
   }
   G.sync();
   // P2
   float Qxx[NXf] = {}, Qxu[NUf] = {}, qx = 0.0f;
   if (xrow) {
+    float2 a2[NXf];  // column l of A
 #pragma unroll
-    for (int j = 0; j < NXf; ++j) {
-      float s = cx[j];
+    for (int k = 0; k < NXf; ++k) a2[k] = dup2(sm[S_A + k * 10 + l]);
 #pragma unroll
-      for (int k = 0; k < NXf; ++k) s = fmaf(sm[S_A + k * 10 + l], sm[S_VA + k * 10 + j], s);
-      Qxx[j] = s;
+    for (int j = 0; j < NXf; j += 2) {
+      float2 s = make_float2(cx[j], cx[j + 1]);
+#pragma unroll
+      for (int k = 0; k < NXf; ++k) s = fma2(a2[k], ld2(sm + S_VA + k * 10 + j), s);
+      Qxx[j] = s.x;
+      Qxx[j + 1] = s.y;
     }
 #pragma unroll
-    for (int j = 0; j < NUf; ++j) {
-      float s = cx[NXf + j];
+    for (int j = 0; j < NUf; j += 2) {
+      float2 s = make_float2(cx[NXf + j], cx[NXf + j + 1]);
 #pragma unroll
-      for (int k = 0; k < NXf; ++k) s = fmaf(sm[S_A + k * 10 + l], sm[S_VB + k * 4 + j], s);
-      Qxu[j] = s;
+      for (int k = 0; k < NXf; ++k) s = fma2(a2[k], ld2(sm + S_VB + k * 4 + j), s);
+      Qxu[j] = s.x;
+      Qxu[j + 1] = s.y;
     }
     float s = lxi;
 #pragma unroll
@@ -493,12 +505,16 @@ __device__ __forceinline__ void riccati_step(const Group& G, float (&Vr)[NXf], c
   G.sync();
   // P4: V = Q_xx + Q_xu K, v = q_x + Q_xu k (the masked Q_xu)
   if (xrow) {
+    float2 u2[NUf];
 #pragma unroll
-    for (int j = 0; j < NXf; ++j) {
-      float s = Qxx[j];
+    for (int m = 0; m < NUf; ++m) u2[m] = dup2(Qxu[m]);
 #pragma unroll
-      for (int m = 0; m < NUf; ++m) s = fmaf(Qxu[m], sm[S_K + m * 10 + j], s);
-      Vr[j] = s;
+    for (int j = 0; j < NXf; j += 2) {
+      float2 s = make_float2(Qxx[j], Qxx[j + 1]);
+#pragma unroll
+      for (int m = 0; m < NUf; ++m) s = fma2(u2[m], ld2(sm + S_K + m * 10 + j), s);
+      Vr[j] = s.x;
+      Vr[j + 1] = s.y;
     }
     float s = qx;
 #pragma unroll
@@ -593,7 +609,7 @@ __device__ __forceinline__ void quad_split(const float* __restrict__ Cm, const f
 template <bool BOUNDED, int LPC, int MINB>
 __global__ void __launch_bounds__(THREADS, MINB) fm_solve_kernel(FmSolveParams p, int it0, int it1) {
   if (*(volatile const int32_t*)(p.flags) != 0) return;  // the batch stopped at an earlier check
-  __shared__ float smem[EPC * S_ELEM];
+  __shared__ __align__(16) float smem[EPC * S_ELEM];
   __shared__ uint32_t jtab[36];
   if (threadIdx.x < 36) jtab[threadIdx.x] = kJacTable[threadIdx.x];
   __syncthreads();
@@ -919,8 +935,8 @@ __global__ void __launch_bounds__(256) fm_finalize_kernel(FmSolveParams p) {
 // Backward: masked adjoint Riccati, tangent sweep, gradients
 // ---------------------------------------------------------------------------
 
-__global__ void __launch_bounds__(THREADS) fm_backward_kernel(FmBackwardParams p) {
-  __shared__ float smem[EPC * S_ELEM];
+__global__ void __launch_bounds__(THREADS, 4) fm_backward_kernel(FmBackwardParams p) {
+  __shared__ __align__(16) float smem[EPC * S_ELEM];
   __shared__ uint32_t jtab[36];
   if (threadIdx.x < 36) jtab[threadIdx.x] = kJacTable[threadIdx.x];
   __syncthreads();
