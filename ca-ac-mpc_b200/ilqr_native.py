@@ -128,11 +128,23 @@ def _ptr(t: Optional[torch.Tensor]):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(device: torch.device):
+    """torch's current stream on `device` as a cudaStream_t (the raw handle
+    getter when this torch has it: a per-call saving on the latency path)."""
+    if _raw_stream is not None:
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        return ctypes.c_void_p(_raw_stream(idx))
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
 
 def _req(t: torch.Tensor, name: str, shape, device, dtype=torch.float32):
+    # the common case in one test; the checks below name what is wrong
+    if (isinstance(t, torch.Tensor) and t.dtype is dtype and t.shape == tuple(shape) and t.device == device
+            and t.is_contiguous()):
+        return t
     if not isinstance(t, torch.Tensor):
         raise TypeError(f"{name} must be a tensor")
     if not t.is_cuda:
@@ -168,11 +180,19 @@ def _device_ok(device: torch.device):
         _checked_devices.add(idx)
 
 
+_ws_sizes = {}
+
+
 def workspace_bytes(kind: str, B: int, T: int) -> int:
+    key = (kind, B, T)
+    n_cached = _ws_sizes.get(key)
+    if n_cached is not None:
+        return n_cached
     n = ctypes.c_size_t(0)
     fn = lib().ilqr_b200_solve_workspace_size if kind == "solve" else lib().ilqr_b200_backward_workspace_size
     _check(fn(B, T, ctypes.byref(n)), "workspace query")
-    return int(n.value)
+    _ws_sizes[key] = int(n.value)
+    return _ws_sizes[key]
 
 
 def solve(x0, U_init, C, c, C_final=None, c_final=None, x_ref=None, u_ref=None,
