@@ -125,7 +125,9 @@ def _check(status: int, what: str):
 
 
 def _ptr(t: Optional[torch.Tensor]):
-    return None if t is None else ctypes.c_void_p(t.data_ptr())
+    # a plain int: the declared c_void_p argtypes convert it (cheaper than a
+    # c_void_p object per argument on the latency path)
+    return None if t is None else t.data_ptr()
 
 
 _raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
@@ -136,8 +138,8 @@ def _stream(device: torch.device):
     getter when this torch has it: a per-call saving on the latency path)."""
     if _raw_stream is not None:
         idx = device.index if device.index is not None else torch.cuda.current_device()
-        return ctypes.c_void_p(_raw_stream(idx))
-    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+        return _raw_stream(idx)
+    return torch.cuda.current_stream(device).cuda_stream
 
 
 def _req(t: torch.Tensor, name: str, shape, device, dtype=torch.float32):
@@ -181,6 +183,17 @@ def _device_ok(device: torch.device):
 
 
 _ws_sizes = {}
+_alpha_arrays = {}
+
+
+def _alpha_array(al):
+    """The step sizes as a C float array, one per distinct tuple (kept alive
+    here, so the pointer passed to the library stays valid)."""
+    key = tuple(al)
+    arr = _alpha_arrays.get(key)
+    if arr is None:
+        arr = _alpha_arrays[key] = (ctypes.c_float * len(key))(*key)
+    return arr
 
 
 def workspace_bytes(kind: str, B: int, T: int) -> int:
@@ -245,7 +258,7 @@ def solve(x0, U_init, C, c, C_final=None, c_final=None, x_ref=None, u_ref=None,
         s_gap = out["stall_gap"] = torch.empty(B, device=dev)
     nbytes = workspace_bytes("solve", B, T)
     ws = torch.empty(max(nbytes, 1), device=dev, dtype=torch.uint8)
-    a_arr = (ctypes.c_float * len(al))(*al)
+    a_arr = _alpha_array(al)
     fn = L.ilqr_b200_solve_tm_f32 if time_major else L.ilqr_b200_solve_f32
     st = fn(
         _ptr(x0), _ptr(U_init), _ptr(C), _ptr(c), _ptr(C_final), _ptr(c_final), _ptr(x_ref),
@@ -348,7 +361,7 @@ def solve_sigmoid(x0, U_init, sigmoid_cost, spec: Optional[SigmoidCostSpec] = No
         s_gap = out["stall_gap"] = torch.empty(B, device=dev)
     nbytes = workspace_bytes("solve", B, T)
     ws = torch.empty(max(nbytes, 1), device=dev, dtype=torch.uint8)
-    a_arr = (ctypes.c_float * len(al))(*al)
+    a_arr = _alpha_array(al)
     st = L.ilqr_b200_solve_sigmoid_f32(
         _ptr(x0), _ptr(U_init), _ptr(sigmoid_cost), *spec.args(), _ptr(u_min), _ptr(u_max),
         B, T, float(dt), int(max_iter), float(reg_eps), float(converge_tol),
@@ -512,7 +525,7 @@ class BoundSolve:
     def _check(self, t, name, shape):
         if t.device != self.dev or t.dtype != torch.float32 or tuple(t.shape) != shape or not t.is_contiguous():
             raise RuntimeError(f"{name} must be a contiguous float32 {shape} tensor on {self.dev}")
-        return ctypes.c_void_p(t.data_ptr())
+        return t.data_ptr()
 
     def __call__(self, x0, U_init, C, c, grad_X=None, grad_U=None):
         B, T = self.B, self.T
@@ -521,7 +534,7 @@ class BoundSolve:
         a[1] = self._check(U_init, "U_init", (B, T, NU))
         a[2] = cp = self._check(C, "C", (B, T, N, N))
         a[3] = self._check(c, "c", (B, T, N))
-        stream = ctypes.c_void_p(torch.cuda.current_stream(self.dev).cuda_stream)
+        stream = _stream(self.dev)
         a[-1] = stream
         _check(self._solve(*a), "ilqr_b200_solve_f32")
         if self._bargs is not None and grad_X is not None:
@@ -699,7 +712,7 @@ def rotor13_solve(x0, U_init, C, c, C_final=None, c_final=None, x_ref=None, u_re
     _check(L.ilqr_b200_rotor13_solve_workspace_size(B, T, len(al), ctypes.byref(n)), "workspace query")
     nbytes = int(n.value)
     ws = torch.empty(max(nbytes, 16), device=dev, dtype=torch.uint8)
-    a_arr = (ctypes.c_float * len(al))(*al)
+    a_arr = _alpha_array(al)
     fn = L.ilqr_b200_rotor13_solve_tm_f32 if time_major else L.ilqr_b200_rotor13_solve_f32
     st = fn(
         _ptr(x0), _ptr(U_init), _ptr(C), _ptr(c), _ptr(C_final), _ptr(c_final), _ptr(x_ref),
@@ -825,7 +838,7 @@ def fastmpc_solve(x0, U_init, C, c, C_final=None, c_final=None, x_ref=None, u_re
     _check(L.ilqr_b200_fastmpc_solve_workspace_size(B, T, len(al), ctypes.byref(n)), "workspace query")
     nbytes = int(n.value)
     ws = torch.empty(max(nbytes, 16), device=dev, dtype=torch.uint8)
-    a_arr = (ctypes.c_float * len(al))(*al)
+    a_arr = _alpha_array(al)
     st = L.ilqr_b200_fastmpc_solve_f32(
         _ptr(x0), _ptr(U_init), _ptr(C), _ptr(c), _ptr(C_final), _ptr(c_final), _ptr(x_ref), _ptr(u_ref),
         _ptr(u_min), _ptr(u_max), B, T, float(dt), int(max_iter), float(reg_eps), float(converge_tol),
