@@ -187,6 +187,36 @@ __device__ __forceinline__ float inv_sqrt(float d) {
   return fmaf(-h, y * y, 1.5f * y);
 }
 
+// chol4's factorisation with the in-range reciprocal square root on every
+// pivot and no branch: returns whether every pivot is a positive normal
+// number, in which case L holds chol4's bits (and chol4 would return true).
+// Otherwise L is meaningless and the caller repeats the factorisation with
+// chol4. The straight-line chain lets the scheduler interleave independent
+// work with it.
+__device__ __forceinline__ bool chol4_fast(const float (&M)[NU][NU], Chol4& L) {
+  auto nr = [](float d) {
+    const float y = rsqrtf(d);
+    const float h = 0.5f * d * y;
+    return fmaf(-h, y * y, 1.5f * y);
+  };
+  auto in_range = [](float d) { return d >= 1.17549435e-38f && d <= 3.4e38f; };
+  const float d0 = M[0][0];
+  L.r0 = nr(d0);
+  L.l10 = M[1][0] * L.r0;
+  L.l20 = M[2][0] * L.r0;
+  L.l30 = M[3][0] * L.r0;
+  const float d1 = M[1][1] - L.l10 * L.l10;
+  L.r1 = nr(d1);
+  L.l21 = (M[2][1] - L.l20 * L.l10) * L.r1;
+  L.l31 = (M[3][1] - L.l30 * L.l10) * L.r1;
+  const float d2 = (M[2][2] - L.l20 * L.l20) - L.l21 * L.l21;
+  L.r2 = nr(d2);
+  L.l32 = ((M[3][2] - L.l30 * L.l20) - L.l31 * L.l21) * L.r2;
+  const float d3 = ((M[3][3] - L.l30 * L.l30) - L.l31 * L.l31) - L.l32 * L.l32;
+  L.r3 = nr(d3);
+  return in_range(d0) & in_range(d1) & in_range(d2) & in_range(d3);
+}
+
 __device__ __forceinline__ bool chol4(const float (&M)[NU][NU], Chol4& L) {
   const float d0 = M[0][0];
   L.r0 = inv_sqrt(d0);

@@ -240,56 +240,84 @@ __device__ __forceinline__ bool pair_riccati(float (&Vr)[NX], float& vr, const J
     const float4 q4 = *reinterpret_cast<const float4*>(sh + PQU);
     qu[0] = q4.x; qu[1] = q4.y; qu[2] = q4.z; qu[3] = q4.w;
   }
-  bool ok;
-  Chol4 L;
-  float* sv = sh + PSV;
+  // Q_xx[i][cc] = C_t[i][cc] + (A^T (V A))[i][cc] for the value update, as
+  // packed pairs of columns: independent of the gains, so formed here, where
+  // its products fill the latency of the factorisation's serial chain.
+  const float* Crow = Ce + (i < NX ? i : NX - 1) * NT;
+  float2 qxx[NX / 2];
   {
-    float Qs[NU][NU];
 #pragma unroll
-    for (int a = 0; a < NU; ++a)
+    for (int hh = 0; hh < NX / 2; ++hh) qxx[hh] = make_float2(0.0f, 0.0f);
 #pragma unroll
-      for (int b = 0; b < NU; ++b) {
-        if (MASKED) {
-          const bool ta = (tight >> a) & 1u, tb = (tight >> b) & 1u;
-          float val = (ta || tb) ? 0.0f : Quu[a][b];
-          if (a == b && ta) val = val + 1.0f;
-          Qs[a][b] = val + (a == b ? 1e-8f * reg : 0.0f);
-        } else {
-          Qs[a][b] = Quu[a][b] + (a == b ? reg : 0.0f);
+    for (int s = 0; s < 7; ++s) {
+      const float* y = sh + PVA + 12 * (3 + s);
+#pragma unroll
+      for (int hh = 0; hh < NX / 2; ++hh) qxx[hh] = fma2(c2[s], ld2(y + 2 * hh), qxx[hh]);
+    }
+#pragma unroll
+    for (int hh = 0; hh < NX / 2; ++hh) {
+      const int cc = 2 * hh;
+      qxx[hh] = add2(ld2(Crow + cc), fma2(c72, ld2(sh + PVA + 12 * own + cc), qxx[hh]));
+    }
+  }
+  // The common case runs straight through: the factorisation with in-range
+  // pivots and the triangular solves. A warp with a pivot outside the normal
+  // range (Q_uu not positive definite, or degenerate) repeats them for those
+  // lanes through chol4 and, where that fails, the SVD inverse.
+  Chol4 L;
+  float Qs[NU][NU];
+#pragma unroll
+  for (int a = 0; a < NU; ++a)
+#pragma unroll
+    for (int b = 0; b < NU; ++b) {
+      if (MASKED) {
+        const bool ta = (tight >> a) & 1u, tb = (tight >> b) & 1u;
+        float val = (ta || tb) ? 0.0f : Quu[a][b];
+        if (a == b && ta) val = val + 1.0f;
+        Qs[a][b] = val + (a == b ? 1e-8f * reg : 0.0f);
+      } else {
+        Qs[a][b] = Quu[a][b] + (a == b ? reg : 0.0f);
+      }
+    }
+  const bool inr = chol4_fast(Qs, L);
+  auto msk = [&](int a, float v) { return (MASKED && ((tight >> a) & 1u)) ? 0.0f : v; };
+  float rhs[NU], sol[NU];
+#pragma unroll
+  for (int a = 0; a < NU; ++a) rhs[a] = msk(a, i < NX ? Qr[a] : qu[a]);
+  chol4_solve(L, rhs, sol);
+  bool ok = true;
+  if (__any_sync(FULL, !inr)) {
+    float* sv = sh + PSV;
+    if (!inr) {
+      // A half without an element never takes the SVD path.
+      ok = chol4(Qs, L) || !live;
+      if (!ok) {
+        // every lane of the half forms the same inverse; identical writes
+#pragma unroll
+        for (int a = 0; a < NU; ++a)
+#pragma unroll
+          for (int b = 0; b < NU; ++b) sv[a * NU + b] = Qs[a][b];
+        svd_inverse4(sv, sv + NU * NU);
+      }
+    }
+    if (__any_sync(FULL, !ok)) __syncwarp();  // every fallback inverse of the warp is written
+    if (!inr) {
+      if (ok) {
+        chol4_solve(L, rhs, sol);
+      } else {
+        const float* Mi = sv + NU * NU;
+#pragma unroll
+        for (int a = 0; a < NU; ++a) {
+          float acc = Mi[a * NU] * rhs[0];
+#pragma unroll
+          for (int b = 1; b < NU; ++b) acc = fmaf(Mi[a * NU + b], rhs[b], acc);
+          sol[a] = acc;
         }
       }
-    // A half without an element never takes the SVD path.
-    ok = chol4(Qs, L) || !live;
-    if (!ok) {
-      // every lane of the half forms the same inverse; identical writes
-#pragma unroll
-      for (int a = 0; a < NU; ++a)
-#pragma unroll
-        for (int b = 0; b < NU; ++b) sv[a * NU + b] = Qs[a][b];
-      svd_inverse4(sv, sv + NU * NU);
     }
   }
-  if (__any_sync(FULL, !ok)) __syncwarp();  // every fallback inverse of the warp is written
-  auto msk = [&](int a, float v) { return (MASKED && ((tight >> a) & 1u)) ? 0.0f : v; };
-  {
-    float rhs[NU], sol[NU];
 #pragma unroll
-    for (int a = 0; a < NU; ++a) rhs[a] = msk(a, i < NX ? Qr[a] : qu[a]);
-    if (ok) {
-      chol4_solve(L, rhs, sol);
-    } else {
-      const float* Mi = sv + NU * NU;
-#pragma unroll
-      for (int a = 0; a < NU; ++a) {
-        float acc = Mi[a * NU] * rhs[0];
-#pragma unroll
-        for (int b = 1; b < NU; ++b) acc = fmaf(Mi[a * NU + b], rhs[b], acc);
-        sol[a] = acc;
-      }
-    }
-#pragma unroll
-    for (int a = 0; a < NU; ++a) Kr[a] = -sol[a];
-  }
+  for (int a = 0; a < NU; ++a) Kr[a] = -sol[a];
   if (i < NX) {
 #pragma unroll
     for (int a = 0; a < NU; ++a) sh[PKR + 12 * a + i] = Kr[a];
@@ -338,46 +366,28 @@ __device__ __forceinline__ bool pair_riccati(float (&Vr)[NX], float& vr, const J
       for (int a = 1; a < NU; ++a) t2 = fmaf(Kr[a], qu[a], t2);
       vr = (qr + t1) + t2;
     }
-    // V[i][cc] = (Q_xx[i][cc] + W_i K_cc) + K_i Q_xu[cc], Q_xx[i][cc] from the
-    // rows of V A in the form of the header comment; packed pairs of columns
-    // (cc, cc + 1), every sum in the order of the scalar formula.
-    const float* Crow = Ce + (i < NX ? i : NX - 1) * NT;
+    // V[i][cc] = (Q_xx[i][cc] + W_i K_cc) + K_i Q_xu[cc] (Q_xx formed before
+    // the factorisation); packed pairs of columns (cc, cc + 1), every sum in
+    // the order of the scalar formula.
     float2 w2[NU], kr2[NU];
 #pragma unroll
     for (int a = 0; a < NU; ++a) {
       w2[a] = dup2(Wr[a]);
       kr2[a] = dup2(Kr[a]);
     }
-    // columns c0 .. c0 + 2 NP - 1 (NP packed pairs)
-    auto cols = [&](auto np_tag, int c0) {
-      constexpr int NP = decltype(np_tag)::value;
-      float2 acc[NP];
 #pragma unroll
-      for (int h = 0; h < NP; ++h) acc[h] = make_float2(0.0f, 0.0f);
+    for (int hh = 0; hh < NX / 2; ++hh) {
+      const int cc = 2 * hh;
+      float2 t1 = mul2(w2[0], ld2(sh + PKR + cc));
 #pragma unroll
-      for (int s = 0; s < 7; ++s) {
-        const float* y = sh + PVA + 12 * (3 + s) + c0;
+      for (int a = 1; a < NU; ++a) t1 = fma2(w2[a], ld2(sh + PKR + 12 * a + cc), t1);
+      float2 t2 = mul2(kr2[0], ld2(sh + PQUX + cc));
 #pragma unroll
-        for (int h = 0; h < NP; ++h) acc[h] = fma2(c2[s], ld2(y + 2 * h), acc[h]);
-      }
-#pragma unroll
-      for (int h = 0; h < NP; ++h) {
-        const int cc = c0 + 2 * h;
-        const float2 q = add2(ld2(Crow + cc), fma2(c72, ld2(sh + PVA + 12 * own + cc), acc[h]));
-        float2 t1 = mul2(w2[0], ld2(sh + PKR + cc));
-#pragma unroll
-        for (int a = 1; a < NU; ++a) t1 = fma2(w2[a], ld2(sh + PKR + 12 * a + cc), t1);
-        float2 t2 = mul2(kr2[0], ld2(sh + PQUX + cc));
-#pragma unroll
-        for (int a = 1; a < NU; ++a) t2 = fma2(kr2[a], ld2(sh + PQUX + 12 * a + cc), t2);
-        const float2 v = add2(add2(q, t1), t2);
-        Vr[cc] = v.x;
-        Vr[cc + 1] = v.y;
-      }
-    };
-    cols(std::integral_constant<int, 2>{}, 0);
-    cols(std::integral_constant<int, 2>{}, 4);
-    cols(std::integral_constant<int, 1>{}, 8);
+      for (int a = 1; a < NU; ++a) t2 = fma2(kr2[a], ld2(sh + PQUX + 12 * a + cc), t2);
+      const float2 v = add2(add2(qxx[hh], t1), t2);
+      Vr[cc] = v.x;
+      Vr[cc + 1] = v.y;
+    }
   }
   __syncwarp();  // C_t and the area are no longer read
   return ok;
