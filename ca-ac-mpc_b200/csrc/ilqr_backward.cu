@@ -363,7 +363,8 @@ __global__ void __launch_bounds__(32, MINB) backward_pair_kernel(const BackwardP
     pair_coef_load(jt, coffs, cf_, c7);
     __syncwarp();
     float Kr[NU];
-    pair_riccati<true>(Vr, vr, J, cf_, c7, own, sigm ? sh + PC0 : cpipe.block(t), lx, p.reg, tight, i, valid, sh,
+    pair_riccati<true>(Vr, vr, J, cf_, c7, own, sigm ? sh + PC0 : cpipe.block(t), [&] { return lx; }, p.reg, tight,
+                       i, valid, sh,
                        Kr);
     if (i <= NX) *reinterpret_cast<float4*>(KS + PKS_F * t + 4 * i) = f4(Kr);
   }

@@ -158,17 +158,19 @@ __device__ __forceinline__ void pair_coef_load(const float* jt, uint64_t offs, f
 // operation order as team_riccati (ilqr_team.cuh), forward or masked.
 // c, c7, own: the coefficients of this lane's row (pair_coef, through the
 // step's Jacobian table; lanes 14, 15 carry row 13's).
-// Lane i < 10: Vr, vr = row i of V and v_i (in V_{t+1}, out V_t). lx: lane
-// i < 10 the gradient term of row i, lane 10 + a that of control a. Ce: the
+// Lane i < 10: Vr, vr = row i of V and v_i (in V_{t+1}, out V_t). lx_fn():
+// lane i < 10 the gradient term of row i, lane 10 + a that of control a;
+// called first, so that its arithmetic overlaps the rows of V A. Ce: the
 // element's C_t block in shared memory. sh: the element's area. On return
 // lane i < 10 holds column i of K in Kr (the four gains of state i), lane 10
 // holds k. Every lane returns whether the Cholesky succeeded (the same in all
 // lanes of the half). Ends with a warp sync: C_t and the area are free.
-template <bool MASKED>
+template <bool MASKED, class LxFn>
 __device__ __forceinline__ bool pair_riccati(float (&Vr)[NX], float& vr, const Jac& J, const float (&c)[7], float c7,
-                                             int own, const float* __restrict__ Ce, float lx, float reg,
+                                             int own, const float* __restrict__ Ce, LxFn&& lx_fn, float reg,
                                              uint32_t tight, int i, bool live, float* __restrict__ sh,
                                              float (&Kr)[NU]) {
+  const float lx = lx_fn();
   // ---- rows of V A (as columns of VAT), V B and v ----------------------------
   // (Lanes 10..15 run every phase on a stand-in row, which keeps the warp in
   // one instruction stream; only the lanes of real rows store.)

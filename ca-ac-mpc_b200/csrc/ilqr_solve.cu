@@ -868,6 +868,12 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
     }
     __syncwarp();
     for (int t = T - 1; t >= 0; --t) {
+      // the step's Jacobian, row coefficients and record (tables written by
+      // the prologue, read-only during the pass)
+      const float* jt = JT + PJT_F * t;
+      const Jac J = jtab_read(jt);
+      float cf_[7], c7;
+      pair_coef_load(jt, coffs, cf_, c7);
       float xb[NX], ub[NU], tau[NT];
       load_rec(reinterpret_cast<const float4*>(REC + PREC_F * t), xb, ub);
       float* cr = CR + PCR_F * t;
@@ -888,22 +894,28 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
       for (int k = 0; k < NX; ++k) tau[k] = xb[k] - xref(t, k);
 #pragma unroll
       for (int a = 0; a < NU; ++a) tau[NX + a] = ub[a] - uref(t, a);
-      // quadraticize: l_tau = C tau + c, row ti
+      // quadraticize: l_tau = C tau + c, row ti (inside the Riccati step,
+      // where its chain overlaps the rows of V A)
       float sdot;
-      {
+      auto lx_fn = [&]() {
         const float2* Cr = reinterpret_cast<const float2*>(Ce + ti * NT);
         float2 c2 = Cr[0];
-        sdot = c2.x * tau[0];
-        sdot = fmaf(c2.y, tau[1], sdot);
+        float s_ = c2.x * tau[0];
+        s_ = fmaf(c2.y, tau[1], s_);
 #pragma unroll
         for (int j = 1; j < NT / 2; ++j) {
           c2 = Cr[j];
-          sdot = fmaf(c2.x, tau[2 * j], sdot);
-          sdot = fmaf(c2.y, tau[2 * j + 1], sdot);
+          s_ = fmaf(c2.x, tau[2 * j], s_);
+          s_ = fmaf(c2.y, tau[2 * j + 1], s_);
         }
-      }
-      const float lx = sdot + cv;
+        sdot = s_;
+        return s_ + cv;
+      };
+      float Kr[NU];
+      if (!pair_riccati<false>(Vr, vr, J, cf_, c7, own, Ce, lx_fn, p.reg, 0u, i, valid, sh, Kr)) fallback = true;
+      if (i <= NX) *reinterpret_cast<float4*>(KS + PKS_F * t + 4 * i) = f4(Kr);
       if (first) {
+        // C_t's buffer is intact until the next step issues its copy
         if (i < NT) {
           sh[PS + i] = sdot;
           sh[PCV + i] = cv;
@@ -914,24 +926,20 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
             offd |= scan_offdiag<HALF>(Ce, i);
           }
         }
+        __syncwarp();
+        if (i < TEAM) {
+          // the initial objective, accumulated as the team kernel's lane m = i does
+          const int ra = row_a(i), rb = row_b(i), ru = NX + (i < NU ? i : 0);
+          float xr[NX], ur[NU];
+          load_rec(reinterpret_cast<const float4*>(REC + PREC_F * t), xr, ur);
+          const float ta = xr[ra] - xref(t, ra), tb = xr[rb] - xref(t, rb), tu = ur[ru - NX] - uref(t, ru - NX);
+          const float sa = sh[PS + ra], sb = sh[PS + rb], su = sh[PS + ru];
+          const float ca_ = sh[PCV + ra], cb_ = sh[PCV + rb], cu = sh[PCV + ru];
+          cost_q += fmaf(ta, sa, tb * sb) + (i < NU ? tu * su : 0.0f);
+          cost_l += fmaf(ca_, ta, cb_ * tb) + (i < NU ? cu * tu : 0.0f);
+        }
+        __syncwarp();
       }
-      const float* jt = JT + PJT_F * t;
-      const Jac J = jtab_read(jt);
-      float cf_[7], c7;
-      pair_coef_load(jt, coffs, cf_, c7);
-      __syncwarp();
-      if (first && i < TEAM) {
-        // the initial objective, accumulated as the team kernel's lane m = i does
-        const int ra = row_a(i), rb = row_b(i), ru = NX + (i < NU ? i : 0);
-        const float sa = sh[PS + ra], sb = sh[PS + rb], su = sh[PS + ru];
-        const float ca_ = sh[PCV + ra], cb_ = sh[PCV + rb], cu = sh[PCV + ru];
-        const float ta = tau[ra], tb = tau[rb], tu = tau[ru];
-        cost_q += fmaf(ta, sa, tb * sb) + (i < NU ? tu * su : 0.0f);
-        cost_l += fmaf(ca_, ta, cb_ * tb) + (i < NU ? cu * tu : 0.0f);
-      }
-      float Kr[NU];
-      if (!pair_riccati<false>(Vr, vr, J, cf_, c7, own, Ce, lx, p.reg, 0u, i, valid, sh, Kr)) fallback = true;
-      if (i <= NX) *reinterpret_cast<float4*>(KS + PKS_F * t + 4 * i) = f4(Kr);
     }
     if (first && p.diag_cache && !sigm) {
       diag = !__any_sync(FULL, offd);
