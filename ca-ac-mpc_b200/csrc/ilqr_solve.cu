@@ -971,9 +971,80 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
       const int cs = j < nom ? j : j + 1;
       float x[NX], sq = 0.0f, sl = 0.0f;
       load_x0(x);
-      if (!diag) cpipe.issue(0);
-      for (int t = 0; t < T; ++t) {
-        if (!diag) {
+      // Step cost l = c_t . tau and q = sum_k tau_k (diag(C_t)_k tau_k) of
+      // one step from its cost record (diagonal costs); a non-finite q with a
+      // non-finite tau becomes NaN (the dense form's 0 * inf), as in the
+      // dense-cost loop below.
+      auto diag_cost = [&](const float (&tau)[NT], int t, float& l, float& q) {
+        const float* cost_t = CR + PCR_F * t;
+        const float4* c4 = reinterpret_cast<const float4*>(cost_t + 16);
+        const float4 h0 = c4[0], h1 = c4[1], h2 = c4[2], h3 = c4[3];
+        const float cvv[NT] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z,
+                               h1.w, h2.x, h2.y, h2.z, h2.w, h3.x, h3.y};
+        l = cvv[0] * tau[0];
+#pragma unroll
+        for (int jj = 1; jj < NT; ++jj) l = fmaf(cvv[jj], tau[jj], l);
+        const float4* d4 = reinterpret_cast<const float4*>(cost_t);
+        const float4 g0 = d4[0], g1 = d4[1], g2 = d4[2], g3 = d4[3];
+        const float dgv[NT] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z,
+                               g1.w, g2.x, g2.y, g2.z, g2.w, g3.x, g3.y};
+        q = 0.0f;
+#pragma unroll
+        for (int k = 0; k < NT; ++k) q = fmaf(tau[k], dgv[k] * tau[k], q);
+      };
+      auto nan_fix = [](const float (&tau)[NT], float& q) {
+        if (!isfinite(q)) {
+          bool nonfinite = false;
+#pragma unroll
+          for (int k = 0; k < NT; ++k) nonfinite |= !isfinite(tau[k]);
+          if (nonfinite) q = __int_as_float(0x7fffffff);
+        }
+      };
+      if (diag) {
+        // Software-pipelined: the cost of step t - 1 is formed beside step
+        // t's candidate control (one straight block, so the two chains
+        // overlap); its rare non-finite fix-up and the sums follow the
+        // dynamics step. The sums take the same terms in the same order.
+        float pt[NT];  // tau of step t - 1 (zero before the first step; its cost is not added)
+#pragma unroll
+        for (int k = 0; k < NT; ++k) pt[k] = 0.0f;
+        for (int t = 0; t < T; ++t) {
+          float lp, qp;
+          diag_cost(pt, t > 0 ? t - 1 : 0, lp, qp);
+          float xb[NX], ub[NU], kt[NU], u[NU];
+          load_rec(reinterpret_cast<const float4*>(REC + PREC_F * t), xb, ub);
+          const float4* ks = reinterpret_cast<const float4*>(KS + PKS_F * t);
+          {
+            const float4 k4 = ks[NX];
+            kt[0] = k4.x; kt[1] = k4.y; kt[2] = k4.z; kt[3] = k4.w;
+          }
+          candidate_u_reg(x, xb, ub, [&](int jj) { return ks[jj]; }, kt, al, bounds, blo, bhi, u);
+          if (keep) store_rec(W.rec(cs, t), x, u);
+          float tau[NT];
+#pragma unroll
+          for (int k = 0; k < NX; ++k) tau[k] = x[k] - xref(t, k);
+#pragma unroll
+          for (int a = 0; a < NU; ++a) tau[NX + a] = u[a] - uref(t, a);
+          float xn[NX];
+          drone_step(x, u, dt, xn);
+#pragma unroll
+          for (int k = 0; k < NX; ++k) x[k] = xn[k];
+          if (t > 0) {
+            nan_fix(pt, qp);
+            sq += qp;
+            sl += lp;
+          }
+#pragma unroll
+          for (int k = 0; k < NT; ++k) pt[k] = tau[k];
+        }
+        float lp, qp;
+        diag_cost(pt, T - 1, lp, qp);
+        nan_fix(pt, qp);
+        sq += qp;
+        sl += lp;
+      } else {
+        cpipe.issue(0);
+        for (int t = 0; t < T; ++t) {
           if (t + 1 < T) {
             cpipe.issue(t + 1);
             cp_async_wait<1>();
@@ -981,68 +1052,54 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
             cp_async_wait<0>();
           }
           __syncwarp();
-        }
-        float xb[NX], ub[NU], kt[NU], u[NU];
-        load_rec(reinterpret_cast<const float4*>(REC + PREC_F * t), xb, ub);
-        const float4* ks = reinterpret_cast<const float4*>(KS + PKS_F * t);
-        {
-          const float4 k4 = ks[NX];
-          kt[0] = k4.x; kt[1] = k4.y; kt[2] = k4.z; kt[3] = k4.w;
-        }
-        candidate_u_reg(x, xb, ub, [&](int jj) { return ks[jj]; }, kt, al, bounds, blo, bhi, u);
-        if (keep) store_rec(W.rec(cs, t), x, u);
-        float tau[NT];
-#pragma unroll
-        for (int k = 0; k < NX; ++k) tau[k] = x[k] - xref(t, k);
-#pragma unroll
-        for (int a = 0; a < NU; ++a) tau[NX + a] = u[a] - uref(t, a);
-        const float* cost_t = CR + PCR_F * t;
-        float l;
-        {
-          const float4* c4 = reinterpret_cast<const float4*>(cost_t + 16);
-          const float4 h0 = c4[0], h1 = c4[1], h2 = c4[2], h3 = c4[3];
-          const float cvv[NT] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z,
-                                 h1.w, h2.x, h2.y, h2.z, h2.w, h3.x, h3.y};
-          l = cvv[0] * tau[0];
-#pragma unroll
-          for (int jj = 1; jj < NT; ++jj) l = fmaf(cvv[jj], tau[jj], l);
-        }
-        float q = 0.0f;
-        if (diag) {
-          const float4* d4 = reinterpret_cast<const float4*>(cost_t);
-          const float4 g0 = d4[0], g1 = d4[1], g2 = d4[2], g3 = d4[3];
-          const float dgv[NT] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z,
-                                 g1.w, g2.x, g2.y, g2.z, g2.w, g3.x, g3.y};
-#pragma unroll
-          for (int k = 0; k < NT; ++k) q = fmaf(tau[k], dgv[k] * tau[k], q);
-          if (!isfinite(q)) {
-            bool nonfinite = false;
-#pragma unroll
-            for (int k = 0; k < NT; ++k) nonfinite |= !isfinite(tau[k]);
-            if (nonfinite) q = __int_as_float(0x7fffffff);
+          float xb[NX], ub[NU], kt[NU], u[NU];
+          load_rec(reinterpret_cast<const float4*>(REC + PREC_F * t), xb, ub);
+          const float4* ks = reinterpret_cast<const float4*>(KS + PKS_F * t);
+          {
+            const float4 k4 = ks[NX];
+            kt[0] = k4.x; kt[1] = k4.y; kt[2] = k4.z; kt[3] = k4.w;
           }
-        } else {
-          const float* Ce = cpipe.block(t);
+          candidate_u_reg(x, xb, ub, [&](int jj) { return ks[jj]; }, kt, al, bounds, blo, bhi, u);
+          if (keep) store_rec(W.rec(cs, t), x, u);
+          float tau[NT];
 #pragma unroll
-          for (int k = 0; k < NT; ++k) {
-            const float2* r2 = reinterpret_cast<const float2*>(Ce + k * NT);
-            float r = 0.0f;
+          for (int k = 0; k < NX; ++k) tau[k] = x[k] - xref(t, k);
 #pragma unroll
-            for (int jj = 0; jj < NT / 2; ++jj) {
-              const float2 c2 = r2[jj];
-              r = (jj == 0) ? c2.x * tau[0] : fmaf(c2.x, tau[2 * jj], r);
-              r = fmaf(c2.y, tau[2 * jj + 1], r);
+          for (int a = 0; a < NU; ++a) tau[NX + a] = u[a] - uref(t, a);
+          float l;
+          {
+            const float4* c4 = reinterpret_cast<const float4*>(CR + PCR_F * t + 16);
+            const float4 h0 = c4[0], h1 = c4[1], h2 = c4[2], h3 = c4[3];
+            const float cvv[NT] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z,
+                                   h1.w, h2.x, h2.y, h2.z, h2.w, h3.x, h3.y};
+            l = cvv[0] * tau[0];
+#pragma unroll
+            for (int jj = 1; jj < NT; ++jj) l = fmaf(cvv[jj], tau[jj], l);
+          }
+          float q = 0.0f;
+          {
+            const float* Ce = cpipe.block(t);
+#pragma unroll
+            for (int k = 0; k < NT; ++k) {
+              const float2* r2 = reinterpret_cast<const float2*>(Ce + k * NT);
+              float r = 0.0f;
+#pragma unroll
+              for (int jj = 0; jj < NT / 2; ++jj) {
+                const float2 c2 = r2[jj];
+                r = (jj == 0) ? c2.x * tau[0] : fmaf(c2.x, tau[2 * jj], r);
+                r = fmaf(c2.y, tau[2 * jj + 1], r);
+              }
+              q = fmaf(tau[k], r, q);
             }
-            q = fmaf(tau[k], r, q);
+            __syncwarp();  // block t is read; the next issue may overwrite it
           }
-          __syncwarp();  // block t is read; the next issue may overwrite it
-        }
-        sq += q;
-        sl += l;
-        float xn[NX];
-        drone_step(x, u, dt, xn);
+          sq += q;
+          sl += l;
+          float xn[NX];
+          drone_step(x, u, dt, xn);
 #pragma unroll
-        for (int k = 0; k < NX; ++k) x[k] = xn[k];
+          for (int k = 0; k < NX; ++k) x[k] = xn[k];
+        }
       }
       if (keep) store_rec_x(W.rec(cs, T), x);
       float tn[NX];
