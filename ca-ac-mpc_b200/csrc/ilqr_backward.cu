@@ -113,7 +113,8 @@ __global__ void __launch_bounds__(32, MINB) backward_kernel(const __grid_constan
     __syncwarp();
     const Jac J = drone_jac(xb, ub, dt);
     float Ka[NU], Kb[NU], k[NU];
-    team_riccati<true>(Va, Vb, va_, vb_, J, DenseC{Ce}, lxa, lxb, p.reg, tight, m, valid, xc, next, Ka, Kb, k);
+    team_riccati<true, (MINB < TIER_LO)>(Va, Vb, va_, vb_, J, DenseC{Ce}, lxa, lxb, p.reg, tight, m, valid, xc, next,
+                                         Ka, Kb, k);
     if (own) {
       *kcol(t, ra) = f4(Ka);
       *kcol(t, rb) = f4(Kb);

@@ -460,8 +460,8 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
       __syncwarp();
       const Jac J = drone_jac(xb, ub, dt);
       float Ka[NU], Kb[NU], k[NU];
-      if (!team_riccati<false>(Va, Vb, va_, vb_, J, DenseC{Ce}, lxa, lxb, p.reg, 0u, m, valid, xc, next, Ka, Kb,
-                               k))
+      if (!team_riccati<false, (MINB < TIER_LO)>(Va, Vb, va_, vb_, J, DenseC{Ce}, lxa, lxb, p.reg, 0u, m, valid, xc,
+                                                 next, Ka, Kb, k))
         fallback = true;
       if (own) {
         *W.kcol(t, ra) = f4(Ka);

@@ -148,7 +148,7 @@ __device__ __forceinline__ void row_VA_VB(const Jac& J, const float (&Vr)[NX], f
 // (DenseC). after_c() is called at the end, once every lane is done reading
 // Ct and the exchange area (it may reuse the slab); it must sync the warp. Outputs: Ka, Kb = K[:, RA],
 // K[:, RB]; k. Returns false if the Cholesky failed (SVD inverse used).
-template <bool MASKED, class CAcc, class AfterC>
+template <bool MASKED, bool STRAIGHT, class CAcc, class AfterC>
 __device__ __forceinline__ bool team_riccati(float (&Va)[NX], float (&Vb)[NX], float& va_, float& vb_,
                                              const Jac& J, const CAcc& Ct, float lxa, float lxb,
                                              float reg, uint32_t tight, int m, bool live,
@@ -272,71 +272,160 @@ __device__ __forceinline__ bool team_riccati(float (&Va)[NX], float (&Vb)[NX], f
   // The rare SVD fallback works in shared memory (over V B, dead here, before
   // K is written): Q at sv[0..16), its inverse at sv[16..32). Every lane of a
   // team forms the same Q and inverse, so their identical writes are benign.
+  // STRAIGHT (the register tiers with room for it): the common case runs
+  // straight through, the factorisation with in-range pivots (chol4_fast) and
+  // the three triangular solves, and a warp with a pivot outside the normal
+  // range (Q_uu not positive definite, or degenerate) repeats them for those
+  // lanes through chol4 and, where that fails, the SVD inverse. Otherwise
+  // (96 registers, where the longer live ranges spill) each lane branches on
+  // its own factorisation. Both give the same bits.
   bool ok;
-  Chol4 L;
-  float* sv = xc + X_K;
-  {
-    float Qs[NU][NU];
-#pragma unroll
-    for (int a = 0; a < NU; ++a)
-#pragma unroll
-      for (int b = 0; b < NU; ++b) {
-        if (MASKED) {
-          const bool ta = (tight >> a) & 1u, tb = (tight >> b) & 1u;
-          float val = (ta || tb) ? 0.0f : Quu[a][b];
-          if (a == b && ta) val = val + 1.0f;
-          Qs[a][b] = val + (a == b ? 1e-8f * reg : 0.0f);
-        } else {
-          Qs[a][b] = Quu[a][b] + (a == b ? reg : 0.0f);
-        }
-      }
-    // A lane without an element (live == false) never takes the SVD path: its
-    // numbers are discarded, and the warp would wait for its sweeps.
-    ok = chol4(Qs, L) || !live;
-    if (!ok) {
+  if constexpr (STRAIGHT) {
+    auto form_qs = [&](float (&Qs)[NU][NU]) {
 #pragma unroll
       for (int a = 0; a < NU; ++a)
 #pragma unroll
-        for (int b = 0; b < NU; ++b) sv[a * NU + b] = Qs[a][b];
-      svd_inverse4(sv, sv + NU * NU);
+        for (int b = 0; b < NU; ++b) {
+          if (MASKED) {
+            const bool ta = (tight >> a) & 1u, tb = (tight >> b) & 1u;
+            float val = (ta || tb) ? 0.0f : Quu[a][b];
+            if (a == b && ta) val = val + 1.0f;
+            Qs[a][b] = val + (a == b ? 1e-8f * reg : 0.0f);
+          } else {
+            Qs[a][b] = Quu[a][b] + (a == b ? reg : 0.0f);
+          }
+        }
+    };
+    Chol4 L;
+    bool inr;
+    {
+      float Qs[NU][NU];
+      form_qs(Qs);
+      inr = chol4_fast(Qs, L);
     }
-  }
-  const bool any_fallback = __any_sync(FULL, !ok);
-  if (any_fallback) __syncwarp();  // every fallback inverse of the warp is written
-  auto solve = [&](const float (&rhs)[NU], float (&out)[NU]) {
-    if (ok) {
-      chol4_solve(L, rhs, out);
-    } else {
-      const float* Mi = sv + NU * NU;
+    auto msk = [&](int a, float v) { return (MASKED && ((tight >> a) & 1u)) ? 0.0f : v; };
+    auto solve_all = [&](auto&& solve) {
+      float rhs[NU], sol[NU];
 #pragma unroll
-      for (int a = 0; a < NU; ++a) {
-        float acc = Mi[a * NU] * rhs[0];
+      for (int a = 0; a < NU; ++a) rhs[a] = msk(a, Qxa[a]);
+      solve(rhs, sol);
 #pragma unroll
-        for (int b = 1; b < NU; ++b) acc = fmaf(Mi[a * NU + b], rhs[b], acc);
-        out[a] = acc;
+      for (int a = 0; a < NU; ++a) Ka[a] = -sol[a];
+#pragma unroll
+      for (int a = 0; a < NU; ++a) rhs[a] = msk(a, Qxb[a]);
+      solve(rhs, sol);
+#pragma unroll
+      for (int a = 0; a < NU; ++a) Kb[a] = -sol[a];
+#pragma unroll
+      for (int a = 0; a < NU; ++a) rhs[a] = msk(a, qu[a]);
+      solve(rhs, sol);
+#pragma unroll
+      for (int a = 0; a < NU; ++a) k[a] = -sol[a];
+    };
+    solve_all([&](const float (&rhs)[NU], float (&out)[NU]) { chol4_solve(L, rhs, out); });
+    ok = true;
+    if (__any_sync(FULL, !inr)) {
+      float* sv = xc + X_K;
+      if (!inr) {
+        float Qs[NU][NU];
+        form_qs(Qs);
+        // A lane without an element (live == false) never takes the SVD path:
+        // its numbers are discarded, and the warp would wait for its sweeps.
+        ok = chol4(Qs, L) || !live;
+        if (!ok) {
+#pragma unroll
+          for (int a = 0; a < NU; ++a)
+#pragma unroll
+            for (int b = 0; b < NU; ++b) sv[a * NU + b] = Qs[a][b];
+          svd_inverse4(sv, sv + NU * NU);
+        }
+      }
+      const bool any_fallback = __any_sync(FULL, !ok);
+      if (any_fallback) __syncwarp();  // every fallback inverse of the warp is written
+      if (!inr) {
+        solve_all([&](const float (&rhs)[NU], float (&out)[NU]) {
+          if (ok) {
+            chol4_solve(L, rhs, out);
+          } else {
+            const float* Mi = sv + NU * NU;
+#pragma unroll
+            for (int a = 0; a < NU; ++a) {
+              float acc = Mi[a * NU] * rhs[0];
+#pragma unroll
+              for (int b = 1; b < NU; ++b) acc = fmaf(Mi[a * NU + b], rhs[b], acc);
+              out[a] = acc;
+            }
+          }
+        });
+      }
+      if (any_fallback) __syncwarp();  // the fallback inverses are read; K goes over them
+    }
+  } else {
+    Chol4 L;
+    float* sv = xc + X_K;
+    {
+      float Qs[NU][NU];
+#pragma unroll
+      for (int a = 0; a < NU; ++a)
+#pragma unroll
+        for (int b = 0; b < NU; ++b) {
+          if (MASKED) {
+            const bool ta = (tight >> a) & 1u, tb = (tight >> b) & 1u;
+            float val = (ta || tb) ? 0.0f : Quu[a][b];
+            if (a == b && ta) val = val + 1.0f;
+            Qs[a][b] = val + (a == b ? 1e-8f * reg : 0.0f);
+          } else {
+            Qs[a][b] = Quu[a][b] + (a == b ? reg : 0.0f);
+          }
+        }
+      // A lane without an element (live == false) never takes the SVD path: its
+      // numbers are discarded, and the warp would wait for its sweeps.
+      ok = chol4(Qs, L) || !live;
+      if (!ok) {
+#pragma unroll
+        for (int a = 0; a < NU; ++a)
+#pragma unroll
+          for (int b = 0; b < NU; ++b) sv[a * NU + b] = Qs[a][b];
+        svd_inverse4(sv, sv + NU * NU);
       }
     }
-  };
-  auto msk = [&](int a, float v) { return (MASKED && ((tight >> a) & 1u)) ? 0.0f : v; };
-  {
-    float rhs[NU], sol[NU];
+    const bool any_fallback = __any_sync(FULL, !ok);
+    if (any_fallback) __syncwarp();  // every fallback inverse of the warp is written
+    auto solve = [&](const float (&rhs)[NU], float (&out)[NU]) {
+      if (ok) {
+        chol4_solve(L, rhs, out);
+      } else {
+        const float* Mi = sv + NU * NU;
 #pragma unroll
-    for (int a = 0; a < NU; ++a) rhs[a] = msk(a, Qxa[a]);
-    solve(rhs, sol);
+        for (int a = 0; a < NU; ++a) {
+          float acc = Mi[a * NU] * rhs[0];
 #pragma unroll
-    for (int a = 0; a < NU; ++a) Ka[a] = -sol[a];
+          for (int b = 1; b < NU; ++b) acc = fmaf(Mi[a * NU + b], rhs[b], acc);
+          out[a] = acc;
+        }
+      }
+    };
+    auto msk = [&](int a, float v) { return (MASKED && ((tight >> a) & 1u)) ? 0.0f : v; };
+    {
+      float rhs[NU], sol[NU];
 #pragma unroll
-    for (int a = 0; a < NU; ++a) rhs[a] = msk(a, Qxb[a]);
-    solve(rhs, sol);
+      for (int a = 0; a < NU; ++a) rhs[a] = msk(a, Qxa[a]);
+      solve(rhs, sol);
 #pragma unroll
-    for (int a = 0; a < NU; ++a) Kb[a] = -sol[a];
+      for (int a = 0; a < NU; ++a) Ka[a] = -sol[a];
 #pragma unroll
-    for (int a = 0; a < NU; ++a) rhs[a] = msk(a, qu[a]);
-    solve(rhs, sol);
+      for (int a = 0; a < NU; ++a) rhs[a] = msk(a, Qxb[a]);
+      solve(rhs, sol);
 #pragma unroll
-    for (int a = 0; a < NU; ++a) k[a] = -sol[a];
+      for (int a = 0; a < NU; ++a) Kb[a] = -sol[a];
+#pragma unroll
+      for (int a = 0; a < NU; ++a) rhs[a] = msk(a, qu[a]);
+      solve(rhs, sol);
+#pragma unroll
+      for (int a = 0; a < NU; ++a) k[a] = -sol[a];
+    }
+    if (any_fallback) __syncwarp();  // the fallback inverses are read; K goes over them
   }
-  if (any_fallback) __syncwarp();  // the fallback inverses are read; K goes over them
   // K columns and Q_xu rows -> exchange (over V B, v, l_u)
 #pragma unroll
   for (int a = 0; a < NU; ++a) {
