@@ -369,12 +369,19 @@ def kernel_source_sha(names):
 
 def solve_variant(B: int) -> str:
     """The solve kernel a batch of B elements launches (the library's own
-    choice): the pair layout up to 2048 elements, else the team layout's
-    register tier, the fattest whose residency fits the grid in one wave."""
+    choice, pick_solve_tier in csrc/ilqr_team.cuh): the pair layout up to 2048
+    elements, else the team layout at 8 CTAs per SM while the grid fits one
+    such wave, at 12 up to one such wave, at 19 up to 1.5 waves of 12, and at
+    12 beyond."""
     if B <= 2048:
         return "pair"
     grid = (B + 5) // 6
-    tier = 8 if grid <= 148 * 8 else (12 if grid <= 148 * 12 else 19)
+    if grid <= 148 * 8:
+        tier = 8
+    elif grid <= 148 * 12 or 2 * grid > 3 * 148 * 12:
+        tier = 12
+    else:
+        tier = 19
     return f"team_tier{tier}"
 
 

@@ -503,7 +503,7 @@ cudaError_t launch_backward(const CUtensorMap& tmC, const CUtensorMap& tmG, cons
   }
   const size_t smem = backward_smem_bytes();
   const unsigned grid = (unsigned)((p.B + EPW - 1) / EPW);
-  const int tier = pick_tier(grid);
+  const int tier = pick_backward_tier(grid);
   if (tier == TIER_HI) backward_kernel<TIER_HI><<<grid, WARP, smem, stream>>>(tmC, tmG, p);
   else if (tier == TIER_MID) backward_kernel<TIER_MID><<<grid, WARP, smem, stream>>>(tmC, tmG, p);
   else backward_kernel<TIER_LO><<<grid, WARP, smem, stream>>>(tmC, tmG, p);

@@ -1242,7 +1242,7 @@ cudaError_t launch_solve(const CUtensorMap& tmC, const SolveParams& p, cudaStrea
     return cudaGetLastError();
   }
   const unsigned grid = (unsigned)((p.B + EPW - 1) / EPW);
-  const int tier = pick_tier(grid);
+  const int tier = pick_solve_tier(grid);
   const size_t smem = solve_smem_bytes(tier);
   if (ref) {
     if (tier == TIER_HI) solve_kernel<TEAM, true, TIER_HI><<<grid, WARP, smem, stream>>>(tmC, p);

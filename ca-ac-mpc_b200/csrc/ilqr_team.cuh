@@ -34,17 +34,31 @@ constexpr int X_K = 100;      // [4][10]  K: gain row a at X_K + 10a (over V B)
 constexpr int X_QXU = 140;    // [4][10]  Q_ux: Q_xu[c][a] at X_QXU + 10a + c (over v, l_u)
 constexpr uint32_t TSLAB_BYTES = EPW * CBLK * 4u;  // bytes one TMA box delivers
 
-// Register tiers. Each kernel is compiled for three minimum residencies
-// (CTAs of one warp per SM); the launch picks the fattest tier whose
-// residency still fits the whole grid in one wave on 148 SMs. 19 CTAs per SM
-// caps registers at 96 (one scheduler holds five warps of its 16 K
-// registers), 12 at 168, 8 at 255; fewer registers spill.
+// Register tiers: minimum residencies (CTAs of one warp per SM) the kernels
+// are compiled for. 19 CTAs per SM caps registers at 96 (one scheduler holds
+// five warps of its 16 K registers), 12 at 168, 8 at 255; fewer registers
+// spill. The launch takes the fattest tier whose residency fits the grid in
+// one wave, except where more waves of a fatter tier are faster (B200,
+// T = 20, 5 iterations):
+//  - The solve's 96-register build spills across every Riccati step. Past
+//    1.5 waves of the 12-CTA tier (B > 15984) that tier is faster than one
+//    19-CTA wave (B = 14336: 2.2 % slower, 15360: even, 16384: 2.7 % faster),
+//    and past one 19-CTA wave by far (B = 20480: 1.34 against 1.98 ms;
+//    B = 65536: 13 %).
+//  - The backward spills less at 96 registers: it takes the 19-CTA tier up
+//    to one wave (B = 16384: 0.245 against 0.259 ms at 12 CTAs) and the
+//    12-CTA tier beyond (B = 20480: 0.280 against 0.383 ms; B = 65536: 2.5 %).
 constexpr int SMS = 148;
 constexpr int TIER_LO = 19, TIER_MID = 12, TIER_HI = 8;
-inline int pick_tier(int64_t grid) {
+inline int pick_solve_tier(int64_t grid) {
   if (grid <= (int64_t)SMS * TIER_HI) return TIER_HI;
   if (grid <= (int64_t)SMS * TIER_MID) return TIER_MID;
-  return TIER_LO;
+  return 2 * grid <= 3 * (int64_t)SMS * TIER_MID ? TIER_LO : TIER_MID;
+}
+inline int pick_backward_tier(int64_t grid) {
+  if (grid <= (int64_t)SMS * TIER_HI) return TIER_HI;
+  if (grid <= (int64_t)SMS * TIER_MID) return TIER_MID;
+  return grid <= (int64_t)SMS * TIER_LO ? TIER_LO : TIER_MID;
 }
 
 __device__ __forceinline__ int row_a(int m) { return m < 4 ? 3 + m : 0; }
