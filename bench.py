@@ -369,11 +369,11 @@ def kernel_source_sha(names):
 
 def solve_variant(B: int) -> str:
     """The solve kernel a batch of B elements launches (the library's own
-    choice, pick_solve_tier in csrc/ilqr_team.cuh): the pair layout up to 2048
+    choice, PAIR_MAX_B and pick_solve_tier in csrc/): the pair layout up to 4096
     elements, else the team layout at 8 CTAs per SM while the grid fits one
     such wave, at 12 up to one such wave, at 19 up to 1.5 waves of 12, and at
     12 beyond."""
-    if B <= 2048:
+    if B <= 4096:
         return "pair"
     grid = (B + 5) // 6
     if grid <= 148 * 8:

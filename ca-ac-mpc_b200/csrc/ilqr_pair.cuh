@@ -36,8 +36,12 @@ namespace ilqr {
 constexpr int HALF = 16;   // lanes per element
 constexpr int EPWP = 2;    // elements per warp
 // Batches up to this size (and horizons up to PAIR_MAX_T, whose per-step
-// tables fit in shared memory) run in the pair layout by default.
-constexpr int64_t PAIR_MAX_B = 2048;
+// tables fit in shared memory) run in the pair layout by default. One wave
+// holds 2368 elements (8 CTAs per SM at T = 20); up to 4096 elements (1.73
+// waves) the pair layout is still faster than the team layout (B200, T = 20,
+// fwd+bwd: B = 2560 10 %, 3072 3 %, 4096 6.5 %), from 5120 it is slower
+// (13 % at 5120: a third wave).
+constexpr int64_t PAIR_MAX_B = 4096;
 constexpr int PAIR_MAX_T = 64;
 
 // Per-element shared-memory area (floats; float4 fields 16-byte aligned).

@@ -127,12 +127,12 @@ def test_default_layout_by_batch(monkeypatch):
     """The default picks the pair layout up to PAIR_MAX_B and the team layout
     above; the first elements of a batch just above the limit equal those of
     a batch just below it (prefix independence across the two layouts)."""
-    cfg, inp = wl.config_inputs("rollout_b16384_t20", B=2052)
+    cfg, inp = wl.config_inputs("rollout_b16384_t20", B=4100)
     t = {k: g(v) for k, v in inp.items()}
     kw = dict(dt=wl.DT, max_iter=cfg["max_iter"], alphas=cfg["alphas"], want_trace=True)
     lo, hi = g(wl.U_MIN), g(wl.U_MAX)
     big = nat.solve(t["x0"], t["U_init"], t["C"], t["c"], None, None, None, None, lo, hi, **kw)
-    small = nat.solve(*(t[k][:2048].contiguous() for k in ("x0", "U_init", "C", "c")), None, None, None, None,
+    small = nat.solve(*(t[k][:4096].contiguous() for k in ("x0", "U_init", "C", "c")), None, None, None, None,
                       lo, hi, **kw)
     for k in ("X", "U", "tight", "trace"):
-        assert torch.equal(big[k][:2048], small[k]), k
+        assert torch.equal(big[k][:4096], small[k]), k
