@@ -1027,9 +1027,10 @@ def run_ours(args):
                             "count": "dense per-unit counts (ilqr_costmodel: Riccati 16.9k, candidate 0.88k, "
                                      "initial 0.75k, backward 18.0k FLOP per element and step)"},
                "e2e": r13_e2e_res,
-               "latency_b16_t5": {"p50_us": statistics.median(lsamp),
-                                  "p90_us": sorted(lsamp)[int(0.9 * len(lsamp))], "reps": len(lsamp),
-                                  "config": "B=16, T=5, 10 iterations, fwd+bwd, device-resident, eager"}}
+               "latency_b16_t5": ({"p50_us": statistics.median(lsamp),
+                                   "p90_us": sorted(lsamp)[int(0.9 * len(lsamp))], "reps": len(lsamp),
+                                   "config": "B=16, T=5, 10 iterations, fwd+bwd, device-resident, eager"}
+                                  if lsamp else None)}
 
     # ---- FastMPC numerics mode (ilqr_fastmpc.cu) --------------------------------
     # The reference FastMPC extension's own numerics on the same inputs: PNQP
