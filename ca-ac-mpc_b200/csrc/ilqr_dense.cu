@@ -34,9 +34,16 @@ namespace {
 
 constexpr int GL = 16;             // lanes per element
 constexpr int EPW = 2;             // elements per warp
-constexpr int WPC = 4;             // warps per CTA
-constexpr int EPC = EPW * WPC;     // elements per CTA
-constexpr int THREADS = WPC * 32;  // threads per CTA
+constexpr int WPC = 4;             // warps per CTA (backward)
+constexpr int EPC = EPW * WPC;     // elements per CTA (backward)
+constexpr int THREADS = WPC * 32;  // threads per CTA (backward)
+// The solve launches one-warp CTAs: its warps share nothing, and its
+// elements run 1 to max_iter iterations (at B = 16384, T = 20, 5 iterations,
+// 63 % stop after one), so a CTA should free its registers as soon as its
+// own two elements are done, not when the slowest of eight is.
+constexpr int S_WPC = 1;
+constexpr int S_EPC = EPW * S_WPC;
+constexpr int S_THREADS = S_WPC * 32;
 constexpr int REC = 20;            // floats per trajectory record: x[13], u[4], 3 pad
 constexpr int SM_COUNT = 148;      // B200 SMs (the launch's one-wave test)
 
@@ -517,17 +524,18 @@ __device__ __forceinline__ float pick(const float (&v)[N], int i) {
 // ---------------------------------------------------------------------------
 // Solve (controller.py:303-435)
 // ---------------------------------------------------------------------------
-// MINB: resident CTAs per SM the register budget targets. 2 (254 registers,
-// no spills) is faster while the grid fits one wave at 2 CTAs per SM; beyond
-// that 3 (168 registers, about 90 B of spills) is, by the extra warps per SM.
+// MINB: resident one-warp CTAs per SM the register budget targets. 8 (255
+// registers, no spills) is faster while the grid fits one wave at 8 CTAs per
+// SM; beyond that 12 (168 registers, some spills) is, by the extra warps per
+// SM.
 template <int MINB>
-__global__ void __launch_bounds__(THREADS, MINB) dense_solve_kernel(DenseSolveParams p) {
+__global__ void __launch_bounds__(S_THREADS, MINB) dense_solve_kernel(DenseSolveParams p) {
   extern __shared__ __align__(16) float smem[];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int e = lane >> 4;   // element slot of the warp
   const int g = lane & 15;   // lane in the group
-  const int64_t b = ((int64_t)blockIdx.x * WPC + warp) * EPW + e;
+  const int64_t b = ((int64_t)blockIdx.x * S_WPC + warp) * EPW + e;
   const bool valid = b < p.B;
   const int64_t bw = valid ? b : 0;  // a valid element for address formation
   float* sm = smem + (warp * EPW + e) * S_ELEM;
@@ -1139,12 +1147,12 @@ static size_t dense_smem_bytes(int elem_floats) { return (size_t)r13::EPC * elem
 
 cudaError_t launch_dense_solve(const DenseSolveParams& p, cudaStream_t stream) {
   if (p.B == 0) return cudaSuccess;
-  const int64_t grid = (p.B + r13::EPC - 1) / r13::EPC;
-  const size_t smem = dense_smem_bytes(r13::S_ELEM);
-  if (grid > 2 * r13::SM_COUNT)
-    r13::dense_solve_kernel<3><<<(unsigned)grid, r13::THREADS, smem, stream>>>(p);
+  const int64_t grid = (p.B + r13::S_EPC - 1) / r13::S_EPC;
+  const size_t smem = (size_t)r13::S_EPC * r13::S_ELEM * sizeof(float);
+  if (grid > 8 * r13::SM_COUNT)
+    r13::dense_solve_kernel<12><<<(unsigned)grid, r13::S_THREADS, smem, stream>>>(p);
   else
-    r13::dense_solve_kernel<2><<<(unsigned)grid, r13::THREADS, smem, stream>>>(p);
+    r13::dense_solve_kernel<8><<<(unsigned)grid, r13::S_THREADS, smem, stream>>>(p);
   return cudaGetLastError();
 }
 
