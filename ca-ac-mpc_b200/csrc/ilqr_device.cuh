@@ -331,6 +331,13 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src)
                "l"(gmem_src)
                : "memory");
 }
+// 4-byte copy (any 4-byte aligned address), cached in L1 like a plain load.
+__device__ __forceinline__ void cp_async_f32(float* smem_dst, const float* gmem_src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+               "l"(gmem_src)
+               : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {

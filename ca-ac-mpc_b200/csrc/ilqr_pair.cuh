@@ -68,8 +68,8 @@ constexpr int PREC_F = 16, PJT_F = 32, PKS_F = 44, PCR_F = 32;
 constexpr int PLX_F = 16;
 // Floats per element: the fixed part and `per_t` floats per step, rounded so
 // that the two elements' areas start 16 floats apart modulo the 32 banks.
-__host__ __device__ __forceinline__ int pair_area(int T, int per_t) {
-  const int n = PBASE + per_t * T;
+__host__ __device__ __forceinline__ int pair_area(int T, int per_t, int extra = 0) {
+  const int n = PBASE + per_t * T + extra;
   return (n + 31) / 32 * 32 + 16;
 }
 
@@ -420,21 +420,30 @@ __device__ __forceinline__ float pair_sum5(float x, int base) {
   return s;
 }
 
-// Double-buffered cp.async stream of one element's C_t blocks (16 lanes,
-// 49 copies of 16 bytes per block). issue(t) copies block t into buffer
-// t & 1; each lane commits one group per issue.
+// cp.async stream of one element's C_t blocks (16 lanes, 49 copies of 16
+// bytes per block) through two buffers (buf) or, with a third buffer (buf3),
+// three: issue(t) copies block t into buffer t mod depth; each lane commits
+// one group per issue. With three buffers a pass can keep two blocks in
+// flight while it works on a third.
 struct PairCPipe {
   const float* Cb;   // C block of (element, t) at Cb + t * tstride * CBLK
   int64_t tstride;
-  float* buf;        // the element's area + PC0
+  float* buf;        // the element's area + PC0 (two blocks)
   int i;
+  float* buf3 = nullptr;  // a third block's buffer, or none
+  __device__ __forceinline__ float* block(int t) const {
+    if (buf3 != nullptr) {
+      const int r = t % 3;
+      return r == 2 ? buf3 : buf + r * CBLK;
+    }
+    return buf + (t & 1) * CBLK;
+  }
   __device__ __forceinline__ void issue(int t) {
     const float* src = Cb + (int64_t)t * tstride * CBLK;
-    float* dst = buf + (t & 1) * CBLK;
+    float* dst = block(t);
     for (int q = i; q < CBLK / 4; q += HALF) cp_async16(dst + 4 * q, src + 4 * q);
     cp_async_commit();
   }
-  __device__ __forceinline__ float* block(int t) const { return buf + (t & 1) * CBLK; }
 };
 
 }  // namespace ilqr

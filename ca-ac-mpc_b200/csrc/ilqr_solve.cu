@@ -740,7 +740,7 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
   const int T = p.T;
   const float dt = p.dt;
   const SolveWs W{p, (uint32_t)bw};
-  float* sh = reinterpret_cast<float*>(smem) + h * pair_area(T, PREC_F + PJT_F + PKS_F + PCR_F);
+  float* sh = reinterpret_cast<float*>(smem) + h * pair_area(T, PREC_F + PJT_F + PKS_F + PCR_F, CBLK);
   float* REC = sh + PBASE;                  // [T][16] nominal x_t, u_t
   float* JT = REC + PREC_F * T;             // [T][32] Jacobian tables
   float* KS = JT + PJT_F * T;               // [T][44] K columns (4 each), then k
@@ -774,24 +774,41 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
 
   const bool sigm = p.sig.p != nullptr;
   const float* sgrow = sigm ? p.sig.p + bw * (int64_t)(2 * NT) * T : nullptr;
-  // c_t (and, from policy parameters, diag C_t) of every step into the cost
-  // records, all (t, k) at once; the loads complete behind the rollout below
-#pragma unroll 4
-  for (int f = i; f < T * NT; f += HALF) {
-    const int t = f / NT, k = f - t * NT;
-    float* cr = CR + PCR_F * t;
-    cr[16 + k] = sigm ? sig_c(p.sig, sgrow, T, t, k) : ldg_or0(cb + t * p.c_tstride + k, valid);
-    if (sigm) cr[k] = sig_diag(p.sig, sgrow, T, t, k);
+  // U_init of every step into the record table (a step per lane), then c_t
+  // of every step into the cost records (all (t, k) at once), as cp.async
+  // groups in that order: the rollout below waits for the first only, and
+  // the second completes behind it. From policy parameters the cost records
+  // (c_t and diag C_t) are computed instead.
+  for (int t = i; t < T; t += HALF) {
+    float* r = REC + PREC_F * t;
+#pragma unroll
+    for (int a = 0; a < NU; ++a) {
+      if (valid) cp_async_f32(r + NX + a, p.U_init + (b * T + t) * NU + a);
+      else r[NX + a] = 0.0f;
+    }
   }
+  cp_async_commit();
+  if (sigm) {
+#pragma unroll 4
+    for (int f = i; f < T * NT; f += HALF) {
+      const int t = f / NT, k = f - t * NT;
+      float* cr = CR + PCR_F * t;
+      cr[16 + k] = sig_c(p.sig, sgrow, T, t, k);
+      cr[k] = sig_diag(p.sig, sgrow, T, t, k);
+    }
+  } else {
+    for (int f = i; f < T * NT; f += HALF) {
+      const int t = f / NT, k = f - t * NT;
+      float* d = CR + PCR_F * t + 16 + k;
+      if (valid) cp_async_f32(d, cb + t * p.c_tstride + k);
+      else *d = 0.0f;
+    }
+  }
+  cp_async_commit();
 
   // ---- initial open-loop rollout with U_init into slot 0 (and the record table)
   {
-    // U_init of every step into the record table first (a step per lane)
-    for (int t = i; t < T; t += HALF) {
-      float* r = REC + PREC_F * t;
-#pragma unroll
-      for (int a = 0; a < NU; ++a) r[NX + a] = ldg_or0(p.U_init + (b * T + t) * NU + a, valid);
-    }
+    cp_async_wait<1>();  // this lane's U_init copies
     __syncwarp();
     float x[NX];
     load_x0(x);
@@ -808,9 +825,11 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
     }
     if (writer) store_rec_x(W.rec(0, T), x);
   }
+  cp_async_wait<0>();  // this lane's cost-record copies
   __syncwarp();
 
-  PairCPipe cpipe{sigm ? nullptr : p.C + bw * p.C_bstride * CBLK, p.C_tstride, sh + PC0, i};
+  PairCPipe cpipe{sigm ? nullptr : p.C + bw * p.C_bstride * CBLK, p.C_tstride, sh + PC0, i,
+                  sh + PBASE + (PREC_F + PJT_F + PKS_F + PCR_F) * T};
   bool diag = sigm;
   bool offd = false;
   if (sigm) {
@@ -852,7 +871,10 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
     bool fallback = false;
     float cost_q = 0.0f, cost_l = 0.0f;
     const bool first = (it == 0);
-    if (!diag) cpipe.issue(T - 1);
+    if (!diag) {  // two blocks in flight ahead of the step that works on a third
+      cpipe.issue(T - 1);
+      if (T >= 2) cpipe.issue(T - 2);
+    }
     // prologue: every step's nominal record (already in the table on the
     // first pass: the initial rollout wrote it) and Jacobian table, a step per lane
     for (int t = i; t < T; t += HALF) {
@@ -879,8 +901,10 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
       float* cr = CR + PCR_F * t;
       const float cv = cr[16 + ti];  // c_t entry ti
       if (!diag) {
-        if (t > 0) {
-          cpipe.issue(t - 1);
+        if (t >= 2) {
+          cpipe.issue(t - 2);
+          cp_async_wait<2>();
+        } else if (t == 1) {
           cp_async_wait<1>();
         } else {
           cp_async_wait<0>();
@@ -1044,9 +1068,12 @@ __global__ void __launch_bounds__(32, MINB) solve_pair_kernel(const SolveParams 
         sl += lp;
       } else {
         cpipe.issue(0);
+        if (T >= 2) cpipe.issue(1);
         for (int t = 0; t < T; ++t) {
-          if (t + 1 < T) {
-            cpipe.issue(t + 1);
+          if (t + 2 < T) {
+            cpipe.issue(t + 2);
+            cp_async_wait<2>();
+          } else if (t + 1 < T) {
             cp_async_wait<1>();
           } else {
             cp_async_wait<0>();
@@ -1227,7 +1254,7 @@ size_t solve_smem_bytes(int tier) {
 }
 
 size_t solve_pair_smem_bytes(int T) {
-  return (size_t)EPWP * pair_area(T, PREC_F + PJT_F + PKS_F + PCR_F) * sizeof(float);
+  return (size_t)EPWP * pair_area(T, PREC_F + PJT_F + PKS_F + PCR_F, CBLK) * sizeof(float);
 }
 
 cudaError_t launch_solve(const CUtensorMap& tmC, const SolveParams& p, cudaStream_t stream) {
