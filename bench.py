@@ -382,7 +382,21 @@ def solve_variant(B: int) -> str:
         tier = 12
     else:
         tier = 19
-    return f"team_tier{tier}"
+    return f"team_tier{tier}" + ("_seg" if solve_segmented(B, 5) else "")
+
+
+def solve_segmented(B: int, max_iter: int) -> bool:
+    """Whether the library runs this solve in two launches (launch_solve in
+    csrc/ilqr_solve.cu: team layout beyond one 8-CTA wave, max_iter >= 4, no
+    forced trace, ILQR_B200_SEGMENT not 0): the first max_iter - 2 iterations,
+    then the elements still improving, compacted."""
+    if os.environ.get("ILQR_B200_SEGMENT", "1").startswith("0"):
+        return False
+    return B > 4096 and (B + 5) // 6 > 148 * 8 and max_iter >= 4
+
+
+def solve_launches(B: int, max_iter: int) -> int:
+    return 2 if solve_segmented(B, max_iter) else 1
 
 
 SOLVE_SOURCES = ("ilqr_solve.cu", "ilqr_team.cuh", "ilqr_pair.cuh", "ilqr_device.cuh")
@@ -1234,7 +1248,7 @@ def run_ours(args):
         "cpu_baseline": cpu,
         "e2e": None if e2e is None else {k: e2e[k] for k in ("value", "unit", "h2d_bytes_per_step",
                                                              "d2h_bytes_per_step")},
-        "gpu_launches": 2 * args.steps, "clocks": clk.summary(),
+        "gpu_launches": (solve_launches(B, iters) + 1) * args.steps, "clocks": clk.summary(),
         "latency_b16_t5_p50_us": None if lat is None else rnd(lat["p50_us"]),
         "kernel_ms": {"solve": rnd(statistics.mean(solve_ms)), "bwd": rnd(statistics.mean(bwd_ms)),
                       "gather": rnd(gather_ms) if world > 1 else None, "eager_step": rnd(eager_per_step * 1e3),

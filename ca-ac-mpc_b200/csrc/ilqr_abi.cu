@@ -155,6 +155,11 @@ int solve_impl(const float* x0, const float* U_init, const float* C, const float
   p.C_bstride = time_major ? 1 : (int64_t)T;
   p.C_tstride = time_major ? B : 1;
   p.layout = layout_from_env();
+  // ILQR_B200_SEGMENT=0 keeps large team-layout solves in one launch (both
+  // give the same bits)
+  const char* sg = std::getenv("ILQR_B200_SEGMENT");
+  p.segment = (sg != nullptr && sg[0] == '0') ? 0 : 1;
+  p.seg = ilqr::SEG_WHOLE;
   CUtensorMap tmC;
   std::memset(&tmC, 0, sizeof(tmC));  // never read in sigmoid mode (no pass copies C)
   if (sig.p == nullptr) {

@@ -60,7 +60,23 @@ struct SolveParams {
   int64_t C_bstride;
   int64_t C_tstride;
   int layout;  // LAYOUT_AUTO, LAYOUT_TEAM or LAYOUT_PAIR
+  int segment;  // 0: off; else the team layout may run in two launches (SEG_*)
+  int seg;      // this launch: SEG_WHOLE, SEG_FIRST or SEG_RESUME
+  int seg_it;   // iterations of the first launch
 };
+
+// Segmented team solve. Elements stop after different numbers of iterations
+// (B = 16384, T = 20, 5 iterations: 3.45 on average), while a warp of six runs
+// until its last one stops (4.74 on average), so a third of the lanes idle.
+// SEG_FIRST runs every element for seg_it iterations; warps whose costs are
+// diagonal then stop, and each of their elements that is still improving
+// saves its state (nominal slot, best cost, status bits) and enters a list.
+// SEG_RESUME runs the listed elements, six per warp, from iteration seg_it
+// to the end. The arithmetic of every element is the same, so the results
+// are the same bits. State, list and count live in floats 12..15 of the
+// t = T records of slots 0, 1 and 2 (element 0's for the count), which the
+// solve never uses otherwise.
+constexpr int SEG_WHOLE = 0, SEG_FIRST = 1, SEG_RESUME = 2;
 
 // Kernel layouts of the 10-state solve and backward. TEAM: six elements per
 // warp, five lanes each (ilqr_team.cuh); PAIR: two elements per warp,

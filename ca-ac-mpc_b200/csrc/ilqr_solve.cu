@@ -100,7 +100,16 @@ struct SolveWs {
     return gk() + (size_t)p.T * (NX + 1) * S() * 4 + (size_t)r * COST_REC;
   }
   __device__ __forceinline__ float* cvec(int t) const { return diag(t) + 16; }
+  // segmented solve (SEG_*): the element's saved state, list entry pos and
+  // the list's count, in floats 12..15 of t = T records
+  __device__ __forceinline__ float4* seg_state() const { return rec(0, p.T) + 3; }
 };
+__device__ __forceinline__ int* seg_entry(const SolveParams& p, int64_t pos) {
+  return reinterpret_cast<int*>(p.ws + (((size_t)(p.T + 1) + p.T) * p.S + pos) * TRJ_REC + 12);
+}
+__device__ __forceinline__ int* seg_count(const SolveParams& p) {
+  return reinterpret_cast<int*>(p.ws + ((size_t)(2 * (p.T + 1) + p.T) * p.S) * TRJ_REC + 12);
+}
 
 __device__ __forceinline__ void load_rec(const float4* r, float (&x)[NX], float (&u)[NU]) {
   const float4 a = r[0], c = r[1], d = r[2], e = r[3];
@@ -258,10 +267,20 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
   const int m = lane - (dup ? EPW * TEAM : e * TEAM);
   const int base = e * TEAM;
   const int64_t b0 = (int64_t)blockIdx.x * EPW;
-  const int64_t b = b0 + e;
-  const bool valid = b < p.B;        // the lane's element exists (loads, compute)
-  const bool own = valid && !dup;     // ... and this lane writes its results
-  const int64_t bw = valid ? b : b0;  // workspace record read by this lane (never written when !own)
+  const bool resume = p.seg == SEG_RESUME;
+  int64_t b = b0 + e;
+  bool valid = b < p.B;  // the lane's element exists (loads, compute)
+  if (resume) {          // elements from the list the first launch made
+    int64_t cnt = *(volatile const int*)seg_count(p);
+    cnt = cnt < 0 ? 0 : (cnt > p.B ? p.B : cnt);
+    if (b0 >= cnt) return;  // the whole CTA lies beyond the list
+    valid = b < cnt;
+    const int64_t ent = valid ? (int64_t)*seg_entry(p, b) : 0;
+    valid = valid && ent >= 0 && ent < p.B;  // (an entry out of range is skipped)
+    b = valid ? ent : 0;
+  }
+  const bool own = valid && !dup;  // ... and this lane writes its results
+  const int64_t bw = valid ? b : (resume ? 0 : b0);  // workspace record read by this lane (never written when !own)
   const int T = p.T;
   const float dt = p.dt;
   const SolveWs W{p, (uint32_t)bw};
@@ -294,11 +313,11 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
     for (int i = 0; i < NX; ++i) x[i] = ldg_or0(p.x0 + b * NX + i, valid);
   };
   const bool writer = own && m == 0;
-  if (p.trace != nullptr && writer)
+  if (p.trace != nullptr && writer && !resume)
     for (int i = 0; i < p.max_iter; ++i) p.trace[b * p.max_iter + i] = (int8_t)-128;
 
   // ---- initial open-loop rollout with U_init into slot 0 (controller.py:305, 578-603)
-  {
+  if (!resume) {
     float x[NX];
     load_x0(x);
     for (int t = 0; t < T; ++t) {
@@ -343,17 +362,33 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
   // zeros off the diagonal from the start, and no pass reads C.
   const bool sigm = p.sig.p != nullptr;
   const float* sgrow = sigm ? p.sig.p + bw * (int64_t)(2 * NT) * T : nullptr;
-  bool diag = sigm;   // warp-uniform: all C[b, t] of the warp's elements are diagonal (known after pass 1)
+  // warp-uniform: all C[b, t] of the warp's elements are diagonal (known
+  // after pass 1; every resumed element comes from such a warp)
+  bool diag = sigm || resume;
   bool offd = false;  // this lane saw a nonzero off-diagonal entry during pass 1
-  if (sigm) {
+  if (diag) {
     for (int f = lane; f < EPW * CBLK; f += WARP) slab[f] = 0.0f;
     __syncwarp();
   }
+  // resumed launch: every lane starts at iteration seg_it (warp-uniform); a
+  // listed element restores the state the first launch saved (it improved in
+  // every iteration so far). Lanes past the end of the list keep slot 0 of
+  // their stand-in element: its saved state may never have been written.
+  const int it_begin = resume ? p.seg_it : 0;
+  if (resume && valid) {
+    const float4 st = *W.seg_state();
+    nom = __float_as_int(st.x);
+    nom = nom < 0 ? 0 : (nom >= SOLVE_SLOTS ? SOLVE_SLOTS - 1 : nom);
+    best = st.y;
+    status = __float_as_uint(st.z);
+    iters = p.seg_it;
+  }
+  bool deferred = false;  // SEG_FIRST: this element continues in the resumed launch
 
   // The first pass always runs: it also yields the initial objective (with
   // max_iter == 0 only that).
   const int n_loop = p.max_iter > 0 ? p.max_iter : 1;
-  for (int it = 0; it < n_loop; ++it) {
+  for (int it = it_begin; it < n_loop; ++it) {
     const bool cost_only = it >= p.max_iter;
     if (!cost_only && p.forced != nullptr && active && p.forced[b * p.max_iter + it] == (int8_t)-128)
       active = false;
@@ -666,11 +701,21 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
       if (rerun) nom = dst;
       __syncwarp();
     }
+    if (p.seg == SEG_FIRST && it + 1 == p.seg_it && diag) {
+      // Elements still improving continue in the resumed launch, six per warp;
+      // this warp stops here.
+      deferred = active;
+      if (deferred && writer) {
+        *W.seg_state() = make_float4(__int_as_float(nom), best, __uint_as_float(status), 0.0f);
+        *seg_entry(p, atomicAdd(seg_count(p), 1)) = (int)b;
+      }
+      break;
+    }
   }
 
   // ---- outputs (lanes of a team split the writes) -----------------------------
   bool finite = true;
-  if (own) {
+  if (own && !deferred) {
     const float* nrec = reinterpret_cast<const float*>(W.rec(nom, 0));
     const int64_t rstride = p.S * TRJ_REC;  // floats between the records of t and t + 1
     for (int f = m; f < (T + 1) * NX; f += TEAM) {
@@ -701,7 +746,7 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
   const bool all_finite = team_sum(finite ? 0.0f : 1.0f, base) == 0.0f;
   if (!all_finite) status |= ELEM_NONFINITE;
   if (diag) status |= ELEM_DIAG_COST;
-  if (writer) {
+  if (writer && !deferred) {
     if (p.iters) p.iters[b] = iters;
     if (p.status) p.status[b] = status;
     if (p.best_cost) p.best_cost[b] = best;
@@ -1269,18 +1314,35 @@ cudaError_t launch_solve(const CUtensorMap& tmC, const SolveParams& p, cudaStrea
     return cudaGetLastError();
   }
   const unsigned grid = (unsigned)((p.B + EPW - 1) / EPW);
-  const int tier = pick_solve_tier(grid);
-  const size_t smem = solve_smem_bytes(tier);
-  if (ref) {
-    if (tier == TIER_HI) solve_kernel<TEAM, true, TIER_HI><<<grid, WARP, smem, stream>>>(tmC, p);
-    else if (tier == TIER_MID) solve_kernel<TEAM, true, TIER_MID><<<grid, WARP, smem, stream>>>(tmC, p);
-    else solve_kernel<TEAM, true, TIER_LO><<<grid, WARP, smem, stream>>>(tmC, p);
-  } else {
-    if (tier == TIER_HI) solve_kernel<TEAM, false, TIER_HI><<<grid, WARP, smem, stream>>>(tmC, p);
-    else if (tier == TIER_MID) solve_kernel<TEAM, false, TIER_MID><<<grid, WARP, smem, stream>>>(tmC, p);
-    else solve_kernel<TEAM, false, TIER_LO><<<grid, WARP, smem, stream>>>(tmC, p);
-  }
-  return cudaGetLastError();
+  auto launch = [&](const SolveParams& q, int tier) {
+    const size_t smem = solve_smem_bytes(tier);
+    if (ref) {
+      if (tier == TIER_HI) solve_kernel<TEAM, true, TIER_HI><<<grid, WARP, smem, stream>>>(tmC, q);
+      else if (tier == TIER_MID) solve_kernel<TEAM, true, TIER_MID><<<grid, WARP, smem, stream>>>(tmC, q);
+      else solve_kernel<TEAM, true, TIER_LO><<<grid, WARP, smem, stream>>>(tmC, q);
+    } else {
+      if (tier == TIER_HI) solve_kernel<TEAM, false, TIER_HI><<<grid, WARP, smem, stream>>>(tmC, q);
+      else if (tier == TIER_MID) solve_kernel<TEAM, false, TIER_MID><<<grid, WARP, smem, stream>>>(tmC, q);
+      else solve_kernel<TEAM, false, TIER_LO><<<grid, WARP, smem, stream>>>(tmC, q);
+    }
+    return cudaGetLastError();
+  };
+  // Batches beyond one 8-CTA wave run in two launches (SEG_*): the first
+  // max_iter - 2 iterations for every element, then the elements still
+  // improving, compacted six per warp, at 12 CTAs per SM (the resumed batch
+  // is a fraction of the first, and the count is known only on the device).
+  const bool segmented = p.segment != 0 && p.forced == nullptr && p.max_iter >= 4 && grid > (unsigned)(SMS * TIER_HI);
+  if (!segmented) return launch(p, pick_solve_tier(grid));
+  SolveParams q = p;
+  q.seg_it = p.max_iter - 2;
+  int* count = reinterpret_cast<int*>(p.ws + ((size_t)(2 * (p.T + 1) + p.T) * p.S) * TRJ_REC + 12);
+  cudaError_t e = cudaMemsetAsync(count, 0, sizeof(int), stream);
+  if (e != cudaSuccess) return e;
+  q.seg = SEG_FIRST;
+  e = launch(q, pick_solve_tier(grid));
+  if (e != cudaSuccess) return e;
+  q.seg = SEG_RESUME;
+  return launch(q, TIER_MID);
 }
 
 }  // namespace ilqr

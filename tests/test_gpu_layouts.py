@@ -136,3 +136,57 @@ def test_default_layout_by_batch(monkeypatch):
                       lo, hi, **kw)
     for k in ("X", "U", "tight", "trace"):
         assert torch.equal(big[k][:4096], small[k]), k
+
+
+def _segmented_vs_whole(monkeypatch, inp, cfg, T):
+    """Solve (and backward) with the segmented team solve and in one launch."""
+    t = {k: g(v) for k, v in inp.items()}
+    lo, hi = g(wl.U_MIN), g(wl.U_MAX)
+    gX, gU = (g(a) for a in wl.make_backward_seeds(t["x0"].shape[0], T))
+    out = {}
+    for seg in ("1", "0"):
+        monkeypatch.setenv("ILQR_B200_SEGMENT", seg)
+        s = nat.solve(t["x0"], t["U_init"], t["C"], t["c"], None, None, None, None, lo, hi, dt=wl.DT,
+                      max_iter=cfg["max_iter"], alphas=cfg["alphas"], want_trace=True, want_stats=True)
+        r = nat.backward(s["X"], s["U"], t["C"], gX, gU, tight=s["tight"], dt=wl.DT, reg_eps=wl.REG_EPS)
+        torch.cuda.synchronize()
+        out[seg] = (s, r)
+    monkeypatch.delenv("ILQR_B200_SEGMENT")
+    return out["1"], out["0"]
+
+
+def test_segmented_team_solve_same_bits(monkeypatch):
+    """Large team-layout batches run in two launches: every element for
+    max_iter - 2 iterations, then the elements still improving, compacted six
+    per warp. The training-scale batch (B = 16384, T = 20, 5 iterations, the
+    diagonal costs the policy builds) gives the same bits as one launch: X, U,
+    tight mask, trace, iterations, status, best cost, stall record and every
+    gradient of the backward at the solution."""
+    cfg, inp = wl.config_inputs("rollout_b16384_t20")
+    (s1, r1), (s0, r0) = _segmented_vs_whole(monkeypatch, inp, cfg, cfg["T"])
+    assert int((s0["iters"] > cfg["max_iter"] - 2).sum()) > 1000  # the resumed launch has work
+    for k in ("X", "U", "tight", "trace", "iters", "status", "best_cost", "stall_iter", "stall_gap"):
+        a, b = s1[k].cpu().numpy(), s0[k].cpu().numpy()
+        assert np.array_equal(a, b, equal_nan=a.dtype.kind == "f"), k
+    for k in r0:
+        assert torch.equal(r1[k], r0[k]), k
+
+
+def test_segmented_team_solve_mixed_warps(monkeypatch):
+    """A batch in which some warps hold a dense (non-diagonal) cost block: those
+    warps finish in the first launch, the others resume; same bits as one
+    launch."""
+    cfg, inp = wl.config_inputs("rollout_b16384_t20", B=9000)
+    C = inp["C"].copy()
+    rng = np.random.default_rng(3)
+    for b in rng.choice(9000, size=40, replace=False):  # one off-diagonal pair in some element's step
+        t = int(rng.integers(0, cfg["T"]))
+        C[b, t, 0, 1] = C[b, t, 1, 0] = 1e-3
+    inp = dict(inp, C=C)
+    (s1, r1), (s0, r0) = _segmented_vs_whole(monkeypatch, inp, cfg, cfg["T"])
+    assert int(((s0["status"] & DIAG_BIT) == 0).sum()) > 0  # some warps dense
+    for k in ("X", "U", "tight", "trace", "iters", "status", "best_cost", "stall_iter", "stall_gap"):
+        a, b = s1[k].cpu().numpy(), s0[k].cpu().numpy()
+        assert np.array_equal(a, b, equal_nan=a.dtype.kind == "f"), k
+    for k in r0:
+        assert torch.equal(r1[k], r0[k]), k
