@@ -386,17 +386,21 @@ def solve_variant(B: int) -> str:
 
 
 def solve_segmented(B: int, max_iter: int) -> bool:
-    """Whether the library runs this solve in two launches (launch_solve in
-    csrc/ilqr_solve.cu: team layout beyond one 8-CTA wave, max_iter >= 4, no
-    forced trace, ILQR_B200_SEGMENT not 0): the first max_iter - 2 iterations,
-    then the elements still improving, compacted."""
+    """Whether the library runs this solve as a chain of launches (launch_solve
+    in csrc/ilqr_solve.cu: team layout beyond one 8-CTA wave, max_iter >= 4, no
+    forced trace, ILQR_B200_SEGMENT not 0), each later launch on the elements
+    still improving, compacted."""
     if os.environ.get("ILQR_B200_SEGMENT", "1").startswith("0"):
         return False
     return B > 4096 and (B + 5) // 6 > 148 * 8 and max_iter >= 4
 
 
 def solve_launches(B: int, max_iter: int) -> int:
-    return 2 if solve_segmented(B, max_iter) else 1
+    """Kernel launches of one solve: two (a split after max_iter - 2) up to
+    5 iterations, else one per iteration."""
+    if not solve_segmented(B, max_iter):
+        return 1
+    return 2 if max_iter <= 5 else max_iter
 
 
 SOLVE_SOURCES = ("ilqr_solve.cu", "ilqr_team.cuh", "ilqr_pair.cuh", "ilqr_device.cuh")

@@ -159,7 +159,7 @@ int solve_impl(const float* x0, const float* U_init, const float* C, const float
   // give the same bits)
   const char* sg = std::getenv("ILQR_B200_SEGMENT");
   p.segment = (sg != nullptr && sg[0] == '0') ? 0 : 1;
-  p.seg = ilqr::SEG_WHOLE;
+  p.seg_in = p.seg_out = -1;
   CUtensorMap tmC;
   std::memset(&tmC, 0, sizeof(tmC));  // never read in sigmoid mode (no pass copies C)
   if (sig.p == nullptr) {

@@ -60,23 +60,24 @@ struct SolveParams {
   int64_t C_bstride;
   int64_t C_tstride;
   int layout;  // LAYOUT_AUTO, LAYOUT_TEAM or LAYOUT_PAIR
-  int segment;  // 0: off; else the team layout may run in two launches (SEG_*)
-  int seg;      // this launch: SEG_WHOLE, SEG_FIRST or SEG_RESUME
-  int seg_it;   // iterations of the first launch
+  int segment;  // 0: off; else large team-layout solves run as a chain of launches
+  int seg_in;   // this launch resumes the elements of list seg_in (0, 1), or -1: all elements
+  int seg_out;  // ... and defers those still improving at seg_it1 into list seg_out, or -1: none
+  int seg_it0;  // iterations [seg_it0, seg_it1) of this launch
+  int seg_it1;
 };
 
 // Segmented team solve. Elements stop after different numbers of iterations
 // (B = 16384, T = 20, 5 iterations: 3.45 on average), while a warp of six runs
 // until its last one stops (4.74 on average), so a third of the lanes idle.
-// SEG_FIRST runs every element for seg_it iterations; warps whose costs are
-// diagonal then stop, and each of their elements that is still improving
-// saves its state (nominal slot, best cost, status bits) and enters a list.
-// SEG_RESUME runs the listed elements, six per warp, from iteration seg_it
-// to the end. The arithmetic of every element is the same, so the results
-// are the same bits. State, list and count live in floats 12..15 of the
-// t = T records of slots 0, 1 and 2 (element 0's for the count), which the
-// solve never uses otherwise.
-constexpr int SEG_WHOLE = 0, SEG_FIRST = 1, SEG_RESUME = 2;
+// A chain of launches: the first runs every element for the first iterations;
+// then, after each iteration, warps whose costs are diagonal stop, and each
+// of their elements that is still improving saves its state (nominal slot,
+// best cost, status bits) and enters a list that the next launch runs, six
+// elements per warp. The arithmetic of every element is the same, so the
+// results are the same bits. State, the two lists (alternating) and their
+// counts live in floats 12..15 of the t = T records of slots 0, 1 and 3,
+// and 2 and 4 (element 0's), which the solve never uses otherwise.
 
 // Kernel layouts of the 10-state solve and backward. TEAM: six elements per
 // warp, five lanes each (ilqr_team.cuh); PAIR: two elements per warp,

@@ -100,15 +100,16 @@ struct SolveWs {
     return gk() + (size_t)p.T * (NX + 1) * S() * 4 + (size_t)r * COST_REC;
   }
   __device__ __forceinline__ float* cvec(int t) const { return diag(t) + 16; }
-  // segmented solve (SEG_*): the element's saved state, list entry pos and
-  // the list's count, in floats 12..15 of t = T records
+  // segmented solve: the element's saved state, list L's entry pos and
+  // list L's count, in floats 12..15 of t = T records (slots 0, 1 + 2 L and
+  // 2 + 2 L, the count at element 0)
   __device__ __forceinline__ float4* seg_state() const { return rec(0, p.T) + 3; }
 };
-__device__ __forceinline__ int* seg_entry(const SolveParams& p, int64_t pos) {
-  return reinterpret_cast<int*>(p.ws + (((size_t)(p.T + 1) + p.T) * p.S + pos) * TRJ_REC + 12);
+__host__ __device__ __forceinline__ int* seg_entry(float* ws, int T, int64_t S, int L, int64_t pos) {
+  return reinterpret_cast<int*>(ws + (((size_t)(1 + 2 * L) * (T + 1) + T) * S + pos) * TRJ_REC + 12);
 }
-__device__ __forceinline__ int* seg_count(const SolveParams& p) {
-  return reinterpret_cast<int*>(p.ws + ((size_t)(2 * (p.T + 1) + p.T) * p.S) * TRJ_REC + 12);
+__host__ __device__ __forceinline__ int* seg_count(float* ws, int T, int64_t S, int L) {
+  return reinterpret_cast<int*>(ws + ((size_t)(2 + 2 * L) * (T + 1) + T) * S * TRJ_REC + 12);
 }
 
 __device__ __forceinline__ void load_rec(const float4* r, float (&x)[NX], float (&u)[NU]) {
@@ -267,15 +268,15 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
   const int m = lane - (dup ? EPW * TEAM : e * TEAM);
   const int base = e * TEAM;
   const int64_t b0 = (int64_t)blockIdx.x * EPW;
-  const bool resume = p.seg == SEG_RESUME;
+  const bool resume = p.seg_in >= 0;
   int64_t b = b0 + e;
   bool valid = b < p.B;  // the lane's element exists (loads, compute)
-  if (resume) {          // elements from the list the first launch made
-    int64_t cnt = *(volatile const int*)seg_count(p);
+  if (resume) {          // elements from the list the previous launch made
+    int64_t cnt = *(volatile const int*)seg_count(p.ws, p.T, p.S, p.seg_in);
     cnt = cnt < 0 ? 0 : (cnt > p.B ? p.B : cnt);
     if (b0 >= cnt) return;  // the whole CTA lies beyond the list
     valid = b < cnt;
-    const int64_t ent = valid ? (int64_t)*seg_entry(p, b) : 0;
+    const int64_t ent = valid ? (int64_t)*seg_entry(p.ws, p.T, p.S, p.seg_in, b) : 0;
     valid = valid && ent >= 0 && ent < p.B;  // (an entry out of range is skipped)
     b = valid ? ent : 0;
   }
@@ -370,20 +371,20 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
     for (int f = lane; f < EPW * CBLK; f += WARP) slab[f] = 0.0f;
     __syncwarp();
   }
-  // resumed launch: every lane starts at iteration seg_it (warp-uniform); a
-  // listed element restores the state the first launch saved (it improved in
-  // every iteration so far). Lanes past the end of the list keep slot 0 of
-  // their stand-in element: its saved state may never have been written.
-  const int it_begin = resume ? p.seg_it : 0;
+  // resumed launch: every lane starts at iteration seg_it0 (warp-uniform); a
+  // listed element restores the state the previous launch saved (it improved
+  // in every iteration so far). Lanes past the end of the list keep slot 0
+  // of their stand-in element: its saved state may never have been written.
+  const int it_begin = resume ? p.seg_it0 : 0;
   if (resume && valid) {
     const float4 st = *W.seg_state();
     nom = __float_as_int(st.x);
     nom = nom < 0 ? 0 : (nom >= SOLVE_SLOTS ? SOLVE_SLOTS - 1 : nom);
     best = st.y;
     status = __float_as_uint(st.z);
-    iters = p.seg_it;
+    iters = p.seg_it0;
   }
-  bool deferred = false;  // SEG_FIRST: this element continues in the resumed launch
+  bool deferred = false;  // this element continues in the next launch
 
   // The first pass always runs: it also yields the initial objective (with
   // max_iter == 0 only that).
@@ -701,13 +702,14 @@ __global__ void __launch_bounds__(32, MINB) solve_kernel(const __grid_constant__
       if (rerun) nom = dst;
       __syncwarp();
     }
-    if (p.seg == SEG_FIRST && it + 1 == p.seg_it && diag) {
-      // Elements still improving continue in the resumed launch, six per warp;
+    if (p.seg_out >= 0 && it + 1 == p.seg_it1 && diag) {
+      // Elements still improving continue in the next launch, six per warp;
       // this warp stops here.
       deferred = active;
       if (deferred && writer) {
         *W.seg_state() = make_float4(__int_as_float(nom), best, __uint_as_float(status), 0.0f);
-        *seg_entry(p, atomicAdd(seg_count(p), 1)) = (int)b;
+        const int pos = atomicAdd(seg_count(p.ws, p.T, p.S, p.seg_out), 1);
+        *seg_entry(p.ws, p.T, p.S, p.seg_out, pos) = (int)b;
       }
       break;
     }
@@ -1302,6 +1304,7 @@ size_t solve_pair_smem_bytes(int T) {
   return (size_t)EPWP * pair_area(T, PREC_F + PJT_F + PKS_F + PCR_F, CBLK) * sizeof(float);
 }
 
+
 cudaError_t launch_solve(const CUtensorMap& tmC, const SolveParams& p, cudaStream_t stream) {
   const bool ref = p.x_ref != nullptr || p.u_ref != nullptr;
   if (p.T <= PAIR_MAX_T && (p.layout == LAYOUT_PAIR || (p.layout == LAYOUT_AUTO && p.B <= PAIR_MAX_B))) {
@@ -1327,22 +1330,40 @@ cudaError_t launch_solve(const CUtensorMap& tmC, const SolveParams& p, cudaStrea
     }
     return cudaGetLastError();
   };
-  // Batches beyond one 8-CTA wave run in two launches (SEG_*): the first
-  // max_iter - 2 iterations for every element, then the elements still
-  // improving, compacted six per warp, at 12 CTAs per SM (the resumed batch
-  // is a fraction of the first, and the count is known only on the device).
+  // Batches beyond one 8-CTA wave run as a chain of launches, each later one
+  // on the elements still improving, compacted six per warp, at 12 CTAs per
+  // SM (each list is a fraction of the batch and its count is known only on
+  // the device; CTAs beyond it return at once). Up to 5 iterations: one split,
+  // after max_iter - 2 (B200, T = 20, 5 iterations: a split after 3 beat
+  // splits after 2 or 4, and chains of three or more launches, at B = 8192,
+  // 12288 and 16384). More iterations: a launch per iteration after the first
+  // (B = 65536, T = 50, 8 iterations, mean 1.78 run: 6.38 ms against 9.34
+  // with the first launch at 3 iterations and 11.6 with one split after 6;
+  // B = 32768, T = 10, 10 iterations: 1.41 ms against 1.74).
   const bool segmented = p.segment != 0 && p.forced == nullptr && p.max_iter >= 4 && grid > (unsigned)(SMS * TIER_HI);
-  if (!segmented) return launch(p, pick_solve_tier(grid));
+  if (!segmented) {
+    SolveParams q = p;
+    q.seg_in = q.seg_out = -1;
+    return launch(q, pick_solve_tier(grid));
+  }
+  const bool one_split = p.max_iter <= 5;
   SolveParams q = p;
-  q.seg_it = p.max_iter - 2;
-  int* count = reinterpret_cast<int*>(p.ws + ((size_t)(2 * (p.T + 1) + p.T) * p.S) * TRJ_REC + 12);
-  cudaError_t e = cudaMemsetAsync(count, 0, sizeof(int), stream);
-  if (e != cudaSuccess) return e;
-  q.seg = SEG_FIRST;
-  e = launch(q, pick_solve_tier(grid));
-  if (e != cudaSuccess) return e;
-  q.seg = SEG_RESUME;
-  return launch(q, TIER_MID);
+  int it0 = 0;
+  for (int k = 0; it0 < p.max_iter; ++k) {
+    const int it1 = k == 0 ? (one_split ? p.max_iter - 2 : 1) : (one_split ? p.max_iter : it0 + 1);
+    q.seg_in = k == 0 ? -1 : (k - 1) % 2;
+    q.seg_out = it1 < p.max_iter ? k % 2 : -1;
+    q.seg_it0 = it0;
+    q.seg_it1 = it1;
+    if (q.seg_out >= 0) {
+      const cudaError_t e = cudaMemsetAsync(seg_count(p.ws, p.T, p.S, q.seg_out), 0, sizeof(int), stream);
+      if (e != cudaSuccess) return e;
+    }
+    const cudaError_t e = launch(q, k == 0 ? pick_solve_tier(grid) : TIER_MID);
+    if (e != cudaSuccess) return e;
+    it0 = it1;
+  }
+  return cudaSuccess;
 }
 
 }  // namespace ilqr

@@ -190,3 +190,30 @@ def test_segmented_team_solve_mixed_warps(monkeypatch):
         assert np.array_equal(a, b, equal_nan=a.dtype.kind == "f"), k
     for k in r0:
         assert torch.equal(r1[k], r0[k]), k
+
+
+def test_segmented_team_solve_chain(monkeypatch):
+    """More than five iterations run as a chain of launches, one per iteration
+    after the first, each on the elements still improving (the long-horizon
+    configuration: T = 50, 8 iterations, step sizes 1 .. 1/8, targets 15 m
+    away); same bits as one launch."""
+    cfg, inp = wl.config_inputs("stress_b65536_t50", B=8192)
+    t = {k: g(v) for k, v in inp.items()}
+    lo, hi = g(wl.U_MIN), g(wl.U_MAX)
+    gX, gU = (g(a) for a in wl.make_backward_seeds(8192, cfg["T"]))
+    out = {}
+    for seg in ("1", "0"):
+        monkeypatch.setenv("ILQR_B200_SEGMENT", seg)
+        s = nat.solve(t["x0"], t["U_init"], t["C"], t["c"], None, None, None, None, lo, hi, dt=wl.DT,
+                      max_iter=cfg["max_iter"], alphas=cfg["alphas"], want_trace=True, want_stats=True)
+        r = nat.backward(s["X"], s["U"], t["C"], gX, gU, tight=s["tight"], dt=wl.DT, reg_eps=wl.REG_EPS)
+        torch.cuda.synchronize()
+        out[seg] = (s, r)
+    monkeypatch.delenv("ILQR_B200_SEGMENT")
+    (s1, r1), (s0, r0) = out["1"], out["0"]
+    assert int((s0["iters"] > 2).sum()) > 100  # several launches of the chain have work
+    for k in ("X", "U", "tight", "trace", "iters", "status", "best_cost", "stall_iter", "stall_gap"):
+        a, b = s1[k].cpu().numpy(), s0[k].cpu().numpy()
+        assert np.array_equal(a, b, equal_nan=a.dtype.kind == "f"), k
+    for k in r0:
+        assert torch.equal(r1[k], r0[k]), k
