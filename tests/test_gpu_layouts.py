@@ -217,3 +217,26 @@ def test_segmented_team_solve_chain(monkeypatch):
         assert np.array_equal(a, b, equal_nan=a.dtype.kind == "f"), k
     for k in r0:
         assert torch.equal(r1[k], r0[k]), k
+
+
+def test_segmented_team_solve_sigmoid_costs(monkeypatch):
+    """Costs built in the kernel from the policy's sigmoid output take the
+    segmented path too (diagonal from the start; the first launch keeps the cost
+    records the resumed one reads); same bits as one launch, B = 9000, T = 20."""
+    B, T = 9000, 20
+    rng = np.random.default_rng(11)
+    sc = g((1.0 / (1.0 + np.exp(-rng.normal(0.0, 1.5, (B, 28 * T))))).astype(np.float32))
+    inp = wl.make_inputs(B, T, seed=4)
+    x0, Ui, lo, hi = g(inp["x0"]), g(inp["U_init"]), g(wl.U_MIN), g(wl.U_MAX)
+    spec = nat.SigmoidCostSpec()
+    out = {}
+    for seg in ("1", "0"):
+        monkeypatch.setenv("ILQR_B200_SEGMENT", seg)
+        out[seg] = nat.solve_sigmoid(x0, Ui, sc, spec, lo, hi, dt=wl.DT, max_iter=5,
+                                     alphas=(1.0, 0.8, 0.5, 0.2, 0.1), want_trace=True, want_stats=True)
+        torch.cuda.synchronize()
+    monkeypatch.delenv("ILQR_B200_SEGMENT")
+    assert int((out["0"]["iters"] > 3).sum()) > 100
+    for k in out["0"]:
+        a, b = out["1"][k].cpu().numpy(), out["0"][k].cpu().numpy()
+        assert np.array_equal(a, b, equal_nan=a.dtype.kind == "f"), k
